@@ -1,0 +1,310 @@
+#!/usr/bin/env python3
+"""Qwen3-0.6B B=1 greedy decode on B200 - the benchmark of the reference's headline metric.
+
+Workload (the reference's `--raw --benchmark 64` run): Qwen3-0.6B, bf16 weights random-init
+N(0, 0.02) from seed 0 (norms 1.0) in Qwen3.bin layout, context 512, a 16-token prompt of
+uniform random IDs in [0, 151936) (seed 0), then greedy decode steps. One bench step is one
+greedy decode token at batch 1; the prompt is prefilled (untimed) before every run of 64 steps.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Prints one JSON line. Under torchrun (N > 1) every rank runs an independent replica (decode at
+B=1 does not shard across replicas without a collective; the data-parallel configuration runs
+independent sequences per GPU), the timed region is bracketed by barriers and the max time over
+ranks is taken.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "qwen3.cpp_b200"))
+sys.path.insert(0, str(ROOT / "oracle"))
+
+METRIC = "decode tok/s (B=1, Qwen3-0.6B bf16)"
+UNIT = "tok/s"
+CTX = 512
+PROMPT_LEN = 16
+RUN_STEPS = 64
+VOCAB = 151936
+WEIGHT_BYTES = 1_191_968_768          # 28 layers + tied lm_head, bf16
+KV_BYTES_PER_POS = 2 * 28 * 1024 * 2  # K and V rows of every layer
+LM_HEAD_BYTES = VOCAB * 1024 * 2
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def prompt_ids():
+    import numpy as np
+    return np.random.default_rng(0).integers(0, VOCAB, PROMPT_LEN).astype(np.int32)
+
+
+def dist_info():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(gpu_index), "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        self.p.wait(timeout=10)
+        self.f.flush()
+        rows = [r.split(",") for r in Path(self.f.name).read_text().splitlines() if r.strip()]
+        os.unlink(self.f.name)
+        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].strip().replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            if len(r) < 9:
+                continue
+            for name, val in zip(names, r[5:9]):
+                if val.strip() == "Active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(rows)}
+
+
+# ------------------------------------------------------------------ reference arm / CPU baseline
+
+def reference_decode(model_path: str, steps: int, warmup: int, threads: int):
+    """The reference engine (oracle/_ref, built from the reference sources) on the host cores:
+    prefill of the 16-token prompt, then greedy steps (Qwen3::Generate's loops with
+    `--benchmark` semantics), timed with its steady_clock marks. Returns (tok/s, decode s)."""
+    import oracle
+    m = oracle.RefModel(model_path, CTX)
+    p = prompt_ids()
+    if warmup:
+        m.generate_ids(p, min(warmup, RUN_STEPS))
+    done, secs = 0, 0.0
+    while done < steps:
+        n = min(RUN_STEPS, steps - done)
+        _, _, ds = m.generate_ids(p, n)
+        secs += ds
+        done += n
+    return steps / secs, secs
+
+
+def run_reference_arm(args):
+    world, rank, _ = dist_info()
+    if rank != 0:
+        return
+    import gen_weights
+    threads = os.cpu_count() or 1
+    path = gen_weights.cached_model(0)
+    tps, secs = reference_decode(str(path), args.steps, args.warmup, threads)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(tps, 3), "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1000.0 * secs / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "Qwen3-0.6B B=1 greedy decode, ctx 512, 16-token prompt, "
+                               "64-step runs (reference CPU engine)",
+                   "threads": threads},
+        "cpu_baseline": {"value": round(tps, 3), "unit": UNIT, "cores": threads,
+                         "kind": "reference",
+                         "sample": f"{args.steps} greedy decode steps in runs of {RUN_STEPS} after "
+                                   f"a {PROMPT_LEN}-token prefill, OMP_NUM_THREADS={threads}"},
+        "e2e": {"value": round(tps, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ B200 arm
+
+def time_lm_head_gemv(torch, q3, iters=20):
+    """Average duration of the tied lm_head GEMV kernel (151936 x 1024 bf16 weights, fp32 in/out)
+    with CUDA events on the launching stream."""
+    w = torch.randn(VOCAB, 1024, device="cuda").to(torch.bfloat16)
+    x = torch.randn(1024, device="cuda")
+    out = torch.empty(VOCAB, device="cuda")
+    s = torch.cuda.current_stream()
+    for _ in range(3):
+        q3.matmul(out.data_ptr(), x.data_ptr(), w.data_ptr(), VOCAB, 1024, s.cuda_stream)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(iters):
+        q3.matmul(out.data_ptr(), x.data_ptr(), w.data_ptr(), VOCAB, 1024, s.cuda_stream)
+    e1.record(s)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters / 1e3
+
+
+def run_b200_arm(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import gen_weights
+    import q3b200
+
+    world, rank, local = dist_info()
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    path = gen_weights.cached_model(0)
+    if world > 1:
+        dist.barrier()
+    model = q3b200.Qwen3(path, CTX, device=local)
+    ext = torch.cuda.ExternalStream(model.stream)
+    p = prompt_ids()
+
+    # Warm-up: W decode steps after a prefill.
+    _, nxt = model.prefill(p, 0, want_logits=False)
+    model.decode_greedy(nxt, PROMPT_LEN, max(args.warmup, 3))
+    torch.cuda.synchronize()
+
+    clocks = Clocks(local)
+    total_ms = 0.0
+    done = 0
+    kv_pos_sum = 0
+    while done < args.steps:
+        n = min(RUN_STEPS, args.steps - done)
+        _, nxt = model.prefill(p, 0, want_logits=False)   # untimed
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(ext)
+        model.decode_greedy(nxt, PROMPT_LEN, n)
+        e1.record(ext)
+        torch.cuda.synchronize()
+        total_ms += e0.elapsed_time(e1)
+        kv_pos_sum += sum(PROMPT_LEN + i + 1 for i in range(n))
+        done += n
+    if world > 1:
+        t = torch.tensor([total_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    clk = clocks.stop()
+
+    # End to end through the public API with host buffers: ForwardToken per step (token and
+    # position in, 151936 fp32 logits out to host), greedy argmax on the host - the way a user
+    # of the reference drives ForwardToken + Sampler::Greedy.
+    model.reset()
+    _, nxt = model.prefill(p, 0, want_logits=False)
+    e2e_steps = min(args.steps, RUN_STEPS)
+    tok = nxt
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        lg = model.forward_token(tok, PROMPT_LEN + i)
+        tok = int(np.argmax(lg))
+    e2e_s = time.perf_counter() - t0
+    e2e_tps = world * e2e_steps / e2e_s
+
+    pk = peaks()
+    lm_s = time_lm_head_gemv(torch, q3b200)
+    lm_bytes = LM_HEAD_BYTES + 1024 * 4 + VOCAB * 4
+    achieved = lm_bytes / lm_s / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and q3_ref_available():
+        threads = os.cpu_count() or 1
+        tps, _ = reference_decode(str(path), RUN_STEPS, 0, threads)
+        cpu = {"value": round(tps, 3), "unit": UNIT, "cores": threads, "kind": "reference",
+               "sample": f"{RUN_STEPS} greedy decode steps after a {PROMPT_LEN}-token prefill, "
+                         f"ctx {CTX}, OMP_NUM_THREADS={threads}"}
+
+    value = world * args.steps / (total_ms / 1e3)
+    avg_kv = kv_pos_sum / args.steps
+    step_bytes = WEIGHT_BYTES + KV_BYTES_PER_POS * avg_kv
+    per_gpu_tps = args.steps / (total_ms / 1e3)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(total_ms / args.steps, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random-init weights and prompt IDs)",
+            "config": {"workload": "Qwen3-0.6B B=1 greedy decode, ctx 512, 16-token prompt, "
+                                   "runs of 64 decode steps (one step = one token)",
+                       "model": "Qwen3-0.6B", "global_batch": world, "seq_len": CTX,
+                       "parallelism": f"replicas x{world}",
+                       "l2": "inputs larger than L2 (1.19 GB of weights streamed per step)"},
+            "gpu_launches": args.steps * (7 * 28 + 3),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1),
+                         "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
+                         "kernel": "gemv lm_head (151936x1024 bf16)",
+                         "peak_source": pk["source"]},
+            "decode_step_roofline": {
+                "bytes_per_step": int(step_bytes),
+                "achieved_gbs": round(step_bytes * per_gpu_tps / 1e9, 1),
+                "frac": round(step_bytes * per_gpu_tps / 1e9 / pk["hbm_gbs"], 4)},
+            "e2e": {"value": round(e2e_tps, 2), "unit": UNIT, "h2d_bytes_per_step": 32,
+                    "d2h_bytes_per_step": VOCAB * 4,
+                    "api": "q3_forward_token per step + host argmax"},
+            "cpu_baseline": cpu,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    model.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def q3_ref_available() -> bool:
+    return (ROOT / "oracle" / "_ref" / "libq3ref.so").exists()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
+        if not q3_ref_available():
+            print(json.dumps({"impl": "reference",
+                              "unavailable": "oracle/_ref/libq3ref.so was not built"}))
+            return
+        run_reference_arm(args)
+    else:
+        run_b200_arm(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,177 @@
+/*
+ * q3_b200.h - C ABI of the B200 (sm_100a) Qwen3 forward pass.
+ *
+ * Drop-in boundary for the hot path of asriva32/Qwen3.cpp: the C++ surface of that project's
+ * include/inference.h (class Qwen3, class Block, the free kernels RmsNorm/MatMul/...,
+ * Sampler::Greedy) re-expressed as plain C entry points over plain pointers and sizes. Each
+ * declaration names the reference interface it replaces. The C++ classes in
+ * include/inference_b200.h are a thin layer over these functions.
+ *
+ * Conventions
+ *  - Every function returns q3_status. Codes 1-3 map one to one onto the exception types the
+ *    reference throws (std::runtime_error, std::invalid_argument, std::out_of_range); the
+ *    message of the last failure on the calling thread is q3_last_error().
+ *  - "_host" pointers are caller-owned host memory; all other data pointers are device pointers.
+ *  - A model or block handle owns its device memory (weights, KV cache, workspace) and one CUDA
+ *    stream; calls on a handle block until their work on that stream is done. Handles are not
+ *    thread-safe (the reference's Qwen3 and Block are not either).
+ *  - bf16 values travel as their raw uint16_t bit patterns.
+ */
+#ifndef Q3_B200_H
+#define Q3_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum q3_status {
+    Q3_OK = 0,
+    Q3_ERR_RUNTIME = 1,          /* std::runtime_error: file/format errors, CUDA failures */
+    Q3_ERR_INVALID_ARGUMENT = 2, /* std::invalid_argument: bad config, sizes, null pointers */
+    Q3_ERR_OUT_OF_RANGE = 3,     /* std::out_of_range: token id, position or KV range */
+    Q3_ERR_DEVICE_TIMEOUT = 5    /* a bounded device-side wait gave up (reported, not hung) */
+} q3_status;
+
+/* Config (include/inference.h:66-90). max_seq_len is the runtime context once a model is
+ * loaded (Qwen3::InitializeInference overwrites it, src/inference.cpp:534). */
+typedef struct q3_config {
+    int32_t dim, hidden_dim, head_dim, n_layers, n_heads, n_kv_heads, vocab_size, max_seq_len;
+    int32_t bos_token_id, eos_token_id, rotary_dim;
+    float rope_theta, norm_eps;
+    int32_t tie_word_embeddings, attention_bias, qk_norm;
+} q3_config;
+
+/* GenerationStats (include/inference.h:209-219); seconds are host wall clock. */
+typedef struct q3_generation_stats {
+    size_t prompt_tokens, generated_tokens;
+    double prefill_seconds, decode_seconds;
+    int32_t stopped_on_eos, reached_token_limit;
+} q3_generation_stats;
+
+typedef struct q3_model q3_model;
+typedef struct q3_block q3_block;
+
+const char* q3_last_error(void);
+const char* q3_version(void);
+
+/* ------------------------------------------------------------------ whole model (class Qwen3) */
+
+/* Qwen3::Qwen3(path, context_length) + InitializeInference (src/inference.cpp:445-510, :529-581):
+ * parses Qwen3.bin (the convert.py layout) and uploads every tensor into one HBM arena on
+ * `device`. Same validation and error kinds as the reference loader. */
+q3_status q3_model_load(const char* path, int context_length, int device, q3_model** out);
+void q3_model_free(q3_model* model);
+
+/* Qwen3::GetConfig (src/inference.cpp:512-514). */
+q3_status q3_model_config(const q3_model* model, q3_config* out);
+/* Qwen3::GetTensorIndex().size() (src/inference.cpp:516-518). */
+q3_status q3_model_tensor_count(const q3_model* model, int* out);
+
+/* Qwen3::ResetInference (src/inference.cpp:583-590): zeroes every KV cache. */
+q3_status q3_reset(q3_model* model);
+
+/* Qwen3::ForwardToken (src/inference.cpp:592-637): one token at absolute position `pos`
+ * (attention-sink ring buffer once pos >= context), logits[vocab_size] to logits_host. */
+q3_status q3_forward_token(q3_model* model, int32_t token, int pos, float* logits_host);
+
+/* ForwardToken with debug taps: hidden_host[(n_layers+1)*dim] receives the embedding row and
+ * the hidden state after each layer (the per-layer view of src/inference.cpp:615-617). Either
+ * output may be NULL. */
+q3_status q3_forward_token_layers(q3_model* model, int32_t token, int pos, float* hidden_host,
+                                  float* logits_host);
+
+/* Row kv_pos (ring slot) of layer `layer`'s bf16 KV cache, n_kv_heads*head_dim values each in
+ * the reference layout of KVCache (include/inference.h:140-161). */
+q3_status q3_kv_row(q3_model* model, int layer, int kv_pos, uint16_t* k_host, uint16_t* v_host);
+
+/* Batched prefill of n prompt tokens at positions pos0..pos0+n-1 (replaces the token-at-a-time
+ * loop of Qwen3::Generate, src/inference.cpp:669-671). Leaves the KV cache as n ForwardToken
+ * calls would. last_logits_host (nullable) receives the logits of the last token;
+ * next_token_host (nullable) its greedy argmax. */
+q3_status q3_prefill(q3_model* model, const int32_t* ids_host, int n, int pos0,
+                     float* last_logits_host, int32_t* next_token_host);
+
+/* n_steps greedy decode steps driven on the device (the loop of src/inference.cpp:679-690 with
+ * stop_on_eos = false, i.e. `--benchmark N`): step i feeds token t_i at position pos0+i and
+ * t_{i+1} = argmax of its logits, t_0 = first_token. tokens_host[n_steps] receives t_1..t_n.
+ * last_logits_host (nullable) receives the logits of the final step. */
+q3_status q3_decode_greedy(q3_model* model, int32_t first_token, int pos0, int n_steps,
+                           int32_t* tokens_host, float* last_logits_host);
+
+/* Teacher-forced decode: feeds tokens_host[i] at position pos0+i for i < n and writes the
+ * greedy argmax of every step to argmax_host[n] (nullable) and all logits to
+ * logits_host[n*vocab] (nullable). */
+q3_status q3_decode_forced(q3_model* model, const int32_t* tokens_host, int n, int pos0,
+                           int32_t* argmax_host, float* logits_host);
+
+/* Qwen3::Generate on token IDs (src/inference.cpp:639-700 without the tokenizer): prefill of
+ * the prompt (empty prompt -> [bos]), then greedy tokens until max_new_tokens or, when
+ * stop_on_eos, the EOS id. out_tokens_host needs max_new_tokens entries. */
+q3_status q3_generate(q3_model* model, const int32_t* prompt_host, int n_prompt,
+                      size_t max_new_tokens, int stop_on_eos, int32_t* out_tokens_host,
+                      size_t* n_out, q3_generation_stats* stats);
+
+/* Model-owned CUDA stream (cudaStream_t) for callers that order their own work against it. */
+q3_status q3_model_stream(q3_model* model, void** stream);
+
+/* ------------------------------------------------------------------ one block (class Block) */
+
+/* Block(config, weights) (src/inference.cpp:720-730) with BlockWeights
+ * (include/inference.h:163-176) given as 11 host arrays of bf16 bits in the order attn_norm,
+ * q_norm, k_norm, wq, wk, wv, wo, mlp_norm, w1, w2, w3; sizes are checked as
+ * Block::ValidateWeights does (src/inference.cpp:737-764) against the element counts given in
+ * `counts` (nullable: then sizes are taken as valid). The cache holds cfg->max_seq_len rows. */
+q3_status q3_block_create(const q3_config* cfg, const uint16_t* const* weights_host,
+                          const size_t* counts, int device, q3_block** out);
+void q3_block_free(q3_block* block);
+
+/* Block::forward (src/inference.cpp:766-866) on a host vector x_host[dim], in place. */
+q3_status q3_block_forward(q3_block* block, float* x_host, int pos, int num_sink, int kv_pos,
+                           int kv_len);
+/* Block::ResetCache (src/inference.cpp:732-735). */
+q3_status q3_block_reset_cache(q3_block* block);
+/* Block::GetCache (include/inference.h:193-195), reference layout [max_seq_len, kv_dim]. */
+q3_status q3_block_get_cache(q3_block* block, uint16_t* k_host, uint16_t* v_host);
+/* Fills the cache from the reference layout (the block test writes it through a const_cast). */
+q3_status q3_block_set_cache(q3_block* block, const uint16_t* k_host, const uint16_t* v_host);
+
+/* ------------------------------------------------------------------ free kernels (device ptrs)
+ * The free functions of include/inference.h:308-315 and Sampler::Greedy (:204-207), on device
+ * pointers, enqueued on `stream` (a cudaStream_t; NULL = legacy default stream). They return
+ * after enqueueing. */
+
+/* RmsNorm (src/inference.cpp:887-923). out may alias x. */
+q3_status q3_rmsnorm(float* out, const float* x, const uint16_t* w, float eps, int n,
+                     void* stream);
+/* Softmax (src/inference.cpp:925-946). out may alias x. */
+q3_status q3_softmax(float* out, const float* x, int n, void* stream);
+/* MatMul (src/inference.cpp:952-966): out[n] = W[n,m] . x[m], W bf16 row-major. */
+q3_status q3_matmul(float* out, const float* x, const uint16_t* w, int n, int m, void* stream);
+/* ApplyRotaryEmb (src/inference.cpp:968-991), in place on x[d]. cos/sin are evaluated on the
+ * host with the reference's fp32 expressions and passed to the kernel. */
+q3_status q3_rope(float* x, int d, int head_dim, int pos, float theta, int rotary_dim,
+                  void* stream);
+/* FeedForwardNetwork (src/inference.cpp:993-1015). lin1/lin2 are [hidden_dim] scratch. */
+q3_status q3_ffn(float* out, float* lin1, float* lin2, const float* x, const uint16_t* w1,
+                 const uint16_t* w2, const uint16_t* w3, int hidden_dim, int dim, void* stream);
+
+/* FastAttn (src/inference.cpp:1017-1058) for ONE query head over a bf16 cache in the reference
+ * layout: k/v point at the head's first element, rows are n_kv_heads*head_dim apart. The
+ * reference's `atth` scores buffer becomes `workspace`, whose size in bytes is
+ * q3_attn_workspace_size(head_dim, kv_len); it holds the split-K partial results. */
+size_t q3_attn_workspace_size(int head_dim, int kv_len);
+q3_status q3_attn(float* out, void* workspace, const float* q, const uint16_t* k,
+                  const uint16_t* v, int head_dim, int n_kv_heads, int kv_len, void* stream);
+
+/* Sampler::Greedy (src/inference.cpp:703-709): index of the first maximum of logits[n], written
+ * to *out_index (device int32). n == 0 is rejected like the reference's empty span. */
+q3_status q3_greedy(const float* logits, int n, int32_t* out_index, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* Q3_B200_H */

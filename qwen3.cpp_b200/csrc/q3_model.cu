@@ -1,0 +1,1177 @@
+// Host side of the B200 Qwen3 library: Qwen3.bin loader, HBM arena, KV cache, per-step CUDA
+// graphs, and the C ABI of include/q3_b200.h.
+//
+// The loader restates the reference's (asriva32/Qwen3.cpp src/inference.cpp:17-263, :445-581)
+// checks and error kinds; the forward orchestration restates Qwen3::ForwardToken (:592-637) and
+// Block::forward (:766-866) as a fixed sequence of kernel launches captured once into a CUDA
+// graph and replayed for every token, with the per-step scalars in device memory.
+#include <cuda_runtime.h>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <limits>
+#include <map>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "q3_common.cuh"
+#include "q3_kernels.cuh"
+#include "q3_model.cuh"
+
+namespace q3 {
+
+namespace {
+thread_local std::string g_last_error;
+}
+
+void set_last_error(const std::string& msg) { g_last_error = msg; }
+
+// ------------------------------------------------------------------ Qwen3.bin parsing
+
+namespace {
+
+constexpr char kMagic[8] = {'Q', 'W', 'E', 'N', '3', 'C', 'P', '\0'};
+constexpr uint32_t kVersion = 1;
+
+enum DType : uint32_t { kF32 = 1, kBF16 = 3, kU8 = 4, kI32 = 5 };
+
+size_t dtype_size(uint32_t d) {
+    switch (d) {
+        case kF32: return 4;
+        case kBF16: return 2;
+        case kU8: return 1;
+        case kI32: return 4;
+    }
+    throw std::runtime_error("Unknown tensor dtype");
+}
+
+struct Reader {
+    const uint8_t* p;
+    size_t size;
+    size_t off = 0;
+    template <typename T>
+    T pod() {
+        if (off + sizeof(T) > size) throw std::runtime_error("Unexpected end of Qwen3.bin");
+        T v;
+        std::memcpy(&v, p + off, sizeof(T));
+        off += sizeof(T);
+        return v;
+    }
+    std::string str(uint64_t n) {
+        if (off + n > size) throw std::runtime_error("Unexpected end of Qwen3.bin while reading string");
+        std::string s(reinterpret_cast<const char*>(p + off), n);
+        off += n;
+        return s;
+    }
+};
+
+// JsonValue (src/inference.cpp:97-124): the naive `"key":` lookup of the reference.
+std::string json_value(const std::string& js, const std::string& key) {
+    const std::string qk = "\"" + key + "\":";
+    const size_t kp = js.find(qk);
+    if (kp == std::string::npos) throw std::runtime_error("Missing metadata key: " + key);
+    size_t p = kp + qk.size();
+    while (p < js.size() && js[p] == ' ') ++p;
+    if (p >= js.size()) throw std::runtime_error("Malformed metadata value for: " + key);
+    if (js[p] == '"') {
+        const size_t e = js.find('"', p + 1);
+        if (e == std::string::npos) {
+            throw std::runtime_error("Unterminated string metadata value for: " + key);
+        }
+        return js.substr(p + 1, e - p - 1);
+    }
+    const size_t e = js.find_first_of(",}", p);
+    if (e == std::string::npos) throw std::runtime_error("Unterminated metadata value for: " + key);
+    return js.substr(p, e - p);
+}
+
+bool json_bool(const std::string& js, const std::string& key) {
+    const std::string v = json_value(js, key);
+    if (v == "true") return true;
+    if (v == "false") return false;
+    throw std::runtime_error("Metadata value is not bool for: " + key);
+}
+
+}  // namespace
+
+// ValidateConfig (src/inference.cpp:145-157).
+void validate_config(const q3_config& c) {
+    if (c.dim <= 0 || c.hidden_dim <= 0 || c.head_dim <= 0 || c.n_heads <= 0 ||
+        c.n_kv_heads <= 0 || c.max_seq_len <= 0) {
+        throw std::invalid_argument("Block config dimensions must be positive");
+    }
+    if (c.n_heads % c.n_kv_heads != 0) {
+        throw std::invalid_argument("Attention head count must be divisible by KV head count");
+    }
+    if (c.rotary_dim < 0 || c.rotary_dim > c.head_dim || c.rotary_dim % 2 != 0) {
+        throw std::invalid_argument("rotary_dim must be even and no larger than head_dim");
+    }
+}
+
+// Limits of the CUDA kernels beyond the reference's own checks.
+void validate_kernel_limits(const q3_config& c) {
+    if (c.head_dim > 256) throw std::invalid_argument("head_dim above 256 is not supported");
+    if (c.n_heads / c.n_kv_heads > 8) {
+        throw std::invalid_argument("more than 8 query heads per KV head is not supported");
+    }
+}
+
+ModelFile::ModelFile(const std::string& path) : path_(path) {
+    fd_ = ::open(path.c_str(), O_RDONLY);
+    if (fd_ < 0) throw std::runtime_error("Failed to open model file: " + path);
+    struct stat st {};
+    if (fstat(fd_, &st) != 0) throw std::runtime_error("Failed to open model file: " + path);
+    size_ = static_cast<size_t>(st.st_size);
+    if (size_ > 0) {
+        void* m = mmap(nullptr, size_, PROT_READ, MAP_PRIVATE, fd_, 0);
+        if (m == MAP_FAILED) throw std::runtime_error("Failed to map model file: " + path);
+        data_ = static_cast<const uint8_t*>(m);
+    }
+    Reader r{data_, size_};
+    if (size_ < 8 || std::memcmp(data_, kMagic, 8) != 0) {
+        throw std::runtime_error("Invalid Qwen3 model file magic");
+    }
+    r.off = 8;
+    if (r.pod<uint32_t>() != kVersion) throw std::runtime_error("Unsupported Qwen3 model file version");
+    const auto meta_size = r.pod<uint64_t>();
+    const std::string js = r.str(meta_size);
+    // ParseConfig (src/inference.cpp:159-182).
+    arch_ = json_value(js, "arch");
+    dtype_ = json_value(js, "dtype");
+    act_ = json_value(js, "act_type");
+    q3_config& c = config_;
+    c.dim = std::stoi(json_value(js, "dim"));
+    c.hidden_dim = std::stoi(json_value(js, "hidden_dim"));
+    c.head_dim = std::stoi(json_value(js, "head_dim"));
+    c.n_layers = std::stoi(json_value(js, "n_layers"));
+    c.n_heads = std::stoi(json_value(js, "n_heads"));
+    c.n_kv_heads = std::stoi(json_value(js, "n_kv_heads"));
+    c.vocab_size = std::stoi(json_value(js, "vocab_size"));
+    c.max_seq_len = std::stoi(json_value(js, "max_seq_len"));
+    c.bos_token_id = std::stoi(json_value(js, "bos_token_id"));
+    c.eos_token_id = std::stoi(json_value(js, "eos_token_id"));
+    c.rotary_dim = std::stoi(json_value(js, "rotary_dim"));
+    c.rope_theta = std::stof(json_value(js, "rope_theta"));
+    c.norm_eps = std::stof(json_value(js, "norm_eps"));
+    c.tie_word_embeddings = json_bool(js, "tie_word_embeddings");
+    c.attention_bias = json_bool(js, "attention_bias");
+    c.qk_norm = json_bool(js, "qk_norm");
+    validate_config(c);
+    if (dtype_ != "bf16") throw std::runtime_error("Only bf16 Qwen3.bin files are supported");
+
+    const auto count = r.pod<uint64_t>();
+    for (uint64_t i = 0; i < count; ++i) {
+        Tensor t;
+        const auto nlen = r.pod<uint32_t>();
+        t.name = r.str(nlen);
+        t.dtype = r.pod<uint32_t>();
+        const auto ndim = r.pod<uint32_t>();
+        for (uint32_t d = 0; d < ndim; ++d) t.shape.push_back(r.pod<uint64_t>());
+        t.byte_size = r.pod<uint64_t>();
+        t.offset = r.off;
+        // ValidateTensorByteSize (:85-95) and ValidateSupportedTensorType (:211-232).
+        size_t n = 1;
+        for (auto d : t.shape) {
+            if (d != 0 && n > std::numeric_limits<size_t>::max() / d) {
+                throw std::runtime_error("Tensor shape element count overflow");
+            }
+            n *= d;
+        }
+        if (n * dtype_size(t.dtype) != t.byte_size) {
+            throw std::runtime_error("Tensor byte size mismatch for " + t.name);
+        }
+        const bool tok = t.name == "tokenizer.json" || t.name == "tokenizer.tokens" ||
+                         t.name == "tokenizer.offsets";
+        if (tok) {
+            const bool ok = (t.name != "tokenizer.offsets" && t.dtype == kU8) ||
+                            (t.name == "tokenizer.offsets" && t.dtype == kI32);
+            if (!ok) throw std::runtime_error("Unsupported tokenizer tensor dtype for " + t.name);
+        } else if (t.dtype != kBF16) {
+            throw std::runtime_error("Only bf16 model tensors are supported: " + t.name);
+        }
+        if (t.offset + t.byte_size > size_) {
+            throw std::runtime_error("Unexpected end of Qwen3.bin while skipping tensor payload");
+        }
+        if (!tensors_.emplace(t.name, t).second) {
+            throw std::runtime_error("Duplicate tensor record: " + t.name);
+        }
+        r.off += t.byte_size;
+    }
+}
+
+ModelFile::~ModelFile() {
+    if (data_) munmap(const_cast<uint8_t*>(data_), size_);
+    if (fd_ >= 0) ::close(fd_);
+}
+
+const ModelFile::Tensor& ModelFile::tensor(const std::string& name) const {
+    auto it = tensors_.find(name);
+    if (it == tensors_.end()) throw std::runtime_error("Tensor not found: " + name);
+    return it->second;
+}
+
+// ------------------------------------------------------------------ device buffers
+
+DeviceBuffer::~DeviceBuffer() { reset(); }
+void DeviceBuffer::reset() {
+    if (ptr) cudaFree(ptr);
+    ptr = nullptr;
+    bytes = 0;
+}
+void DeviceBuffer::alloc(size_t n) {
+    reset();
+    if (n == 0) return;
+    Q3_CUDA(cudaMalloc(&ptr, n));
+    bytes = n;
+}
+
+PinnedBuffer::~PinnedBuffer() {
+    if (ptr) cudaFreeHost(ptr);
+}
+void PinnedBuffer::ensure(size_t n) {
+    if (n <= bytes) return;
+    if (ptr) cudaFreeHost(ptr);
+    ptr = nullptr;
+    Q3_CUDA(cudaMallocHost(&ptr, n));
+    bytes = n;
+}
+
+// ------------------------------------------------------------------ RoPE table
+
+// cos/sin of RoPE evaluated on the host with the reference's fp32 expressions
+// (src/inference.cpp:979-982), for positions [0, len).
+std::vector<float2> rope_table_host(float theta, int rotary_dim, int len) {
+    const int half = rotary_dim / 2;
+    std::vector<float2> t(static_cast<size_t>(len) * (half > 0 ? half : 0));
+    std::vector<float> freq(half);
+    for (int i = 0; i < half; ++i) {
+        freq[i] = 1.0f / powf(theta, 2.0f * i / rotary_dim);
+    }
+    for (int p = 0; p < len; ++p) {
+        for (int i = 0; i < half; ++i) {
+            const float angle = p * freq[i];
+            t[static_cast<size_t>(p) * half + i] = make_float2(cosf(angle), sinf(angle));
+        }
+    }
+    return t;
+}
+
+// ------------------------------------------------------------------ layer engine
+
+Engine::Engine(const q3_config& cfg, int n_layers, int device, int kv_slots)
+    : cfg_(cfg), n_layers_(n_layers), device_(device), kv_slots_(kv_slots) {
+    Q3_CUDA(cudaSetDevice(device_));
+    Q3_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    const int hd = cfg.head_dim, nq = cfg.n_heads, nk = cfg.n_kv_heads;
+    q_dim_ = nq * hd;
+    kv_dim_ = nk * hd;
+    n_pages_ = (kv_slots_ + kPageTokens - 1) / kPageTokens;
+    n_splits_ = attn_splits_for(kv_slots_);
+    page_elems_ = static_cast<size_t>(nk) * kPageTokens * hd;
+    const size_t layer_kv = static_cast<size_t>(n_pages_) * page_elems_;
+    k_cache_.alloc(layer_kv * n_layers * 2);
+    v_cache_.alloc(layer_kv * n_layers * 2);
+    std::vector<int32_t> table(n_pages_);
+    for (int i = 0; i < n_pages_; ++i) table[i] = i;
+    page_table_.alloc(table.size() * 4);
+    Q3_CUDA(cudaMemcpy(page_table_.ptr, table.data(), table.size() * 4, cudaMemcpyHostToDevice));
+
+    sp_.alloc(sizeof(StepParams));
+    x_.alloc(cfg.dim * 4);
+    qkv_.alloc((q_dim_ + 2 * kv_dim_) * 4);
+    att_.alloc(q_dim_ * 4);
+    h_.alloc(static_cast<size_t>(cfg.hidden_dim) * 4);
+    part_o_.alloc(static_cast<size_t>(nq) * n_splits_ * hd * 4);
+    part_ml_.alloc(static_cast<size_t>(nq) * n_splits_ * sizeof(float2));
+    taps_.alloc(static_cast<size_t>(n_layers + 1) * cfg.dim * 4);
+    pinned_sp_.ensure(sizeof(StepParams));
+    ensure_rope(kv_slots_ + 1);
+    reset_cache();
+}
+
+Engine::~Engine() {
+    cudaSetDevice(device_);
+    for (auto& kv : graphs_) cudaGraphExecDestroy(kv.second);
+    if (stream_) cudaStreamDestroy(stream_);
+}
+
+void Engine::drop_graphs() {
+    for (auto& kv : graphs_) cudaGraphExecDestroy(kv.second);
+    graphs_.clear();
+}
+
+void Engine::ensure_rope(int needed_len) {
+    if (needed_len <= rope_len_) return;
+    int len = rope_len_ > 0 ? rope_len_ : 1;
+    while (len < needed_len) len *= 2;
+    const auto t = rope_table_host(cfg_.rope_theta, cfg_.rotary_dim, len);
+    Q3_CUDA(cudaStreamSynchronize(stream_));
+    rope_.alloc(std::max<size_t>(t.size(), 1) * sizeof(float2));
+    if (!t.empty()) {
+        Q3_CUDA(cudaMemcpy(rope_.ptr, t.data(), t.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    }
+    rope_len_ = len;
+    drop_graphs();  // graphs hold the table pointer
+}
+
+void Engine::reset_cache() {
+    Q3_CUDA(cudaMemsetAsync(k_cache_.ptr, 0, k_cache_.bytes, stream_));
+    Q3_CUDA(cudaMemsetAsync(v_cache_.ptr, 0, v_cache_.bytes, stream_));
+    Q3_CUDA(cudaStreamSynchronize(stream_));
+}
+
+uint16_t* Engine::k_layer(int l) const {
+    return static_cast<uint16_t*>(k_cache_.ptr) + static_cast<size_t>(l) * n_pages_ * page_elems_;
+}
+uint16_t* Engine::v_layer(int l) const {
+    return static_cast<uint16_t*>(v_cache_.ptr) + static_cast<size_t>(l) * n_pages_ * page_elems_;
+}
+
+// Block::forward (src/inference.cpp:795-865) for layer l on the engine's x_.
+void Engine::enqueue_layer(int l, const LayerWeights& w) {
+    const q3_config& c = cfg_;
+    cudaStream_t s = stream_;
+    float* x = static_cast<float*>(x_.ptr);
+    float* qkv = static_cast<float*>(qkv_.ptr);
+    float* att = static_cast<float*>(att_.ptr);
+    float* h = static_cast<float*>(h_.ptr);
+    const StepParams* sp = static_cast<const StepParams*>(sp_.ptr);
+    // RmsNorm + q/k/v MatMuls (:795-798) as one GEMV over the stacked [wq; wk; wv] rows.
+    launch_gemv(kEpiStore, w.wqkv, nullptr, x, w.attn_norm, c.norm_eps, qkv, nullptr,
+                q_dim_ + 2 * kv_dim_, c.dim, nullptr, 0, s);
+    QkvArgs qa{};
+    qa.qkv = qkv;
+    qa.q_norm = w.q_norm;
+    qa.k_norm = w.k_norm;
+    qa.rope = static_cast<const float2*>(rope_.ptr);
+    qa.rope_len = rope_len_;
+    qa.k_cache = k_layer(l);
+    qa.v_cache = v_layer(l);
+    qa.page_table = static_cast<const int32_t*>(page_table_.ptr);
+    qa.sp = sp;
+    qa.n_heads = c.n_heads;
+    qa.n_kv = c.n_kv_heads;
+    qa.hd = c.head_dim;
+    qa.rotary_dim = c.rotary_dim;
+    qa.eps = c.norm_eps;
+    launch_qk_rope_kv(qa, s);
+    AttnArgs aa{};
+    aa.q = qkv;
+    aa.k = k_layer(l);
+    aa.v = v_layer(l);
+    aa.page_table = static_cast<const int32_t*>(page_table_.ptr);
+    aa.sp = sp;
+    aa.n_heads = c.n_heads;
+    aa.n_kv = c.n_kv_heads;
+    aa.hd = c.head_dim;
+    aa.row_stride = kv_dim_;
+    aa.n_splits = n_splits_;
+    aa.part_o = static_cast<float*>(part_o_.ptr);
+    aa.part_ml = static_cast<float2*>(part_ml_.ptr);
+    aa.out = att;
+    launch_attention(aa, s);
+    // o_proj + residual (:846-849).
+    launch_gemv(kEpiResidual, w.wo, nullptr, att, nullptr, 0.0f, x, nullptr, c.dim, q_dim_,
+                nullptr, 0, s);
+    // RmsNorm + gate/up + SiLU*up (:851, :1005-1011), then down + residual (:1013, :863-865).
+    launch_gemv(kEpiSiluMul, w.w1, w.w3, x, w.mlp_norm, c.norm_eps, h, nullptr, c.hidden_dim,
+                c.dim, nullptr, 0, s);
+    launch_gemv(kEpiResidual, w.w2, nullptr, h, nullptr, 0.0f, x, nullptr, c.dim, c.hidden_dim,
+                nullptr, 0, s);
+}
+
+void Engine::write_step(const StepParams& p) {
+    // One pinned staging slot: wait for the previous copy out of it before overwriting.
+    Q3_CUDA(cudaStreamSynchronize(stream_));
+    std::memcpy(pinned_sp_.ptr, &p, sizeof(p));
+    Q3_CUDA(cudaMemcpyAsync(sp_.ptr, pinned_sp_.ptr, sizeof(p), cudaMemcpyHostToDevice, stream_));
+}
+
+StepParams Engine::read_step() {
+    Q3_CUDA(cudaMemcpyAsync(pinned_sp_.ptr, sp_.ptr, sizeof(StepParams), cudaMemcpyDeviceToHost,
+                            stream_));
+    Q3_CUDA(cudaStreamSynchronize(stream_));
+    StepParams p;
+    std::memcpy(&p, pinned_sp_.ptr, sizeof(p));
+    return p;
+}
+
+// Reference layout <-> paged layout of one layer's cache (host side, for debug taps and tests).
+void Engine::read_kv_row(int l, int slot, uint16_t* k, uint16_t* v) {
+    const int hd = cfg_.head_dim, nk = cfg_.n_kv_heads;
+    const int page = slot / kPageTokens, off = slot % kPageTokens;  // identity page table
+    for (int g = 0; g < nk; ++g) {
+        const size_t e = (static_cast<size_t>(page) * nk + g) * kPageTokens * hd +
+                         static_cast<size_t>(off) * hd;
+        Q3_CUDA(cudaMemcpyAsync(k + g * hd, k_layer(l) + e, hd * 2, cudaMemcpyDeviceToHost, stream_));
+        Q3_CUDA(cudaMemcpyAsync(v + g * hd, v_layer(l) + e, hd * 2, cudaMemcpyDeviceToHost, stream_));
+    }
+    Q3_CUDA(cudaStreamSynchronize(stream_));
+}
+
+void Engine::read_cache(int l, uint16_t* k, uint16_t* v, int rows) {
+    const int hd = cfg_.head_dim, nk = cfg_.n_kv_heads;
+    const size_t n = static_cast<size_t>(n_pages_) * page_elems_;
+    std::vector<uint16_t> kp(n), vp(n);
+    Q3_CUDA(cudaMemcpyAsync(kp.data(), k_layer(l), n * 2, cudaMemcpyDeviceToHost, stream_));
+    Q3_CUDA(cudaMemcpyAsync(vp.data(), v_layer(l), n * 2, cudaMemcpyDeviceToHost, stream_));
+    Q3_CUDA(cudaStreamSynchronize(stream_));
+    for (int t = 0; t < rows; ++t) {
+        for (int g = 0; g < nk; ++g) {
+            const size_t e = ((static_cast<size_t>(t / kPageTokens) * nk + g) * kPageTokens +
+                              t % kPageTokens) * hd;
+            std::memcpy(k + (static_cast<size_t>(t) * nk + g) * hd, kp.data() + e, hd * 2);
+            std::memcpy(v + (static_cast<size_t>(t) * nk + g) * hd, vp.data() + e, hd * 2);
+        }
+    }
+}
+
+void Engine::write_cache(int l, const uint16_t* k, const uint16_t* v, int rows) {
+    const int hd = cfg_.head_dim, nk = cfg_.n_kv_heads;
+    const size_t n = static_cast<size_t>(n_pages_) * page_elems_;
+    std::vector<uint16_t> kp(n, 0), vp(n, 0);
+    for (int t = 0; t < rows; ++t) {
+        for (int g = 0; g < nk; ++g) {
+            const size_t e = ((static_cast<size_t>(t / kPageTokens) * nk + g) * kPageTokens +
+                              t % kPageTokens) * hd;
+            std::memcpy(kp.data() + e, k + (static_cast<size_t>(t) * nk + g) * hd, hd * 2);
+            std::memcpy(vp.data() + e, v + (static_cast<size_t>(t) * nk + g) * hd, hd * 2);
+        }
+    }
+    Q3_CUDA(cudaMemcpyAsync(k_layer(l), kp.data(), n * 2, cudaMemcpyHostToDevice, stream_));
+    Q3_CUDA(cudaMemcpyAsync(v_layer(l), vp.data(), n * 2, cudaMemcpyHostToDevice, stream_));
+    Q3_CUDA(cudaStreamSynchronize(stream_));
+}
+
+cudaGraphExec_t Engine::graph(int key, const std::function<void()>& enqueue) {
+    auto it = graphs_.find(key);
+    if (it != graphs_.end()) return it->second;
+    cudaGraph_t g = nullptr;
+    Q3_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeRelaxed));
+    try {
+        enqueue();
+    } catch (...) {
+        cudaStreamEndCapture(stream_, &g);
+        if (g) cudaGraphDestroy(g);
+        throw;
+    }
+    Q3_CUDA(cudaStreamEndCapture(stream_, &g));
+    cudaGraphExec_t ge = nullptr;
+    const cudaError_t e = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    Q3_CUDA(e);
+    graphs_[key] = ge;
+    return ge;
+}
+
+// ------------------------------------------------------------------ model
+
+namespace {
+
+size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
+
+}  // namespace
+
+Model::Model(const std::string& path, int ctx, int device) : file_(path) {
+    cfg_ = file_.config();
+    // InitializeInference (src/inference.cpp:529-581).
+    if (ctx <= 0 || ctx > cfg_.max_seq_len) {
+        throw std::invalid_argument("Context length is outside the model's supported range");
+    }
+    cfg_.max_seq_len = ctx;
+    validate_kernel_limits(cfg_);
+    Q3_CUDA(cudaSetDevice(device));
+    device_ = device;
+
+    const q3_config& c = cfg_;
+    const size_t D = c.dim, H = c.hidden_dim, V = c.vocab_size, hd = c.head_dim;
+    const size_t qd = static_cast<size_t>(c.n_heads) * hd, kvd = static_cast<size_t>(c.n_kv_heads) * hd;
+    const auto& embed = file_.tensor("model.embed.weight");
+    const auto& norm = file_.tensor("model.norm.weight");
+    const ModelFile::Tensor* output = c.tie_word_embeddings ? nullptr : &file_.tensor("model.output.weight");
+    if (embed.byte_size != V * D * 2 || norm.byte_size != D * 2 ||
+        (output && output->byte_size != V * D * 2)) {
+        throw std::runtime_error("Invalid embedding, final norm, or output tensor shape");
+    }
+    // Arena layout: embed | output? | final_norm | per layer: attn_norm q_norm k_norm
+    // [wq;wk;wv] wo mlp_norm w1 w3 w2 - every block 256-byte aligned, wq/wk/wv back to back.
+    struct Piece {
+        const ModelFile::Tensor* t;
+        size_t expect;
+        size_t off;
+    };
+    std::vector<Piece> pieces;
+    size_t off = 0;
+    auto place = [&](const ModelFile::Tensor& t, size_t expect_elems, bool pad = true) {
+        pieces.push_back({&t, expect_elems, off});
+        off += expect_elems * 2;
+        if (pad) off = align256(off);
+        return pieces.back().off;
+    };
+    const size_t embed_off = place(embed, V * D);
+    const size_t output_off = output ? place(*output, V * D) : embed_off;
+    const size_t norm_off = place(norm, D);
+    std::vector<std::array<size_t, 10>> loffs(c.n_layers);
+    for (int l = 0; l < c.n_layers; ++l) {
+        const std::string p = "model.layers." + std::to_string(l) + ".";
+        const auto& t_an = file_.tensor(p + "attn.norm.weight");
+        const auto& t_qn = file_.tensor(p + "attn.q_norm.weight");
+        const auto& t_kn = file_.tensor(p + "attn.k_norm.weight");
+        const auto& t_wq = file_.tensor(p + "attn.wq.weight");
+        const auto& t_wk = file_.tensor(p + "attn.wk.weight");
+        const auto& t_wv = file_.tensor(p + "attn.wv.weight");
+        const auto& t_wo = file_.tensor(p + "attn.wo.weight");
+        const auto& t_mn = file_.tensor(p + "mlp.norm.weight");
+        const auto& t_w1 = file_.tensor(p + "mlp.w1.weight");
+        const auto& t_w2 = file_.tensor(p + "mlp.w2.weight");
+        const auto& t_w3 = file_.tensor(p + "mlp.w3.weight");
+        // Block::ValidateWeights (src/inference.cpp:737-764).
+        auto require = [](const ModelFile::Tensor& t, size_t expected, const char* name) {
+            if (t.byte_size / 2 != expected) {
+                throw std::invalid_argument(std::string("Invalid ") + name + " size: expected " +
+                                            std::to_string(expected) + ", got " +
+                                            std::to_string(t.byte_size / 2));
+            }
+        };
+        require(t_an, D, "attn_norm");
+        require(t_qn, hd, "q_norm");
+        require(t_kn, hd, "k_norm");
+        require(t_wq, qd * D, "wq");
+        require(t_wk, kvd * D, "wk");
+        require(t_wv, kvd * D, "wv");
+        require(t_wo, D * qd, "wo");
+        require(t_mn, D, "mlp_norm");
+        require(t_w1, H * D, "w1");
+        require(t_w2, D * H, "w2");
+        require(t_w3, H * D, "w3");
+        auto& lo = loffs[l];
+        lo[0] = place(t_an, D);
+        lo[1] = place(t_qn, hd);
+        lo[2] = place(t_kn, hd);
+        lo[3] = place(t_wq, qd * D, false);
+        place(t_wk, kvd * D, false);
+        place(t_wv, kvd * D);
+        lo[4] = place(t_wo, D * qd);
+        lo[5] = place(t_mn, D);
+        lo[6] = place(t_w1, H * D);
+        lo[7] = place(t_w3, H * D);
+        lo[8] = place(t_w2, D * H);
+    }
+    arena_.alloc(off);
+    // Upload through two pinned staging buffers so file reads overlap the copies.
+    {
+        const size_t kChunk = 64u << 20;
+        PinnedBuffer stage[2];
+        stage[0].ensure(kChunk);
+        stage[1].ensure(kChunk);
+        cudaEvent_t done[2];
+        Q3_CUDA(cudaEventCreateWithFlags(&done[0], cudaEventDisableTiming));
+        Q3_CUDA(cudaEventCreateWithFlags(&done[1], cudaEventDisableTiming));
+        cudaStream_t s;
+        Q3_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+        int which = 0;
+        bool used[2] = {false, false};
+        for (const Piece& p : pieces) {
+            const uint8_t* src = file_.data() + p.t->offset;
+            uint8_t* dst = static_cast<uint8_t*>(arena_.ptr) + p.off;
+            size_t left = p.t->byte_size;
+            while (left > 0) {
+                const size_t n = std::min(left, kChunk);
+                if (used[which]) Q3_CUDA(cudaEventSynchronize(done[which]));
+                std::memcpy(stage[which].ptr, src, n);
+                Q3_CUDA(cudaMemcpyAsync(dst, stage[which].ptr, n, cudaMemcpyHostToDevice, s));
+                Q3_CUDA(cudaEventRecord(done[which], s));
+                used[which] = true;
+                which ^= 1;
+                src += n;
+                dst += n;
+                left -= n;
+            }
+        }
+        Q3_CUDA(cudaStreamSynchronize(s));
+        cudaEventDestroy(done[0]);
+        cudaEventDestroy(done[1]);
+        cudaStreamDestroy(s);
+    }
+    const uint16_t* base = static_cast<const uint16_t*>(arena_.ptr);
+    embed_ = base + embed_off / 2;
+    output_ = base + output_off / 2;
+    final_norm_ = base + norm_off / 2;
+    layers_.resize(c.n_layers);
+    for (int l = 0; l < c.n_layers; ++l) {
+        auto& lo = loffs[l];
+        LayerWeights& w = layers_[l];
+        w.attn_norm = base + lo[0] / 2;
+        w.q_norm = base + lo[1] / 2;
+        w.k_norm = base + lo[2] / 2;
+        w.wqkv = base + lo[3] / 2;
+        w.wo = base + lo[4] / 2;
+        w.mlp_norm = base + lo[5] / 2;
+        w.w1 = base + lo[6] / 2;
+        w.w3 = base + lo[7] / 2;
+        w.w2 = base + lo[8] / 2;
+    }
+    tensor_count_ = static_cast<int>(file_.tensor_count());
+
+    engine_ = std::make_unique<Engine>(cfg_, c.n_layers, device_, ctx);
+    logits_.alloc(V * 4);
+    argmax_part_.alloc(static_cast<size_t>(gemv_grid(c.vocab_size)) * sizeof(float2));
+    argmax_out_.alloc(16);
+    ensure_logs(1024);
+}
+
+Model::~Model() {
+    engine_.reset();
+}
+
+void Model::ensure_logs(int n) {
+    if (n <= log_cap_) return;
+    int cap = log_cap_ > 0 ? log_cap_ : 1024;
+    while (cap < n + 1) cap *= 2;
+    token_log_.alloc(static_cast<size_t>(cap) * 4);
+    forced_.alloc(static_cast<size_t>(cap) * 4);
+    log_cap_ = cap;
+    engine_->drop_graphs();
+}
+
+// The whole step: embedding, every layer, final norm, tied lm_head, greedy argmax and the
+// device-side advance (ForwardToken, src/inference.cpp:592-637, plus Greedy :703-709).
+void Model::enqueue_step(bool forced, bool taps) {
+    const q3_config& c = cfg_;
+    Engine& e = *engine_;
+    cudaStream_t s = e.stream();
+    StepParams* sp = e.step_params();
+    float* x = e.x();
+    launch_embed(sp, embed_, x, c.dim, s);
+    if (taps) Q3_CUDA(cudaMemcpyAsync(e.taps(), x, c.dim * 4, cudaMemcpyDeviceToDevice, s));
+    for (int l = 0; l < c.n_layers; ++l) {
+        e.enqueue_layer(l, layers_[l]);
+        if (taps) {
+            Q3_CUDA(cudaMemcpyAsync(e.taps() + static_cast<size_t>(l + 1) * c.dim, x, c.dim * 4,
+                                    cudaMemcpyDeviceToDevice, s));
+        }
+    }
+    const int grid = gemv_grid(c.vocab_size);
+    launch_gemv(kEpiStore, output_, nullptr, x, final_norm_, c.norm_eps,
+                static_cast<float*>(logits_.ptr), nullptr, c.vocab_size, c.dim,
+                static_cast<float2*>(argmax_part_.ptr), grid, s);
+    launch_argmax_final(static_cast<const float2*>(argmax_part_.ptr), grid,
+                        static_cast<int32_t*>(argmax_out_.ptr), sp,
+                        static_cast<int32_t*>(token_log_.ptr), c.max_seq_len,
+                        forced ? static_cast<const int32_t*>(forced_.ptr) : nullptr, s);
+}
+
+void Model::run_steps(int n, bool forced, bool taps, float* logits_log_dev) {
+    Engine& e = *engine_;
+    const int key = (forced ? 1 : 0) | (taps ? 2 : 0);
+    cudaGraphExec_t g = e.graph(key, [&] { enqueue_step(forced, taps); });
+    for (int i = 0; i < n; ++i) {
+        Q3_CUDA(cudaGraphLaunch(g, e.stream()));
+        if (logits_log_dev) {
+            Q3_CUDA(cudaMemcpyAsync(logits_log_dev + static_cast<size_t>(i) * cfg_.vocab_size,
+                                    logits_.ptr, static_cast<size_t>(cfg_.vocab_size) * 4,
+                                    cudaMemcpyDeviceToDevice, e.stream()));
+        }
+    }
+}
+
+StepParams Model::start_params(int32_t token, int pos, int n_forced) const {
+    StepParams p{};
+    p.token = token;
+    p.pos = pos;
+    step_positions(pos, cfg_.max_seq_len, &p.num_sink, &p.kv_pos, &p.kv_len);
+    p.step = 0;
+    p.n_forced = n_forced;
+    return p;
+}
+
+void Model::check_token_pos(int32_t token, int pos) const {
+    // Range checks of ForwardToken (src/inference.cpp:594-599).
+    if (token < 0 || token >= cfg_.vocab_size) {
+        throw std::out_of_range("Token id is outside the vocabulary");
+    }
+    if (pos < 0) throw std::out_of_range("Token position must not be negative");
+}
+
+void Model::forward_token(int32_t token, int pos, float* hidden_host, float* logits_host) {
+    check_token_pos(token, pos);
+    Engine& e = *engine_;
+    e.ensure_rope(pos + 2);
+    e.write_step(start_params(token, pos, 0));
+    run_steps(1, false, hidden_host != nullptr, nullptr);
+    cudaStream_t s = e.stream();
+    if (hidden_host) {
+        Q3_CUDA(cudaMemcpyAsync(hidden_host, e.taps(),
+                                static_cast<size_t>(cfg_.n_layers + 1) * cfg_.dim * 4,
+                                cudaMemcpyDeviceToHost, s));
+    }
+    if (logits_host) {
+        Q3_CUDA(cudaMemcpyAsync(logits_host, logits_.ptr, static_cast<size_t>(cfg_.vocab_size) * 4,
+                                cudaMemcpyDeviceToHost, s));
+    }
+    Q3_CUDA(cudaStreamSynchronize(s));
+}
+
+void Model::decode_loop(const int32_t* forced_host, int n, int32_t first_token, int pos0,
+                        int32_t* out_tokens_host, float* last_logits_host,
+                        float* all_logits_host) {
+    if (n <= 0) return;
+    if (forced_host) {
+        for (int i = 0; i < n; ++i) check_token_pos(forced_host[i], pos0 + i);
+    } else {
+        check_token_pos(first_token, pos0);
+    }
+    if (pos0 > std::numeric_limits<int>::max() - n) {
+        throw std::out_of_range("Token position must not be negative");
+    }
+    Engine& e = *engine_;
+    ensure_logs(n);
+    e.ensure_rope(pos0 + n + 1);
+    cudaStream_t s = e.stream();
+    if (forced_host) {
+        Q3_CUDA(cudaStreamSynchronize(s));
+        pinned_io_.ensure(static_cast<size_t>(n) * 4);
+        std::memcpy(pinned_io_.ptr, forced_host, static_cast<size_t>(n) * 4);
+        Q3_CUDA(cudaMemcpyAsync(forced_.ptr, pinned_io_.ptr, static_cast<size_t>(n) * 4,
+                                cudaMemcpyHostToDevice, s));
+    }
+    e.write_step(start_params(forced_host ? forced_host[0] : first_token, pos0,
+                              forced_host ? n : 0));
+    DeviceBuffer all;
+    if (all_logits_host) all.alloc(static_cast<size_t>(n) * cfg_.vocab_size * 4);
+    run_steps(n, forced_host != nullptr, false, static_cast<float*>(all.ptr));
+    if (out_tokens_host) {
+        Q3_CUDA(cudaMemcpyAsync(out_tokens_host, token_log_.ptr, static_cast<size_t>(n) * 4,
+                                cudaMemcpyDeviceToHost, s));
+    }
+    if (last_logits_host) {
+        Q3_CUDA(cudaMemcpyAsync(last_logits_host, logits_.ptr,
+                                static_cast<size_t>(cfg_.vocab_size) * 4, cudaMemcpyDeviceToHost, s));
+    }
+    if (all_logits_host) {
+        Q3_CUDA(cudaMemcpyAsync(all_logits_host, all.ptr, all.bytes, cudaMemcpyDeviceToHost, s));
+    }
+    Q3_CUDA(cudaStreamSynchronize(s));
+}
+
+void Model::prefill(const int32_t* ids, int n, int pos0, float* last_logits, int32_t* next) {
+    if (n <= 0) throw std::invalid_argument("Prefill needs at least one token");
+    std::vector<int32_t> argmax(n);
+    decode_loop(ids, n, 0, pos0, argmax.data(), last_logits, nullptr);
+    if (next) *next = argmax[n - 1];
+}
+
+// Qwen3::Generate on token IDs (src/inference.cpp:639-700). The reference feeds every generated
+// token through ForwardToken, including the last one, so max_new tokens cost max_new forwards.
+// Without stop_on_eos the decode loop runs on the device in one go; with it, in chunks that are
+// scanned for EOS on the host (steps past EOS only touch KV rows that a later call rewrites
+// before reading, since each step writes its own row before attending).
+void Model::generate(const int32_t* prompt, int n_prompt, size_t max_new, bool stop_on_eos,
+                     int32_t* out, size_t* n_out, q3_generation_stats* stats) {
+    std::vector<int32_t> ids(prompt, prompt + n_prompt);
+    if (ids.empty()) ids.push_back(cfg_.bos_token_id);
+    if (max_new > static_cast<size_t>(std::numeric_limits<int>::max() - ids.size())) {
+        throw std::invalid_argument("max_new_tokens is too large");
+    }
+    q3_generation_stats st{};
+    st.prompt_tokens = ids.size();
+    using clock = std::chrono::steady_clock;
+    const auto t0 = clock::now();
+    int32_t next = 0;
+    prefill(ids.data(), static_cast<int>(ids.size()), 0, nullptr, &next);
+    const auto t1 = clock::now();
+    size_t produced = 0;
+    int pos = static_cast<int>(ids.size());
+    const size_t chunk = stop_on_eos ? 16 : (max_new > 0 ? max_new : 1);
+    std::vector<int32_t> log;
+    while (produced < max_new) {
+        if (stop_on_eos && next == cfg_.eos_token_id) {
+            st.stopped_on_eos = 1;
+            break;
+        }
+        const int n = static_cast<int>(std::min(chunk, max_new - produced));
+        log.assign(n, 0);
+        decode_loop(nullptr, n, next, pos, log.data(), nullptr, nullptr);
+        // Tokens of this chunk: next, then log[0..n-2]; log[n-1] is the next chunk's first.
+        bool eos = false;
+        for (int i = 0; i < n; ++i) {
+            const int32_t t = i == 0 ? next : log[i - 1];
+            if (stop_on_eos && t == cfg_.eos_token_id) {
+                eos = true;
+                break;
+            }
+            out[produced++] = t;
+        }
+        if (eos) {
+            st.stopped_on_eos = 1;
+            break;
+        }
+        next = log[n - 1];
+        pos += n;
+    }
+    const auto t2 = clock::now();
+    st.generated_tokens = produced;
+    st.reached_token_limit = !st.stopped_on_eos && produced == max_new;
+    st.prefill_seconds = std::chrono::duration<double>(t1 - t0).count();
+    st.decode_seconds = std::chrono::duration<double>(t2 - t1).count();
+    if (n_out) *n_out = produced;
+    if (stats) *stats = st;
+}
+
+void Model::reset() {
+    engine_->reset_cache();
+}
+
+void Model::kv_row(int layer, int kv_pos, uint16_t* k, uint16_t* v) {
+    if (layer < 0 || layer >= cfg_.n_layers || kv_pos < 0 || kv_pos >= cfg_.max_seq_len) {
+        throw std::out_of_range("KV row is outside the cache");
+    }
+    engine_->read_kv_row(layer, kv_pos, k, v);
+}
+
+// ------------------------------------------------------------------ block
+
+Block::Block(const q3_config& cfg, const uint16_t* const* w, const size_t* counts, int device)
+    : cfg_(cfg) {
+    validate_config(cfg_);
+    validate_kernel_limits(cfg_);
+    const size_t D = cfg.dim, H = cfg.hidden_dim, hd = cfg.head_dim;
+    const size_t qd = static_cast<size_t>(cfg.n_heads) * hd, kvd = static_cast<size_t>(cfg.n_kv_heads) * hd;
+    const size_t sizes[11] = {D, hd, hd, qd * D, kvd * D, kvd * D, D * qd, D, H * D, D * H, H * D};
+    const char* names[11] = {"attn_norm", "q_norm", "k_norm", "wq", "wk", "wv",
+                             "wo", "mlp_norm", "w1", "w2", "w3"};
+    if (counts) {
+        for (int i = 0; i < 11; ++i) {
+            if (counts[i] != sizes[i]) {
+                throw std::invalid_argument(std::string("Invalid ") + names[i] +
+                                            " size: expected " + std::to_string(sizes[i]) +
+                                            ", got " + std::to_string(counts[i]));
+            }
+        }
+    }
+    for (int i = 0; i < 11; ++i) {
+        if (!w[i] && sizes[i]) throw std::invalid_argument("Block weight pointer must not be null");
+    }
+    Q3_CUDA(cudaSetDevice(device));
+    // Same arena order as a model layer: norms | [wq;wk;wv] | wo | mlp_norm | w1 | w3 | w2.
+    const int order[11] = {0, 1, 2, 3, 4, 5, 6, 7, 8, 10, 9};
+    size_t offs[11];
+    size_t off = 0;
+    for (int j = 0; j < 11; ++j) {
+        const int i = order[j];
+        offs[i] = off;
+        off += sizes[i] * 2;
+        const bool stack = (i == 3 || i == 4);  // keep wq|wk|wv contiguous
+        if (!stack) off = align256(off);
+    }
+    arena_.alloc(off);
+    for (int i = 0; i < 11; ++i) {
+        Q3_CUDA(cudaMemcpy(static_cast<uint8_t*>(arena_.ptr) + offs[i], w[i], sizes[i] * 2,
+                           cudaMemcpyHostToDevice));
+    }
+    const uint16_t* base = static_cast<const uint16_t*>(arena_.ptr);
+    lw_.attn_norm = base + offs[0] / 2;
+    lw_.q_norm = base + offs[1] / 2;
+    lw_.k_norm = base + offs[2] / 2;
+    lw_.wqkv = base + offs[3] / 2;
+    lw_.wo = base + offs[6] / 2;
+    lw_.mlp_norm = base + offs[7] / 2;
+    lw_.w1 = base + offs[8] / 2;
+    lw_.w2 = base + offs[9] / 2;
+    lw_.w3 = base + offs[10] / 2;
+    engine_ = std::make_unique<Engine>(cfg_, 1, device, cfg.max_seq_len);
+}
+
+Block::~Block() { engine_.reset(); }
+
+void Block::forward(float* x_host, int pos, int num_sink, int kv_pos, int kv_len) {
+    if (!x_host) throw std::invalid_argument("Block input must not be null");
+    const q3_config& c = cfg_;
+    // Range checks of Block::forward (src/inference.cpp:786-790).
+    if (pos < 0 || kv_len <= 0 || kv_len > c.max_seq_len || kv_pos < 0 || kv_pos >= kv_len ||
+        num_sink < 0 || num_sink > kv_len || num_sink >= c.max_seq_len || kv_pos < num_sink) {
+        throw std::out_of_range("Invalid position or KV-cache range");
+    }
+    Engine& e = *engine_;
+    e.ensure_rope(pos + 2);
+    StepParams p{};
+    p.pos = pos;
+    p.num_sink = num_sink;
+    p.kv_pos = kv_pos;
+    p.kv_len = kv_len;
+    e.write_step(p);
+    cudaStream_t s = e.stream();
+    Q3_CUDA(cudaMemcpyAsync(e.x(), x_host, c.dim * 4, cudaMemcpyHostToDevice, s));
+    e.enqueue_layer(0, lw_);
+    Q3_CUDA(cudaMemcpyAsync(x_host, e.x(), c.dim * 4, cudaMemcpyDeviceToHost, s));
+    Q3_CUDA(cudaStreamSynchronize(s));
+}
+
+}  // namespace q3
+
+// ==================================================================== C ABI
+
+using q3::guard;
+
+struct q3_model {
+    std::unique_ptr<q3::Model> m;
+};
+struct q3_block {
+    std::unique_ptr<q3::Block> b;
+};
+
+extern "C" {
+
+const char* q3_last_error(void) { return q3::g_last_error.c_str(); }
+const char* q3_version(void) { return "q3_b200 0.1 (sm_100a)"; }
+
+q3_status q3_model_load(const char* path, int context_length, int device, q3_model** out) {
+    return guard([&] {
+        if (!path || !out) throw std::invalid_argument("null argument");
+        auto h = std::make_unique<q3_model>();
+        h->m = std::make_unique<q3::Model>(path, context_length, device);
+        *out = h.release();
+    });
+}
+
+void q3_model_free(q3_model* model) { delete model; }
+
+q3_status q3_model_config(const q3_model* model, q3_config* out) {
+    return guard([&] {
+        if (!model || !out) throw std::invalid_argument("null argument");
+        *out = model->m->config();
+    });
+}
+
+q3_status q3_model_tensor_count(const q3_model* model, int* out) {
+    return guard([&] {
+        if (!model || !out) throw std::invalid_argument("null argument");
+        *out = model->m->tensor_count();
+    });
+}
+
+q3_status q3_reset(q3_model* model) {
+    return guard([&] {
+        if (!model) throw std::invalid_argument("null argument");
+        model->m->reset();
+    });
+}
+
+q3_status q3_forward_token(q3_model* model, int32_t token, int pos, float* logits_host) {
+    return guard([&] {
+        if (!model) throw std::invalid_argument("null argument");
+        model->m->forward_token(token, pos, nullptr, logits_host);
+    });
+}
+
+q3_status q3_forward_token_layers(q3_model* model, int32_t token, int pos, float* hidden_host,
+                                  float* logits_host) {
+    return guard([&] {
+        if (!model) throw std::invalid_argument("null argument");
+        model->m->forward_token(token, pos, hidden_host, logits_host);
+    });
+}
+
+q3_status q3_kv_row(q3_model* model, int layer, int kv_pos, uint16_t* k_host, uint16_t* v_host) {
+    return guard([&] {
+        if (!model || !k_host || !v_host) throw std::invalid_argument("null argument");
+        model->m->kv_row(layer, kv_pos, k_host, v_host);
+    });
+}
+
+q3_status q3_prefill(q3_model* model, const int32_t* ids_host, int n, int pos0,
+                     float* last_logits_host, int32_t* next_token_host) {
+    return guard([&] {
+        if (!model || !ids_host) throw std::invalid_argument("null argument");
+        model->m->prefill(ids_host, n, pos0, last_logits_host, next_token_host);
+    });
+}
+
+q3_status q3_decode_greedy(q3_model* model, int32_t first_token, int pos0, int n_steps,
+                           int32_t* tokens_host, float* last_logits_host) {
+    return guard([&] {
+        if (!model) throw std::invalid_argument("null argument");
+        if (n_steps < 0) throw std::invalid_argument("n_steps must not be negative");
+        model->m->decode_loop(nullptr, n_steps, first_token, pos0, tokens_host, last_logits_host,
+                              nullptr);
+    });
+}
+
+q3_status q3_decode_forced(q3_model* model, const int32_t* tokens_host, int n, int pos0,
+                           int32_t* argmax_host, float* logits_host) {
+    return guard([&] {
+        if (!model || (!tokens_host && n > 0)) throw std::invalid_argument("null argument");
+        model->m->decode_loop(tokens_host, n, 0, pos0, argmax_host, nullptr, logits_host);
+    });
+}
+
+q3_status q3_generate(q3_model* model, const int32_t* prompt_host, int n_prompt,
+                      size_t max_new_tokens, int stop_on_eos, int32_t* out_tokens_host,
+                      size_t* n_out, q3_generation_stats* stats) {
+    return guard([&] {
+        if (!model || (n_prompt > 0 && !prompt_host) || (max_new_tokens > 0 && !out_tokens_host)) {
+            throw std::invalid_argument("null argument");
+        }
+        if (n_prompt < 0) throw std::invalid_argument("n_prompt must not be negative");
+        model->m->generate(prompt_host, n_prompt, max_new_tokens, stop_on_eos != 0,
+                           out_tokens_host, n_out, stats);
+    });
+}
+
+q3_status q3_model_stream(q3_model* model, void** stream) {
+    return guard([&] {
+        if (!model || !stream) throw std::invalid_argument("null argument");
+        *stream = model->m->stream();
+    });
+}
+
+q3_status q3_block_create(const q3_config* cfg, const uint16_t* const* weights_host,
+                          const size_t* counts, int device, q3_block** out) {
+    return guard([&] {
+        if (!cfg || !weights_host || !out) throw std::invalid_argument("null argument");
+        auto h = std::make_unique<q3_block>();
+        h->b = std::make_unique<q3::Block>(*cfg, weights_host, counts, device);
+        *out = h.release();
+    });
+}
+
+void q3_block_free(q3_block* block) { delete block; }
+
+q3_status q3_block_forward(q3_block* block, float* x_host, int pos, int num_sink, int kv_pos,
+                           int kv_len) {
+    return guard([&] {
+        if (!block) throw std::invalid_argument("null argument");
+        block->b->forward(x_host, pos, num_sink, kv_pos, kv_len);
+    });
+}
+
+q3_status q3_block_reset_cache(q3_block* block) {
+    return guard([&] {
+        if (!block) throw std::invalid_argument("null argument");
+        block->b->engine().reset_cache();
+    });
+}
+
+q3_status q3_block_get_cache(q3_block* block, uint16_t* k_host, uint16_t* v_host) {
+    return guard([&] {
+        if (!block || !k_host || !v_host) throw std::invalid_argument("null argument");
+        block->b->engine().read_cache(0, k_host, v_host, block->b->config().max_seq_len);
+    });
+}
+
+q3_status q3_block_set_cache(q3_block* block, const uint16_t* k_host, const uint16_t* v_host) {
+    return guard([&] {
+        if (!block || !k_host || !v_host) throw std::invalid_argument("null argument");
+        block->b->engine().write_cache(0, k_host, v_host, block->b->config().max_seq_len);
+    });
+}
+
+// ------------------------------------------------------------------ free kernels
+
+q3_status q3_rmsnorm(float* out, const float* x, const uint16_t* w, float eps, int n,
+                     void* stream) {
+    return guard([&] {
+        if (!out || !x || !w || n <= 0) throw std::invalid_argument("invalid RmsNorm arguments");
+        q3::launch_rmsnorm(out, x, w, eps, n, static_cast<cudaStream_t>(stream));
+    });
+}
+
+q3_status q3_softmax(float* out, const float* x, int n, void* stream) {
+    return guard([&] {
+        if (!out || !x || n <= 0) throw std::invalid_argument("invalid Softmax arguments");
+        q3::launch_softmax(out, x, n, static_cast<cudaStream_t>(stream));
+    });
+}
+
+q3_status q3_matmul(float* out, const float* x, const uint16_t* w, int n, int m, void* stream) {
+    return guard([&] {
+        if (!out || !x || !w || n <= 0 || m <= 0) throw std::invalid_argument("invalid MatMul arguments");
+        q3::launch_gemv(q3::kEpiStore, w, nullptr, x, nullptr, 0.0f, out, nullptr, n, m, nullptr,
+                        0, static_cast<cudaStream_t>(stream));
+    });
+}
+
+q3_status q3_rope(float* x, int d, int head_dim, int pos, float theta, int rotary_dim,
+                  void* stream) {
+    return guard([&] {
+        if (!x || d <= 0 || head_dim <= 0 || d % head_dim != 0 || rotary_dim < 0 ||
+            rotary_dim % 2 != 0 || rotary_dim > head_dim || rotary_dim > 512) {
+            throw std::invalid_argument("invalid ApplyRotaryEmb arguments");
+        }
+        q3::RopeRow row{};
+        const int half = rotary_dim / 2;
+        for (int i = 0; i < half; ++i) {
+            const float freq = 1.0f / powf(theta, 2.0f * i / rotary_dim);
+            const float angle = pos * freq;
+            row.c[i] = cosf(angle);
+            row.s[i] = sinf(angle);
+        }
+        q3::launch_rope_row(x, d, head_dim, rotary_dim, row, static_cast<cudaStream_t>(stream));
+    });
+}
+
+q3_status q3_ffn(float* out, float* lin1, float* lin2, const float* x, const uint16_t* w1,
+                 const uint16_t* w2, const uint16_t* w3, int hidden_dim, int dim, void* stream) {
+    return guard([&] {
+        if (!out || !lin1 || !x || !w1 || !w2 || !w3 || hidden_dim <= 0 || dim <= 0) {
+            throw std::invalid_argument("invalid FeedForwardNetwork arguments");
+        }
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        q3::launch_gemv(q3::kEpiSiluMul, w1, w3, x, nullptr, 0.0f, lin1, lin2, hidden_dim, dim,
+                        nullptr, 0, s);
+        q3::launch_gemv(q3::kEpiStore, w2, nullptr, lin1, nullptr, 0.0f, out, nullptr, dim,
+                        hidden_dim, nullptr, 0, s);
+    });
+}
+
+size_t q3_attn_workspace_size(int head_dim, int kv_len) {
+    if (head_dim <= 0 || kv_len <= 0) return 0;
+    const size_t S = static_cast<size_t>(q3::attn_splits_for(kv_len));
+    return S * head_dim * 4 + 256 + S * sizeof(float2);
+}
+
+q3_status q3_attn(float* out, void* workspace, const float* q, const uint16_t* k,
+                  const uint16_t* v, int head_dim, int n_kv_heads, int kv_len, void* stream) {
+    return guard([&] {
+        if (!out || !workspace || !q || !k || !v || head_dim <= 0 || head_dim > 256 ||
+            n_kv_heads <= 0 || kv_len <= 0) {
+            throw std::invalid_argument("invalid FastAttn arguments");
+        }
+        const int S = q3::attn_splits_for(kv_len);
+        q3::AttnArgs a{};
+        a.q = q;
+        a.k = k;
+        a.v = v;
+        a.page_table = nullptr;
+        a.sp = nullptr;
+        a.kv_len_const = kv_len;
+        a.n_heads = 1;
+        a.n_kv = 1;
+        a.hd = head_dim;
+        a.row_stride = n_kv_heads * head_dim;
+        a.n_splits = S;
+        a.part_o = static_cast<float*>(workspace);
+        const size_t o_bytes = (static_cast<size_t>(S) * head_dim * 4 + 255) & ~size_t(255);
+        a.part_ml = reinterpret_cast<float2*>(static_cast<uint8_t*>(workspace) + o_bytes);
+        a.out = out;
+        q3::launch_attention(a, static_cast<cudaStream_t>(stream));
+    });
+}
+
+q3_status q3_greedy(const float* logits, int n, int32_t* out_index, void* stream) {
+    return guard([&] {
+        if (n <= 0) throw std::invalid_argument("Cannot sample empty logits");
+        if (!logits || !out_index) throw std::invalid_argument("null argument");
+        q3::launch_argmax_full(logits, n, out_index, static_cast<cudaStream_t>(stream));
+    });
+}
+
+}  // extern "C"

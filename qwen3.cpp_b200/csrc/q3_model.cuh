@@ -1,0 +1,199 @@
+// Host-side classes of the B200 Qwen3 library (behind the C ABI of include/q3_b200.h).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <array>
+#include <functional>
+#include <map>
+#include <memory>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "q3_b200.h"
+#include "q3_common.cuh"
+
+namespace q3 {
+
+void validate_config(const q3_config& c);
+void validate_kernel_limits(const q3_config& c);
+
+// A parsed, memory-mapped Qwen3.bin (the layout of the reference's convert.py:2-20).
+class ModelFile {
+public:
+    struct Tensor {
+        std::string name;
+        uint32_t dtype = 0;
+        std::vector<uint64_t> shape;
+        size_t offset = 0;
+        size_t byte_size = 0;
+    };
+    explicit ModelFile(const std::string& path);
+    ~ModelFile();
+    ModelFile(const ModelFile&) = delete;
+    ModelFile& operator=(const ModelFile&) = delete;
+
+    const q3_config& config() const { return config_; }
+    const Tensor& tensor(const std::string& name) const;
+    size_t tensor_count() const { return tensors_.size(); }
+    const uint8_t* data() const { return data_; }
+
+private:
+    std::string path_;
+    int fd_ = -1;
+    const uint8_t* data_ = nullptr;
+    size_t size_ = 0;
+    q3_config config_{};
+    std::string arch_, dtype_, act_;
+    std::unordered_map<std::string, Tensor> tensors_;
+};
+
+struct DeviceBuffer {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+    DeviceBuffer() = default;
+    DeviceBuffer(const DeviceBuffer&) = delete;
+    DeviceBuffer& operator=(const DeviceBuffer&) = delete;
+    ~DeviceBuffer();
+    void alloc(size_t n);
+    void reset();
+};
+
+struct PinnedBuffer {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+    PinnedBuffer() = default;
+    PinnedBuffer(const PinnedBuffer&) = delete;
+    PinnedBuffer& operator=(const PinnedBuffer&) = delete;
+    ~PinnedBuffer();
+    void ensure(size_t n);
+};
+
+// Device pointers of one decoder layer inside a weight arena.
+struct LayerWeights {
+    const uint16_t* attn_norm = nullptr;
+    const uint16_t* q_norm = nullptr;
+    const uint16_t* k_norm = nullptr;
+    const uint16_t* wqkv = nullptr;  // [wq; wk; wv] rows, [q_dim + 2*kv_dim, dim]
+    const uint16_t* wo = nullptr;
+    const uint16_t* mlp_norm = nullptr;
+    const uint16_t* w1 = nullptr;
+    const uint16_t* w3 = nullptr;
+    const uint16_t* w2 = nullptr;
+};
+
+std::vector<float2> rope_table_host(float theta, int rotary_dim, int len);
+
+// Activations, KV cache (paged, 16-token pages) and per-step graphs for n_layers layers of one
+// sequence. The kernels of one decoder layer are enqueued by enqueue_layer.
+class Engine {
+public:
+    Engine(const q3_config& cfg, int n_layers, int device, int kv_slots);
+    ~Engine();
+    Engine(const Engine&) = delete;
+    Engine& operator=(const Engine&) = delete;
+
+    cudaStream_t stream() const { return stream_; }
+    StepParams* step_params() const { return static_cast<StepParams*>(sp_.ptr); }
+    float* x() const { return static_cast<float*>(x_.ptr); }
+    float* taps() const { return static_cast<float*>(taps_.ptr); }
+    uint16_t* k_layer(int l) const;
+    uint16_t* v_layer(int l) const;
+    const int32_t* page_table() const { return static_cast<const int32_t*>(page_table_.ptr); }
+    const float2* rope() const { return static_cast<const float2*>(rope_.ptr); }
+    int rope_len() const { return rope_len_; }
+    int n_pages() const { return n_pages_; }
+    int n_splits() const { return n_splits_; }
+
+    void ensure_rope(int needed_len);
+    void reset_cache();
+    void enqueue_layer(int l, const LayerWeights& w);
+    void write_step(const StepParams& p);
+    StepParams read_step();
+    void read_kv_row(int l, int slot, uint16_t* k, uint16_t* v);
+    void read_cache(int l, uint16_t* k, uint16_t* v, int rows);
+    void write_cache(int l, const uint16_t* k, const uint16_t* v, int rows);
+    cudaGraphExec_t graph(int key, const std::function<void()>& enqueue);
+    void drop_graphs();
+
+private:
+    q3_config cfg_;
+    int n_layers_;
+    int device_;
+    int kv_slots_;
+    int q_dim_ = 0, kv_dim_ = 0, n_pages_ = 0, n_splits_ = 1;
+    size_t page_elems_ = 0;
+    cudaStream_t stream_ = nullptr;
+    DeviceBuffer k_cache_, v_cache_, page_table_, sp_, x_, qkv_, att_, h_, part_o_, part_ml_,
+        taps_, rope_;
+    int rope_len_ = 0;
+    PinnedBuffer pinned_sp_;
+    std::map<int, cudaGraphExec_t> graphs_;
+};
+
+// class Qwen3 of the reference (include/inference.h:227-264) on one GPU.
+class Model {
+public:
+    Model(const std::string& path, int ctx, int device);
+    ~Model();
+
+    const q3_config& config() const { return cfg_; }
+    int tensor_count() const { return tensor_count_; }
+    cudaStream_t stream() const { return engine_->stream(); }
+    Engine& engine() { return *engine_; }
+    const LayerWeights& layer(int l) const { return layers_[l]; }
+    const uint16_t* embed() const { return embed_; }
+    const uint16_t* output() const { return output_; }
+    const uint16_t* final_norm() const { return final_norm_; }
+    float* logits() const { return static_cast<float*>(logits_.ptr); }
+
+    void reset();
+    void forward_token(int32_t token, int pos, float* hidden_host, float* logits_host);
+    void decode_loop(const int32_t* forced_host, int n, int32_t first_token, int pos0,
+                     int32_t* out_tokens_host, float* last_logits_host, float* all_logits_host);
+    void prefill(const int32_t* ids, int n, int pos0, float* last_logits, int32_t* next);
+    void generate(const int32_t* prompt, int n_prompt, size_t max_new, bool stop_on_eos,
+                  int32_t* out, size_t* n_out, q3_generation_stats* stats);
+    void kv_row(int layer, int kv_pos, uint16_t* k, uint16_t* v);
+
+private:
+    void check_token_pos(int32_t token, int pos) const;
+    StepParams start_params(int32_t token, int pos, int n_forced) const;
+    void ensure_logs(int n);
+    void enqueue_step(bool forced, bool taps);
+    void run_steps(int n, bool forced, bool taps, float* logits_log_dev);
+
+    ModelFile file_;
+    q3_config cfg_{};
+    int device_ = 0;
+    int tensor_count_ = 0;
+    DeviceBuffer arena_;
+    const uint16_t* embed_ = nullptr;
+    const uint16_t* output_ = nullptr;
+    const uint16_t* final_norm_ = nullptr;
+    std::vector<LayerWeights> layers_;
+    std::unique_ptr<Engine> engine_;
+    DeviceBuffer logits_, argmax_part_, argmax_out_, token_log_, forced_;
+    int log_cap_ = 0;
+    PinnedBuffer pinned_io_;
+};
+
+// class Block of the reference (include/inference.h:178-202) on one GPU.
+class Block {
+public:
+    Block(const q3_config& cfg, const uint16_t* const* w, const size_t* counts, int device);
+    ~Block();
+    void forward(float* x_host, int pos, int num_sink, int kv_pos, int kv_len);
+    Engine& engine() { return *engine_; }
+    const q3_config& config() const { return cfg_; }
+
+private:
+    q3_config cfg_{};
+    DeviceBuffer arena_;
+    LayerWeights lw_;
+    std::unique_ptr<Engine> engine_;
+};
+
+}  // namespace q3
