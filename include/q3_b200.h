@@ -117,6 +117,18 @@ q3_status q3_generate(q3_model* model, const int32_t* prompt_host, int n_prompt,
 /* Model-owned CUDA stream (cudaStream_t) for callers that order their own work against it. */
 q3_status q3_model_stream(q3_model* model, void** stream);
 
+/* Decode paths (no reference counterpart: the reference has one CPU path). FUSED is one
+ * persistent kernel per call that runs whole decode steps (Qwen3-0.6B shape only); LAYERWISE is
+ * a CUDA graph of per-layer kernels (any shape). Both run on the GPU; FUSED is the default when
+ * the model's shape allows it. */
+enum { Q3_PATH_LAYERWISE = 0, Q3_PATH_FUSED = 1 };
+q3_status q3_model_set_decode_path(q3_model* model, int path);
+q3_status q3_model_decode_path(const q3_model* model, int* path);
+/* Failure-path check of the fused kernel's bounded waits: runs one launch whose grid-wide wait
+ * can never be satisfied, with a ~10 ms bound, and reports in *timed_out whether the kernel
+ * returned with its timeout status set. The model stays usable afterwards. */
+q3_status q3_model_fused_timeout_selftest(q3_model* model, int* timed_out);
+
 /* ------------------------------------------------------------------ one block (class Block) */
 
 /* Block(config, weights) (src/inference.cpp:720-730) with BlockWeights

@@ -23,6 +23,7 @@
 #include <vector>
 
 #include "q3_common.cuh"
+#include "q3_decode_fused.cuh"
 #include "q3_kernels.cuh"
 #include "q3_model.cuh"
 
@@ -626,6 +627,97 @@ Model::Model(const std::string& path, int ctx, int device) : file_(path) {
     argmax_part_.alloc(static_cast<size_t>(gemv_grid(c.vocab_size)) * sizeof(float2));
     argmax_out_.alloc(16);
     ensure_logs(1024);
+
+    if (fused_supported(cfg_)) {
+        fused_grid_ = q3::fused_grid(device_);
+        if (fused_grid_ >= 8) {
+            fused_s_max_ = fused_grid_ / c.n_kv_heads;
+            fused_layers_.alloc(layers_.size() * sizeof(LayerWeights));
+            Q3_CUDA(cudaMemcpy(fused_layers_.ptr, layers_.data(), layers_.size() * sizeof(LayerWeights),
+                               cudaMemcpyHostToDevice));
+            fused_part_o_.alloc(static_cast<size_t>(c.n_heads) * fused_s_max_ * c.head_dim * 4);
+            fused_part_ml_.alloc(static_cast<size_t>(c.n_heads) * fused_s_max_ * sizeof(float2));
+            fused_am_.alloc(static_cast<size_t>(fused_grid_) * sizeof(float2));
+            fused_sync_.alloc(256);  // [0] arrival counter, [32] error word
+            Q3_CUDA(cudaMemset(fused_sync_.ptr, 0, 256));
+        } else {
+            fused_grid_ = 0;
+        }
+    }
+}
+
+void Model::launch_fused(int n_steps, bool forced, bool taps, long long spin_cycles, int offset) {
+    Engine& e = *engine_;
+    FusedArgs a{};
+    a.layers = static_cast<const LayerWeights*>(fused_layers_.ptr);
+    a.embed = embed_;
+    a.lm_head = output_;
+    a.final_norm = final_norm_;
+    a.k_cache = e.k_layer(0);
+    a.v_cache = e.v_layer(0);
+    a.layer_elems = e.layer_elems();
+    a.page_table = e.page_table();
+    a.rope = e.rope();
+    a.rope_len = e.rope_len();
+    a.x = e.x();
+    a.qkv = e.qkv();
+    a.h = e.h();
+    a.part_o = static_cast<float*>(fused_part_o_.ptr);
+    a.part_ml = static_cast<float2*>(fused_part_ml_.ptr);
+    a.am_part = static_cast<float2*>(fused_am_.ptr);
+    a.logits = static_cast<float*>(logits_.ptr);
+    a.taps = taps ? e.taps() : nullptr;
+    a.sp = e.step_params();
+    a.token_log = static_cast<int32_t*>(token_log_.ptr);
+    a.forced = forced ? static_cast<const int32_t*>(forced_.ptr) : nullptr;
+    a.bar = static_cast<unsigned*>(fused_sync_.ptr);
+    a.err = static_cast<unsigned*>(fused_sync_.ptr) + 32;
+    a.n_layers = cfg_.n_layers;
+    a.vocab = cfg_.vocab_size;
+    a.ctx = cfg_.max_seq_len;
+    a.n_steps = n_steps;
+    a.s_max = fused_s_max_;
+    a.eps = cfg_.norm_eps;
+    a.spin_cycles = spin_cycles;
+    a.barrier_offset = offset;
+    Q3_CUDA(cudaMemsetAsync(a.bar, 0, sizeof(unsigned), e.stream()));
+    launch_decode_fused(a, fused_grid_, e.stream());
+}
+
+void Model::clear_fused_error() {
+    if (!fused_enabled()) return;
+    Q3_CUDA(cudaMemsetAsync(static_cast<unsigned*>(fused_sync_.ptr) + 32, 0, sizeof(unsigned),
+                            engine_->stream()));
+}
+
+void Model::check_fused_error() {
+    if (!fused_enabled()) return;
+    unsigned err = 0;
+    Q3_CUDA(cudaMemcpyAsync(&err, static_cast<unsigned*>(fused_sync_.ptr) + 32, sizeof(unsigned),
+                            cudaMemcpyDeviceToHost, engine_->stream()));
+    Q3_CUDA(cudaStreamSynchronize(engine_->stream()));
+    if (err) {
+        throw DeviceTimeout("fused decode kernel: a bounded device-side wait gave up");
+    }
+}
+
+bool Model::fused_timeout_selftest() {
+    if (!fused_available()) throw std::runtime_error("fused decode path is not available");
+    Engine& e = *engine_;
+    e.ensure_rope(2);
+    e.write_step(start_params(0, 0, 0));
+    Q3_CUDA(cudaMemsetAsync(static_cast<unsigned*>(fused_sync_.ptr) + 32, 0, sizeof(unsigned),
+                            e.stream()));
+    // ~10 ms bound; barrier target one above what the grid can reach.
+    launch_fused(1, false, false, 20000000LL, 1);
+    unsigned err = 0;
+    Q3_CUDA(cudaMemcpyAsync(&err, static_cast<unsigned*>(fused_sync_.ptr) + 32, sizeof(unsigned),
+                            cudaMemcpyDeviceToHost, e.stream()));
+    Q3_CUDA(cudaStreamSynchronize(e.stream()));
+    Q3_CUDA(cudaMemsetAsync(static_cast<unsigned*>(fused_sync_.ptr) + 32, 0, sizeof(unsigned),
+                            e.stream()));
+    Q3_CUDA(cudaStreamSynchronize(e.stream()));
+    return err != 0;
 }
 
 Model::~Model() {
@@ -671,6 +763,25 @@ void Model::enqueue_step(bool forced, bool taps) {
 
 void Model::run_steps(int n, bool forced, bool taps, float* logits_log_dev) {
     Engine& e = *engine_;
+    if (fused_enabled()) {
+        constexpr long long kSpinCycles = 4000000000LL;  // ~2 s at the B200 boost clock
+        if (logits_log_dev || taps) {
+            for (int i = 0; i < n; ++i) {
+                launch_fused(1, forced, taps, kSpinCycles, 0);
+                if (logits_log_dev) {
+                    Q3_CUDA(cudaMemcpyAsync(logits_log_dev + static_cast<size_t>(i) * cfg_.vocab_size,
+                                            logits_.ptr, static_cast<size_t>(cfg_.vocab_size) * 4,
+                                            cudaMemcpyDeviceToDevice, e.stream()));
+                }
+            }
+        } else {
+            constexpr int kMaxStepsPerLaunch = 256;
+            for (int done = 0; done < n; done += kMaxStepsPerLaunch) {
+                launch_fused(std::min(kMaxStepsPerLaunch, n - done), forced, false, kSpinCycles, 0);
+            }
+        }
+        return;
+    }
     const int key = (forced ? 1 : 0) | (taps ? 2 : 0);
     cudaGraphExec_t g = e.graph(key, [&] { enqueue_step(forced, taps); });
     for (int i = 0; i < n; ++i) {
@@ -706,7 +817,9 @@ void Model::forward_token(int32_t token, int pos, float* hidden_host, float* log
     Engine& e = *engine_;
     e.ensure_rope(pos + 2);
     e.write_step(start_params(token, pos, 0));
+    clear_fused_error();
     run_steps(1, false, hidden_host != nullptr, nullptr);
+    check_fused_error();
     cudaStream_t s = e.stream();
     if (hidden_host) {
         Q3_CUDA(cudaMemcpyAsync(hidden_host, e.taps(),
@@ -747,7 +860,9 @@ void Model::decode_loop(const int32_t* forced_host, int n, int32_t first_token, 
                               forced_host ? n : 0));
     DeviceBuffer all;
     if (all_logits_host) all.alloc(static_cast<size_t>(n) * cfg_.vocab_size * 4);
+    clear_fused_error();
     run_steps(n, forced_host != nullptr, false, static_cast<float*>(all.ptr));
+    check_fused_error();
     if (out_tokens_host) {
         Q3_CUDA(cudaMemcpyAsync(out_tokens_host, token_log_.ptr, static_cast<size_t>(n) * 4,
                                 cudaMemcpyDeviceToHost, s));
@@ -1030,6 +1145,33 @@ q3_status q3_model_stream(q3_model* model, void** stream) {
     return guard([&] {
         if (!model || !stream) throw std::invalid_argument("null argument");
         *stream = model->m->stream();
+    });
+}
+
+q3_status q3_model_set_decode_path(q3_model* model, int path) {
+    return guard([&] {
+        if (!model) throw std::invalid_argument("null argument");
+        if (path != Q3_PATH_LAYERWISE && path != Q3_PATH_FUSED) {
+            throw std::invalid_argument("unknown decode path");
+        }
+        if (path == Q3_PATH_FUSED && !model->m->fused_available()) {
+            throw std::invalid_argument("the fused decode kernel does not serve this model");
+        }
+        model->m->set_fused(path == Q3_PATH_FUSED);
+    });
+}
+
+q3_status q3_model_decode_path(const q3_model* model, int* path) {
+    return guard([&] {
+        if (!model || !path) throw std::invalid_argument("null argument");
+        *path = model->m->fused_enabled() ? Q3_PATH_FUSED : Q3_PATH_LAYERWISE;
+    });
+}
+
+q3_status q3_model_fused_timeout_selftest(q3_model* model, int* timed_out) {
+    return guard([&] {
+        if (!model || !timed_out) throw std::invalid_argument("null argument");
+        *timed_out = model->m->fused_timeout_selftest() ? 1 : 0;
     });
 }
 

@@ -98,6 +98,9 @@ public:
     cudaStream_t stream() const { return stream_; }
     StepParams* step_params() const { return static_cast<StepParams*>(sp_.ptr); }
     float* x() const { return static_cast<float*>(x_.ptr); }
+    float* qkv() const { return static_cast<float*>(qkv_.ptr); }
+    float* h() const { return static_cast<float*>(h_.ptr); }
+    size_t layer_elems() const { return static_cast<size_t>(n_pages_) * page_elems_; }
     float* taps() const { return static_cast<float*>(taps_.ptr); }
     uint16_t* k_layer(int l) const;
     uint16_t* v_layer(int l) const;
@@ -158,12 +161,25 @@ public:
                   int32_t* out, size_t* n_out, q3_generation_stats* stats);
     void kv_row(int layer, int kv_pos, uint16_t* k, uint16_t* v);
 
+    // Decode path: the fused whole-step kernel when the config is the Qwen3-0.6B shape and the
+    // device can hold one CTA per SM, else the layer-wise kernels (both on the GPU).
+    bool fused_available() const { return fused_grid_ > 0; }
+    bool fused_enabled() const { return use_fused_ && fused_grid_ > 0; }
+    void set_fused(bool on) { use_fused_ = on; }
+    int fused_grid() const { return fused_grid_; }
+    // Runs one fused launch whose grid-wide waits can never complete, with a short bound, and
+    // reports whether the kernel returned with its timeout status set (failure-path test).
+    bool fused_timeout_selftest();
+
 private:
     void check_token_pos(int32_t token, int pos) const;
     StepParams start_params(int32_t token, int pos, int n_forced) const;
     void ensure_logs(int n);
     void enqueue_step(bool forced, bool taps);
     void run_steps(int n, bool forced, bool taps, float* logits_log_dev);
+    void launch_fused(int n_steps, bool forced, bool taps, long long spin_cycles, int offset);
+    void clear_fused_error();
+    void check_fused_error();
 
     ModelFile file_;
     q3_config cfg_{};
@@ -178,6 +194,11 @@ private:
     DeviceBuffer logits_, argmax_part_, argmax_out_, token_log_, forced_;
     int log_cap_ = 0;
     PinnedBuffer pinned_io_;
+    // Fused decode state.
+    int fused_grid_ = 0;
+    int fused_s_max_ = 0;
+    bool use_fused_ = true;
+    DeviceBuffer fused_layers_, fused_part_o_, fused_part_ml_, fused_am_, fused_sync_;
 };
 
 // class Block of the reference (include/inference.h:178-202) on one GPU.

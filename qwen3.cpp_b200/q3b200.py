@@ -102,6 +102,9 @@ def lib() -> C.CDLL:
         "q3_decode_forced": [vp, I32P, C.c_int, C.c_int, vp, vp],
         "q3_generate": [vp, vp, C.c_int, sz, C.c_int, vp, C.POINTER(sz), C.POINTER(GenStats)],
         "q3_model_stream": [vp, C.POINTER(vp)],
+        "q3_model_set_decode_path": [vp, C.c_int],
+        "q3_model_decode_path": [vp, C.POINTER(C.c_int)],
+        "q3_model_fused_timeout_selftest": [vp, C.POINTER(C.c_int)],
         "q3_block_create": [C.POINTER(Config), C.POINTER(vp), C.POINTER(sz), C.c_int, C.POINTER(vp)],
         "q3_block_forward": [vp, F32P, C.c_int, C.c_int, C.c_int, C.c_int],
         "q3_block_reset_cache": [vp],
@@ -176,6 +179,24 @@ class Qwen3:
     def reset(self) -> None:
         """ResetInference (src/inference.cpp:583-590)."""
         check(lib().q3_reset(self._h))
+
+    PATH_LAYERWISE = 0
+    PATH_FUSED = 1
+
+    @property
+    def decode_path(self) -> int:
+        p = C.c_int()
+        check(lib().q3_model_decode_path(self._h, C.byref(p)))
+        return p.value
+
+    @decode_path.setter
+    def decode_path(self, path: int) -> None:
+        check(lib().q3_model_set_decode_path(self._h, int(path)))
+
+    def fused_timeout_selftest(self) -> bool:
+        t = C.c_int()
+        check(lib().q3_model_fused_timeout_selftest(self._h, C.byref(t)))
+        return bool(t.value)
 
     def forward_token(self, token: int, pos: int) -> np.ndarray:
         """ForwardToken (src/inference.cpp:592-637): logits of one token."""
