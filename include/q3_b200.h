@@ -128,6 +128,12 @@ q3_status q3_model_decode_path(const q3_model* model, int* path);
  * can never be satisfied, with a ~10 ms bound, and reports in *timed_out whether the kernel
  * returned with its timeout status set. The model stays usable afterwards. */
 q3_status q3_model_fused_timeout_selftest(q3_model* model, int* timed_out);
+/* Instrumentation of the fused kernel (no reference counterpart): runs one decode step of
+ * `token` at `pos` and writes globaltimer nanosecond stamps [n_phases][grid][8] (0 phase entry,
+ * 1 phase start, 2-5 points inside the phase, 6 work done, 7 arrival; unset stamps are 0) to
+ * stamps_host (capacity in elements). */
+q3_status q3_model_fused_profile(q3_model* model, int32_t token, int pos, uint64_t* stamps_host,
+                                 size_t capacity, int* n_phases, int* grid);
 
 /* ------------------------------------------------------------------ one block (class Block) */
 

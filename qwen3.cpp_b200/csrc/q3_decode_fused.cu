@@ -4,23 +4,29 @@
 // is the reference's ForwardToken (asriva32/Qwen3.cpp src/inference.cpp:592-637) + Greedy
 // (:703-709): 28 x Block::forward (:766-866), final RmsNorm, tied lm_head, argmax.
 //
-// Dataflow. Decode at batch 1 streams 1.19 GB of bf16 weights per token, so the kernel is built
-// around one continuous weight stream per SM: a producer warp walks the fixed sequence of weight
-// row-chunks this CTA owns for the whole call (layer by layer: [wq;wk;wv], wo, w1|w3 pairs, w2,
-// then lm_head rows) and copies them with TMA bulk copies (cp.async.bulk, no multicast) into a
-// 32-slot shared-memory ring guarded by full/empty mbarriers. It never waits for activations, so
-// the stream runs ahead across the grid-wide dependencies. Eight consumer warps wait for the
-// activation vector of each phase (a monotonic arrival counter in global memory, acquire/release),
-// stage it in shared memory (with the RMSNorm fused in), and dot it with the weight rows as they
-// land. Phases per layer:
-//   A  x -> RmsNorm -> qkv = [wq;wk;wv] . xn                     (:795-798)
-//   B  per (KV head, split): QK-RMSNorm + RoPE of q/k, bf16 K/V write at kv_pos, attention-sink
-//      re-rotation, split-K attention over the paged KV cache     (:800-844)
-//   C  combine splits; x += wo . attn                              (:846-849)
-//   D  x -> RmsNorm -> h = silu(w1 . xn) * (w3 . xn)               (:851, :1005-1011)
-//   E  x += w2 . h                                                 (:1013, :863-865)
-// then the final RmsNorm + lm_head with a per-CTA argmax; the next step (or the host) reduces the
-// per-CTA (value, index) pairs, lowest index winning ties.
+// Dataflow. Decode at batch 1 streams 1.19 GB of bf16 weights per token. Each SM runs one
+// continuous stream: a producer warp walks the fixed sequence of byte ranges this CTA owns for the
+// whole call and copies them with TMA bulk copies (cp.async.bulk, no multicast) into a 24-slot
+// shared-memory ring guarded by full/empty mbarriers. It runs ahead across the grid-wide
+// dependencies (it only waits for a free slot, and - for KV pages - for the step that wrote
+// them). Eight consumer warps wait for each phase's input (a monotonic arrival counter in global
+// memory, release/acquire), stage it in shared memory with the RMSNorm fused in, and dot it with
+// the rows as they land. Three grid-wide phases per layer (four past 128 cached positions):
+//   A   x = Xprev + Y[l-1] (or the embedding row); Xcur = x; qkv = [wq;wk;wv] . RmsNorm(x)
+//       (src/inference.cpp:795-798)
+//   BC  CTA (g, p) of KV head g: QK-RMSNorm + RoPE (:800-810), bf16 K/V write at kv_pos
+//       (:812-815), attention over the KV pages streamed through the ring with the sink rows
+//       re-rotated on the fly (:817-844), then rows p of wo[:, 256g:256g+256] . attn_g added into
+//       Xcur (split-K o_proj, x += proj, :846-849)
+//   (past 128 positions: B = split-K attention partials read through L2, C = combine + the same
+//    split-K o_proj)
+//   DE  h_i = silu(w1_i . xn) * (w3_i . xn) for this CTA's MLP indices i, then
+//       Y[l] += sum_i h_i * w2[:, i] (split-K down_proj, :851, :1005-1015, :863-865); the
+//       attention-sink rows are written back rotated (:817-827)
+// then the final RmsNorm + lm_head with a per-CTA argmax; every CTA reduces the (value, index)
+// pairs itself (lowest index wins ties) for the next step's embedding row.
+//
+// Split-K sums use fp32 atomics, so the order of the fp32 additions varies from run to run.
 //
 // Every wait is bounded (clock64): on timeout the kernel sets *err, stops issuing copies, waits
 // for the copies already issued and returns; the host reports Q3_ERR_DEVICE_TIMEOUT.
@@ -36,25 +42,40 @@ namespace {
 
 constexpr int D = 1024, H = 3072, NQ = 16, NKV = 8, HD = 128;
 constexpr int QD = NQ * HD, KVD = NKV * HD, QKV_ROWS = QD + 2 * KVD;
+constexpr int GRP = 2 * HD;            // attention output of one KV-head group (2 query heads)
 constexpr int NCW = 8;                 // consumer warps
 constexpr int NCT = NCW * 32;          // consumer threads
 constexpr int NT = NCT + 32;           // + one producer warp
-constexpr int NS = 32;                 // ring slots
-constexpr int SLOT = 6144;             // bytes per slot
-constexpr int ATT_TOK = 24;            // KV positions staged per attention sub-chunk
+constexpr int NS = 8;                  // ring slots
+constexpr int SLOT = 16384;            // bytes per slot
+// Chunk q lives in slot q % NS and, in warp-owned tasks, is consumed by warp q % NCW. With NS a
+// multiple of NCW every use of a slot inside such a task belongs to the same warp, which consumes
+// them in order: no warp can wait on use n of a slot while use n-1 is still unconsumed (a parity
+// wait for use n would then be satisfied by the completion of use n-2).
+static_assert(NS % 8 == 0, "ring slots must be a multiple of the consumer warps");
+// Rows per ring chunk: 8-row groups feed one m16n8k16 MMA column block.
+constexpr int RPC_ROW = 8;             // 1024-element rows ([wq;wk;wv], lm_head, w2t)
+constexpr int RPC_GRP = 8;             // 256-element rows (wo split by KV-head group)
+constexpr int RPC_PAIR = 4;            // w1 | w3 row pairs (4 + 4 rows)
+constexpr int XSTRIDE = D + 32;        // bf16 elements between the hi and lo activation rows
+constexpr int T_SHORT = 128;           // KV positions up to which attention runs from the ring
+constexpr int ATT_TOK = 24;            // positions staged per sub-chunk (long contexts)
+constexpr int PAGE_BYTES = kPageTokens * HD * 2;
 
-enum Mode : int { kStore = 0, kResid = 1, kPair = 2, kLogits = 3 };
+enum Mode : int { kStore = 0, kRed = 1, kPair = 2, kLogits = 3 };
 
 struct __align__(128) Smem {
     uint8_t ring[NS][SLOT];
-    float4 xs4[H / 4];        // staged activation, permuted per 8-element vector (see stage_*)
-    float xres[D];            // residual-stream copy for the o/down epilogues
-    float qk[3][HD];          // normalised + rotated q heads (2) and k head of a KV group
+    uint16_t xhl[2][XSTRIDE]; // staged activation as bf16 hi / lo parts (x = hi + lo)
+    float4 xs4[H / 4];        // attention staging and merge buffers
+    float qk[4][HD];          // q head 2g, q head 2g+1, k and v at kv_pos (bf16-rounded)
+    float hbuf[64];           // h of this CTA's MLP indices
     float2 mlw[NCW][2];       // per-warp attention (max, sum)
     float red[NCW];
     float2 best[NCW];
     uint64_t full[NS];
     uint64_t empty[NS];
+    unsigned long long wait_cycles;  // instrumentation only
     int abort_flag;
     int token;
     int go;
@@ -93,6 +114,11 @@ __device__ __forceinline__ uint64_t evict_first_policy() {
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
     return p;
 }
+__device__ __forceinline__ uint64_t evict_last_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
 // 1-D TMA bulk copy global -> this CTA's shared memory, completing on an mbarrier.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
                                          uint64_t* bar, uint64_t policy) {
@@ -107,8 +133,16 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+__device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ void bar_consumers() {
     asm volatile("bar.sync 1, %0;" ::"n"(NCT) : "memory");
+}
+__device__ __forceinline__ unsigned long long globaltimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
 }
 
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
@@ -116,9 +150,37 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
 }
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
 
+// ------------------------------------------------------------------ self-checks
+//
+// Builds with Q3_FUSED_CHECKS validate every shared-memory offset, bulk-copy range and epilogue
+// index of the kernel, and record the first failed check (or the site of a wait that gave up)
+// in a.dbg: [0] code, [1] CTA, [2] thread, [3..5] values; a failed access is skipped.
+
+#ifdef Q3_FUSED_CHECKS
+__device__ __noinline__ void dbg_report(const FusedArgs& a, unsigned long long code, long long v0,
+                                        long long v1, long long v2) {
+    if (a.dbg && atomicCAS(a.dbg, 0ull, code) == 0ull) {
+        a.dbg[1] = blockIdx.x;
+        a.dbg[2] = threadIdx.x;
+        a.dbg[3] = static_cast<unsigned long long>(v0);
+        a.dbg[4] = static_cast<unsigned long long>(v1);
+        a.dbg[5] = static_cast<unsigned long long>(v2);
+        __threadfence();
+    }
+}
+#define Q3_CHECK(cond, code, v0, v1, v2)                  \
+    (((cond)) ? true                                      \
+              : (dbg_report(a, (code), (long long)(v0),   \
+                            (long long)(v1), (long long)(v2)), \
+                 false))
+#else
+#define Q3_CHECK(cond, code, v0, v1, v2) true
+#endif
+
 // ------------------------------------------------------------------ bounded waits
 
-__device__ bool mbar_wait(uint64_t* b, uint32_t parity, const FusedArgs& a, volatile int* abort) {
+__device__ bool mbar_wait(uint64_t* b, uint32_t parity, const FusedArgs& a, volatile int* abort,
+                          int site = 0, long long info = 0) {
     if (mbar_try_wait(b, parity)) return true;
     const long long t0 = clock64();
     for (uint32_t it = 0;; ++it) {
@@ -128,28 +190,66 @@ __device__ bool mbar_wait(uint64_t* b, uint32_t parity, const FusedArgs& a, vola
             if (clock64() - t0 > a.spin_cycles) {
                 *abort = 1;
                 atomicOr(a.err, 1u);
+                Q3_CHECK(false, 1000 + site, info, parity, 0);
                 return false;
             }
         }
     }
 }
 
-// Consumer thread 0: wait until `target` CTAs have arrived on the grid counter.
-__device__ bool grid_wait(const FusedArgs& a, unsigned target, volatile int* abort) {
+// Wait until `target` CTA arrivals are visible on the grid counter.
+__device__ bool grid_wait(const FusedArgs& a, unsigned target, volatile int* abort, int site = 0) {
     const long long t0 = clock64();
     for (uint32_t it = 0;; ++it) {
-        if (ld_acquire(a.bar) >= target) return true;
-        if (*reinterpret_cast<volatile unsigned*>(a.err) != 0u) {
-            *abort = 1;
-            return false;
+        const unsigned seen = ld_acquire(a.bar);
+        if (seen >= target) return true;
+        if ((it & 15) == 15) {
+            if (*reinterpret_cast<volatile unsigned*>(a.err) != 0u || *abort) {
+                *abort = 1;
+                return false;
+            }
+            if (clock64() - t0 > a.spin_cycles) {
+                *abort = 1;
+                atomicOr(a.err, 1u);
+                Q3_CHECK(false, 2000 + site, target, seen, 0);
+                return false;
+            }
+            if (it > 4096) __nanosleep(64);
         }
-        if (clock64() - t0 > a.spin_cycles) {
-            *abort = 1;
-            atomicOr(a.err, 1u);
-            return false;
-        }
-        if (it > 16) __nanosleep(32);
     }
+}
+
+// Warp-level wait on a ring slot: lane 0 does the bounded wait, the verdict is made warp-uniform,
+// then every lane observes the completed phase (so the copied bytes are visible to it; the phase
+// cannot advance again before the slot is released, so that second wait returns at once).
+__device__ __forceinline__ bool warp_wait_full(Smem& sm, int slot, uint32_t parity,
+                                               const FusedArgs& a) {
+    const int lane = threadIdx.x & 31;
+    int ok = 0;
+    if (!Q3_CHECK(slot >= 0 && slot < NS, 20, slot, parity, 0)) return false;
+    if (lane == 0) {
+        if (a.prof && !mbar_try_wait(&sm.full[slot], parity)) {
+            // Instrumentation: time this warp spends waiting for ring data.
+            const long long t0 = clock64();
+            ok = static_cast<int>(mbar_wait(&sm.full[slot], parity, a, &sm.abort_flag, 1, slot));
+            atomicAdd(&sm.wait_cycles, static_cast<unsigned long long>(clock64() - t0));
+        } else {
+            ok = static_cast<int>(mbar_wait(&sm.full[slot], parity, a, &sm.abort_flag, 1, slot));
+        }
+    }
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    if (!ok) return false;
+    // Bounded as well: the phase already completed for lane 0 and cannot advance again before
+    // this warp releases the slot.
+    bool seen = false;
+    for (int spin = 0; spin < (1 << 20); ++spin) {
+        if (mbar_try_wait(&sm.full[slot], parity)) {
+            seen = true;
+            break;
+        }
+    }
+    if (!seen) Q3_CHECK(false, 21, slot, parity, 0);
+    return __all_sync(0xffffffffu, seen);
 }
 
 // ------------------------------------------------------------------ work partition
@@ -162,16 +262,34 @@ __device__ __forceinline__ Span part(int rows, int G, int c) {
     const int r1 = static_cast<int>((static_cast<long long>(rows) * (c + 1)) / G);
     return {r0, r1 - r0};
 }
-template <int K, int MODE>
-struct Chunking {
-    // Rows (or gate/up pairs) per ring slot.
-    static constexpr int RPC = MODE == kPair ? SLOT / (2 * K * 2) : SLOT / (K * 2);
-    static_assert(RPC >= 1, "slot too small");
+
+static_assert(RPC_ROW * D * 2 <= SLOT && RPC_GRP * GRP * 2 <= SLOT &&
+                  2 * RPC_PAIR * D * 2 <= SLOT && 2 * kPageTokens * HD * 2 <= SLOT,
+              "ring slot too small");
+
+__device__ __forceinline__ size_t page_elem(const int32_t* table, int page, int g) {
+    return (static_cast<size_t>(__ldg(table + page)) * NKV + g) * kPageTokens * HD;
+}
+__device__ __forceinline__ size_t paged(const int32_t* table, int t, int g) {
+    return page_elem(table, t / kPageTokens, g) + static_cast<size_t>(t % kPageTokens) * HD;
+}
+
+struct StepPos {
+    int pos, num_sink, kv_pos, kv_len, splits;
+    bool shrt;
 };
 
-__device__ __forceinline__ size_t paged(const int32_t* table, int t, int g) {
-    const int page = __ldg(table + t / kPageTokens);
-    return ((static_cast<size_t>(page) * NKV + g) * kPageTokens + (t % kPageTokens)) * HD;
+__device__ __forceinline__ StepPos step_pos(const FusedArgs& a, const StepParams& sp0, int st) {
+    StepPos p;
+    p.pos = sp0.pos + st;
+    step_positions(p.pos, a.ctx, &p.num_sink, &p.kv_pos, &p.kv_len);
+    p.shrt = p.kv_len <= T_SHORT;
+    p.splits = min(max((p.kv_len + ATT_TOK - 1) / ATT_TOK, 1), a.s_max);
+    return p;
+}
+
+__device__ __forceinline__ int phases_of(const FusedArgs& a, bool shrt) {
+    return a.n_layers * (shrt ? 3 : 4) + 1;
 }
 
 // ------------------------------------------------------------------ producer
@@ -179,13 +297,33 @@ __device__ __forceinline__ size_t paged(const int32_t* table, int t, int g) {
 struct Producer {
     Smem& sm;
     const FusedArgs& a;
-    uint64_t pol;
+    uint64_t pol_w, pol_kv;
     uint32_t q = 0;
 
-    __device__ bool issue(const void* s1, uint32_t b1, const void* s2, uint32_t b2, int off2) {
+    unsigned long long blocked = 0;  // instrumentation: cycles spent waiting for a free slot
+
+    __device__ bool issue(const void* s1, uint32_t b1, const void* s2, uint32_t b2, int off2,
+                          uint64_t pol) {
         const int slot = q % NS;
-        if (q >= NS && !mbar_wait(&sm.empty[slot], ((q / NS) - 1) & 1, a, &sm.abort_flag)) {
+        if (!Q3_CHECK(b1 % 16 == 0 && b2 % 16 == 0 && b1 > 0 && b1 <= SLOT &&
+                          (b2 == 0 || (off2 % 16 == 0 && off2 >= static_cast<int>(b1) &&
+                                       off2 + b2 <= SLOT)),
+                      30, b1, b2, off2) ||
+            !Q3_CHECK((reinterpret_cast<uintptr_t>(s1) & 15) == 0 &&
+                          (reinterpret_cast<uintptr_t>(s2) & 15) == 0,
+                      31, reinterpret_cast<uintptr_t>(s1), reinterpret_cast<uintptr_t>(s2), q)) {
             return false;
+        }
+        if (q >= NS) {
+            const uint32_t par = ((q / NS) - 1) & 1;
+            if (a.prof && !mbar_try_wait(&sm.empty[slot], par)) {
+                const long long t0 = clock64();
+                const bool ok = mbar_wait(&sm.empty[slot], par, a, &sm.abort_flag, 2, q);
+                blocked += clock64() - t0;
+                if (!ok) return false;
+            } else if (!mbar_wait(&sm.empty[slot], par, a, &sm.abort_flag, 2, q)) {
+                return false;
+            }
         }
         mbar_arrive_expect_tx(&sm.full[slot], b1 + b2);
         bulk_g2s(sm.ring[slot], s1, b1, &sm.full[slot], pol);
@@ -194,34 +332,79 @@ struct Producer {
         return true;
     }
 
-    template <int K, int MODE>
-    __device__ bool rows(const uint16_t* w, const uint16_t* w2, Span sp) {
-        constexpr int RPC = Chunking<K, MODE>::RPC;
+    template <int ROW_BYTES, int RPC>
+    __device__ bool rows(const void* base, Span sp) {
+        const uint8_t* b = static_cast<const uint8_t*>(base);
         for (int rb = sp.r0; rb < sp.r0 + sp.n; rb += RPC) {
             const int rn = min(RPC, sp.r0 + sp.n - rb);
-            const uint32_t bytes = static_cast<uint32_t>(rn) * K * 2;
-            const size_t off = static_cast<size_t>(rb) * K;
-            if (!issue(w + off, bytes, MODE == kPair ? w2 + off : nullptr,
-                       MODE == kPair ? bytes : 0u, RPC * K * 2)) {
+            if (!issue(b + static_cast<size_t>(rb) * ROW_BYTES, rn * ROW_BYTES, nullptr, 0u, 0,
+                       pol_w)) {
                 return false;
             }
         }
         return true;
     }
 
-    __device__ void run(int G, int c) {
-        pol = evict_first_policy();
-        bool ok = true;
-        for (int st = 0; ok && st < a.n_steps; ++st) {
-            for (int l = 0; ok && l < a.n_layers; ++l) {
-                const LayerWeights w = a.layers[l];
-                ok = ok && rows<D, kStore>(w.wqkv, nullptr, part(QKV_ROWS, G, c));
-                ok = ok && rows<QD, kResid>(w.wo, nullptr, part(D, G, c));
-                ok = ok && rows<D, kPair>(w.w1, w.w3, part(H, G, c));
-                ok = ok && rows<H, kResid>(w.w2, nullptr, part(D, G, c));
+    __device__ bool pairs(const uint16_t* w1, const uint16_t* w3, Span sp) {
+        constexpr int RPC = RPC_PAIR;
+        for (int rb = sp.r0; rb < sp.r0 + sp.n; rb += RPC) {
+            const int rn = min(RPC, sp.r0 + sp.n - rb);
+            const size_t off = static_cast<size_t>(rb) * D;
+            if (!issue(w1 + off, rn * D * 2, w3 + off, rn * D * 2, RPC * D * 2, pol_w)) {
+                return false;
             }
-            ok = ok && rows<D, kLogits>(a.lm_head, nullptr, part(a.vocab, G, c));
         }
+        return true;
+    }
+
+    __device__ bool kv_pages(int l, int g, int kv_len) {
+        const uint16_t* kc = a.k_cache + static_cast<size_t>(l) * a.layer_elems;
+        const uint16_t* vc = a.v_cache + static_cast<size_t>(l) * a.layer_elems;
+        const int np = (kv_len + kPageTokens - 1) / kPageTokens;
+        for (int j = 0; j < np; ++j) {
+            const size_t e = page_elem(a.page_table, j, g);
+            if (!issue(kc + e, PAGE_BYTES, vc + e, PAGE_BYTES, PAGE_BYTES, pol_kv)) return false;
+        }
+        return true;
+    }
+
+    __device__ void run(int G, int c) {
+        pol_w = evict_first_policy();
+        pol_kv = evict_last_policy();
+        const StepParams sp0 = *a.sp;
+        const int P = G / NKV;
+        const bool in_grp = c < NKV * P;
+        const int g = c % NKV, p = c / NKV;
+        bool ok = true;
+        unsigned base = 0, prev_base = 0;
+        bool prev_short = true;
+        for (int st = 0; ok && st < a.n_steps; ++st) {
+            const StepPos sp = step_pos(a, sp0, st);
+            for (int l = 0; ok && l < a.n_layers; ++l) {
+                const FusedLayer w = a.layers[l];
+                ok = ok && rows<D * 2, RPC_ROW>(w.wqkv, part(QKV_ROWS, G, c));
+                if (ok && sp.shrt && in_grp) {
+                    // KV pages of this layer were last written (row kv_pos, sink rows) by the
+                    // previous step's phases up to DE(l): wait until every CTA is past them.
+                    if (st > 0) {
+                        const unsigned de = prev_base + l * (prev_short ? 3 : 4) + (prev_short ? 2 : 3);
+                        ok = grid_wait(a, G * (de + 1) + a.barrier_offset, &sm.abort_flag, 3);
+                    }
+                    ok = ok && kv_pages(l, g, sp.kv_len);
+                }
+                if (in_grp) {
+                    ok = ok && rows<GRP * 2, RPC_GRP>(w.wop + static_cast<size_t>(g) * D * GRP,
+                                                      part(D, P, p));
+                }
+                ok = ok && pairs(w.w1, w.w3, part(H, G, c));
+                ok = ok && rows<D * 2, RPC_ROW>(w.w2t, part(H, G, c));
+            }
+            ok = ok && rows<D * 2, RPC_ROW>(a.lm_head, part(a.vocab, G, c));
+            prev_base = base;
+            prev_short = sp.shrt;
+            base += phases_of(a, sp.shrt);
+        }
+        if (a.prof) a.prof[static_cast<size_t>(c) * 8 + 4] = blocked;
         // Wait for every copy still in flight before the CTA may exit.
         const uint32_t first = q > NS ? q - NS : 0;
         for (uint32_t k = first; k < q; ++k) {
@@ -235,6 +418,7 @@ struct Producer {
 };
 
 // ------------------------------------------------------------------ consumer helpers
+//
 
 __device__ __forceinline__ float consumer_sum(float v, Smem& sm) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -248,102 +432,187 @@ __device__ __forceinline__ float consumer_sum(float v, Smem& sm) {
     return t;
 }
 
-// Stage a 1024-vector for a K=1024 GEMV: xres = x, xs = RmsNorm(x, nw) (src/inference.cpp:887-923)
-// in the permuted layout xs4[v] = x[8v..8v+3], xs4[128+v] = x[8v+4..8v+7].
-__device__ void stage_norm(Smem& sm, float4 xv, const uint16_t* nw, float eps) {
+// The staged activation x of a GEMV is kept as two bf16 vectors hi = bf16(x), lo = bf16(x - hi):
+// hi + lo carries 16 significant bits of each fp32 element (relative error <= 2^-17), and both
+// are multiplied against the bf16 weights by the tensor core with fp32 accumulation.
+__device__ __forceinline__ void split_bf16(float v, uint16_t& hi, uint16_t& lo) {
+    hi = f32_to_bf16(v);
+    lo = f32_to_bf16(v - bf16_to_f32(hi));
+}
+
+__device__ __forceinline__ void xs_put(Smem& sm, int e, float val) {
+    split_bf16(val, sm.xhl[0][e], sm.xhl[1][e]);
+}
+
+// Stage xs = RmsNorm(x) (src/inference.cpp:887-923) for a K=1024 GEMV; thread t holds x[4t..4t+3]
+// and its norm weights wv.
+__device__ __forceinline__ void stage_norm(Smem& sm, float4 xv, uint2 wv, float eps) {
     const int t = threadIdx.x;
-    reinterpret_cast<float4*>(sm.xres)[t] = xv;
     const float ss = consumer_sum(xv.x * xv.x + xv.y * xv.y + xv.z * xv.z + xv.w * xv.w, sm);
     const float inv = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
-    const uint2 wv = __ldg(reinterpret_cast<const uint2*>(nw) + t);
-    float4 y;
-    y.x = (xv.x * inv) * bf16_lo(wv.x);
-    y.y = (xv.y * inv) * bf16_hi(wv.x);
-    y.z = (xv.z * inv) * bf16_lo(wv.y);
-    y.w = (xv.w * inv) * bf16_hi(wv.y);
-    sm.xs4[(t & 1) * (D / 8) + (t >> 1)] = y;
+    const float y[4] = {(xv.x * inv) * bf16_lo(wv.x), (xv.y * inv) * bf16_hi(wv.x),
+                        (xv.z * inv) * bf16_lo(wv.y), (xv.w * inv) * bf16_hi(wv.y)};
+    uint16_t hi[4], lo[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) split_bf16(y[j], hi[j], lo[j]);
+    reinterpret_cast<uint2*>(sm.xhl[0])[t] =
+        make_uint2(hi[0] | (static_cast<uint32_t>(hi[1]) << 16), hi[2] | (static_cast<uint32_t>(hi[3]) << 16));
+    reinterpret_cast<uint2*>(sm.xhl[1])[t] =
+        make_uint2(lo[0] | (static_cast<uint32_t>(lo[1]) << 16), lo[2] | (static_cast<uint32_t>(lo[3]) << 16));
     bar_consumers();
 }
 
-__device__ __forceinline__ float4 load_x_global(const FusedArgs& a) {
-    return __ldcg(reinterpret_cast<const float4*>(a.x) + threadIdx.x);
+// D += A . B for one m16n8k16 bf16 MMA with fp32 accumulation, A rows 8-15 zero.
+__device__ __forceinline__ void mma_16816(float d[4], uint32_t a0, uint32_t a2, uint32_t b0,
+                                          uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ float4 load_embed(const FusedArgs& a, int token) {
-    const uint2 e = __ldg(reinterpret_cast<const uint2*>(a.embed + static_cast<size_t>(token) * D) +
-                          threadIdx.x);
-    return make_float4(bf16_lo(e.x), bf16_hi(e.x), bf16_lo(e.y), bf16_hi(e.y));
-}
-
-// Dot the rows of this CTA's chunks of one task with the staged activation. After an abort the
-// remaining chunks are skipped (each wait then fails at once), but the warp still returns to the
-// caller so that every consumer thread reaches the same barriers.
-template <int K, int MODE>
-__device__ void consume(Smem& sm, const FusedArgs& a, uint32_t& q, Span sp, float* out,
-                        float& best_v, int& best_i) {
-    constexpr int RPC = Chunking<K, MODE>::RPC;
-    constexpr int NV = K / 8;  // 16-byte vectors per row
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int nch = (sp.n + RPC - 1) / RPC;
-    for (int ci = 0; ci < nch; ++ci) {
-        const uint32_t qq = q + ci;
-        if (static_cast<int>(qq % NCW) != warp) continue;
-        const int slot = qq % NS;
-        const uint32_t parity = (qq / NS) & 1;
-        // Lane 0 does the bounded wait; the verdict is made warp-uniform before any shuffle.
-        int ok = lane == 0 ? static_cast<int>(mbar_wait(&sm.full[slot], parity, a, &sm.abort_flag)) : 0;
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) continue;
-        // Every lane observes the completed phase (the copy's bytes are then visible to it); the
-        // phase cannot advance again before this warp releases the slot, so this returns at once.
-        while (!mbar_try_wait(&sm.full[slot], parity)) {
-        }
-        const uint8_t* base = sm.ring[slot];
-        const int rb = sp.r0 + ci * RPC;
-        const int rn = min(RPC, sp.r0 + sp.n - rb);
-        for (int j = 0; j < rn; ++j) {
-            const uint4* wrow = reinterpret_cast<const uint4*>(base + j * K * 2);
-            const uint4* urow = reinterpret_cast<const uint4*>(base + (RPC + j) * K * 2);
-            float acc = 0.0f, acc2 = 0.0f;
+// Dot products of 8 weight rows (a ring chunk, row-major, K bf16 per row, rows swizzled by row
+// parity: in odd rows the two 64-byte halves of every 128-byte block are swapped) with the staged
+// activation. The MMA's n dimension runs over the 8 rows and its m dimension holds the activation
+// (row 0 = hi, row 1 = lo, rows 2-15 zero); k is consumed 32 at a time, each lane supplying 8
+// consecutive elements of its row (the same permutation of k is applied to both operands, which
+// leaves the sum unchanged). Result: lanes 0-3 hold rows 2t and 2t+1 (t = lane) in y0, y1.
+template <int K>
+__device__ __forceinline__ void mma_rows8(const Smem& sm, const FusedArgs& a, const uint8_t* rows,
+                                          int row0, float& y0, float& y1) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const uint8_t* rp = rows + g * K * 2;
+    const int sw = ((row0 + g) & 1) << 2;
+    const uint16_t* xp = sm.xhl[g & 1];
+    const bool xlane = lane < 8;
+    float d[4][4];
 #pragma unroll
-            for (int v = lane; v < NV; v += 32) {
-                const uint4 w = wrow[v];
-                const float4 xa = sm.xs4[v];
-                const float4 xb = sm.xs4[NV + v];
-                acc = dot8(w, xa, xb, acc);
-                if (MODE == kPair) acc2 = dot8(urow[v], xa, xb, acc2);
-            }
-            acc = warp_sum(acc);
-            if (MODE == kPair) acc2 = warp_sum(acc2);
-            const int r = rb + j;
-            if (lane == 0) {
-                if (MODE == kStore || MODE == kLogits) out[r] = acc;
-                if (MODE == kResid) out[r] = sm.xres[r] + acc;
-                if (MODE == kPair) out[r] = silu(acc) * acc2;
-            }
-            if (MODE == kLogits && better(acc, r, best_v, best_i)) {
-                best_v = acc;
-                best_i = r;
-            }
-        }
+    for (int i = 0; i < 4; ++i) d[i][0] = d[i][1] = d[i][2] = d[i][3] = 0.0f;
+    // mma.sync.aligned needs the whole warp converged: no branches inside the loop below (the
+    // activation fragment is loaded by every lane and zeroed by a select outside lanes 0-7).
+    __syncwarp();
+#pragma unroll 4
+    for (int kt = 0; kt < K / 32; ++kt) {
+        const int u = kt * 4 + t;  // this lane's 16-byte unit of the row
+#ifdef Q3_FUSED_CHECKS
+        const long long woff = (rp - &sm.ring[0][0]) + ((u ^ sw) << 4);
+        Q3_CHECK(woff >= 0 && woff + 16 <= static_cast<long long>(NS) * SLOT && (woff & 15) == 0,
+                 40, woff, row0, kt);
+        Q3_CHECK(u * 16 + 16 <= K * 2, 41, u, K, 0);
+#endif
+        const uint4 w = *reinterpret_cast<const uint4*>(rp + ((u ^ sw) << 4));
+        uint4 x = *reinterpret_cast<const uint4*>(xp + u * 8);
+        x.x = xlane ? x.x : 0u;
+        x.y = xlane ? x.y : 0u;
+        x.z = xlane ? x.z : 0u;
+        x.w = xlane ? x.w : 0u;
+        mma_16816(d[kt & 3], x.x, x.y, w.x, w.y);
+        mma_16816(d[kt & 3], x.z, x.w, w.z, w.w);
+    }
+    float s0 = (d[0][0] + d[1][0]) + (d[2][0] + d[3][0]);
+    float s1 = (d[0][1] + d[1][1]) + (d[2][1] + d[3][1]);
+    s0 += __shfl_down_sync(0xffffffffu, s0, 4);  // + the lo part (m = 1) held by lane t + 4
+    s1 += __shfl_down_sync(0xffffffffu, s1, 4);
+    y0 = s0;
+    y1 = s1;
+}
+
+__device__ __forceinline__ uint2 load_norm(const uint16_t* nw) {
+    return __ldg(reinterpret_cast<const uint2*>(nw) + threadIdx.x);
+}
+
+__device__ __forceinline__ float4 add4(float4 a, float4 b) {
+    return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+}
+
+// Dot the rows of this CTA's warp-owned chunks of one task (chunks q0.. of `rpc` rows of K
+// elements) with the staged activation, epilogue by `mode`. kLogits leaves each warp's best
+// (value, index) in sm.best. After an abort the remaining chunks are skipped (each wait then fails
+// at once) but the warp still returns, so every consumer thread reaches the same barriers.
+template <int K, int rpc, int mode>
+__device__ __forceinline__ void consume_rows(Smem& sm, const FusedArgs& a, uint32_t q0, int r0,
+                                             int n, float* out, int out_n) {
+    static_assert(mode == kPair ? rpc == 4 : rpc == 8, "one 8-row MMA group per chunk");
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, t = lane & 3;
+    const int nch = (n + rpc - 1) / rpc;
+    float bv = -FLT_MAX;
+    int bi = INT_MAX;
+    for (int ci = (warp - static_cast<int>(q0 % NCW) + NCW) % NCW; ci < nch; ci += NCW) {
+        const uint32_t qq = q0 + ci;
+        const int slot = qq % NS;
+        if (!warp_wait_full(sm, slot, (qq / NS) & 1, a)) continue;
+        const int rb = r0 + ci * rpc;
+        const int rn = min(rpc, r0 + n - rb);
+        float y0, y1;
+        mma_rows8<K>(sm, a, sm.ring[slot], rb, y0, y1);
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.empty[slot]);
+        if (mode == kPair) {
+            // Rows 0-3 of the group are w1 rows rb..rb+3 (lanes 0-1), rows 4-7 the w3 rows
+            // (lanes 2-3): h = silu(gate) * up (src/inference.cpp:1009-1011).
+            const float u0 = __shfl_down_sync(0xffffffffu, y0, 2);
+            const float u1 = __shfl_down_sync(0xffffffffu, y1, 2);
+            if (lane < 2) {
+                const int i = 2 * t;
+                if (i < rn && Q3_CHECK(rb - r0 + i < out_n, 50, rb, r0, i)) {
+                    out[rb - r0 + i] = silu(y0) * u0;
+                }
+                if (i + 1 < rn && Q3_CHECK(rb - r0 + i + 1 < out_n, 51, rb, r0, i)) {
+                    out[rb - r0 + i + 1] = silu(y1) * u1;
+                }
+            }
+        } else if (lane < 4) {
+            const int i = 2 * t;
+            const float yy[2] = {y0, y1};
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                if (i + j >= rn) break;
+                const int r = rb + i + j;
+                if (!Q3_CHECK(r >= 0 && r < out_n, 52, r, out_n, mode)) break;
+                if (mode == kStore || mode == kLogits) out[r] = yy[j];
+                if (mode == kRed) atomicAdd(out + r, yy[j]);
+                if (mode == kLogits && better(yy[j], r, bv, bi)) {
+                    bv = yy[j];
+                    bi = r;
+                }
+            }
+        }
     }
-    q += nch;
+    if (mode == kLogits) {
+#pragma unroll
+        for (int o = 1; o < 4; o <<= 1) {
+            const float v = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int j = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (better(v, j, bv, bi)) {
+                bv = v;
+                bi = j;
+            }
+        }
+        if (lane == 0) sm.best[warp] = make_float2(bv, __int_as_float(bi));
+    }
+}
+
+__device__ __forceinline__ uint32_t chunks_of(int n, int rpc) {
+    return static_cast<uint32_t>((n + rpc - 1) / rpc);
 }
 
 // RoPE on a 128-vector spread over a warp, 4 elements per lane: lanes 0-15 hold the first half,
 // lanes 16-31 the second; pairs (i, i+64) sit 16 lanes apart (src/inference.cpp:976-990).
-__device__ __forceinline__ void rope_warp(float y[4], const float2* row) {
-    const int lane = threadIdx.x & 31;
-    const bool first = lane < 16;
-    const int i0 = (lane & 15) * 4;
+__device__ __forceinline__ void rope_warp(float y[4], const float2 cs[4]) {
+    const bool first = (threadIdx.x & 31) < 16;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const float p = __shfl_xor_sync(0xffffffffu, y[j], 16);
-        const float2 cs = __ldg(row + i0 + j);
-        y[j] = first ? (y[j] * cs.x - p * cs.y) : (y[j] * cs.x + p * cs.y);
+        y[j] = first ? (y[j] * cs[j].x - p * cs[j].y) : (y[j] * cs[j].x + p * cs[j].y);
     }
+}
+
+__device__ __forceinline__ void load_rope(float2 cs[4], const FusedArgs& a, int pos) {
+    const int rp = min(pos, a.rope_len - 1);
+    const float2* row = a.rope + static_cast<size_t>(rp) * (HD / 2) + ((threadIdx.x & 31) & 15) * 4;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) cs[j] = __ldg(row + j);
 }
 
 __device__ __forceinline__ uint2 pack_bf16x4(const float y[4]) {
@@ -352,62 +621,214 @@ __device__ __forceinline__ uint2 pack_bf16x4(const float y[4]) {
                       static_cast<uint32_t>(f32_to_bf16(y[2])) |
                           (static_cast<uint32_t>(f32_to_bf16(y[3])) << 16));
 }
+__device__ __forceinline__ void unpack_bf16x4(uint2 v, float y[4]) {
+    y[0] = bf16_lo(v.x);
+    y[1] = bf16_hi(v.x);
+    y[2] = bf16_lo(v.y);
+    y[3] = bf16_hi(v.y);
+}
 
-struct StepPos {
-    int pos, num_sink, kv_pos, kv_len, splits;
+// Static inputs of the attention prologue, loaded before the phase's grid wait.
+struct HeadPre {
+    uint2 nw;        // q_norm (warps 0-1) or k_norm (warp 2) for this lane
+    float2 cs[4];    // RoPE at pos
+    float2 cs1[4];   // RoPE at position 1 (sink re-rotation)
 };
 
-// Phase B for one (KV head, split) item of this CTA.
-__device__ void attention_item(Smem& sm, const FusedArgs& a, const LayerWeights& w, int l,
-                               const StepPos& p, int item) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int S = p.splits;
-    const int g = item % NKV, s = item / NKV;
-    const int chunk = (p.kv_len + S - 1) / S;
-    const int t0 = s * chunk, t1 = min(p.kv_len, t0 + chunk);
-    const bool own = p.kv_pos >= t0 && p.kv_pos < t1;
-    uint16_t* kc = a.k_cache + static_cast<size_t>(l) * a.layer_elems;
-    uint16_t* vc = a.v_cache + static_cast<size_t>(l) * a.layer_elems;
-    const int rp = min(p.pos, a.rope_len - 1);
+__device__ __forceinline__ void head_preload(HeadPre& hp, const FusedArgs& a, const FusedLayer& w,
+                                             int pos) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    hp.nw = __ldg(reinterpret_cast<const uint2*>(warp < 2 ? w.q_norm : w.k_norm) + lane);
+    load_rope(hp.cs, a, pos);
+    load_rope(hp.cs1, a, 1);
+}
 
+// QK-RMSNorm (src/inference.cpp:800-807) + RoPE (:809-810) of q heads 2g, 2g+1 and k head g into
+// sm.qk[0..2]; v head g into sm.qk[3]; k and v rounded to bf16 as the cache stores them (:812-815)
+// and, when `writer`, written to the cache at kv_pos. Ends with a consumer barrier.
+__device__ __forceinline__ void prep_heads(Smem& sm, const FusedArgs& a, const HeadPre& hp, int l,
+                                        int g, int kv_pos, bool writer) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (warp < 3) {
-        // QK-RMSNorm (src/inference.cpp:800-807) + RoPE (:809-810) of q heads 2g, 2g+1 and k head g.
         const float* src = warp < 2 ? a.qkv + (2 * g + warp) * HD : a.qkv + QD + g * HD;
         const float4 e = __ldcg(reinterpret_cast<const float4*>(src) + lane);
         const float ss = warp_sum(e.x * e.x + e.y * e.y + e.z * e.z + e.w * e.w);
         const float inv = 1.0f / sqrtf(ss / static_cast<float>(HD) + a.eps);
-        const uint2 wv = __ldg(reinterpret_cast<const uint2*>(warp < 2 ? w.q_norm : w.k_norm) + lane);
-        float y[4] = {(e.x * inv) * bf16_lo(wv.x), (e.y * inv) * bf16_hi(wv.x),
-                      (e.z * inv) * bf16_lo(wv.y), (e.w * inv) * bf16_hi(wv.y)};
-        rope_warp(y, a.rope + static_cast<size_t>(rp) * (HD / 2));
+        float y[4] = {(e.x * inv) * bf16_lo(hp.nw.x), (e.y * inv) * bf16_hi(hp.nw.x),
+                      (e.z * inv) * bf16_lo(hp.nw.y), (e.w * inv) * bf16_hi(hp.nw.y)};
+        rope_warp(y, hp.cs);
+        if (warp == 2) {
+            const uint2 kb = pack_bf16x4(y);
+            unpack_bf16x4(kb, y);
+            if (writer) {
+                uint16_t* kc = a.k_cache + static_cast<size_t>(l) * a.layer_elems;
+                reinterpret_cast<uint2*>(kc + paged(a.page_table, kv_pos, g))[lane] = kb;
+            }
+        }
         reinterpret_cast<float4*>(sm.qk[warp])[lane] = make_float4(y[0], y[1], y[2], y[3]);
-        if (warp == 2 && own) {
-            // bf16 K write at kv_pos (:812-815).
-            reinterpret_cast<uint2*>(kc + paged(a.page_table, p.kv_pos, g))[lane] = pack_bf16x4(y);
-        }
     } else if (warp == 3) {
-        if (own) {
-            const float4 e = __ldcg(reinterpret_cast<const float4*>(a.qkv + QD + KVD + g * HD) + lane);
-            const float y[4] = {e.x, e.y, e.z, e.w};
-            reinterpret_cast<uint2*>(vc + paged(a.page_table, p.kv_pos, g))[lane] = pack_bf16x4(y);
+        const float4 e = __ldcg(reinterpret_cast<const float4*>(a.qkv + QD + KVD + g * HD) + lane);
+        float y[4] = {e.x, e.y, e.z, e.w};
+        const uint2 vb = pack_bf16x4(y);
+        unpack_bf16x4(vb, y);
+        if (writer) {
+            uint16_t* vc = a.v_cache + static_cast<size_t>(l) * a.layer_elems;
+            reinterpret_cast<uint2*>(vc + paged(a.page_table, kv_pos, g))[lane] = vb;
         }
-    } else if (s == 0 && warp - 4 < p.num_sink) {
-        // Attention-sink re-rotation once the ring buffer has wrapped (:817-827).
-        uint2* row = reinterpret_cast<uint2*>(kc + paged(a.page_table, warp - 4, g));
-        const uint2 v = __ldcg(row + lane);
-        float y[4] = {bf16_lo(v.x), bf16_hi(v.x), bf16_lo(v.y), bf16_hi(v.y)};
-        rope_warp(y, a.rope + static_cast<size_t>(1) * (HD / 2));
-        row[lane] = pack_bf16x4(y);
+        reinterpret_cast<float4*>(sm.qk[3])[lane] = make_float4(y[0], y[1], y[2], y[3]);
     }
     bar_consumers();
+}
 
-    // Split-K attention over positions [t0, t1) for the two query heads of KV head g
-    // (FastAttn + Softmax, :1017-1058, :925-946), online softmax per warp.
-    const float4 q0 = reinterpret_cast<const float4*>(sm.qk[0])[lane];
-    const float4 q1 = reinterpret_cast<const float4*>(sm.qk[1])[lane];
-    const float sq = sqrtf(static_cast<float>(HD));
-    float m0 = -FLT_MAX, m1 = -FLT_MAX, l0 = 0.0f, l1 = 0.0f;
-    float o0[4] = {0.f, 0.f, 0.f, 0.f}, o1[4] = {0.f, 0.f, 0.f, 0.f};
+// Online-softmax state of one warp for the two query heads of a KV group.
+struct AttnAcc {
+    float m0, m1, l0, l1;
+    float o0[4], o1[4];
+};
+
+__device__ __forceinline__ void acc_init(AttnAcc& s) {
+    s.m0 = s.m1 = -FLT_MAX;
+    s.l0 = s.l1 = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) s.o0[j] = s.o1[j] = 0.0f;
+}
+
+// One cached position: k4/v4 are this lane's 4 elements (FastAttn, src/inference.cpp:1029-1057).
+__device__ __forceinline__ void acc_add(AttnAcc& s, const float k4[4], const float v4[4],
+                                        float4 q0, float4 q1) {
+    const float sq = 11.313708498984761f;  // sqrtf(128), the reference's sqrtf(head_dim)
+    float d0 = k4[0] * q0.x;
+    d0 = fmaf(k4[1], q0.y, d0);
+    d0 = fmaf(k4[2], q0.z, d0);
+    d0 = fmaf(k4[3], q0.w, d0);
+    float d1 = k4[0] * q1.x;
+    d1 = fmaf(k4[1], q1.y, d1);
+    d1 = fmaf(k4[2], q1.z, d1);
+    d1 = fmaf(k4[3], q1.w, d1);
+    const float s0 = warp_sum(d0) / sq, s1 = warp_sum(d1) / sq;
+    const float n0 = fmaxf(s.m0, s0), n1 = fmaxf(s.m1, s1);
+    const float a0 = expf(s.m0 - n0), a1 = expf(s.m1 - n1);
+    const float p0 = expf(s0 - n0), p1 = expf(s1 - n1);
+    s.l0 = s.l0 * a0 + p0;
+    s.l1 = s.l1 * a1 + p1;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        s.o0[j] = s.o0[j] * a0 + p0 * v4[j];
+        s.o1[j] = s.o1[j] * a1 + p1 * v4[j];
+    }
+    s.m0 = n0;
+    s.m1 = n1;
+}
+
+// Key/value of cached position t for this lane: the in-register current row at kv_pos, and the
+// attention-sink rows rotated by RoPE(position 1) and re-rounded (the reference rotates them in
+// the cache before attending, :817-827; the rotated rows are written back in phase DE).
+__device__ __forceinline__ void kv_lane(Smem& sm, const HeadPre& hp, int t, int kv_pos,
+                                        int num_sink, uint2 kk, uint2 vv, float k4[4],
+                                        float v4[4]) {
+    const int lane = threadIdx.x & 31;
+    if (t == kv_pos) {
+        const float4 kc = reinterpret_cast<const float4*>(sm.qk[2])[lane];
+        const float4 vc = reinterpret_cast<const float4*>(sm.qk[3])[lane];
+        k4[0] = kc.x; k4[1] = kc.y; k4[2] = kc.z; k4[3] = kc.w;
+        v4[0] = vc.x; v4[1] = vc.y; v4[2] = vc.z; v4[3] = vc.w;
+        return;
+    }
+    unpack_bf16x4(kk, k4);
+    unpack_bf16x4(vv, v4);
+    if (t < num_sink) {
+        rope_warp(k4, hp.cs1);
+        unpack_bf16x4(pack_bf16x4(k4), k4);
+    }
+}
+
+// Merge the 8 warps' online-softmax states: into the staged attention output of the group
+// (K = 256 layout) or, for a split of a long context, into the partial buffers.
+__device__ __forceinline__ void merge_warps(Smem& sm, const FusedArgs& a, const AttnAcc& acc, int g,
+                                         int split, bool to_partials) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    bar_consumers();  // staging buffers alias the merge buffer
+    float* mb = reinterpret_cast<float*>(sm.xs4) + 2 * GRP;  // [NCW][2][HD] after the output
+    reinterpret_cast<float4*>(mb + (warp * 2 + 0) * HD)[lane] =
+        make_float4(acc.o0[0], acc.o0[1], acc.o0[2], acc.o0[3]);
+    reinterpret_cast<float4*>(mb + (warp * 2 + 1) * HD)[lane] =
+        make_float4(acc.o1[0], acc.o1[1], acc.o1[2], acc.o1[3]);
+    if (lane == 0) {
+        sm.mlw[warp][0] = make_float2(acc.m0, acc.l0);
+        sm.mlw[warp][1] = make_float2(acc.m1, acc.l1);
+    }
+    bar_consumers();
+    const int hq = tid >> 7, d = tid & (HD - 1);
+    float M = -FLT_MAX;
+#pragma unroll
+    for (int w = 0; w < NCW; ++w)
+        if (sm.mlw[w][hq].y > 0.0f) M = fmaxf(M, sm.mlw[w][hq].x);
+    float L = 0.0f, o = 0.0f;
+#pragma unroll
+    for (int w = 0; w < NCW; ++w) {
+        const float2 ml = sm.mlw[w][hq];
+        if (ml.y > 0.0f) {
+            const float sc = expf(ml.x - M);
+            L += ml.y * sc;
+            o += mb[(w * 2 + hq) * HD + d] * sc;
+        }
+    }
+    if (to_partials) {
+        const size_t pi = static_cast<size_t>(2 * g + hq) * a.s_max + split;
+        a.part_o[pi * HD + d] = o;
+        if (d == 0) a.part_ml[pi] = make_float2(M, L);
+    } else {
+        xs_put(sm, tid, o / L);
+    }
+    bar_consumers();
+}
+
+// Phase BC attention (<= 128 cached positions): all positions of KV head g from the KV pages the
+// producer streamed into the ring (shared chunks, released by thread 0 after each page).
+__device__ __forceinline__ void attention_short(Smem& sm, const FusedArgs& a, const HeadPre& hp,
+                                             int kv_len, int kv_pos, int num_sink, int g,
+                                             uint32_t q0) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const float4 q0v = reinterpret_cast<const float4*>(sm.qk[0])[lane];
+    const float4 q1v = reinterpret_cast<const float4*>(sm.qk[1])[lane];
+    AttnAcc acc;
+    acc_init(acc);
+    const int np = (kv_len + kPageTokens - 1) / kPageTokens;
+    for (int j = 0; j < np; ++j) {
+        const uint32_t qq = q0 + j;
+        const int slot = qq % NS;
+        if (warp_wait_full(sm, slot, (qq / NS) & 1, a)) {
+            const uint8_t* page = sm.ring[slot];
+            for (int tt = warp; tt < kPageTokens; tt += NCW) {
+                const int t = j * kPageTokens + tt;
+                if (t >= kv_len) break;
+                const uint2 kk = reinterpret_cast<const uint2*>(page + tt * HD * 2)[lane];
+                const uint2 vv = reinterpret_cast<const uint2*>(page + PAGE_BYTES + tt * HD * 2)[lane];
+                float k4[4], v4[4];
+                kv_lane(sm, hp, t, kv_pos, num_sink, kk, vv, k4, v4);
+                acc_add(acc, k4, v4, q0v, q1v);
+            }
+        }
+        bar_consumers();
+        if (threadIdx.x == 0) mbar_arrive(&sm.empty[slot]);
+    }
+    merge_warps(sm, a, acc, g, 0, false);
+}
+
+// Phase B attention item (> 128 cached positions): split `split` of KV head g, positions staged
+// from global memory (L2) in sub-chunks; writes (max, sum, unnormalised output) partials.
+__device__ __forceinline__ void attention_long(Smem& sm, const FusedArgs& a, const HeadPre& hp,
+                                            int kv_len, int kv_pos, int num_sink, int splits,
+                                            int l, int g, int split) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int chunk = (kv_len + splits - 1) / splits;
+    const int t0 = split * chunk, t1 = min(kv_len, t0 + chunk);
+    const uint16_t* kc = a.k_cache + static_cast<size_t>(l) * a.layer_elems;
+    const uint16_t* vc = a.v_cache + static_cast<size_t>(l) * a.layer_elems;
+    const float4 q0v = reinterpret_cast<const float4*>(sm.qk[0])[lane];
+    const float4 q1v = reinterpret_cast<const float4*>(sm.qk[1])[lane];
+    AttnAcc acc;
+    acc_init(acc);
     uint4* stage = reinterpret_cast<uint4*>(sm.xs4);  // [ATT_TOK][K 16 | V 16] uint4
     for (int tb = t0; tb < t1; tb += ATT_TOK) {
         const int n = min(ATT_TOK, t1 - tb);
@@ -420,106 +841,85 @@ __device__ void attention_item(Smem& sm, const FusedArgs& a, const LayerWeights&
         for (int tok = warp; tok < n; tok += NCW) {
             const uint2 kk = reinterpret_cast<const uint2*>(stage + tok * 32)[lane];
             const uint2 vv = reinterpret_cast<const uint2*>(stage + tok * 32 + 16)[lane];
-            const float k4[4] = {bf16_lo(kk.x), bf16_hi(kk.x), bf16_lo(kk.y), bf16_hi(kk.y)};
-            const float v4[4] = {bf16_lo(vv.x), bf16_hi(vv.x), bf16_lo(vv.y), bf16_hi(vv.y)};
-            float d0 = k4[0] * q0.x;
-            d0 = fmaf(k4[1], q0.y, d0);
-            d0 = fmaf(k4[2], q0.z, d0);
-            d0 = fmaf(k4[3], q0.w, d0);
-            float d1 = k4[0] * q1.x;
-            d1 = fmaf(k4[1], q1.y, d1);
-            d1 = fmaf(k4[2], q1.z, d1);
-            d1 = fmaf(k4[3], q1.w, d1);
-            const float s0 = warp_sum(d0) / sq, s1 = warp_sum(d1) / sq;
-            const float n0 = fmaxf(m0, s0), n1 = fmaxf(m1, s1);
-            const float a0 = expf(m0 - n0), a1 = expf(m1 - n1);
-            const float p0 = expf(s0 - n0), p1 = expf(s1 - n1);
-            l0 = l0 * a0 + p0;
-            l1 = l1 * a1 + p1;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                o0[j] = o0[j] * a0 + p0 * v4[j];
-                o1[j] = o1[j] * a1 + p1 * v4[j];
-            }
-            m0 = n0;
-            m1 = n1;
+            float k4[4], v4[4];
+            kv_lane(sm, hp, tb + tok, kv_pos, num_sink, kk, vv, k4, v4);
+            acc_add(acc, k4, v4, q0v, q1v);
         }
         bar_consumers();
     }
-    // Merge the warps and write this split's partial (max, sum, unnormalised output).
-    float* mb = reinterpret_cast<float*>(sm.xs4);  // [NCW][2][HD]
-    reinterpret_cast<float4*>(mb + (warp * 2 + 0) * HD)[lane] = make_float4(o0[0], o0[1], o0[2], o0[3]);
-    reinterpret_cast<float4*>(mb + (warp * 2 + 1) * HD)[lane] = make_float4(o1[0], o1[1], o1[2], o1[3]);
-    if (lane == 0) {
-        sm.mlw[warp][0] = make_float2(m0, l0);
-        sm.mlw[warp][1] = make_float2(m1, l1);
-    }
-    bar_consumers();
-    {
-        const int hq = tid >> 7, d = tid & (HD - 1);
-        float M = -FLT_MAX;
-#pragma unroll
-        for (int w2 = 0; w2 < NCW; ++w2)
-            if (sm.mlw[w2][hq].y > 0.0f) M = fmaxf(M, sm.mlw[w2][hq].x);
-        float L = 0.0f, acc = 0.0f;
-#pragma unroll
-        for (int w2 = 0; w2 < NCW; ++w2) {
-            const float2 ml = sm.mlw[w2][hq];
-            if (ml.y > 0.0f) {
-                const float sc = expf(ml.x - M);
-                L += ml.y * sc;
-                acc += mb[(w2 * 2 + hq) * HD + d] * sc;
-            }
-        }
-        const size_t pi = static_cast<size_t>(2 * g + hq) * a.s_max + s;
-        a.part_o[pi * HD + d] = acc;
-        if (d == 0) a.part_ml[pi] = make_float2(M, L);
-    }
+    merge_warps(sm, a, acc, g, split, true);
 }
 
-// Phase C prologue: merge the split partials of all 16 heads into the staged attention output
-// (permuted layout for K = 2048).
-__device__ void stage_attention(Smem& sm, const FusedArgs& a, int S) {
+// Phase C prologue (> 128 positions): combine the split partials of heads 2g, 2g+1.
+__device__ __forceinline__ void combine_group(Smem& sm, const FusedArgs& a, int S, int g) {
     const int t = threadIdx.x;
-    const int head = t >> 4, d0 = (t & 15) * 8;
+    const int head = 2 * g + (t >> 7), d = t & (HD - 1);
     float M = -FLT_MAX;
     for (int s = 0; s < S; ++s) {
         const float2 ml = __ldcg(a.part_ml + head * a.s_max + s);
         if (ml.y > 0.0f) M = fmaxf(M, ml.x);
     }
-    float L = 0.0f;
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float L = 0.0f, o = 0.0f;
     for (int s = 0; s < S; ++s) {
         const size_t pi = static_cast<size_t>(head) * a.s_max + s;
         const float2 ml = __ldcg(a.part_ml + pi);
         if (ml.y > 0.0f) {
             const float sc = expf(ml.x - M);
             L += ml.y * sc;
-            const float4 u = __ldcg(reinterpret_cast<const float4*>(a.part_o + pi * HD + d0));
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(a.part_o + pi * HD + d0 + 4));
-            acc[0] += u.x * sc; acc[1] += u.y * sc; acc[2] += u.z * sc; acc[3] += u.w * sc;
-            acc[4] += v.x * sc; acc[5] += v.y * sc; acc[6] += v.z * sc; acc[7] += v.w * sc;
+            o += __ldcg(a.part_o + pi * HD + d) * sc;
         }
     }
-    const int vidx = (head * HD + d0) / 8;
-    sm.xs4[vidx] = make_float4(acc[0] / L, acc[1] / L, acc[2] / L, acc[3] / L);
-    sm.xs4[QD / 8 + vidx] = make_float4(acc[4] / L, acc[5] / L, acc[6] / L, acc[7] / L);
+    xs_put(sm, t, o / L);
     bar_consumers();
 }
 
-// Phase E prologue: stage h (K = 3072) in the permuted layout.
-__device__ void stage_h(Smem& sm, const FusedArgs& a) {
-    const int t = threadIdx.x;
-#pragma unroll
-    for (int k = 0; k < 3; ++k) {
-        const int f = t + k * NCT;  // float4 index: elements 4f..4f+3
-        sm.xs4[(f & 1) * (H / 8) + (f >> 1)] = __ldcg(reinterpret_cast<const float4*>(a.h) + f);
+// Phase DE tail: Y[l] += sum_i h_i * w2t[i] over this CTA's MLP indices (shared chunks: warp w
+// owns output columns [128w, 128w+128), 4 per lane), then one float4 atomic per lane.
+__device__ __forceinline__ void down_splitk(Smem& sm, const FusedArgs& a, uint32_t q0, int n,
+                                         float* y) {
+    constexpr int RPC = RPC_ROW;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nch = (n + RPC - 1) / RPC;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int ci = 0; ci < nch; ++ci) {
+        const uint32_t qq = q0 + ci;
+        const int slot = qq % NS;
+        if (warp_wait_full(sm, slot, (qq / NS) & 1, a)) {
+            const int rn = min(RPC, n - ci * RPC);
+            for (int j = 0; j < rn; ++j) {
+                if (!Q3_CHECK(ci * RPC + j < 64, 60, ci, j, n)) break;
+                const float hv = sm.hbuf[ci * RPC + j];
+                const uint2 wv = reinterpret_cast<const uint2*>(sm.ring[slot] + j * D * 2 +
+                                                                warp * 256)[lane];
+                acc[0] = fmaf(hv, bf16_lo(wv.x), acc[0]);
+                acc[1] = fmaf(hv, bf16_hi(wv.x), acc[1]);
+                acc[2] = fmaf(hv, bf16_lo(wv.y), acc[2]);
+                acc[3] = fmaf(hv, bf16_hi(wv.y), acc[3]);
+            }
+        }
+        bar_consumers();
+        if (threadIdx.x == 0) mbar_arrive(&sm.empty[slot]);
     }
-    bar_consumers();
+    atomicAdd(reinterpret_cast<float4*>(y + warp * 128 + lane * 4),
+              make_float4(acc[0], acc[1], acc[2], acc[3]));
 }
 
-// Greedy argmax over the per-CTA partials (consumer warp 0), lowest index on ties.
-__device__ int reduce_argmax(const FusedArgs& a, int G) {
+// Write back the attention-sink rows of KV head g rotated by RoPE(position 1) (:817-827); every
+// reader of this step applied the same rotation on the fly.
+__device__ __forceinline__ void sink_writeback(const FusedArgs& a, const HeadPre& hp, int l, int g,
+                                            int num_sink) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp >= num_sink) return;
+    uint16_t* kcache = a.k_cache + static_cast<size_t>(l) * a.layer_elems;
+    uint2* row = reinterpret_cast<uint2*>(kcache + paged(a.page_table, warp, g));
+    float y[4];
+    unpack_bf16x4(__ldcg(row + lane), y);
+    rope_warp(y, hp.cs1);
+    row[lane] = pack_bf16x4(y);
+}
+
+// Greedy argmax over the per-CTA partials (one warp), lowest index on ties.
+__device__ __forceinline__ int reduce_argmax(const FusedArgs& a, int G) {
     const int lane = threadIdx.x & 31;
     float bv = -FLT_MAX;
     int bi = INT_MAX;
@@ -543,6 +943,81 @@ __device__ int reduce_argmax(const FusedArgs& a, int G) {
     return bi == INT_MAX ? 0 : bi;
 }
 
+__device__ __forceinline__ void stamp(const FusedArgs& a, unsigned kk, int G, int c, int which) {
+    if (a.prof && threadIdx.x == 0) {
+        a.prof[(static_cast<size_t>(kk) * G + c) * 8 + which] = globaltimer();
+    }
+}
+
+// Phase entry: thread 0 waits until every CTA has arrived for phases < k and publishes one
+// verdict that all consumer threads read after the same barrier (so all leave together on abort).
+__device__ __forceinline__ bool phase_begin(Smem& sm, const FusedArgs& a, unsigned k, int G, int c) {
+    stamp(a, k, G, c, 0);
+    if (threadIdx.x == 0) {
+        const bool ok = k == 0 || grid_wait(a, G * k + a.barrier_offset, &sm.abort_flag, 4);
+        sm.go = ok && sm.abort_flag == 0;
+    }
+    bar_consumers();
+    stamp(a, k, G, c, 1);
+    return sm.go != 0;
+}
+
+// Phase exit: all consumer threads are done with phase k; thread 0 arrives (release).
+__device__ __forceinline__ void phase_end(Smem& sm, const FusedArgs& a, unsigned k, int G, int c) {
+    stamp(a, k, G, c, 6);
+    bar_consumers();
+    stamp(a, k, G, c, 7);
+    if (threadIdx.x == 0) {
+        red_release_add(a.bar, 1u);
+        if (a.prof) {
+            // Summed ring-wait cycles of all consumer warps in this phase.
+            a.prof[(static_cast<size_t>(k) * G + c) * 8 + 5] = sm.wait_cycles;
+            sm.wait_cycles = 0;
+        }
+    }
+}
+
+// Phase A input: the embedding row of the step's token (layer 0; the token is the greedy argmax of
+// the previous step, or the teacher-forced one) or x = Xprev + Y[l-1]; writes this CTA's slice of
+// Xcur and (CTA 0) the debug tap. Returns this thread's 4 elements.
+__device__ __forceinline__ float4 phase_a_input(Smem& sm, const FusedArgs& a, const StepParams& sp0,
+                                             int st, int l, float* xc, const float* xp, int G,
+                                             int c) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    float4 xv;
+    if (l == 0) {
+        if (warp == 0) {
+            int tok = sp0.token;
+            if (st > 0) {
+                const int best = reduce_argmax(a, G);
+                const int idx = sp0.step + st;
+                tok = (a.forced && idx < sp0.n_forced) ? __ldg(a.forced + idx) : best;
+                if (c == 0 && lane == 0) a.token_log[idx - 1] = best;
+            }
+            if (lane == 0) sm.token = tok;
+        }
+        bar_consumers();
+        const uint2 e = __ldg(reinterpret_cast<const uint2*>(
+                                  a.embed + static_cast<size_t>(sm.token) * D) + tid);
+        xv = make_float4(bf16_lo(e.x), bf16_hi(e.x), bf16_lo(e.y), bf16_hi(e.y));
+        // Zero this CTA's share of the down-projection accumulators for the step.
+        const Span ys = part(a.n_layers * D, G, c);
+        for (int i = tid; i < ys.n; i += NCT) a.ybuf[ys.r0 + i] = 0.0f;
+    } else {
+        xv = add4(__ldcg(reinterpret_cast<const float4*>(xp) + tid),
+                  __ldcg(reinterpret_cast<const float4*>(a.ybuf + (l - 1) * D) + tid));
+    }
+    const Span xs = part(D, G, c);
+    const float e4[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int r = 4 * tid + j;
+        if (r >= xs.r0 && r < xs.r0 + xs.n) xc[r] = e4[j];
+    }
+    if (a.taps && c == 0) reinterpret_cast<float4*>(a.taps + static_cast<size_t>(l) * D)[tid] = xv;
+    return xv;
+}
+
 __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
@@ -555,6 +1030,7 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) 
             mbar_init(&sm.empty[i], 1);
         }
         sm.abort_flag = 0;
+        sm.wait_cycles = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
@@ -569,93 +1045,103 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) 
 
     // ---------------- consumers
     const StepParams sp0 = *a.sp;
+    const int P = G / NKV;
+    const bool in_grp = c < NKV * P;
+    const int g = c % NKV, gp = c / NKV;
     unsigned k = 0;  // global phase index
     uint32_t q = 0;  // ring chunk index
-    float dummy_v = 0.0f;
-    int dummy_i = 0;
-    volatile int* abort = &sm.abort_flag;
-
-    // Phase entry: thread 0 waits for the previous phase grid-wide and publishes one verdict
-    // that every consumer thread reads after the same barrier (so all leave together on abort).
-    auto begin = [&](unsigned kk) -> bool {
-        if (tid == 0) {
-            const bool ok = kk == 0 || grid_wait(a, G * kk + a.barrier_offset, abort);
-            sm.go = ok && *abort == 0;
-        }
-        bar_consumers();
-        return sm.go != 0;
-    };
-    auto end = [&]() {
-        bar_consumers();
-        if (tid == 0) {
-            __threadfence();
-            atomicAdd(a.bar, 1u);
-        }
-    };
 
     for (int st = 0; st < a.n_steps; ++st) {
-        StepPos p;
-        p.pos = sp0.pos + st;
-        step_positions(p.pos, a.ctx, &p.num_sink, &p.kv_pos, &p.kv_len);
-        p.splits = min(max((p.kv_len + ATT_TOK - 1) / ATT_TOK, 1), a.s_max);
+        const StepPos p = step_pos(a, sp0, st);
         for (int l = 0; l < a.n_layers; ++l) {
-            const LayerWeights w = a.layers[l];
-            // ---- A: x -> RmsNorm -> [wq;wk;wv]
-            if (!begin(k++)) return;
-            float4 xv;
-            if (l == 0) {
-                if (warp == 0) {
-                    int tok = sp0.token;
-                    if (st > 0) {
-                        const int best = reduce_argmax(a, G);
-                        const int idx = sp0.step + st;
-                        tok = (a.forced && idx < sp0.n_forced) ? __ldg(a.forced + idx) : best;
-                        if (c == 0 && lane == 0) a.token_log[idx - 1] = best;
-                    }
-                    if (lane == 0) sm.token = tok;
-                }
-                bar_consumers();
-                xv = load_embed(a, sm.token);
-            } else {
-                xv = load_x_global(a);
+            const FusedLayer w = a.layers[l];
+            float* xc = a.xbuf + (l & 1) * D;
+            const float* xp = a.xbuf + ((l & 1) ^ 1) * D;
+            // ---- A: x -> Xcur, RmsNorm -> [wq;wk;wv]
+            {
+                const uint2 nw = load_norm(w.attn_norm);
+                if (!phase_begin(sm, a, k, G, c)) return;
+                const float4 xv = phase_a_input(sm, a, sp0, st, l, xc, xp, G, c);
+                stage_norm(sm, xv, nw, a.eps);
+                stamp(a, k, G, c, 3);
+                const Span s = part(QKV_ROWS, G, c);
+                consume_rows<D, RPC_ROW, kStore>(sm, a, q, s.r0, s.n, a.qkv, QKV_ROWS);
+                q += chunks_of(s.n, RPC_ROW);
+                phase_end(sm, a, k++, G, c);
             }
-            if (a.taps && c == 0) reinterpret_cast<float4*>(a.taps + static_cast<size_t>(l) * D)[tid] = xv;
-            stage_norm(sm, xv, w.attn_norm, a.eps);
-            consume<D, kStore>(sm, a, q, part(QKV_ROWS, G, c), a.qkv, dummy_v, dummy_i);
-            end();
-            // ---- B: QK-norm, RoPE, KV write, attention partials
-            if (!begin(k++)) return;
-            if (c < NKV * p.splits) attention_item(sm, a, w, l, p, c);
-            end();
-            // ---- C: combine, x += wo . attn
-            if (!begin(k++)) return;
-            stage_attention(sm, a, p.splits);
-            consume<QD, kResid>(sm, a, q, part(D, G, c), a.x, dummy_v, dummy_i);
-            end();
-            // ---- D: x -> RmsNorm -> silu(w1 .) * (w3 .)
-            if (!begin(k++)) return;
-            stage_norm(sm, load_x_global(a), w.mlp_norm, a.eps);
-            consume<D, kPair>(sm, a, q, part(H, G, c), a.h, dummy_v, dummy_i);
-            end();
-            // ---- E: x += w2 . h
-            if (!begin(k++)) return;
-            stage_h(sm, a);
-            consume<H, kResid>(sm, a, q, part(D, G, c), a.x, dummy_v, dummy_i);
-            end();
+            HeadPre hp;
+            head_preload(hp, a, w, p.pos);
+            const Span os = part(D, P, gp);
+            if (p.shrt) {
+                // ---- BC: attention of KV head g from the ring, split-K o_proj into Xcur
+                if (!phase_begin(sm, a, k, G, c)) return;
+                if (in_grp) {
+                    prep_heads(sm, a, hp, l, g, p.kv_pos, gp == 0);
+                    stamp(a, k, G, c, 2);
+                    attention_short(sm, a, hp, p.kv_len, p.kv_pos, p.num_sink, g, q);
+                    q += chunks_of(p.kv_len, kPageTokens);
+                    stamp(a, k, G, c, 3);
+                    consume_rows<GRP, RPC_GRP, kRed>(sm, a, q, os.r0, os.n, xc, D);
+                    q += chunks_of(os.n, RPC_GRP);
+                }
+                phase_end(sm, a, k++, G, c);
+            } else {
+                // ---- B: split-K attention partials
+                if (!phase_begin(sm, a, k, G, c)) return;
+                if (c < NKV * p.splits) {
+                    const int gg = c % NKV, s = c / NKV;
+                    const int chunk = (p.kv_len + p.splits - 1) / p.splits;
+                    const bool own =
+                        p.kv_pos >= s * chunk && p.kv_pos < min(p.kv_len, (s + 1) * chunk);
+                    prep_heads(sm, a, hp, l, gg, p.kv_pos, own);
+                    attention_long(sm, a, hp, p.kv_len, p.kv_pos, p.num_sink, p.splits, l, gg, s);
+                }
+                phase_end(sm, a, k++, G, c);
+                // ---- C: combine + split-K o_proj into Xcur
+                if (!phase_begin(sm, a, k, G, c)) return;
+                if (in_grp) {
+                    combine_group(sm, a, p.splits, g);
+                    consume_rows<GRP, RPC_GRP, kRed>(sm, a, q, os.r0, os.n, xc, D);
+                    q += chunks_of(os.n, RPC_GRP);
+                }
+                phase_end(sm, a, k++, G, c);
+            }
+            // ---- DE: RmsNorm -> silu(w1 .) * (w3 .) -> split-K down into Y[l]
+            {
+                const uint2 mw = load_norm(w.mlp_norm);
+                if (!phase_begin(sm, a, k, G, c)) return;
+                stage_norm(sm, __ldcg(reinterpret_cast<const float4*>(xc) + tid), mw, a.eps);
+                stamp(a, k, G, c, 2);
+                const Span hs = part(H, G, c);
+                consume_rows<D, RPC_PAIR, kPair>(sm, a, q, hs.r0, hs.n, sm.hbuf, 64);
+                q += chunks_of(hs.n, RPC_PAIR);
+                bar_consumers();
+                stamp(a, k, G, c, 3);
+                down_splitk(sm, a, q, hs.n, a.ybuf + static_cast<size_t>(l) * D);
+                q += chunks_of(hs.n, RPC_ROW);
+                stamp(a, k, G, c, 4);
+                if (c < NKV && p.num_sink > 0) sink_writeback(a, hp, l, c, p.num_sink);
+                phase_end(sm, a, k++, G, c);
+            }
         }
         // ---- final RmsNorm + lm_head + per-CTA argmax
-        if (!begin(k++)) return;
-        const float4 xv = load_x_global(a);
+        const uint2 fw = load_norm(a.final_norm);
+        if (!phase_begin(sm, a, k, G, c)) return;
+        const float* xl = a.xbuf + ((a.n_layers - 1) & 1) * D;
+        const float4 xv = add4(__ldcg(reinterpret_cast<const float4*>(xl) + tid),
+                               __ldcg(reinterpret_cast<const float4*>(
+                                          a.ybuf + static_cast<size_t>(a.n_layers - 1) * D) + tid));
         if (a.taps && c == 0) {
             reinterpret_cast<float4*>(a.taps + static_cast<size_t>(a.n_layers) * D)[tid] = xv;
         }
-        stage_norm(sm, xv, a.final_norm, a.eps);
-        float bv = -FLT_MAX;
-        int bi = INT_MAX;
-        consume<D, kLogits>(sm, a, q, part(a.vocab, G, c), a.logits, bv, bi);
-        if (lane == 0) sm.best[warp] = make_float2(bv, __int_as_float(bi));
+        stage_norm(sm, xv, fw, a.eps);
+        const Span vs = part(a.vocab, G, c);
+        consume_rows<D, RPC_ROW, kLogits>(sm, a, q, vs.r0, vs.n, a.logits, a.vocab);
+        q += chunks_of(vs.n, RPC_ROW);
         bar_consumers();
         if (tid == 0) {
+            float bv = sm.best[0].x;
+            int bi = __float_as_int(sm.best[0].y);
             for (int w2 = 1; w2 < NCW; ++w2) {
                 const float v = sm.best[w2].x;
                 const int i = __float_as_int(sm.best[w2].y);
@@ -666,12 +1152,12 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) 
             }
             a.am_part[c] = make_float2(bv, __int_as_float(bi));
         }
-        end();
+        phase_end(sm, a, k++, G, c);
     }
 
     // Final greedy token and the device-side advance of the step parameters (CTA 0).
     if (c == 0) {
-        if (!begin(k)) return;
+        if (!phase_begin(sm, a, k, G, c)) return;
         if (warp == 0) {
             const int best = reduce_argmax(a, G);
             if (lane == 0) {
@@ -688,6 +1174,45 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) 
     }
 }
 
+// ------------------------------------------------------------------ weight re-layout
+
+__global__ void permute_wo_kernel(const uint16_t* __restrict__ wo, uint16_t* __restrict__ wop) {
+    // wop[g][r][j] = wo[r][256 g + j]; one thread per 8-element vector.
+    const size_t n = static_cast<size_t>(D) * QD / 8;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const size_t e = i * 8;
+        const int r = static_cast<int>(e / QD), col = static_cast<int>(e % QD);
+        const int gg = col / GRP, j = col % GRP;
+        const uint4 v = *reinterpret_cast<const uint4*>(wo + e);
+        *reinterpret_cast<uint4*>(wop + (static_cast<size_t>(gg) * D + r) * GRP + j) = v;
+    }
+}
+
+__global__ void swizzle_rows_kernel(const uint16_t* __restrict__ src, uint16_t* __restrict__ dst,
+                                    size_t rows, int K) {
+    // Odd rows: swap the two 64-byte halves of every 128-byte block (the layout mma_rows8 reads).
+    const size_t units = static_cast<size_t>(K) / 8;
+    const size_t n = rows * units;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const size_t r = i / units, u = i % units;
+        const size_t du = u ^ ((r & 1) << 2);
+        reinterpret_cast<uint4*>(dst)[r * units + du] = reinterpret_cast<const uint4*>(src)[i];
+    }
+}
+
+__global__ void transpose_w2_kernel(const uint16_t* __restrict__ w2, uint16_t* __restrict__ w2t) {
+    // w2t[i][r] = w2[r][i] for w2 [1024][3072], through 32x32 shared tiles.
+    __shared__ uint16_t tile[32][33];
+    const int i0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+    for (int y = threadIdx.y; y < 32; y += blockDim.y)
+        tile[y][threadIdx.x] = w2[static_cast<size_t>(r0 + y) * H + i0 + threadIdx.x];
+    __syncthreads();
+    for (int y = threadIdx.y; y < 32; y += blockDim.y)
+        w2t[static_cast<size_t>(i0 + y) * D + r0 + threadIdx.x] = tile[threadIdx.x][y];
+}
+
 }  // namespace
 
 bool fused_supported(const q3_config& c) {
@@ -696,6 +1221,10 @@ bool fused_supported(const q3_config& c) {
 }
 
 size_t fused_smem_bytes() { return sizeof(Smem); }
+
+int fused_phases_per_step(int n_layers, int kv_len) {
+    return n_layers * (kv_len <= T_SHORT ? 3 : 4) + 1;
+}
 
 int fused_grid(int device) {
     int sms = 0;
@@ -706,6 +1235,8 @@ int fused_grid(int device) {
     Q3_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_fused_kernel, NT,
                                                           sizeof(Smem)));
     if (per_sm < 1) return 0;
+    // Every CTA must own at most 64 MLP indices (the h buffer) and the grid must cover 8 groups.
+    if (sms < 48) return 0;
     return sms;
 }
 
@@ -721,6 +1252,22 @@ void launch_decode_fused(const FusedArgs& a, int grid, cudaStream_t s) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     Q3_CUDA(cudaLaunchKernelEx(&cfg, decode_fused_kernel, a));
+}
+
+void launch_permute_wo(const uint16_t* wo, uint16_t* wop, cudaStream_t s) {
+    permute_wo_kernel<<<1024, 256, 0, s>>>(wo, wop);
+    Q3_CUDA(cudaGetLastError());
+}
+
+void launch_swizzle_rows(const uint16_t* src, uint16_t* dst, size_t rows, int K, cudaStream_t s) {
+    if (K % 64 != 0) throw std::invalid_argument("row swizzle needs K % 64 == 0");
+    swizzle_rows_kernel<<<2048, 256, 0, s>>>(src, dst, rows, K);
+    Q3_CUDA(cudaGetLastError());
+}
+
+void launch_transpose_w2(const uint16_t* w2, uint16_t* w2t, cudaStream_t s) {
+    transpose_w2_kernel<<<dim3(H / 32, D / 32), dim3(32, 8), 0, s>>>(w2, w2t);
+    Q3_CUDA(cudaGetLastError());
 }
 
 }  // namespace q3

@@ -11,21 +11,38 @@
 
 namespace q3 {
 
+// Per-layer weights as the fused kernel streams them: copies made at load time so that every
+// CTA's share of a phase is one contiguous byte range, with the row-parity swizzle on the matrices
+// multiplied by MMAs (wqkv, wop, w1, w3 and the lm_head copy):
+//   wop[g][r][j] = wo[r][256*g + j]   (o_proj split by KV-head group: [8][1024][256])
+//   w2t[i][r]    = w2[r][i]           (down_proj split by MLP index: [3072][1024])
+struct FusedLayer {
+    const uint16_t* wqkv;       // [4096][1024]: wq; wk; wv rows (swizzled)
+    const uint16_t* wop;        // [8][1024][256] (swizzled)
+    const uint16_t* w1;         // [3072][1024] (swizzled)
+    const uint16_t* w3;         // [3072][1024] (swizzled)
+    const uint16_t* w2t;        // [3072][1024]
+    const uint16_t* attn_norm;  // [1024]
+    const uint16_t* q_norm;     // [128]
+    const uint16_t* k_norm;     // [128]
+    const uint16_t* mlp_norm;   // [1024]
+};
+
 struct FusedArgs {
-    const LayerWeights* layers;  // device array [n_layers]
-    const uint16_t* embed;       // [vocab, 1024] (also the tied classifier)
-    const uint16_t* lm_head;     // classifier rows (== embed when tied)
+    const FusedLayer* layers;    // device array [n_layers]
+    const uint16_t* embed;       // [vocab, 1024] (original layout, for the embedding gather)
+    const uint16_t* lm_head;     // classifier rows, swizzled copy
     const uint16_t* final_norm;  // [1024]
-    uint16_t* k_cache;           // paged pools, layer l at + l * layer_elems
+    uint16_t* k_cache;           // paged pools [page][8][16][128], layer l at + l * layer_elems
     uint16_t* v_cache;
     size_t layer_elems;
     const int32_t* page_table;
-    const float2* rope;          // [rope_len][64]
+    const float2* rope;          // [rope_len][64] (cos, sin)
     int rope_len;
-    float* x;                    // [1024] residual stream
+    float* xbuf;                 // [2][1024] residual stream (ping-pong)
+    float* ybuf;                 // [n_layers][1024] down-projection accumulators
     float* qkv;                  // [4096]
-    float* h;                    // [3072]
-    float* part_o;               // [16][s_max][128]
+    float* part_o;               // [16][s_max][128]  (long-context attention)
     float2* part_ml;             // [16][s_max]
     float2* am_part;             // [grid] per-CTA (value, index) of the lm_head rows
     float* logits;               // [vocab]
@@ -39,6 +56,8 @@ struct FusedArgs {
     float eps;
     long long spin_cycles;       // bound of every wait, in SM clock cycles
     int barrier_offset;          // 0; a test sets 1 so that a grid wait can never complete
+    unsigned long long* prof;    // nullable: per (phase, CTA) globaltimer stamps [k][G][8]
+    unsigned long long* dbg;     // nullable: first failed self-check (builds with Q3_FUSED_CHECKS)
 };
 
 // Whether the fused kernel serves this config, and its launch geometry on `device`.
@@ -46,5 +65,13 @@ bool fused_supported(const q3_config& c);
 int fused_grid(int device);
 size_t fused_smem_bytes();
 void launch_decode_fused(const FusedArgs& a, int grid, cudaStream_t s);
+// Phases of one decode step at kv_len (3 per layer up to 128 positions, else 4; + lm_head).
+int fused_phases_per_step(int n_layers, int kv_len);
+// Re-layout kernels: wop / w2t, and the row-parity swizzle of every matrix the fused kernel
+// multiplies with tensor-core MMAs (in odd rows the two 64-byte halves of each 128-byte block are
+// swapped, which makes the MMA operand loads from shared memory bank-conflict free).
+void launch_permute_wo(const uint16_t* wo, uint16_t* wop, cudaStream_t s);
+void launch_transpose_w2(const uint16_t* w2, uint16_t* w2t, cudaStream_t s);
+void launch_swizzle_rows(const uint16_t* src, uint16_t* dst, size_t rows, int K, cudaStream_t s);
 
 }  // namespace q3

@@ -632,26 +632,93 @@ Model::Model(const std::string& path, int ctx, int device) : file_(path) {
         fused_grid_ = q3::fused_grid(device_);
         if (fused_grid_ >= 8) {
             fused_s_max_ = fused_grid_ / c.n_kv_heads;
-            fused_layers_.alloc(layers_.size() * sizeof(LayerWeights));
-            Q3_CUDA(cudaMemcpy(fused_layers_.ptr, layers_.data(), layers_.size() * sizeof(LayerWeights),
+            // The fused kernel's weight copies, per layer: [wq;wk;wv], wo split by KV-head group,
+            // w1 and w3 (row-parity swizzled), and w2 transposed; plus the swizzled lm_head.
+            const size_t qkv_elems = (qd + 2 * kvd) * D;
+            const size_t wo_elems = D * qd;
+            const size_t w13_elems = H * D;
+            const size_t w2_elems = D * H;
+            const size_t per_layer = qkv_elems + wo_elems + 2 * w13_elems + w2_elems;
+            fused_wperm_.alloc((per_layer * c.n_layers + V * D) * 2);
+            DeviceBuffer tmp;
+            tmp.alloc(wo_elems * 2);
+            cudaStream_t ls = engine_->stream();
+            std::vector<FusedLayer> fl(c.n_layers);
+            uint16_t* wp = static_cast<uint16_t*>(fused_wperm_.ptr);
+            for (int l = 0; l < c.n_layers; ++l) {
+                const LayerWeights& w = layers_[l];
+                uint16_t* qkv = wp + per_layer * l;
+                uint16_t* wop = qkv + qkv_elems;
+                uint16_t* w1 = wop + wo_elems;
+                uint16_t* w3 = w1 + w13_elems;
+                uint16_t* w2t = w3 + w13_elems;
+                launch_swizzle_rows(w.wqkv, qkv, qd + 2 * kvd, static_cast<int>(D), ls);
+                launch_permute_wo(w.wo, static_cast<uint16_t*>(tmp.ptr), ls);
+                launch_swizzle_rows(static_cast<uint16_t*>(tmp.ptr), wop, c.n_kv_heads * D,
+                                    static_cast<int>(wo_elems / (c.n_kv_heads * D)), ls);
+                launch_swizzle_rows(w.w1, w1, H, static_cast<int>(D), ls);
+                launch_swizzle_rows(w.w3, w3, H, static_cast<int>(D), ls);
+                launch_transpose_w2(w.w2, w2t, ls);
+                fl[l] = FusedLayer{qkv, wop, w1, w3, w2t, w.attn_norm, w.q_norm, w.k_norm,
+                                   w.mlp_norm};
+                Q3_CUDA(cudaStreamSynchronize(ls));  // tmp is reused by the next layer
+            }
+            fused_lm_ = wp + per_layer * c.n_layers;
+            launch_swizzle_rows(output_, const_cast<uint16_t*>(fused_lm_), V, static_cast<int>(D), ls);
+            Q3_CUDA(cudaStreamSynchronize(ls));
+            fused_layers_.alloc(fl.size() * sizeof(FusedLayer));
+            Q3_CUDA(cudaMemcpy(fused_layers_.ptr, fl.data(), fl.size() * sizeof(FusedLayer),
                                cudaMemcpyHostToDevice));
+            fused_xy_.alloc((2 + static_cast<size_t>(c.n_layers)) * D * 4);
             fused_part_o_.alloc(static_cast<size_t>(c.n_heads) * fused_s_max_ * c.head_dim * 4);
             fused_part_ml_.alloc(static_cast<size_t>(c.n_heads) * fused_s_max_ * sizeof(float2));
             fused_am_.alloc(static_cast<size_t>(fused_grid_) * sizeof(float2));
             fused_sync_.alloc(256);  // [0] arrival counter, [32] error word
             Q3_CUDA(cudaMemset(fused_sync_.ptr, 0, 256));
+            if (getenv("Q3_FUSED_CHECKS")) {
+                // Record buffer of the self-checking build (compiled with -DQ3_FUSED_CHECKS).
+                fused_dbg_.alloc(8 * sizeof(unsigned long long));
+                Q3_CUDA(cudaMemset(fused_dbg_.ptr, 0, fused_dbg_.bytes));
+            }
         } else {
             fused_grid_ = 0;
         }
     }
 }
 
-void Model::launch_fused(int n_steps, bool forced, bool taps, long long spin_cycles, int offset) {
+void Model::fused_profile(int32_t token, int pos, uint64_t* stamps, size_t cap, int* n_phases,
+                          int* grid) {
+    if (!fused_available()) throw std::runtime_error("fused decode path is not available");
+    check_token_pos(token, pos);
+    int ns = 0, kp = 0, kl = 0;
+    step_positions(pos, cfg_.max_seq_len, &ns, &kp, &kl);
+    const int phases = fused_phases_per_step(cfg_.n_layers, kl) + 1;
+    const size_t n = static_cast<size_t>(phases) * fused_grid_ * 8;
+    *n_phases = phases;
+    *grid = fused_grid_;
+    if (cap < n) throw std::invalid_argument("stamp buffer too small");
+    Engine& e = *engine_;
+    e.ensure_rope(pos + 2);
+    e.write_step(start_params(token, pos, 0));
+    DeviceBuffer prof;
+    prof.alloc(n * 8);
+    Q3_CUDA(cudaMemsetAsync(prof.ptr, 0, n * 8, e.stream()));
+    clear_fused_error();
+    launch_fused(1, false, false, 4000000000LL, 0, static_cast<unsigned long long*>(prof.ptr));
+    check_fused_error();
+    Q3_CUDA(cudaMemcpyAsync(stamps, prof.ptr, n * 8, cudaMemcpyDeviceToHost, e.stream()));
+    Q3_CUDA(cudaStreamSynchronize(e.stream()));
+}
+
+void Model::launch_fused(int n_steps, bool forced, bool taps, long long spin_cycles, int offset,
+                         unsigned long long* prof) {
     Engine& e = *engine_;
     FusedArgs a{};
-    a.layers = static_cast<const LayerWeights*>(fused_layers_.ptr);
+    a.prof = prof;
+    a.dbg = static_cast<unsigned long long*>(fused_dbg_.ptr);
+    a.layers = static_cast<const FusedLayer*>(fused_layers_.ptr);
     a.embed = embed_;
-    a.lm_head = output_;
+    a.lm_head = fused_lm_;
     a.final_norm = final_norm_;
     a.k_cache = e.k_layer(0);
     a.v_cache = e.v_layer(0);
@@ -659,9 +726,9 @@ void Model::launch_fused(int n_steps, bool forced, bool taps, long long spin_cyc
     a.page_table = e.page_table();
     a.rope = e.rope();
     a.rope_len = e.rope_len();
-    a.x = e.x();
+    a.xbuf = static_cast<float*>(fused_xy_.ptr);
+    a.ybuf = static_cast<float*>(fused_xy_.ptr) + 2 * cfg_.dim;
     a.qkv = e.qkv();
-    a.h = e.h();
     a.part_o = static_cast<float*>(fused_part_o_.ptr);
     a.part_ml = static_cast<float2*>(fused_part_ml_.ptr);
     a.am_part = static_cast<float2*>(fused_am_.ptr);
@@ -688,14 +755,30 @@ void Model::clear_fused_error() {
     if (!fused_enabled()) return;
     Q3_CUDA(cudaMemsetAsync(static_cast<unsigned*>(fused_sync_.ptr) + 32, 0, sizeof(unsigned),
                             engine_->stream()));
+    if (fused_dbg_.ptr) {
+        Q3_CUDA(cudaMemsetAsync(fused_dbg_.ptr, 0, fused_dbg_.bytes, engine_->stream()));
+    }
 }
 
 void Model::check_fused_error() {
     if (!fused_enabled()) return;
     unsigned err = 0;
+    unsigned long long dbg[8] = {};
     Q3_CUDA(cudaMemcpyAsync(&err, static_cast<unsigned*>(fused_sync_.ptr) + 32, sizeof(unsigned),
                             cudaMemcpyDeviceToHost, engine_->stream()));
+    if (fused_dbg_.ptr) {
+        Q3_CUDA(cudaMemcpyAsync(dbg, fused_dbg_.ptr, sizeof(dbg), cudaMemcpyDeviceToHost,
+                                engine_->stream()));
+    }
     Q3_CUDA(cudaStreamSynchronize(engine_->stream()));
+    if (dbg[0]) {
+        throw std::runtime_error(
+            "fused decode kernel self-check " + std::to_string(dbg[0]) + " failed in CTA " +
+            std::to_string(dbg[1]) + " thread " + std::to_string(dbg[2]) + " values " +
+            std::to_string(static_cast<long long>(dbg[3])) + " " +
+            std::to_string(static_cast<long long>(dbg[4])) + " " +
+            std::to_string(static_cast<long long>(dbg[5])));
+    }
     if (err) {
         throw DeviceTimeout("fused decode kernel: a bounded device-side wait gave up");
     }
@@ -1165,6 +1248,14 @@ q3_status q3_model_decode_path(const q3_model* model, int* path) {
     return guard([&] {
         if (!model || !path) throw std::invalid_argument("null argument");
         *path = model->m->fused_enabled() ? Q3_PATH_FUSED : Q3_PATH_LAYERWISE;
+    });
+}
+
+q3_status q3_model_fused_profile(q3_model* model, int32_t token, int pos, uint64_t* stamps_host,
+                                 size_t capacity, int* n_phases, int* grid) {
+    return guard([&] {
+        if (!model || !stamps_host || !n_phases || !grid) throw std::invalid_argument("null argument");
+        model->m->fused_profile(token, pos, stamps_host, capacity, n_phases, grid);
     });
 }
 

@@ -170,6 +170,9 @@ public:
     // Runs one fused launch whose grid-wide waits can never complete, with a short bound, and
     // reports whether the kernel returned with its timeout status set (failure-path test).
     bool fused_timeout_selftest();
+    // One fused decode step with per-(phase, CTA) globaltimer stamps [phases][grid][4].
+    void fused_profile(int32_t token, int pos, uint64_t* stamps, size_t cap, int* n_phases,
+                       int* grid);
 
 private:
     void check_token_pos(int32_t token, int pos) const;
@@ -177,7 +180,8 @@ private:
     void ensure_logs(int n);
     void enqueue_step(bool forced, bool taps);
     void run_steps(int n, bool forced, bool taps, float* logits_log_dev);
-    void launch_fused(int n_steps, bool forced, bool taps, long long spin_cycles, int offset);
+    void launch_fused(int n_steps, bool forced, bool taps, long long spin_cycles, int offset,
+                      unsigned long long* prof = nullptr);
     void clear_fused_error();
     void check_fused_error();
 
@@ -197,8 +201,10 @@ private:
     // Fused decode state.
     int fused_grid_ = 0;
     int fused_s_max_ = 0;
+    const uint16_t* fused_lm_ = nullptr;
     bool use_fused_ = true;
-    DeviceBuffer fused_layers_, fused_part_o_, fused_part_ml_, fused_am_, fused_sync_;
+    DeviceBuffer fused_layers_, fused_part_o_, fused_part_ml_, fused_am_, fused_sync_, fused_wperm_,
+        fused_xy_, fused_dbg_;
 };
 
 // class Block of the reference (include/inference.h:178-202) on one GPU.

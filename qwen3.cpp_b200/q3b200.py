@@ -19,7 +19,8 @@ from pathlib import Path
 import numpy as np
 
 PKG = Path(__file__).resolve().parent
-LIB_PATH = PKG / "lib" / "libq3b200.so"
+# Q3B200_LIB selects another build of the library (e.g. one compiled with self-checks).
+LIB_PATH = Path(os.environ.get("Q3B200_LIB", PKG / "lib" / "libq3b200.so"))
 
 F32P = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 U16P = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
@@ -105,6 +106,8 @@ def lib() -> C.CDLL:
         "q3_model_set_decode_path": [vp, C.c_int],
         "q3_model_decode_path": [vp, C.POINTER(C.c_int)],
         "q3_model_fused_timeout_selftest": [vp, C.POINTER(C.c_int)],
+        "q3_model_fused_profile": [vp, i32, C.c_int, vp, sz, C.POINTER(C.c_int),
+                                   C.POINTER(C.c_int)],
         "q3_block_create": [C.POINTER(Config), C.POINTER(vp), C.POINTER(sz), C.c_int, C.POINTER(vp)],
         "q3_block_forward": [vp, F32P, C.c_int, C.c_int, C.c_int, C.c_int],
         "q3_block_reset_cache": [vp],
@@ -192,6 +195,16 @@ class Qwen3:
     @decode_path.setter
     def decode_path(self, path: int) -> None:
         check(lib().q3_model_set_decode_path(self._h, int(path)))
+
+    def fused_profile(self, token: int, pos: int) -> np.ndarray:
+        """globaltimer stamps of one fused decode step, [phases, grid, 4] (ns)."""
+        c = self.config
+        cap = (5 * c["n_layers"] + 2) * 1024 * 8
+        buf = np.zeros(cap, np.uint64)
+        nph, grid = C.c_int(), C.c_int()
+        check(lib().q3_model_fused_profile(self._h, int(token), int(pos), buf.ctypes.data, cap,
+                                           C.byref(nph), C.byref(grid)))
+        return buf[: nph.value * grid.value * 8].reshape(nph.value, grid.value, 8)
 
     def fused_timeout_selftest(self) -> bool:
         t = C.c_int()
