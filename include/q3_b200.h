@@ -184,6 +184,20 @@ size_t q3_attn_workspace_size(int head_dim, int kv_len);
 q3_status q3_attn(float* out, void* workspace, const float* q, const uint16_t* k,
                   const uint16_t* v, int head_dim, int n_kv_heads, int kv_len, void* stream);
 
+/* q3_attn without a workspace, for callers that cannot allocate device memory when they call in
+ * (runtimes that own a fixed, pre-planned device-memory budget; callers that must avoid the device
+ * synchronisation cudaMalloc/cudaFree can cause). No counterpart in the reference, which runs on
+ * the CPU with caller-provided buffers. The split-K scratch is a static device array of
+ * q3_attn_noalloc_max_scratch() bytes (66,304: 64 splits of head_dim up to 256), held by every GPU
+ * that loads the library until exit; sizes that would need more are rejected with
+ * Q3_ERR_INVALID_ARGUMENT. The first call on each device looks up the array's device address with
+ * that device current - make it before any stream capture. All calls on a device share the
+ * array: calls that may overlap on the GPU race and must be ordered by the caller. Nothing in the
+ * array needs clearing between calls. Allocates nothing. */
+size_t q3_attn_noalloc_max_scratch(void);
+q3_status q3_attn_noalloc(float* out, const float* q, const uint16_t* k, const uint16_t* v,
+                          int head_dim, int n_kv_heads, int kv_len, void* stream);
+
 /* Sampler::Greedy (src/inference.cpp:703-709): index of the first maximum of logits[n], written
  * to *out_index (device int32). n == 0 is rejected like the reference's empty span. */
 q3_status q3_greedy(const float* logits, int n, int32_t* out_index, void* stream);

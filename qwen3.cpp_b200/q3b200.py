@@ -119,6 +119,7 @@ def lib() -> C.CDLL:
         "q3_rope": [vp, C.c_int, C.c_int, C.c_int, C.c_float, C.c_int, vp],
         "q3_ffn": [vp, vp, vp, vp, vp, vp, vp, C.c_int, C.c_int, vp],
         "q3_attn": [vp, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, vp],
+        "q3_attn_noalloc": [vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, vp],
         "q3_greedy": [vp, C.c_int, vp, vp],
     }
     for name, args in sig.items():
@@ -131,6 +132,8 @@ def lib() -> C.CDLL:
     L.q3_block_free.restype = None
     L.q3_attn_workspace_size.argtypes = [C.c_int, C.c_int]
     L.q3_attn_workspace_size.restype = sz
+    L.q3_attn_noalloc_max_scratch.argtypes = []
+    L.q3_attn_noalloc_max_scratch.restype = sz
     _lib = L
     return L
 
@@ -338,6 +341,14 @@ def attn_workspace_size(head_dim: int, kv_len: int) -> int:
 def attn(out_ptr, ws_ptr, q_ptr, k_ptr, v_ptr, head_dim, n_kv_heads, kv_len, stream=None):
     check(lib().q3_attn(out_ptr, ws_ptr, q_ptr, k_ptr, v_ptr, head_dim, n_kv_heads, kv_len,
                         stream))
+
+
+def attn_noalloc(out_ptr, q_ptr, k_ptr, v_ptr, head_dim, n_kv_heads, kv_len, stream=None):
+    """attn without a workspace: the scratch is a static device array inside the library, so the
+    call allocates nothing (for callers that cannot allocate device memory). Calls that may
+    overlap on the GPU share that array and must be ordered by the caller."""
+    check(lib().q3_attn_noalloc(out_ptr, q_ptr, k_ptr, v_ptr, head_dim, n_kv_heads, kv_len,
+                                stream))
 
 
 def greedy(logits_ptr, n, out_ptr, stream=None):
