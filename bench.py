@@ -38,6 +38,10 @@ VOCAB = 151936
 WEIGHT_BYTES = 1_191_968_768          # 28 layers + tied lm_head, bf16
 KV_BYTES_PER_POS = 2 * 28 * 1024 * 2  # K and V rows of every layer
 LM_HEAD_BYTES = VOCAB * 1024 * 2
+# DRAM traffic of one fused decode step (dram__bytes_read.sum + dram__bytes_write.sum), from an
+# `ncu --set full` capture of the timed one-step launch of `bench.py --steps 1 --warmup 3`
+# (kv_len 17): 1.1959 GB read + 5.22 MB written. Re-captured whenever the kernel changes.
+FUSED_TRAFFIC_PER_STEP = 1_201_132_000
 
 
 def peaks():
@@ -73,7 +77,7 @@ class Clocks:
         try:
             self.p = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", str(gpu_index), "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+                 "-i", str(gpu_index), "-lms", "20"], stdout=self.f, stderr=subprocess.DEVNULL)
         except (FileNotFoundError, OSError):
             self.p = None
 
@@ -277,7 +281,9 @@ def run_b200_arm(args):
             "decode_path": "fused" if fused else "layerwise",
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1),
                          "peak": pk["hbm_gbs"], "unit": "GB/s",
-                         "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
+                         "frac": round(achieved / pk["hbm_gbs"], 4),
+                         "traffic": FUSED_TRAFFIC_PER_STEP if fused else None,
+                         "traffic_unit": "bytes per decode step (ncu)" if fused else None,
                          "kernel": kernel, "peak_source": pk["source"]},
             "decode_step_roofline": {
                 "bytes_per_step": int(step_bytes),

@@ -70,6 +70,32 @@ q3_status q3_model_config(const q3_model* model, q3_config* out);
 /* Qwen3::GetTensorIndex().size() (src/inference.cpp:516-518). */
 q3_status q3_model_tensor_count(const q3_model* model, int* out);
 
+/* Config::arch / dtype / act_type (include/inference.h:66-90), the metadata strings of the file.
+ * key is "arch", "dtype" or "act_type"; *length (nullable) receives the string length; buf
+ * (nullable) receives the NUL-terminated string and needs length+1 bytes. */
+q3_status q3_model_metadata(const q3_model* model, const char* key, char* buf, size_t capacity,
+                            size_t* length);
+
+/* TensorInfo (include/inference.h:30-36) of one record of the file; dtype uses the reference's
+ * TensorDType codes (1 f32, 3 bf16, 4 u8, 5 i32); data_offset is the payload's byte offset in
+ * the file. Unknown names fail like Qwen3::LoadTensor ("Tensor not found", runtime error). */
+typedef struct q3_tensor_info {
+    uint32_t dtype, rank;
+    uint64_t shape[8];
+    uint64_t data_offset, byte_size;
+} q3_tensor_info;
+/* Name of record `index` (0 .. tensor_count-1, file order): the keys of Qwen3::GetTensorIndex()
+ * (src/inference.cpp:516-518). *length and buf as in q3_model_metadata. */
+q3_status q3_model_tensor_name(const q3_model* model, int index, char* buf, size_t capacity,
+                               size_t* length);
+/* Qwen3::GetTensorIndex().find(name) (src/inference.cpp:516-518). */
+q3_status q3_model_tensor_info(const q3_model* model, const char* name, q3_tensor_info* out);
+/* Qwen3::LoadTensor<T>(name) (include/inference.h:289-305, LoadTensorBytes at
+ * src/inference.cpp:307-317): copies the payload (byte_size bytes) to host; a record whose dtype
+ * is not expected_dtype fails with "Tensor dtype mismatch" (runtime error). */
+q3_status q3_model_load_tensor(const q3_model* model, const char* name, uint32_t expected_dtype,
+                               void* host, size_t capacity);
+
 /* Qwen3::ResetInference (src/inference.cpp:583-590): zeroes every KV cache. */
 q3_status q3_reset(q3_model* model);
 

@@ -39,6 +39,10 @@ def nvcc() -> str:
     raise FileNotFoundError("nvcc not found")
 
 
+def cuda_home() -> Path:
+    return Path(nvcc()).resolve().parent.parent
+
+
 def host_cxx() -> str:
     # The image exports CXX pointing at a gcc without libgomp; the system g++ is complete.
     for c in ("/usr/bin/g++", shutil.which("g++")):
@@ -84,8 +88,11 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if cxx_src.exists():
         deps = [cxx_src, SO, *INCLUDE.glob("*.h")]
         if force or not CXX_SO.exists() or CXX_SO.stat().st_mtime < _newest(deps):
-            _run([host_cxx(), "-std=gnu++23", "-O2", "-fPIC", "-shared", "-I", str(INCLUDE),
-                  str(cxx_src), "-o", str(CXX_SO), f"-L{LIB}", "-lq3b200", "-Wl,-rpath,$ORIGIN"])
+            # -Wno-free-nonheap-object: a known false positive of g++ 13 in std::vector growth.
+            _run([host_cxx(), "-std=gnu++23", "-O2", "-fPIC", "-shared", "-Wno-free-nonheap-object",
+                  "-I", str(INCLUDE), "-I", str(cuda_home() / "include"), str(cxx_src), "-o", str(CXX_SO),
+                  f"-L{LIB}", "-lq3b200", f"-L{cuda_home() / 'lib64'}", "-lcudart",
+                  "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{cuda_home() / 'lib64'}"])
     if verbose:
         print(f"built {SO}")
     return SO

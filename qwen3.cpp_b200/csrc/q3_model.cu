@@ -204,6 +204,7 @@ ModelFile::ModelFile(const std::string& path) : path_(path) {
         if (!tensors_.emplace(t.name, t).second) {
             throw std::runtime_error("Duplicate tensor record: " + t.name);
         }
+        names_.push_back(t.name);
         r.off += t.byte_size;
     }
 }
@@ -217,6 +218,13 @@ const ModelFile::Tensor& ModelFile::tensor(const std::string& name) const {
     auto it = tensors_.find(name);
     if (it == tensors_.end()) throw std::runtime_error("Tensor not found: " + name);
     return it->second;
+}
+
+const std::string& ModelFile::metadata(const std::string& key) const {
+    if (key == "arch") return arch_;
+    if (key == "dtype") return dtype_;
+    if (key == "act_type") return act_;
+    throw std::invalid_argument("Unknown metadata key: " + key);
 }
 
 // ------------------------------------------------------------------ device buffers
@@ -1153,6 +1161,65 @@ q3_status q3_model_tensor_count(const q3_model* model, int* out) {
     return guard([&] {
         if (!model || !out) throw std::invalid_argument("null argument");
         *out = model->m->tensor_count();
+    });
+}
+
+q3_status q3_model_metadata(const q3_model* model, const char* key, char* buf, size_t capacity,
+                            size_t* length) {
+    return guard([&] {
+        if (!model || !key) throw std::invalid_argument("null argument");
+        const std::string& v = model->m->file().metadata(key);
+        if (length) *length = v.size();
+        if (buf) {
+            if (capacity <= v.size()) throw std::invalid_argument("metadata buffer too small");
+            std::memcpy(buf, v.c_str(), v.size() + 1);
+        }
+    });
+}
+
+q3_status q3_model_tensor_name(const q3_model* model, int index, char* buf, size_t capacity,
+                               size_t* length) {
+    return guard([&] {
+        if (!model) throw std::invalid_argument("null argument");
+        if (index < 0 || static_cast<size_t>(index) >= model->m->file().tensor_count()) {
+            throw std::out_of_range("tensor index out of range");
+        }
+        const std::string& v = model->m->file().tensor_name(static_cast<size_t>(index));
+        if (length) *length = v.size();
+        if (buf) {
+            if (capacity <= v.size()) throw std::invalid_argument("name buffer too small");
+            std::memcpy(buf, v.c_str(), v.size() + 1);
+        }
+    });
+}
+
+q3_status q3_model_tensor_info(const q3_model* model, const char* name, q3_tensor_info* out) {
+    return guard([&] {
+        if (!model || !name || !out) throw std::invalid_argument("null argument");
+        const auto& t = model->m->file().tensor(name);
+        if (t.shape.size() > 8) throw std::runtime_error("Tensor rank above 8: " + t.name);
+        *out = q3_tensor_info{};
+        out->dtype = t.dtype;
+        out->rank = static_cast<uint32_t>(t.shape.size());
+        for (size_t i = 0; i < t.shape.size(); ++i) out->shape[i] = t.shape[i];
+        out->data_offset = t.offset;
+        out->byte_size = t.byte_size;
+    });
+}
+
+q3_status q3_model_load_tensor(const q3_model* model, const char* name, uint32_t expected_dtype,
+                               void* host, size_t capacity) {
+    return guard([&] {
+        if (!model || !name) throw std::invalid_argument("null argument");
+        const auto& t = model->m->file().tensor(name);
+        // LoadTensorBytes (src/inference.cpp:307-317).
+        if (t.dtype != expected_dtype) throw std::runtime_error("Tensor dtype mismatch: " + t.name);
+        if (t.byte_size > 0) {
+            if (!host || capacity < t.byte_size) {
+                throw std::invalid_argument("tensor buffer too small: " + t.name);
+            }
+            std::memcpy(host, model->m->file().data() + t.offset, t.byte_size);
+        }
     });
 }
 

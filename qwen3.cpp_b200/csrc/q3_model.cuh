@@ -39,6 +39,10 @@ public:
     const Tensor& tensor(const std::string& name) const;
     size_t tensor_count() const { return tensors_.size(); }
     const uint8_t* data() const { return data_; }
+    // Metadata strings of the header ("arch", "dtype", "act_type").
+    const std::string& metadata(const std::string& key) const;
+    // Name of record i in file order.
+    const std::string& tensor_name(size_t i) const { return names_.at(i); }
 
 private:
     std::string path_;
@@ -48,6 +52,7 @@ private:
     q3_config config_{};
     std::string arch_, dtype_, act_;
     std::unordered_map<std::string, Tensor> tensors_;
+    std::vector<std::string> names_;  // record order
 };
 
 struct DeviceBuffer {
@@ -144,6 +149,7 @@ public:
 
     const q3_config& config() const { return cfg_; }
     int tensor_count() const { return tensor_count_; }
+    const ModelFile& file() const { return file_; }
     cudaStream_t stream() const { return engine_->stream(); }
     Engine& engine() { return *engine_; }
     const LayerWeights& layer(int l) const { return layers_[l]; }
