@@ -120,6 +120,21 @@ q3_status q3_kv_row(q3_model* model, int layer, int kv_pos, uint16_t* k_host, ui
 q3_status q3_prefill(q3_model* model, const int32_t* ids_host, int n, int pos0,
                      float* last_logits_host, int32_t* next_token_host);
 
+/* q3_prefill with debug taps: hidden_host[(n_layers+1)*dim] (nullable) receives the hidden state
+ * of the LAST prompt token before the first layer and after every layer. */
+q3_status q3_prefill_layers(q3_model* model, const int32_t* ids_host, int n, int pos0,
+                            float* hidden_host, float* last_logits_host, int32_t* next_token_host);
+
+/* Prefill paths (no reference counterpart: the reference prefills token by token). BATCHED runs
+ * every projection as a tensor-core contraction over all prompt tokens (tcgen05, bf16 operands,
+ * fp32 accumulation) and causal attention over the paged cache; it is used when the model shape
+ * allows it (head_dim 128, two query heads per KV head) and pos0 + n <= context, and is the
+ * default. TOKENWISE feeds the prompt through the decode path one token at a time. */
+enum { Q3_PREFILL_TOKENWISE = 0, Q3_PREFILL_BATCHED = 1 };
+q3_status q3_model_set_prefill_path(q3_model* model, int path);
+/* The path q3_prefill takes for prompts that fit below the context. */
+q3_status q3_model_prefill_path(const q3_model* model, int* path);
+
 /* n_steps greedy decode steps driven on the device (the loop of src/inference.cpp:679-690 with
  * stop_on_eos = false, i.e. `--benchmark N`): step i feeds token t_i at position pos0+i and
  * t_{i+1} = argmax of its logits, t_0 = first_token. tokens_host[n_steps] receives t_1..t_n.
@@ -223,6 +238,17 @@ q3_status q3_attn(float* out, void* workspace, const float* q, const uint16_t* k
 size_t q3_attn_noalloc_max_scratch(void);
 q3_status q3_attn_noalloc(float* out, const float* q, const uint16_t* k, const uint16_t* v,
                           int head_dim, int n_kv_heads, int kv_len, void* stream);
+
+/* Tensor-core contraction used by the batched prefill (no reference counterpart; the reference's
+ * MatMul is one fp32 vector at a time): out[M, N] = epilogue(A[M, K] . W[N, K]^T) with A and W bf16
+ * row-major, fp32 accumulation. epilogue Q3_GEMM_STORE_F32 writes fp32 out[M, N];
+ * Q3_GEMM_ADD_F32 adds into fp32 out[M, N]; Q3_GEMM_STORE_BF16 writes bf16 out[M, N];
+ * Q3_GEMM_SWIGLU writes bf16 out[M, N] = silu(A . W^T) * (A . W3^T) (W and W3 both [N, K]).
+ * K must be a multiple of 64; N a multiple of 128; all pointers 16-byte aligned. Synchronises
+ * `stream` and reports a device timeout of the pipeline as Q3_ERR_DEVICE_TIMEOUT. */
+enum { Q3_GEMM_STORE_F32 = 0, Q3_GEMM_ADD_F32 = 1, Q3_GEMM_SWIGLU = 2, Q3_GEMM_STORE_BF16 = 3 };
+q3_status q3_gemm_bf16(void* out, const uint16_t* a, const uint16_t* w, const uint16_t* w3, int M,
+                       int N, int K, int epilogue, void* stream);
 
 /* Sampler::Greedy (src/inference.cpp:703-709): index of the first maximum of logits[n], written
  * to *out_index (device int32). n == 0 is rejected like the reference's empty span. */

@@ -1,0 +1,421 @@
+// Prefill contractions on tcgen05 tensor cores (sm_100a).
+//
+// Persistent, warp-specialised kernel, one CTA per SM (192 threads):
+//   warp 0      TMA producer: for every (tile, k-block) of this CTA, waits for a free stage and
+//               loads the 128 x 64 A box and the BN x 64 B box (128-byte swizzle) into it.
+//   warp 1      MMA issuer (one thread): per k-block four tcgen05.mma (M=128, N=BN, K=16) into
+//               one of two TMEM accumulators; tcgen05.commit frees the stage when the MMAs that
+//               read it are done, and signals the epilogue after the tile's last k-block.
+//   warps 2-5   epilogue: warp w reads TMEM lanes 32*(w%4).. (one output row per thread), 32
+//               fp32 columns per tcgen05.ld, applies the fused op and stores to global memory,
+//               then hands the accumulator back. Two accumulators let the epilogue of one tile
+//               overlap the MMAs of the next.
+// Every mbarrier wait is bounded; a wait that gives up sets args.err and the CTA drains its
+// outstanding TMA loads and MMAs before freeing TMEM and returning.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+
+#include <mutex>
+#include <stdexcept>
+#include <string>
+
+#include "q3_b200.h"
+#include "q3_common.cuh"
+#include "q3_gemm.cuh"
+#include "q3_sm100.cuh"
+
+namespace q3 {
+
+namespace {
+
+using namespace sm100;
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int NTHREADS = 192;
+
+template <int BN>
+struct GemmCfg {
+    static constexpr int STAGES = BN == 256 ? 4 : 6;
+    static constexpr int A_BYTES = BM * BK * 2;
+    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int TMEM_COLS = 2 * BN;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+};
+
+__device__ __forceinline__ void store_f32x32(float* dst, const float (&v)[32]) {
+    float4* d = reinterpret_cast<float4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) d[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
+
+__device__ __forceinline__ void add_f32x32(float* dst, const float (&v)[32]) {
+    float4* d = reinterpret_cast<float4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        float4 o = d[i];
+        o.x += v[4 * i];
+        o.y += v[4 * i + 1];
+        o.z += v[4 * i + 2];
+        o.w += v[4 * i + 3];
+        d[i] = o;
+    }
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);  // RNE, like static_cast<bfloat16_t>
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__device__ __forceinline__ void store_bf16x32(uint16_t* dst, const float (&v)[32]) {
+    uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        d[i] = make_uint4(pack_bf16(v[8 * i], v[8 * i + 1]), pack_bf16(v[8 * i + 2], v[8 * i + 3]),
+                          pack_bf16(v[8 * i + 4], v[8 * i + 5]), pack_bf16(v[8 * i + 6], v[8 * i + 7]));
+    }
+}
+
+__device__ __forceinline__ void fail(volatile int* abort, unsigned* err, unsigned code) {
+    *abort = 1;
+    if (err) atomicCAS(err, 0u, code);
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
+                const __grid_constant__ CUtensorMap tb2, const GemmArgs args) {
+    using C = GemmCfg<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+    uint64_t* empty = full + C::STAGES;
+    uint64_t* tfull = empty + C::STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* done = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int num_m = (args.M + BM - 1) / BM;
+    const int num_n = args.N / BN;
+    const int tiles = num_m * num_n;
+    const int kblocks = args.K / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 4);
+        }
+        mbar_init(done, 1);
+        *abort = 0;
+        mbar_fence_init();
+    }
+    if (warp == 0) {
+        tma_prefetch_map(&ta);
+        tma_prefetch_map(&tb);
+        if (EPI == kEpiSwiGLU) tma_prefetch_map(&tb2);
+        tmem_alloc(tmem_slot, C::TMEM_COLS);
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------------------------------------------------------- producer
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued_mask = 0, issued_parity = 0;
+            for (int t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
+                const int tm = t % num_m, tn = t / num_m;
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1, args.budget, abort)) {
+                        fail(abort, args.err, 1);
+                        break;
+                    }
+                    uint8_t* sa = smem + stage * C::STAGE_BYTES;
+                    uint8_t* sb = sa + C::A_BYTES;
+                    mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+                    tma_load_2d(sa, &ta, kb * BK, tm * BM, &full[stage]);
+                    if (EPI == kEpiSwiGLU) {
+                        tma_load_2d(sb, &tb, kb * BK, tn * (BN / 2), &full[stage]);
+                        tma_load_2d(sb + C::B_BYTES / 2, &tb2, kb * BK, tn * (BN / 2), &full[stage]);
+                    } else {
+                        tma_load_2d(sb, &tb, kb * BK, tn * BN, &full[stage]);
+                    }
+                    issued_mask |= 1u << stage;
+                    issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+                    if (++stage == C::STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            // Drain: every load issued into shared memory has landed before the CTA exits.
+            for (int s = 0; s < C::STAGES; ++s) {
+                if (issued_mask & (1u << s)) {
+                    const long long t0 = clock64();
+                    while (!mbar_try_wait(&full[s], (issued_parity >> s) & 1)) {
+                        if (clock64() - t0 > args.budget) {
+                            fail(abort, args.err, 2);
+                            break;
+                        }
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------------------------------------------------------- MMA issuer
+            const uint32_t idesc = idesc_bf16_f32(BM, BN);
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < tiles && ok && !*abort; t += gridDim.x) {
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1, args.budget, abort)) {
+                    fail(abort, args.err, 3);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem + static_cast<uint32_t>(acc * BN);
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, args.budget, abort)) {
+                        fail(abort, args.err, 4);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
+                    const uint64_t adesc = desc_k_sw128(sa);
+                    const uint64_t bdesc = desc_k_sw128(sa + C::A_BYTES);
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k) {
+                        mma_bf16(d, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+                    }
+                    mma_commit(&empty[stage]);
+                    if (++stage == C::STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+                mma_commit(&tfull[acc]);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1;
+                }
+            }
+            // Drain: all MMAs issued by this thread complete before TMEM is freed.
+            mma_commit(done);
+            const long long t0 = clock64();
+            while (!mbar_try_wait(done, 0)) {
+                if (clock64() - t0 > args.budget) {
+                    fail(abort, args.err, 5);
+                    break;
+                }
+            }
+        }
+    } else {
+        // -------------------------------------------------------------------- epilogue
+        const int lg = warp & 3;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
+            const int tm = t % num_m, tn = t / num_m;
+            if (!mbar_wait(&tfull[acc], acc_phase, args.budget, abort)) {
+                fail(abort, args.err, 6);
+                break;
+            }
+            tc_fence_after();
+            const uint32_t tb_addr = tmem + (static_cast<uint32_t>(lg * 32) << 16) +
+                                     static_cast<uint32_t>(acc * BN);
+            const int r = tm * BM + lg * 32 + lane;
+            const bool row_ok = r < args.M;
+            if (EPI == kEpiSwiGLU) {
+                uint16_t* out = static_cast<uint16_t*>(args.out) + static_cast<size_t>(r) * args.ldo +
+                                tn * (BN / 2);
+#pragma unroll 1
+                for (int c = 0; c < BN / 2; c += 32) {
+                    float g[32], u[32];
+                    tmem_ld32(tb_addr + c, g);
+                    tmem_ld32(tb_addr + BN / 2 + c, u);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) g[i] = g[i] / (1.0f + expf(-g[i])) * u[i];
+                    if (row_ok) store_bf16x32(out + c, g);
+                }
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < BN; c += 32) {
+                    float v[32];
+                    tmem_ld32(tb_addr + c, v);
+                    if (row_ok) {
+                        const size_t off = static_cast<size_t>(r) * args.ldo + tn * BN + c;
+                        if (EPI == kEpiStoreF32) store_f32x32(static_cast<float*>(args.out) + off, v);
+                        if (EPI == kEpiAddF32) add_f32x32(static_cast<float*>(args.out) + off, v);
+                        if (EPI == kEpiStoreBF16) store_bf16x32(static_cast<uint16_t*>(args.out) + off, v);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1;
+            }
+        }
+    }
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000,
+                                             cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess) {
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        }
+    });
+    if (!fn) throw std::runtime_error("cuTensorMapEncodeTiled is unavailable");
+    return fn;
+}
+
+template <int BN, int EPI>
+cudaError_t launch_t(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& b2,
+                     const GemmArgs& args, int num_sms, cudaStream_t stream) {
+    using C = GemmCfg<BN>;
+    auto kern = gemm_kernel<BN, EPI>;
+    static thread_local int configured_device = -1;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (configured_device != dev) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        configured_device = dev;
+    }
+    const int tiles = ((args.M + BM - 1) / BM) * (args.N / BN);
+    const int grid = tiles < num_sms ? tiles : num_sms;
+    if (grid <= 0) return cudaSuccess;
+    kern<<<grid, NTHREADS, C::SMEM_BYTES, stream>>>(a, b, b2, args);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+void make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                    uint32_t box_rows) {
+    if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || cols % 8 != 0 || rows == 0 ||
+        box_rows == 0 || box_rows > 256) {
+        throw std::invalid_argument("tensor map: misaligned base or unsupported shape");
+    }
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base),
+                                   dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string(static_cast<int>(r)));
+    }
+}
+
+int gemm_tile_n(int epi, int N) {
+    if (epi == kEpiSwiGLU) return 256;
+    return (N % 256 == 0 && N >= 4096) ? 256 : 128;
+}
+
+cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap* b2,
+                        const GemmArgs& args, int epi, int num_sms, cudaStream_t stream) {
+    if (args.K % BK != 0 || args.K <= 0 || args.M <= 0) return cudaErrorInvalidValue;
+    const int bn = gemm_tile_n(epi, args.N);
+    if (args.N % bn != 0) return cudaErrorInvalidValue;
+    if (epi == kEpiSwiGLU && !b2) return cudaErrorInvalidValue;
+    const CUtensorMap& bb = b2 ? *b2 : b;
+    switch (epi) {
+        case kEpiStoreF32:
+            return bn == 256 ? launch_t<256, kEpiStoreF32>(a, b, bb, args, num_sms, stream)
+                             : launch_t<128, kEpiStoreF32>(a, b, bb, args, num_sms, stream);
+        case kEpiAddF32:
+            return bn == 256 ? launch_t<256, kEpiAddF32>(a, b, bb, args, num_sms, stream)
+                             : launch_t<128, kEpiAddF32>(a, b, bb, args, num_sms, stream);
+        case kEpiStoreBF16:
+            return bn == 256 ? launch_t<256, kEpiStoreBF16>(a, b, bb, args, num_sms, stream)
+                             : launch_t<128, kEpiStoreBF16>(a, b, bb, args, num_sms, stream);
+        case kEpiSwiGLU:
+            return launch_t<256, kEpiSwiGLU>(a, b, bb, args, num_sms, stream);
+    }
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace q3
+
+// ------------------------------------------------------------------ C ABI
+
+extern "C" q3_status q3_gemm_bf16(void* out, const uint16_t* a, const uint16_t* w,
+                                  const uint16_t* w3, int M, int N, int K, int epilogue,
+                                  void* stream) {
+    using namespace q3;
+    return guard([&] {
+        if (!out || !a || !w) throw std::invalid_argument("null argument");
+        if (M <= 0 || N <= 0 || K <= 0 || K % 64 != 0 || N % 128 != 0) {
+            throw std::invalid_argument("gemm: M, N > 0, K a multiple of 64, N of 128");
+        }
+        if (epilogue < Q3_GEMM_STORE_F32 || epilogue > Q3_GEMM_STORE_BF16) {
+            throw std::invalid_argument("gemm: unknown epilogue");
+        }
+        const bool swiglu = epilogue == Q3_GEMM_SWIGLU;
+        if (swiglu && !w3) throw std::invalid_argument("gemm: SwiGLU needs w3");
+        const int tile_space = swiglu ? 2 * N : N;
+        const int bn = gemm_tile_n(epilogue, tile_space);
+        if (tile_space % bn != 0) throw std::invalid_argument("gemm: N does not tile");
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        int dev = 0, sms = 0;
+        Q3_CUDA(cudaGetDevice(&dev));
+        Q3_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        CUtensorMap ma, mb, mb3;
+        make_tmap_bf16(&ma, a, M, K, 128);
+        make_tmap_bf16(&mb, w, N, K, swiglu ? 128 : bn);
+        if (swiglu) make_tmap_bf16(&mb3, w3, N, K, 128);
+        unsigned* err = nullptr;
+        Q3_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&err), sizeof(unsigned), s));
+        Q3_CUDA(cudaMemsetAsync(err, 0, sizeof(unsigned), s));
+        GemmArgs g;
+        g.M = M;
+        g.N = tile_space;
+        g.K = K;
+        g.out = out;
+        g.ldo = N;
+        g.err = err;
+        const cudaError_t le = launch_gemm(ma, mb, swiglu ? &mb3 : nullptr, g, epilogue, sms, s);
+        unsigned herr = 0;
+        const cudaError_t ce = cudaMemcpyAsync(&herr, err, sizeof(unsigned),
+                                               cudaMemcpyDeviceToHost, s);
+        const cudaError_t se = cudaStreamSynchronize(s);
+        cudaFreeAsync(err, s);
+        Q3_CUDA(le);
+        Q3_CUDA(ce);
+        Q3_CUDA(se);
+        if (herr) throw DeviceTimeout("gemm: a pipeline wait gave up (code " + std::to_string(herr) + ")");
+    });
+}

@@ -1,0 +1,44 @@
+// Batched-token (prefill) contractions on the sm_100a tensor cores: C[M, N] = A[M, K] . B[N, K]^T
+// with A the bf16 activations of M tokens and B a bf16 weight matrix in the reference's row-major
+// [out, in] layout (both K-major), fp32 accumulation in TMEM, and the epilogue of the op that
+// follows the projection fused in.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace q3 {
+
+enum GemmEpilogue : int {
+    kEpiStoreF32 = 0,  // out[m, n] = acc (fp32)
+    kEpiAddF32 = 1,    // out[m, n] += acc (fp32 residual stream: x += proj)
+    kEpiSwiGLU = 2,    // B rows = 128 of w1 then the same 128 of w3 per tile; out bf16 [M, N/2]:
+                       // h = silu(w1 . x) * (w3 . x)
+    kEpiStoreBF16 = 3, // out[m, n] = bf16(acc)
+};
+
+// A 2-D K-major bf16 matrix [rows, cols] (cols contiguous) as a TMA tensor map with 128-byte
+// swizzling and a box of 64 columns x box_rows rows. base must be 16-byte aligned and cols a
+// multiple of 8.
+void make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                    uint32_t box_rows);
+
+struct GemmArgs {
+    int M = 0, N = 0, K = 0;  // N: output columns of the tile space (2 x hidden for SwiGLU)
+    void* out = nullptr;      // fp32 or bf16 [M, ldo]
+    int ldo = 0;              // elements between output rows
+    unsigned* err = nullptr;  // set non-zero when a bounded wait gives up
+    long long budget = 4000000000LL;  // cycles per wait
+};
+
+// Tile N width used for an epilogue and output width (128 or 256).
+int gemm_tile_n(int epi, int N);
+// Enqueues the contraction. `a` maps A [M, K] with 128-row boxes; `b` maps B [N, K] with
+// box_rows = gemm_tile_n(...) (SwiGLU: `b` = w1 and `b2` = w3, each [N/2, K] with 128-row boxes).
+// K must be a multiple of 64, N a multiple of the tile width. Grid: one persistent CTA per SM at
+// most. Returns cudaSuccess or the launch error.
+cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap* b2,
+                        const GemmArgs& args, int epi, int num_sms, cudaStream_t stream);
+
+}  // namespace q3

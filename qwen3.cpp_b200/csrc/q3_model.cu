@@ -11,6 +11,7 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <chrono>
 #include <cmath>
 #include <cstring>
@@ -26,6 +27,7 @@
 #include "q3_decode_fused.cuh"
 #include "q3_kernels.cuh"
 #include "q3_model.cuh"
+#include "q3_prefill.cuh"
 
 namespace q3 {
 
@@ -968,11 +970,77 @@ void Model::decode_loop(const int32_t* forced_host, int n, int32_t first_token, 
     Q3_CUDA(cudaStreamSynchronize(s));
 }
 
-void Model::prefill(const int32_t* ids, int n, int pos0, float* last_logits, int32_t* next) {
+bool Model::batched_prefill_ok(int n, int pos0) const {
+    return use_batched_prefill_ && Prefill::supported(cfg_) && n > 0 && pos0 >= 0 &&
+           pos0 <= cfg_.max_seq_len - n;
+}
+
+void Model::prefill(const int32_t* ids, int n, int pos0, float* last_logits, int32_t* next,
+                    float* hidden_host) {
     if (n <= 0) throw std::invalid_argument("Prefill needs at least one token");
+    if (!ids) throw std::invalid_argument("null argument");
+    if (batched_prefill_ok(n, pos0)) {
+        prefill_batched(ids, n, pos0, last_logits, next, hidden_host);
+        return;
+    }
+    // Token by token: the reference's loop (src/inference.cpp:669-671) driven on the device;
+    // the last token runs alone when its per-layer hidden states are wanted.
+    const int bulk = hidden_host ? n - 1 : n;
     std::vector<int32_t> argmax(n);
-    decode_loop(ids, n, 0, pos0, argmax.data(), last_logits, nullptr);
+    if (bulk > 0) decode_loop(ids, bulk, 0, pos0, argmax.data(), last_logits, nullptr);
+    if (hidden_host) {
+        forward_token(ids[n - 1], pos0 + n - 1, hidden_host, nullptr);
+        std::vector<float> lg(cfg_.vocab_size);
+        Q3_CUDA(cudaMemcpy(lg.data(), logits_.ptr, lg.size() * 4, cudaMemcpyDeviceToHost));
+        if (last_logits) std::memcpy(last_logits, lg.data(), lg.size() * 4);
+        argmax[n - 1] = static_cast<int32_t>(std::max_element(lg.begin(), lg.end()) - lg.begin());
+    }
     if (next) *next = argmax[n - 1];
+}
+
+void Model::prefill_batched(const int32_t* ids, int n, int pos0, float* last_logits,
+                            int32_t* next, float* hidden_host) {
+    for (int i = 0; i < n; ++i) check_token_pos(ids[i], pos0 + i);
+    Engine& e = *engine_;
+    cudaStream_t s = e.stream();
+    e.ensure_rope(pos0 + n + 1);
+    if (!prefill_) prefill_ = std::make_unique<Prefill>(cfg_, device_);
+    if (prefill_ids_.bytes < static_cast<size_t>(n) * 4) {
+        Q3_CUDA(cudaStreamSynchronize(s));
+        prefill_ids_.alloc(static_cast<size_t>(n) * 4);
+    }
+    Q3_CUDA(cudaStreamSynchronize(s));
+    pinned_io_.ensure(static_cast<size_t>(n) * 4);
+    std::memcpy(pinned_io_.ptr, ids, static_cast<size_t>(n) * 4);
+    Q3_CUDA(cudaMemcpyAsync(prefill_ids_.ptr, pinned_io_.ptr, static_cast<size_t>(n) * 4,
+                            cudaMemcpyHostToDevice, s));
+    prefill_->run(static_cast<const int32_t*>(prefill_ids_.ptr), n, pos0, embed_, layers_, e,
+                  e.x(), hidden_host ? e.taps() : nullptr, s);
+    // Final RmsNorm + tied lm_head of the last token (src/inference.cpp:619-635) and Greedy.
+    const q3_config& c = cfg_;
+    launch_gemv(kEpiStore, output_, nullptr, e.x(), final_norm_, c.norm_eps,
+                static_cast<float*>(logits_.ptr), nullptr, c.vocab_size, c.dim, nullptr,
+                gemv_grid(c.vocab_size), s);
+    launch_argmax_full(static_cast<const float*>(logits_.ptr), c.vocab_size,
+                       static_cast<int32_t*>(argmax_out_.ptr), s);
+    int32_t am = 0;
+    Q3_CUDA(cudaMemcpyAsync(&am, argmax_out_.ptr, 4, cudaMemcpyDeviceToHost, s));
+    if (last_logits) {
+        Q3_CUDA(cudaMemcpyAsync(last_logits, logits_.ptr, static_cast<size_t>(c.vocab_size) * 4,
+                                cudaMemcpyDeviceToHost, s));
+    }
+    if (hidden_host) {
+        Q3_CUDA(cudaMemcpyAsync(hidden_host, e.taps(),
+                                static_cast<size_t>(c.n_layers + 1) * c.dim * 4,
+                                cudaMemcpyDeviceToHost, s));
+    }
+    Q3_CUDA(cudaStreamSynchronize(s));
+    const unsigned err = prefill_->read_error(s);
+    if (err) {
+        throw DeviceTimeout("batched prefill: a tensor-core pipeline wait gave up (code " +
+                            std::to_string(err) + ")");
+    }
+    if (next) *next = am;
 }
 
 // Qwen3::Generate on token IDs (src/inference.cpp:639-700). The reference feeds every generated
@@ -1257,6 +1325,33 @@ q3_status q3_prefill(q3_model* model, const int32_t* ids_host, int n, int pos0,
     return guard([&] {
         if (!model || !ids_host) throw std::invalid_argument("null argument");
         model->m->prefill(ids_host, n, pos0, last_logits_host, next_token_host);
+    });
+}
+
+q3_status q3_prefill_layers(q3_model* model, const int32_t* ids_host, int n, int pos0,
+                            float* hidden_host, float* last_logits_host, int32_t* next_token_host) {
+    return guard([&] {
+        if (!model || !ids_host) throw std::invalid_argument("null argument");
+        model->m->prefill(ids_host, n, pos0, last_logits_host, next_token_host, hidden_host);
+    });
+}
+
+q3_status q3_model_set_prefill_path(q3_model* model, int path) {
+    return guard([&] {
+        if (!model) throw std::invalid_argument("null argument");
+        if (path != Q3_PREFILL_TOKENWISE && path != Q3_PREFILL_BATCHED) {
+            throw std::invalid_argument("unknown prefill path");
+        }
+        model->m->set_batched_prefill(path == Q3_PREFILL_BATCHED);
+    });
+}
+
+q3_status q3_model_prefill_path(const q3_model* model, int* path) {
+    return guard([&] {
+        if (!model || !path) throw std::invalid_argument("null argument");
+        *path = model->m->batched_prefill_enabled() && q3::Prefill::supported(model->m->config())
+                    ? Q3_PREFILL_BATCHED
+                    : Q3_PREFILL_TOKENWISE;
     });
 }
 

@@ -141,6 +141,8 @@ private:
     std::map<int, cudaGraphExec_t> graphs_;
 };
 
+class Prefill;
+
 // class Qwen3 of the reference (include/inference.h:227-264) on one GPU.
 class Model {
 public:
@@ -162,7 +164,15 @@ public:
     void forward_token(int32_t token, int pos, float* hidden_host, float* logits_host);
     void decode_loop(const int32_t* forced_host, int n, int32_t first_token, int pos0,
                      int32_t* out_tokens_host, float* last_logits_host, float* all_logits_host);
-    void prefill(const int32_t* ids, int n, int pos0, float* last_logits, int32_t* next);
+    // Prompt prefill. Batched (tensor-core contractions over all tokens) when the shape allows
+    // it, the batched path is selected and the prompt fits below the context; token by token
+    // otherwise. hidden_host (nullable) receives the last token's hidden state before the
+    // first layer and after every layer ([(n_layers+1) * dim]).
+    void prefill(const int32_t* ids, int n, int pos0, float* last_logits, int32_t* next,
+                 float* hidden_host = nullptr);
+    bool batched_prefill_enabled() const { return use_batched_prefill_; }
+    void set_batched_prefill(bool on) { use_batched_prefill_ = on; }
+    bool batched_prefill_ok(int n, int pos0) const;
     void generate(const int32_t* prompt, int n_prompt, size_t max_new, bool stop_on_eos,
                   int32_t* out, size_t* n_out, q3_generation_stats* stats);
     void kv_row(int layer, int kv_pos, uint16_t* k, uint16_t* v);
@@ -186,6 +196,8 @@ private:
     void ensure_logs(int n);
     void enqueue_step(bool forced, bool taps);
     void run_steps(int n, bool forced, bool taps, float* logits_log_dev);
+    void prefill_batched(const int32_t* ids, int n, int pos0, float* last_logits, int32_t* next,
+                         float* hidden_host);
     void launch_fused(int n_steps, bool forced, bool taps, long long spin_cycles, int offset,
                       unsigned long long* prof = nullptr);
     void clear_fused_error();
@@ -209,6 +221,9 @@ private:
     int fused_s_max_ = 0;
     const uint16_t* fused_lm_ = nullptr;
     bool use_fused_ = true;
+    bool use_batched_prefill_ = true;
+    std::unique_ptr<Prefill> prefill_;
+    DeviceBuffer prefill_ids_;
     DeviceBuffer fused_layers_, fused_part_o_, fused_part_ml_, fused_am_, fused_sync_, fused_wperm_,
         fused_xy_, fused_dbg_;
 };

@@ -1,0 +1,568 @@
+// Batched prefill (see q3_prefill.cuh): row RmsNorm into bf16 operands, per-head QK-norm + RoPE
+// with the paged K/V write, causal flash attention over the paged cache, and the driver that
+// chains them with the tensor-core contractions of q3_gemm.cu.
+#include <cuda_bf16.h>
+#include <float.h>
+
+#include <algorithm>
+#include <stdexcept>
+
+#include "q3_gemm.cuh"
+#include "q3_prefill.cuh"
+
+namespace q3 {
+
+namespace {
+
+constexpr int HD = 128;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint32_t pack2_bf16(float a, float b) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);  // low half = a
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// ------------------------------------------------------------------ row RmsNorm -> bf16
+
+constexpr int kNormThreads = 256;
+
+__global__ void __launch_bounds__(kNormThreads)
+    rmsnorm_rows_kernel(const int32_t* __restrict__ ids, const uint16_t* __restrict__ embed,
+                        float* __restrict__ x, const uint16_t* __restrict__ w, float eps,
+                        uint16_t* __restrict__ out, int dim) {
+    __shared__ float red[kNormThreads / 32];
+    const size_t row = blockIdx.x;
+    float* xr = x + row * dim;
+    if (ids) {
+        const uint16_t* er = embed + static_cast<size_t>(ids[row]) * dim;
+        for (int i = threadIdx.x; i < dim; i += kNormThreads) xr[i] = bf16_to_f32(er[i]);
+        __syncthreads();
+    }
+    float ss = 0.0f;
+    for (int i = threadIdx.x * 4; i < dim; i += kNormThreads * 4) {
+        const float4 v = *reinterpret_cast<const float4*>(xr + i);
+        ss = fmaf(v.x, v.x, ss);
+        ss = fmaf(v.y, v.y, ss);
+        ss = fmaf(v.z, v.z, ss);
+        ss = fmaf(v.w, v.w, ss);
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kNormThreads / 32; ++i) tot += red[i];
+    // RmsNorm (src/inference.cpp:905-921): (x * (1 / rms)) * w, rms = sqrtf(ss / n + eps).
+    const float inv = 1.0f / sqrtf(tot / static_cast<float>(dim) + eps);
+    uint16_t* orow = out + row * dim;
+    for (int i = threadIdx.x * 4; i < dim; i += kNormThreads * 4) {
+        const float4 v = *reinterpret_cast<const float4*>(xr + i);
+        const uint2 wb = *reinterpret_cast<const uint2*>(w + i);
+        const uint2 o = make_uint2(pack2_bf16((v.x * inv) * bf16_lo(wb.x), (v.y * inv) * bf16_hi(wb.x)),
+                                   pack2_bf16((v.z * inv) * bf16_lo(wb.y), (v.w * inv) * bf16_hi(wb.y)));
+        *reinterpret_cast<uint2*>(orow + i) = o;
+    }
+}
+
+// ------------------------------------------------------------------ QK-norm + RoPE + KV write
+
+// One warp per (token, head); lane l holds elements 4l..4l+3 of the 128-wide head, so the RoPE
+// partner of element e (e + 64 or e - 64) sits in lane l ^ 16.
+__global__ void __launch_bounds__(256) prefill_qkv_kernel(PrefillQkvArgs a) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row = blockIdx.x;
+    const int head = blockIdx.y * 8 + warp;
+    const int nq = a.n_heads, nk = a.n_kv;
+    if (head >= nq + 2 * nk) return;
+    const int pos = a.pos0 + row;
+    const float* src = a.qkv + static_cast<size_t>(row) * (nq + 2 * nk) * HD + head * HD;
+    float4 v = reinterpret_cast<const float4*>(src)[lane];
+    const int e = lane * 4;
+    uint16_t* dst;
+    if (head < nq + nk) {
+        const bool isq = head < nq;
+        const uint16_t* w = isq ? a.q_norm : a.k_norm;
+        float ss = v.x * v.x;
+        ss = fmaf(v.y, v.y, ss);
+        ss = fmaf(v.z, v.z, ss);
+        ss = fmaf(v.w, v.w, ss);
+        ss = warp_sum(ss);
+        const float inv = 1.0f / sqrtf(ss / static_cast<float>(HD) + a.eps);
+        const uint2 wb = *reinterpret_cast<const uint2*>(w + e);
+        v.x = (v.x * inv) * bf16_lo(wb.x);
+        v.y = (v.y * inv) * bf16_hi(wb.x);
+        v.z = (v.z * inv) * bf16_lo(wb.y);
+        v.w = (v.w * inv) * bf16_hi(wb.y);
+        // ApplyRotaryEmb (src/inference.cpp:968-991): (a, b) = (x_i, x_{i+64}) ->
+        // (a cos - b sin, b cos + a sin).
+        const float4 p = make_float4(__shfl_xor_sync(0xffffffffu, v.x, 16),
+                                     __shfl_xor_sync(0xffffffffu, v.y, 16),
+                                     __shfl_xor_sync(0xffffffffu, v.z, 16),
+                                     __shfl_xor_sync(0xffffffffu, v.w, 16));
+        const float2* cs = a.rope + static_cast<size_t>(pos) * (HD / 2) + (e & 63);
+        const float4 c01 = *reinterpret_cast<const float4*>(cs);
+        const float4 c23 = *reinterpret_cast<const float4*>(cs + 2);
+        if (lane < 16) {
+            v.x = v.x * c01.x - p.x * c01.y;
+            v.y = v.y * c01.z - p.y * c01.w;
+            v.z = v.z * c23.x - p.z * c23.y;
+            v.w = v.w * c23.z - p.w * c23.w;
+        } else {
+            v.x = v.x * c01.x + p.x * c01.y;
+            v.y = v.y * c01.z + p.y * c01.w;
+            v.z = v.z * c23.x + p.z * c23.y;
+            v.w = v.w * c23.z + p.w * c23.w;
+        }
+        if (isq) {
+            dst = a.q_out + static_cast<size_t>(row) * nq * HD + head * HD;
+        } else {
+            const int g = head - nq;
+            dst = a.k_cache +
+                  ((static_cast<size_t>(a.page_table[pos / kPageTokens]) * nk + g) * kPageTokens +
+                   pos % kPageTokens) * HD;
+        }
+    } else {
+        const int g = head - nq - nk;
+        dst = a.v_cache +
+              ((static_cast<size_t>(a.page_table[pos / kPageTokens]) * nk + g) * kPageTokens +
+               pos % kPageTokens) * HD;
+    }
+    reinterpret_cast<uint2*>(dst)[lane] = make_uint2(pack2_bf16(v.x, v.y), pack2_bf16(v.z, v.w));
+}
+
+// ------------------------------------------------------------------ causal flash attention
+
+constexpr int PA_THREADS = 256;          // 8 warps: 2 query heads x 4 groups of 16 rows
+constexpr int PA_BQ = 64;                // query tokens per CTA
+constexpr int PA_BKV = 64;               // KV positions per tile (4 pages)
+constexpr int PA_TILE = PA_BKV * HD * 2; // bytes of one K (or V) tile
+constexpr int PA_SMEM = 2 * 2 * PA_TILE; // double-buffered K and V
+
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                               uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// Byte offset of 16-byte chunk `ch` of tile row `row` (256-byte rows, XOR swizzle on the low 3
+// bits of the chunk so that 8 consecutive rows at one chunk hit 8 different bank groups).
+__device__ __forceinline__ uint32_t tile_off(int row, int ch) {
+    return static_cast<uint32_t>(row * 256 + ((ch ^ (row & 7)) << 4));
+}
+
+__global__ void __launch_bounds__(PA_THREADS, 1) prefill_attn_kernel(PrefillAttnArgs a) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    const int qb = gridDim.x - 1 - blockIdx.x;  // longest query blocks first
+    const int g = blockIdx.y;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int h = g * 2 + (warp >> 2);
+    const int qd = a.n_heads * HD;
+    const int r0 = qb * PA_BQ + (warp & 3) * 16;
+    const int last_row = min(a.rows, (qb + 1) * PA_BQ) - 1;
+    const int kv_end = a.pos0 + last_row + 1;
+    const int ntiles = (kv_end + PA_BKV - 1) / PA_BKV;
+    const int valid_pages = (kv_end + kPageTokens - 1) / kPageTokens;
+    const int cq = (lane & 3) * 2;
+    const int ra = r0 + (lane >> 2), rb = ra + 8;
+    const int qpos_a = a.pos0 + min(ra, a.rows - 1);
+    const int qpos_b = a.pos0 + min(rb, a.rows - 1);
+    const int warp_qmax = a.pos0 + min(r0 + 15, a.rows - 1);
+
+    // Q fragments (m16 x k16 row-major A operand) of this warp's 16 rows, 8 k-steps of 16 dims.
+    uint32_t qf[8][4];
+    {
+        const uint16_t* qa = a.q + static_cast<size_t>(min(ra, a.rows - 1)) * qd + h * HD + cq;
+        const uint16_t* qbp = a.q + static_cast<size_t>(min(rb, a.rows - 1)) * qd + h * HD + cq;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+            qf[kk][0] = *reinterpret_cast<const uint32_t*>(qa + kk * 16);
+            qf[kk][1] = *reinterpret_cast<const uint32_t*>(qbp + kk * 16);
+            qf[kk][2] = *reinterpret_cast<const uint32_t*>(qa + kk * 16 + 8);
+            qf[kk][3] = *reinterpret_cast<const uint32_t*>(qbp + kk * 16 + 8);
+        }
+    }
+
+    auto load_tile = [&](int j, int st) {
+        uint8_t* ks = sm + st * 2 * PA_TILE;
+        uint8_t* vs = ks + PA_TILE;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int c = tid + PA_THREADS * i;  // 1024 chunks of 16 B per tile
+            const int row = c >> 4, ch = c & 15;
+            const int t = j * PA_BKV + row;
+            const int page = t / kPageTokens;
+            const uint32_t off = tile_off(row, ch);
+            if (page < valid_pages) {
+                const size_t e =
+                    ((static_cast<size_t>(a.page_table[page]) * a.n_kv + g) * kPageTokens +
+                     t % kPageTokens) * HD + ch * 8;
+                cp_async16(smem_addr(ks + off), a.k_cache + e);
+                cp_async16(smem_addr(vs + off), a.v_cache + e);
+            } else {
+                *reinterpret_cast<uint4*>(ks + off) = make_uint4(0, 0, 0, 0);
+                *reinterpret_cast<uint4*>(vs + off) = make_uint4(0, 0, 0, 0);
+            }
+        }
+        cp_async_commit();
+    };
+
+    float o[16][4];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
+    float m_a = -FLT_MAX, m_b = -FLT_MAX, l_a = 0.0f, l_b = 0.0f;
+    // Scores in the log2 domain: s * log2(e) / sqrt(head_dim), then exp2.
+    const float scale = 1.4426950408889634f / sqrtf(static_cast<float>(HD));
+
+    load_tile(0, 0);
+    for (int j = 0; j < ntiles; ++j) {
+        if (j + 1 < ntiles) {
+            load_tile(j + 1, (j + 1) & 1);
+        } else {
+            cp_async_commit();
+        }
+        cp_async_wait<1>();
+        __syncthreads();
+        const uint8_t* ks = sm + (j & 1) * 2 * PA_TILE;
+        const uint8_t* vs = ks + PA_TILE;
+        if (j * PA_BKV <= warp_qmax) {
+            float s[8][4];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.0f;
+            const int mat = lane >> 3;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+#pragma unroll
+                for (int np = 0; np < 4; ++np) {
+                    uint32_t b[4];
+                    const int row = np * 16 + (lane & 7) + (mat >> 1) * 8;
+                    ldsm_x4(b, smem_addr(ks + tile_off(row, kk * 2 + (mat & 1))));
+                    mma_bf16_16816(s[2 * np], qf[kk], b[0], b[1]);
+                    mma_bf16_16816(s[2 * np + 1], qf[kk], b[2], b[3]);
+                }
+            }
+            float mx_a = -FLT_MAX, mx_b = -FLT_MAX;
+#pragma unroll
+            for (int nb = 0; nb < 8; ++nb) {
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int t = j * PA_BKV + nb * 8 + cq + e;
+                    s[nb][e] = t <= qpos_a ? s[nb][e] * scale : -INFINITY;
+                    s[nb][2 + e] = t <= qpos_b ? s[nb][2 + e] * scale : -INFINITY;
+                    mx_a = fmaxf(mx_a, s[nb][e]);
+                    mx_b = fmaxf(mx_b, s[nb][2 + e]);
+                }
+            }
+            mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
+            mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
+            mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
+            mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
+            const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+            const float corr_a = exp2f(m_a - mn_a), corr_b = exp2f(m_b - mn_b);
+            m_a = mn_a;
+            m_b = mn_b;
+            float sum_a = 0.0f, sum_b = 0.0f;
+#pragma unroll
+            for (int nb = 0; nb < 8; ++nb) {
+                s[nb][0] = exp2f(s[nb][0] - mn_a);
+                s[nb][1] = exp2f(s[nb][1] - mn_a);
+                s[nb][2] = exp2f(s[nb][2] - mn_b);
+                s[nb][3] = exp2f(s[nb][3] - mn_b);
+                sum_a += s[nb][0] + s[nb][1];
+                sum_b += s[nb][2] + s[nb][3];
+            }
+            l_a = l_a * corr_a + sum_a;
+            l_b = l_b * corr_b + sum_b;
+#pragma unroll
+            for (int nb = 0; nb < 16; ++nb) {
+                o[nb][0] *= corr_a;
+                o[nb][1] *= corr_a;
+                o[nb][2] *= corr_b;
+                o[nb][3] *= corr_b;
+            }
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                const uint32_t pa[4] = {pack2_bf16(s[2 * kk][0], s[2 * kk][1]),
+                                        pack2_bf16(s[2 * kk][2], s[2 * kk][3]),
+                                        pack2_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]),
+                                        pack2_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3])};
+#pragma unroll
+                for (int np = 0; np < 8; ++np) {
+                    uint32_t b[4];
+                    const int row = kk * 16 + (lane & 7) + (mat & 1) * 8;
+                    ldsm_x4_t(b, smem_addr(vs + tile_off(row, np * 2 + (mat >> 1))));
+                    mma_bf16_16816(o[2 * np], pa, b[0], b[1]);
+                    mma_bf16_16816(o[2 * np + 1], pa, b[2], b[3]);
+                }
+            }
+        }
+        __syncthreads();
+    }
+    cp_async_wait<0>();
+
+    l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
+    l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
+    l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
+    l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
+    const float inv_a = 1.0f / l_a, inv_b = 1.0f / l_b;
+    if (ra < a.rows) {
+        uint16_t* out = a.out + static_cast<size_t>(ra) * qd + h * HD + cq;
+#pragma unroll
+        for (int nb = 0; nb < 16; ++nb) {
+            *reinterpret_cast<uint32_t*>(out + nb * 8) = pack2_bf16(o[nb][0] * inv_a, o[nb][1] * inv_a);
+        }
+    }
+    if (rb < a.rows) {
+        uint16_t* out = a.out + static_cast<size_t>(rb) * qd + h * HD + cq;
+#pragma unroll
+        for (int nb = 0; nb < 16; ++nb) {
+            *reinterpret_cast<uint32_t*>(out + nb * 8) = pack2_bf16(o[nb][2] * inv_b, o[nb][3] * inv_b);
+        }
+    }
+}
+
+int device_sms(int device) {
+    int n = 0;
+    Q3_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device));
+    return n;
+}
+
+}  // namespace
+
+void launch_rmsnorm_rows_bf16(const int32_t* ids, const uint16_t* embed, float* x,
+                              const uint16_t* w, float eps, uint16_t* out, int rows, int dim,
+                              cudaStream_t s) {
+    if (rows <= 0) return;
+    rmsnorm_rows_kernel<<<rows, kNormThreads, 0, s>>>(ids, embed, x, w, eps, out, dim);
+    Q3_CUDA(cudaGetLastError());
+}
+
+void launch_prefill_qkv(const PrefillQkvArgs& a, cudaStream_t s) {
+    if (a.rows <= 0) return;
+    const dim3 grid(a.rows, (a.n_heads + 2 * a.n_kv + 7) / 8);
+    prefill_qkv_kernel<<<grid, 256, 0, s>>>(a);
+    Q3_CUDA(cudaGetLastError());
+}
+
+void launch_prefill_attention(const PrefillAttnArgs& a, cudaStream_t s) {
+    if (a.rows <= 0) return;
+    static bool configured[64] = {};
+    int dev = 0;
+    Q3_CUDA(cudaGetDevice(&dev));
+    if (!configured[dev & 63]) {
+        Q3_CUDA(cudaFuncSetAttribute(prefill_attn_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, PA_SMEM));
+        configured[dev & 63] = true;
+    }
+    const dim3 grid((a.rows + PA_BQ - 1) / PA_BQ, a.n_kv);
+    prefill_attn_kernel<<<grid, PA_THREADS, PA_SMEM, s>>>(a);
+    Q3_CUDA(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------ driver
+
+bool Prefill::supported(const q3_config& c) {
+    return c.head_dim == HD && c.rotary_dim == HD && c.n_kv_heads > 0 &&
+           c.n_heads == 2 * c.n_kv_heads && c.dim % 256 == 0 && c.hidden_dim % 128 == 0 &&
+           (c.n_heads * HD) % 64 == 0 && ((c.n_heads + 2 * c.n_kv_heads) * HD) % 128 == 0 &&
+           c.dim % 128 == 0;
+}
+
+Prefill::Prefill(const q3_config& c, int device) : cfg_(c), device_(device) {
+    num_sms_ = device_sms(device);
+    err_.alloc(sizeof(unsigned));
+    Q3_CUDA(cudaMemset(err_.ptr, 0, sizeof(unsigned)));
+}
+
+void Prefill::ensure_rows(int rows) {
+    if (rows <= cap_rows_) return;
+    const int cap = (rows + 127) / 128 * 128;
+    const q3_config& c = cfg_;
+    const size_t qd = static_cast<size_t>(c.n_heads) * HD;
+    const size_t qkv = static_cast<size_t>(c.n_heads + 2 * c.n_kv_heads) * HD;
+    x_.alloc(static_cast<size_t>(cap) * c.dim * 4);
+    xn_.alloc(static_cast<size_t>(cap) * c.dim * 2);
+    qkv_.alloc(static_cast<size_t>(cap) * qkv * 4);
+    q_.alloc(static_cast<size_t>(cap) * qd * 2);
+    o_.alloc(static_cast<size_t>(cap) * qd * 2);
+    h_.alloc(static_cast<size_t>(cap) * c.hidden_dim * 2);
+    cap_rows_ = cap;
+}
+
+void Prefill::ensure_weight_maps(const std::vector<LayerWeights>& layers) {
+    if (!layers.empty() && wmaps_key_ == layers[0].wqkv && wmaps_.size() == layers.size()) return;
+    const q3_config& c = cfg_;
+    const int qd = c.n_heads * HD;
+    const int qkv = (c.n_heads + 2 * c.n_kv_heads) * HD;
+    wmaps_.resize(layers.size());
+    for (size_t l = 0; l < layers.size(); ++l) {
+        const LayerWeights& w = layers[l];
+        make_tmap_bf16(&wmaps_[l].wqkv, w.wqkv, qkv, c.dim, gemm_tile_n(kEpiStoreF32, qkv));
+        make_tmap_bf16(&wmaps_[l].wo, w.wo, c.dim, qd, gemm_tile_n(kEpiAddF32, c.dim));
+        make_tmap_bf16(&wmaps_[l].w1, w.w1, c.hidden_dim, c.dim, 128);
+        make_tmap_bf16(&wmaps_[l].w3, w.w3, c.hidden_dim, c.dim, 128);
+        make_tmap_bf16(&wmaps_[l].w2, w.w2, c.dim, c.hidden_dim, gemm_tile_n(kEpiAddF32, c.dim));
+    }
+    wmaps_key_ = layers.empty() ? nullptr : layers[0].wqkv;
+}
+
+unsigned Prefill::read_error(cudaStream_t s) {
+    unsigned v = 0;
+    Q3_CUDA(cudaMemcpyAsync(&v, err_.ptr, sizeof(v), cudaMemcpyDeviceToHost, s));
+    Q3_CUDA(cudaStreamSynchronize(s));
+    if (v) Q3_CUDA(cudaMemsetAsync(err_.ptr, 0, sizeof(unsigned), s));
+    return v;
+}
+
+void Prefill::run(const int32_t* ids_dev, int n, int pos0, const uint16_t* embed,
+                  const std::vector<LayerWeights>& layers, Engine& e, float* x_last, float* taps,
+                  cudaStream_t s) {
+    const q3_config& c = cfg_;
+    if (n <= 0) return;
+    if (pos0 < 0 || pos0 + n > c.max_seq_len) {
+        throw std::out_of_range("batched prefill past the context length");
+    }
+    if (e.rope_len() < pos0 + n) throw std::runtime_error("RoPE table shorter than the prompt");
+    const int qd = c.n_heads * HD;
+    const int qkv = (c.n_heads + 2 * c.n_kv_heads) * HD;
+    const int L = static_cast<int>(layers.size());
+    ensure_rows(std::min(n, kMaxChunk));
+    ensure_weight_maps(layers);
+    if (kv_key_ != e.k_layer(0)) {
+        const uint64_t kv_rows =
+            static_cast<uint64_t>(L) * e.n_pages() * c.n_kv_heads * kPageTokens;
+        make_tmap_bf16(&kmap_, e.k_layer(0), kv_rows, HD, kPageTokens);
+        make_tmap_bf16(&vmap_, e.v_layer(0), kv_rows, HD, kPageTokens);
+        kv_key_ = e.k_layer(0);
+    }
+    float* X = static_cast<float*>(x_.ptr);
+    uint16_t* Xn = static_cast<uint16_t*>(xn_.ptr);
+    unsigned* err = static_cast<unsigned*>(err_.ptr);
+
+    for (int c0 = 0; c0 < n; c0 += kMaxChunk) {
+        const int S = std::min(kMaxChunk, n - c0);
+        const int p0 = pos0 + c0;
+        const bool last = c0 + S == n;
+        CUtensorMap m_xn, m_o, m_h, m_q;
+        make_tmap_bf16(&m_q, q_.ptr, S, qd, 64);
+        make_tmap_bf16(&m_xn, xn_.ptr, S, c.dim, 128);
+        make_tmap_bf16(&m_o, o_.ptr, S, qd, 128);
+        make_tmap_bf16(&m_h, h_.ptr, S, c.hidden_dim, 128);
+        auto tap = [&](int slot) {
+            if (taps && last) {
+                Q3_CUDA(cudaMemcpyAsync(taps + static_cast<size_t>(slot) * c.dim,
+                                        X + static_cast<size_t>(S - 1) * c.dim, c.dim * 4,
+                                        cudaMemcpyDeviceToDevice, s));
+            }
+        };
+        launch_rmsnorm_rows_bf16(ids_dev + c0, embed, X, layers[0].attn_norm, c.norm_eps, Xn, S,
+                                 c.dim, s);
+        tap(0);
+        for (int l = 0; l < L; ++l) {
+            const LayerWeights& w = layers[l];
+            const LayerMaps& wm = wmaps_[l];
+            GemmArgs g;
+            g.err = err;
+            g.M = S;
+            // [wq; wk; wv] . xn -> fp32 q|k|v rows (src/inference.cpp:795-798).
+            g.N = qkv;
+            g.K = c.dim;
+            g.out = qkv_.ptr;
+            g.ldo = qkv;
+            Q3_CUDA(launch_gemm(m_xn, wm.wqkv, nullptr, g, kEpiStoreF32, num_sms_, s));
+            PrefillQkvArgs qa{};
+            qa.qkv = static_cast<const float*>(qkv_.ptr);
+            qa.q_norm = w.q_norm;
+            qa.k_norm = w.k_norm;
+            qa.rope = e.rope();
+            qa.q_out = static_cast<uint16_t*>(q_.ptr);
+            qa.k_cache = e.k_layer(l);
+            qa.v_cache = e.v_layer(l);
+            qa.page_table = e.page_table();
+            qa.rows = S;
+            qa.pos0 = p0;
+            qa.n_heads = c.n_heads;
+            qa.n_kv = c.n_kv_heads;
+            qa.eps = c.norm_eps;
+            launch_prefill_qkv(qa, s);
+            if (use_tc_attention_) {
+                PrefillAttnTcArgs ta{};
+                ta.page_table = e.page_table();
+                ta.out = static_cast<uint16_t*>(o_.ptr);
+                ta.err = err;
+                ta.rows = S;
+                ta.pos0 = p0;
+                ta.n_kv = c.n_kv_heads;
+                ta.n_pages = e.n_pages();
+                ta.layer = l;
+                launch_prefill_attention_tc(m_q, kmap_, vmap_, ta, s);
+            } else {
+                PrefillAttnArgs aa{};
+                aa.q = static_cast<const uint16_t*>(q_.ptr);
+                aa.k_cache = e.k_layer(l);
+                aa.v_cache = e.v_layer(l);
+                aa.page_table = e.page_table();
+                aa.out = static_cast<uint16_t*>(o_.ptr);
+                aa.rows = S;
+                aa.pos0 = p0;
+                aa.n_heads = c.n_heads;
+                aa.n_kv = c.n_kv_heads;
+                launch_prefill_attention(aa, s);
+            }
+            // x += wo . attn (:846-849).
+            g.N = c.dim;
+            g.K = qd;
+            g.out = X;
+            g.ldo = c.dim;
+            Q3_CUDA(launch_gemm(m_o, wm.wo, nullptr, g, kEpiAddF32, num_sms_, s));
+            launch_rmsnorm_rows_bf16(nullptr, nullptr, X, w.mlp_norm, c.norm_eps, Xn, S, c.dim, s);
+            // h = silu(w1 . xn) * (w3 . xn) (:851, :1005-1011).
+            g.N = 2 * c.hidden_dim;
+            g.K = c.dim;
+            g.out = h_.ptr;
+            g.ldo = c.hidden_dim;
+            Q3_CUDA(launch_gemm(m_xn, wm.w1, &wm.w3, g, kEpiSwiGLU, num_sms_, s));
+            // x += w2 . h (:1013, :863-865).
+            g.N = c.dim;
+            g.K = c.hidden_dim;
+            g.out = X;
+            g.ldo = c.dim;
+            Q3_CUDA(launch_gemm(m_h, wm.w2, nullptr, g, kEpiAddF32, num_sms_, s));
+            if (l + 1 < L) {
+                launch_rmsnorm_rows_bf16(nullptr, nullptr, X, layers[l + 1].attn_norm, c.norm_eps,
+                                         Xn, S, c.dim, s);
+            }
+            tap(l + 1);
+        }
+        if (last) {
+            Q3_CUDA(cudaMemcpyAsync(x_last, X + static_cast<size_t>(S - 1) * c.dim, c.dim * 4,
+                                    cudaMemcpyDeviceToDevice, s));
+        }
+    }
+}
+
+}  // namespace q3

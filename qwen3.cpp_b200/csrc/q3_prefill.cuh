@@ -1,0 +1,109 @@
+// Batched prefill of a prompt chunk (the reference prefills one token at a time through
+// ForwardToken, src/inference.cpp:669-671): every projection is a tensor-core contraction over all
+// tokens of the chunk (q3_gemm.cuh), attention is causal flash attention over the paged KV cache.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <vector>
+
+#include "q3_common.cuh"
+#include "q3_model.cuh"
+
+namespace q3 {
+
+// Row-wise RmsNorm (src/inference.cpp:887-923) of fp32 rows into bf16 MMA operands; with ids
+// non-null, the fp32 rows are first gathered from the embedding (:601-603) into x.
+void launch_rmsnorm_rows_bf16(const int32_t* ids, const uint16_t* embed, float* x,
+                              const uint16_t* w, float eps, uint16_t* out, int rows, int dim,
+                              cudaStream_t s);
+
+// Per-token, per-head QK-RMSNorm + RoPE (src/inference.cpp:800-810) and bf16 K/V write into the
+// paged cache at kv_pos = pos (:812-815) for tokens at positions pos0 .. pos0+rows-1, all below
+// the context length (no ring wrap). q is written as bf16 [rows, n_heads*128].
+struct PrefillQkvArgs {
+    const float* qkv;          // [rows, (n_heads + 2*n_kv) * 128] fp32
+    const uint16_t* q_norm;
+    const uint16_t* k_norm;
+    const float2* rope;        // [len][64] (cos, sin)
+    uint16_t* q_out;           // [rows, n_heads*128] bf16
+    uint16_t* k_cache;
+    uint16_t* v_cache;
+    const int32_t* page_table;
+    int rows, pos0, n_heads, n_kv;
+    float eps;
+};
+void launch_prefill_qkv(const PrefillQkvArgs& a, cudaStream_t s);
+
+// Causal attention of `rows` query tokens (positions pos0..) over KV positions [0, pos] of the
+// paged cache (FastAttn + Softmax, src/inference.cpp:1017-1058, :925-946, for every prompt token
+// at once); head_dim 128, two query heads per KV head. out bf16 [rows, n_heads*128].
+struct PrefillAttnArgs {
+    const uint16_t* q;
+    const uint16_t* k_cache;
+    const uint16_t* v_cache;
+    const int32_t* page_table;
+    uint16_t* out;
+    int rows, pos0, n_heads, n_kv;
+};
+void launch_prefill_attention(const PrefillAttnArgs& a, cudaStream_t s);
+
+// The same attention on tcgen05 tensor cores (q3_prefill_attn.cu). q maps the bf16 q rows
+// [rows, n_heads*128] with 64 x 64 boxes; k and v map each whole paged cache (every layer) as
+// [n_layers * n_pages * n_kv * 16, 128] with 64 x 16 boxes.
+struct PrefillAttnTcArgs {
+    const int32_t* page_table;
+    uint16_t* out;             // [rows, n_heads*128] bf16
+    unsigned* err;             // set non-zero when a bounded wait gives up
+    long long budget = 4000000000LL;
+    int rows, pos0, n_kv, n_pages, layer;
+};
+void launch_prefill_attention_tc(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
+                                 const PrefillAttnTcArgs& a, cudaStream_t s);
+
+// Driver of a batched prefill over the layers of a Model.
+class Prefill {
+public:
+    static constexpr int kMaxChunk = 4096;  // tokens per pass; longer prompts run in chunks
+
+    // The shapes the batched path handles (head_dim 128 with full rotary width, 2 query heads
+    // per KV head, widths that tile by the contraction kernel); others prefill token by token.
+    static bool supported(const q3_config& c);
+
+    Prefill(const q3_config& c, int device);
+    ~Prefill() = default;
+
+    // Runs every layer for tokens ids_dev[0..n) at positions pos0..pos0+n-1 (pos0 + n <= ctx),
+    // writing each layer's K/V rows into the engine's cache, and leaves the hidden state of the
+    // last token in x_last (fp32 [dim]). taps (nullable) receive the last token's hidden state
+    // before the first layer and after every layer ([(n_layers+1) * dim]).
+    void run(const int32_t* ids_dev, int n, int pos0, const uint16_t* embed,
+             const std::vector<LayerWeights>& layers, Engine& e, float* x_last, float* taps,
+             cudaStream_t s);
+    // Non-zero when a contraction's bounded wait gave up in the last run.
+    unsigned read_error(cudaStream_t s);
+    // Attention kernel: tcgen05 (default) or the mma.sync flash-attention kernel.
+    void set_tc_attention(bool on) { use_tc_attention_ = on; }
+
+private:
+    void ensure_rows(int rows);
+    void ensure_weight_maps(const std::vector<LayerWeights>& layers);
+
+    q3_config cfg_;
+    int device_ = 0;
+    int num_sms_ = 148;
+    int cap_rows_ = 0;
+    bool use_tc_attention_ = true;
+    DeviceBuffer x_, xn_, qkv_, q_, o_, h_, err_;
+    struct LayerMaps {
+        CUtensorMap wqkv, wo, w1, w3, w2;
+    };
+    std::vector<LayerMaps> wmaps_;
+    const uint16_t* wmaps_key_ = nullptr;
+    CUtensorMap kmap_, vmap_;
+    const uint16_t* kv_key_ = nullptr;
+};
+
+}  // namespace q3

@@ -1,0 +1,416 @@
+// Causal prefill attention on tcgen05 tensor cores (sm_100a): FastAttn + Softmax
+// (src/inference.cpp:1017-1058, :925-946) for every prompt token of a chunk at once.
+//
+// One CTA per (64-token query block, KV head g). The two query heads 2g and 2g+1 share the KV
+// head, so their 64 rows each are stacked into one 128-row operand Q (rows 0-63 head 2g, rows
+// 64-127 head 2g+1) and every K/V tile is read once for both. KV tiles are 128 positions (8
+// pages of 16), streamed by TMA from the paged cache. Per tile j:
+//   MMA warp      S_j = Q . K_j^T into TMEM buffer j%2 (M=128, N=128, K=128 dims)
+//   softmax warps two threads per row r (64 keys each): masked row max (exchanged through shared
+//                 memory), P_j = exp2(S_j*scale - m_j) written to shared memory as bf16 in the
+//                 MMA's operand layout, partial row sums
+//   MMA warp      O_j = P_j . V_j into TMEM buffer 2 + j%2 (V read as an MN-major operand)
+//   softmax warps acc = acc * exp2(m_{j-1} - m_j) + O_j in registers (64 fp32 per thread)
+// S_{j+1} runs on the tensor cores while the softmax warps work on S_j, and O_j while they work
+// on S_{j+1}. Warp roles: 0 TMA producer, 1 MMA issuer, 2-9 softmax (warp w reads TMEM lanes
+// 32*(w%4).. and column half (w-2)/4).
+// Every wait is bounded; a wait that gives up sets *err and the CTA drains and returns.
+#include <cuda_bf16.h>
+
+#include <stdexcept>
+
+#include "q3_prefill.cuh"
+#include "q3_sm100.cuh"
+
+namespace q3 {
+
+namespace {
+
+using namespace sm100;
+
+constexpr int HD = 128;
+constexpr int ROWS = 128;                 // 64 tokens x 2 query heads
+constexpr int TOK = 64;
+constexpr int KEYS = 128;                 // KV positions per tile
+constexpr int PANEL = ROWS * 128;         // bytes of a 64-column panel of 128 rows
+constexpr int Q_OFF = 0;                  // Q: 2 panels
+constexpr int KV_OFF = 2 * PANEL;         // 2 stages x (K: 2 panels, V: 2 panels)
+constexpr int KV_STAGE = 4 * PANEL;
+constexpr int P_OFF = KV_OFF + 2 * KV_STAGE;  // 2 buffers x 2 panels
+constexpr int P_BUF = 2 * PANEL;
+constexpr int RED_OFF = P_OFF + 2 * P_BUF;    // 229,376: row-max exchange [2][2][128] floats
+constexpr int BAR_OFF = RED_OFF + 2 * 2 * ROWS * 4;
+constexpr int SMEM = BAR_OFF + 256;           // 231,680 (base 1024-aligned, checked)
+constexpr int NSOFT = 8;                      // softmax warps
+constexpr int NTHREADS = 64 + NSOFT * 32;
+constexpr uint32_t TMEM_COLS = 512;       // S0, S1, O0, O1: 128 fp32 columns each
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// MN-major operand descriptor with 128-byte swizzling: 64-element rows of 128 B along N, 8-row
+// groups along K at 1024 B, further 64-element panels along N at `panel_bytes`.
+__device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t saddr, uint32_t panel_bytes) {
+    uint64_t d = static_cast<uint64_t>((saddr & 0x3FFFF) >> 4);
+    d |= static_cast<uint64_t>((panel_bytes >> 4) & 0x3FFF) << 16;  // leading: next N panel
+    d |= static_cast<uint64_t>(1024 >> 4) << 32;                     // stride: next 8 K rows
+    d |= static_cast<uint64_t>(1) << 46;
+    d |= static_cast<uint64_t>(2) << 61;
+    return d;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__device__ __forceinline__ void fail(volatile int* abort, unsigned* err, unsigned code) {
+    *abort = 1;
+    if (err) atomicCAS(err, 0u, code);
+}
+
+// acc = acc * exp2(m_acc - m_i) + O_i for this thread's 64 columns of O_i (TMEM buffer
+// 2 + i%2); m_acc = m_i.
+__device__ __forceinline__ bool fold_o(float (&acc)[HD / 2], float& m_acc, int i, float m_i,
+                                       uint32_t tmem_lane_half, uint64_t* o_full,
+                                       uint64_t* o_empty, int lane, long long budget,
+                                       volatile int* abort) {
+    if (!mbar_wait(&o_full[i & 1], (i >> 1) & 1, budget, abort)) return false;
+    tc_fence_after();
+    const float f = exp2f(m_acc - m_i);
+    const uint32_t ob = tmem_lane_half + static_cast<uint32_t>(256 + (i & 1) * 128);
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+        float o[32];
+        tmem_ld32(ob + c * 32, o);
+#pragma unroll
+        for (int k = 0; k < 32; ++k) acc[c * 32 + k] = fmaf(acc[c * 32 + k], f, o[k]);
+    }
+    m_acc = m_i;
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&o_empty[i & 1]);
+    return true;
+}
+
+// The two threads of row r (one per column half) publish a value and read the other's, through
+// shared memory and an mbarrier of the tile parity t & 1. NaN when the wait gave up.
+__device__ __forceinline__ float exchange_row(float* red, uint64_t* mx_bar, int t, int half, int r,
+                                              float v, long long budget, volatile int* abort) {
+    red[((t & 1) * 2 + half) * ROWS + r] = v;
+    mbar_arrive(&mx_bar[t & 1]);
+    if (!mbar_wait(&mx_bar[t & 1], (t >> 1) & 1, budget, abort)) return __int_as_float(0x7fc00000);
+    return red[((t & 1) * 2 + (half ^ 1)) * ROWS + r];
+}
+
+__global__ void __launch_bounds__(NTHREADS, 1)
+    prefill_attn_tc_kernel(const __grid_constant__ CUtensorMap tq,
+                           const __grid_constant__ CUtensorMap tk,
+                           const __grid_constant__ CUtensorMap tv, const PrefillAttnTcArgs a) {
+    extern __shared__ __align__(1024) uint8_t sm[];
+    // The swizzled operand panels need a 1024-byte aligned base; nothing is touched otherwise.
+    if ((smem_u32(sm) & 1023) != 0) {
+        if (threadIdx.x == 0 && a.err) atomicCAS(a.err, 0u, 10u);
+        return;
+    }
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + BAR_OFF);
+    uint64_t* q_full = bars;
+    uint64_t* kv_full = bars + 1;   // [2]
+    uint64_t* kv_empty = bars + 3;  // [2]
+    uint64_t* s_full = bars + 5;    // [2]
+    uint64_t* s_empty = bars + 7;   // [2]
+    uint64_t* p_full = bars + 9;    // [2]
+    uint64_t* o_full = bars + 11;   // [2]
+    uint64_t* o_empty = bars + 13;  // [2]
+    uint64_t* done = bars + 15;
+    uint64_t* mx_bar = bars + 16;   // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+    float* red = reinterpret_cast<float*>(sm + RED_OFF);  // [tile parity][half][row]
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int qb = gridDim.x - 1 - blockIdx.x;  // longest query blocks first
+    const int g = blockIdx.y;
+    const int tok0 = qb * TOK;
+    const int last_tok = min(a.rows, tok0 + TOK) - 1;
+    const int kv_end = a.pos0 + last_tok + 1;
+    const int ntiles = (kv_end + KEYS - 1) / KEYS;
+    const int valid_pages = (kv_end + kPageTokens - 1) / kPageTokens;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&kv_full[i], 1);
+            mbar_init(&kv_empty[i], 1);
+            mbar_init(&s_full[i], 1);
+            mbar_init(&s_empty[i], NSOFT);
+            mbar_init(&p_full[i], NSOFT);
+            mbar_init(&o_full[i], 1);
+            mbar_init(&o_empty[i], NSOFT);
+            mbar_init(&mx_bar[i], NSOFT * 32);
+        }
+        mbar_init(done, 1);
+        *abort = 0;
+        mbar_fence_init();
+    }
+    if (warp == 0) {
+        tma_prefetch_map(&tq);
+        tma_prefetch_map(&tk);
+        tma_prefetch_map(&tv);
+        tmem_alloc(tmem_slot, TMEM_COLS);
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ------------------------------------------------------------ TMA producer
+            uint32_t issued = 0, issued_parity = 0;  // bit 0: q, bits 1-2: kv stages
+            mbar_arrive_expect_tx(q_full, 2 * PANEL);
+            for (int hs = 0; hs < 2; ++hs) {
+                for (int p = 0; p < 2; ++p) {
+                    tma_load_2d(sm + Q_OFF + p * PANEL + hs * (PANEL / 2), &tq,
+                                (2 * g + hs) * HD + p * 64, tok0, q_full);
+                }
+            }
+            issued |= 1u;
+            for (int j = 0; j < ntiles && !*abort; ++j) {
+                const int st = j & 1;
+                const uint32_t ph = (j >> 1) & 1;
+                if (!mbar_wait(&kv_empty[st], ph ^ 1, a.budget, abort)) {
+                    fail(abort, a.err, 11);
+                    break;
+                }
+                uint8_t* ks = sm + KV_OFF + st * KV_STAGE;
+                uint8_t* vs = ks + 2 * PANEL;
+                mbar_arrive_expect_tx(&kv_full[st], KV_STAGE);
+                for (int pg = 0; pg < KEYS / kPageTokens; ++pg) {
+                    // Pages past the last valid one repeat it: finite values whose scores the
+                    // softmax masks (a zero probability times a finite value adds nothing).
+                    const int page = min(j * (KEYS / kPageTokens) + pg, valid_pages - 1);
+                    const int phys = __ldg(a.page_table + page);
+                    const int row = ((a.layer * a.n_pages + phys) * a.n_kv + g) * kPageTokens;
+                    for (int p = 0; p < 2; ++p) {
+                        tma_load_2d(ks + p * PANEL + pg * (kPageTokens * 128), &tk, p * 64, row,
+                                    &kv_full[st]);
+                        tma_load_2d(vs + p * PANEL + pg * (kPageTokens * 128), &tv, p * 64, row,
+                                    &kv_full[st]);
+                    }
+                }
+                issued |= 2u << st;
+                issued_parity = (issued_parity & ~(2u << st)) | (ph << (st + 1));
+            }
+            // Drain: every issued load has landed before the CTA exits.
+            const long long t0 = clock64();
+            while (!mbar_try_wait(q_full, 0)) {
+                if (clock64() - t0 > a.budget) {
+                    fail(abort, a.err, 12);
+                    break;
+                }
+            }
+            for (int st = 0; st < 2; ++st) {
+                if (!(issued & (2u << st))) continue;
+                const long long t1 = clock64();
+                while (!mbar_try_wait(&kv_full[st], (issued_parity >> (st + 1)) & 1)) {
+                    if (clock64() - t1 > a.budget) {
+                        fail(abort, a.err, 12);
+                        break;
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ------------------------------------------------------------ MMA issuer
+            const uint32_t idesc_s = idesc_bf16_f32(ROWS, KEYS);
+            const uint32_t idesc_pv = idesc_bf16_f32(ROWS, HD) | (1u << 16);  // B MN-major
+            const uint32_t q_addr = smem_u32(sm + Q_OFF);
+            bool ok = mbar_wait(q_full, 0, a.budget, abort);
+            if (!ok) fail(abort, a.err, 13);
+            for (int j = 0; ok && j <= ntiles && !*abort; ++j) {
+                if (j < ntiles) {
+                    const int st = j & 1;
+                    if (!mbar_wait(&kv_full[st], (j >> 1) & 1, a.budget, abort) ||
+                        !mbar_wait(&s_empty[j & 1], ((j >> 1) & 1) ^ 1, a.budget, abort)) {
+                        fail(abort, a.err, 14);
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t k_addr = smem_u32(sm + KV_OFF + st * KV_STAGE);
+                    const uint32_t d = tmem + static_cast<uint32_t>((j & 1) * 128);
+#pragma unroll
+                    for (int kk = 0; kk < HD / 16; ++kk) {
+                        const uint64_t ad = desc_k_sw128(q_addr + (kk >> 2) * PANEL) + 2 * (kk & 3);
+                        const uint64_t bd = desc_k_sw128(k_addr + (kk >> 2) * PANEL) + 2 * (kk & 3);
+                        mma_bf16(d, ad, bd, idesc_s, kk > 0);
+                    }
+                    mma_commit(&s_full[j & 1]);
+                }
+                if (j >= 1) {
+                    const int i = j - 1, st = i & 1;
+                    if (!mbar_wait(&p_full[i & 1], (i >> 1) & 1, a.budget, abort) ||
+                        !mbar_wait(&o_empty[i & 1], ((i >> 1) & 1) ^ 1, a.budget, abort)) {
+                        fail(abort, a.err, 15);
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t p_addr = smem_u32(sm + P_OFF + (i & 1) * P_BUF);
+                    const uint32_t v_addr = smem_u32(sm + KV_OFF + st * KV_STAGE + 2 * PANEL);
+                    const uint32_t d = tmem + static_cast<uint32_t>(256 + (i & 1) * 128);
+#pragma unroll
+                    for (int kk = 0; kk < KEYS / 16; ++kk) {
+                        const uint64_t ad = desc_k_sw128(p_addr + (kk >> 2) * PANEL) + 2 * (kk & 3);
+                        const uint64_t bd = desc_mn_sw128(v_addr + kk * 16 * 128, PANEL);
+                        mma_bf16(d, ad, bd, idesc_pv, kk > 0);
+                    }
+                    mma_commit(&o_full[i & 1]);
+                    mma_commit(&kv_empty[st]);
+                }
+            }
+            mma_commit(done);
+            const long long t0 = clock64();
+            while (!mbar_try_wait(done, 0)) {
+                if (clock64() - t0 > a.budget) {
+                    fail(abort, a.err, 16);
+                    break;
+                }
+            }
+        }
+    } else {
+        // ---------------------------------------------------------------- softmax warps
+        const int lg = warp & 3;
+        const int half = (warp - 2) >> 2;                // key half of S, column half of O
+        const int r = lg * 32 + lane;                    // row of the 128-row tile
+        const int tok = min(tok0 + (r & (TOK - 1)), last_tok);
+        const int qpos = a.pos0 + tok;
+        const uint32_t lane_half = tmem + (static_cast<uint32_t>(lg * 32) << 16) +
+                                   static_cast<uint32_t>(half * 64);
+        const float scale = 1.4426950408889634f / sqrtf(static_cast<float>(HD));
+        float acc[HD / 2];
+#pragma unroll
+        for (int i = 0; i < HD / 2; ++i) acc[i] = 0.0f;
+        float m_run = -1e30f, l = 0.0f, m_acc = -1e30f, m_prev = -1e30f;
+        bool ok = true;
+
+        for (int t = 0; t < ntiles && !*abort; ++t) {
+            if (!mbar_wait(&s_full[t & 1], (t >> 1) & 1, a.budget, abort)) {
+                fail(abort, a.err, 17);
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t sb = lane_half + static_cast<uint32_t>((t & 1) * 128);
+            const int key0 = t * KEYS + half * 64;
+            float mx = -1e30f;
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                float s[32];
+                tmem_ld32(sb + c * 32, s);
+#pragma unroll
+                for (int k = 0; k < 32; ++k) {
+                    if (key0 + c * 32 + k <= qpos) mx = fmaxf(mx, s[k] * scale);
+                }
+            }
+            const float other = exchange_row(red, mx_bar, t, half, r, mx, a.budget, abort);
+            if (other != other) {
+                fail(abort, a.err, 19);
+                ok = false;
+                break;
+            }
+            const float m_new = fmaxf(m_run, fmaxf(mx, other));
+            float sum = 0.0f;
+            uint8_t* prow = sm + P_OFF + (t & 1) * P_BUF + half * PANEL + r * 128;
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                float s[32];
+                tmem_ld32(sb + c * 32, s);
+#pragma unroll
+                for (int k = 0; k < 32; ++k) {
+                    const float p = key0 + c * 32 + k <= qpos ? exp2f(s[k] * scale - m_new) : 0.0f;
+                    s[k] = p;
+                    sum += p;
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int chunk = (c * 4 + q) ^ (r & 7);
+                    *reinterpret_cast<uint4*>(prow + chunk * 16) =
+                        make_uint4(pack_bf16x2(s[8 * q], s[8 * q + 1]),
+                                   pack_bf16x2(s[8 * q + 2], s[8 * q + 3]),
+                                   pack_bf16x2(s[8 * q + 4], s[8 * q + 5]),
+                                   pack_bf16x2(s[8 * q + 6], s[8 * q + 7]));
+                }
+            }
+            tc_fence_before();
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&s_empty[t & 1]);
+                mbar_arrive(&p_full[t & 1]);
+            }
+            l = l * exp2f(m_run - m_new) + sum;
+            m_run = m_new;
+            if (t >= 1 && !fold_o(acc, m_acc, t - 1, m_prev, lane_half, o_full, o_empty, lane,
+                                   a.budget, abort)) {
+                fail(abort, a.err, 18);
+                ok = false;
+                break;
+            }
+            m_prev = m_new;
+        }
+        if (ok && !*abort && ntiles > 0 &&
+            !fold_o(acc, m_acc, ntiles - 1, m_prev, lane_half, o_full, o_empty, lane, a.budget,
+                    abort)) {
+            fail(abort, a.err, 18);
+            ok = false;
+        }
+        if (ok && !*abort) {
+            // Row sum = the two halves' partial sums (both relative to the same running max).
+            const float l_other = exchange_row(red, mx_bar, ntiles, half, r, l, a.budget, abort);
+            if (l_other != l_other) {
+                fail(abort, a.err, 19);
+            } else {
+                const int token = tok0 + (r & (TOK - 1));
+                if (token < a.rows) {
+                    const float inv = 1.0f / (l + l_other);
+                    uint4* dst = reinterpret_cast<uint4*>(
+                        a.out + static_cast<size_t>(token) * (2 * a.n_kv) * HD +
+                        (2 * g + (r >> 6)) * HD + half * 64);
+#pragma unroll
+                    for (int i = 0; i < HD / 16; ++i) {
+                        dst[i] = make_uint4(pack_bf16x2(acc[8 * i] * inv, acc[8 * i + 1] * inv),
+                                            pack_bf16x2(acc[8 * i + 2] * inv, acc[8 * i + 3] * inv),
+                                            pack_bf16x2(acc[8 * i + 4] * inv, acc[8 * i + 5] * inv),
+                                            pack_bf16x2(acc[8 * i + 6] * inv, acc[8 * i + 7] * inv));
+                    }
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+}  // namespace
+
+void launch_prefill_attention_tc(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
+                                 const PrefillAttnTcArgs& a, cudaStream_t s) {
+    if (a.rows <= 0) return;
+    static bool configured[64] = {};
+    int dev = 0;
+    Q3_CUDA(cudaGetDevice(&dev));
+    if (!configured[dev & 63]) {
+        Q3_CUDA(cudaFuncSetAttribute(prefill_attn_tc_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+        configured[dev & 63] = true;
+    }
+    const dim3 grid((a.rows + TOK - 1) / TOK, a.n_kv);
+    prefill_attn_tc_kernel<<<grid, NTHREADS, SMEM, s>>>(q, k, v, a);
+    Q3_CUDA(cudaGetLastError());
+}
+
+}  // namespace q3

@@ -99,6 +99,10 @@ def lib() -> C.CDLL:
         "q3_forward_token_layers": [vp, i32, C.c_int, vp, vp],
         "q3_kv_row": [vp, C.c_int, C.c_int, U16P, U16P],
         "q3_prefill": [vp, I32P, C.c_int, C.c_int, vp, vp],
+        "q3_prefill_layers": [vp, I32P, C.c_int, C.c_int, vp, vp, vp],
+        "q3_model_set_prefill_path": [vp, C.c_int],
+        "q3_model_prefill_path": [vp, C.POINTER(C.c_int)],
+        "q3_gemm_bf16": [vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, vp],
         "q3_decode_greedy": [vp, i32, C.c_int, C.c_int, vp, vp],
         "q3_decode_forced": [vp, I32P, C.c_int, C.c_int, vp, vp],
         "q3_generate": [vp, vp, C.c_int, sz, C.c_int, vp, C.POINTER(sz), C.POINTER(GenStats)],
@@ -153,7 +157,8 @@ class Qwen3:
 
     def __init__(self, path: str | os.PathLike, context_length: int = 512, device: int = 0):
         h = C.c_void_p()
-        check(lib().q3_model_load(str(path).encode(), context_length, device, C.byref(h)))
+        self._lib = lib()  # held so that close() still works during interpreter shutdown
+        check(self._lib.q3_model_load(str(path).encode(), context_length, device, C.byref(h)))
         self._h = h
         cfg = Config()
         check(lib().q3_model_config(h, C.byref(cfg)))
@@ -164,7 +169,7 @@ class Qwen3:
 
     def close(self) -> None:
         if getattr(self, "_h", None):
-            lib().q3_model_free(self._h)
+            self._lib.q3_model_free(self._h)
             self._h = None
 
     def __del__(self):
@@ -242,6 +247,30 @@ class Qwen3:
         check(lib().q3_prefill(self._h, ids, ids.size, pos0, _ptr(logits), nxt.ctypes.data))
         return logits, int(nxt[0])
 
+    def prefill_layers(self, ids, pos0: int = 0):
+        """Prefill returning the last prompt token's hidden state before the first layer and
+        after every layer, its logits and its greedy argmax."""
+        c = self.config
+        ids = np.ascontiguousarray(ids, np.int32)
+        hid = np.empty((c["n_layers"] + 1, c["dim"]), np.float32)
+        logits = np.empty(c["vocab_size"], np.float32)
+        nxt = np.zeros(1, np.int32)
+        check(lib().q3_prefill_layers(self._h, ids, ids.size, pos0, hid.ctypes.data,
+                                      logits.ctypes.data, nxt.ctypes.data))
+        return hid, logits, int(nxt[0])
+
+    PREFILL_TOKENWISE, PREFILL_BATCHED = 0, 1
+
+    @property
+    def prefill_path(self) -> int:
+        p = C.c_int()
+        check(lib().q3_model_prefill_path(self._h, C.byref(p)))
+        return p.value
+
+    @prefill_path.setter
+    def prefill_path(self, path: int) -> None:
+        check(lib().q3_model_set_prefill_path(self._h, int(path)))
+
     def decode_greedy(self, first_token: int, pos0: int, n_steps: int, want_logits=False):
         toks = np.empty(max(n_steps, 1), np.int32)
         logits = np.empty(self.config["vocab_size"], np.float32) if want_logits else None
@@ -280,13 +309,14 @@ class Block:
         counts = (C.c_size_t * 11)(*[w.size for w in self.weights])
         c = Config.from_dict(cfg)
         h = C.c_void_p()
-        check(lib().q3_block_create(C.byref(c), arr, counts, device, C.byref(h)))
+        self._lib = lib()
+        check(self._lib.q3_block_create(C.byref(c), arr, counts, device, C.byref(h)))
         self._h = h
         self.kv_shape = (cfg["max_seq_len"], cfg["n_kv_heads"] * cfg["head_dim"])
 
     def close(self):
         if getattr(self, "_h", None):
-            lib().q3_block_free(self._h)
+            self._lib.q3_block_free(self._h)
             self._h = None
 
     def __del__(self):
@@ -353,3 +383,11 @@ def attn_noalloc(out_ptr, q_ptr, k_ptr, v_ptr, head_dim, n_kv_heads, kv_len, str
 
 def greedy(logits_ptr, n, out_ptr, stream=None):
     check(lib().q3_greedy(logits_ptr, n, out_ptr, stream))
+
+
+GEMM_STORE_F32, GEMM_ADD_F32, GEMM_SWIGLU, GEMM_STORE_BF16 = 0, 1, 2, 3
+
+
+def gemm_bf16(out: int, a: int, w: int, w3, M: int, N: int, K: int, epilogue: int, stream=None):
+    """q3_gemm_bf16 on device pointers: out[M, N] = epilogue(A[M, K] . W[N, K]^T)."""
+    check(lib().q3_gemm_bf16(out, a, w, w3, M, N, K, epilogue, stream))

@@ -30,6 +30,9 @@ def models(request, q3lib, full_weights, cpu_model):
     """The GPU model on each decode path (fused whole-step kernel, layer-wise kernels)."""
     gpu = q3lib.Qwen3(full_weights, 512)
     gpu.decode_path = gpu.PATH_FUSED if request.param == "fused" else gpu.PATH_LAYERWISE
+    # These tests check the decode paths token for token against the oracle's free-running
+    # greedy run; the batched (bf16-operand) prefill has its own tests in test_gpu_prefill.py.
+    gpu.prefill_path = gpu.PREFILL_TOKENWISE
     assert gpu.decode_path == (gpu.PATH_FUSED if request.param == "fused" else gpu.PATH_LAYERWISE)
     yield gpu, cpu_model
     gpu.close()

@@ -1,0 +1,220 @@
+"""Batched prefill on the tensor cores.
+
+* The tcgen05 contraction (q3_gemm_bf16) against a float64 host product of the same bf16
+  operands, for every epilogue, at the prefill shapes and ragged row counts.
+* The whole batched prefill against the oracle: per-layer hidden state of the last prompt token
+  rel-L2 <= 1e-2, its logits max-abs <= 5e-2, KV rows rel-L2 <= 1e-2, and teacher-forced top-1
+  agreement >= 99% for decode steps that read the batched cache.
+"""
+import numpy as np
+import pytest
+
+import gen_weights
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+HIDDEN_REL_L2 = 1e-2
+LOGITS_MAX_ABS = 5e-2
+TOP1_AGREEMENT = 0.99
+GEMM_REL = 1e-4  # fp32 accumulation of exact bf16 products, any summation order
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def _bf16(t):
+    import torch
+    return t.to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 1024), (100, 1024, 2048), (128, 1024, 3072),
+                                   (300, 4096, 1024), (2048, 1024, 2048), (257, 256, 64)])
+def test_gemm_store_f32(q3lib, M, N, K):
+    import torch
+    g = torch.Generator().manual_seed(M * 7 + N + K)
+    a = _bf16(torch.randn(M, K, generator=g))
+    w = _bf16(torch.randn(N, K, generator=g) * 0.02)
+    ref = a.double() @ w.double().T
+    da, dw = a.cuda(), w.cuda()
+    out = torch.full((M, N), float("nan"), device="cuda")
+    q3lib.gemm_bf16(out.data_ptr(), da.data_ptr(), dw.data_ptr(), None, M, N, K,
+                    q3lib.GEMM_STORE_F32, torch.cuda.current_stream().cuda_stream)
+    got = out.cpu().double()
+    assert torch.isfinite(got).all()
+    assert float((got - ref).abs().max() / ref.abs().max()) < GEMM_REL
+
+
+def test_gemm_add_and_bf16(q3lib):
+    import torch
+    M, N, K = 333, 1024, 3072
+    g = torch.Generator().manual_seed(3)
+    a = _bf16(torch.randn(M, K, generator=g))
+    w = _bf16(torch.randn(N, K, generator=g) * 0.02)
+    base = torch.randn(M, N, generator=g)
+    ref = a.double() @ w.double().T
+    s = torch.cuda.current_stream().cuda_stream
+    da, dw = a.cuda(), w.cuda()  # kept alive while the library reads them
+    out = base.cuda()
+    q3lib.gemm_bf16(out.data_ptr(), da.data_ptr(), dw.data_ptr(), None, M, N, K,
+                    q3lib.GEMM_ADD_F32, s)
+    assert float((out.cpu().double() - (base.double() + ref)).abs().max() / ref.abs().max()) < GEMM_REL
+    ob = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    q3lib.gemm_bf16(ob.data_ptr(), da.data_ptr(), dw.data_ptr(), None, M, N, K,
+                    q3lib.GEMM_STORE_BF16, s)
+    got = ob.cpu().double()
+    # one bf16 rounding of the fp32 result
+    assert float(((got - ref).abs() / (ref.abs() + 1e-3 * ref.abs().max())).max()) < 2 ** -7
+
+
+def test_gemm_swiglu(q3lib):
+    import torch
+    M, N, K = 200, 3072, 1024
+    g = torch.Generator().manual_seed(4)
+    a = _bf16(torch.randn(M, K, generator=g))
+    w1 = _bf16(torch.randn(N, K, generator=g) * 0.05)
+    w3 = _bf16(torch.randn(N, K, generator=g) * 0.05)
+    g1 = a.double() @ w1.double().T
+    g3 = a.double() @ w3.double().T
+    ref = g1 / (1.0 + torch.exp(-g1)) * g3
+    out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    da, d1, d3 = a.cuda(), w1.cuda(), w3.cuda()
+    q3lib.gemm_bf16(out.data_ptr(), da.data_ptr(), d1.data_ptr(), d3.data_ptr(), M, N, K,
+                    q3lib.GEMM_SWIGLU, torch.cuda.current_stream().cuda_stream)
+    got = out.cpu().double()
+    scale = ref.abs().max()
+    assert float(((got - ref).abs() / (ref.abs() + 1e-3 * scale)).max()) < 2 ** -7
+
+
+def test_gemm_rejects_bad_shapes(q3lib):
+    with pytest.raises(q3lib.InvalidArgument):
+        q3lib.gemm_bf16(16, 16, 16, None, 4, 1024, 100, q3lib.GEMM_STORE_F32)
+    with pytest.raises(q3lib.InvalidArgument):
+        q3lib.gemm_bf16(16, 16, 16, None, 4, 1000, 128, q3lib.GEMM_STORE_F32)
+    with pytest.raises(q3lib.InvalidArgument):
+        q3lib.gemm_bf16(16, 16, 16, None, 4, 1024, 128, q3lib.GEMM_SWIGLU)
+
+
+@pytest.fixture(scope="module")
+def prompt100():
+    return np.random.default_rng(11).integers(0, 151936, 100).astype(np.int32)
+
+
+@pytest.fixture(scope="module")
+def oracle_prompt100(full_weights, prompt100):
+    cpu = oracle.PortModel(full_weights, 512)
+    for pos, t in enumerate(prompt100[:-1]):
+        cpu.forward(int(t), pos)
+    h, lg = cpu.forward(int(prompt100[-1]), len(prompt100) - 1, layers=True)
+    kv = {(l, s): cpu.kv_row(l, s) for l in (0, 13, 27) for s in (0, 50, 99)}
+    return h, lg, kv
+
+
+def test_batched_prefill_matches_oracle(q3lib, full_weights, prompt100, oracle_prompt100):
+    ho, lo, kvo = oracle_prompt100
+    m = q3lib.Qwen3(full_weights, 512)
+    try:
+        assert m.prefill_path == m.PREFILL_BATCHED
+        h, lg, nxt = m.prefill_layers(prompt100, 0)
+        for l in range(h.shape[0]):
+            assert rel_l2(h[l], ho[l]) <= HIDDEN_REL_L2, (l, rel_l2(h[l], ho[l]))
+        assert np.abs(lg - lo).max() <= LOGITS_MAX_ABS, np.abs(lg - lo).max()
+        assert nxt == int(np.argmax(lg))
+        f = gen_weights.bf16_bits_to_f32
+        for (l, s), (ko, vo) in kvo.items():
+            k, v = m.kv_row(l, s)
+            assert rel_l2(f(k), f(ko)) <= HIDDEN_REL_L2, ("k", l, s)
+            assert rel_l2(f(v), f(vo)) <= HIDDEN_REL_L2, ("v", l, s)
+        # The q3_prefill entry point gives the same logits and token.
+        m.reset()
+        lg2, nxt2 = m.prefill(prompt100, 0)
+        assert nxt2 == nxt and np.abs(lg2 - lg).max() <= 1e-3
+    finally:
+        m.close()
+
+
+def test_decode_after_batched_prefill(q3lib, full_weights):
+    """Teacher-forced decode over the cache a batched prefill wrote."""
+    rng = np.random.default_rng(0)
+    seq = rng.integers(0, 151936, 80).astype(np.int32)
+    cpu = oracle.PortModel(full_weights, 512)
+    ref_am, ref_lg = [], []
+    for pos, t in enumerate(seq):
+        lg = cpu.forward(int(t), pos)
+        ref_am.append(int(np.argmax(lg)))
+        ref_lg.append(lg)
+    m = q3lib.Qwen3(full_weights, 512)
+    try:
+        for path in (m.PATH_FUSED, m.PATH_LAYERWISE):
+            m.decode_path = path
+            m.reset()
+            _, nxt = m.prefill(seq[:32], 0)
+            am, lg = m.decode_forced(seq[32:], 32, want_logits=True)
+            agree = float((am == np.array(ref_am[32:])).mean())
+            assert agree >= TOP1_AGREEMENT, (path, agree)
+            assert np.abs(lg - np.stack(ref_lg[32:])).max() <= LOGITS_MAX_ABS
+    finally:
+        m.close()
+
+
+def test_batched_and_tokenwise_prefill_agree_chunked(q3lib, full_weights):
+    """A prompt longer than one batched pass (4096 tokens): chunks see the earlier chunks' KV."""
+    rng = np.random.default_rng(7)
+    prompt = rng.integers(0, 151936, 4200).astype(np.int32)
+    res = {}
+    for path in ("batched", "tokenwise"):
+        m = q3lib.Qwen3(full_weights, 8192)
+        try:
+            m.prefill_path = m.PREFILL_BATCHED if path == "batched" else m.PREFILL_TOKENWISE
+            res[path] = m.prefill_layers(prompt, 0)
+            res[path + "_kv"] = [m.kv_row(l, s) for l in (0, 27) for s in (0, 4095, 4096, 4199)]
+        finally:
+            m.close()
+    hb, lb, nb = res["batched"]
+    ht, lt, nt = res["tokenwise"]
+    for l in range(hb.shape[0]):
+        assert rel_l2(hb[l], ht[l]) <= HIDDEN_REL_L2, (l, rel_l2(hb[l], ht[l]))
+    assert np.abs(lb - lt).max() <= LOGITS_MAX_ABS
+    f = gen_weights.bf16_bits_to_f32
+    for (kb, vb), (kt, vt) in zip(res["batched_kv"], res["tokenwise_kv"]):
+        assert rel_l2(f(kb), f(kt)) <= HIDDEN_REL_L2
+        assert rel_l2(f(vb), f(vt)) <= HIDDEN_REL_L2
+
+
+def test_prompt_past_context_falls_back(q3lib, full_weights):
+    """A prompt that wraps the ring buffer prefills token by token (sinks re-rotated)."""
+    rng = np.random.default_rng(9)
+    prompt = rng.integers(0, 151936, 80).astype(np.int32)
+    outs = []
+    for path in (1, 0):
+        m = q3lib.Qwen3(full_weights, 64)
+        try:
+            m.prefill_path = path
+            outs.append(m.prefill(prompt, 0))
+        finally:
+            m.close()
+    assert outs[0][1] == outs[1][1]
+    assert np.abs(outs[0][0] - outs[1][0]).max() <= LOGITS_MAX_ABS
+
+
+def test_generate_with_batched_prefill(q3lib, full_weights):
+    """Generate's tokens, each checked against the oracle's argmax given the same history."""
+    rng = np.random.default_rng(21)
+    prompt = rng.integers(0, 151936, 48).astype(np.int32)
+    m = q3lib.Qwen3(full_weights, 512)
+    try:
+        toks, st = m.generate(prompt, 24, stop_on_eos=False)
+    finally:
+        m.close()
+    assert st["prompt_tokens"] == 48 and st["generated_tokens"] == 24
+    cpu = oracle.PortModel(full_weights, 512)
+    seq = list(prompt) + list(toks)
+    agree = 0
+    for pos in range(len(seq) - 1):
+        lg = cpu.forward(int(seq[pos]), pos)
+        if pos >= len(prompt) - 1:
+            agree += int(np.argmax(lg)) == int(seq[pos + 1])
+    assert agree / len(toks) >= TOP1_AGREEMENT, agree
