@@ -340,6 +340,23 @@ void make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t 
     }
 }
 
+void make_tmap_kv_pages(CUtensorMap* map, const void* base, uint64_t n_kv, uint64_t pages) {
+    if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || n_kv == 0 || pages < 8) {
+        throw std::invalid_argument("tensor map: misaligned KV cache or too few pages");
+    }
+    const cuuint64_t dims[4] = {128, 16, n_kv, pages};
+    const cuuint64_t strides[3] = {256, 16 * 256, n_kv * 16 * 256};
+    const cuuint32_t box[4] = {64, 16, 1, 8};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUresult r = encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base),
+                                   dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string(static_cast<int>(r)));
+    }
+}
+
 int gemm_tile_n(int epi, int N) {
     if (epi == kEpiSwiGLU) return 256;
     return (N % 256 == 0 && N >= 4096) ? 256 : 128;

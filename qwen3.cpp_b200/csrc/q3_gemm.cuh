@@ -24,6 +24,11 @@ enum GemmEpilogue : int {
 void make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
                     uint32_t box_rows);
 
+// The paged KV cache of every layer, [pages][n_kv][16][128] bf16, as a 4-D TMA map
+// {128, 16, n_kv, pages} with a box of 64 x 16 x 1 x 8 (eight consecutive pages of one KV head, one
+// 64-column panel) and 128-byte swizzling.
+void make_tmap_kv_pages(CUtensorMap* map, const void* base, uint64_t n_kv, uint64_t pages);
+
 struct GemmArgs {
     int M = 0, N = 0, K = 0;  // N: output columns of the tile space (2 x hidden for SwiGLU)
     void* out = nullptr;      // fp32 or bf16 [M, ldo]

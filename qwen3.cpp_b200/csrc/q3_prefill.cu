@@ -457,6 +457,16 @@ void Prefill::run(const int32_t* ids_dev, int n, int pos0, const uint16_t* embed
             static_cast<uint64_t>(L) * e.n_pages() * c.n_kv_heads * kPageTokens;
         make_tmap_bf16(&kmap_, e.k_layer(0), kv_rows, HD, kPageTokens);
         make_tmap_bf16(&vmap_, e.v_layer(0), kv_rows, HD, kPageTokens);
+        // The 4-D page maps serve tiles of 8 pages inside one layer; with fewer pages per layer
+        // the kernel never takes that path and the 2-D maps stand in.
+        if (e.n_pages() >= 8) {
+            const uint64_t pages = static_cast<uint64_t>(L) * e.n_pages();
+            make_tmap_kv_pages(&kmap4_, e.k_layer(0), c.n_kv_heads, pages);
+            make_tmap_kv_pages(&vmap4_, e.v_layer(0), c.n_kv_heads, pages);
+        } else {
+            kmap4_ = kmap_;
+            vmap4_ = vmap_;
+        }
         kv_key_ = e.k_layer(0);
     }
     float* X = static_cast<float*>(x_.ptr);
@@ -519,7 +529,7 @@ void Prefill::run(const int32_t* ids_dev, int n, int pos0, const uint16_t* embed
                 ta.n_kv = c.n_kv_heads;
                 ta.n_pages = e.n_pages();
                 ta.layer = l;
-                launch_prefill_attention_tc(m_q, kmap_, vmap_, ta, s);
+                launch_prefill_attention_tc(m_q, kmap_, vmap_, kmap4_, vmap4_, ta, s);
             } else {
                 PrefillAttnArgs aa{};
                 aa.q = static_cast<const uint16_t*>(q_.ptr);

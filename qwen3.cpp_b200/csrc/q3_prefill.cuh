@@ -52,7 +52,8 @@ void launch_prefill_attention(const PrefillAttnArgs& a, cudaStream_t s);
 
 // The same attention on tcgen05 tensor cores (q3_prefill_attn.cu). q maps the bf16 q rows
 // [rows, n_heads*128] with 64 x 64 boxes; k and v map each whole paged cache (every layer) as
-// [n_layers * n_pages * n_kv * 16, 128] with 64 x 16 boxes.
+// [n_layers * n_pages * n_kv * 16, 128] with 64 x 16 boxes, k4 and v4 as 4-D page maps
+// (make_tmap_kv_pages over n_layers * n_pages pages).
 struct PrefillAttnTcArgs {
     const int32_t* page_table;
     uint16_t* out;             // [rows, n_heads*128] bf16
@@ -61,6 +62,7 @@ struct PrefillAttnTcArgs {
     int rows, pos0, n_kv, n_pages, layer;
 };
 void launch_prefill_attention_tc(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
+                                 const CUtensorMap& k4, const CUtensorMap& v4,
                                  const PrefillAttnTcArgs& a, cudaStream_t s);
 
 // Driver of a batched prefill over the layers of a Model.
@@ -102,7 +104,7 @@ private:
     };
     std::vector<LayerMaps> wmaps_;
     const uint16_t* wmaps_key_ = nullptr;
-    CUtensorMap kmap_, vmap_;
+    CUtensorMap kmap_, vmap_, kmap4_, vmap4_;
     const uint16_t* kv_key_ = nullptr;
 };
 
