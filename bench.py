@@ -42,6 +42,17 @@ LM_HEAD_BYTES = VOCAB * 1024 * 2
 # `ncu --set full` capture of the timed one-step launch of `bench.py --steps 1 --warmup 3`
 # (kv_len 17): 1.1959 GB read + 5.22 MB written. Re-captured whenever the kernel changes.
 FUSED_TRAFFIC_PER_STEP = 1_201_132_000
+# Long-prompt prefill: 2048 seeded prompt IDs (seed 2) at context 4096, batched on the tensor cores.
+PREFILL_LEN = 2048
+PREFILL_CTX = 4096
+PREFILL_RUNS = 5
+
+
+def prefill_flops(n: int) -> float:
+    """Algorithmic FLOPs of a prefill of n tokens: the layer contractions (2 * n * 440,401,920),
+    causal attention (4 * head_dim * n_heads * n_layers * n(n+1)/2) and the lm_head of the last
+    token (2 * 151936 * 1024)."""
+    return 2.0 * n * 440_401_920 + 4.0 * 128 * 16 * 28 * n * (n + 1) / 2 + 2.0 * VOCAB * 1024
 
 
 def peaks():
@@ -106,21 +117,27 @@ class Clocks:
 
 # ------------------------------------------------------------------ reference arm / CPU baseline
 
-def reference_decode(model_path: str, steps: int, warmup: int, threads: int):
+def reference_decode(model_path: str, steps: int, warmup: int, threads: int,
+                     with_prefill: bool = False):
     """The reference engine (oracle/_ref, built from the reference sources) on the host cores:
     prefill of the 16-token prompt, then greedy steps (Qwen3::Generate's loops with
-    `--benchmark` semantics), timed with its steady_clock marks. Returns (tok/s, decode s)."""
+    `--benchmark` semantics), timed with its steady_clock marks. Returns (tok/s, decode s), plus
+    its prefill tok/s when with_prefill."""
     import oracle
     m = oracle.RefModel(model_path, CTX)
     p = prompt_ids()
     if warmup:
         m.generate_ids(p, min(warmup, RUN_STEPS))
-    done, secs = 0, 0.0
+    done, secs, pre_secs, pre_tokens = 0, 0.0, 0.0, 0
     while done < steps:
         n = min(RUN_STEPS, steps - done)
-        _, _, ds = m.generate_ids(p, n)
+        _, ps, ds = m.generate_ids(p, n)
         secs += ds
+        pre_secs += ps
+        pre_tokens += len(p)
         done += n
+    if with_prefill:
+        return steps / secs, secs, pre_tokens / pre_secs
     return steps / secs, secs
 
 
@@ -238,8 +255,36 @@ def run_b200_arm(args):
     e2e_s = time.perf_counter() - t0
     e2e_tps = world * e2e_steps / e2e_s
 
-    pk = peaks()
     fused = model.decode_path == model.PATH_FUSED
+    model.close()
+
+    # Prefill of the long prompt through q3_prefill (ids in from host, next token out), timed with
+    # CUDA events on the model's stream; the max over ranks.
+    pm = q3b200.Qwen3(path, PREFILL_CTX, device=local)
+    pext = torch.cuda.ExternalStream(pm.stream)
+    pp = np.random.default_rng(2).integers(0, VOCAB, PREFILL_LEN).astype(np.int32)
+    for _ in range(2):
+        pm.prefill(pp, 0, want_logits=False)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    p_ms = 0.0
+    for _ in range(PREFILL_RUNS):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(pext)
+        pm.prefill(pp, 0, want_logits=False)
+        e1.record(pext)
+        torch.cuda.synchronize()
+        p_ms += e0.elapsed_time(e1)
+    p_ms /= PREFILL_RUNS
+    if world > 1:
+        t = torch.tensor([p_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        p_ms = float(t.item())
+    batched = pm.prefill_path == pm.PREFILL_BATCHED
+    pm.close()
+
+    pk = peaks()
     value = world * args.steps / (total_ms / 1e3)
     avg_kv = kv_pos_sum / args.steps
     step_bytes = WEIGHT_BYTES + KV_BYTES_PER_POS * avg_kv
@@ -258,12 +303,18 @@ def run_b200_arm(args):
         launches = args.steps * (7 * 28 + 3)
 
     cpu = None
+    cpu_prefill = None
     if rank == 0 and world == 1 and q3_ref_available():
         threads = os.cpu_count() or 1
-        tps, _ = reference_decode(str(path), RUN_STEPS, 0, threads)
+        tps, _, pre_tps = reference_decode(str(path), RUN_STEPS, 0, threads, with_prefill=True)
         cpu = {"value": round(tps, 3), "unit": UNIT, "cores": threads, "kind": "reference",
                "sample": f"{RUN_STEPS} greedy decode steps after a {PROMPT_LEN}-token prefill, "
                          f"ctx {CTX}, OMP_NUM_THREADS={threads}"}
+        cpu_prefill = {"value": round(pre_tps, 3), "unit": "tok/s", "cores": threads,
+                       "kind": "reference",
+                       "sample": f"its token-by-token prefill of the {PROMPT_LEN}-token prompt"}
+    p_tps = world * PREFILL_LEN / (p_ms / 1e3)
+    p_tflops = prefill_flops(PREFILL_LEN) / (p_ms / 1e3) / 1e12
 
     if rank == 0:
         line = {
@@ -294,9 +345,20 @@ def run_b200_arm(args):
                     "api": "q3_forward_token per step + host argmax"},
             "cpu_baseline": cpu,
             "clocks": clk,
+            "prefill": {
+                "metric": "prefill tok/s (2048-token prompt, ctx 4096, Qwen3-0.6B bf16)",
+                "value": round(p_tps, 1), "unit": "tok/s", "ms_per_prefill": round(p_ms, 4),
+                "runs": PREFILL_RUNS, "path": "batched tcgen05" if batched else "token by token",
+                "api": "q3_prefill (ids in from host, next token out)",
+                "roofline": {"bound": "tensor", "achieved": round(p_tflops, 1),
+                             "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                             "frac": round(p_tflops / pk["bf16_tflops"], 4),
+                             "flops_per_prefill": prefill_flops(PREFILL_LEN),
+                             "peak_source": pk["source"] + " (burst bf16 GEMM)"},
+                "cpu_baseline": cpu_prefill,
+            },
         }
         print(json.dumps(line), flush=True)
-    model.close()
     if world > 1:
         dist.destroy_process_group()
 

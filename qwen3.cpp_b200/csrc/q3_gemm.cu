@@ -7,9 +7,11 @@
 //               one of two TMEM accumulators; tcgen05.commit frees the stage when the MMAs that
 //               read it are done, and signals the epilogue after the tile's last k-block.
 //   warps 2-5   epilogue: warp w reads TMEM lanes 32*(w%4).. (one output row per thread), 32
-//               fp32 columns per tcgen05.ld, applies the fused op and stores to global memory,
-//               then hands the accumulator back. Two accumulators let the epilogue of one tile
-//               overlap the MMAs of the next.
+//               fp32 columns per tcgen05.ld, applies the fused op, writes its 32-row block into
+//               a double-buffered 128-byte-swizzled shared-memory tile and one lane hands it to
+//               a TMA store (or a TMA reduce-add for the residual stream), so the global writes
+//               run asynchronously as full lines. Two TMEM accumulators let the epilogue of one
+//               tile overlap the MMAs of the next.
 // Every mbarrier wait is bounded; a wait that gives up sets args.err and the CTA drains its
 // outstanding TMA loads and MMAs before freeing TMEM and returning.
 #include <cuda.h>
@@ -42,26 +44,35 @@ struct GemmCfg {
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+    static constexpr int STG_BYTES = 4 * 2 * 4096;  // per epilogue warp: 2 x (32 rows x 128 B)
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STG_BYTES + 1024 + 256;
 };
 
-__device__ __forceinline__ void store_f32x32(float* dst, const float (&v)[32]) {
-    float4* d = reinterpret_cast<float4*>(dst);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) d[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+// TMA store / reduce-add of a shared-memory box to global memory (asynchronous, bulk group).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(smem_u32(src)), "r"(x), "r"(y)
+        : "memory");
 }
-
-__device__ __forceinline__ void add_f32x32(float* dst, const float (&v)[32]) {
-    float4* d = reinterpret_cast<float4*>(dst);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        float4 o = d[i];
-        o.x += v[4 * i];
-        o.y += v[4 * i + 1];
-        o.z += v[4 * i + 2];
-        o.w += v[4 * i + 3];
-        d[i] = o;
-    }
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int x,
+                                                  int y) {
+    asm volatile(
+        "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], "
+        "[%1];" ::"l"(reinterpret_cast<uint64_t>(map)),
+        "r"(smem_u32(src)), "r"(x), "r"(y)
+        : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until at most N committed bulk groups still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
@@ -69,14 +80,6 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-__device__ __forceinline__ void store_bf16x32(uint16_t* dst, const float (&v)[32]) {
-    uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        d[i] = make_uint4(pack_bf16(v[8 * i], v[8 * i + 1]), pack_bf16(v[8 * i + 2], v[8 * i + 3]),
-                          pack_bf16(v[8 * i + 4], v[8 * i + 5]), pack_bf16(v[8 * i + 6], v[8 * i + 7]));
-    }
-}
 
 __device__ __forceinline__ void fail(volatile int* abort, unsigned* err, unsigned code) {
     *abort = 1;
@@ -86,12 +89,14 @@ __device__ __forceinline__ void fail(volatile int* abort, unsigned* err, unsigne
 template <int BN, int EPI>
 __global__ void __launch_bounds__(NTHREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
-                const __grid_constant__ CUtensorMap tb2, const GemmArgs args) {
+                const __grid_constant__ CUtensorMap tb2, const __grid_constant__ CUtensorMap tout,
+                const GemmArgs args) {
     using C = GemmCfg<BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+    uint8_t* stg_all = smem + C::STAGES * C::STAGE_BYTES;  // epilogue staging, 1024-aligned
+    uint64_t* full = reinterpret_cast<uint64_t*>(stg_all + C::STG_BYTES);
     uint64_t* empty = full + C::STAGES;
     uint64_t* tfull = empty + C::STAGES;
     uint64_t* tempty = tfull + 2;
@@ -122,6 +127,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         tma_prefetch_map(&ta);
         tma_prefetch_map(&tb);
         if (EPI == kEpiSwiGLU) tma_prefetch_map(&tb2);
+        tma_prefetch_map(&tout);
         tmem_alloc(tmem_slot, C::TMEM_COLS);
     }
     __syncthreads();
@@ -228,6 +234,30 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     } else {
         // -------------------------------------------------------------------- epilogue
         const int lg = warp & 3;
+        uint8_t* stg = stg_all + lg * 8192;
+        int nbuf = 0;  // staging buffers used so far (alternating)
+        // Row `lane` of the warp's 32-row box as 128 bytes, 16-byte chunks XOR-swizzled by the
+        // row (the TMA 128-byte swizzle pattern: 8 rows hit 8 different bank groups).
+        auto stage_store = [&](const uint4 (&row)[8], int x, int y) {
+            uint8_t* buf = stg + (nbuf & 1) * 4096;
+            if (lane == 0) bulk_wait_read<1>();  // the store that used this buffer has read it
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                *reinterpret_cast<uint4*>(buf + lane * 128 + ((i ^ (lane & 7)) << 4)) = row[i];
+            }
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                if (EPI == kEpiAddF32) {
+                    tma_reduce_add_2d(&tout, buf, x, y);
+                } else {
+                    tma_store_2d(&tout, buf, x, y);
+                }
+                bulk_commit();
+            }
+            ++nbuf;
+        };
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
@@ -239,31 +269,58 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             tc_fence_after();
             const uint32_t tb_addr = tmem + (static_cast<uint32_t>(lg * 32) << 16) +
                                      static_cast<uint32_t>(acc * BN);
-            const int r = tm * BM + lg * 32 + lane;
-            const bool row_ok = r < args.M;
+            const int y = tm * BM + lg * 32;  // rows past M are clipped by the TMA store
             if (EPI == kEpiSwiGLU) {
-                uint16_t* out = static_cast<uint16_t*>(args.out) + static_cast<size_t>(r) * args.ldo +
-                                tn * (BN / 2);
+                // 64 hidden columns per box: h = silu(w1 . x) * (w3 . x) as bf16.
 #pragma unroll 1
-                for (int c = 0; c < BN / 2; c += 32) {
-                    float g[32], u[32];
-                    tmem_ld32(tb_addr + c, g);
-                    tmem_ld32(tb_addr + BN / 2 + c, u);
+                for (int c = 0; c < BN / 2; c += 64) {
+                    uint4 row[8];
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) g[i] = g[i] / (1.0f + expf(-g[i])) * u[i];
-                    if (row_ok) store_bf16x32(out + c, g);
+                    for (int hlf = 0; hlf < 2; ++hlf) {
+                        float g[32], u[32];
+                        tmem_ld32(tb_addr + c + hlf * 32, g);
+                        tmem_ld32(tb_addr + BN / 2 + c + hlf * 32, u);
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) g[i] = g[i] / (1.0f + expf(-g[i])) * u[i];
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            row[hlf * 4 + i] = make_uint4(
+                                pack_bf16(g[8 * i], g[8 * i + 1]), pack_bf16(g[8 * i + 2], g[8 * i + 3]),
+                                pack_bf16(g[8 * i + 4], g[8 * i + 5]), pack_bf16(g[8 * i + 6], g[8 * i + 7]));
+                        }
+                    }
+                    stage_store(row, tn * (BN / 2) + c, y);
+                }
+            } else if (EPI == kEpiStoreBF16) {
+#pragma unroll 1
+                for (int c = 0; c < BN; c += 64) {
+                    uint4 row[8];
+#pragma unroll
+                    for (int hlf = 0; hlf < 2; ++hlf) {
+                        float v[32];
+                        tmem_ld32(tb_addr + c + hlf * 32, v);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            row[hlf * 4 + i] = make_uint4(
+                                pack_bf16(v[8 * i], v[8 * i + 1]), pack_bf16(v[8 * i + 2], v[8 * i + 3]),
+                                pack_bf16(v[8 * i + 4], v[8 * i + 5]), pack_bf16(v[8 * i + 6], v[8 * i + 7]));
+                        }
+                    }
+                    stage_store(row, tn * BN + c, y);
                 }
             } else {
+                // fp32: 32 columns per box (stored, or added into the residual stream in L2).
 #pragma unroll 1
                 for (int c = 0; c < BN; c += 32) {
                     float v[32];
                     tmem_ld32(tb_addr + c, v);
-                    if (row_ok) {
-                        const size_t off = static_cast<size_t>(r) * args.ldo + tn * BN + c;
-                        if (EPI == kEpiStoreF32) store_f32x32(static_cast<float*>(args.out) + off, v);
-                        if (EPI == kEpiAddF32) add_f32x32(static_cast<float*>(args.out) + off, v);
-                        if (EPI == kEpiStoreBF16) store_bf16x32(static_cast<uint16_t*>(args.out) + off, v);
+                    uint4 row[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        row[i] = make_uint4(__float_as_uint(v[4 * i]), __float_as_uint(v[4 * i + 1]),
+                                            __float_as_uint(v[4 * i + 2]), __float_as_uint(v[4 * i + 3]));
                     }
+                    stage_store(row, tn * BN + c, y);
                 }
             }
             tc_fence_before();
@@ -274,6 +331,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 acc_phase ^= 1;
             }
         }
+        // Every store has completed (global writes done) before the CTA exits.
+        if (lane == 0) bulk_wait_all();
+        __syncwarp();
     }
     __syncthreads();
     if (warp == 0) {
@@ -300,7 +360,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 template <int BN, int EPI>
 cudaError_t launch_t(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& b2,
-                     const GemmArgs& args, int num_sms, cudaStream_t stream) {
+                     const CUtensorMap& out, const GemmArgs& args, int num_sms,
+                     cudaStream_t stream) {
     using C = GemmCfg<BN>;
     auto kern = gemm_kernel<BN, EPI>;
     static thread_local int configured_device = -1;
@@ -315,7 +376,7 @@ cudaError_t launch_t(const CUtensorMap& a, const CUtensorMap& b, const CUtensorM
     const int tiles = ((args.M + BM - 1) / BM) * (args.N / BN);
     const int grid = tiles < num_sms ? tiles : num_sms;
     if (grid <= 0) return cudaSuccess;
-    kern<<<grid, NTHREADS, C::SMEM_BYTES, stream>>>(a, b, b2, args);
+    kern<<<grid, NTHREADS, C::SMEM_BYTES, stream>>>(a, b, b2, out, args);
     return cudaGetLastError();
 }
 
@@ -335,6 +396,24 @@ void make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t 
                                    dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string(static_cast<int>(r)));
+    }
+}
+
+void make_tmap_out(CUtensorMap* map, void* base, uint64_t rows, uint64_t cols, bool bf16) {
+    const uint64_t esz = bf16 ? 2 : 4;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (cols * esz) % 128 != 0 || rows == 0) {
+        throw std::invalid_argument("tensor map: misaligned output or width not a multiple of 128 B");
+    }
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * esz};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / esz), 32};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode_fn()(
+        map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims,
+        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string(static_cast<int>(r)));
     }
@@ -363,7 +442,8 @@ int gemm_tile_n(int epi, int N) {
 }
 
 cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap* b2,
-                        const GemmArgs& args, int epi, int num_sms, cudaStream_t stream) {
+                        const CUtensorMap& out, const GemmArgs& args, int epi, int num_sms,
+                        cudaStream_t stream) {
     if (args.K % BK != 0 || args.K <= 0 || args.M <= 0) return cudaErrorInvalidValue;
     const int bn = gemm_tile_n(epi, args.N);
     if (args.N % bn != 0) return cudaErrorInvalidValue;
@@ -371,16 +451,16 @@ cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtens
     const CUtensorMap& bb = b2 ? *b2 : b;
     switch (epi) {
         case kEpiStoreF32:
-            return bn == 256 ? launch_t<256, kEpiStoreF32>(a, b, bb, args, num_sms, stream)
-                             : launch_t<128, kEpiStoreF32>(a, b, bb, args, num_sms, stream);
+            return bn == 256 ? launch_t<256, kEpiStoreF32>(a, b, bb, out, args, num_sms, stream)
+                             : launch_t<128, kEpiStoreF32>(a, b, bb, out, args, num_sms, stream);
         case kEpiAddF32:
-            return bn == 256 ? launch_t<256, kEpiAddF32>(a, b, bb, args, num_sms, stream)
-                             : launch_t<128, kEpiAddF32>(a, b, bb, args, num_sms, stream);
+            return bn == 256 ? launch_t<256, kEpiAddF32>(a, b, bb, out, args, num_sms, stream)
+                             : launch_t<128, kEpiAddF32>(a, b, bb, out, args, num_sms, stream);
         case kEpiStoreBF16:
-            return bn == 256 ? launch_t<256, kEpiStoreBF16>(a, b, bb, args, num_sms, stream)
-                             : launch_t<128, kEpiStoreBF16>(a, b, bb, args, num_sms, stream);
+            return bn == 256 ? launch_t<256, kEpiStoreBF16>(a, b, bb, out, args, num_sms, stream)
+                             : launch_t<128, kEpiStoreBF16>(a, b, bb, out, args, num_sms, stream);
         case kEpiSwiGLU:
-            return launch_t<256, kEpiSwiGLU>(a, b, bb, args, num_sms, stream);
+            return launch_t<256, kEpiSwiGLU>(a, b, bb, out, args, num_sms, stream);
     }
     return cudaErrorInvalidValue;
 }
@@ -414,6 +494,8 @@ extern "C" q3_status q3_gemm_bf16(void* out, const uint16_t* a, const uint16_t* 
         make_tmap_bf16(&ma, a, M, K, 128);
         make_tmap_bf16(&mb, w, N, K, swiglu ? 128 : bn);
         if (swiglu) make_tmap_bf16(&mb3, w3, N, K, 128);
+        CUtensorMap mo;
+        make_tmap_out(&mo, out, M, N, swiglu || epilogue == Q3_GEMM_STORE_BF16);
         unsigned* err = nullptr;
         Q3_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&err), sizeof(unsigned), s));
         Q3_CUDA(cudaMemsetAsync(err, 0, sizeof(unsigned), s));
@@ -421,10 +503,8 @@ extern "C" q3_status q3_gemm_bf16(void* out, const uint16_t* a, const uint16_t* 
         g.M = M;
         g.N = tile_space;
         g.K = K;
-        g.out = out;
-        g.ldo = N;
         g.err = err;
-        const cudaError_t le = launch_gemm(ma, mb, swiglu ? &mb3 : nullptr, g, epilogue, sms, s);
+        const cudaError_t le = launch_gemm(ma, mb, swiglu ? &mb3 : nullptr, mo, g, epilogue, sms, s);
         unsigned herr = 0;
         const cudaError_t ce = cudaMemcpyAsync(&herr, err, sizeof(unsigned),
                                                cudaMemcpyDeviceToHost, s);

@@ -29,10 +29,13 @@ void make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t 
 // 64-column panel) and 128-byte swizzling.
 void make_tmap_kv_pages(CUtensorMap* map, const void* base, uint64_t n_kv, uint64_t pages);
 
+// The output [rows, cols] of a contraction (fp32, or bf16 when bf16) as a TMA map for the
+// epilogue's stores: boxes of 128 bytes x 32 rows with 128-byte swizzling. cols * element size
+// must be a multiple of 128 bytes.
+void make_tmap_out(CUtensorMap* map, void* base, uint64_t rows, uint64_t cols, bool bf16);
+
 struct GemmArgs {
     int M = 0, N = 0, K = 0;  // N: output columns of the tile space (2 x hidden for SwiGLU)
-    void* out = nullptr;      // fp32 or bf16 [M, ldo]
-    int ldo = 0;              // elements between output rows
     unsigned* err = nullptr;  // set non-zero when a bounded wait gives up
     long long budget = 4000000000LL;  // cycles per wait
 };
@@ -40,10 +43,12 @@ struct GemmArgs {
 // Tile N width used for an epilogue and output width (128 or 256).
 int gemm_tile_n(int epi, int N);
 // Enqueues the contraction. `a` maps A [M, K] with 128-row boxes; `b` maps B [N, K] with
-// box_rows = gemm_tile_n(...) (SwiGLU: `b` = w1 and `b2` = w3, each [N/2, K] with 128-row boxes).
-// K must be a multiple of 64, N a multiple of the tile width. Grid: one persistent CTA per SM at
-// most. Returns cudaSuccess or the launch error.
+// box_rows = gemm_tile_n(...) (SwiGLU: `b` = w1 and `b2` = w3, each [N/2, K] with 128-row boxes);
+// `out` (make_tmap_out) maps the output: fp32 [M, N] (store or residual add) or bf16 ([M, N/2]
+// for SwiGLU, [M, N] for kEpiStoreBF16). K must be a multiple of 64, N a multiple of the tile
+// width. Grid: one persistent CTA per SM at most. Returns cudaSuccess or the launch error.
 cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap* b2,
-                        const GemmArgs& args, int epi, int num_sms, cudaStream_t stream);
+                        const CUtensorMap& out, const GemmArgs& args, int epi, int num_sms,
+                        cudaStream_t stream);
 
 }  // namespace q3

@@ -482,6 +482,10 @@ void Prefill::run(const int32_t* ids_dev, int n, int pos0, const uint16_t* embed
         make_tmap_bf16(&m_xn, xn_.ptr, S, c.dim, 128);
         make_tmap_bf16(&m_o, o_.ptr, S, qd, 128);
         make_tmap_bf16(&m_h, h_.ptr, S, c.hidden_dim, 128);
+        CUtensorMap o_qkv, o_x, o_h;  // contraction outputs
+        make_tmap_out(&o_qkv, qkv_.ptr, S, qkv, false);
+        make_tmap_out(&o_x, X, S, c.dim, false);
+        make_tmap_out(&o_h, h_.ptr, S, c.hidden_dim, true);
         auto tap = [&](int slot) {
             if (taps && last) {
                 Q3_CUDA(cudaMemcpyAsync(taps + static_cast<size_t>(slot) * c.dim,
@@ -501,9 +505,7 @@ void Prefill::run(const int32_t* ids_dev, int n, int pos0, const uint16_t* embed
             // [wq; wk; wv] . xn -> fp32 q|k|v rows (src/inference.cpp:795-798).
             g.N = qkv;
             g.K = c.dim;
-            g.out = qkv_.ptr;
-            g.ldo = qkv;
-            Q3_CUDA(launch_gemm(m_xn, wm.wqkv, nullptr, g, kEpiStoreF32, num_sms_, s));
+            Q3_CUDA(launch_gemm(m_xn, wm.wqkv, nullptr, o_qkv, g, kEpiStoreF32, num_sms_, s));
             PrefillQkvArgs qa{};
             qa.qkv = static_cast<const float*>(qkv_.ptr);
             qa.q_norm = w.q_norm;
@@ -546,22 +548,16 @@ void Prefill::run(const int32_t* ids_dev, int n, int pos0, const uint16_t* embed
             // x += wo . attn (:846-849).
             g.N = c.dim;
             g.K = qd;
-            g.out = X;
-            g.ldo = c.dim;
-            Q3_CUDA(launch_gemm(m_o, wm.wo, nullptr, g, kEpiAddF32, num_sms_, s));
+            Q3_CUDA(launch_gemm(m_o, wm.wo, nullptr, o_x, g, kEpiAddF32, num_sms_, s));
             launch_rmsnorm_rows_bf16(nullptr, nullptr, X, w.mlp_norm, c.norm_eps, Xn, S, c.dim, s);
             // h = silu(w1 . xn) * (w3 . xn) (:851, :1005-1011).
             g.N = 2 * c.hidden_dim;
             g.K = c.dim;
-            g.out = h_.ptr;
-            g.ldo = c.hidden_dim;
-            Q3_CUDA(launch_gemm(m_xn, wm.w1, &wm.w3, g, kEpiSwiGLU, num_sms_, s));
+            Q3_CUDA(launch_gemm(m_xn, wm.w1, &wm.w3, o_h, g, kEpiSwiGLU, num_sms_, s));
             // x += w2 . h (:1013, :863-865).
             g.N = c.dim;
             g.K = c.hidden_dim;
-            g.out = X;
-            g.ldo = c.dim;
-            Q3_CUDA(launch_gemm(m_h, wm.w2, nullptr, g, kEpiAddF32, num_sms_, s));
+            Q3_CUDA(launch_gemm(m_h, wm.w2, nullptr, o_x, g, kEpiAddF32, num_sms_, s));
             if (l + 1 < L) {
                 launch_rmsnorm_rows_bf16(nullptr, nullptr, X, layers[l + 1].attn_norm, c.norm_eps,
                                          Xn, S, c.dim, s);
