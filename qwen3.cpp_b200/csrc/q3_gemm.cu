@@ -107,8 +107,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int num_m = (args.M + BM - 1) / BM;
     const int num_n = args.N / BN;
-    const int tiles = num_m * num_n;
-    const int kblocks = args.K / BK;
+    // Residual-add contractions may split K: every slice reduce-adds its partial sum.
+    const int ksplit = EPI == kEpiAddF32 ? args.ksplit : 1;
+    const int tiles = num_m * num_n * ksplit;
+    const int kblocks = args.K / BK / ksplit;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) {
@@ -141,8 +143,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             uint32_t phase = 0;
             uint32_t issued_mask = 0, issued_parity = 0;
             for (int t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
-                const int tm = t % num_m, tn = t / num_m;
-                for (int kb = 0; kb < kblocks; ++kb) {
+                const int tmn = t % (num_m * num_n), ks = t / (num_m * num_n);
+                const int tm = tmn % num_m, tn = tmn / num_m;
+                for (int kbi = 0; kbi < kblocks; ++kbi) {
+                    const int kb = ks * kblocks + kbi;
                     if (!mbar_wait(&empty[stage], phase ^ 1, args.budget, abort)) {
                         fail(abort, args.err, 1);
                         break;
@@ -194,7 +198,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
                 tc_fence_after();
                 const uint32_t d = tmem + static_cast<uint32_t>(acc * BN);
-                for (int kb = 0; kb < kblocks; ++kb) {
+                for (int kbi = 0; kbi < kblocks; ++kbi) {
                     if (!mbar_wait(&full[stage], phase, args.budget, abort)) {
                         fail(abort, args.err, 4);
                         ok = false;
@@ -206,7 +210,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     const uint64_t bdesc = desc_k_sw128(sa + C::A_BYTES);
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k) {
-                        mma_bf16(d, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+                        mma_bf16(d, adesc + 2 * k, bdesc + 2 * k, idesc, (kbi | k) != 0);
                     }
                     mma_commit(&empty[stage]);
                     if (++stage == C::STAGES) {
@@ -261,7 +265,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
-            const int tm = t % num_m, tn = t / num_m;
+            const int tmn = t % (num_m * num_n);
+            const int tm = tmn % num_m, tn = tmn / num_m;
             if (!mbar_wait(&tfull[acc], acc_phase, args.budget, abort)) {
                 fail(abort, args.err, 6);
                 break;
@@ -281,7 +286,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         tmem_ld32(tb_addr + c + hlf * 32, g);
                         tmem_ld32(tb_addr + BN / 2 + c + hlf * 32, u);
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) g[i] = g[i] / (1.0f + expf(-g[i])) * u[i];
+                        for (int i = 0; i < 32; ++i) {
+                            // silu(g) * u (src/inference.cpp:948-950, :1009-1011) with the fast
+                            // exponential and division: the result is rounded to bf16.
+                            g[i] = __fdividef(g[i], 1.0f + __expf(-g[i])) * u[i];
+                        }
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
                             row[hlf * 4 + i] = make_uint4(
@@ -373,10 +382,21 @@ cudaError_t launch_t(const CUtensorMap& a, const CUtensorMap& b, const CUtensorM
         if (e != cudaSuccess) return e;
         configured_device = dev;
     }
-    const int tiles = ((args.M + BM - 1) / BM) * (args.N / BN);
+    GemmArgs g = args;
+    const int mn_tiles = ((args.M + BM - 1) / BM) * (args.N / BN);
+    g.ksplit = 1;
+    if (EPI == kEpiAddF32) {
+        // Split K while the tiles fill less than half the SMs (slices reduce-add in L2).
+        const int kb = args.K / BK;
+        while (g.ksplit < 4 && mn_tiles * g.ksplit * 2 <= num_sms && kb % (g.ksplit * 2) == 0 &&
+               kb / (g.ksplit * 2) >= 8) {
+            g.ksplit *= 2;
+        }
+    }
+    const int tiles = mn_tiles * g.ksplit;
     const int grid = tiles < num_sms ? tiles : num_sms;
     if (grid <= 0) return cudaSuccess;
-    kern<<<grid, NTHREADS, C::SMEM_BYTES, stream>>>(a, b, b2, out, args);
+    kern<<<grid, NTHREADS, C::SMEM_BYTES, stream>>>(a, b, b2, out, g);
     return cudaGetLastError();
 }
 
@@ -438,7 +458,7 @@ void make_tmap_kv_pages(CUtensorMap* map, const void* base, uint64_t n_kv, uint6
 
 int gemm_tile_n(int epi, int N) {
     if (epi == kEpiSwiGLU) return 256;
-    return (N % 256 == 0 && N >= 4096) ? 256 : 128;
+    return N % 256 == 0 ? 256 : 128;
 }
 
 cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap* b2,

@@ -38,6 +38,7 @@ struct GemmArgs {
     int M = 0, N = 0, K = 0;  // N: output columns of the tile space (2 x hidden for SwiGLU)
     unsigned* err = nullptr;  // set non-zero when a bounded wait gives up
     long long budget = 4000000000LL;  // cycles per wait
+    int ksplit = 1;           // K slices (residual add only; chosen by launch_gemm)
 };
 
 // Tile N width used for an epilogue and output width (128 or 256).

@@ -27,22 +27,27 @@ __device__ __forceinline__ uint32_t pack2_bf16(float a, float b) {
 
 // ------------------------------------------------------------------ row RmsNorm -> bf16
 
-constexpr int kNormThreads = 256;
+constexpr int kNormWarps = 8;  // rows per block, one warp per row
 
-__global__ void __launch_bounds__(kNormThreads)
+__global__ void __launch_bounds__(kNormWarps * 32)
     rmsnorm_rows_kernel(const int32_t* __restrict__ ids, const uint16_t* __restrict__ embed,
                         float* __restrict__ x, const uint16_t* __restrict__ w, float eps,
-                        uint16_t* __restrict__ out, int dim) {
-    __shared__ float red[kNormThreads / 32];
-    const size_t row = blockIdx.x;
-    float* xr = x + row * dim;
+                        uint16_t* __restrict__ out, int rows, int dim) {
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * kNormWarps + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    float* xr = x + static_cast<size_t>(row) * dim;
     if (ids) {
         const uint16_t* er = embed + static_cast<size_t>(ids[row]) * dim;
-        for (int i = threadIdx.x; i < dim; i += kNormThreads) xr[i] = bf16_to_f32(er[i]);
-        __syncthreads();
+        for (int i = lane * 8; i < dim; i += 256) {
+            const uint4 e = *reinterpret_cast<const uint4*>(er + i);
+            *reinterpret_cast<float4*>(xr + i) = make_float4(bf16_lo(e.x), bf16_hi(e.x), bf16_lo(e.y), bf16_hi(e.y));
+            *reinterpret_cast<float4*>(xr + i + 4) = make_float4(bf16_lo(e.z), bf16_hi(e.z), bf16_lo(e.w), bf16_hi(e.w));
+        }
+        __syncwarp();
     }
     float ss = 0.0f;
-    for (int i = threadIdx.x * 4; i < dim; i += kNormThreads * 4) {
+    for (int i = lane * 4; i < dim; i += 128) {
         const float4 v = *reinterpret_cast<const float4*>(xr + i);
         ss = fmaf(v.x, v.x, ss);
         ss = fmaf(v.y, v.y, ss);
@@ -50,20 +55,15 @@ __global__ void __launch_bounds__(kNormThreads)
         ss = fmaf(v.w, v.w, ss);
     }
     ss = warp_sum(ss);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-    __syncthreads();
-    float tot = 0.0f;
-#pragma unroll
-    for (int i = 0; i < kNormThreads / 32; ++i) tot += red[i];
     // RmsNorm (src/inference.cpp:905-921): (x * (1 / rms)) * w, rms = sqrtf(ss / n + eps).
-    const float inv = 1.0f / sqrtf(tot / static_cast<float>(dim) + eps);
-    uint16_t* orow = out + row * dim;
-    for (int i = threadIdx.x * 4; i < dim; i += kNormThreads * 4) {
+    const float inv = 1.0f / sqrtf(ss / static_cast<float>(dim) + eps);
+    uint16_t* orow = out + static_cast<size_t>(row) * dim;
+    for (int i = lane * 4; i < dim; i += 128) {
         const float4 v = *reinterpret_cast<const float4*>(xr + i);
         const uint2 wb = *reinterpret_cast<const uint2*>(w + i);
-        const uint2 o = make_uint2(pack2_bf16((v.x * inv) * bf16_lo(wb.x), (v.y * inv) * bf16_hi(wb.x)),
-                                   pack2_bf16((v.z * inv) * bf16_lo(wb.y), (v.w * inv) * bf16_hi(wb.y)));
-        *reinterpret_cast<uint2*>(orow + i) = o;
+        *reinterpret_cast<uint2*>(orow + i) =
+            make_uint2(pack2_bf16((v.x * inv) * bf16_lo(wb.x), (v.y * inv) * bf16_hi(wb.x)),
+                       pack2_bf16((v.z * inv) * bf16_lo(wb.y), (v.w * inv) * bf16_hi(wb.y)));
     }
 }
 
@@ -357,7 +357,9 @@ void launch_rmsnorm_rows_bf16(const int32_t* ids, const uint16_t* embed, float* 
                               const uint16_t* w, float eps, uint16_t* out, int rows, int dim,
                               cudaStream_t s) {
     if (rows <= 0) return;
-    rmsnorm_rows_kernel<<<rows, kNormThreads, 0, s>>>(ids, embed, x, w, eps, out, dim);
+    if (dim % 256 != 0) throw std::invalid_argument("row RmsNorm needs a width that is a multiple of 256");
+    rmsnorm_rows_kernel<<<(rows + kNormWarps - 1) / kNormWarps, kNormWarps * 32, 0, s>>>(
+        ids, embed, x, w, eps, out, rows, dim);
     Q3_CUDA(cudaGetLastError());
 }
 

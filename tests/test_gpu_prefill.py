@@ -128,10 +128,11 @@ def test_batched_prefill_matches_oracle(q3lib, full_weights, prompt100, oracle_p
             k, v = m.kv_row(l, s)
             assert rel_l2(f(k), f(ko)) <= HIDDEN_REL_L2, ("k", l, s)
             assert rel_l2(f(v), f(vo)) <= HIDDEN_REL_L2, ("v", l, s)
-        # The q3_prefill entry point gives the same logits and token.
+        # The q3_prefill entry point gives the same token and logits (to the run-to-run variation
+        # of the split-K fp32 sums, which the bf16 activations then round either way).
         m.reset()
         lg2, nxt2 = m.prefill(prompt100, 0)
-        assert nxt2 == nxt and np.abs(lg2 - lg).max() <= 1e-3
+        assert nxt2 == nxt and np.abs(lg2 - lg).max() <= LOGITS_MAX_ABS
     finally:
         m.close()
 
