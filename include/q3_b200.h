@@ -176,6 +176,35 @@ q3_status q3_model_fused_timeout_selftest(q3_model* model, int* timed_out);
 q3_status q3_model_fused_profile(q3_model* model, int32_t token, int pos, uint64_t* stamps_host,
                                  size_t capacity, int* n_phases, int* grid);
 
+/* ------------------------------------------------------------------ batched decode
+ * Independent sequences decoded together on one GPU (the data-parallel serving configuration).
+ * The reference runs one sequence at a time (Qwen3::Generate, src/inference.cpp:639-700); a
+ * batch produces, for every sequence, the tokens that Generate's greedy loop would (prefill of
+ * the prompt, then one greedy token per step, no EOS stop), with every decode step of all
+ * sequences computed at once: the weights are read once per step for all of them. The batch owns
+ * a paged KV pool (16-token pages, a contiguous page range per sequence) sized for max_seqs
+ * sequences of up to max_tokens positions (prompt + generated); positions never wrap. The model
+ * handle must outlive the batch; the model's own single-sequence state is not touched. */
+typedef struct q3_batch q3_batch;
+q3_status q3_batch_create(q3_model* model, int max_seqs, int max_tokens, q3_batch** out);
+void q3_batch_free(q3_batch* batch);
+/* Adds a sequence and prefills its prompt (batched, on the tensor cores): *slot (nullable)
+ * receives its index, *next_token_host (nullable) the greedy token after the prompt,
+ * last_logits_host (nullable, vocab_size floats) the prompt's last logits. */
+q3_status q3_batch_add(q3_batch* batch, const int32_t* ids_host, int n, int* slot,
+                       int32_t* next_token_host, float* last_logits_host);
+q3_status q3_batch_size(const q3_batch* batch, int* n_seqs);
+/* n_steps greedy decode steps for every sequence; tokens_host[n_steps][n_seqs] (nullable)
+ * receives the generated tokens (step-major). */
+q3_status q3_batch_decode(q3_batch* batch, int n_steps, int32_t* tokens_host);
+/* Teacher-forced steps: feeds tokens_host[step][n_seqs]; argmax_host[n_steps][n_seqs] receives
+ * each step's greedy argmax, logits_host[n_steps][n_seqs][vocab_size] (nullable) all logits. */
+q3_status q3_batch_decode_forced(q3_batch* batch, const int32_t* tokens_host, int n_steps,
+                                 int32_t* argmax_host, float* logits_host);
+/* Row `pos` of sequence `slot`'s layer-`layer` K/V (n_kv_heads*head_dim values each). */
+q3_status q3_batch_kv_row(q3_batch* batch, int slot, int layer, int pos, uint16_t* k_host,
+                          uint16_t* v_host);
+
 /* ------------------------------------------------------------------ one block (class Block) */
 
 /* Block(config, weights) (src/inference.cpp:720-730) with BlockWeights

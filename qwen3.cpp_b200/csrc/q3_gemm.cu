@@ -37,10 +37,14 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int NTHREADS = 192;
 
-template <int BN>
+// SPLIT: the A operand comes as two bf16 parts (hi and lo, a = hi + lo) that both multiply the same
+// B tile into the accumulator - fp32-like activations at twice the MMA work, for the
+// weight-streaming small-M contractions of batched decode.
+template <int BN, bool SPLIT = false>
 struct GemmCfg {
-    static constexpr int STAGES = BN == 256 ? 4 : 6;
-    static constexpr int A_BYTES = BM * BK * 2;
+    static constexpr int A_PART = BM * BK * 2;
+    static constexpr int A_BYTES = (SPLIT ? 2 : 1) * A_PART;
+    static constexpr int STAGES = (196608 / (A_BYTES + BN * BK * 2)) > 6 ? 6 : (196608 / (A_BYTES + BN * BK * 2));
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
@@ -86,12 +90,12 @@ __device__ __forceinline__ void fail(volatile int* abort, unsigned* err, unsigne
     if (err) atomicCAS(err, 0u, code);
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool SPLIT = false>
 __global__ void __launch_bounds__(NTHREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
                 const __grid_constant__ CUtensorMap tb2, const __grid_constant__ CUtensorMap tout,
-                const GemmArgs args) {
-    using C = GemmCfg<BN>;
+                const __grid_constant__ CUtensorMap ta_lo, const GemmArgs args) {
+    using C = GemmCfg<BN, SPLIT>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -129,6 +133,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         tma_prefetch_map(&ta);
         tma_prefetch_map(&tb);
         if (EPI == kEpiSwiGLU) tma_prefetch_map(&tb2);
+        if (SPLIT) tma_prefetch_map(&ta_lo);
         tma_prefetch_map(&tout);
         tmem_alloc(tmem_slot, C::TMEM_COLS);
     }
@@ -155,6 +160,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     uint8_t* sb = sa + C::A_BYTES;
                     mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
                     tma_load_2d(sa, &ta, kb * BK, tm * BM, &full[stage]);
+                    if (SPLIT) tma_load_2d(sa + C::A_PART, &ta_lo, kb * BK, tm * BM, &full[stage]);
                     if (EPI == kEpiSwiGLU) {
                         tma_load_2d(sb, &tb, kb * BK, tn * (BN / 2), &full[stage]);
                         tma_load_2d(sb + C::B_BYTES / 2, &tb2, kb * BK, tn * (BN / 2), &full[stage]);
@@ -211,6 +217,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k) {
                         mma_bf16(d, adesc + 2 * k, bdesc + 2 * k, idesc, (kbi | k) != 0);
+                        if (SPLIT) {
+                            mma_bf16(d, adesc + (C::A_PART >> 4) + 2 * k, bdesc + 2 * k, idesc, 1);
+                        }
                     }
                     mma_commit(&empty[stage]);
                     if (++stage == C::STAGES) {
@@ -367,36 +376,46 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-template <int BN, int EPI>
-cudaError_t launch_t(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& b2,
-                     const CUtensorMap& out, const GemmArgs& args, int num_sms,
-                     cudaStream_t stream) {
-    using C = GemmCfg<BN>;
-    auto kern = gemm_kernel<BN, EPI>;
-    static thread_local int configured_device = -1;
+// Large dynamic shared memory is opted into once per kernel instance and device.
+template <int BN, int EPI, bool SPLIT = false>
+cudaError_t configure_t() {
+    static bool configured[64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    if (configured_device != dev) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    if (!configured[dev & 63]) {
+        e = cudaFuncSetAttribute(gemm_kernel<BN, EPI, SPLIT>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 GemmCfg<BN, SPLIT>::SMEM_BYTES);
         if (e != cudaSuccess) return e;
-        configured_device = dev;
+        configured[dev & 63] = true;
     }
+    return cudaSuccess;
+}
+
+template <int BN, int EPI, bool SPLIT = false>
+cudaError_t launch_t(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& b2,
+                     const CUtensorMap& out, const GemmArgs& args, int num_sms,
+                     cudaStream_t stream, const CUtensorMap& a_lo) {
+    using C = GemmCfg<BN, SPLIT>;
+    auto kern = gemm_kernel<BN, EPI, SPLIT>;
+    cudaError_t e = configure_t<BN, EPI, SPLIT>();
+    if (e != cudaSuccess) return e;
     GemmArgs g = args;
     const int mn_tiles = ((args.M + BM - 1) / BM) * (args.N / BN);
     g.ksplit = 1;
     if (EPI == kEpiAddF32) {
         // Split K while the tiles fill less than half the SMs (slices reduce-add in L2).
         const int kb = args.K / BK;
-        while (g.ksplit < 4 && mn_tiles * g.ksplit * 2 <= num_sms && kb % (g.ksplit * 2) == 0 &&
-               kb / (g.ksplit * 2) >= 8) {
+        while (g.ksplit < args.max_ksplit && mn_tiles * g.ksplit * 2 <= num_sms &&
+               kb % (g.ksplit * 2) == 0 && kb / (g.ksplit * 2) >= args.min_slice_kblocks) {
             g.ksplit *= 2;
         }
     }
     const int tiles = mn_tiles * g.ksplit;
     const int grid = tiles < num_sms ? tiles : num_sms;
     if (grid <= 0) return cudaSuccess;
-    kern<<<grid, NTHREADS, C::SMEM_BYTES, stream>>>(a, b, b2, out, g);
+    kern<<<grid, NTHREADS, C::SMEM_BYTES, stream>>>(a, b, b2, out, a_lo, g);
     return cudaGetLastError();
 }
 
@@ -461,26 +480,51 @@ int gemm_tile_n(int epi, int N) {
     return N % 256 == 0 ? 256 : 128;
 }
 
+void prepare_gemm_kernels() {
+    Q3_CUDA((configure_t<256, kEpiStoreF32>()));
+    Q3_CUDA((configure_t<128, kEpiStoreF32>()));
+    Q3_CUDA((configure_t<256, kEpiAddF32>()));
+    Q3_CUDA((configure_t<128, kEpiAddF32>()));
+    Q3_CUDA((configure_t<256, kEpiStoreBF16>()));
+    Q3_CUDA((configure_t<128, kEpiStoreBF16>()));
+    Q3_CUDA((configure_t<256, kEpiSwiGLU>()));
+    Q3_CUDA((configure_t<128, kEpiStoreF32, true>()));
+    Q3_CUDA((configure_t<128, kEpiAddF32, true>()));
+    Q3_CUDA((configure_t<256, kEpiStoreF32, true>()));
+    Q3_CUDA((configure_t<256, kEpiAddF32, true>()));
+}
+
 cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap* b2,
                         const CUtensorMap& out, const GemmArgs& args, int epi, int num_sms,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, const CUtensorMap* a_lo) {
     if (args.K % BK != 0 || args.K <= 0 || args.M <= 0) return cudaErrorInvalidValue;
-    const int bn = gemm_tile_n(epi, args.N);
-    if (args.N % bn != 0) return cudaErrorInvalidValue;
-    if (epi == kEpiSwiGLU && !b2) return cudaErrorInvalidValue;
+    const int bn = args.bn ? args.bn : gemm_tile_n(epi, args.N);
+    if ((bn != 128 && bn != 256) || args.N % bn != 0) return cudaErrorInvalidValue;
+    if (epi == kEpiSwiGLU && (!b2 || bn != 256)) return cudaErrorInvalidValue;
     const CUtensorMap& bb = b2 ? *b2 : b;
+    if (a_lo) {
+        if (epi == kEpiStoreF32) {
+            return bn == 256 ? launch_t<256, kEpiStoreF32, true>(a, b, bb, out, args, num_sms, stream, *a_lo)
+                             : launch_t<128, kEpiStoreF32, true>(a, b, bb, out, args, num_sms, stream, *a_lo);
+        }
+        if (epi == kEpiAddF32) {
+            return bn == 256 ? launch_t<256, kEpiAddF32, true>(a, b, bb, out, args, num_sms, stream, *a_lo)
+                             : launch_t<128, kEpiAddF32, true>(a, b, bb, out, args, num_sms, stream, *a_lo);
+        }
+        return cudaErrorInvalidValue;
+    }
     switch (epi) {
         case kEpiStoreF32:
-            return bn == 256 ? launch_t<256, kEpiStoreF32>(a, b, bb, out, args, num_sms, stream)
-                             : launch_t<128, kEpiStoreF32>(a, b, bb, out, args, num_sms, stream);
+            return bn == 256 ? launch_t<256, kEpiStoreF32>(a, b, bb, out, args, num_sms, stream, a)
+                             : launch_t<128, kEpiStoreF32>(a, b, bb, out, args, num_sms, stream, a);
         case kEpiAddF32:
-            return bn == 256 ? launch_t<256, kEpiAddF32>(a, b, bb, out, args, num_sms, stream)
-                             : launch_t<128, kEpiAddF32>(a, b, bb, out, args, num_sms, stream);
+            return bn == 256 ? launch_t<256, kEpiAddF32>(a, b, bb, out, args, num_sms, stream, a)
+                             : launch_t<128, kEpiAddF32>(a, b, bb, out, args, num_sms, stream, a);
         case kEpiStoreBF16:
-            return bn == 256 ? launch_t<256, kEpiStoreBF16>(a, b, bb, out, args, num_sms, stream)
-                             : launch_t<128, kEpiStoreBF16>(a, b, bb, out, args, num_sms, stream);
+            return bn == 256 ? launch_t<256, kEpiStoreBF16>(a, b, bb, out, args, num_sms, stream, a)
+                             : launch_t<128, kEpiStoreBF16>(a, b, bb, out, args, num_sms, stream, a);
         case kEpiSwiGLU:
-            return launch_t<256, kEpiSwiGLU>(a, b, bb, out, args, num_sms, stream);
+            return launch_t<256, kEpiSwiGLU>(a, b, bb, out, args, num_sms, stream, a);
     }
     return cudaErrorInvalidValue;
 }

@@ -39,7 +39,14 @@ struct GemmArgs {
     unsigned* err = nullptr;  // set non-zero when a bounded wait gives up
     long long budget = 4000000000LL;  // cycles per wait
     int ksplit = 1;           // K slices (residual add only; chosen by launch_gemm)
+    int bn = 0;               // tile width override (128 or 256; 0: gemm_tile_n)
+    int max_ksplit = 4;       // residual add: split K up to this many slices ...
+    int min_slice_kblocks = 8;  // ... of at least this many 64-wide k-blocks
 };
+
+// Opts every contraction kernel into its shared memory on the current device (launch_gemm does it
+// on first use; call this before capturing launches into a CUDA graph).
+void prepare_gemm_kernels();
 
 // Tile N width used for an epilogue and output width (128 or 256).
 int gemm_tile_n(int epi, int N);
@@ -48,8 +55,10 @@ int gemm_tile_n(int epi, int N);
 // `out` (make_tmap_out) maps the output: fp32 [M, N] (store or residual add) or bf16 ([M, N/2]
 // for SwiGLU, [M, N] for kEpiStoreBF16). K must be a multiple of 64, N a multiple of the tile
 // width. Grid: one persistent CTA per SM at most. Returns cudaSuccess or the launch error.
+// a_lo (optional; store and residual-add epilogues): the A operand is a + a_lo, two bf16 parts of
+// fp32 activations (same shape and boxes as a), multiplied into the same accumulator.
 cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap* b2,
                         const CUtensorMap& out, const GemmArgs& args, int epi, int num_sms,
-                        cudaStream_t stream);
+                        cudaStream_t stream, const CUtensorMap* a_lo = nullptr);
 
 }  // namespace q3

@@ -28,6 +28,7 @@
 #include "q3_kernels.cuh"
 #include "q3_model.cuh"
 #include "q3_prefill.cuh"
+#include "q3_batch.cuh"
 
 namespace q3 {
 
@@ -513,7 +514,8 @@ Model::Model(const std::string& path, int ctx, int device) : file_(path) {
         throw std::runtime_error("Invalid embedding, final norm, or output tensor shape");
     }
     // Arena layout: embed | output? | final_norm | per layer: attn_norm q_norm k_norm
-    // [wq;wk;wv] wo mlp_norm w1 w3 w2 - every block 256-byte aligned, wq/wk/wv back to back.
+    // [wq;wk;wv] wo mlp_norm [w1;w3] w2 - every block 256-byte aligned, wq/wk/wv and w1/w3 back
+    // to back.
     struct Piece {
         const ModelFile::Tensor* t;
         size_t expect;
@@ -572,7 +574,7 @@ Model::Model(const std::string& path, int ctx, int device) : file_(path) {
         place(t_wv, kvd * D);
         lo[4] = place(t_wo, D * qd);
         lo[5] = place(t_mn, D);
-        lo[6] = place(t_w1, H * D);
+        lo[6] = place(t_w1, H * D, false);  // w1 and w3 back to back: one [2H, D] operand
         lo[7] = place(t_w3, H * D);
         lo[8] = place(t_w2, D * H);
     }
@@ -1014,8 +1016,8 @@ void Model::prefill_batched(const int32_t* ids, int n, int pos0, float* last_log
     std::memcpy(pinned_io_.ptr, ids, static_cast<size_t>(n) * 4);
     Q3_CUDA(cudaMemcpyAsync(prefill_ids_.ptr, pinned_io_.ptr, static_cast<size_t>(n) * 4,
                             cudaMemcpyHostToDevice, s));
-    prefill_->run(static_cast<const int32_t*>(prefill_ids_.ptr), n, pos0, embed_, layers_, e,
-                  e.x(), hidden_host ? e.taps() : nullptr, s);
+    prefill_->run(static_cast<const int32_t*>(prefill_ids_.ptr), n, pos0, embed_, layers_,
+                  engine_view(e), e.x(), hidden_host ? e.taps() : nullptr, s);
     // Final RmsNorm + tied lm_head of the last token (src/inference.cpp:619-635) and Greedy.
     const q3_config& c = cfg_;
     launch_gemv(kEpiStore, output_, nullptr, e.x(), final_norm_, c.norm_eps,
@@ -1198,6 +1200,10 @@ using q3::guard;
 struct q3_model {
     std::unique_ptr<q3::Model> m;
 };
+struct q3_batch {
+    std::unique_ptr<q3::Batch> b;
+};
+
 struct q3_block {
     std::unique_ptr<q3::Block> b;
 };
@@ -1425,6 +1431,56 @@ q3_status q3_model_fused_timeout_selftest(q3_model* model, int* timed_out) {
     return guard([&] {
         if (!model || !timed_out) throw std::invalid_argument("null argument");
         *timed_out = model->m->fused_timeout_selftest() ? 1 : 0;
+    });
+}
+
+q3_status q3_batch_create(q3_model* model, int max_seqs, int max_tokens, q3_batch** out) {
+    return guard([&] {
+        if (!model || !out) throw std::invalid_argument("null argument");
+        auto h = std::make_unique<q3_batch>();
+        h->b = std::make_unique<q3::Batch>(*model->m, max_seqs, max_tokens);
+        *out = h.release();
+    });
+}
+
+void q3_batch_free(q3_batch* batch) { delete batch; }
+
+q3_status q3_batch_add(q3_batch* batch, const int32_t* ids_host, int n, int* slot,
+                       int32_t* next_token_host, float* last_logits_host) {
+    return guard([&] {
+        if (!batch) throw std::invalid_argument("null argument");
+        const int s = batch->b->add(ids_host, n, next_token_host, last_logits_host);
+        if (slot) *slot = s;
+    });
+}
+
+q3_status q3_batch_size(const q3_batch* batch, int* n_seqs) {
+    return guard([&] {
+        if (!batch || !n_seqs) throw std::invalid_argument("null argument");
+        *n_seqs = batch->b->size();
+    });
+}
+
+q3_status q3_batch_decode(q3_batch* batch, int n_steps, int32_t* tokens_host) {
+    return guard([&] {
+        if (!batch) throw std::invalid_argument("null argument");
+        batch->b->decode(n_steps, tokens_host);
+    });
+}
+
+q3_status q3_batch_decode_forced(q3_batch* batch, const int32_t* tokens_host, int n_steps,
+                                 int32_t* argmax_host, float* logits_host) {
+    return guard([&] {
+        if (!batch) throw std::invalid_argument("null argument");
+        batch->b->decode_forced(tokens_host, n_steps, argmax_host, logits_host);
+    });
+}
+
+q3_status q3_batch_kv_row(q3_batch* batch, int slot, int layer, int pos, uint16_t* k_host,
+                          uint16_t* v_host) {
+    return guard([&] {
+        if (!batch) throw std::invalid_argument("null argument");
+        batch->b->kv_row(slot, layer, pos, k_host, v_host);
     });
 }
 

@@ -150,6 +150,7 @@ public:
     ~Model();
 
     const q3_config& config() const { return cfg_; }
+    int device() const { return device_; }
     int tensor_count() const { return tensor_count_; }
     const ModelFile& file() const { return file_; }
     cudaStream_t stream() const { return engine_->stream(); }

@@ -32,7 +32,8 @@ constexpr int kNormWarps = 8;  // rows per block, one warp per row
 __global__ void __launch_bounds__(kNormWarps * 32)
     rmsnorm_rows_kernel(const int32_t* __restrict__ ids, const uint16_t* __restrict__ embed,
                         float* __restrict__ x, const uint16_t* __restrict__ w, float eps,
-                        uint16_t* __restrict__ out, int rows, int dim) {
+                        uint16_t* __restrict__ out, uint16_t* __restrict__ out_lo, int rows,
+                        int dim) {
     const int lane = threadIdx.x & 31;
     const int row = blockIdx.x * kNormWarps + (threadIdx.x >> 5);
     if (row >= rows) return;
@@ -61,9 +62,15 @@ __global__ void __launch_bounds__(kNormWarps * 32)
     for (int i = lane * 4; i < dim; i += 128) {
         const float4 v = *reinterpret_cast<const float4*>(xr + i);
         const uint2 wb = *reinterpret_cast<const uint2*>(w + i);
-        *reinterpret_cast<uint2*>(orow + i) =
-            make_uint2(pack2_bf16((v.x * inv) * bf16_lo(wb.x), (v.y * inv) * bf16_hi(wb.x)),
-                       pack2_bf16((v.z * inv) * bf16_lo(wb.y), (v.w * inv) * bf16_hi(wb.y)));
+        const float y0 = (v.x * inv) * bf16_lo(wb.x), y1 = (v.y * inv) * bf16_hi(wb.x);
+        const float y2 = (v.z * inv) * bf16_lo(wb.y), y3 = (v.w * inv) * bf16_hi(wb.y);
+        const uint2 hi = make_uint2(pack2_bf16(y0, y1), pack2_bf16(y2, y3));
+        *reinterpret_cast<uint2*>(orow + i) = hi;
+        if (out_lo) {  // y - bf16(y): the hi + lo pair carries 16 significant bits
+            *reinterpret_cast<uint2*>(out_lo + static_cast<size_t>(row) * dim + i) =
+                make_uint2(pack2_bf16(y0 - bf16_lo(hi.x), y1 - bf16_hi(hi.x)),
+                           pack2_bf16(y2 - bf16_lo(hi.y), y3 - bf16_hi(hi.y)));
+        }
     }
 }
 
@@ -77,7 +84,9 @@ __global__ void __launch_bounds__(256) prefill_qkv_kernel(PrefillQkvArgs a) {
     const int head = blockIdx.y * 8 + warp;
     const int nq = a.n_heads, nk = a.n_kv;
     if (head >= nq + 2 * nk) return;
-    const int pos = a.pos0 + row;
+    const int pos = a.dec_pos ? a.dec_pos[row] : a.pos0 + row;
+    const int32_t* table = a.dec_pos ? a.page_table + static_cast<size_t>(row) * a.pages_per_seq
+                                     : a.page_table;
     const float* src = a.qkv + static_cast<size_t>(row) * (nq + 2 * nk) * HD + head * HD;
     float4 v = reinterpret_cast<const float4*>(src)[lane];
     const int e = lane * 4;
@@ -121,13 +130,13 @@ __global__ void __launch_bounds__(256) prefill_qkv_kernel(PrefillQkvArgs a) {
         } else {
             const int g = head - nq;
             dst = a.k_cache +
-                  ((static_cast<size_t>(a.page_table[pos / kPageTokens]) * nk + g) * kPageTokens +
+                  ((static_cast<size_t>(table[pos / kPageTokens]) * nk + g) * kPageTokens +
                    pos % kPageTokens) * HD;
         }
     } else {
         const int g = head - nq - nk;
         dst = a.v_cache +
-              ((static_cast<size_t>(a.page_table[pos / kPageTokens]) * nk + g) * kPageTokens +
+              ((static_cast<size_t>(table[pos / kPageTokens]) * nk + g) * kPageTokens +
                pos % kPageTokens) * HD;
     }
     reinterpret_cast<uint2*>(dst)[lane] = make_uint2(pack2_bf16(v.x, v.y), pack2_bf16(v.z, v.w));
@@ -355,11 +364,11 @@ int device_sms(int device) {
 
 void launch_rmsnorm_rows_bf16(const int32_t* ids, const uint16_t* embed, float* x,
                               const uint16_t* w, float eps, uint16_t* out, int rows, int dim,
-                              cudaStream_t s) {
+                              cudaStream_t s, uint16_t* out_lo) {
     if (rows <= 0) return;
     if (dim % 256 != 0) throw std::invalid_argument("row RmsNorm needs a width that is a multiple of 256");
     rmsnorm_rows_kernel<<<(rows + kNormWarps - 1) / kNormWarps, kNormWarps * 32, 0, s>>>(
-        ids, embed, x, w, eps, out, rows, dim);
+        ids, embed, x, w, eps, out, out_lo, rows, dim);
     Q3_CUDA(cudaGetLastError());
 }
 
@@ -432,6 +441,30 @@ void Prefill::ensure_weight_maps(const std::vector<LayerWeights>& layers) {
     wmaps_key_ = layers.empty() ? nullptr : layers[0].wqkv;
 }
 
+size_t Prefill::layer_elems(const KvView& kv) const {
+    return static_cast<size_t>(kv.n_pages) * cfg_.n_kv_heads * kPageTokens * HD;
+}
+
+void Prefill::ensure_kv_maps(const KvView& kv, int L) {
+    if (kv_key_ == kv.k_base && kv_pages_ == kv.n_pages) return;
+    const q3_config& c = cfg_;
+    const uint64_t kv_rows = static_cast<uint64_t>(L) * kv.n_pages * c.n_kv_heads * kPageTokens;
+    make_tmap_bf16(&kmap_, kv.k_base, kv_rows, HD, kPageTokens);
+    make_tmap_bf16(&vmap_, kv.v_base, kv_rows, HD, kPageTokens);
+    // The 4-D page maps serve tiles of 8 pages inside one layer; with fewer pages per layer the
+    // kernel never takes that path and the 2-D maps stand in.
+    if (kv.n_pages >= 8) {
+        const uint64_t pages = static_cast<uint64_t>(L) * kv.n_pages;
+        make_tmap_kv_pages(&kmap4_, kv.k_base, c.n_kv_heads, pages);
+        make_tmap_kv_pages(&vmap4_, kv.v_base, c.n_kv_heads, pages);
+    } else {
+        kmap4_ = kmap_;
+        vmap4_ = vmap_;
+    }
+    kv_key_ = kv.k_base;
+    kv_pages_ = kv.n_pages;
+}
+
 unsigned Prefill::read_error(cudaStream_t s) {
     unsigned v = 0;
     Q3_CUDA(cudaMemcpyAsync(&v, err_.ptr, sizeof(v), cudaMemcpyDeviceToHost, s));
@@ -440,37 +473,33 @@ unsigned Prefill::read_error(cudaStream_t s) {
     return v;
 }
 
+KvView engine_view(Engine& e) {
+    KvView v;
+    v.k_base = e.k_layer(0);
+    v.v_base = e.v_layer(0);
+    v.n_pages = e.n_pages();
+    v.page_table = e.page_table();
+    v.rope = e.rope();
+    v.rope_len = e.rope_len();
+    return v;
+}
+
 void Prefill::run(const int32_t* ids_dev, int n, int pos0, const uint16_t* embed,
-                  const std::vector<LayerWeights>& layers, Engine& e, float* x_last, float* taps,
-                  cudaStream_t s) {
+                  const std::vector<LayerWeights>& layers, const KvView& kv, float* x_last,
+                  float* taps, cudaStream_t s) {
     const q3_config& c = cfg_;
     if (n <= 0) return;
-    if (pos0 < 0 || pos0 + n > c.max_seq_len) {
+    const int table_len = kv.table_len ? kv.table_len : kv.n_pages;
+    if (pos0 < 0 || pos0 + n > table_len * kPageTokens) {
         throw std::out_of_range("batched prefill past the context length");
     }
-    if (e.rope_len() < pos0 + n) throw std::runtime_error("RoPE table shorter than the prompt");
+    if (kv.rope_len < pos0 + n) throw std::runtime_error("RoPE table shorter than the prompt");
     const int qd = c.n_heads * HD;
     const int qkv = (c.n_heads + 2 * c.n_kv_heads) * HD;
     const int L = static_cast<int>(layers.size());
     ensure_rows(std::min(n, kMaxChunk));
     ensure_weight_maps(layers);
-    if (kv_key_ != e.k_layer(0)) {
-        const uint64_t kv_rows =
-            static_cast<uint64_t>(L) * e.n_pages() * c.n_kv_heads * kPageTokens;
-        make_tmap_bf16(&kmap_, e.k_layer(0), kv_rows, HD, kPageTokens);
-        make_tmap_bf16(&vmap_, e.v_layer(0), kv_rows, HD, kPageTokens);
-        // The 4-D page maps serve tiles of 8 pages inside one layer; with fewer pages per layer
-        // the kernel never takes that path and the 2-D maps stand in.
-        if (e.n_pages() >= 8) {
-            const uint64_t pages = static_cast<uint64_t>(L) * e.n_pages();
-            make_tmap_kv_pages(&kmap4_, e.k_layer(0), c.n_kv_heads, pages);
-            make_tmap_kv_pages(&vmap4_, e.v_layer(0), c.n_kv_heads, pages);
-        } else {
-            kmap4_ = kmap_;
-            vmap4_ = vmap_;
-        }
-        kv_key_ = e.k_layer(0);
-    }
+    ensure_kv_maps(kv, L);
     float* X = static_cast<float*>(x_.ptr);
     uint16_t* Xn = static_cast<uint16_t*>(xn_.ptr);
     unsigned* err = static_cast<unsigned*>(err_.ptr);
@@ -512,11 +541,11 @@ void Prefill::run(const int32_t* ids_dev, int n, int pos0, const uint16_t* embed
             qa.qkv = static_cast<const float*>(qkv_.ptr);
             qa.q_norm = w.q_norm;
             qa.k_norm = w.k_norm;
-            qa.rope = e.rope();
+            qa.rope = kv.rope;
             qa.q_out = static_cast<uint16_t*>(q_.ptr);
-            qa.k_cache = e.k_layer(l);
-            qa.v_cache = e.v_layer(l);
-            qa.page_table = e.page_table();
+            qa.k_cache = kv.k_base + layer_elems(kv) * l;
+            qa.v_cache = kv.v_base + layer_elems(kv) * l;
+            qa.page_table = kv.page_table;
             qa.rows = S;
             qa.pos0 = p0;
             qa.n_heads = c.n_heads;
@@ -525,21 +554,22 @@ void Prefill::run(const int32_t* ids_dev, int n, int pos0, const uint16_t* embed
             launch_prefill_qkv(qa, s);
             if (use_tc_attention_) {
                 PrefillAttnTcArgs ta{};
-                ta.page_table = e.page_table();
+                ta.page_table = kv.page_table;
                 ta.out = static_cast<uint16_t*>(o_.ptr);
                 ta.err = err;
                 ta.rows = S;
                 ta.pos0 = p0;
                 ta.n_kv = c.n_kv_heads;
-                ta.n_pages = e.n_pages();
+                ta.n_pages = kv.n_pages;
+                ta.pages_per_seq = table_len;
                 ta.layer = l;
                 launch_prefill_attention_tc(m_q, kmap_, vmap_, kmap4_, vmap4_, ta, s);
             } else {
                 PrefillAttnArgs aa{};
                 aa.q = static_cast<const uint16_t*>(q_.ptr);
-                aa.k_cache = e.k_layer(l);
-                aa.v_cache = e.v_layer(l);
-                aa.page_table = e.page_table();
+                aa.k_cache = kv.k_base + layer_elems(kv) * l;
+                aa.v_cache = kv.v_base + layer_elems(kv) * l;
+                aa.page_table = kv.page_table;
                 aa.out = static_cast<uint16_t*>(o_.ptr);
                 aa.rows = S;
                 aa.pos0 = p0;

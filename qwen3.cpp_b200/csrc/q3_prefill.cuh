@@ -16,9 +16,10 @@ namespace q3 {
 
 // Row-wise RmsNorm (src/inference.cpp:887-923) of fp32 rows into bf16 MMA operands; with ids
 // non-null, the fp32 rows are first gathered from the embedding (:601-603) into x.
+// out_lo (nullable) receives y - bf16(y), so that out + out_lo carries 16 significant bits.
 void launch_rmsnorm_rows_bf16(const int32_t* ids, const uint16_t* embed, float* x,
                               const uint16_t* w, float eps, uint16_t* out, int rows, int dim,
-                              cudaStream_t s);
+                              cudaStream_t s, uint16_t* out_lo = nullptr);
 
 // Per-token, per-head QK-RMSNorm + RoPE (src/inference.cpp:800-810) and bf16 K/V write into the
 // paged cache at kv_pos = pos (:812-815) for tokens at positions pos0 .. pos0+rows-1, all below
@@ -34,6 +35,10 @@ struct PrefillQkvArgs {
     const int32_t* page_table;
     int rows, pos0, n_heads, n_kv;
     float eps;
+    // Decode of independent sequences: row b is at position dec_pos[b] and uses the page table
+    // page_table + b * pages_per_seq (null: row i is at pos0 + i of one sequence).
+    const int32_t* dec_pos = nullptr;
+    int pages_per_seq = 0;
 };
 void launch_prefill_qkv(const PrefillQkvArgs& a, cudaStream_t s);
 
@@ -60,10 +65,30 @@ struct PrefillAttnTcArgs {
     unsigned* err;             // set non-zero when a bounded wait gives up
     long long budget = 4000000000LL;
     int rows, pos0, n_kv, n_pages, layer;
+    // Decode of independent sequences (one query row each): row b attends positions
+    // [0, dec_pos[b]] through page_table + b * pages_per_seq (null: causal prefill). In prefill,
+    // pages_per_seq is the length of page_table (0: n_pages).
+    const int32_t* dec_pos = nullptr;
+    int pages_per_seq = 0;
+    uint16_t* out_lo = nullptr;  // optional: attention output - bf16(output)
 };
 void launch_prefill_attention_tc(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
                                  const CUtensorMap& k4, const CUtensorMap& v4,
                                  const PrefillAttnTcArgs& a, cudaStream_t s);
+
+// A paged KV cache as the prefill sees it: every layer's pages back to back from k_base /
+// v_base ([n_layers][n_pages][n_kv][16][128] bf16), the page table of the sequence being
+// prefilled, and the RoPE table.
+struct KvView {
+    uint16_t* k_base = nullptr;
+    uint16_t* v_base = nullptr;
+    int n_pages = 0;                     // pages per layer
+    const int32_t* page_table = nullptr; // logical -> physical page of this sequence
+    const float2* rope = nullptr;        // [rope_len][64] (cos, sin)
+    int rope_len = 0;
+    int table_len = 0;                   // entries of page_table (0: n_pages)
+};
+KvView engine_view(Engine& e);
 
 // Driver of a batched prefill over the layers of a Model.
 class Prefill {
@@ -82,16 +107,26 @@ public:
     // last token in x_last (fp32 [dim]). taps (nullable) receive the last token's hidden state
     // before the first layer and after every layer ([(n_layers+1) * dim]).
     void run(const int32_t* ids_dev, int n, int pos0, const uint16_t* embed,
-             const std::vector<LayerWeights>& layers, Engine& e, float* x_last, float* taps,
-             cudaStream_t s);
+             const std::vector<LayerWeights>& layers, const KvView& kv, float* x_last,
+             float* taps, cudaStream_t s);
     // Non-zero when a contraction's bounded wait gave up in the last run.
     unsigned read_error(cudaStream_t s);
     // Attention kernel: tcgen05 (default) or the mma.sync flash-attention kernel.
     void set_tc_attention(bool on) { use_tc_attention_ = on; }
 
+    // TMA maps of the paged caches (2-D rows and 4-D page boxes) for a view; cached.
+    void ensure_kv_maps(const KvView& kv, int n_layers);
+    const CUtensorMap& kmap() const { return kmap_; }
+    const CUtensorMap& vmap() const { return vmap_; }
+    const CUtensorMap& kmap4() const { return kmap4_; }
+    const CUtensorMap& vmap4() const { return vmap4_; }
+    unsigned* err() const { return static_cast<unsigned*>(err_.ptr); }
+    int num_sms() const { return num_sms_; }
+
 private:
     void ensure_rows(int rows);
     void ensure_weight_maps(const std::vector<LayerWeights>& layers);
+    size_t layer_elems(const KvView& kv) const;
 
     q3_config cfg_;
     int device_ = 0;
@@ -106,6 +141,7 @@ private:
     const uint16_t* wmaps_key_ = nullptr;
     CUtensorMap kmap_, vmap_, kmap4_, vmap4_;
     const uint16_t* kv_key_ = nullptr;
+    int kv_pages_ = 0;
 };
 
 }  // namespace q3

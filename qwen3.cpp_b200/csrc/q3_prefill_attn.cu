@@ -205,14 +205,28 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // 1-D grid, longest query blocks first across every KV head, so that the block scheduler
-    // starts the longest work first and the short blocks fill the tail.
-    const int n_qb = gridDim.x / a.n_kv;
-    const int qb = n_qb - 1 - static_cast<int>(blockIdx.x) / a.n_kv;
+    // Prefill: 1-D grid, longest query blocks first across every KV head, so that the block
+    // scheduler starts the longest work first and the short blocks fill the tail. Decode: block
+    // (b, g) serves the one query row of sequence b; the other 63 rows of each head's Q box are
+    // computed with the same mask and dropped.
+    const bool dec = a.dec_pos != nullptr;
     const int g = static_cast<int>(blockIdx.x) % a.n_kv;
-    const int tok0 = qb * TOK;
-    const int last_tok = min(a.rows, tok0 + TOK) - 1;
-    const int kv_end = a.pos0 + last_tok + 1;
+    int tok0, last_tok, kv_end;
+    const int32_t* table = a.page_table;
+    if (dec) {
+        const int b = static_cast<int>(blockIdx.x) / a.n_kv;
+        tok0 = b;
+        last_tok = b;
+        kv_end = a.dec_pos[b] + 1;
+        table += static_cast<size_t>(b) * a.pages_per_seq;
+    } else {
+        const int n_qb = gridDim.x / a.n_kv;
+        const int qb = n_qb - 1 - static_cast<int>(blockIdx.x) / a.n_kv;
+        tok0 = qb * TOK;
+        last_tok = min(a.rows, tok0 + TOK) - 1;
+        kv_end = a.pos0 + last_tok + 1;
+    }
+    const int table_len = a.pages_per_seq ? a.pages_per_seq : a.n_pages;
     const int ntiles = (kv_end + KEYS - 1) / KEYS;
     const int valid_pages = (kv_end + kPageTokens - 1) / kPageTokens;
 
@@ -272,11 +286,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     uint64_t* ful = kind ? &v_full[st] : &kv_full[st];
                     int rows8[KEYS / kPageTokens];
                     const int lp0 = j * (KEYS / kPageTokens);
-                    const bool all_in = lp0 + KEYS / kPageTokens <= a.n_pages;
+                    const bool all_in = lp0 + KEYS / kPageTokens <= table_len;
 #pragma unroll
                     for (int pg = 0; pg < KEYS / kPageTokens; ++pg) {
                         const int page = all_in ? lp0 + pg : min(lp0 + pg, valid_pages - 1);
-                        rows8[pg] = __ldg(a.page_table + page);
+                        rows8[pg] = __ldg(table + page);
                     }
                     bool contiguous = all_in;
 #pragma unroll
@@ -405,8 +419,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int lg = warp & 3;
         const int half = (warp - 2) >> 2;                // key half of S, column half of O
         const int r = lg * 32 + lane;                    // row of the 128-row tile
-        const int tok = min(tok0 + (r & (TOK - 1)), last_tok);
-        const int qpos = a.pos0 + tok;
+        const int qpos = dec ? kv_end - 1 : a.pos0 + min(tok0 + (r & (TOK - 1)), last_tok);
         const uint32_t lane_half = tmem + (static_cast<uint32_t>(lg * 32) << 16) +
                                    static_cast<uint32_t>(half * 64);
         const float scale = 1.4426950408889634f / sqrtf(static_cast<float>(HD));
@@ -506,18 +519,30 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (l_other != l_other) {
                 fail(abort, a.err, 19);
             } else {
-                const int token = tok0 + (r & (TOK - 1));
+                const int token = dec ? ((r & (TOK - 1)) == 0 ? tok0 : a.rows) : tok0 + (r & (TOK - 1));
                 if (token < a.rows) {
                     const float inv = 1.0f / (l + l_other);
-                    uint4* dst = reinterpret_cast<uint4*>(
-                        a.out + static_cast<size_t>(token) * (2 * a.n_kv) * HD +
-                        (2 * g + (r >> 6)) * HD + half * 64);
+                    const size_t off = static_cast<size_t>(token) * (2 * a.n_kv) * HD +
+                                       (2 * g + (r >> 6)) * HD + half * 64;
+                    uint4* dst = reinterpret_cast<uint4*>(a.out + off);
 #pragma unroll
                     for (int i = 0; i < HD / 16; ++i) {
-                        dst[i] = make_uint4(pack_bf16x2(acc[8 * i] * inv, acc[8 * i + 1] * inv),
-                                            pack_bf16x2(acc[8 * i + 2] * inv, acc[8 * i + 3] * inv),
-                                            pack_bf16x2(acc[8 * i + 4] * inv, acc[8 * i + 5] * inv),
-                                            pack_bf16x2(acc[8 * i + 6] * inv, acc[8 * i + 7] * inv));
+                        float y[8];
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) y[k] = acc[8 * i + k] * inv;
+                        const uint4 hi = make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]),
+                                                    pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7]));
+                        dst[i] = hi;
+                        if (a.out_lo) {
+                            const uint32_t h4[4] = {hi.x, hi.y, hi.z, hi.w};
+                            uint32_t l4[4];
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                l4[k] = pack_bf16x2(y[2 * k] - __uint_as_float(h4[k] << 16),
+                                                    y[2 * k + 1] - __uint_as_float(h4[k] & 0xffff0000u));
+                            }
+                            reinterpret_cast<uint4*>(a.out_lo + off)[i] = make_uint4(l4[0], l4[1], l4[2], l4[3]);
+                        }
                     }
                 }
             }
@@ -544,7 +569,7 @@ void launch_prefill_attention_tc(const CUtensorMap& q, const CUtensorMap& k, con
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
         configured[dev & 63] = true;
     }
-    const dim3 grid(((a.rows + TOK - 1) / TOK) * a.n_kv);
+    const dim3 grid(a.dec_pos ? a.rows * a.n_kv : ((a.rows + TOK - 1) / TOK) * a.n_kv);
     prefill_attn_tc_kernel<<<grid, NTHREADS, SMEM, s>>>(q, k, v, k4, v4, a);
     Q3_CUDA(cudaGetLastError());
 }

@@ -103,6 +103,12 @@ def lib() -> C.CDLL:
         "q3_model_set_prefill_path": [vp, C.c_int],
         "q3_model_prefill_path": [vp, C.POINTER(C.c_int)],
         "q3_gemm_bf16": [vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, vp],
+        "q3_batch_create": [vp, C.c_int, C.c_int, C.POINTER(vp)],
+        "q3_batch_add": [vp, I32P, C.c_int, C.POINTER(C.c_int), vp, vp],
+        "q3_batch_size": [vp, C.POINTER(C.c_int)],
+        "q3_batch_decode": [vp, C.c_int, vp],
+        "q3_batch_decode_forced": [vp, I32P, C.c_int, vp, vp],
+        "q3_batch_kv_row": [vp, C.c_int, C.c_int, C.c_int, U16P, U16P],
         "q3_decode_greedy": [vp, i32, C.c_int, C.c_int, vp, vp],
         "q3_decode_forced": [vp, I32P, C.c_int, C.c_int, vp, vp],
         "q3_generate": [vp, vp, C.c_int, sz, C.c_int, vp, C.POINTER(sz), C.POINTER(GenStats)],
@@ -134,6 +140,8 @@ def lib() -> C.CDLL:
     L.q3_model_free.restype = None
     L.q3_block_free.argtypes = [vp]
     L.q3_block_free.restype = None
+    L.q3_batch_free.argtypes = [vp]
+    L.q3_batch_free.restype = None
     L.q3_attn_workspace_size.argtypes = [C.c_int, C.c_int]
     L.q3_attn_workspace_size.restype = sz
     L.q3_attn_noalloc_max_scratch.argtypes = []
@@ -297,6 +305,64 @@ class Qwen3:
                                 int(stop_on_eos), out.ctypes.data, C.byref(n), C.byref(st)))
         stats = {k: getattr(st, k) for k, _ in GenStats._fields_}
         return out[:n.value].copy(), stats
+
+
+class Batch:
+    """Independent sequences decoded together on the model's GPU (q3_batch_*)."""
+
+    def __init__(self, model: "Qwen3", max_seqs: int, max_tokens: int):
+        self._lib = lib()
+        self.model = model  # the model must outlive the batch
+        self.vocab = model.config["vocab_size"]
+        self.kvd = model.config["n_kv_heads"] * model.config["head_dim"]
+        h = C.c_void_p()
+        check(self._lib.q3_batch_create(model._h, max_seqs, max_tokens, C.byref(h)))
+        self._h = h
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._lib.q3_batch_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    @property
+    def size(self) -> int:
+        n = C.c_int()
+        check(self._lib.q3_batch_size(self._h, C.byref(n)))
+        return n.value
+
+    def add(self, ids, want_logits: bool = False):
+        """Adds a sequence (prefilling its prompt); returns (slot, next token, logits|None)."""
+        ids = np.ascontiguousarray(ids, np.int32)
+        slot = C.c_int()
+        nxt = np.zeros(1, np.int32)
+        lg = np.empty(self.vocab, np.float32) if want_logits else None
+        check(self._lib.q3_batch_add(self._h, ids, ids.size, C.byref(slot), nxt.ctypes.data,
+                                     _ptr(lg)))
+        return slot.value, int(nxt[0]), lg
+
+    def decode(self, n_steps: int) -> np.ndarray:
+        """n_steps greedy steps for every sequence: tokens [n_steps, n_seqs]."""
+        out = np.empty((max(n_steps, 1), self.size), np.int32)
+        check(self._lib.q3_batch_decode(self._h, n_steps, out.ctypes.data))
+        return out[:n_steps]
+
+    def decode_forced(self, tokens, want_logits: bool = False):
+        """Teacher-forced steps on tokens [n_steps, n_seqs]: (argmax, logits|None)."""
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        n = tokens.shape[0]
+        am = np.empty(tokens.shape, np.int32)
+        lg = np.empty(tokens.shape + (self.vocab,), np.float32) if want_logits else None
+        check(self._lib.q3_batch_decode_forced(self._h, tokens, n, am.ctypes.data, _ptr(lg)))
+        return am, lg
+
+    def kv_row(self, slot: int, layer: int, pos: int):
+        k = np.empty(self.kvd, np.uint16)
+        v = np.empty(self.kvd, np.uint16)
+        check(self._lib.q3_batch_kv_row(self._h, slot, layer, pos, k, v))
+        return k, v
 
 
 class Block:

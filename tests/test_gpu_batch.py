@@ -1,0 +1,135 @@
+"""Batched decode of independent sequences (q3_batch_*) against the oracle.
+
+Each sequence of a batch must behave like the reference run on that sequence alone: its prompt's
+next token and logits, teacher-forced argmax agreement >= 99% with logits max-abs <= 5e-2, and
+KV rows (rel-L2 <= 1e-2) in its own pages. The device-driven greedy loop (CUDA graph) must agree
+with teacher-forced steps fed its own tokens, and capacity and range errors must be reported.
+"""
+import numpy as np
+import pytest
+
+import gen_weights
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+LOGITS_MAX_ABS = 5e-2
+TOP1_AGREEMENT = 0.99
+REL_L2 = 1e-2
+
+PROMPT_LENS = (40, 130, 75)
+STEPS = 24
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+@pytest.fixture(scope="module")
+def seqs():
+    rng = np.random.default_rng(31)
+    return [(rng.integers(0, 151936, n).astype(np.int32),
+             rng.integers(0, 151936, STEPS).astype(np.int32)) for n in PROMPT_LENS]
+
+
+@pytest.fixture(scope="module")
+def oracle_runs(full_weights, seqs):
+    """Per sequence: argmax and logits after every position of prompt + continuation, and a few
+    KV rows, from the oracle run on that sequence alone."""
+    out = []
+    for prompt, cont in seqs:
+        cpu = oracle.PortModel(full_weights, 512)
+        full = np.concatenate([prompt, cont])
+        am, lgs = [], []
+        for pos, t in enumerate(full):
+            lg = cpu.forward(int(t), pos)
+            am.append(int(np.argmax(lg)))
+            lgs.append(lg)
+        kv = {(l, p): cpu.kv_row(l, p) for l in (0, 27) for p in (0, len(prompt) - 1, len(full) - 1)}
+        out.append((np.array(am), np.stack(lgs), kv))
+    return out
+
+
+@pytest.fixture(scope="module")
+def model(q3lib, full_weights):
+    m = q3lib.Qwen3(full_weights, 512)
+    yield m
+    m.close()
+
+
+def test_batch_matches_oracle(q3lib, model, seqs, oracle_runs):
+    batch = q3lib.Batch(model, 4, 512)
+    try:
+        for i, (prompt, _) in enumerate(seqs):
+            slot, nxt, lg = batch.add(prompt, want_logits=True)
+            am, lgs, _ = oracle_runs[i]
+            assert slot == i
+            assert nxt == am[len(prompt) - 1]
+            assert np.abs(lg - lgs[len(prompt) - 1]).max() <= LOGITS_MAX_ABS
+        forced = np.stack([cont for _, cont in seqs], axis=1)  # [steps, seqs]
+        am, lg = batch.decode_forced(forced, want_logits=True)
+        for i, (prompt, cont) in enumerate(seqs):
+            ref_am, ref_lg, kv = oracle_runs[i]
+            n = len(prompt)
+            agree = float((am[:, i] == ref_am[n:n + STEPS]).mean())
+            assert agree >= TOP1_AGREEMENT, (i, agree)
+            assert np.abs(lg[:, i] - ref_lg[n:n + STEPS]).max() <= LOGITS_MAX_ABS
+            f = gen_weights.bf16_bits_to_f32
+            for (l, p), (ko, vo) in kv.items():
+                k, v = batch.kv_row(i, l, p)
+                assert rel_l2(f(k), f(ko)) <= REL_L2, ("k", i, l, p)
+                assert rel_l2(f(v), f(vo)) <= REL_L2, ("v", i, l, p)
+    finally:
+        batch.close()
+
+
+def test_graph_loop_matches_forced_steps(q3lib, model, seqs):
+    """The captured greedy loop and teacher-forced steps fed its own tokens agree."""
+    a = q3lib.Batch(model, 4, 512)
+    b = q3lib.Batch(model, 4, 512)
+    try:
+        firsts = []
+        for prompt, _ in seqs:
+            _, n1, _ = a.add(prompt)
+            _, n2, _ = b.add(prompt)
+            assert n1 == n2
+            firsts.append(n1)
+        toks = a.decode(16)
+        assert toks.shape == (16, len(seqs))
+        feed = np.concatenate([np.array(firsts, np.int32)[None, :], toks[:-1]], axis=0)
+        am, lg = b.decode_forced(feed, want_logits=True)
+        # Split-K sums vary in their last bits from run to run: a disagreement must be a near
+        # tie of the two tokens in the forced step's own logits.
+        for st, sq in zip(*np.nonzero(am != toks)):
+            gap = lg[st, sq, am[st, sq]] - lg[st, sq, toks[st, sq]]
+            assert 0.0 <= gap <= 1e-2, (st, sq, gap)
+        assert float((am == toks).mean()) >= 0.9
+        # A second call continues where the first stopped.
+        more = a.decode(4)
+        assert more.shape == (4, len(seqs))
+    finally:
+        a.close()
+        b.close()
+
+
+def test_batch_capacity_and_range_errors(q3lib, model):
+    batch = q3lib.Batch(model, 2, 64)
+    try:
+        with pytest.raises(q3lib.OutOfRange):
+            batch.add(np.zeros(65, np.int32))
+        with pytest.raises(q3lib.OutOfRange):
+            batch.add(np.array([151936], np.int32))
+        with pytest.raises(q3lib.InvalidArgument):
+            batch.decode(1)  # no sequence yet
+        batch.add(np.arange(60, dtype=np.int32))
+        batch.add(np.arange(10, dtype=np.int32))
+        with pytest.raises(q3lib.OutOfRange):
+            batch.add(np.arange(5, dtype=np.int32))  # full
+        with pytest.raises(q3lib.OutOfRange):
+            batch.decode(5)  # 60 + 5 > 64
+        toks = batch.decode(4)
+        assert toks.shape == (4, 2)
+    finally:
+        batch.close()
