@@ -48,6 +48,22 @@ PREFILL_CTX = 4096
 PREFILL_RUNS = 5
 
 
+# Data-parallel batched decode: 64 sequences with context lengths uniform in [128, 4096] (seed 3)
+# and seeded random prompts of those lengths, 16-token KV pages, 128 greedy steps each, the
+# sequences split evenly over the ranks (strong scaling: the total work is fixed).
+DP_SEQS = 64
+DP_STEPS = 128
+DP_WARMUP = 2
+
+
+def dp_workload():
+    import numpy as np
+    rng = np.random.default_rng(3)
+    lens = rng.integers(128, 4097, DP_SEQS)
+    prompts = [rng.integers(0, VOCAB, int(n)).astype(np.int32) for n in lens]
+    return lens, prompts
+
+
 def prefill_flops(n: int) -> float:
     """Algorithmic FLOPs of a prefill of n tokens: the layer contractions (2 * n * 440,401,920),
     causal attention (4 * head_dim * n_heads * n_layers * n(n+1)/2) and the lm_head of the last
@@ -282,6 +298,33 @@ def run_b200_arm(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         p_ms = float(t.item())
     batched = pm.prefill_path == pm.PREFILL_BATCHED
+
+    # Data-parallel batched decode: this rank's share of the 64 sequences in one batch.
+    lens, prompts = dp_workload()
+    mine = list(range(rank, DP_SEQS, world))
+    batch = q3b200.Batch(pm, len(mine), int(max(lens[i] for i in mine)) + DP_WARMUP + DP_STEPS)
+    for i in mine:
+        batch.add(prompts[i])
+    bext = torch.cuda.ExternalStream(batch.stream)
+    batch.decode(DP_WARMUP)  # warm-up (graph capture); positions advance by DP_WARMUP
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(bext)
+    batch.decode(DP_STEPS)
+    e1.record(bext)
+    torch.cuda.synchronize()
+    dp_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([dp_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dp_ms = float(t.item())
+    # Bytes per step on this rank: the weights once + every sequence's KV rows at its length.
+    kv_tokens = sum(int(lens[i]) + DP_WARMUP + DP_STEPS / 2 for i in mine)
+    dp_bytes_step = WEIGHT_BYTES + KV_BYTES_PER_POS * kv_tokens
+    dp_gbs = dp_bytes_step * DP_STEPS / (dp_ms / 1e3) / 1e9
+    batch.close()
     pm.close()
 
     pk = peaks()
@@ -345,6 +388,17 @@ def run_b200_arm(args):
                     "api": "q3_forward_token per step + host argmax"},
             "cpu_baseline": cpu,
             "clocks": clk,
+            "dp_decode": {
+                "metric": "batched greedy decode tok/s (64 sequences, ctx U[128,4096], "
+                          "Qwen3-0.6B bf16)",
+                "value": round(DP_SEQS * DP_STEPS / (dp_ms / 1e3), 1), "unit": "tok/s",
+                "steps": DP_STEPS, "ms_per_step": round(dp_ms / DP_STEPS, 4),
+                "seqs_per_gpu": len(mine), "scaling": "strong",
+                "roofline": {"bound": "hbm", "achieved": round(dp_gbs, 1),
+                             "peak": pk["hbm_gbs"], "unit": "GB/s",
+                             "frac": round(dp_gbs / pk["hbm_gbs"], 4),
+                             "bytes_per_step_per_gpu": int(dp_bytes_step)},
+            },
             "prefill": {
                 "metric": "prefill tok/s (2048-token prompt, ctx 4096, Qwen3-0.6B bf16)",
                 "value": round(p_tps, 1), "unit": "tok/s", "ms_per_prefill": round(p_ms, 4),

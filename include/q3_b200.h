@@ -194,6 +194,8 @@ void q3_batch_free(q3_batch* batch);
 q3_status q3_batch_add(q3_batch* batch, const int32_t* ids_host, int n, int* slot,
                        int32_t* next_token_host, float* last_logits_host);
 q3_status q3_batch_size(const q3_batch* batch, int* n_seqs);
+/* The batch's CUDA stream (cudaStream_t) for callers that order or time work against it. */
+q3_status q3_batch_stream(q3_batch* batch, void** stream);
 /* n_steps greedy decode steps for every sequence; tokens_host[n_steps][n_seqs] (nullable)
  * receives the generated tokens (step-major). */
 q3_status q3_batch_decode(q3_batch* batch, int n_steps, int32_t* tokens_host);

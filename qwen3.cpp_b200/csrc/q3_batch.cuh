@@ -30,6 +30,7 @@ public:
     // last_logits (nullable, host) its logits.
     int add(const int32_t* ids_host, int n, int32_t* next_token, float* last_logits);
     int size() const { return static_cast<int>(len_.size()); }
+    cudaStream_t stream() const { return s_; }
     int length(int slot) const { return len_.at(slot); }
 
     // n_steps greedy steps for every sequence: each feeds its current token at its next

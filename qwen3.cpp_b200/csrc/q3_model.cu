@@ -1461,6 +1461,13 @@ q3_status q3_batch_size(const q3_batch* batch, int* n_seqs) {
     });
 }
 
+q3_status q3_batch_stream(q3_batch* batch, void** stream) {
+    return guard([&] {
+        if (!batch || !stream) throw std::invalid_argument("null argument");
+        *stream = batch->b->stream();
+    });
+}
+
 q3_status q3_batch_decode(q3_batch* batch, int n_steps, int32_t* tokens_host) {
     return guard([&] {
         if (!batch) throw std::invalid_argument("null argument");

@@ -106,6 +106,7 @@ def lib() -> C.CDLL:
         "q3_batch_create": [vp, C.c_int, C.c_int, C.POINTER(vp)],
         "q3_batch_add": [vp, I32P, C.c_int, C.POINTER(C.c_int), vp, vp],
         "q3_batch_size": [vp, C.POINTER(C.c_int)],
+        "q3_batch_stream": [vp, C.POINTER(vp)],
         "q3_batch_decode": [vp, C.c_int, vp],
         "q3_batch_decode_forced": [vp, I32P, C.c_int, vp, vp],
         "q3_batch_kv_row": [vp, C.c_int, C.c_int, C.c_int, U16P, U16P],
@@ -332,6 +333,12 @@ class Batch:
         n = C.c_int()
         check(self._lib.q3_batch_size(self._h, C.byref(n)))
         return n.value
+
+    @property
+    def stream(self) -> int:
+        s = C.c_void_p()
+        check(self._lib.q3_batch_stream(self._h, C.byref(s)))
+        return s.value or 0
 
     def add(self, ids, want_logits: bool = False):
         """Adds a sequence (prefilling its prompt); returns (slot, next token, logits|None)."""
