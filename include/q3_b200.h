@@ -207,6 +207,31 @@ q3_status q3_batch_decode_forced(q3_batch* batch, const int32_t* tokens_host, in
 q3_status q3_batch_kv_row(q3_batch* batch, int slot, int layer, int pos, uint16_t* k_host,
                           uint16_t* v_host);
 
+/* ------------------------------------------------------------------ tensor-parallel decode
+ * Single-sequence greedy decode split over the GPUs of one node, one process (and model handle)
+ * per GPU (no reference counterpart: the reference runs on one CPU). Rank r of `world` computes
+ * query heads [r*16/world, ...), KV heads [r*8/world, ...), MLP rows/columns
+ * [r*H/world, ...) and a slice of the vocabulary; after o_proj and down_proj the ranks all-reduce
+ * their partial sums over NVLink peer memory (a kernel of this library, not NCCL), and the argmax
+ * likewise. Every rank prefills the prompt on its own model first (q3_prefill, full width), so
+ * that the KV cache of its local heads is in place. world must divide the KV heads (1, 2, 4, 8).
+ * Setup: q3_tp_create on every rank, exchange the 64-byte handles of q3_tp_ipc_handle (any
+ * host channel), q3_tp_connect with all handles in rank order; then every rank calls the same
+ * decode functions with the same arguments. */
+typedef struct q3_tp q3_tp;
+q3_status q3_tp_create(q3_model* model, int rank, int world, q3_tp** out);
+void q3_tp_free(q3_tp* tp);
+q3_status q3_tp_ipc_handle(q3_tp* tp, void* handle_host);
+q3_status q3_tp_connect(q3_tp* tp, const void* handles_host);
+q3_status q3_tp_stream(q3_tp* tp, void** stream);
+/* n_steps greedy steps from first_token at position pos0 (positions < pos0 already in the cache);
+ * tokens_host[n_steps] (nullable) receives the generated tokens, identical on every rank. */
+q3_status q3_tp_decode(q3_tp* tp, int32_t first_token, int pos0, int n_steps,
+                       int32_t* tokens_host);
+/* Teacher-forced: feeds tokens_host[i] at pos0 + i; argmax_host[n] receives each step's argmax. */
+q3_status q3_tp_decode_forced(q3_tp* tp, const int32_t* tokens_host, int n, int pos0,
+                              int32_t* argmax_host);
+
 /* ------------------------------------------------------------------ one block (class Block) */
 
 /* Block(config, weights) (src/inference.cpp:720-730) with BlockWeights

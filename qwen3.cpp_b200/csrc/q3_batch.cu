@@ -274,7 +274,7 @@ void Batch::enqueue_step(bool forced, int n_forced) {
         Q3_CUDA(cudaMemsetAsync(qkv_.ptr, 0, qkv_.bytes, s_));
         gemm(a_xn_, a_xn_lo_, wm.wqkv, o_qkv_, qkv, c.dim, kEpiAddF32);
         PrefillQkvArgs qa{};
-        qa.qkv = static_cast<const float*>(qkv_.ptr);
+        qa.qkv = static_cast<float*>(qkv_.ptr);
         qa.q_norm = w.q_norm;
         qa.k_norm = w.k_norm;
         qa.rope = static_cast<const float2*>(rope_.ptr);

@@ -6,7 +6,7 @@
 //
 // Dataflow. Decode at batch 1 streams 1.19 GB of bf16 weights per token. Each SM runs one
 // continuous stream: a producer warp walks the fixed sequence of byte ranges this CTA owns for the
-// whole call and copies them with TMA bulk copies (cp.async.bulk, no multicast) into a 24-slot
+// whole call and copies them with 1-D TMA bulk copies (cp.async.bulk into this CTA only) into an 8-slot
 // shared-memory ring guarded by full/empty mbarriers. It runs ahead across the grid-wide
 // dependencies (it only waits for a free slot, and - for KV pages - for the step that wrote
 // them). Eight consumer warps wait for each phase's input (a monotonic arrival counter in global

@@ -423,12 +423,17 @@ cudaError_t launch_t(const CUtensorMap& a, const CUtensorMap& b, const CUtensorM
 
 void make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
                     uint32_t box_rows) {
-    if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || cols % 8 != 0 || rows == 0 ||
-        box_rows == 0 || box_rows > 256) {
+    make_tmap_bf16_strided(map, base, rows, cols, cols, box_rows);
+}
+
+void make_tmap_bf16_strided(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                            uint64_t row_stride, uint32_t box_rows) {
+    if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || cols % 8 != 0 || row_stride % 8 != 0 ||
+        row_stride < cols || rows == 0 || box_rows == 0 || box_rows > 256) {
         throw std::invalid_argument("tensor map: misaligned base or unsupported shape");
     }
     const cuuint64_t dims[2] = {cols, rows};
-    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint64_t strides[1] = {row_stride * 2};
     const cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), box_rows};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base),

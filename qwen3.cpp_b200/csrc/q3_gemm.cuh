@@ -29,6 +29,11 @@ void make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t 
 // 64-column panel) and 128-byte swizzling.
 void make_tmap_kv_pages(CUtensorMap* map, const void* base, uint64_t n_kv, uint64_t pages);
 
+// As make_tmap_bf16 for a sub-matrix: rows are row_stride elements apart (a column slice of a
+// wider matrix); base and row_stride * 2 bytes must be 16-byte aligned.
+void make_tmap_bf16_strided(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                            uint64_t row_stride, uint32_t box_rows);
+
 // The output [rows, cols] of a contraction (fp32, or bf16 when bf16) as a TMA map for the
 // epilogue's stores: boxes of 128 bytes x 32 rows with 128-byte swizzling. cols * element size
 // must be a multiple of 128 bytes.

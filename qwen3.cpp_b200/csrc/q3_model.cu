@@ -29,6 +29,7 @@
 #include "q3_model.cuh"
 #include "q3_prefill.cuh"
 #include "q3_batch.cuh"
+#include "q3_tp.cuh"
 
 namespace q3 {
 
@@ -1204,6 +1205,10 @@ struct q3_batch {
     std::unique_ptr<q3::Batch> b;
 };
 
+struct q3_tp {
+    std::unique_ptr<q3::TpDecoder> t;
+};
+
 struct q3_block {
     std::unique_ptr<q3::Block> b;
 };
@@ -1488,6 +1493,54 @@ q3_status q3_batch_kv_row(q3_batch* batch, int slot, int layer, int pos, uint16_
     return guard([&] {
         if (!batch) throw std::invalid_argument("null argument");
         batch->b->kv_row(slot, layer, pos, k_host, v_host);
+    });
+}
+
+q3_status q3_tp_create(q3_model* model, int rank, int world, q3_tp** out) {
+    return guard([&] {
+        if (!model || !out) throw std::invalid_argument("null argument");
+        auto h = std::make_unique<q3_tp>();
+        h->t = std::make_unique<q3::TpDecoder>(*model->m, rank, world);
+        *out = h.release();
+    });
+}
+
+void q3_tp_free(q3_tp* tp) { delete tp; }
+
+q3_status q3_tp_ipc_handle(q3_tp* tp, void* handle_host) {
+    return guard([&] {
+        if (!tp || !handle_host) throw std::invalid_argument("null argument");
+        tp->t->ipc_handle(handle_host);
+    });
+}
+
+q3_status q3_tp_connect(q3_tp* tp, const void* handles_host) {
+    return guard([&] {
+        if (!tp || !handles_host) throw std::invalid_argument("null argument");
+        tp->t->connect(handles_host);
+    });
+}
+
+q3_status q3_tp_stream(q3_tp* tp, void** stream) {
+    return guard([&] {
+        if (!tp || !stream) throw std::invalid_argument("null argument");
+        *stream = tp->t->stream();
+    });
+}
+
+q3_status q3_tp_decode(q3_tp* tp, int32_t first_token, int pos0, int n_steps,
+                       int32_t* tokens_host) {
+    return guard([&] {
+        if (!tp) throw std::invalid_argument("null argument");
+        tp->t->decode(first_token, pos0, n_steps, nullptr, tokens_host);
+    });
+}
+
+q3_status q3_tp_decode_forced(q3_tp* tp, const int32_t* tokens_host, int n, int pos0,
+                              int32_t* argmax_host) {
+    return guard([&] {
+        if (!tp || !tokens_host) throw std::invalid_argument("null argument");
+        tp->t->decode(0, pos0, n, tokens_host, argmax_host);
     });
 }
 

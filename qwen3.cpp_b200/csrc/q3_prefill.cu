@@ -82,13 +82,14 @@ __global__ void __launch_bounds__(256) prefill_qkv_kernel(PrefillQkvArgs a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x;
     const int head = blockIdx.y * 8 + warp;
-    const int nq = a.n_heads, nk = a.n_kv;
+    const int nq = a.n_heads, nk = a.n_kv, nkc = a.n_kv_cache ? a.n_kv_cache : a.n_kv;
     if (head >= nq + 2 * nk) return;
     const int pos = a.dec_pos ? a.dec_pos[row] : a.pos0 + row;
     const int32_t* table = a.dec_pos ? a.page_table + static_cast<size_t>(row) * a.pages_per_seq
                                      : a.page_table;
-    const float* src = a.qkv + static_cast<size_t>(row) * (nq + 2 * nk) * HD + head * HD;
+    float* src = a.qkv + static_cast<size_t>(row) * (nq + 2 * nk) * HD + head * HD;
     float4 v = reinterpret_cast<const float4*>(src)[lane];
+    if (a.clear_input) reinterpret_cast<float4*>(src)[lane] = make_float4(0.f, 0.f, 0.f, 0.f);
     const int e = lane * 4;
     uint16_t* dst;
     if (head < nq + nk) {
@@ -128,15 +129,15 @@ __global__ void __launch_bounds__(256) prefill_qkv_kernel(PrefillQkvArgs a) {
         if (isq) {
             dst = a.q_out + static_cast<size_t>(row) * nq * HD + head * HD;
         } else {
-            const int g = head - nq;
+            const int g = a.kv_head0 + head - nq;
             dst = a.k_cache +
-                  ((static_cast<size_t>(table[pos / kPageTokens]) * nk + g) * kPageTokens +
+                  ((static_cast<size_t>(table[pos / kPageTokens]) * nkc + g) * kPageTokens +
                    pos % kPageTokens) * HD;
         }
     } else {
-        const int g = head - nq - nk;
+        const int g = a.kv_head0 + head - nq - nk;
         dst = a.v_cache +
-              ((static_cast<size_t>(table[pos / kPageTokens]) * nk + g) * kPageTokens +
+              ((static_cast<size_t>(table[pos / kPageTokens]) * nkc + g) * kPageTokens +
                pos % kPageTokens) * HD;
     }
     reinterpret_cast<uint2*>(dst)[lane] = make_uint2(pack2_bf16(v.x, v.y), pack2_bf16(v.z, v.w));
@@ -538,7 +539,7 @@ void Prefill::run(const int32_t* ids_dev, int n, int pos0, const uint16_t* embed
             g.K = c.dim;
             Q3_CUDA(launch_gemm(m_xn, wm.wqkv, nullptr, o_qkv, g, kEpiStoreF32, num_sms_, s));
             PrefillQkvArgs qa{};
-            qa.qkv = static_cast<const float*>(qkv_.ptr);
+            qa.qkv = static_cast<float*>(qkv_.ptr);
             qa.q_norm = w.q_norm;
             qa.k_norm = w.k_norm;
             qa.rope = kv.rope;

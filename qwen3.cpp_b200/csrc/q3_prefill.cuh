@@ -25,7 +25,7 @@ void launch_rmsnorm_rows_bf16(const int32_t* ids, const uint16_t* embed, float* 
 // paged cache at kv_pos = pos (:812-815) for tokens at positions pos0 .. pos0+rows-1, all below
 // the context length (no ring wrap). q is written as bf16 [rows, n_heads*128].
 struct PrefillQkvArgs {
-    const float* qkv;          // [rows, (n_heads + 2*n_kv) * 128] fp32
+    float* qkv;                // [rows, (n_heads + 2*n_kv) * 128] fp32
     const uint16_t* q_norm;
     const uint16_t* k_norm;
     const float2* rope;        // [len][64] (cos, sin)
@@ -39,6 +39,10 @@ struct PrefillQkvArgs {
     // page_table + b * pages_per_seq (null: row i is at pos0 + i of one sequence).
     const int32_t* dec_pos = nullptr;
     int pages_per_seq = 0;
+    // Tensor-parallel shard: the n_kv local KV heads are heads kv_head0.. of a cache laid out
+    // for n_kv_cache heads (0: n_kv).
+    int kv_head0 = 0, n_kv_cache = 0;
+    int clear_input = 0;  // zero qkv after reading it (for reduce-add producers of the next step)
 };
 void launch_prefill_qkv(const PrefillQkvArgs& a, cudaStream_t s);
 
@@ -71,7 +75,19 @@ struct PrefillAttnTcArgs {
     const int32_t* dec_pos = nullptr;
     int pages_per_seq = 0;
     uint16_t* out_lo = nullptr;  // optional: attention output - bf16(output)
+    // Tensor-parallel shard: local KV head g is head kv_head0 + g of a cache of n_kv_cache heads
+    // (0: n_kv); q and out hold the local query heads only.
+    int kv_head0 = 0, n_kv_cache = 0;
+    // Decode split over KV positions (flash-decoding): `splits` blocks per (sequence, KV head),
+    // each over tiles_per_split tiles of 128 positions, write unnormalised partials
+    // part_o [rows][2*n_kv][splits][128] and part_ml [rows][2*n_kv][splits] (max in log2 units
+    // of the scaled scores, sum); launch_attention_combine merges them into out (and out_lo).
+    int splits = 1, tiles_per_split = 0;
+    float* part_o = nullptr;
+    float2* part_ml = nullptr;
 };
+// Merge of the split partials of a decode-mode attention (a.splits > 1).
+void launch_attention_combine(const PrefillAttnTcArgs& a, cudaStream_t s);
 void launch_prefill_attention_tc(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
                                  const CUtensorMap& k4, const CUtensorMap& v4,
                                  const PrefillAttnTcArgs& a, cudaStream_t s);

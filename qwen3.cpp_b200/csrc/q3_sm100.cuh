@@ -1,4 +1,4 @@
-// PTX wrappers for the sm_100a tensor-core path: mbarriers, 2-D TMA tile loads (no multicast),
+// PTX wrappers for the sm_100a tensor-core path: mbarriers, 2-D TMA tile loads (into this CTA only),
 // tcgen05 TMEM allocation, MMA, commit and loads. Every wait is bounded by a clock64 budget.
 #pragma once
 

@@ -1,0 +1,77 @@
+// Tensor-parallel single-sequence decode over the GPUs of one node (one process per GPU).
+//
+// Rank r of N holds, for every layer, the query heads [r*16/N, (r+1)*16/N) and KV heads
+// [r*8/N, (r+1)*8/N) (QKV projection rows, attention, o_proj columns), the MLP rows/columns
+// [r*H/N, (r+1)*H/N) (gate/up rows, down columns), and a 128-row-aligned slice of the tied
+// lm_head; the residual stream x is replicated. After o_proj and after down_proj every rank holds
+// a partial sum of x's update: an all-reduce over NVLink peer memory (each rank pushes its 4 KB
+// partial into every peer's buffer, then raises a flag there) adds them in rank order, so x stays
+// bit-identical on every rank. The greedy argmax is all-reduced the same way over the vocabulary
+// slices (lowest index on ties). The reference has no counterpart (it runs on one CPU).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <memory>
+#include <vector>
+
+#include "q3_model.cuh"
+#include "q3_prefill.cuh"
+
+namespace q3 {
+
+constexpr int kTpMaxRanks = 8;
+
+class TpDecoder {
+public:
+    // model: this rank's full model (its prompt prefill fills the KV cache of every head; the
+    // decoder then only touches the local heads). The model must outlive the decoder.
+    TpDecoder(Model& model, int rank, int world);
+    ~TpDecoder();
+    TpDecoder(const TpDecoder&) = delete;
+    TpDecoder& operator=(const TpDecoder&) = delete;
+
+    // CUDA IPC handle (64 bytes) of this rank's exchange buffer.
+    void ipc_handle(void* out) const;
+    // Maps every peer's exchange buffer (handles of all ranks, rank order, 64 bytes each).
+    void connect(const void* handles);
+
+    // n_steps greedy steps from token `first` at position pos0 (positions below pos0 are in the
+    // KV cache); tokens_host[n_steps] receives the generated tokens (identical on every rank).
+    // forced_host (nullable): teacher forcing, token i fed at step i; argmax to tokens_host.
+    void decode(int32_t first, int pos0, int n_steps, const int32_t* forced_host,
+                int32_t* tokens_host);
+    cudaStream_t stream() const { return s_; }
+
+private:
+    void enqueue_step(bool forced);
+
+    Model& m_;
+    q3_config cfg_;
+    int rank_, world_;
+    int hq_, hkv_, hl_;     // local query heads, KV heads, MLP rows
+    int v0_, vn_;           // local vocabulary rows [v0, v0 + vn)
+    cudaStream_t s_ = nullptr;
+    std::unique_ptr<Prefill> maps_;  // TMA maps of the model's paged KV cache
+    DeviceBuffer shard_;    // per layer: [wq_l; wk_l; wv_l] then [w1_l; w3_l]
+    DeviceBuffer x_, xn_, xn_lo_, qkv_, q_, o_, o_lo_, part_, gu_, h_, h_lo_, logits_;
+    DeviceBuffer pos_, tok_, step_, forced_, log_, err_, counter_, part_o_, part_ml_;
+    DeviceBuffer xbuf_;     // exchange buffer (IPC-exported): data, argmax slots, flags
+    std::vector<void*> peer_mapped_;
+    bool connected_ = false;
+    int log_cap_ = 0;
+    int splits_ = 1, tiles_per_split_ = 0;
+    struct LayerMaps {
+        CUtensorMap wqkv, wo, w13, w2;
+    };
+    std::vector<LayerMaps> wmaps_;
+    CUtensorMap lm_, a_xn_, a_xn_lo_, a_o_, a_o_lo_, a_h_, a_h_lo_, q_map_, o_qkv_, o_part_,
+        o_gu_, o_logits_;
+    cudaGraphExec_t graph_ = nullptr;
+    bool graph_forced_ = false;
+    const float2* graph_rope_ = nullptr;
+};
+
+}  // namespace q3

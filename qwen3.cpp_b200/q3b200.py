@@ -110,6 +110,12 @@ def lib() -> C.CDLL:
         "q3_batch_decode": [vp, C.c_int, vp],
         "q3_batch_decode_forced": [vp, I32P, C.c_int, vp, vp],
         "q3_batch_kv_row": [vp, C.c_int, C.c_int, C.c_int, U16P, U16P],
+        "q3_tp_create": [vp, C.c_int, C.c_int, C.POINTER(vp)],
+        "q3_tp_ipc_handle": [vp, vp],
+        "q3_tp_connect": [vp, vp],
+        "q3_tp_stream": [vp, C.POINTER(vp)],
+        "q3_tp_decode": [vp, i32, C.c_int, C.c_int, vp],
+        "q3_tp_decode_forced": [vp, I32P, C.c_int, C.c_int, vp],
         "q3_decode_greedy": [vp, i32, C.c_int, C.c_int, vp, vp],
         "q3_decode_forced": [vp, I32P, C.c_int, C.c_int, vp, vp],
         "q3_generate": [vp, vp, C.c_int, sz, C.c_int, vp, C.POINTER(sz), C.POINTER(GenStats)],
@@ -143,6 +149,8 @@ def lib() -> C.CDLL:
     L.q3_block_free.restype = None
     L.q3_batch_free.argtypes = [vp]
     L.q3_batch_free.restype = None
+    L.q3_tp_free.argtypes = [vp]
+    L.q3_tp_free.restype = None
     L.q3_attn_workspace_size.argtypes = [C.c_int, C.c_int]
     L.q3_attn_workspace_size.restype = sz
     L.q3_attn_noalloc_max_scratch.argtypes = []
@@ -370,6 +378,53 @@ class Batch:
         v = np.empty(self.kvd, np.uint16)
         check(self._lib.q3_batch_kv_row(self._h, slot, layer, pos, k, v))
         return k, v
+
+
+class TpDecoder:
+    """Tensor-parallel decode (q3_tp_*): rank `rank` of `world`, on `model`'s GPU."""
+
+    def __init__(self, model: "Qwen3", rank: int, world: int):
+        self._lib = lib()
+        self.model = model
+        h = C.c_void_p()
+        check(self._lib.q3_tp_create(model._h, rank, world, C.byref(h)))
+        self._h = h
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._lib.q3_tp_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def ipc_handle(self) -> bytes:
+        buf = (C.c_uint8 * 64)()
+        check(self._lib.q3_tp_ipc_handle(self._h, buf))
+        return bytes(buf)
+
+    def connect(self, handles) -> None:
+        """handles: the 64-byte handles of every rank, in rank order."""
+        blob = b"".join(handles)
+        buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
+        check(self._lib.q3_tp_connect(self._h, buf))
+
+    @property
+    def stream(self) -> int:
+        s = C.c_void_p()
+        check(self._lib.q3_tp_stream(self._h, C.byref(s)))
+        return s.value or 0
+
+    def decode(self, first_token: int, pos0: int, n_steps: int) -> np.ndarray:
+        out = np.empty(max(n_steps, 1), np.int32)
+        check(self._lib.q3_tp_decode(self._h, int(first_token), pos0, n_steps, out.ctypes.data))
+        return out[:n_steps]
+
+    def decode_forced(self, tokens, pos0: int) -> np.ndarray:
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        out = np.empty(max(tokens.size, 1), np.int32)
+        check(self._lib.q3_tp_decode_forced(self._h, tokens, tokens.size, pos0, out.ctypes.data))
+        return out[:tokens.size]
 
 
 class Block:
