@@ -64,6 +64,14 @@ def dp_workload():
     return lens, prompts
 
 
+# Tensor-parallel single-stream decode: context 32768, a 32000-token prompt of seeded random IDs
+# (seed 4) prefilled on every rank, then 128 greedy steps with heads / MLP split over the ranks.
+TP_CTX = 32768
+TP_PROMPT = 32000
+TP_STEPS = 128
+TP_WARMUP = 2
+
+
 def prefill_flops(n: int) -> float:
     """Algorithmic FLOPs of a prefill of n tokens: the layer contractions (2 * n * 440,401,920),
     causal attention (4 * head_dim * n_heads * n_layers * n(n+1)/2) and the lm_head of the last
@@ -327,6 +335,38 @@ def run_b200_arm(args):
     batch.close()
     pm.close()
 
+    # Tensor-parallel decode of one long-context stream over all ranks.
+    tm = q3b200.Qwen3(path, TP_CTX, device=local)
+    tprompt = np.random.default_rng(4).integers(0, VOCAB, TP_PROMPT).astype(np.int32)
+    _, tnext = tm.prefill(tprompt, 0, want_logits=False)
+    tp = q3b200.TpDecoder(tm, rank, world)
+    if world > 1:
+        handles = [None] * world
+        dist.all_gather_object(handles, tp.ipc_handle())
+    else:
+        handles = [tp.ipc_handle()]
+    tp.connect(handles)
+    tpx = torch.cuda.ExternalStream(tp.stream)
+    warm = tp.decode(tnext, TP_PROMPT, TP_WARMUP)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(tpx)
+    tp.decode(int(warm[-1]), TP_PROMPT + TP_WARMUP, TP_STEPS)
+    e1.record(tpx)
+    torch.cuda.synchronize()
+    tp_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([tp_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        tp_ms = float(t.item())
+    tp_kv = TP_PROMPT + TP_WARMUP + TP_STEPS / 2
+    tp_bytes_gpu = (WEIGHT_BYTES + KV_BYTES_PER_POS * tp_kv) / world
+    tp_gbs = tp_bytes_gpu * TP_STEPS / (tp_ms / 1e3) / 1e9
+    tp.close()
+    tm.close()
+
     pk = peaks()
     value = world * args.steps / (total_ms / 1e3)
     avg_kv = kv_pos_sum / args.steps
@@ -398,6 +438,18 @@ def run_b200_arm(args):
                              "peak": pk["hbm_gbs"], "unit": "GB/s",
                              "frac": round(dp_gbs / pk["hbm_gbs"], 4),
                              "bytes_per_step_per_gpu": int(dp_bytes_step)},
+            },
+            "tp_decode": {
+                "metric": "tensor-parallel greedy decode tok/s (B=1, ctx 32768, 32000-token "
+                          "prompt, Qwen3-0.6B bf16)",
+                "value": round(TP_STEPS / (tp_ms / 1e3), 1), "unit": "tok/s",
+                "steps": TP_STEPS, "ms_per_step": round(tp_ms / TP_STEPS, 4),
+                "parallelism": f"tp{world}", "scaling": "strong",
+                "collective": "one-shot all-reduce over NVLink peer memory (library kernel)",
+                "roofline": {"bound": "hbm", "achieved": round(tp_gbs, 1),
+                             "peak": pk["hbm_gbs"], "unit": "GB/s per GPU",
+                             "frac": round(tp_gbs / pk["hbm_gbs"], 4),
+                             "bytes_per_step_per_gpu": int(tp_bytes_gpu)},
             },
             "prefill": {
                 "metric": "prefill tok/s (2048-token prompt, ctx 4096, Qwen3-0.6B bf16)",
