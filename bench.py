@@ -229,150 +229,171 @@ def run_b200_arm(args):
     path = gen_weights.cached_model(0)
     if world > 1:
         dist.barrier()
-    model = q3b200.Qwen3(path, CTX, device=local)
-    if args.path != "auto":
-        model.decode_path = model.PATH_FUSED if args.path == "fused" else model.PATH_LAYERWISE
-    ext = torch.cuda.ExternalStream(model.stream)
-    p = prompt_ids()
-
-    # Warm-up: W decode steps after a prefill.
-    _, nxt = model.prefill(p, 0, want_logits=False)
-    model.decode_greedy(nxt, PROMPT_LEN, max(args.warmup, 3))
-    torch.cuda.synchronize()
-
-    clocks = Clocks(local)
-    total_ms = 0.0
-    done = 0
+    legs = set(args.legs.split(","))
+    unknown = legs - {"decode", "prefill", "dp", "tp"}
+    if unknown:
+        raise SystemExit(f"unknown --legs entries: {sorted(unknown)}")
+    total_ms = e2e_tps = 0.0
     kv_pos_sum = 0
-    while done < args.steps:
-        n = min(RUN_STEPS, args.steps - done)
-        _, nxt = model.prefill(p, 0, want_logits=False)   # untimed
+    fused = False
+    clk = None
+    if "decode" in legs:
+        model = q3b200.Qwen3(path, CTX, device=local)
+        if args.path != "auto":
+            model.decode_path = model.PATH_FUSED if args.path == "fused" else model.PATH_LAYERWISE
+        ext = torch.cuda.ExternalStream(model.stream)
+        p = prompt_ids()
+
+        # Warm-up: W decode steps after a prefill.
+        _, nxt = model.prefill(p, 0, want_logits=False)
+        model.decode_greedy(nxt, PROMPT_LEN, max(args.warmup, 3))
         torch.cuda.synchronize()
+
+        clocks = Clocks(local)
+        total_ms = 0.0
+        done = 0
+        kv_pos_sum = 0
+        while done < args.steps:
+            n = min(RUN_STEPS, args.steps - done)
+            _, nxt = model.prefill(p, 0, want_logits=False)   # untimed
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(ext)
+            model.decode_greedy(nxt, PROMPT_LEN, n)
+            e1.record(ext)
+            torch.cuda.synchronize()
+            total_ms += e0.elapsed_time(e1)
+            kv_pos_sum += sum(PROMPT_LEN + i + 1 for i in range(n))
+            done += n
         if world > 1:
-            dist.barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(ext)
-        model.decode_greedy(nxt, PROMPT_LEN, n)
-        e1.record(ext)
+            t = torch.tensor([total_ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            total_ms = float(t.item())
+        clk = clocks.stop()
+
+        # End to end through the public API with host buffers: ForwardToken per step (token and
+        # position in, 151936 fp32 logits out to host), greedy argmax on the host - the way a user
+        # of the reference drives ForwardToken + Sampler::Greedy.
+        model.reset()
+        _, nxt = model.prefill(p, 0, want_logits=False)
+        e2e_steps = min(args.steps, RUN_STEPS)
+        tok = nxt
         torch.cuda.synchronize()
-        total_ms += e0.elapsed_time(e1)
-        kv_pos_sum += sum(PROMPT_LEN + i + 1 for i in range(n))
-        done += n
-    if world > 1:
-        t = torch.tensor([total_ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
-    clk = clocks.stop()
+        t0 = time.perf_counter()
+        for i in range(e2e_steps):
+            lg = model.forward_token(tok, PROMPT_LEN + i)
+            tok = int(np.argmax(lg))
+        e2e_s = time.perf_counter() - t0
+        e2e_tps = world * e2e_steps / e2e_s
 
-    # End to end through the public API with host buffers: ForwardToken per step (token and
-    # position in, 151936 fp32 logits out to host), greedy argmax on the host - the way a user
-    # of the reference drives ForwardToken + Sampler::Greedy.
-    model.reset()
-    _, nxt = model.prefill(p, 0, want_logits=False)
-    e2e_steps = min(args.steps, RUN_STEPS)
-    tok = nxt
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    for i in range(e2e_steps):
-        lg = model.forward_token(tok, PROMPT_LEN + i)
-        tok = int(np.argmax(lg))
-    e2e_s = time.perf_counter() - t0
-    e2e_tps = world * e2e_steps / e2e_s
-
-    fused = model.decode_path == model.PATH_FUSED
-    model.close()
+        fused = model.decode_path == model.PATH_FUSED
+        model.close()
 
     # Prefill of the long prompt through q3_prefill (ids in from host, next token out), timed with
     # CUDA events on the model's stream; the max over ranks.
     pm = q3b200.Qwen3(path, PREFILL_CTX, device=local)
-    pext = torch.cuda.ExternalStream(pm.stream)
-    pp = np.random.default_rng(2).integers(0, VOCAB, PREFILL_LEN).astype(np.int32)
-    for _ in range(2):
-        pm.prefill(pp, 0, want_logits=False)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
     p_ms = 0.0
-    for _ in range(PREFILL_RUNS):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(pext)
-        pm.prefill(pp, 0, want_logits=False)
-        e1.record(pext)
+    batched = False
+    if "prefill" in legs:
+        pext = torch.cuda.ExternalStream(pm.stream)
+        pp = np.random.default_rng(2).integers(0, VOCAB, PREFILL_LEN).astype(np.int32)
+        for _ in range(2):
+            pm.prefill(pp, 0, want_logits=False)
         torch.cuda.synchronize()
-        p_ms += e0.elapsed_time(e1)
-    p_ms /= PREFILL_RUNS
-    if world > 1:
-        t = torch.tensor([p_ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        p_ms = float(t.item())
-    batched = pm.prefill_path == pm.PREFILL_BATCHED
+        if world > 1:
+            dist.barrier()
+        p_ms = 0.0
+        for _ in range(PREFILL_RUNS):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(pext)
+            pm.prefill(pp, 0, want_logits=False)
+            e1.record(pext)
+            torch.cuda.synchronize()
+            p_ms += e0.elapsed_time(e1)
+        p_ms /= PREFILL_RUNS
+        if world > 1:
+            t = torch.tensor([p_ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            p_ms = float(t.item())
+        batched = pm.prefill_path == pm.PREFILL_BATCHED
 
     # Data-parallel batched decode: this rank's share of the 64 sequences in one batch.
-    lens, prompts = dp_workload()
-    mine = list(range(rank, DP_SEQS, world))
-    batch = q3b200.Batch(pm, len(mine), int(max(lens[i] for i in mine)) + DP_WARMUP + DP_STEPS)
-    for i in mine:
-        batch.add(prompts[i])
-    bext = torch.cuda.ExternalStream(batch.stream)
-    batch.decode(DP_WARMUP)  # warm-up (graph capture); positions advance by DP_WARMUP
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(bext)
-    batch.decode(DP_STEPS)
-    e1.record(bext)
-    torch.cuda.synchronize()
-    dp_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([dp_ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dp_ms = float(t.item())
-    # Bytes per step on this rank: the weights once + every sequence's KV rows at its length.
-    kv_tokens = sum(int(lens[i]) + DP_WARMUP + DP_STEPS / 2 for i in mine)
-    dp_bytes_step = WEIGHT_BYTES + KV_BYTES_PER_POS * kv_tokens
-    dp_gbs = dp_bytes_step * DP_STEPS / (dp_ms / 1e3) / 1e9
-    batch.close()
+    dp_ms = dp_gbs = dp_bytes_step = 0.0
+    mine = []
+    if "dp" in legs:
+        lens, prompts = dp_workload()
+        mine = list(range(rank, DP_SEQS, world))
+        batch = q3b200.Batch(pm, len(mine), int(max(lens[i] for i in mine)) + DP_WARMUP + DP_STEPS)
+        for i in mine:
+            batch.add(prompts[i])
+        bext = torch.cuda.ExternalStream(batch.stream)
+        batch.decode(DP_WARMUP)  # warm-up (graph capture); positions advance by DP_WARMUP
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(bext)
+        batch.decode(DP_STEPS)
+        e1.record(bext)
+        torch.cuda.synchronize()
+        dp_ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([dp_ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            dp_ms = float(t.item())
+        # Bytes per step on this rank: the weights once + every sequence's KV rows at its length.
+        kv_tokens = sum(int(lens[i]) + DP_WARMUP + DP_STEPS / 2 for i in mine)
+        dp_bytes_step = WEIGHT_BYTES + KV_BYTES_PER_POS * kv_tokens
+        dp_gbs = dp_bytes_step * DP_STEPS / (dp_ms / 1e3) / 1e9
+        batch.close()
+
     pm.close()
 
     # Tensor-parallel decode of one long-context stream over all ranks.
-    tm = q3b200.Qwen3(path, TP_CTX, device=local)
-    tprompt = np.random.default_rng(4).integers(0, VOCAB, TP_PROMPT).astype(np.int32)
-    _, tnext = tm.prefill(tprompt, 0, want_logits=False)
-    tp = q3b200.TpDecoder(tm, rank, world)
-    if world > 1:
-        handles = [None] * world
-        dist.all_gather_object(handles, tp.ipc_handle())
-    else:
-        handles = [tp.ipc_handle()]
-    tp.connect(handles)
-    tpx = torch.cuda.ExternalStream(tp.stream)
-    warm = tp.decode(tnext, TP_PROMPT, TP_WARMUP)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(tpx)
-    tp.decode(int(warm[-1]), TP_PROMPT + TP_WARMUP, TP_STEPS)
-    e1.record(tpx)
-    torch.cuda.synchronize()
-    tp_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([tp_ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        tp_ms = float(t.item())
-    tp_kv = TP_PROMPT + TP_WARMUP + TP_STEPS / 2
-    tp_bytes_gpu = (WEIGHT_BYTES + KV_BYTES_PER_POS * tp_kv) / world
-    tp_gbs = tp_bytes_gpu * TP_STEPS / (tp_ms / 1e3) / 1e9
-    tp.close()
-    tm.close()
+    tp_ms = tp_gbs = tp_bytes_gpu = 0.0
+    if "tp" in legs:
+        tm = q3b200.Qwen3(path, TP_CTX, device=local)
+        tprompt = np.random.default_rng(4).integers(0, VOCAB, TP_PROMPT).astype(np.int32)
+        _, tnext = tm.prefill(tprompt, 0, want_logits=False)
+        tp = q3b200.TpDecoder(tm, rank, world)
+        if world > 1:
+            handles = [None] * world
+            dist.all_gather_object(handles, tp.ipc_handle())
+        else:
+            handles = [tp.ipc_handle()]
+        tp.connect(handles)
+        tpx = torch.cuda.ExternalStream(tp.stream)
+        warm = tp.decode(tnext, TP_PROMPT, TP_WARMUP)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(tpx)
+        tp.decode(int(warm[-1]), TP_PROMPT + TP_WARMUP, TP_STEPS)
+        e1.record(tpx)
+        torch.cuda.synchronize()
+        tp_ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([tp_ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            tp_ms = float(t.item())
+        tp_kv = TP_PROMPT + TP_WARMUP + TP_STEPS / 2
+        tp_bytes_gpu = (WEIGHT_BYTES + KV_BYTES_PER_POS * tp_kv) / world
+        tp_gbs = tp_bytes_gpu * TP_STEPS / (tp_ms / 1e3) / 1e9
+        tp.close()
+        tm.close()
 
     pk = peaks()
-    value = world * args.steps / (total_ms / 1e3)
+    dec = "decode" in legs
+    value = world * args.steps / (total_ms / 1e3) if dec else 0.0
     avg_kv = kv_pos_sum / args.steps
     step_bytes = WEIGHT_BYTES + KV_BYTES_PER_POS * avg_kv
-    per_gpu_tps = args.steps / (total_ms / 1e3)
-    if fused:
+    per_gpu_tps = args.steps / (total_ms / 1e3) if dec else 0.0
+    if not dec:
+        achieved, kernel, launches = 0.0, None, 0
+    elif fused:
         # The whole decode step is one kernel: algorithmic bytes per step (weights + the KV rows
         # read at the step's kv_len) over its event-timed duration.
         achieved = step_bytes * per_gpu_tps / 1e9
@@ -387,7 +408,7 @@ def run_b200_arm(args):
 
     cpu = None
     cpu_prefill = None
-    if rank == 0 and world == 1 and q3_ref_available():
+    if rank == 0 and world == 1 and dec and q3_ref_available():
         threads = os.cpu_count() or 1
         tps, _, pre_tps = reference_decode(str(path), RUN_STEPS, 0, threads, with_prefill=True)
         cpu = {"value": round(tps, 3), "unit": UNIT, "cores": threads, "kind": "reference",
@@ -396,8 +417,8 @@ def run_b200_arm(args):
         cpu_prefill = {"value": round(pre_tps, 3), "unit": "tok/s", "cores": threads,
                        "kind": "reference",
                        "sample": f"its token-by-token prefill of the {PROMPT_LEN}-token prompt"}
-    p_tps = world * PREFILL_LEN / (p_ms / 1e3)
-    p_tflops = prefill_flops(PREFILL_LEN) / (p_ms / 1e3) / 1e12
+    p_tps = world * PREFILL_LEN / (p_ms / 1e3) if p_ms else 0.0
+    p_tflops = prefill_flops(PREFILL_LEN) / (p_ms / 1e3) / 1e12 if p_ms else 0.0
 
     if rank == 0:
         line = {
@@ -431,7 +452,7 @@ def run_b200_arm(args):
             "dp_decode": {
                 "metric": "batched greedy decode tok/s (64 sequences, ctx U[128,4096], "
                           "Qwen3-0.6B bf16)",
-                "value": round(DP_SEQS * DP_STEPS / (dp_ms / 1e3), 1), "unit": "tok/s",
+                "value": round(DP_SEQS * DP_STEPS / max(dp_ms / 1e3, 1e-12), 1), "unit": "tok/s",
                 "steps": DP_STEPS, "ms_per_step": round(dp_ms / DP_STEPS, 4),
                 "seqs_per_gpu": len(mine), "scaling": "strong",
                 "roofline": {"bound": "hbm", "achieved": round(dp_gbs, 1),
@@ -442,7 +463,7 @@ def run_b200_arm(args):
             "tp_decode": {
                 "metric": "tensor-parallel greedy decode tok/s (B=1, ctx 32768, 32000-token "
                           "prompt, Qwen3-0.6B bf16)",
-                "value": round(TP_STEPS / (tp_ms / 1e3), 1), "unit": "tok/s",
+                "value": round(TP_STEPS / max(tp_ms / 1e3, 1e-12), 1), "unit": "tok/s",
                 "steps": TP_STEPS, "ms_per_step": round(tp_ms / TP_STEPS, 4),
                 "parallelism": f"tp{world}", "scaling": "strong",
                 "collective": "one-shot all-reduce over NVLink peer memory (library kernel)",
@@ -464,6 +485,12 @@ def run_b200_arm(args):
                 "cpu_baseline": cpu_prefill,
             },
         }
+        for key, leg in (("dp_decode", "dp"), ("tp_decode", "tp"), ("prefill", "prefill")):
+            if leg not in legs:
+                del line[key]
+        if not dec:
+            line["value"] = None
+            line["note"] = f"decode leg not run (--legs {args.legs})"
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
@@ -481,6 +508,10 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--path", choices=["auto", "fused", "layerwise"], default="auto",
                     help="decode path of the b200 arm (auto: fused when the shape allows)")
+    ap.add_argument("--legs", default="decode,prefill,dp,tp",
+                    help="comma-separated legs of the b200 arm to run (decode: the headline "
+                         "B=1 decode; prefill; dp: batched decode; tp: tensor-parallel decode); "
+                         "a profiler run can select one")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

@@ -33,6 +33,7 @@
 #include <cuda_runtime.h>
 #include <float.h>
 #include <limits.h>
+#include <stdlib.h>
 
 #include "q3_decode_fused.cuh"
 
@@ -53,11 +54,10 @@ constexpr int SLOT = 16384;            // bytes per slot
 // them in order: no warp can wait on use n of a slot while use n-1 is still unconsumed (a parity
 // wait for use n would then be satisfied by the completion of use n-2).
 static_assert(NS % 8 == 0, "ring slots must be a multiple of the consumer warps");
-// Rows per ring chunk: 8-row groups feed one m16n8k16 MMA column block.
+// Rows per ring chunk: one 8-row dot group (fma_rows8) per chunk.
 constexpr int RPC_ROW = 8;             // 1024-element rows ([wq;wk;wv], lm_head, w2t)
 constexpr int RPC_GRP = 8;             // 256-element rows (wo split by KV-head group)
 constexpr int RPC_PAIR = 4;            // w1 | w3 row pairs (4 + 4 rows)
-constexpr int XSTRIDE = D + 32;        // bf16 elements between the hi and lo activation rows
 constexpr int T_SHORT = 128;           // KV positions up to which attention runs from the ring
 constexpr int ATT_TOK = 24;            // positions staged per sub-chunk (long contexts)
 constexpr int PAGE_BYTES = kPageTokens * HD * 2;
@@ -66,7 +66,7 @@ enum Mode : int { kStore = 0, kRed = 1, kPair = 2, kLogits = 3 };
 
 struct __align__(128) Smem {
     uint8_t ring[NS][SLOT];
-    uint16_t xhl[2][XSTRIDE]; // staged activation as bf16 hi / lo parts (x = hi + lo)
+    float xf[D];              // staged fp32 activation of a GEMV
     float4 xs4[H / 4];        // attention staging and merge buffers
     float qk[4][HD];          // q head 2g, q head 2g+1, k and v at kv_pos (bf16-rounded)
     float hbuf[64];           // h of this CTA's MLP indices
@@ -76,6 +76,8 @@ struct __align__(128) Smem {
     uint64_t full[NS];
     uint64_t empty[NS];
     unsigned long long wait_cycles;  // instrumentation only
+    unsigned long long gt0;          // instrumentation: globaltimer and clock64 at the start
+    long long clk0;
     int abort_flag;
     int token;
     int go;
@@ -109,6 +111,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// Non-blocking probe (try_wait may suspend the thread for a while before it reports failure).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
 __device__ __forceinline__ uint64_t evict_first_policy() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
@@ -127,6 +141,25 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         "[%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
+}
+// L2 prefetch of a 16-byte aligned range (no completion, no shared memory).
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+    const uint8_t* b = static_cast<const uint8_t*>(src);
+    constexpr uint32_t kPiece = 16384;
+    for (uint32_t o = 0; o < bytes; o += kPiece) {
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(b + o),
+                     "r"(min(kPiece, bytes - o))
+                     : "memory");
+    }
+}
+// Fire-and-forget fp32 additions in L2 (no value returned, the thread does not wait).
+__device__ __forceinline__ void red_add(float* p, float v) {
+    asm volatile("red.relaxed.gpu.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+}
+__device__ __forceinline__ void red_add4(float* p, float4 v) {
+    asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x),
+                 "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
 }
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     unsigned v;
@@ -228,7 +261,7 @@ __device__ __forceinline__ bool warp_wait_full(Smem& sm, int slot, uint32_t pari
     int ok = 0;
     if (!Q3_CHECK(slot >= 0 && slot < NS, 20, slot, parity, 0)) return false;
     if (lane == 0) {
-        if (a.prof && !mbar_try_wait(&sm.full[slot], parity)) {
+        if (a.prof && !mbar_test_wait(&sm.full[slot], parity)) {
             // Instrumentation: time this warp spends waiting for ring data.
             const long long t0 = clock64();
             ok = static_cast<int>(mbar_wait(&sm.full[slot], parity, a, &sm.abort_flag, 1, slot));
@@ -316,7 +349,7 @@ struct Producer {
         }
         if (q >= NS) {
             const uint32_t par = ((q / NS) - 1) & 1;
-            if (a.prof && !mbar_try_wait(&sm.empty[slot], par)) {
+            if (a.prof && !mbar_test_wait(&sm.empty[slot], par)) {
                 const long long t0 = clock64();
                 const bool ok = mbar_wait(&sm.empty[slot], par, a, &sm.abort_flag, 2, q);
                 blocked += clock64() - t0;
@@ -368,6 +401,36 @@ struct Producer {
         return true;
     }
 
+    // L2 prefetch of unit u of the copy sequence (u < n_layers: this CTA's weight rows of layer
+    // u; u == n_layers: the first rows of its lm_head slice), so that the ring copies of that
+    // unit hit L2 while the HBM stream keeps running through the grid-wide waits in between.
+    __device__ void prefetch_unit(int u, int G, int c) {
+        const int P = G / NKV;
+        const int g = c % NKV, p = c / NKV;
+        if (u < a.n_layers) {
+            const FusedLayer w = a.layers[u];
+            Span sp = part(QKV_ROWS, G, c);
+            prefetch_l2(w.wqkv + static_cast<size_t>(sp.r0) * D, sp.n * D * 2);
+            if (c < NKV * P) {
+                sp = part(D, P, p);
+                prefetch_l2(w.wop + static_cast<size_t>(g) * D * GRP + static_cast<size_t>(sp.r0) * GRP,
+                            sp.n * GRP * 2);
+            }
+            sp = part(H, G, c);
+            prefetch_l2(w.w1 + static_cast<size_t>(sp.r0) * D, sp.n * D * 2);
+            prefetch_l2(w.w3 + static_cast<size_t>(sp.r0) * D, sp.n * D * 2);
+            prefetch_l2(w.w2t + static_cast<size_t>(sp.r0) * D, sp.n * D * 2);
+        } else {
+            const Span sp = part(a.vocab, G, c);
+            prefetch_l2(a.lm_head + static_cast<size_t>(sp.r0) * D, min(sp.n, 96) * D * 2);
+        }
+    }
+    // Prefetches unit k of the whole call (units n_layers + 1 per step) if it exists.
+    __device__ void prefetch_ahead(int k, int G, int c) {
+        const int per = a.n_layers + 1;
+        if (a.l2_ahead > 0 && k < a.n_steps * per) prefetch_unit(k % per, G, c);
+    }
+
     __device__ void run(int G, int c) {
         pol_w = evict_first_policy();
         pol_kv = evict_last_policy();
@@ -375,13 +438,16 @@ struct Producer {
         const int P = G / NKV;
         const bool in_grp = c < NKV * P;
         const int g = c % NKV, p = c / NKV;
+        const int per = a.n_layers + 1;
         bool ok = true;
         unsigned base = 0, prev_base = 0;
         bool prev_short = true;
+        for (int k = 1; k < a.l2_ahead; ++k) prefetch_ahead(k, G, c);
         for (int st = 0; ok && st < a.n_steps; ++st) {
             const StepPos sp = step_pos(a, sp0, st);
             for (int l = 0; ok && l < a.n_layers; ++l) {
                 const FusedLayer w = a.layers[l];
+                prefetch_ahead(st * per + l + a.l2_ahead, G, c);
                 ok = ok && rows<D * 2, RPC_ROW>(w.wqkv, part(QKV_ROWS, G, c));
                 if (ok && sp.shrt && in_grp) {
                     // KV pages of this layer were last written (row kv_pos, sink rows) by the
@@ -399,6 +465,7 @@ struct Producer {
                 ok = ok && pairs(w.w1, w.w3, part(H, G, c));
                 ok = ok && rows<D * 2, RPC_ROW>(w.w2t, part(H, G, c));
             }
+            prefetch_ahead(st * per + a.n_layers + a.l2_ahead, G, c);
             ok = ok && rows<D * 2, RPC_ROW>(a.lm_head, part(a.vocab, G, c));
             prev_base = base;
             prev_short = sp.shrt;
@@ -432,17 +499,9 @@ __device__ __forceinline__ float consumer_sum(float v, Smem& sm) {
     return t;
 }
 
-// The staged activation x of a GEMV is kept as two bf16 vectors hi = bf16(x), lo = bf16(x - hi):
-// hi + lo carries 16 significant bits of each fp32 element (relative error <= 2^-17), and both
-// are multiplied against the bf16 weights by the tensor core with fp32 accumulation.
-__device__ __forceinline__ void split_bf16(float v, uint16_t& hi, uint16_t& lo) {
-    hi = f32_to_bf16(v);
-    lo = f32_to_bf16(v - bf16_to_f32(hi));
-}
-
-__device__ __forceinline__ void xs_put(Smem& sm, int e, float val) {
-    split_bf16(val, sm.xhl[0][e], sm.xhl[1][e]);
-}
+// The staged activation x of a GEMV is kept in fp32 (sm.xf) and multiplied against the bf16
+// weights on the CUDA cores with fp32 accumulation, as the reference's MatMul does.
+__device__ __forceinline__ void xs_put(Smem& sm, int e, float val) { sm.xf[e] = val; }
 
 // Stage xs = RmsNorm(x) (src/inference.cpp:887-923) for a K=1024 GEMV; thread t holds x[4t..4t+3]
 // and its norm weights wv.
@@ -450,72 +509,78 @@ __device__ __forceinline__ void stage_norm(Smem& sm, float4 xv, uint2 wv, float 
     const int t = threadIdx.x;
     const float ss = consumer_sum(xv.x * xv.x + xv.y * xv.y + xv.z * xv.z + xv.w * xv.w, sm);
     const float inv = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
-    const float y[4] = {(xv.x * inv) * bf16_lo(wv.x), (xv.y * inv) * bf16_hi(wv.x),
-                        (xv.z * inv) * bf16_lo(wv.y), (xv.w * inv) * bf16_hi(wv.y)};
-    uint16_t hi[4], lo[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) split_bf16(y[j], hi[j], lo[j]);
-    reinterpret_cast<uint2*>(sm.xhl[0])[t] =
-        make_uint2(hi[0] | (static_cast<uint32_t>(hi[1]) << 16), hi[2] | (static_cast<uint32_t>(hi[3]) << 16));
-    reinterpret_cast<uint2*>(sm.xhl[1])[t] =
-        make_uint2(lo[0] | (static_cast<uint32_t>(lo[1]) << 16), lo[2] | (static_cast<uint32_t>(lo[3]) << 16));
+    reinterpret_cast<float4*>(sm.xf)[t] =
+        make_float4((xv.x * inv) * bf16_lo(wv.x), (xv.y * inv) * bf16_hi(wv.x),
+                    (xv.z * inv) * bf16_lo(wv.y), (xv.w * inv) * bf16_hi(wv.y));
     bar_consumers();
-}
-
-// D += A . B for one m16n8k16 bf16 MMA with fp32 accumulation, A rows 8-15 zero.
-__device__ __forceinline__ void mma_16816(float d[4], uint32_t a0, uint32_t a2, uint32_t b0,
-                                          uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-        "{%8,%9}, {%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
 }
 
 // Dot products of 8 weight rows (a ring chunk, row-major, K bf16 per row, rows swizzled by row
 // parity: in odd rows the two 64-byte halves of every 128-byte block are swapped) with the staged
-// activation. The MMA's n dimension runs over the 8 rows and its m dimension holds the activation
-// (row 0 = hi, row 1 = lo, rows 2-15 zero); k is consumed 32 at a time, each lane supplying 8
-// consecutive elements of its row (the same permutation of k is applied to both operands, which
-// leaves the sum unchanged). Result: lanes 0-3 hold rows 2t and 2t+1 (t = lane) in y0, y1.
+// fp32 activation. Lane l takes the 16-byte units u = l + 32 j (j < K / 256) of every row and
+// holds the matching activation elements 8u..8u+7 in registers; a transposing butterfly over the
+// eight row sums leaves row q in lanes 4q..4q+3. Result: lanes 0-3 hold rows 2t and 2t+1
+// (t = lane) in y0, y1.
 template <int K>
-__device__ __forceinline__ void mma_rows8(const Smem& sm, const FusedArgs& a, const uint8_t* rows,
+__device__ __forceinline__ void fma_rows8(const Smem& sm, const FusedArgs& a, const uint8_t* rows,
                                           int row0, float& y0, float& y1) {
-    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const uint8_t* rp = rows + g * K * 2;
-    const int sw = ((row0 + g) & 1) << 2;
-    const uint16_t* xp = sm.xhl[g & 1];
-    const bool xlane = lane < 8;
-    float d[4][4];
+    constexpr int U = K / 256;
+    const int lane = threadIdx.x & 31;
+    float xr[U][8];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) d[i][0] = d[i][1] = d[i][2] = d[i][3] = 0.0f;
-    // mma.sync.aligned needs the whole warp converged: no branches inside the loop below (the
-    // activation fragment is loaded by every lane and zeroed by a select outside lanes 0-7).
-    __syncwarp();
-#pragma unroll 4
-    for (int kt = 0; kt < K / 32; ++kt) {
-        const int u = kt * 4 + t;  // this lane's 16-byte unit of the row
-#ifdef Q3_FUSED_CHECKS
-        const long long woff = (rp - &sm.ring[0][0]) + ((u ^ sw) << 4);
-        Q3_CHECK(woff >= 0 && woff + 16 <= static_cast<long long>(NS) * SLOT && (woff & 15) == 0,
-                 40, woff, row0, kt);
-        Q3_CHECK(u * 16 + 16 <= K * 2, 41, u, K, 0);
-#endif
-        const uint4 w = *reinterpret_cast<const uint4*>(rp + ((u ^ sw) << 4));
-        uint4 x = *reinterpret_cast<const uint4*>(xp + u * 8);
-        x.x = xlane ? x.x : 0u;
-        x.y = xlane ? x.y : 0u;
-        x.z = xlane ? x.z : 0u;
-        x.w = xlane ? x.w : 0u;
-        mma_16816(d[kt & 3], x.x, x.y, w.x, w.y);
-        mma_16816(d[kt & 3], x.z, x.w, w.z, w.w);
+    for (int j = 0; j < U; ++j) {
+        const float4 p = reinterpret_cast<const float4*>(sm.xf)[2 * (lane + 32 * j)];
+        const float4 q = reinterpret_cast<const float4*>(sm.xf)[2 * (lane + 32 * j) + 1];
+        xr[j][0] = p.x; xr[j][1] = p.y; xr[j][2] = p.z; xr[j][3] = p.w;
+        xr[j][4] = q.x; xr[j][5] = q.y; xr[j][6] = q.z; xr[j][7] = q.w;
     }
-    float s0 = (d[0][0] + d[1][0]) + (d[2][0] + d[3][0]);
-    float s1 = (d[0][1] + d[1][1]) + (d[2][1] + d[3][1]);
-    s0 += __shfl_down_sync(0xffffffffu, s0, 4);  // + the lo part (m = 1) held by lane t + 4
-    s1 += __shfl_down_sync(0xffffffffu, s1, 4);
-    y0 = s0;
-    y1 = s1;
+    float s[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+        const uint8_t* rp = rows + r * K * 2;
+        const int sw = ((row0 + r) & 1) << 2;
+        float acc0 = 0.0f, acc1 = 0.0f;
+#pragma unroll
+        for (int j = 0; j < U; ++j) {
+            const int u = (lane + 32 * j) ^ sw;
+#ifdef Q3_FUSED_CHECKS
+            const long long woff = (rp - &sm.ring[0][0]) + (u << 4);
+            Q3_CHECK(woff >= 0 && woff + 16 <= static_cast<long long>(NS) * SLOT, 40, woff, row0, j);
+#endif
+            const uint4 w = *reinterpret_cast<const uint4*>(rp + (u << 4));
+            acc0 = fmaf(bf16_lo(w.x), xr[j][0], acc0);
+            acc1 = fmaf(bf16_hi(w.x), xr[j][1], acc1);
+            acc0 = fmaf(bf16_lo(w.y), xr[j][2], acc0);
+            acc1 = fmaf(bf16_hi(w.y), xr[j][3], acc1);
+            acc0 = fmaf(bf16_lo(w.z), xr[j][4], acc0);
+            acc1 = fmaf(bf16_hi(w.z), xr[j][5], acc1);
+            acc0 = fmaf(bf16_lo(w.w), xr[j][6], acc0);
+            acc1 = fmaf(bf16_hi(w.w), xr[j][7], acc1);
+        }
+        s[r] = acc0 + acc1;
+    }
+    // Butterfly: after xor 16 / 8 / 4 each lane keeps one row, q = lane >> 2, then xor 2 / 1.
+    const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+    float t4[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float send = b4 ? s[i] : s[i + 4];
+        const float keep = b4 ? s[i + 4] : s[i];
+        t4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+    float t2[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const float send = b3 ? t4[i] : t4[i + 2];
+        const float keep = b3 ? t4[i + 2] : t4[i];
+        t2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+    float v = (b2 ? t2[1] : t2[0]) + __shfl_xor_sync(0xffffffffu, b2 ? t2[0] : t2[1], 4);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    const int t = lane & 3;
+    y0 = __shfl_sync(0xffffffffu, v, 8 * t);
+    y1 = __shfl_sync(0xffffffffu, v, 8 * t + 4);
 }
 
 __device__ __forceinline__ uint2 load_norm(const uint16_t* nw) {
@@ -533,7 +598,7 @@ __device__ __forceinline__ float4 add4(float4 a, float4 b) {
 template <int K, int rpc, int mode>
 __device__ __forceinline__ void consume_rows(Smem& sm, const FusedArgs& a, uint32_t q0, int r0,
                                              int n, float* out, int out_n) {
-    static_assert(mode == kPair ? rpc == 4 : rpc == 8, "one 8-row MMA group per chunk");
+    static_assert(mode == kPair ? rpc == 4 : rpc == 8, "one 8-row dot group per chunk");
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, t = lane & 3;
     const int nch = (n + rpc - 1) / rpc;
     float bv = -FLT_MAX;
@@ -545,7 +610,7 @@ __device__ __forceinline__ void consume_rows(Smem& sm, const FusedArgs& a, uint3
         const int rb = r0 + ci * rpc;
         const int rn = min(rpc, r0 + n - rb);
         float y0, y1;
-        mma_rows8<K>(sm, a, sm.ring[slot], rb, y0, y1);
+        fma_rows8<K>(sm, a, sm.ring[slot], rb, y0, y1);
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.empty[slot]);
         if (mode == kPair) {
@@ -571,7 +636,7 @@ __device__ __forceinline__ void consume_rows(Smem& sm, const FusedArgs& a, uint3
                 const int r = rb + i + j;
                 if (!Q3_CHECK(r >= 0 && r < out_n, 52, r, out_n, mode)) break;
                 if (mode == kStore || mode == kLogits) out[r] = yy[j];
-                if (mode == kRed) atomicAdd(out + r, yy[j]);
+                if (mode == kRed) red_add(out + r, yy[j]);
                 if (mode == kLogits && better(yy[j], r, bv, bi)) {
                     bv = yy[j];
                     bi = r;
@@ -900,8 +965,7 @@ __device__ __forceinline__ void down_splitk(Smem& sm, const FusedArgs& a, uint32
         bar_consumers();
         if (threadIdx.x == 0) mbar_arrive(&sm.empty[slot]);
     }
-    atomicAdd(reinterpret_cast<float4*>(y + warp * 128 + lane * 4),
-              make_float4(acc[0], acc[1], acc[2], acc[3]));
+    red_add4(y + warp * 128 + lane * 4, make_float4(acc[0], acc[1], acc[2], acc[3]));
 }
 
 // Write back the attention-sink rows of KV head g rotated by RoPE(position 1) (:817-827); every
@@ -943,9 +1007,19 @@ __device__ __forceinline__ int reduce_argmax(const FusedArgs& a, int G) {
     return bi == INT_MAX ? 0 : bi;
 }
 
+__device__ __forceinline__ uint8_t* smem_raw_ptr() {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    return smem_raw;
+}
+
 __device__ __forceinline__ void stamp(const FusedArgs& a, unsigned kk, int G, int c, int which) {
     if (a.prof && threadIdx.x == 0) {
-        a.prof[(static_cast<size_t>(kk) * G + c) * 8 + which] = globaltimer();
+        // Nanoseconds on the globaltimer scale, interpolated with the SM cycle counter (at the
+        // 1965 MHz maximum clock) for a resolution finer than the globaltimer's update interval.
+        Smem& sm = *reinterpret_cast<Smem*>(smem_raw_ptr());
+        const long long dc = clock64() - sm.clk0;
+        a.prof[(static_cast<size_t>(kk) * G + c) * 8 + which] =
+            sm.gt0 + static_cast<unsigned long long>(dc * 1000 / 1965);
     }
 }
 
@@ -1031,6 +1105,8 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) 
         }
         sm.abort_flag = 0;
         sm.wait_cycles = 0;
+        sm.gt0 = globaltimer();
+        sm.clk0 = clock64();
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
@@ -1067,6 +1143,7 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) 
                 const Span s = part(QKV_ROWS, G, c);
                 consume_rows<D, RPC_ROW, kStore>(sm, a, q, s.r0, s.n, a.qkv, QKV_ROWS);
                 q += chunks_of(s.n, RPC_ROW);
+                stamp(a, k, G, c, 4);
                 phase_end(sm, a, k++, G, c);
             }
             HeadPre hp;
@@ -1083,6 +1160,7 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) 
                     stamp(a, k, G, c, 3);
                     consume_rows<GRP, RPC_GRP, kRed>(sm, a, q, os.r0, os.n, xc, D);
                     q += chunks_of(os.n, RPC_GRP);
+                    stamp(a, k, G, c, 4);
                 }
                 phase_end(sm, a, k++, G, c);
             } else {
@@ -1191,7 +1269,7 @@ __global__ void permute_wo_kernel(const uint16_t* __restrict__ wo, uint16_t* __r
 
 __global__ void swizzle_rows_kernel(const uint16_t* __restrict__ src, uint16_t* __restrict__ dst,
                                     size_t rows, int K) {
-    // Odd rows: swap the two 64-byte halves of every 128-byte block (the layout mma_rows8 reads).
+    // Odd rows: swap the two 64-byte halves of every 128-byte block (the layout fma_rows8 reads).
     const size_t units = static_cast<size_t>(K) / 8;
     const size_t n = rows * units;
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
@@ -1221,6 +1299,16 @@ bool fused_supported(const q3_config& c) {
 }
 
 size_t fused_smem_bytes() { return sizeof(Smem); }
+
+int fused_l2_ahead() {
+    // Layers of L2 run-ahead; Q3_FUSED_L2_AHEAD overrides (0 turns the prefetch off).
+    static const int v = [] {
+        const char* e = getenv("Q3_FUSED_L2_AHEAD");
+        const int n = e ? atoi(e) : 1;
+        return n < 0 ? 0 : (n > 3 ? 3 : n);
+    }();
+    return v;
+}
 
 int fused_phases_per_step(int n_layers, int kv_len) {
     return n_layers * (kv_len <= T_SHORT ? 3 : 4) + 1;

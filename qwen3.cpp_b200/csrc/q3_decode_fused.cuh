@@ -56,6 +56,8 @@ struct FusedArgs {
     float eps;
     long long spin_cycles;       // bound of every wait, in SM clock cycles
     int barrier_offset;          // 0; a test sets 1 so that a grid wait can never complete
+    int l2_ahead;                // layers of weights the producer prefetches into L2 ahead of its
+                                 // ring copies (0: none)
     unsigned long long* prof;    // nullable: per (phase, CTA) globaltimer stamps [k][G][8]
     unsigned long long* dbg;     // nullable: first failed self-check (builds with Q3_FUSED_CHECKS)
 };
@@ -64,6 +66,8 @@ struct FusedArgs {
 bool fused_supported(const q3_config& c);
 int fused_grid(int device);
 size_t fused_smem_bytes();
+// Layers of weights prefetched into L2 ahead of the ring copies.
+int fused_l2_ahead();
 void launch_decode_fused(const FusedArgs& a, int grid, cudaStream_t s);
 // Phases of one decode step at kv_len (3 per layer up to 128 positions, else 4; + lm_head).
 int fused_phases_per_step(int n_layers, int kv_len);

@@ -760,6 +760,7 @@ void Model::launch_fused(int n_steps, bool forced, bool taps, long long spin_cyc
     a.eps = cfg_.norm_eps;
     a.spin_cycles = spin_cycles;
     a.barrier_offset = offset;
+    a.l2_ahead = fused_l2_ahead();
     Q3_CUDA(cudaMemsetAsync(a.bar, 0, sizeof(unsigned), e.stream()));
     launch_decode_fused(a, fused_grid_, e.stream());
 }
