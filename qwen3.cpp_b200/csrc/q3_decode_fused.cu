@@ -12,21 +12,28 @@
 // them). Eight consumer warps wait for each phase's input (a monotonic arrival counter in global
 // memory, release/acquire), stage it in shared memory with the RMSNorm fused in, and dot it with
 // the rows as they land. Three grid-wide phases per layer (four past 128 cached positions):
-//   A   x = Xprev + Y[l-1] (or the embedding row); Xcur = x; qkv = [wq;wk;wv] . RmsNorm(x)
+//   A   x = Xprev + Y[l-1] (or the embedding row); qkv = [wq;wk;wv] . RmsNorm(x)
 //       (src/inference.cpp:795-798)
 //   BC  CTA (g, p) of KV head g: QK-RMSNorm + RoPE (:800-810), bf16 K/V write at kv_pos
 //       (:812-815), attention over the KV pages streamed through the ring with the sink rows
-//       re-rotated on the fly (:817-844), then rows p of wo[:, 256g:256g+256] . attn_g added into
-//       Xcur (split-K o_proj, x += proj, :846-849)
+//       re-rotated on the fly (:817-844), then rows p of wo[:, 256g:256g+256] . attn_g, the
+//       group-g partial of the o_proj (:846-849)
 //   (past 128 positions: B = split-K attention partials read through L2, C = combine + the same
-//    split-K o_proj)
-//   DE  h_i = silu(w1_i . xn) * (w3_i . xn) for this CTA's MLP indices i, then
-//       Y[l] += sum_i h_i * w2[:, i] (split-K down_proj, :851, :1005-1015, :863-865); the
-//       attention-sink rows are written back rotated (:817-827)
+//    o_proj partial)
+//   DE  Xcur = x + sum_g partial_g (x += proj, :849), h_i = silu(w1_i . xn) * (w3_i . xn) for this
+//       CTA's MLP indices i, then Y[l] += sum_i h_i * w2[:, i] (split-K down_proj, :851,
+//       :1005-1015, :863-865); the attention-sink rows are written back rotated (:817-827)
 // then the final RmsNorm + lm_head with a per-CTA argmax; every CTA reduces the (value, index)
 // pairs itself (lowest index wins ties) for the next step's embedding row.
 //
-// Split-K sums use fp32 atomics, so the order of the fp32 additions varies from run to run.
+// Hand-offs. Only DE (and B, past 128 positions) and the lm_head end with a grid-wide arrival
+// counter. A -> BC and BC -> DE hand their outputs over as tagged 64-bit words (fp32 bits | the
+// (launch, step, layer) tag), each written once and polled by its readers until the tag matches:
+// one L2 round trip instead of a release, a counter and a reload. Every thread keeps its four
+// elements of the residual stream in registers from phase to phase.
+//
+// The down_proj split-K sums use fp32 atomics, so the order of those fp32 additions varies from
+// run to run; the o_proj partials are summed in group order.
 //
 // Every wait is bounded (clock64): on timeout the kernel sets *err, stops issuing copies, waits
 // for the copies already issued and returns; the host reports Q3_ERR_DEVICE_TIMEOUT.
@@ -48,11 +55,15 @@ constexpr int NCW = 8;                 // consumer warps
 constexpr int NCT = NCW * 32;          // consumer threads
 constexpr int NT = NCT + 32;           // + one producer warp
 constexpr int NS = 8;                  // ring slots
+constexpr int kProducerSleepNs = 256;  // back-off of the producer while the ring is full
 constexpr int SLOT = 16384;            // bytes per slot
-// Chunk q lives in slot q % NS and, in warp-owned tasks, is consumed by warp q % NCW. With NS a
-// multiple of NCW every use of a slot inside such a task belongs to the same warp, which consumes
-// them in order: no warp can wait on use n of a slot while use n-1 is still unconsumed (a parity
-// wait for use n would then be satisfied by the completion of use n-2).
+// Chunk q lives in slot q % NS and, in warp-owned tasks, is consumed by warp q % NCW; shared
+// chunks (KV pages, w2t rows) are read by every consumer warp. A slot is free again after NCW
+// arrivals: the owner warp arrives with count NCW, each warp once for a shared chunk. With NS a
+// multiple of NCW every use of a slot inside a warp-owned task belongs to the same warp, every
+// warp consumes its chunks in order, and every shared section starts after a consumer barrier, so
+// no warp can wait on use n of a slot before use n-1 was filled (a parity wait for use n would
+// then be satisfied by the completion of use n-2).
 static_assert(NS % 8 == 0, "ring slots must be a multiple of the consumer warps");
 // Rows per ring chunk: one 8-row dot group (fma_rows8) per chunk.
 constexpr int RPC_ROW = 8;             // 1024-element rows ([wq;wk;wv], lm_head, w2t)
@@ -62,7 +73,7 @@ constexpr int T_SHORT = 128;           // KV positions up to which attention run
 constexpr int ATT_TOK = 24;            // positions staged per sub-chunk (long contexts)
 constexpr int PAGE_BYTES = kPageTokens * HD * 2;
 
-enum Mode : int { kStore = 0, kRed = 1, kPair = 2, kLogits = 3 };
+enum Mode : int { kTag = 0, kPair = 2, kLogits = 3 };
 
 struct __align__(128) Smem {
     uint8_t ring[NS][SLOT];
@@ -99,6 +110,10 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* b, uint32_t byte
 }
 __device__ __forceinline__ void mbar_arrive(uint64_t* b) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_n(uint64_t* b, uint32_t n) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(n)
+                 : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
     uint32_t ok;
@@ -153,12 +168,23 @@ __device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
     }
 }
 // Fire-and-forget fp32 additions in L2 (no value returned, the thread does not wait).
-__device__ __forceinline__ void red_add(float* p, float v) {
-    asm volatile("red.relaxed.gpu.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
-}
 __device__ __forceinline__ void red_add4(float* p, float4 v) {
     asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x),
                  "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+// Tagged hand-off words: fp32 bits in the low half, the producing (launch, step, layer) tag in the
+// high half, written and read as single 64-bit accesses (a reader that sees the tag sees the
+// value written with it).
+__device__ __forceinline__ void st_tagged(unsigned long long* p, float v, unsigned tag) {
+    const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ void ld_tagged2(const unsigned long long* p, unsigned long long& w0,
+                                           unsigned long long& w1) {
+    asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];"
+                 : "=l"(w0), "=l"(w1)
+                 : "l"(p)
                  : "memory");
 }
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
@@ -212,12 +238,15 @@ __device__ __noinline__ void dbg_report(const FusedArgs& a, unsigned long long c
 
 // ------------------------------------------------------------------ bounded waits
 
+// sleep_ns > 0: back off between probes (a waiting thread then takes almost no issue slots from
+// the warps that share its scheduler).
 __device__ bool mbar_wait(uint64_t* b, uint32_t parity, const FusedArgs& a, volatile int* abort,
-                          int site = 0, long long info = 0) {
+                          int site = 0, long long info = 0, int sleep_ns = 0) {
     if (mbar_try_wait(b, parity)) return true;
     const long long t0 = clock64();
     for (uint32_t it = 0;; ++it) {
         if (mbar_try_wait(b, parity)) return true;
+        if (sleep_ns > 0) __nanosleep(sleep_ns);
         if ((it & 31) == 31) {
             if (*abort) return false;
             if (clock64() - t0 > a.spin_cycles) {
@@ -228,6 +257,42 @@ __device__ bool mbar_wait(uint64_t* b, uint32_t parity, const FusedArgs& a, vola
             }
         }
     }
+}
+
+// Tag of the hand-offs of layer l in step st of this launch.
+__device__ __forceinline__ unsigned step_tag(const FusedArgs& a, int st, int l) {
+    return ((a.epoch & 0xFFFu) << 20) | (static_cast<unsigned>(st * a.n_layers + l) & 0xFFFFFu);
+}
+
+// Bounded wait until the four tagged words at p (32-byte aligned) carry `tag`; their values.
+__device__ float4 poll4(const FusedArgs& a, const unsigned long long* p, unsigned tag,
+                        volatile int* abort, int site) {
+    unsigned long long w0, w1, w2, w3;
+    const long long t0 = clock64();
+    for (uint32_t it = 0;; ++it) {
+        ld_tagged2(p, w0, w1);
+        ld_tagged2(p + 2, w2, w3);
+        if (static_cast<unsigned>(w0 >> 32) == tag && static_cast<unsigned>(w1 >> 32) == tag &&
+            static_cast<unsigned>(w2 >> 32) == tag && static_cast<unsigned>(w3 >> 32) == tag) {
+            break;
+        }
+        if ((it & 15) == 15) {
+            if (*abort || *reinterpret_cast<volatile unsigned*>(a.err) != 0u) {
+                *abort = 1;
+                break;
+            }
+            if (clock64() - t0 > a.spin_cycles) {
+                *abort = 1;
+                atomicOr(a.err, 1u);
+                Q3_CHECK(false, 3000 + site, tag, static_cast<long long>(w0 >> 32), 0);
+                break;
+            }
+        }
+    }
+    return make_float4(__uint_as_float(static_cast<unsigned>(w0)),
+                       __uint_as_float(static_cast<unsigned>(w1)),
+                       __uint_as_float(static_cast<unsigned>(w2)),
+                       __uint_as_float(static_cast<unsigned>(w3)));
 }
 
 // Wait until `target` CTA arrivals are visible on the grid counter.
@@ -321,8 +386,9 @@ __device__ __forceinline__ StepPos step_pos(const FusedArgs& a, const StepParams
     return p;
 }
 
-__device__ __forceinline__ int phases_of(const FusedArgs& a, bool shrt) {
-    return a.n_layers * (shrt ? 3 : 4) + 1;
+// Grid arrivals of one step: after every DE (and every B past 128 positions) and the lm_head.
+__device__ __forceinline__ int barriers_of(const FusedArgs& a, bool shrt) {
+    return a.n_layers * (shrt ? 1 : 2) + 1;
 }
 
 // ------------------------------------------------------------------ producer
@@ -351,10 +417,10 @@ struct Producer {
             const uint32_t par = ((q / NS) - 1) & 1;
             if (a.prof && !mbar_test_wait(&sm.empty[slot], par)) {
                 const long long t0 = clock64();
-                const bool ok = mbar_wait(&sm.empty[slot], par, a, &sm.abort_flag, 2, q);
+                const bool ok = mbar_wait(&sm.empty[slot], par, a, &sm.abort_flag, 2, q, kProducerSleepNs);
                 blocked += clock64() - t0;
                 if (!ok) return false;
-            } else if (!mbar_wait(&sm.empty[slot], par, a, &sm.abort_flag, 2, q)) {
+            } else if (!mbar_wait(&sm.empty[slot], par, a, &sm.abort_flag, 2, q, kProducerSleepNs)) {
                 return false;
             }
         }
@@ -453,7 +519,7 @@ struct Producer {
                     // KV pages of this layer were last written (row kv_pos, sink rows) by the
                     // previous step's phases up to DE(l): wait until every CTA is past them.
                     if (st > 0) {
-                        const unsigned de = prev_base + l * (prev_short ? 3 : 4) + (prev_short ? 2 : 3);
+                        const unsigned de = prev_base + (prev_short ? l : 2 * l + 1);
                         ok = grid_wait(a, G * (de + 1) + a.barrier_offset, &sm.abort_flag, 3);
                     }
                     ok = ok && kv_pages(l, g, sp.kv_len);
@@ -469,7 +535,7 @@ struct Producer {
             ok = ok && rows<D * 2, RPC_ROW>(a.lm_head, part(a.vocab, G, c));
             prev_base = base;
             prev_short = sp.shrt;
-            base += phases_of(a, sp.shrt);
+            base += barriers_of(a, sp.shrt);
         }
         if (a.prof) a.prof[static_cast<size_t>(c) * 8 + 4] = blocked;
         // Wait for every copy still in flight before the CTA may exit.
@@ -592,12 +658,15 @@ __device__ __forceinline__ float4 add4(float4 a, float4 b) {
 }
 
 // Dot the rows of this CTA's warp-owned chunks of one task (chunks q0.. of `rpc` rows of K
-// elements) with the staged activation, epilogue by `mode`. kLogits leaves each warp's best
-// (value, index) in sm.best. After an abort the remaining chunks are skipped (each wait then fails
-// at once) but the warp still returns, so every consumer thread reaches the same barriers.
+// elements) with the staged activation, epilogue by `mode`: kTag writes row r as a tagged word to
+// outt[r], kPair h to out[], kLogits the logits to out[] and leaves each warp's best (value, index)
+// in sm.best. After an abort the remaining chunks are skipped (each wait then fails at once) but
+// the warp still returns, so every consumer thread reaches the same barriers.
 template <int K, int rpc, int mode>
 __device__ __forceinline__ void consume_rows(Smem& sm, const FusedArgs& a, uint32_t q0, int r0,
-                                             int n, float* out, int out_n) {
+                                             int n, float* out, int out_n,
+                                             unsigned long long* outt = nullptr,
+                                             unsigned tag = 0) {
     static_assert(mode == kPair ? rpc == 4 : rpc == 8, "one 8-row dot group per chunk");
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, t = lane & 3;
     const int nch = (n + rpc - 1) / rpc;
@@ -612,7 +681,7 @@ __device__ __forceinline__ void consume_rows(Smem& sm, const FusedArgs& a, uint3
         float y0, y1;
         fma_rows8<K>(sm, a, sm.ring[slot], rb, y0, y1);
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.empty[slot]);
+        if (lane == 0) mbar_arrive_n(&sm.empty[slot], NCW);  // a warp-owned chunk
         if (mode == kPair) {
             // Rows 0-3 of the group are w1 rows rb..rb+3 (lanes 0-1), rows 4-7 the w3 rows
             // (lanes 2-3): h = silu(gate) * up (src/inference.cpp:1009-1011).
@@ -635,8 +704,8 @@ __device__ __forceinline__ void consume_rows(Smem& sm, const FusedArgs& a, uint3
                 if (i + j >= rn) break;
                 const int r = rb + i + j;
                 if (!Q3_CHECK(r >= 0 && r < out_n, 52, r, out_n, mode)) break;
-                if (mode == kStore || mode == kLogits) out[r] = yy[j];
-                if (mode == kRed) red_add(out + r, yy[j]);
+                if (mode == kLogits) out[r] = yy[j];
+                if (mode == kTag) st_tagged(outt + r, yy[j], tag);
                 if (mode == kLogits && better(yy[j], r, bv, bi)) {
                     bv = yy[j];
                     bi = r;
@@ -712,11 +781,11 @@ __device__ __forceinline__ void head_preload(HeadPre& hp, const FusedArgs& a, co
 // sm.qk[0..2]; v head g into sm.qk[3]; k and v rounded to bf16 as the cache stores them (:812-815)
 // and, when `writer`, written to the cache at kv_pos. Ends with a consumer barrier.
 __device__ __forceinline__ void prep_heads(Smem& sm, const FusedArgs& a, const HeadPre& hp, int l,
-                                        int g, int kv_pos, bool writer) {
+                                        int g, int kv_pos, bool writer, unsigned tag) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (warp < 3) {
-        const float* src = warp < 2 ? a.qkv + (2 * g + warp) * HD : a.qkv + QD + g * HD;
-        const float4 e = __ldcg(reinterpret_cast<const float4*>(src) + lane);
+        const unsigned long long* src = warp < 2 ? a.qkvt + (2 * g + warp) * HD : a.qkvt + QD + g * HD;
+        const float4 e = poll4(a, src + 4 * lane, tag, &sm.abort_flag, 1);
         const float ss = warp_sum(e.x * e.x + e.y * e.y + e.z * e.z + e.w * e.w);
         const float inv = 1.0f / sqrtf(ss / static_cast<float>(HD) + a.eps);
         float y[4] = {(e.x * inv) * bf16_lo(hp.nw.x), (e.y * inv) * bf16_hi(hp.nw.x),
@@ -732,7 +801,7 @@ __device__ __forceinline__ void prep_heads(Smem& sm, const FusedArgs& a, const H
         }
         reinterpret_cast<float4*>(sm.qk[warp])[lane] = make_float4(y[0], y[1], y[2], y[3]);
     } else if (warp == 3) {
-        const float4 e = __ldcg(reinterpret_cast<const float4*>(a.qkv + QD + KVD + g * HD) + lane);
+        const float4 e = poll4(a, a.qkvt + QD + KVD + g * HD + 4 * lane, tag, &sm.abort_flag, 2);
         float y[4] = {e.x, e.y, e.z, e.w};
         const uint2 vb = pack_bf16x4(y);
         unpack_bf16x4(vb, y);
@@ -780,6 +849,49 @@ __device__ __forceinline__ void acc_add(AttnAcc& s, const float k4[4], const flo
     for (int j = 0; j < 4; ++j) {
         s.o0[j] = s.o0[j] * a0 + p0 * v4[j];
         s.o1[j] = s.o1[j] * a1 + p1 * v4[j];
+    }
+    s.m0 = n0;
+    s.m1 = n1;
+}
+
+// Two cached positions a, b (b only when has_b) in one online-softmax update: the four dot
+// products and their warp reductions are independent, and the running state is rescaled once.
+__device__ __forceinline__ void acc_add2(AttnAcc& s, const float ka[4], const float va[4],
+                                         const float kb[4], const float vb[4], bool has_b,
+                                         float4 q0, float4 q1) {
+    const float sq = 11.313708498984761f;  // sqrtf(128), the reference's sqrtf(head_dim)
+    float da0 = ka[0] * q0.x, da1 = ka[0] * q1.x, db0 = kb[0] * q0.x, db1 = kb[0] * q1.x;
+    da0 = fmaf(ka[1], q0.y, da0);
+    da1 = fmaf(ka[1], q1.y, da1);
+    db0 = fmaf(kb[1], q0.y, db0);
+    db1 = fmaf(kb[1], q1.y, db1);
+    da0 = fmaf(ka[2], q0.z, da0);
+    da1 = fmaf(ka[2], q1.z, da1);
+    db0 = fmaf(kb[2], q0.z, db0);
+    db1 = fmaf(kb[2], q1.z, db1);
+    da0 = fmaf(ka[3], q0.w, da0);
+    da1 = fmaf(ka[3], q1.w, da1);
+    db0 = fmaf(kb[3], q0.w, db0);
+    db1 = fmaf(kb[3], q1.w, db1);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        da0 += __shfl_xor_sync(0xffffffffu, da0, o);
+        da1 += __shfl_xor_sync(0xffffffffu, da1, o);
+        db0 += __shfl_xor_sync(0xffffffffu, db0, o);
+        db1 += __shfl_xor_sync(0xffffffffu, db1, o);
+    }
+    const float sa0 = da0 / sq, sa1 = da1 / sq;
+    const float sb0 = has_b ? db0 / sq : -FLT_MAX, sb1 = has_b ? db1 / sq : -FLT_MAX;
+    const float n0 = fmaxf(s.m0, fmaxf(sa0, sb0)), n1 = fmaxf(s.m1, fmaxf(sa1, sb1));
+    const float a0 = expf(s.m0 - n0), a1 = expf(s.m1 - n1);
+    const float pa0 = expf(sa0 - n0), pa1 = expf(sa1 - n1);
+    const float pb0 = has_b ? expf(sb0 - n0) : 0.0f, pb1 = has_b ? expf(sb1 - n1) : 0.0f;
+    s.l0 = (s.l0 * a0 + pa0) + pb0;
+    s.l1 = (s.l1 * a1 + pa1) + pb1;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        s.o0[j] = (s.o0[j] * a0 + pa0 * va[j]) + pb0 * vb[j];
+        s.o1[j] = (s.o1[j] * a1 + pa1 * va[j]) + pb1 * vb[j];
     }
     s.m0 = n0;
     s.m1 = n1;
@@ -863,19 +975,23 @@ __device__ __forceinline__ void attention_short(Smem& sm, const FusedArgs& a, co
         const uint32_t qq = q0 + j;
         const int slot = qq % NS;
         if (warp_wait_full(sm, slot, (qq / NS) & 1, a)) {
+            static_assert(kPageTokens == 2 * NCW, "two positions of a page per warp");
             const uint8_t* page = sm.ring[slot];
-            for (int tt = warp; tt < kPageTokens; tt += NCW) {
-                const int t = j * kPageTokens + tt;
-                if (t >= kv_len) break;
-                const uint2 kk = reinterpret_cast<const uint2*>(page + tt * HD * 2)[lane];
-                const uint2 vv = reinterpret_cast<const uint2*>(page + PAGE_BYTES + tt * HD * 2)[lane];
-                float k4[4], v4[4];
-                kv_lane(sm, hp, t, kv_pos, num_sink, kk, vv, k4, v4);
-                acc_add(acc, k4, v4, q0v, q1v);
+            const int ta = j * kPageTokens + warp, tb = ta + NCW;
+            if (ta < kv_len) {
+                const uint2 ka = reinterpret_cast<const uint2*>(page + warp * HD * 2)[lane];
+                const uint2 va = reinterpret_cast<const uint2*>(page + PAGE_BYTES + warp * HD * 2)[lane];
+                const int ub = tb < kv_len ? warp + NCW : warp;
+                const uint2 kb = reinterpret_cast<const uint2*>(page + ub * HD * 2)[lane];
+                const uint2 vb = reinterpret_cast<const uint2*>(page + PAGE_BYTES + ub * HD * 2)[lane];
+                float k4[4], v4[4], k4b[4], v4b[4];
+                kv_lane(sm, hp, ta, kv_pos, num_sink, ka, va, k4, v4);
+                kv_lane(sm, hp, tb < kv_len ? tb : ta, kv_pos, num_sink, kb, vb, k4b, v4b);
+                acc_add2(acc, k4, v4, k4b, v4b, tb < kv_len, q0v, q1v);
             }
         }
-        bar_consumers();
-        if (threadIdx.x == 0) mbar_arrive(&sm.empty[slot]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.empty[slot]);  // one of NCW releases of a shared chunk
     }
     merge_warps(sm, a, acc, g, 0, false);
 }
@@ -962,8 +1078,8 @@ __device__ __forceinline__ void down_splitk(Smem& sm, const FusedArgs& a, uint32
                 acc[3] = fmaf(hv, bf16_hi(wv.y), acc[3]);
             }
         }
-        bar_consumers();
-        if (threadIdx.x == 0) mbar_arrive(&sm.empty[slot]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.empty[slot]);  // one of NCW releases of a shared chunk
     }
     red_add4(y + warp * 128 + lane * 4, make_float4(acc[0], acc[1], acc[2], acc[3]));
 }
@@ -1023,12 +1139,14 @@ __device__ __forceinline__ void stamp(const FusedArgs& a, unsigned kk, int G, in
     }
 }
 
-// Phase entry: thread 0 waits until every CTA has arrived for phases < k and publishes one
-// verdict that all consumer threads read after the same barrier (so all leave together on abort).
-__device__ __forceinline__ bool phase_begin(Smem& sm, const FusedArgs& a, unsigned k, int G, int c) {
+// Phase entry: with nb > 0 thread 0 waits until every CTA has made nb arrivals; in any case one
+// verdict (no abort so far) is published to all consumer threads after the same barrier, so
+// that all leave together on abort.
+__device__ __forceinline__ bool phase_begin(Smem& sm, const FusedArgs& a, unsigned k, unsigned nb,
+                                            int G, int c) {
     stamp(a, k, G, c, 0);
     if (threadIdx.x == 0) {
-        const bool ok = k == 0 || grid_wait(a, G * k + a.barrier_offset, &sm.abort_flag, 4);
+        const bool ok = nb == 0 || grid_wait(a, G * nb + a.barrier_offset, &sm.abort_flag, 4);
         sm.go = ok && sm.abort_flag == 0;
     }
     bar_consumers();
@@ -1036,13 +1154,15 @@ __device__ __forceinline__ bool phase_begin(Smem& sm, const FusedArgs& a, unsign
     return sm.go != 0;
 }
 
-// Phase exit: all consumer threads are done with phase k; thread 0 arrives (release).
-__device__ __forceinline__ void phase_end(Smem& sm, const FusedArgs& a, unsigned k, int G, int c) {
+// Phase exit: all consumer threads are done with phase k; with `arrive` thread 0 adds this CTA's
+// arrival on the grid counter (release).
+__device__ __forceinline__ void phase_end(Smem& sm, const FusedArgs& a, unsigned k, bool arrive,
+                                          int G, int c) {
     stamp(a, k, G, c, 6);
     bar_consumers();
     stamp(a, k, G, c, 7);
     if (threadIdx.x == 0) {
-        red_release_add(a.bar, 1u);
+        if (arrive) red_release_add(a.bar, 1u);
         if (a.prof) {
             // Summed ring-wait cycles of all consumer warps in this phase.
             a.prof[(static_cast<size_t>(k) * G + c) * 8 + 5] = sm.wait_cycles;
@@ -1052,10 +1172,12 @@ __device__ __forceinline__ void phase_end(Smem& sm, const FusedArgs& a, unsigned
 }
 
 // Phase A input: the embedding row of the step's token (layer 0; the token is the greedy argmax of
-// the previous step, or the teacher-forced one) or x = Xprev + Y[l-1]; writes this CTA's slice of
-// Xcur and (CTA 0) the debug tap. Returns this thread's 4 elements.
+// the previous step, or the teacher-forced one) or x = Xcur + Y[l-1], with Xcur this thread's four
+// elements of the residual stream after the previous layer's o_proj (kept in registers) and yb the
+// step's down-projection accumulators; writes (CTA 0) the debug tap. Returns this thread's
+// four elements of x.
 __device__ __forceinline__ float4 phase_a_input(Smem& sm, const FusedArgs& a, const StepParams& sp0,
-                                             int st, int l, float* xc, const float* xp, int G,
+                                             int st, int l, float4 xcur, const float* yb, int G,
                                              int c) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     float4 xv;
@@ -1074,22 +1196,31 @@ __device__ __forceinline__ float4 phase_a_input(Smem& sm, const FusedArgs& a, co
         const uint2 e = __ldg(reinterpret_cast<const uint2*>(
                                   a.embed + static_cast<size_t>(sm.token) * D) + tid);
         xv = make_float4(bf16_lo(e.x), bf16_hi(e.x), bf16_lo(e.y), bf16_hi(e.y));
-        // Zero this CTA's share of the down-projection accumulators for the step.
+        // Zero this CTA's share of the other step parity's down-projection accumulators: their
+        // last readers arrived at the previous step's lm_head barrier, their next writers (next
+        // step) come after this step's.
+        float* yz = a.ybuf + static_cast<size_t>((st + 1) & 1) * a.n_layers * D;
         const Span ys = part(a.n_layers * D, G, c);
-        for (int i = tid; i < ys.n; i += NCT) a.ybuf[ys.r0 + i] = 0.0f;
+        for (int i = tid; i < ys.n; i += NCT) yz[ys.r0 + i] = 0.0f;
     } else {
-        xv = add4(__ldcg(reinterpret_cast<const float4*>(xp) + tid),
-                  __ldcg(reinterpret_cast<const float4*>(a.ybuf + (l - 1) * D) + tid));
-    }
-    const Span xs = part(D, G, c);
-    const float e4[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int r = 4 * tid + j;
-        if (r >= xs.r0 && r < xs.r0 + xs.n) xc[r] = e4[j];
+        xv = add4(xcur, __ldcg(reinterpret_cast<const float4*>(yb + static_cast<size_t>(l - 1) * D) + tid));
     }
     if (a.taps && c == 0) reinterpret_cast<float4*>(a.taps + static_cast<size_t>(l) * D)[tid] = xv;
     return xv;
+}
+
+// Xcur = x + sum_g partial_g over the eight KV-head groups (in group order), this thread's four
+// elements, from the tagged o_proj partials of phase BC / C.
+__device__ __forceinline__ float4 gather_oproj(Smem& sm, const FusedArgs& a, float4 xv,
+                                               unsigned tag) {
+    float4 proj = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+    for (int gg = 0; gg < NKV; ++gg) {
+        const float4 p = poll4(a, a.opart + static_cast<size_t>(gg) * D + 4 * threadIdx.x, tag,
+                               &sm.abort_flag, 3);
+        proj = add4(proj, p);
+    }
+    return add4(xv, proj);
 }
 
 __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) {
@@ -1101,7 +1232,7 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) 
     if (tid == 0) {
         for (int i = 0; i < NS; ++i) {
             mbar_init(&sm.full[i], 1);
-            mbar_init(&sm.empty[i], 1);
+            mbar_init(&sm.empty[i], NCW);  // every consumer warp releases each chunk
         }
         sm.abort_flag = 0;
         sm.wait_cycles = 0;
@@ -1124,91 +1255,96 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) 
     const int P = G / NKV;
     const bool in_grp = c < NKV * P;
     const int g = c % NKV, gp = c / NKV;
-    unsigned k = 0;  // global phase index
-    uint32_t q = 0;  // ring chunk index
+    unsigned k = 0;   // global phase index (profiling stamps)
+    unsigned nb = 0;  // grid arrivals every CTA has made so far
+    uint32_t q = 0;   // ring chunk index
+    float4 xcur = make_float4(0.0f, 0.0f, 0.0f, 0.0f);  // Xcur, this thread's 4 elements
 
     for (int st = 0; st < a.n_steps; ++st) {
         const StepPos p = step_pos(a, sp0, st);
+        float* yb = a.ybuf + static_cast<size_t>(st & 1) * a.n_layers * D;
         for (int l = 0; l < a.n_layers; ++l) {
             const FusedLayer w = a.layers[l];
-            float* xc = a.xbuf + (l & 1) * D;
-            const float* xp = a.xbuf + ((l & 1) ^ 1) * D;
-            // ---- A: x -> Xcur, RmsNorm -> [wq;wk;wv]
+            const unsigned tag = step_tag(a, st, l);
+            // ---- A: x = Xcur + Y[l-1], RmsNorm -> [wq;wk;wv] (tagged)
+            float4 xv;
             {
                 const uint2 nw = load_norm(w.attn_norm);
-                if (!phase_begin(sm, a, k, G, c)) return;
-                const float4 xv = phase_a_input(sm, a, sp0, st, l, xc, xp, G, c);
+                if (!phase_begin(sm, a, k, nb, G, c)) return;
+                xv = phase_a_input(sm, a, sp0, st, l, xcur, yb, G, c);
                 stage_norm(sm, xv, nw, a.eps);
                 stamp(a, k, G, c, 3);
                 const Span s = part(QKV_ROWS, G, c);
-                consume_rows<D, RPC_ROW, kStore>(sm, a, q, s.r0, s.n, a.qkv, QKV_ROWS);
+                consume_rows<D, RPC_ROW, kTag>(sm, a, q, s.r0, s.n, nullptr, QKV_ROWS, a.qkvt, tag);
                 q += chunks_of(s.n, RPC_ROW);
                 stamp(a, k, G, c, 4);
-                phase_end(sm, a, k++, G, c);
+                phase_end(sm, a, k++, false, G, c);
             }
             HeadPre hp;
             head_preload(hp, a, w, p.pos);
             const Span os = part(D, P, gp);
+            unsigned long long* opart_g = a.opart + static_cast<size_t>(g) * D;
             if (p.shrt) {
-                // ---- BC: attention of KV head g from the ring, split-K o_proj into Xcur
-                if (!phase_begin(sm, a, k, G, c)) return;
+                // ---- BC: attention of KV head g from the ring, o_proj partial of group g
+                if (!phase_begin(sm, a, k, 0, G, c)) return;
                 if (in_grp) {
-                    prep_heads(sm, a, hp, l, g, p.kv_pos, gp == 0);
+                    prep_heads(sm, a, hp, l, g, p.kv_pos, gp == 0, tag);
                     stamp(a, k, G, c, 2);
                     attention_short(sm, a, hp, p.kv_len, p.kv_pos, p.num_sink, g, q);
                     q += chunks_of(p.kv_len, kPageTokens);
                     stamp(a, k, G, c, 3);
-                    consume_rows<GRP, RPC_GRP, kRed>(sm, a, q, os.r0, os.n, xc, D);
+                    consume_rows<GRP, RPC_GRP, kTag>(sm, a, q, os.r0, os.n, nullptr, D, opart_g, tag);
                     q += chunks_of(os.n, RPC_GRP);
                     stamp(a, k, G, c, 4);
                 }
-                phase_end(sm, a, k++, G, c);
+                phase_end(sm, a, k++, false, G, c);
             } else {
                 // ---- B: split-K attention partials
-                if (!phase_begin(sm, a, k, G, c)) return;
+                if (!phase_begin(sm, a, k, 0, G, c)) return;
                 if (c < NKV * p.splits) {
                     const int gg = c % NKV, s = c / NKV;
                     const int chunk = (p.kv_len + p.splits - 1) / p.splits;
                     const bool own =
                         p.kv_pos >= s * chunk && p.kv_pos < min(p.kv_len, (s + 1) * chunk);
-                    prep_heads(sm, a, hp, l, gg, p.kv_pos, own);
+                    prep_heads(sm, a, hp, l, gg, p.kv_pos, own, tag);
                     attention_long(sm, a, hp, p.kv_len, p.kv_pos, p.num_sink, p.splits, l, gg, s);
                 }
-                phase_end(sm, a, k++, G, c);
-                // ---- C: combine + split-K o_proj into Xcur
-                if (!phase_begin(sm, a, k, G, c)) return;
+                phase_end(sm, a, k++, true, G, c);
+                ++nb;
+                // ---- C: combine + o_proj partial of group g
+                if (!phase_begin(sm, a, k, nb, G, c)) return;
                 if (in_grp) {
                     combine_group(sm, a, p.splits, g);
-                    consume_rows<GRP, RPC_GRP, kRed>(sm, a, q, os.r0, os.n, xc, D);
+                    consume_rows<GRP, RPC_GRP, kTag>(sm, a, q, os.r0, os.n, nullptr, D, opart_g, tag);
                     q += chunks_of(os.n, RPC_GRP);
                 }
-                phase_end(sm, a, k++, G, c);
+                phase_end(sm, a, k++, false, G, c);
             }
-            // ---- DE: RmsNorm -> silu(w1 .) * (w3 .) -> split-K down into Y[l]
+            // ---- DE: Xcur = x + o_proj, RmsNorm -> silu(w1 .) * (w3 .) -> split-K down into Y[l]
             {
                 const uint2 mw = load_norm(w.mlp_norm);
-                if (!phase_begin(sm, a, k, G, c)) return;
-                stage_norm(sm, __ldcg(reinterpret_cast<const float4*>(xc) + tid), mw, a.eps);
+                if (!phase_begin(sm, a, k, 0, G, c)) return;
+                xcur = gather_oproj(sm, a, xv, tag);
+                stage_norm(sm, xcur, mw, a.eps);
                 stamp(a, k, G, c, 2);
                 const Span hs = part(H, G, c);
                 consume_rows<D, RPC_PAIR, kPair>(sm, a, q, hs.r0, hs.n, sm.hbuf, 64);
                 q += chunks_of(hs.n, RPC_PAIR);
                 bar_consumers();
                 stamp(a, k, G, c, 3);
-                down_splitk(sm, a, q, hs.n, a.ybuf + static_cast<size_t>(l) * D);
+                down_splitk(sm, a, q, hs.n, yb + static_cast<size_t>(l) * D);
                 q += chunks_of(hs.n, RPC_ROW);
                 stamp(a, k, G, c, 4);
                 if (c < NKV && p.num_sink > 0) sink_writeback(a, hp, l, c, p.num_sink);
-                phase_end(sm, a, k++, G, c);
+                phase_end(sm, a, k++, true, G, c);
+                ++nb;
             }
         }
         // ---- final RmsNorm + lm_head + per-CTA argmax
         const uint2 fw = load_norm(a.final_norm);
-        if (!phase_begin(sm, a, k, G, c)) return;
-        const float* xl = a.xbuf + ((a.n_layers - 1) & 1) * D;
-        const float4 xv = add4(__ldcg(reinterpret_cast<const float4*>(xl) + tid),
-                               __ldcg(reinterpret_cast<const float4*>(
-                                          a.ybuf + static_cast<size_t>(a.n_layers - 1) * D) + tid));
+        if (!phase_begin(sm, a, k, nb, G, c)) return;
+        const float4 xv = add4(xcur, __ldcg(reinterpret_cast<const float4*>(
+                                               yb + static_cast<size_t>(a.n_layers - 1) * D) + tid));
         if (a.taps && c == 0) {
             reinterpret_cast<float4*>(a.taps + static_cast<size_t>(a.n_layers) * D)[tid] = xv;
         }
@@ -1230,12 +1366,13 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) 
             }
             a.am_part[c] = make_float2(bv, __int_as_float(bi));
         }
-        phase_end(sm, a, k++, G, c);
+        phase_end(sm, a, k++, true, G, c);
+        ++nb;
     }
 
     // Final greedy token and the device-side advance of the step parameters (CTA 0).
     if (c == 0) {
-        if (!phase_begin(sm, a, k, G, c)) return;
+        if (!phase_begin(sm, a, k, nb, G, c)) return;
         if (warp == 0) {
             const int best = reduce_argmax(a, G);
             if (lane == 0) {

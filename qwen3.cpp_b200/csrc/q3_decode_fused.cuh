@@ -39,9 +39,11 @@ struct FusedArgs {
     const int32_t* page_table;
     const float2* rope;          // [rope_len][64] (cos, sin)
     int rope_len;
-    float* xbuf;                 // [2][1024] residual stream (ping-pong)
-    float* ybuf;                 // [n_layers][1024] down-projection accumulators
-    float* qkv;                  // [4096]
+    float* ybuf;                 // [2][n_layers][1024] down-projection accumulators (by step
+                                 // parity; parity 0 zero at launch)
+    unsigned long long* qkvt;    // [4096] q|k|v, tagged (value bits | tag << 32)
+    unsigned long long* opart;   // [8][1024] o_proj partial of each KV-head group, tagged
+    unsigned epoch;              // tag base of this launch (differs from the previous launch)
     float* part_o;               // [16][s_max][128]  (long-context attention)
     float2* part_ml;             // [16][s_max]
     float2* am_part;             // [grid] per-CTA (value, index) of the lm_head rows

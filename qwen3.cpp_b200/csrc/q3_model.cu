@@ -682,7 +682,11 @@ Model::Model(const std::string& path, int ctx, int device) : file_(path) {
             fused_layers_.alloc(fl.size() * sizeof(FusedLayer));
             Q3_CUDA(cudaMemcpy(fused_layers_.ptr, fl.data(), fl.size() * sizeof(FusedLayer),
                                cudaMemcpyHostToDevice));
-            fused_xy_.alloc((2 + static_cast<size_t>(c.n_layers)) * D * 4);
+            fused_y_.alloc(2 * static_cast<size_t>(c.n_layers) * D * 4);
+            // Tagged q|k|v [4096] and o_proj partials [8][1024]; zero tags never match a launch's.
+            fused_tagged_.alloc((static_cast<size_t>(c.n_heads + 2 * c.n_kv_heads) * c.head_dim +
+                                 static_cast<size_t>(c.n_kv_heads) * D) * 8);
+            Q3_CUDA(cudaMemset(fused_tagged_.ptr, 0, fused_tagged_.bytes));
             fused_part_o_.alloc(static_cast<size_t>(c.n_heads) * fused_s_max_ * c.head_dim * 4);
             fused_part_ml_.alloc(static_cast<size_t>(c.n_heads) * fused_s_max_ * sizeof(float2));
             fused_am_.alloc(static_cast<size_t>(fused_grid_) * sizeof(float2));
@@ -739,9 +743,12 @@ void Model::launch_fused(int n_steps, bool forced, bool taps, long long spin_cyc
     a.page_table = e.page_table();
     a.rope = e.rope();
     a.rope_len = e.rope_len();
-    a.xbuf = static_cast<float*>(fused_xy_.ptr);
-    a.ybuf = static_cast<float*>(fused_xy_.ptr) + 2 * cfg_.dim;
-    a.qkv = e.qkv();
+    a.ybuf = static_cast<float*>(fused_y_.ptr);
+    a.qkvt = static_cast<unsigned long long*>(fused_tagged_.ptr);
+    a.opart = a.qkvt + static_cast<size_t>(cfg_.n_heads + 2 * cfg_.n_kv_heads) * cfg_.head_dim;
+    fused_epoch_ = (fused_epoch_ + 1) & 0xFFFu;
+    if (fused_epoch_ == 0) fused_epoch_ = 1;
+    a.epoch = fused_epoch_;
     a.part_o = static_cast<float*>(fused_part_o_.ptr);
     a.part_ml = static_cast<float2*>(fused_part_ml_.ptr);
     a.am_part = static_cast<float2*>(fused_am_.ptr);
@@ -762,6 +769,7 @@ void Model::launch_fused(int n_steps, bool forced, bool taps, long long spin_cyc
     a.barrier_offset = offset;
     a.l2_ahead = fused_l2_ahead();
     Q3_CUDA(cudaMemsetAsync(a.bar, 0, sizeof(unsigned), e.stream()));
+    Q3_CUDA(cudaMemsetAsync(fused_y_.ptr, 0, fused_y_.bytes, e.stream()));
     launch_decode_fused(a, fused_grid_, e.stream());
 }
 

@@ -226,7 +226,8 @@ private:
     std::unique_ptr<Prefill> prefill_;
     DeviceBuffer prefill_ids_;
     DeviceBuffer fused_layers_, fused_part_o_, fused_part_ml_, fused_am_, fused_sync_, fused_wperm_,
-        fused_xy_, fused_dbg_;
+        fused_y_, fused_tagged_, fused_dbg_;
+    unsigned fused_epoch_ = 0;  // tag base of the last fused launch (1..4095)
 };
 
 // class Block of the reference (include/inference.h:178-202) on one GPU.
