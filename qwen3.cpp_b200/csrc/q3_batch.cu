@@ -17,6 +17,7 @@
 #include <string>
 
 #include "q3_batch.cuh"
+#include "q3_decode_attn.cuh"
 #include "q3_gemm.cuh"
 #include "q3_kernels.cuh"
 
@@ -219,7 +220,6 @@ void Batch::ensure_step_buffers() {
     o_lo_.alloc(static_cast<size_t>(B) * qd * 2);
     h_lo_.alloc(static_cast<size_t>(B) * H * 2);
     qkv_.alloc(static_cast<size_t>(B) * qkv * 4);
-    q_.alloc(static_cast<size_t>(B) * qd * 2);
     o_.alloc(static_cast<size_t>(B) * qd * 2);
     gu_.alloc(static_cast<size_t>(B) * 2 * H * 4);
     h_.alloc(static_cast<size_t>(B) * H * 2);
@@ -230,11 +230,19 @@ void Batch::ensure_step_buffers() {
     make_tmap_bf16(&a_xn_lo_, xn_lo_.ptr, B, c.dim, 128);
     make_tmap_bf16(&a_o_lo_, o_lo_.ptr, B, qd, 128);
     make_tmap_bf16(&a_h_lo_, h_lo_.ptr, B, H, 128);
-    make_tmap_bf16(&q_map_, q_.ptr, B, qd, 64);
     make_tmap_out(&o_qkv_, qkv_.ptr, B, qkv, false);
     make_tmap_out(&o_x_, x_.ptr, B, c.dim, false);
     make_tmap_out(&o_gu_, gu_.ptr, B, 2 * static_cast<uint64_t>(H), false);
     make_tmap_out(&o_logits_, logits_.ptr, B, c.vocab_size, false);
+    // Decode attention on the CUDA cores: fp32 q rows, split partials and merge counters.
+    q32_.alloc(static_cast<size_t>(B) * qd * 4);
+    attn_pps_ = decode_attn_pages_per_split(B, c.n_kv_heads, pps_, prefill_->num_sms());
+    attn_splits_ = (pps_ + attn_pps_ - 1) / attn_pps_;
+    const size_t pairs = static_cast<size_t>(B) * c.n_kv_heads;
+    attn_part_o_.alloc(pairs * attn_splits_ * 2 * HD * 4);
+    attn_part_ml_.alloc(pairs * attn_splits_ * 2 * sizeof(float2));
+    attn_counter_.alloc(pairs * sizeof(unsigned));
+    Q3_CUDA(cudaMemset(attn_counter_.ptr, 0, attn_counter_.bytes));
     cap_rows_ = B;
     if (graph_) {
         cudaGraphExecDestroy(graph_);
@@ -278,7 +286,6 @@ void Batch::enqueue_step(bool forced, int n_forced) {
         qa.q_norm = w.q_norm;
         qa.k_norm = w.k_norm;
         qa.rope = static_cast<const float2*>(rope_.ptr);
-        qa.q_out = static_cast<uint16_t*>(q_.ptr);
         qa.k_cache = static_cast<uint16_t*>(k_.ptr) + layer_elems * l;
         qa.v_cache = static_cast<uint16_t*>(v_.ptr) + layer_elems * l;
         qa.page_table = static_cast<const int32_t*>(table_.ptr);
@@ -289,21 +296,31 @@ void Batch::enqueue_step(bool forced, int n_forced) {
         qa.eps = c.norm_eps;
         qa.dec_pos = static_cast<const int32_t*>(pos_.ptr);
         qa.pages_per_seq = pps_;
+        qa.q_out_f32 = static_cast<float*>(q32_.ptr);
         launch_prefill_qkv(qa, s_);
-        PrefillAttnTcArgs ta{};
-        ta.page_table = static_cast<const int32_t*>(table_.ptr);
-        ta.out = static_cast<uint16_t*>(o_.ptr);
-        ta.err = err;
-        ta.rows = B;
-        ta.pos0 = 0;
-        ta.n_kv = c.n_kv_heads;
-        ta.n_pages = pool_pages_;
-        ta.layer = l;
-        ta.dec_pos = static_cast<const int32_t*>(pos_.ptr);
-        ta.pages_per_seq = pps_;
-        ta.out_lo = static_cast<uint16_t*>(o_lo_.ptr);
-        launch_prefill_attention_tc(q_map_, prefill_->kmap(), prefill_->vmap(), prefill_->kmap4(),
-                                    prefill_->vmap4(), ta, s_);
+        {
+            DecodeAttnArgs da{};
+            da.q = static_cast<const float*>(q32_.ptr);
+            da.q_stride = qd;
+            da.k_cache = static_cast<const uint16_t*>(k_.ptr) + layer_elems * l;
+            da.v_cache = static_cast<const uint16_t*>(v_.ptr) + layer_elems * l;
+            da.page_table = static_cast<const int32_t*>(table_.ptr);
+            da.pages_per_seq = pps_;
+            da.dec_pos = static_cast<const int32_t*>(pos_.ptr);
+            da.rows = B;
+            da.n_kv = c.n_kv_heads;
+            da.kv_head0 = 0;
+            da.n_kv_cache = c.n_kv_heads;
+            da.pages_per_split = attn_pps_;
+            da.max_splits = attn_splits_;
+            da.part_o = static_cast<float*>(attn_part_o_.ptr);
+            da.part_ml = static_cast<float2*>(attn_part_ml_.ptr);
+            da.counter = static_cast<unsigned*>(attn_counter_.ptr);
+            da.out = static_cast<uint16_t*>(o_.ptr);
+            da.out_lo = static_cast<uint16_t*>(o_lo_.ptr);
+            da.out_stride = qd;
+            launch_decode_attention(da, s_);
+        }
         gemm(a_o_, a_o_lo_, wm.wo, o_x_, c.dim, qd, kEpiAddF32);
         launch_rmsnorm_rows_bf16(nullptr, nullptr, X, w.mlp_norm, c.norm_eps, Xn, B, c.dim, s_,
                                  Xn_lo);

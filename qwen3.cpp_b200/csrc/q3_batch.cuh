@@ -55,7 +55,9 @@ private:
     cudaStream_t s_ = nullptr;
     std::unique_ptr<Prefill> prefill_;
     DeviceBuffer k_, v_, table_, rope_, pos_, tok_, step_, forced_, log_, err_;
-    DeviceBuffer x_, xn_, qkv_, q_, o_, gu_, h_, logits_, x_last_, ids_, xn_lo_, o_lo_, h_lo_;
+    DeviceBuffer x_, xn_, qkv_, o_, gu_, h_, logits_, x_last_, ids_, xn_lo_, o_lo_, h_lo_;
+    DeviceBuffer q32_, attn_part_o_, attn_part_ml_, attn_counter_;
+    int attn_pps_ = 8, attn_splits_ = 1;
     int rope_len_ = 0;
     int cap_rows_ = 0;  // rows the step buffers and maps were built for
     int log_cap_ = 0;
@@ -63,7 +65,7 @@ private:
     std::vector<int32_t> next_;        // token each sequence feeds next
     PinnedBuffer pinned_;
     // TMA maps for the decode step (rebuilt when the number of sequences changes).
-    CUtensorMap a_xn_, a_o_, a_h_, a_xn_lo_, a_o_lo_, a_h_lo_, q_map_, o_qkv_, o_x_, o_gu_,
+    CUtensorMap a_xn_, a_o_, a_h_, a_xn_lo_, a_o_lo_, a_h_lo_, o_qkv_, o_x_, o_gu_,
         o_logits_;
     struct LayerMaps {
         CUtensorMap wqkv, wo, w13, w2;

@@ -127,6 +127,11 @@ __global__ void __launch_bounds__(256) prefill_qkv_kernel(PrefillQkvArgs a) {
             v.w = v.w * c23.z + p.w * c23.w;
         }
         if (isq) {
+            if (a.q_out_f32) {
+                reinterpret_cast<float4*>(a.q_out_f32 + static_cast<size_t>(row) * nq * HD +
+                                          head * HD)[lane] = v;
+            }
+            if (!a.q_out) return;
             dst = a.q_out + static_cast<size_t>(row) * nq * HD + head * HD;
         } else {
             const int g = a.kv_head0 + head - nq;

@@ -29,7 +29,7 @@ struct PrefillQkvArgs {
     const uint16_t* q_norm;
     const uint16_t* k_norm;
     const float2* rope;        // [len][64] (cos, sin)
-    uint16_t* q_out;           // [rows, n_heads*128] bf16
+    uint16_t* q_out;           // nullable: [rows, n_heads*128] bf16
     uint16_t* k_cache;
     uint16_t* v_cache;
     const int32_t* page_table;
@@ -43,6 +43,7 @@ struct PrefillQkvArgs {
     // for n_kv_cache heads (0: n_kv).
     int kv_head0 = 0, n_kv_cache = 0;
     int clear_input = 0;  // zero qkv after reading it (for reduce-add producers of the next step)
+    float* q_out_f32 = nullptr;  // nullable: the fp32 q rows as well [rows, n_heads*128]
 };
 void launch_prefill_qkv(const PrefillQkvArgs& a, cudaStream_t s);
 
@@ -69,25 +70,9 @@ struct PrefillAttnTcArgs {
     unsigned* err;             // set non-zero when a bounded wait gives up
     long long budget = 4000000000LL;
     int rows, pos0, n_kv, n_pages, layer;
-    // Decode of independent sequences (one query row each): row b attends positions
-    // [0, dec_pos[b]] through page_table + b * pages_per_seq (null: causal prefill). In prefill,
-    // pages_per_seq is the length of page_table (0: n_pages).
-    const int32_t* dec_pos = nullptr;
-    int pages_per_seq = 0;
+    int pages_per_seq = 0;       // length of page_table (0: n_pages)
     uint16_t* out_lo = nullptr;  // optional: attention output - bf16(output)
-    // Tensor-parallel shard: local KV head g is head kv_head0 + g of a cache of n_kv_cache heads
-    // (0: n_kv); q and out hold the local query heads only.
-    int kv_head0 = 0, n_kv_cache = 0;
-    // Decode split over KV positions (flash-decoding): `splits` blocks per (sequence, KV head),
-    // each over tiles_per_split tiles of 128 positions, write unnormalised partials
-    // part_o [rows][2*n_kv][splits][128] and part_ml [rows][2*n_kv][splits] (max in log2 units
-    // of the scaled scores, sum); launch_attention_combine merges them into out (and out_lo).
-    int splits = 1, tiles_per_split = 0;
-    float* part_o = nullptr;
-    float2* part_ml = nullptr;
 };
-// Merge of the split partials of a decode-mode attention (a.splits > 1).
-void launch_attention_combine(const PrefillAttnTcArgs& a, cudaStream_t s);
 void launch_prefill_attention_tc(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
                                  const CUtensorMap& k4, const CUtensorMap& v4,
                                  const PrefillAttnTcArgs& a, cudaStream_t s);

@@ -205,45 +205,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // Prefill: 1-D grid, longest query blocks first across every KV head, so that the block
-    // scheduler starts the longest work first and the short blocks fill the tail. Decode: block
-    // (b, g) serves the one query row of sequence b; the other 63 rows of each head's Q box are
-    // computed with the same mask and dropped.
-    const bool dec = a.dec_pos != nullptr;
+    // 1-D grid, longest query blocks first across every KV head, so that the block scheduler
+    // starts the longest work first and the short blocks fill the tail.
     const int g = static_cast<int>(blockIdx.x) % a.n_kv;
-    int tok0, last_tok, kv_end, split = 0;
+    const int n_qb = gridDim.x / a.n_kv;
+    const int qb = n_qb - 1 - static_cast<int>(blockIdx.x) / a.n_kv;
+    const int tok0 = qb * TOK;
+    const int last_tok = min(a.rows, tok0 + TOK) - 1;
+    const int kv_end = a.pos0 + last_tok + 1;
     const int32_t* table = a.page_table;
-    if (dec) {
-        const int rest = static_cast<int>(blockIdx.x) / a.n_kv;
-        split = rest % a.splits;
-        const int b = rest / a.splits;
-        tok0 = b;
-        last_tok = b;
-        kv_end = a.dec_pos[b] + 1;
-        table += static_cast<size_t>(b) * a.pages_per_seq;
-    } else {
-        const int n_qb = gridDim.x / a.n_kv;
-        const int qb = n_qb - 1 - static_cast<int>(blockIdx.x) / a.n_kv;
-        tok0 = qb * TOK;
-        last_tok = min(a.rows, tok0 + TOK) - 1;
-        kv_end = a.pos0 + last_tok + 1;
-    }
     const int table_len = a.pages_per_seq ? a.pages_per_seq : a.n_pages;
-    const int gc = a.kv_head0 + g;                         // KV head in the cache
-    const int nkc = a.n_kv_cache ? a.n_kv_cache : a.n_kv;  // KV heads of the cache layout
-    const int all_tiles = (kv_end + KEYS - 1) / KEYS;
-    // This block's KV tiles [tb, tb + ntiles) (one split of a decode; everything otherwise).
-    const int tb = dec && a.splits > 1 ? split * a.tiles_per_split : 0;
-    const int ntiles = dec && a.splits > 1 ? min(all_tiles, tb + a.tiles_per_split) - tb : all_tiles;
-    if (ntiles <= 0) {
-        // An empty split (the sequence is shorter than the other splits): an empty partial.
-        if (threadIdx.x < 2) {
-            const int head = 2 * g + static_cast<int>(threadIdx.x);
-            a.part_ml[(static_cast<size_t>(tok0) * 2 * a.n_kv + head) * a.splits + split] =
-                make_float2(-1e30f, 0.0f);
-        }
-        return;
-    }
+    const int ntiles = (kv_end + KEYS - 1) / KEYS;
     const int valid_pages = (kv_end + kPageTokens - 1) / kPageTokens;
 
     if (threadIdx.x == 0) {
@@ -301,7 +273,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     uint64_t* emp = kind ? &v_empty[st] : &kv_empty[st];
                     uint64_t* ful = kind ? &v_full[st] : &kv_full[st];
                     int rows8[KEYS / kPageTokens];
-                    const int lp0 = (tb + j) * (KEYS / kPageTokens);
+                    const int lp0 = j * (KEYS / kPageTokens);
                     const bool all_in = lp0 + KEYS / kPageTokens <= table_len;
 #pragma unroll
                     for (int pg = 0; pg < KEYS / kPageTokens; ++pg) {
@@ -322,13 +294,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     if (contiguous) {
 #pragma unroll
                         for (int p = 0; p < 2; ++p) {
-                            tma_load_4d(dst + p * PANEL, kind ? &tv4 : &tk4, p * 64, 0, gc, page4, ful);
+                            tma_load_4d(dst + p * PANEL, kind ? &tv4 : &tk4, p * 64, 0, g, page4, ful);
                         }
                     } else {
 #pragma unroll
                         for (int pg = 0; pg < KEYS / kPageTokens; ++pg) {
                             const int row =
-                                ((a.layer * a.n_pages + rows8[pg]) * nkc + gc) * kPageTokens;
+                                ((a.layer * a.n_pages + rows8[pg]) * a.n_kv + g) * kPageTokens;
 #pragma unroll
                             for (int p = 0; p < 2; ++p) {
                                 tma_load_2d(dst + p * PANEL + pg * (kPageTokens * 128),
@@ -435,7 +407,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int lg = warp & 3;
         const int half = (warp - 2) >> 2;                // key half of S, column half of O
         const int r = lg * 32 + lane;                    // row of the 128-row tile
-        const int qpos = dec ? kv_end - 1 : a.pos0 + min(tok0 + (r & (TOK - 1)), last_tok);
+        const int qpos = a.pos0 + min(tok0 + (r & (TOK - 1)), last_tok);
         const uint32_t lane_half = tmem + (static_cast<uint32_t>(lg * 32) << 16) +
                                    static_cast<uint32_t>(half * 64);
         const float scale = 1.4426950408889634f / sqrtf(static_cast<float>(HD));
@@ -455,7 +427,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const uint32_t srow = tmem + (static_cast<uint32_t>(lg * 32) << 16) +
                                   static_cast<uint32_t>((t & 1) * 128);
             const uint32_t sb = srow + static_cast<uint32_t>(half * 64);
-            const int tile_key0 = (tb + t) * KEYS;
+            const int tile_key0 = t * KEYS;
             const int key0 = tile_key0 + half * 64;
             // Row max over all 128 keys of the tile (both halves read the whole row from TMEM, so
             // they agree on it without exchanging). Scores are scaled after the max (scale > 0).
@@ -535,18 +507,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const float l_other = exchange_row(red, mx_bar, ntiles, half, r, l, a.budget, abort);
             if (l_other != l_other) {
                 fail(abort, a.err, 19);
-            } else if (dec && a.splits > 1) {
-                // Unnormalised partial of this split for the one real row of each head.
-                if ((r & (TOK - 1)) == 0) {
-                    const int head = 2 * g + (r >> 6);
-                    const size_t pi = (static_cast<size_t>(tok0) * 2 * a.n_kv + head) * a.splits + split;
-                    float4* po = reinterpret_cast<float4*>(a.part_o + pi * HD + half * 64);
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) po[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
-                    if (half == 0) a.part_ml[pi] = make_float2(m_run, l + l_other);
-                }
             } else {
-                const int token = dec ? ((r & (TOK - 1)) == 0 ? tok0 : a.rows) : tok0 + (r & (TOK - 1));
+                const int token = tok0 + (r & (TOK - 1));
                 if (token < a.rows) {
                     const float inv = 1.0f / (l + l_other);
                     const size_t off = static_cast<size_t>(token) * (2 * a.n_kv) * HD +
@@ -582,37 +544,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
 }
 
-// Block (row b, query head h): out = sum_s o_s 2^(m_s - M) / sum_s l_s 2^(m_s - M).
-__global__ void attention_combine_kernel(const PrefillAttnTcArgs a) {
-    const int bh = blockIdx.x, d = threadIdx.x;  // 128 threads: one per dim
-    const int S = a.splits;
-    const float2* ml = a.part_ml + static_cast<size_t>(bh) * S;
-    float M = -1e30f;
-    for (int s = 0; s < S; ++s) {
-        if (ml[s].y > 0.0f) M = fmaxf(M, ml[s].x);
-    }
-    float L = 0.0f, o = 0.0f;
-    for (int s = 0; s < S; ++s) {
-        if (ml[s].y > 0.0f) {
-            const float f = ex2(ml[s].x - M);
-            L += ml[s].y * f;
-            o += a.part_o[(static_cast<size_t>(bh) * S + s) * HD + d] * f;
-        }
-    }
-    const float y = o / L;
-    const size_t off = static_cast<size_t>(bh) * HD + d;  // rows of 2*n_kv heads x 128
-    const __nv_bfloat16 hi = __float2bfloat16_rn(y);
-    a.out[off] = __bfloat16_as_ushort(hi);
-    if (a.out_lo) a.out_lo[off] = __bfloat16_as_ushort(__float2bfloat16_rn(y - __bfloat162float(hi)));
-}
-
 }  // namespace
-
-void launch_attention_combine(const PrefillAttnTcArgs& a, cudaStream_t s) {
-    if (a.rows <= 0 || a.splits <= 1) return;
-    attention_combine_kernel<<<a.rows * 2 * a.n_kv, HD, 0, s>>>(a);
-    Q3_CUDA(cudaGetLastError());
-}
 
 void launch_prefill_attention_tc(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
                                  const CUtensorMap& k4, const CUtensorMap& v4,
@@ -626,11 +558,7 @@ void launch_prefill_attention_tc(const CUtensorMap& q, const CUtensorMap& k, con
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
         configured[dev & 63] = true;
     }
-    if (a.dec_pos && a.splits > 1 && (!a.part_o || !a.part_ml || a.tiles_per_split <= 0)) {
-        throw std::invalid_argument("split attention needs partial buffers and a split size");
-    }
-    const dim3 grid(a.dec_pos ? a.rows * a.n_kv * (a.splits > 1 ? a.splits : 1)
-                              : ((a.rows + TOK - 1) / TOK) * a.n_kv);
+    const dim3 grid(((a.rows + TOK - 1) / TOK) * a.n_kv);
     prefill_attn_tc_kernel<<<grid, NTHREADS, SMEM, s>>>(q, k, v, k4, v4, a);
     Q3_CUDA(cudaGetLastError());
 }

@@ -29,7 +29,9 @@
 
 #include "q3_gemm.cuh"
 #include "q3_kernels.cuh"
+#include "q3_prefill.cuh"
 #include "q3_tp.cuh"
+#include "q3_decode_attn.cuh"
 
 namespace q3 {
 
@@ -298,7 +300,7 @@ TpDecoder::TpDecoder(Model& model, int rank, int world)
     xn_.alloc(D * 2);
     xn_lo_.alloc(D * 2);
     qkv_.alloc(qkv_l * 4);
-    q_.alloc(static_cast<size_t>(hq_) * HD * 2);
+    q32_.alloc(static_cast<size_t>(hq_) * HD * 4);
     o_.alloc(static_cast<size_t>(hq_) * HD * 2);
     o_lo_.alloc(static_cast<size_t>(hq_) * HD * 2);
     part_.alloc(D * 4);
@@ -321,19 +323,19 @@ TpDecoder::TpDecoder(Model& model, int rank, int world)
     make_tmap_bf16(&a_o_lo_, o_lo_.ptr, 1, static_cast<uint64_t>(hq_) * HD, 128);
     make_tmap_bf16(&a_h_, h_.ptr, 1, hl_, 128);
     make_tmap_bf16(&a_h_lo_, h_lo_.ptr, 1, hl_, 128);
-    make_tmap_bf16(&q_map_, q_.ptr, 1, static_cast<uint64_t>(hq_) * HD, 64);
     make_tmap_out(&o_qkv_, qkv_.ptr, 1, qkv_l, false);
     make_tmap_out(&o_part_, part_.ptr, 1, D, false);
     make_tmap_out(&o_gu_, gu_.ptr, 1, 2 * static_cast<uint64_t>(hl_), false);
     make_tmap_out(&o_logits_, logits_.ptr, 1, vn_, false);
-    // Attention split over KV positions so that ~128 blocks share the context.
-    const int max_tiles = (c.max_seq_len + 127) / 128;
-    tiles_per_split_ = std::max(1, (max_tiles * hkv_ + 127) / 128);
-    splits_ = (max_tiles + tiles_per_split_ - 1) / tiles_per_split_;
-    part_o_.alloc(static_cast<size_t>(2 * hkv_) * splits_ * HD * 4);
-    part_ml_.alloc(static_cast<size_t>(2 * hkv_) * splits_ * sizeof(float2));
-    maps_ = std::make_unique<Prefill>(c, model.device());
-    maps_->ensure_kv_maps(engine_view(model.engine()), c.n_layers);
+    // Decode attention split over the cached pages of the local KV heads.
+    Q3_CUDA(cudaDeviceGetAttribute(&sms_, cudaDevAttrMultiProcessorCount, model.device()));
+    const int max_pages = model.engine().n_pages();
+    attn_pps_ = decode_attn_pages_per_split(1, hkv_, max_pages, sms_);
+    attn_splits_ = (max_pages + attn_pps_ - 1) / attn_pps_;
+    part_o_.alloc(static_cast<size_t>(hkv_) * attn_splits_ * 2 * HD * 4);
+    part_ml_.alloc(static_cast<size_t>(hkv_) * attn_splits_ * 2 * sizeof(float2));
+    attn_counter_.alloc(static_cast<size_t>(hkv_) * sizeof(unsigned));
+    Q3_CUDA(cudaMemsetAsync(attn_counter_.ptr, 0, attn_counter_.bytes, s_));
     prepare_gemm_kernels();
     Q3_CUDA(cudaStreamSynchronize(s_));
 }
@@ -371,7 +373,7 @@ void TpDecoder::connect(const void* handles) {
 void TpDecoder::enqueue_step(bool forced) {
     const q3_config& c = cfg_;
     const int qkv_l = (hq_ + 2 * hkv_) * HD;
-    const int sms = maps_->num_sms();
+    const int sms = sms_;
     unsigned* err = static_cast<unsigned*>(err_.ptr);
     unsigned* counter = static_cast<unsigned*>(counter_.ptr);
     TpPeers P{};
@@ -406,7 +408,7 @@ void TpDecoder::enqueue_step(bool forced) {
         qa.q_norm = w.q_norm;
         qa.k_norm = w.k_norm;
         qa.rope = e.rope();
-        qa.q_out = static_cast<uint16_t*>(q_.ptr);
+        qa.q_out_f32 = static_cast<float*>(q32_.ptr);
         qa.k_cache = e.k_layer(l);
         qa.v_cache = e.v_layer(l);
         qa.page_table = e.page_table();
@@ -420,26 +422,27 @@ void TpDecoder::enqueue_step(bool forced) {
         qa.n_kv_cache = c.n_kv_heads;
         qa.clear_input = 1;
         launch_prefill_qkv(qa, s_);
-        PrefillAttnTcArgs ta{};
-        ta.page_table = e.page_table();
-        ta.out = static_cast<uint16_t*>(o_.ptr);
-        ta.out_lo = static_cast<uint16_t*>(o_lo_.ptr);
-        ta.err = err;
-        ta.rows = 1;
-        ta.n_kv = hkv_;
-        ta.n_pages = e.n_pages();
-        ta.layer = l;
-        ta.dec_pos = static_cast<const int32_t*>(pos_.ptr);
-        ta.pages_per_seq = e.n_pages();
-        ta.kv_head0 = rank_ * hkv_;
-        ta.n_kv_cache = c.n_kv_heads;
-        ta.splits = splits_;
-        ta.tiles_per_split = tiles_per_split_;
-        ta.part_o = static_cast<float*>(part_o_.ptr);
-        ta.part_ml = static_cast<float2*>(part_ml_.ptr);
-        launch_prefill_attention_tc(q_map_, maps_->kmap(), maps_->vmap(), maps_->kmap4(),
-                                    maps_->vmap4(), ta, s_);
-        launch_attention_combine(ta, s_);
+        DecodeAttnArgs da{};
+        da.q = static_cast<const float*>(q32_.ptr);
+        da.q_stride = hq_ * HD;
+        da.k_cache = e.k_layer(l);
+        da.v_cache = e.v_layer(l);
+        da.page_table = e.page_table();
+        da.pages_per_seq = e.n_pages();
+        da.dec_pos = static_cast<const int32_t*>(pos_.ptr);
+        da.rows = 1;
+        da.n_kv = hkv_;
+        da.kv_head0 = rank_ * hkv_;
+        da.n_kv_cache = c.n_kv_heads;
+        da.pages_per_split = attn_pps_;
+        da.max_splits = attn_splits_;
+        da.part_o = static_cast<float*>(part_o_.ptr);
+        da.part_ml = static_cast<float2*>(part_ml_.ptr);
+        da.counter = static_cast<unsigned*>(attn_counter_.ptr);
+        da.out = static_cast<uint16_t*>(o_.ptr);
+        da.out_lo = static_cast<uint16_t*>(o_lo_.ptr);
+        da.out_stride = hq_ * HD;
+        launch_decode_attention(da, s_);
         gemm(a_o_, a_o_lo_, wm.wo, o_part_, c.dim, hq_ * HD, kEpiAddF32);
         tp_allreduce_norm_kernel<<<1, 256, 0, s_>>>(P, static_cast<float*>(part_.ptr), X, rank_,
                                                     world_, counter, err, kBudget, w.mlp_norm,

@@ -18,7 +18,7 @@
 #include <vector>
 
 #include "q3_model.cuh"
-#include "q3_prefill.cuh"
+#include "q3_gemm.cuh"
 
 namespace q3 {
 
@@ -54,21 +54,21 @@ private:
     int hq_, hkv_, hl_;     // local query heads, KV heads, MLP rows
     int v0_, vn_;           // local vocabulary rows [v0, v0 + vn)
     cudaStream_t s_ = nullptr;
-    std::unique_ptr<Prefill> maps_;  // TMA maps of the model's paged KV cache
     DeviceBuffer shard_;    // per layer: [wq_l; wk_l; wv_l] then [w1_l; w3_l]
-    DeviceBuffer x_, xn_, xn_lo_, qkv_, q_, o_, o_lo_, part_, gu_, h_, h_lo_, logits_;
-    DeviceBuffer pos_, tok_, step_, forced_, log_, err_, counter_, part_o_, part_ml_;
+    DeviceBuffer x_, xn_, xn_lo_, qkv_, q32_, o_, o_lo_, part_, gu_, h_, h_lo_, logits_;
+    DeviceBuffer pos_, tok_, step_, forced_, log_, err_, counter_, part_o_, part_ml_, attn_counter_;
     DeviceBuffer xbuf_;     // exchange buffer (IPC-exported): data, argmax slots, flags
     std::vector<void*> peer_mapped_;
     bool connected_ = false;
     int log_cap_ = 0;
-    int splits_ = 1, tiles_per_split_ = 0;
+    int attn_pps_ = 8, attn_splits_ = 1;  // decode attention: pages per split, splits
+    int sms_ = 0;
     struct LayerMaps {
         CUtensorMap wqkv, wo, w13, w2;
     };
     std::vector<LayerMaps> wmaps_;
-    CUtensorMap lm_, a_xn_, a_xn_lo_, a_o_, a_o_lo_, a_h_, a_h_lo_, q_map_, o_qkv_, o_part_,
-        o_gu_, o_logits_;
+    CUtensorMap lm_, a_xn_, a_xn_lo_, a_o_, a_o_lo_, a_h_, a_h_lo_, o_qkv_, o_part_, o_gu_,
+        o_logits_;
     cudaGraphExec_t graph_ = nullptr;
     bool graph_forced_ = false;
     const float2* graph_rope_ = nullptr;
