@@ -37,15 +37,18 @@ __device__ __forceinline__ void unpack8(const uint4 w, float f[8]) {
     f[7] = bf16_hi(w.w);
 }
 
-// Writes o (already divided by the softmax sum) as bf16 hi (and lo) at dst + d.
+// Writes o (already divided by the softmax sum) at element off of the outputs.
 __device__ __forceinline__ void put_out(const DecodeAttnArgs& a, size_t off, float o) {
-    const uint16_t hi = f32_to_bf16(o);
-    a.out[off] = hi;
-    if (a.out_lo) a.out_lo[off] = f32_to_bf16(o - bf16_to_f32(hi));
+    if (a.out_f32) a.out_f32[off] = o;
+    if (a.out) {
+        const uint16_t hi = f32_to_bf16(o);
+        a.out[off] = hi;
+        if (a.out_lo) a.out_lo[off] = f32_to_bf16(o - bf16_to_f32(hi));
+    }
 }
 
 __global__ void __launch_bounds__(DA_THREADS) decode_attn_kernel(const DecodeAttnArgs a) {
-    __shared__ float s_o[DA_WARPS][2][HD];
+    __shared__ __align__(16) float s_o[DA_WARPS][2][HD];  // written as float4
     __shared__ float2 s_ml[DA_WARPS][2];
     __shared__ int s_last;
     __shared__ float2 s_pml[2 * kMaxSplits];  // merge: (max, sum) per (split, head)

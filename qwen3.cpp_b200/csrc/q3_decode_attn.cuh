@@ -25,8 +25,10 @@ struct DecodeAttnArgs {
     float* part_o;             // [rows * n_kv][max_splits][2][128]
     float2* part_ml;           // [rows * n_kv][max_splits][2] (max, sum)
     unsigned* counter;         // [rows * n_kv], zero; reset by the merging split
-    uint16_t* out;             // bf16 attention output, heads 2g, 2g+1 at out + row*out_stride + 2g*128
+    uint16_t* out;             // nullable: bf16 attention output, heads 2g, 2g+1 at
+                               // out + row * out_stride + 2g * 128
     uint16_t* out_lo;          // nullable: bf16(o - out), the low part of a split activation
+    float* out_f32;            // nullable: the fp32 output, same layout
     int out_stride;
 };
 

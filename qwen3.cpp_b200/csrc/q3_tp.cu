@@ -27,7 +27,6 @@
 #include <stdexcept>
 #include <string>
 
-#include "q3_gemm.cuh"
 #include "q3_kernels.cuh"
 #include "q3_prefill.cuh"
 #include "q3_tp.cuh"
@@ -56,10 +55,6 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-__device__ __forceinline__ uint32_t pack2(float a, float b) {
-    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-    return *reinterpret_cast<const uint32_t*>(&h);
-}
 
 // Waits (bounded) until every source's flag in this rank's buffer reached seq. Threads
 // [0, world) poll one source each. Returns false on timeout.
@@ -84,12 +79,11 @@ __device__ void raise_flags(const TpPeers& P, int world, int rank, unsigned seq)
     }
 }
 
-// x += sum over ranks of part (rank order), then xn/xn_lo = RmsNorm(x) * w as a bf16 hi + lo pair
-// (src/inference.cpp:905-921); part is cleared for the next step's reduce-adds. One block.
-__global__ void __launch_bounds__(256) tp_allreduce_norm_kernel(
-    TpPeers P, float* part, float* x, int rank, int world, unsigned* counter, unsigned* err,
-    long long budget, const uint16_t* w, float eps, uint16_t* xn, uint16_t* xn_lo) {
-    __shared__ float red[8];
+// x += sum over ranks of part, in rank order, so that x stays bit-identical on every rank (the
+// residual adds x += proj of src/inference.cpp:847-849, 863-865). One block of 256 threads.
+__global__ void __launch_bounds__(256) tp_allreduce_kernel(TpPeers P, const float* part, float* x,
+                                                           int rank, int world, unsigned* counter,
+                                                           unsigned* err, long long budget) {
     __shared__ unsigned s_seq;
     const int tid = threadIdx.x;
     if (tid == 0) s_seq = *counter + 1;
@@ -102,8 +96,8 @@ __global__ void __launch_bounds__(256) tp_allreduce_norm_kernel(
         float* dst = reinterpret_cast<float*>(P.buf[p]) + (par * kTpMaxRanks + rank) * kDim;
         *reinterpret_cast<float4*>(dst + i) = mine;
     }
-    *reinterpret_cast<float4*>(part + i) = make_float4(0.f, 0.f, 0.f, 0.f);
-    __threadfence_system();
+    // The flag stores are releases at system scope, ordered after every thread's data stores by
+    // the barrier (release is cumulative).
     __syncthreads();
     raise_flags(P, world, rank, seq);
     if (!wait_flags(P.buf[rank], world, seq, budget)) {
@@ -126,24 +120,6 @@ __global__ void __launch_bounds__(256) tp_allreduce_norm_kernel(
     xv.z += sum.z;
     xv.w += sum.w;
     *reinterpret_cast<float4*>(x + i) = xv;
-    float ss = xv.x * xv.x;
-    ss = fmaf(xv.y, xv.y, ss);
-    ss = fmaf(xv.z, xv.z, ss);
-    ss = fmaf(xv.w, xv.w, ss);
-    ss = warp_sum(ss);
-    if ((tid & 31) == 0) red[tid >> 5] = ss;
-    __syncthreads();
-    float tot = 0.f;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) tot += red[k];
-    const float inv = 1.0f / sqrtf(tot / static_cast<float>(kDim) + eps);
-    const uint2 wb = *reinterpret_cast<const uint2*>(w + i);
-    const float y0 = (xv.x * inv) * bf16_lo(wb.x), y1 = (xv.y * inv) * bf16_hi(wb.x);
-    const float y2 = (xv.z * inv) * bf16_lo(wb.y), y3 = (xv.w * inv) * bf16_hi(wb.y);
-    const uint2 hi = make_uint2(pack2(y0, y1), pack2(y2, y3));
-    *reinterpret_cast<uint2*>(xn + i) = hi;
-    *reinterpret_cast<uint2*>(xn_lo + i) =
-        make_uint2(pack2(y0 - bf16_lo(hi.x), y1 - bf16_hi(hi.x)), pack2(y2 - bf16_lo(hi.y), y3 - bf16_hi(hi.y)));
     if (tid == 0) *counter = seq;
 }
 
@@ -194,9 +170,8 @@ __global__ void __launch_bounds__(1024) tp_argmax_kernel(
         for (int p = 0; p < world; ++p) {
             reinterpret_cast<float2*>(P.buf[p] + kAmOff)[par * kTpMaxRanks + rank] = mine;
         }
-        __threadfence_system();
     }
-    __syncthreads();
+    __syncthreads();  // the flag releases below are ordered after thread 0's stores
     raise_flags(P, world, rank, seq);
     if (!wait_flags(P.buf[rank], world, seq, budget)) {
         if (tid == 0) atomicCAS(err, 0u, 22u);
@@ -221,19 +196,6 @@ __global__ void __launch_bounds__(1024) tp_argmax_kernel(
         pos[0] += 1;
         state[0] = step + 1;
         *counter = seq;
-    }
-}
-
-// h = silu(gu[:H]) * gu[H:] as bf16 hi + lo; gu is cleared for the next step's reduce-add.
-__global__ void tp_swiglu_kernel(float* gu, uint16_t* h, uint16_t* h_lo, int H) {
-    for (int i = (blockIdx.x * blockDim.x + threadIdx.x) * 2; i < H; i += gridDim.x * blockDim.x * 2) {
-        const float g0 = gu[i], g1 = gu[i + 1], u0 = gu[H + i], u1 = gu[H + i + 1];
-        gu[i] = gu[i + 1] = gu[H + i] = gu[H + i + 1] = 0.0f;
-        const float a = g0 / (1.0f + expf(-g0)) * u0, b = g1 / (1.0f + expf(-g1)) * u1;
-        const uint32_t hi = pack2(a, b);
-        *reinterpret_cast<uint32_t*>(h + i) = hi;
-        *reinterpret_cast<uint32_t*>(h_lo + i) =
-            pack2(a - __uint_as_float(hi << 16), b - __uint_as_float(hi & 0xffff0000u));
     }
 }
 
@@ -262,14 +224,18 @@ TpDecoder::TpDecoder(Model& model, int rank, int world)
     const size_t D = c.dim, qd = static_cast<size_t>(c.n_heads) * HD;
     const size_t kvd = static_cast<size_t>(c.n_kv_heads) * HD;
     const size_t qkv_l = static_cast<size_t>(hq_ + 2 * hkv_) * HD;
-    const size_t shard_layer = (qkv_l + 2 * static_cast<size_t>(hl_)) * D;
+    const size_t qc = static_cast<size_t>(hq_) * HD;  // local attention-output columns
+    // Per layer, contiguous: [wq;wk;wv] rows of the local heads, [w1;w3] rows of the local MLP
+    // slice, and the column slices wo[:, local q columns], w2[:, local MLP columns].
+    const size_t shard_layer = (qkv_l + 2 * static_cast<size_t>(hl_)) * D + D * qc + D * hl_;
     shard_.alloc(shard_layer * c.n_layers * 2);
-    wmaps_.resize(c.n_layers);
+    layers_.resize(c.n_layers);
     for (int l = 0; l < c.n_layers; ++l) {
         const LayerWeights& w = model.layer(l);
         uint16_t* sq = static_cast<uint16_t*>(shard_.ptr) + shard_layer * l;
         uint16_t* s13 = sq + qkv_l * D;
-        // [wq;wk;wv] rows of the local heads, then [w1;w3] rows of the local MLP slice.
+        uint16_t* so = s13 + 2 * static_cast<size_t>(hl_) * D;
+        uint16_t* s2 = so + D * qc;
         const uint16_t* wq = w.wqkv;
         const uint16_t* wk = w.wqkv + qd * D;
         const uint16_t* wv = wk + kvd * D;
@@ -286,27 +252,22 @@ TpDecoder::TpDecoder(Model& model, int rank, int world)
         Q3_CUDA(cudaMemcpyAsync(s13 + static_cast<size_t>(hl_) * D,
                                 w.w3 + static_cast<size_t>(rank) * hl_ * D,
                                 static_cast<size_t>(hl_) * D * 2, cudaMemcpyDeviceToDevice, s_));
-        make_tmap_bf16(&wmaps_[l].wqkv, sq, qkv_l, D, 128);
-        make_tmap_bf16(&wmaps_[l].w13, s13, 2 * static_cast<uint64_t>(hl_), D, 128);
-        // Column slices read in place: wo[:, local q columns], w2[:, local MLP columns].
-        make_tmap_bf16_strided(&wmaps_[l].wo, w.wo + static_cast<size_t>(rank) * hq_ * HD, D,
-                               static_cast<uint64_t>(hq_) * HD, qd, 128);
-        make_tmap_bf16_strided(&wmaps_[l].w2, w.w2 + static_cast<size_t>(rank) * hl_, D, hl_,
-                               c.hidden_dim, 128);
+        Q3_CUDA(cudaMemcpy2DAsync(so, qc * 2, w.wo + static_cast<size_t>(rank) * qc, qd * 2,
+                                  qc * 2, D, cudaMemcpyDeviceToDevice, s_));
+        Q3_CUDA(cudaMemcpy2DAsync(s2, static_cast<size_t>(hl_) * 2,
+                                  w.w2 + static_cast<size_t>(rank) * hl_,
+                                  static_cast<size_t>(c.hidden_dim) * 2,
+                                  static_cast<size_t>(hl_) * 2, D, cudaMemcpyDeviceToDevice, s_));
+        layers_[l] = ShardLayer{sq, s13, s13 + static_cast<size_t>(hl_) * D, so, s2};
     }
-    make_tmap_bf16(&lm_, model.output() + static_cast<size_t>(v0_) * D, vn_, D, 128);
 
     x_.alloc(D * 4);
-    xn_.alloc(D * 2);
-    xn_lo_.alloc(D * 2);
     qkv_.alloc(qkv_l * 4);
-    q32_.alloc(static_cast<size_t>(hq_) * HD * 4);
-    o_.alloc(static_cast<size_t>(hq_) * HD * 2);
-    o_lo_.alloc(static_cast<size_t>(hq_) * HD * 2);
+    q32_.alloc(qc * 4);
+    o32_.alloc(qc * 4);
     part_.alloc(D * 4);
-    gu_.alloc(2 * static_cast<size_t>(hl_) * 4);
-    h_.alloc(static_cast<size_t>(hl_) * 2);
-    h_lo_.alloc(static_cast<size_t>(hl_) * 2);
+    h32_.alloc(static_cast<size_t>(hl_) * 4);
+    scratch_.alloc(D * 2);
     logits_.alloc(static_cast<size_t>(vn_) * 4);
     pos_.alloc(4);
     tok_.alloc(4);
@@ -314,19 +275,9 @@ TpDecoder::TpDecoder(Model& model, int rank, int world)
     err_.alloc(4);
     counter_.alloc(4);
     xbuf_.alloc(kXbufBytes);
-    for (DeviceBuffer* b : {&qkv_, &part_, &gu_, &err_, &counter_, &xbuf_}) {
+    for (DeviceBuffer* b : {&err_, &counter_, &xbuf_}) {
         Q3_CUDA(cudaMemsetAsync(b->ptr, 0, b->bytes, s_));
     }
-    make_tmap_bf16(&a_xn_, xn_.ptr, 1, D, 128);
-    make_tmap_bf16(&a_xn_lo_, xn_lo_.ptr, 1, D, 128);
-    make_tmap_bf16(&a_o_, o_.ptr, 1, static_cast<uint64_t>(hq_) * HD, 128);
-    make_tmap_bf16(&a_o_lo_, o_lo_.ptr, 1, static_cast<uint64_t>(hq_) * HD, 128);
-    make_tmap_bf16(&a_h_, h_.ptr, 1, hl_, 128);
-    make_tmap_bf16(&a_h_lo_, h_lo_.ptr, 1, hl_, 128);
-    make_tmap_out(&o_qkv_, qkv_.ptr, 1, qkv_l, false);
-    make_tmap_out(&o_part_, part_.ptr, 1, D, false);
-    make_tmap_out(&o_gu_, gu_.ptr, 1, 2 * static_cast<uint64_t>(hl_), false);
-    make_tmap_out(&o_logits_, logits_.ptr, 1, vn_, false);
     // Decode attention split over the cached pages of the local KV heads.
     Q3_CUDA(cudaDeviceGetAttribute(&sms_, cudaDevAttrMultiProcessorCount, model.device()));
     const int max_pages = model.engine().n_pages();
@@ -336,7 +287,6 @@ TpDecoder::TpDecoder(Model& model, int rank, int world)
     part_ml_.alloc(static_cast<size_t>(hkv_) * attn_splits_ * 2 * sizeof(float2));
     attn_counter_.alloc(static_cast<size_t>(hkv_) * sizeof(unsigned));
     Q3_CUDA(cudaMemsetAsync(attn_counter_.ptr, 0, attn_counter_.bytes, s_));
-    prepare_gemm_kernels();
     Q3_CUDA(cudaStreamSynchronize(s_));
 }
 
@@ -372,8 +322,7 @@ void TpDecoder::connect(const void* handles) {
 
 void TpDecoder::enqueue_step(bool forced) {
     const q3_config& c = cfg_;
-    const int qkv_l = (hq_ + 2 * hkv_) * HD;
-    const int sms = sms_;
+    const int qkv_l = (hq_ + 2 * hkv_) * HD, qc = hq_ * HD;
     unsigned* err = static_cast<unsigned*>(err_.ptr);
     unsigned* counter = static_cast<unsigned*>(counter_.ptr);
     TpPeers P{};
@@ -381,33 +330,36 @@ void TpDecoder::enqueue_step(bool forced) {
         P.buf[p] = static_cast<uint8_t*>(p == rank_ ? xbuf_.ptr : peer_mapped_[p]);
     }
     constexpr long long kBudget = 4000000000LL;
-    auto gemm = [&](const CUtensorMap& a, const CUtensorMap& a_lo, const CUtensorMap& b,
-                    const CUtensorMap& out, int N, int K, int epi) {
-        GemmArgs g;
-        g.M = 1;
-        g.N = N;
-        g.K = K;
-        g.err = err;
-        g.bn = 128;
-        g.max_ksplit = 16;
-        g.min_slice_kblocks = 2;
-        Q3_CUDA(launch_gemm(a, b, nullptr, out, g, epi, sms, s_, &a_lo));
-    };
     float* X = static_cast<float*>(x_.ptr);
-    uint16_t* Xn = static_cast<uint16_t*>(xn_.ptr);
-    uint16_t* Xn_lo = static_cast<uint16_t*>(xn_lo_.ptr);
+    float* qkv = static_cast<float*>(qkv_.ptr);
+    float* part = static_cast<float*>(part_.ptr);
     Engine& e = m_.engine();
+    // One rank: the projections add straight into x. Several: each writes its partial, and the
+    // all-reduce adds the ranks' partials in rank order.
+    const bool solo = world_ == 1;
+    const int proj_epi = solo ? kEpiResidual : kEpiStore;
+    float* proj_out = solo ? X : part;
+    auto allreduce = [&]() {
+        if (solo) return;
+        tp_allreduce_kernel<<<1, 256, 0, s_>>>(P, part, X, rank_, world_, counter, err, kBudget);
+        Q3_CUDA(cudaGetLastError());
+    };
+    // x = embedding row of the step's token (the bf16 normalised copy is not used).
     launch_rmsnorm_rows_bf16(static_cast<const int32_t*>(tok_.ptr), m_.embed(), X,
-                             m_.layer(0).attn_norm, c.norm_eps, Xn, 1, c.dim, s_, Xn_lo);
+                             m_.layer(0).attn_norm, c.norm_eps,
+                             static_cast<uint16_t*>(scratch_.ptr), 1, c.dim, s_);
     for (int l = 0; l < c.n_layers; ++l) {
         const LayerWeights& w = m_.layer(l);
-        const LayerMaps& wm = wmaps_[l];
-        gemm(a_xn_, a_xn_lo_, wm.wqkv, o_qkv_, qkv_l, c.dim, kEpiAddF32);
+        const ShardLayer& sl = layers_[l];
+        // q|k|v of the local heads = [wq;wk;wv]_local . RmsNorm(x) (src/inference.cpp:795-798).
+        launch_gemv(kEpiStore, sl.wqkv, nullptr, X, w.attn_norm, c.norm_eps, qkv, nullptr, qkv_l,
+                    c.dim, nullptr, 0, s_);
         PrefillQkvArgs qa{};
-        qa.qkv = static_cast<float*>(qkv_.ptr);
+        qa.qkv = qkv;
         qa.q_norm = w.q_norm;
         qa.k_norm = w.k_norm;
         qa.rope = e.rope();
+        qa.q_out = nullptr;
         qa.q_out_f32 = static_cast<float*>(q32_.ptr);
         qa.k_cache = e.k_layer(l);
         qa.v_cache = e.v_layer(l);
@@ -420,11 +372,10 @@ void TpDecoder::enqueue_step(bool forced) {
         qa.pages_per_seq = e.n_pages();
         qa.kv_head0 = rank_ * hkv_;
         qa.n_kv_cache = c.n_kv_heads;
-        qa.clear_input = 1;
         launch_prefill_qkv(qa, s_);
         DecodeAttnArgs da{};
         da.q = static_cast<const float*>(q32_.ptr);
-        da.q_stride = hq_ * HD;
+        da.q_stride = qc;
         da.k_cache = e.k_layer(l);
         da.v_cache = e.v_layer(l);
         da.page_table = e.page_table();
@@ -439,28 +390,24 @@ void TpDecoder::enqueue_step(bool forced) {
         da.part_o = static_cast<float*>(part_o_.ptr);
         da.part_ml = static_cast<float2*>(part_ml_.ptr);
         da.counter = static_cast<unsigned*>(attn_counter_.ptr);
-        da.out = static_cast<uint16_t*>(o_.ptr);
-        da.out_lo = static_cast<uint16_t*>(o_lo_.ptr);
-        da.out_stride = hq_ * HD;
+        da.out_f32 = static_cast<float*>(o32_.ptr);
+        da.out_stride = qc;
         launch_decode_attention(da, s_);
-        gemm(a_o_, a_o_lo_, wm.wo, o_part_, c.dim, hq_ * HD, kEpiAddF32);
-        tp_allreduce_norm_kernel<<<1, 256, 0, s_>>>(P, static_cast<float*>(part_.ptr), X, rank_,
-                                                    world_, counter, err, kBudget, w.mlp_norm,
-                                                    c.norm_eps, Xn, Xn_lo);
-        Q3_CUDA(cudaGetLastError());
-        gemm(a_xn_, a_xn_lo_, wm.w13, o_gu_, 2 * hl_, c.dim, kEpiAddF32);
-        tp_swiglu_kernel<<<std::max(1, hl_ / 256), 128, 0, s_>>>(
-            static_cast<float*>(gu_.ptr), static_cast<uint16_t*>(h_.ptr),
-            static_cast<uint16_t*>(h_lo_.ptr), hl_);
-        Q3_CUDA(cudaGetLastError());
-        gemm(a_h_, a_h_lo_, wm.w2, o_part_, c.dim, hl_, kEpiAddF32);
-        const uint16_t* next_norm = l + 1 < c.n_layers ? m_.layer(l + 1).attn_norm : m_.final_norm();
-        tp_allreduce_norm_kernel<<<1, 256, 0, s_>>>(P, static_cast<float*>(part_.ptr), X, rank_,
-                                                    world_, counter, err, kBudget, next_norm,
-                                                    c.norm_eps, Xn, Xn_lo);
-        Q3_CUDA(cudaGetLastError());
+        // x += wo[:, local] . attn_local summed over ranks (:846-849).
+        launch_gemv(proj_epi, sl.wo, nullptr, static_cast<const float*>(o32_.ptr), nullptr, 0.0f,
+                    proj_out, nullptr, c.dim, qc, nullptr, 0, s_);
+        allreduce();
+        // h = silu(w1 . xn) * (w3 . xn) on the local MLP slice, x += w2[:, local] . h (:851-865).
+        launch_gemv(kEpiSiluMul, sl.w1, sl.w3, X, w.mlp_norm, c.norm_eps,
+                    static_cast<float*>(h32_.ptr), nullptr, hl_, c.dim, nullptr, 0, s_);
+        launch_gemv(proj_epi, sl.w2, nullptr, static_cast<const float*>(h32_.ptr), nullptr, 0.0f,
+                    proj_out, nullptr, c.dim, hl_, nullptr, 0, s_);
+        allreduce();
     }
-    gemm(a_xn_, a_xn_lo_, lm_, o_logits_, vn_, c.dim, kEpiStoreF32);
+    // Final RmsNorm + this rank's slice of the tied lm_head, then the all-reduced argmax.
+    launch_gemv(kEpiStore, m_.output() + static_cast<size_t>(v0_) * c.dim, nullptr, X,
+                m_.final_norm(), c.norm_eps, static_cast<float*>(logits_.ptr), nullptr, vn_, c.dim,
+                nullptr, 0, s_);
     tp_argmax_kernel<<<1, 1024, 0, s_>>>(
         P, static_cast<const float*>(logits_.ptr), vn_, v0_, rank_, world_, counter, err, kBudget,
         static_cast<int32_t*>(tok_.ptr), static_cast<int32_t*>(pos_.ptr),

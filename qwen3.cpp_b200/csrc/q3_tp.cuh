@@ -7,7 +7,10 @@
 // a partial sum of x's update: an all-reduce over NVLink peer memory (each rank pushes its 4 KB
 // partial into every peer's buffer, then raises a flag there) adds them in rank order, so x stays
 // bit-identical on every rank. The greedy argmax is all-reduced the same way over the vocabulary
-// slices (lowest index on ties). The reference has no counterpart (it runs on one CPU).
+// slices (lowest index on ties). A step is one captured CUDA graph: CUDA-core GEMVs on the local
+// weight slices (fp32 activations, RmsNorm fused as their prologue), the paged decode attention
+// of the local KV heads, and the two all-reduces. The reference has no counterpart (it runs on
+// one CPU).
 #pragma once
 
 #include <cuda.h>
@@ -18,7 +21,6 @@
 #include <vector>
 
 #include "q3_model.cuh"
-#include "q3_gemm.cuh"
 
 namespace q3 {
 
@@ -54,8 +56,16 @@ private:
     int hq_, hkv_, hl_;     // local query heads, KV heads, MLP rows
     int v0_, vn_;           // local vocabulary rows [v0, v0 + vn)
     cudaStream_t s_ = nullptr;
-    DeviceBuffer shard_;    // per layer: [wq_l; wk_l; wv_l] then [w1_l; w3_l]
-    DeviceBuffer x_, xn_, xn_lo_, qkv_, q32_, o_, o_lo_, part_, gu_, h_, h_lo_, logits_;
+    DeviceBuffer shard_;    // this rank's weight slices (ShardLayer per layer)
+    struct ShardLayer {
+        const uint16_t* wqkv;  // [(hq + 2 hkv) * 128][1024]: local rows of wq; wk; wv
+        const uint16_t* w1;    // [hl][1024]
+        const uint16_t* w3;    // [hl][1024]
+        const uint16_t* wo;    // [1024][hq * 128]: wo[:, local attention columns]
+        const uint16_t* w2;    // [1024][hl]: w2[:, local MLP columns]
+    };
+    std::vector<ShardLayer> layers_;
+    DeviceBuffer x_, qkv_, q32_, o32_, part_, h32_, logits_, scratch_;
     DeviceBuffer pos_, tok_, step_, forced_, log_, err_, counter_, part_o_, part_ml_, attn_counter_;
     DeviceBuffer xbuf_;     // exchange buffer (IPC-exported): data, argmax slots, flags
     std::vector<void*> peer_mapped_;
@@ -63,12 +73,6 @@ private:
     int log_cap_ = 0;
     int attn_pps_ = 8, attn_splits_ = 1;  // decode attention: pages per split, splits
     int sms_ = 0;
-    struct LayerMaps {
-        CUtensorMap wqkv, wo, w13, w2;
-    };
-    std::vector<LayerMaps> wmaps_;
-    CUtensorMap lm_, a_xn_, a_xn_lo_, a_o_, a_o_lo_, a_h_, a_h_lo_, o_qkv_, o_part_, o_gu_,
-        o_logits_;
     cudaGraphExec_t graph_ = nullptr;
     bool graph_forced_ = false;
     const float2* graph_rope_ = nullptr;
