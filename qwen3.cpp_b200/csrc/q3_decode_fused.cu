@@ -56,6 +56,9 @@ constexpr int NCT = NCW * 32;          // consumer threads
 constexpr int NT = NCT + 32;           // + one producer warp
 constexpr int NS = 8;                  // ring slots
 constexpr int kProducerSleepNs = 256;  // back-off of the producer while the ring is full
+// Copies of each layer's down-projection accumulator: CTA c adds into copy c % kYRep, which cuts
+// the number of fp32 atomics per address kYRep-fold; phase A sums the copies.
+constexpr int kYRep = 8;
 constexpr int SLOT = 16384;            // bytes per slot
 // Chunk q lives in slot q % NS and, in warp-owned tasks, is consumed by warp q % NCW; shared
 // chunks (KV pages, w2t rows) are read by every consumer warp. A slot is free again after NCW
@@ -1054,10 +1057,10 @@ __device__ __forceinline__ void combine_group(Smem& sm, const FusedArgs& a, int 
     bar_consumers();
 }
 
-// Phase DE tail: Y[l] += sum_i h_i * w2t[i] over this CTA's MLP indices (shared chunks: warp w
-// owns output columns [128w, 128w+128), 4 per lane), then one float4 atomic per lane.
-__device__ __forceinline__ void down_splitk(Smem& sm, const FusedArgs& a, uint32_t q0, int n,
-                                         float* y) {
+// Phase DE tail: sum_i h_i * w2t[i] over this CTA's MLP indices (shared chunks: warp w owns
+// output columns [128w, 128w+128), 4 per lane); returns this lane's 4 sums (columns
+// 128 warp + 4 lane ..), which the caller adds into Y[l] with one float4 atomic.
+__device__ __forceinline__ float4 down_splitk(Smem& sm, const FusedArgs& a, uint32_t q0, int n) {
     constexpr int RPC = RPC_ROW;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int nch = (n + RPC - 1) / RPC;
@@ -1067,21 +1070,28 @@ __device__ __forceinline__ void down_splitk(Smem& sm, const FusedArgs& a, uint32
         const int slot = qq % NS;
         if (warp_wait_full(sm, slot, (qq / NS) & 1, a)) {
             const int rn = min(RPC, n - ci * RPC);
-            for (int j = 0; j < rn; ++j) {
-                if (!Q3_CHECK(ci * RPC + j < 64, 60, ci, j, n)) break;
-                const float hv = sm.hbuf[ci * RPC + j];
-                const uint2 wv = reinterpret_cast<const uint2*>(sm.ring[slot] + j * D * 2 +
-                                                                warp * 256)[lane];
-                acc[0] = fmaf(hv, bf16_lo(wv.x), acc[0]);
-                acc[1] = fmaf(hv, bf16_hi(wv.x), acc[1]);
-                acc[2] = fmaf(hv, bf16_lo(wv.y), acc[2]);
-                acc[3] = fmaf(hv, bf16_hi(wv.y), acc[3]);
+            // Unrolled with a predicate, so that the 16 shared-memory loads issue back to back.
+            float hv[RPC];
+            uint2 wv[RPC];
+#pragma unroll
+            for (int j = 0; j < RPC; ++j) {
+                const bool in = j < rn && Q3_CHECK(ci * RPC + j < 64, 60, ci, j, n);
+                hv[j] = in ? sm.hbuf[ci * RPC + j] : 0.0f;
+                wv[j] = in ? reinterpret_cast<const uint2*>(sm.ring[slot] + j * D * 2 + warp * 256)[lane]
+                           : make_uint2(0u, 0u);
+            }
+#pragma unroll
+            for (int j = 0; j < RPC; ++j) {
+                acc[0] = fmaf(hv[j], bf16_lo(wv[j].x), acc[0]);
+                acc[1] = fmaf(hv[j], bf16_hi(wv[j].x), acc[1]);
+                acc[2] = fmaf(hv[j], bf16_lo(wv[j].y), acc[2]);
+                acc[3] = fmaf(hv[j], bf16_hi(wv[j].y), acc[3]);
             }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.empty[slot]);  // one of NCW releases of a shared chunk
     }
-    red_add4(y + warp * 128 + lane * 4, make_float4(acc[0], acc[1], acc[2], acc[3]));
+    return make_float4(acc[0], acc[1], acc[2], acc[3]);
 }
 
 // Write back the attention-sink rows of KV head g rotated by RoPE(position 1) (:817-827); every
@@ -1171,6 +1181,17 @@ __device__ __forceinline__ void phase_end(Smem& sm, const FusedArgs& a, unsigned
     }
 }
 
+// This thread's four elements of a layer's down-projection output: the sum of its kYRep copies.
+__device__ __forceinline__ float4 sum_y(const float* y) {
+    float4 v[kYRep];
+#pragma unroll
+    for (int r = 0; r < kYRep; ++r) v[r] = __ldcg(reinterpret_cast<const float4*>(y + r * D) + threadIdx.x);
+    float4 t = v[0];
+#pragma unroll
+    for (int r = 1; r < kYRep; ++r) t = add4(t, v[r]);
+    return t;
+}
+
 // Phase A input: the embedding row of the step's token (layer 0; the token is the greedy argmax of
 // the previous step, or the teacher-forced one) or x = Xcur + Y[l-1], with Xcur this thread's four
 // elements of the residual stream after the previous layer's o_proj (kept in registers) and yb the
@@ -1199,11 +1220,11 @@ __device__ __forceinline__ float4 phase_a_input(Smem& sm, const FusedArgs& a, co
         // Zero this CTA's share of the other step parity's down-projection accumulators: their
         // last readers arrived at the previous step's lm_head barrier, their next writers (next
         // step) come after this step's.
-        float* yz = a.ybuf + static_cast<size_t>((st + 1) & 1) * a.n_layers * D;
-        const Span ys = part(a.n_layers * D, G, c);
+        float* yz = a.ybuf + static_cast<size_t>((st + 1) & 1) * a.n_layers * kYRep * D;
+        const Span ys = part(a.n_layers * kYRep * D, G, c);
         for (int i = tid; i < ys.n; i += NCT) yz[ys.r0 + i] = 0.0f;
     } else {
-        xv = add4(xcur, __ldcg(reinterpret_cast<const float4*>(yb + static_cast<size_t>(l - 1) * D) + tid));
+        xv = add4(xcur, sum_y(yb + static_cast<size_t>(l - 1) * kYRep * D));
     }
     if (a.taps && c == 0) reinterpret_cast<float4*>(a.taps + static_cast<size_t>(l) * D)[tid] = xv;
     return xv;
@@ -1262,7 +1283,7 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) 
 
     for (int st = 0; st < a.n_steps; ++st) {
         const StepPos p = step_pos(a, sp0, st);
-        float* yb = a.ybuf + static_cast<size_t>(st & 1) * a.n_layers * D;
+        float* yb = a.ybuf + static_cast<size_t>(st & 1) * a.n_layers * kYRep * D;
         for (int l = 0; l < a.n_layers; ++l) {
             const FusedLayer w = a.layers[l];
             const unsigned tag = step_tag(a, st, l);
@@ -1332,9 +1353,10 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) 
                 q += chunks_of(hs.n, RPC_PAIR);
                 bar_consumers();
                 stamp(a, k, G, c, 3);
-                down_splitk(sm, a, q, hs.n, yb + static_cast<size_t>(l) * D);
+                const float4 yd = down_splitk(sm, a, q, hs.n);
                 q += chunks_of(hs.n, RPC_ROW);
                 stamp(a, k, G, c, 4);
+                red_add4(yb + (static_cast<size_t>(l) * kYRep + c % kYRep) * D + 4 * tid, yd);
                 if (c < NKV && p.num_sink > 0) sink_writeback(a, hp, l, c, p.num_sink);
                 phase_end(sm, a, k++, true, G, c);
                 ++nb;
@@ -1343,8 +1365,7 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) 
         // ---- final RmsNorm + lm_head + per-CTA argmax
         const uint2 fw = load_norm(a.final_norm);
         if (!phase_begin(sm, a, k, nb, G, c)) return;
-        const float4 xv = add4(xcur, __ldcg(reinterpret_cast<const float4*>(
-                                               yb + static_cast<size_t>(a.n_layers - 1) * D) + tid));
+        const float4 xv = add4(xcur, sum_y(yb + static_cast<size_t>(a.n_layers - 1) * kYRep * D));
         if (a.taps && c == 0) {
             reinterpret_cast<float4*>(a.taps + static_cast<size_t>(a.n_layers) * D)[tid] = xv;
         }
@@ -1436,6 +1457,8 @@ bool fused_supported(const q3_config& c) {
 }
 
 size_t fused_smem_bytes() { return sizeof(Smem); }
+
+size_t fused_ybuf_floats(int n_layers) { return 2ull * n_layers * kYRep * D; }
 
 int fused_l2_ahead() {
     // Layers of L2 run-ahead; Q3_FUSED_L2_AHEAD overrides (0 turns the prefetch off).

@@ -39,8 +39,8 @@ struct FusedArgs {
     const int32_t* page_table;
     const float2* rope;          // [rope_len][64] (cos, sin)
     int rope_len;
-    float* ybuf;                 // [2][n_layers][1024] down-projection accumulators (by step
-                                 // parity; parity 0 zero at launch)
+    float* ybuf;                 // [2][n_layers][copies][1024] down-projection accumulators (by
+                                 // step parity; parity 0 zero at launch), fused_ybuf_floats()
     unsigned long long* qkvt;    // [4096] q|k|v, tagged (value bits | tag << 32)
     unsigned long long* opart;   // [8][1024] o_proj partial of each KV-head group, tagged
     unsigned epoch;              // tag base of this launch (differs from the previous launch)
@@ -70,6 +70,8 @@ int fused_grid(int device);
 size_t fused_smem_bytes();
 // Layers of weights prefetched into L2 ahead of the ring copies.
 int fused_l2_ahead();
+// Floats of FusedArgs::ybuf for n_layers.
+size_t fused_ybuf_floats(int n_layers);
 void launch_decode_fused(const FusedArgs& a, int grid, cudaStream_t s);
 // Phases of one decode step at kv_len (3 per layer up to 128 positions, else 4; + lm_head).
 int fused_phases_per_step(int n_layers, int kv_len);

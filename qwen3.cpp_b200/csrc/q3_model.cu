@@ -682,7 +682,7 @@ Model::Model(const std::string& path, int ctx, int device) : file_(path) {
             fused_layers_.alloc(fl.size() * sizeof(FusedLayer));
             Q3_CUDA(cudaMemcpy(fused_layers_.ptr, fl.data(), fl.size() * sizeof(FusedLayer),
                                cudaMemcpyHostToDevice));
-            fused_y_.alloc(2 * static_cast<size_t>(c.n_layers) * D * 4);
+            fused_y_.alloc(fused_ybuf_floats(c.n_layers) * 4);
             // Tagged q|k|v [4096] and o_proj partials [8][1024]; zero tags never match a launch's.
             fused_tagged_.alloc((static_cast<size_t>(c.n_heads + 2 * c.n_kv_heads) * c.head_dim +
                                  static_cast<size_t>(c.n_kv_heads) * D) * 8);
