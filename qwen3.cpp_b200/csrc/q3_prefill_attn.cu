@@ -433,17 +433,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             // they agree on it without exchanging). Scores are scaled after the max (scale > 0).
             const bool full_tile = tile_key0 + KEYS - 1 <= qpos;  // no masked key in this tile
             float sv[64];
-            float mx = -1e30f;
             tmem_ld64(sb, sv);
+            // Max as 8 independent chains and a tree (short dependent latency).
+            float mx8[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) mx8[j] = -1e30f;
             if (full_tile) {
 #pragma unroll
-                for (int k = 0; k < 64; ++k) mx = fmaxf(mx, sv[k]);
+                for (int k = 0; k < 64; ++k) mx8[k & 7] = fmaxf(mx8[k & 7], sv[k]);
             } else {
 #pragma unroll
                 for (int k = 0; k < 64; ++k) {
-                    if (key0 + k <= qpos) mx = fmaxf(mx, sv[k]);
+                    if (key0 + k <= qpos) mx8[k & 7] = fmaxf(mx8[k & 7], sv[k]);
                 }
             }
+            float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
             const float other = exchange_row(red, mx_bar, t, half, r, mx, a.budget, abort);
             if (other != other) {
                 fail(abort, a.err, 19);
@@ -465,9 +470,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
                 for (int k = 0; k < 64; ++k) sv[k] = key0 + k <= qpos ? sv[k] : 0.0f;
             }
-            float2 s2 = make_float2(0.0f, 0.0f);
+            float2 s4[4] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f),
+                            make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
 #pragma unroll
-            for (int k = 0; k < 64; k += 2) s2 = fadd2(s2, make_float2(sv[k], sv[k + 1]));
+            for (int k = 0; k < 64; k += 2) s4[(k >> 1) & 3] = fadd2(s4[(k >> 1) & 3], make_float2(sv[k], sv[k + 1]));
+            const float2 s2 = fadd2(fadd2(s4[0], s4[1]), fadd2(s4[2], s4[3]));
             sum = s2.x + s2.y;
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
