@@ -309,6 +309,89 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     }
                     stage_store(row, tn * (BN / 2) + c, y);
                 }
+            } else if (EPI == kEpiQkvRope) {
+                // Two 128-column heads per tile; this thread's row is token y + lane.
+                const QkvEpilogue& e = args.qkv;
+                const int token = y + lane;
+                const bool live = token < args.M;
+                const int pos = e.pos0 + token;
+                const int nq = e.n_heads, nk = e.n_kv;
+#pragma unroll 1
+                for (int hh = 0; hh < 2; ++hh) {
+                    const int head = tn * 2 + hh;
+                    const uint32_t hcol = tb_addr + hh * 128;
+                    const bool qk = head < nq + nk;
+                    // Pass 1 (q, k): the head's sum of squares.
+                    float inv = 1.0f;
+                    if (qk) {
+                        float ss = 0.0f;
+#pragma unroll 1
+                        for (int c = 0; c < 128; c += 32) {
+                            float t32[32];
+                            tmem_ld32(hcol + c, t32);
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) ss = fmaf(t32[i], t32[i], ss);
+                        }
+                        inv = 1.0f / sqrtf(ss / 128.0f + e.eps);
+                    }
+                    uint16_t* dst = nullptr;
+                    if (live) {
+                        if (head < nq) {
+                            dst = e.q_out + static_cast<size_t>(token) * nq * 128 + head * 128;
+                        } else {
+                            const int g = qk ? head - nq : head - nq - nk;
+                            const size_t page = static_cast<size_t>(__ldg(e.page_table + pos / 16));
+                            dst = (qk ? e.k_cache : e.v_cache) + ((page * nk + g) * 16 + pos % 16) * 128;
+                        }
+                    }
+                    const uint16_t* w = head < nq ? e.q_norm : e.k_norm;
+                    const float4* cs = reinterpret_cast<const float4*>(
+                        e.rope + static_cast<size_t>(live ? pos : e.pos0) * 64);
+                    // Pass 2: columns (c .. c+31) and their RoPE partners (c+64 ..), normalised
+                    // (:800-807), rotated (:809-810: (a, b) -> (a cos - b sin, b cos + a sin)), bf16.
+#pragma unroll 1
+                    for (int c = 0; c < 64; c += 32) {
+                        float a[32], b[32];
+                        tmem_ld32(hcol + c, a);
+                        tmem_ld32(hcol + 64 + c, b);
+                        if (qk) {
+#pragma unroll
+                            for (int i = 0; i < 32; i += 8) {
+                                const uint4 wa = __ldg(reinterpret_cast<const uint4*>(w + c + i));
+                                const uint4 wb = __ldg(reinterpret_cast<const uint4*>(w + 64 + c + i));
+                                const uint32_t wav[4] = {wa.x, wa.y, wa.z, wa.w};
+                                const uint32_t wbv[4] = {wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+                                for (int j = 0; j < 4; ++j) {
+                                    a[i + 2 * j] = (a[i + 2 * j] * inv) * __uint_as_float(wav[j] << 16);
+                                    a[i + 2 * j + 1] = (a[i + 2 * j + 1] * inv) * __uint_as_float(wav[j] & 0xffff0000u);
+                                    b[i + 2 * j] = (b[i + 2 * j] * inv) * __uint_as_float(wbv[j] << 16);
+                                    b[i + 2 * j + 1] = (b[i + 2 * j + 1] * inv) * __uint_as_float(wbv[j] & 0xffff0000u);
+                                }
+                            }
+#pragma unroll
+                            for (int i = 0; i < 32; i += 2) {
+                                const float4 c2 = __ldg(cs + (c + i) / 2);  // (cos, sin) of c+i, c+i+1
+                                const float a0 = a[i], b0 = b[i], a1 = a[i + 1], b1 = b[i + 1];
+                                a[i] = a0 * c2.x - b0 * c2.y;
+                                b[i] = b0 * c2.x + a0 * c2.y;
+                                a[i + 1] = a1 * c2.z - b1 * c2.w;
+                                b[i + 1] = b1 * c2.z + a1 * c2.w;
+                            }
+                        }
+                        if (live) {
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                reinterpret_cast<uint4*>(dst + c)[i] = make_uint4(
+                                    pack_bf16(a[8 * i], a[8 * i + 1]), pack_bf16(a[8 * i + 2], a[8 * i + 3]),
+                                    pack_bf16(a[8 * i + 4], a[8 * i + 5]), pack_bf16(a[8 * i + 6], a[8 * i + 7]));
+                                reinterpret_cast<uint4*>(dst + 64 + c)[i] = make_uint4(
+                                    pack_bf16(b[8 * i], b[8 * i + 1]), pack_bf16(b[8 * i + 2], b[8 * i + 3]),
+                                    pack_bf16(b[8 * i + 4], b[8 * i + 5]), pack_bf16(b[8 * i + 6], b[8 * i + 7]));
+                            }
+                        }
+                    }
+                }
             } else if (EPI == kEpiStoreBF16) {
 #pragma unroll 1
                 for (int c = 0; c < BN; c += 64) {
@@ -481,7 +564,7 @@ void make_tmap_kv_pages(CUtensorMap* map, const void* base, uint64_t n_kv, uint6
 }
 
 int gemm_tile_n(int epi, int N) {
-    if (epi == kEpiSwiGLU) return 256;
+    if (epi == kEpiSwiGLU || epi == kEpiQkvRope) return 256;
     return N % 256 == 0 ? 256 : 128;
 }
 
@@ -493,6 +576,7 @@ void prepare_gemm_kernels() {
     Q3_CUDA((configure_t<256, kEpiStoreBF16>()));
     Q3_CUDA((configure_t<128, kEpiStoreBF16>()));
     Q3_CUDA((configure_t<256, kEpiSwiGLU>()));
+    Q3_CUDA((configure_t<256, kEpiQkvRope>()));
     Q3_CUDA((configure_t<128, kEpiStoreF32, true>()));
     Q3_CUDA((configure_t<128, kEpiAddF32, true>()));
     Q3_CUDA((configure_t<256, kEpiStoreF32, true>()));
@@ -506,6 +590,10 @@ cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtens
     const int bn = args.bn ? args.bn : gemm_tile_n(epi, args.N);
     if ((bn != 128 && bn != 256) || args.N % bn != 0) return cudaErrorInvalidValue;
     if (epi == kEpiSwiGLU && (!b2 || bn != 256)) return cudaErrorInvalidValue;
+    if (epi == kEpiQkvRope && (bn != 256 || !args.qkv.q_out || !args.qkv.k_cache ||
+                               !args.qkv.v_cache || !args.qkv.page_table || !args.qkv.rope)) {
+        return cudaErrorInvalidValue;
+    }
     const CUtensorMap& bb = b2 ? *b2 : b;
     if (a_lo) {
         if (epi == kEpiStoreF32) {
@@ -530,6 +618,8 @@ cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtens
                              : launch_t<128, kEpiStoreBF16>(a, b, bb, out, args, num_sms, stream, a);
         case kEpiSwiGLU:
             return launch_t<256, kEpiSwiGLU>(a, b, bb, out, args, num_sms, stream, a);
+        case kEpiQkvRope:
+            return launch_t<256, kEpiQkvRope>(a, b, bb, out, args, num_sms, stream, a);
     }
     return cudaErrorInvalidValue;
 }

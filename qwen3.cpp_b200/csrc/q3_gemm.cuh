@@ -16,6 +16,22 @@ enum GemmEpilogue : int {
     kEpiSwiGLU = 2,    // B rows = 128 of w1 then the same 128 of w3 per tile; out bf16 [M, N/2]:
                        // h = silu(w1 . x) * (w3 . x)
     kEpiStoreBF16 = 3, // out[m, n] = bf16(acc)
+    kEpiQkvRope = 4,   // [wq;wk;wv] rows: per 128-column head QK-RMSNorm + RoPE of q and k, then q
+                       // rows to GemmArgs::qkv.q_out (bf16) and k, v rows into the paged cache
+};
+
+// Destinations of the kEpiQkvRope epilogue (src/inference.cpp:800-815 for every row m, the token
+// at position pos0 + m).
+struct QkvEpilogue {
+    uint16_t* q_out = nullptr;           // [M, n_heads * 128] bf16
+    uint16_t* k_cache = nullptr;         // this layer's paged pools [page][n_kv][16][128] bf16
+    uint16_t* v_cache = nullptr;
+    const int32_t* page_table = nullptr; // page of positions [16p, 16p + 16)
+    const float2* rope = nullptr;        // [pos][64] (cos, sin)
+    const uint16_t* q_norm = nullptr;    // [128]
+    const uint16_t* k_norm = nullptr;    // [128]
+    int pos0 = 0, n_heads = 0, n_kv = 0;
+    float eps = 0.0f;
 };
 
 // A 2-D K-major bf16 matrix [rows, cols] (cols contiguous) as a TMA tensor map with 128-byte
@@ -47,6 +63,7 @@ struct GemmArgs {
     int bn = 0;               // tile width override (128 or 256; 0: gemm_tile_n)
     int max_ksplit = 4;       // residual add: split K up to this many slices ...
     int min_slice_kblocks = 8;  // ... of at least this many 64-wide k-blocks
+    QkvEpilogue qkv;            // kEpiQkvRope only
 };
 
 // Opts every contraction kernel into its shared memory on the current device (launch_gemm does it

@@ -420,10 +420,8 @@ void Prefill::ensure_rows(int rows) {
     const int cap = (rows + 127) / 128 * 128;
     const q3_config& c = cfg_;
     const size_t qd = static_cast<size_t>(c.n_heads) * HD;
-    const size_t qkv = static_cast<size_t>(c.n_heads + 2 * c.n_kv_heads) * HD;
     x_.alloc(static_cast<size_t>(cap) * c.dim * 4);
     xn_.alloc(static_cast<size_t>(cap) * c.dim * 2);
-    qkv_.alloc(static_cast<size_t>(cap) * qkv * 4);
     q_.alloc(static_cast<size_t>(cap) * qd * 2);
     o_.alloc(static_cast<size_t>(cap) * qd * 2);
     h_.alloc(static_cast<size_t>(cap) * c.hidden_dim * 2);
@@ -519,8 +517,7 @@ void Prefill::run(const int32_t* ids_dev, int n, int pos0, const uint16_t* embed
         make_tmap_bf16(&m_xn, xn_.ptr, S, c.dim, 128);
         make_tmap_bf16(&m_o, o_.ptr, S, qd, 128);
         make_tmap_bf16(&m_h, h_.ptr, S, c.hidden_dim, 128);
-        CUtensorMap o_qkv, o_x, o_h;  // contraction outputs
-        make_tmap_out(&o_qkv, qkv_.ptr, S, qkv, false);
+        CUtensorMap o_x, o_h;  // contraction outputs
         make_tmap_out(&o_x, X, S, c.dim, false);
         make_tmap_out(&o_h, h_.ptr, S, c.hidden_dim, true);
         auto tap = [&](int slot) {
@@ -539,25 +536,23 @@ void Prefill::run(const int32_t* ids_dev, int n, int pos0, const uint16_t* embed
             GemmArgs g;
             g.err = err;
             g.M = S;
-            // [wq; wk; wv] . xn -> fp32 q|k|v rows (src/inference.cpp:795-798).
+            // [wq; wk; wv] . xn (src/inference.cpp:795-798) with the QK-RMSNorm, RoPE and the
+            // paged K/V write (:800-815) in the epilogue: q rows to q_ (bf16).
             g.N = qkv;
             g.K = c.dim;
-            Q3_CUDA(launch_gemm(m_xn, wm.wqkv, nullptr, o_qkv, g, kEpiStoreF32, num_sms_, s));
-            PrefillQkvArgs qa{};
-            qa.qkv = static_cast<float*>(qkv_.ptr);
-            qa.q_norm = w.q_norm;
-            qa.k_norm = w.k_norm;
-            qa.rope = kv.rope;
-            qa.q_out = static_cast<uint16_t*>(q_.ptr);
-            qa.k_cache = kv.k_base + layer_elems(kv) * l;
-            qa.v_cache = kv.v_base + layer_elems(kv) * l;
-            qa.page_table = kv.page_table;
-            qa.rows = S;
-            qa.pos0 = p0;
-            qa.n_heads = c.n_heads;
-            qa.n_kv = c.n_kv_heads;
-            qa.eps = c.norm_eps;
-            launch_prefill_qkv(qa, s);
+            g.qkv.q_out = static_cast<uint16_t*>(q_.ptr);
+            g.qkv.k_cache = kv.k_base + layer_elems(kv) * l;
+            g.qkv.v_cache = kv.v_base + layer_elems(kv) * l;
+            g.qkv.page_table = kv.page_table;
+            g.qkv.rope = kv.rope;
+            g.qkv.q_norm = w.q_norm;
+            g.qkv.k_norm = w.k_norm;
+            g.qkv.pos0 = p0;
+            g.qkv.n_heads = c.n_heads;
+            g.qkv.n_kv = c.n_kv_heads;
+            g.qkv.eps = c.norm_eps;
+            Q3_CUDA(launch_gemm(m_xn, wm.wqkv, nullptr, m_xn, g, kEpiQkvRope, num_sms_, s));
+            g.qkv = QkvEpilogue{};
             if (use_tc_attention_) {
                 PrefillAttnTcArgs ta{};
                 ta.page_table = kv.page_table;

@@ -134,7 +134,7 @@ private:
     int num_sms_ = 148;
     int cap_rows_ = 0;
     bool use_tc_attention_ = true;
-    DeviceBuffer x_, xn_, qkv_, q_, o_, h_, err_;
+    DeviceBuffer x_, xn_, q_, o_, h_, err_;
     struct LayerMaps {
         CUtensorMap wqkv, wo, w1, w3, w2;
     };
