@@ -36,6 +36,8 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
 // hi + lo pair.
 __global__ void swiglu_rows_kernel(const float* __restrict__ gu, uint16_t* __restrict__ h,
                                    uint16_t* __restrict__ h_lo, int rows, int H) {
+    pdl_wait();
+    pdl_trigger();
     const size_t n = static_cast<size_t>(rows) * H / 4;
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
          i += static_cast<size_t>(gridDim.x) * blockDim.x) {
@@ -60,6 +62,8 @@ __global__ void __launch_bounds__(1024) batch_argmax_kernel(const float* __restr
                                                             int32_t* pos, int32_t* log,
                                                             const int32_t* state,
                                                             const int32_t* forced) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float bv[32];
     __shared__ int bi[32];
     const int b = blockIdx.x;
@@ -101,7 +105,11 @@ __global__ void __launch_bounds__(1024) batch_argmax_kernel(const float* __restr
     }
 }
 
-__global__ void advance_step_kernel(int32_t* state) { state[0] += 1; }
+__global__ void advance_step_kernel(int32_t* state) {
+    pdl_wait();
+    pdl_trigger();
+    state[0] += 1;
+}
 
 }  // namespace
 
@@ -327,10 +335,10 @@ void Batch::enqueue_step(bool forced, int n_forced) {
         Q3_CUDA(cudaMemsetAsync(gu_.ptr, 0, gu_.bytes, s_));
         gemm(a_xn_, a_xn_lo_, wm.w13, o_gu_, 2 * H, c.dim, kEpiAddF32);
         const size_t quads = static_cast<size_t>(B) * H / 4;
-        swiglu_rows_kernel<<<static_cast<unsigned>(std::min<size_t>((quads + 255) / 256, 4096)),
-                             256, 0, s_>>>(static_cast<const float*>(gu_.ptr),
-                                           static_cast<uint16_t*>(h_.ptr),
-                                           static_cast<uint16_t*>(h_lo_.ptr), B, H);
+        launch_dep(false, swiglu_rows_kernel,
+                   dim3(static_cast<unsigned>(std::min<size_t>((quads + 255) / 256, 4096))), dim3(256),
+                   0, s_, static_cast<const float*>(gu_.ptr), static_cast<uint16_t*>(h_.ptr),
+                   static_cast<uint16_t*>(h_lo_.ptr), B, H);
         Q3_CUDA(cudaGetLastError());
         gemm(a_h_, a_h_lo_, wm.w2, o_x_, c.dim, H, kEpiAddF32);
         const uint16_t* next_norm = l + 1 < c.n_layers ? m_.layer(l + 1).attn_norm : m_.final_norm();
@@ -339,13 +347,13 @@ void Batch::enqueue_step(bool forced, int n_forced) {
     }
     // Tied lm_head for every row, argmax and the advance.
     gemm(a_xn_, a_xn_lo_, lm_, o_logits_, c.vocab_size, c.dim, kEpiStoreF32);
-    batch_argmax_kernel<<<B, 1024, 0, s_>>>(
-        static_cast<const float*>(logits_.ptr), B, c.vocab_size, static_cast<int32_t*>(tok_.ptr),
-        static_cast<int32_t*>(pos_.ptr), static_cast<int32_t*>(log_.ptr),
-        static_cast<const int32_t*>(step_.ptr),
-        forced ? static_cast<const int32_t*>(forced_.ptr) : nullptr);
+    launch_dep(false, batch_argmax_kernel, dim3(B), dim3(1024), 0, s_,
+               static_cast<const float*>(logits_.ptr), B, c.vocab_size,
+               static_cast<int32_t*>(tok_.ptr), static_cast<int32_t*>(pos_.ptr),
+               static_cast<int32_t*>(log_.ptr), static_cast<const int32_t*>(step_.ptr),
+               forced ? static_cast<const int32_t*>(forced_.ptr) : nullptr);
     Q3_CUDA(cudaGetLastError());
-    advance_step_kernel<<<1, 1, 0, s_>>>(static_cast<int32_t*>(step_.ptr));
+    launch_dep(false, advance_step_kernel, dim3(1), dim3(1), 0, s_, static_cast<int32_t*>(step_.ptr));
     Q3_CUDA(cudaGetLastError());
     (void)n_forced;
 }

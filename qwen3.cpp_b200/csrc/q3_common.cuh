@@ -6,6 +6,7 @@
 
 #include <stdexcept>
 #include <string>
+#include <utility>
 
 #include "q3_b200.h"
 
@@ -50,6 +51,37 @@ q3_status guard(F&& fn) {
         set_last_error(e.what());
         return Q3_ERR_RUNTIME;
     }
+}
+
+// ------------------------------------------------------------------ dependent launches
+
+// Programmatic dependent launch: a kernel launched by launch_dep(dependent = true) may start
+// (prologue, shared memory and TMEM set-up) while the kernel before it in the stream finishes; its
+// pdl_wait() blocks until that kernel has completed and its writes are visible, so every kernel
+// launched this way calls it before its first global-memory access. pdl_trigger() lets the next
+// kernel's blocks be scheduled once all blocks of this one have started. Both are no-ops for a
+// kernel launched without the attribute. Measured: the prefill's long kernels gain (4.04 -> 3.68 ms
+// for 2048 tokens); the graph-captured decode steps of many short kernels lose 4-10%, so they
+// launch without it.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+void launch_dep(bool dependent, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                cudaStream_t s, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = dependent ? 1 : 0;
+    Q3_CUDA(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
 }
 
 // ------------------------------------------------------------------ device helpers

@@ -48,6 +48,8 @@ __device__ __forceinline__ void put_out(const DecodeAttnArgs& a, size_t off, flo
 }
 
 __global__ void __launch_bounds__(DA_THREADS) decode_attn_kernel(const DecodeAttnArgs a) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ __align__(16) float s_o[DA_WARPS][2][HD];  // written as float4
     __shared__ float2 s_ml[DA_WARPS][2];
     __shared__ int s_last;
@@ -330,7 +332,7 @@ void launch_decode_attention(const DecodeAttnArgs& a, cudaStream_t s) {
         throw std::invalid_argument("decode attention: 1..64 splits of at least one page");
     }
     const dim3 grid(static_cast<unsigned>(a.rows * a.n_kv * a.max_splits));
-    decode_attn_kernel<<<grid, DA_THREADS, 0, s>>>(a);
+    launch_dep(false, decode_attn_kernel, grid, dim3(DA_THREADS), 0, s, a);
     Q3_CUDA(cudaGetLastError());
 }
 

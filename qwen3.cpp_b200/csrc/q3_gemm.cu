@@ -140,6 +140,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // Set-up above touches no global data; the previous kernel's outputs are read below.
+    pdl_wait();
+    pdl_trigger();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -498,7 +501,7 @@ cudaError_t launch_t(const CUtensorMap& a, const CUtensorMap& b, const CUtensorM
     const int tiles = mn_tiles * g.ksplit;
     const int grid = tiles < num_sms ? tiles : num_sms;
     if (grid <= 0) return cudaSuccess;
-    kern<<<grid, NTHREADS, C::SMEM_BYTES, stream>>>(a, b, b2, out, a_lo, g);
+    launch_dep(g.dependent, kern, dim3(grid), dim3(NTHREADS), C::SMEM_BYTES, stream, a, b, b2, out, a_lo, g);
     return cudaGetLastError();
 }
 

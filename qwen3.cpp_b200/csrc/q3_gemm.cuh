@@ -64,6 +64,7 @@ struct GemmArgs {
     int max_ksplit = 4;       // residual add: split K up to this many slices ...
     int min_slice_kblocks = 8;  // ... of at least this many 64-wide k-blocks
     QkvEpilogue qkv;            // kEpiQkvRope only
+    bool dependent = false;     // programmatic dependent launch (see launch_dep)
 };
 
 // Opts every contraction kernel into its shared memory on the current device (launch_gemm does it

@@ -67,6 +67,8 @@ gemv_kernel(const uint16_t* __restrict__ W, const uint16_t* __restrict__ Wb,
             const float* __restrict__ x, const uint16_t* __restrict__ nw, float eps,
             float* out, float* lin2, int n, int k, float2* argmax_part) {
     extern __shared__ float4 smem4[];
+    pdl_wait();
+    pdl_trigger();
     float* xs = reinterpret_cast<float*>(smem4);
     __shared__ float red[32];
     __shared__ float2 best_s[kGemvWarps];
@@ -153,7 +155,7 @@ void gemv_launch_t(const uint16_t* W, const uint16_t* Wb, const float* x, const 
         Q3_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
         configured[dev & 63] = true;
     }
-    fn<<<grid, kGemvThreads, smem, s>>>(W, Wb, x, nw, eps, out, lin2, n, k, part);
+    launch_dep(false, fn, dim3(grid), dim3(kGemvThreads), smem, s, W, Wb, x, nw, eps, out, lin2, n, k, part);
     Q3_CUDA(cudaGetLastError());
 }
 

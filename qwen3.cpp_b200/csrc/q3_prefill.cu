@@ -34,6 +34,8 @@ __global__ void __launch_bounds__(kNormWarps * 32)
                         float* __restrict__ x, const uint16_t* __restrict__ w, float eps,
                         uint16_t* __restrict__ out, uint16_t* __restrict__ out_lo, int rows,
                         int dim) {
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int row = blockIdx.x * kNormWarps + (threadIdx.x >> 5);
     if (row >= rows) return;
@@ -79,6 +81,8 @@ __global__ void __launch_bounds__(kNormWarps * 32)
 // One warp per (token, head); lane l holds elements 4l..4l+3 of the 128-wide head, so the RoPE
 // partner of element e (e + 64 or e - 64) sits in lane l ^ 16.
 __global__ void __launch_bounds__(256) prefill_qkv_kernel(PrefillQkvArgs a) {
+    pdl_wait();
+    pdl_trigger();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x;
     const int head = blockIdx.y * 8 + warp;
@@ -370,18 +374,18 @@ int device_sms(int device) {
 
 void launch_rmsnorm_rows_bf16(const int32_t* ids, const uint16_t* embed, float* x,
                               const uint16_t* w, float eps, uint16_t* out, int rows, int dim,
-                              cudaStream_t s, uint16_t* out_lo) {
+                              cudaStream_t s, uint16_t* out_lo, bool dependent) {
     if (rows <= 0) return;
     if (dim % 256 != 0) throw std::invalid_argument("row RmsNorm needs a width that is a multiple of 256");
-    rmsnorm_rows_kernel<<<(rows + kNormWarps - 1) / kNormWarps, kNormWarps * 32, 0, s>>>(
-        ids, embed, x, w, eps, out, out_lo, rows, dim);
+    launch_dep(dependent, rmsnorm_rows_kernel, dim3((rows + kNormWarps - 1) / kNormWarps),
+               dim3(kNormWarps * 32), 0, s, ids, embed, x, w, eps, out, out_lo, rows, dim);
     Q3_CUDA(cudaGetLastError());
 }
 
 void launch_prefill_qkv(const PrefillQkvArgs& a, cudaStream_t s) {
     if (a.rows <= 0) return;
     const dim3 grid(a.rows, (a.n_heads + 2 * a.n_kv + 7) / 8);
-    prefill_qkv_kernel<<<grid, 256, 0, s>>>(a);
+    launch_dep(false, prefill_qkv_kernel, grid, dim3(256), 0, s, a);
     Q3_CUDA(cudaGetLastError());
 }
 
@@ -528,13 +532,14 @@ void Prefill::run(const int32_t* ids_dev, int n, int pos0, const uint16_t* embed
             }
         };
         launch_rmsnorm_rows_bf16(ids_dev + c0, embed, X, layers[0].attn_norm, c.norm_eps, Xn, S,
-                                 c.dim, s);
+                                 c.dim, s, nullptr, true);
         tap(0);
         for (int l = 0; l < L; ++l) {
             const LayerWeights& w = layers[l];
             const LayerMaps& wm = wmaps_[l];
             GemmArgs g;
             g.err = err;
+            g.dependent = true;  // the prefill's kernels launch as programmatic dependents
             g.M = S;
             // [wq; wk; wv] . xn (src/inference.cpp:795-798) with the QK-RMSNorm, RoPE and the
             // paged K/V write (:800-815) in the epilogue: q rows to q_ (bf16).
@@ -582,7 +587,8 @@ void Prefill::run(const int32_t* ids_dev, int n, int pos0, const uint16_t* embed
             g.N = c.dim;
             g.K = qd;
             Q3_CUDA(launch_gemm(m_o, wm.wo, nullptr, o_x, g, kEpiAddF32, num_sms_, s));
-            launch_rmsnorm_rows_bf16(nullptr, nullptr, X, w.mlp_norm, c.norm_eps, Xn, S, c.dim, s);
+            launch_rmsnorm_rows_bf16(nullptr, nullptr, X, w.mlp_norm, c.norm_eps, Xn, S, c.dim, s,
+                                     nullptr, true);
             // h = silu(w1 . xn) * (w3 . xn) (:851, :1005-1011).
             g.N = 2 * c.hidden_dim;
             g.K = c.dim;
@@ -593,7 +599,7 @@ void Prefill::run(const int32_t* ids_dev, int n, int pos0, const uint16_t* embed
             Q3_CUDA(launch_gemm(m_h, wm.w2, nullptr, o_x, g, kEpiAddF32, num_sms_, s));
             if (l + 1 < L) {
                 launch_rmsnorm_rows_bf16(nullptr, nullptr, X, layers[l + 1].attn_norm, c.norm_eps,
-                                         Xn, S, c.dim, s);
+                                         Xn, S, c.dim, s, nullptr, true);
             }
             tap(l + 1);
         }

@@ -17,9 +17,10 @@ namespace q3 {
 // Row-wise RmsNorm (src/inference.cpp:887-923) of fp32 rows into bf16 MMA operands; with ids
 // non-null, the fp32 rows are first gathered from the embedding (:601-603) into x.
 // out_lo (nullable) receives y - bf16(y), so that out + out_lo carries 16 significant bits.
+// dependent: programmatic dependent launch (launch_dep).
 void launch_rmsnorm_rows_bf16(const int32_t* ids, const uint16_t* embed, float* x,
                               const uint16_t* w, float eps, uint16_t* out, int rows, int dim,
-                              cudaStream_t s, uint16_t* out_lo = nullptr);
+                              cudaStream_t s, uint16_t* out_lo = nullptr, bool dependent = false);
 
 // Per-token, per-head QK-RMSNorm + RoPE (src/inference.cpp:800-810) and bf16 K/V write into the
 // paged cache at kv_pos = pos (:812-815) for tokens at positions pos0 .. pos0+rows-1, all below

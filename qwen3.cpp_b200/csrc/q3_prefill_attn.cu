@@ -182,6 +182,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                            const __grid_constant__ CUtensorMap tk4,
                            const __grid_constant__ CUtensorMap tv4, const PrefillAttnTcArgs a) {
     extern __shared__ __align__(1024) uint8_t sm[];
+    pdl_wait();
+    pdl_trigger();
     // The swizzled operand panels need a 1024-byte aligned base; nothing is touched otherwise.
     if ((smem_u32(sm) & 1023) != 0) {
         if (threadIdx.x == 0 && a.err) atomicCAS(a.err, 0u, 10u);
@@ -566,7 +568,7 @@ void launch_prefill_attention_tc(const CUtensorMap& q, const CUtensorMap& k, con
         configured[dev & 63] = true;
     }
     const dim3 grid(((a.rows + TOK - 1) / TOK) * a.n_kv);
-    prefill_attn_tc_kernel<<<grid, NTHREADS, SMEM, s>>>(q, k, v, k4, v4, a);
+    launch_dep(true, prefill_attn_tc_kernel, grid, dim3(NTHREADS), SMEM, s, q, k, v, k4, v4, a);
     Q3_CUDA(cudaGetLastError());
 }
 

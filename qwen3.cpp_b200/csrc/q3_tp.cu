@@ -85,6 +85,8 @@ __global__ void __launch_bounds__(256) tp_allreduce_kernel(TpPeers P, const floa
                                                            int rank, int world, unsigned* counter,
                                                            unsigned* err, long long budget) {
     __shared__ unsigned s_seq;
+    pdl_wait();
+    pdl_trigger();
     const int tid = threadIdx.x;
     if (tid == 0) s_seq = *counter + 1;
     __syncthreads();
@@ -130,6 +132,8 @@ __global__ void __launch_bounds__(1024) tp_argmax_kernel(
     TpPeers P, const float* logits, int vn, int v0, int rank, int world, unsigned* counter,
     unsigned* err, long long budget, int32_t* tok, int32_t* pos, int32_t* log, int32_t* state,
     const int32_t* forced) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float bv[32];
     __shared__ int bi[32];
     __shared__ unsigned s_seq;
@@ -341,7 +345,8 @@ void TpDecoder::enqueue_step(bool forced) {
     float* proj_out = solo ? X : part;
     auto allreduce = [&]() {
         if (solo) return;
-        tp_allreduce_kernel<<<1, 256, 0, s_>>>(P, part, X, rank_, world_, counter, err, kBudget);
+        launch_dep(false, tp_allreduce_kernel, dim3(1), dim3(256), 0, s_, P, static_cast<const float*>(part), X,
+                   rank_, world_, counter, err, kBudget);
         Q3_CUDA(cudaGetLastError());
     };
     // x = embedding row of the step's token (the bf16 normalised copy is not used).
@@ -408,11 +413,11 @@ void TpDecoder::enqueue_step(bool forced) {
     launch_gemv(kEpiStore, m_.output() + static_cast<size_t>(v0_) * c.dim, nullptr, X,
                 m_.final_norm(), c.norm_eps, static_cast<float*>(logits_.ptr), nullptr, vn_, c.dim,
                 nullptr, 0, s_);
-    tp_argmax_kernel<<<1, 1024, 0, s_>>>(
-        P, static_cast<const float*>(logits_.ptr), vn_, v0_, rank_, world_, counter, err, kBudget,
-        static_cast<int32_t*>(tok_.ptr), static_cast<int32_t*>(pos_.ptr),
-        static_cast<int32_t*>(log_.ptr), static_cast<int32_t*>(step_.ptr),
-        forced ? static_cast<const int32_t*>(forced_.ptr) : nullptr);
+    launch_dep(false, tp_argmax_kernel, dim3(1), dim3(1024), 0, s_, P,
+               static_cast<const float*>(logits_.ptr), vn_, v0_, rank_, world_, counter, err,
+               kBudget, static_cast<int32_t*>(tok_.ptr), static_cast<int32_t*>(pos_.ptr),
+               static_cast<int32_t*>(log_.ptr), static_cast<int32_t*>(step_.ptr),
+               forced ? static_cast<const int32_t*>(forced_.ptr) : nullptr);
     Q3_CUDA(cudaGetLastError());
 }
 
