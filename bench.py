@@ -56,12 +56,13 @@ DP_STEPS = 128
 DP_WARMUP = 2
 
 
-def dp_workload():
+def dp_workload(n=DP_SEQS):
+    """The first n (of 64) sequences of the seeded batched-decode workload."""
     import numpy as np
     rng = np.random.default_rng(3)
     lens = rng.integers(128, 4097, DP_SEQS)
     prompts = [rng.integers(0, VOCAB, int(n)).astype(np.int32) for n in lens]
-    return lens, prompts
+    return lens[:n], prompts[:n]
 
 
 # Tensor-parallel single-stream decode: context 32768, a 32000-token prompt of seeded random IDs
@@ -323,8 +324,8 @@ def run_b200_arm(args):
     dp_ms = dp_gbs = dp_bytes_step = 0.0
     mine = []
     if "dp" in legs:
-        lens, prompts = dp_workload()
-        mine = list(range(rank, DP_SEQS, world))
+        lens, prompts = dp_workload(args.dp_seqs)
+        mine = list(range(rank, args.dp_seqs, world))
         batch = q3b200.Batch(pm, len(mine), int(max(lens[i] for i in mine)) + DP_WARMUP + DP_STEPS)
         for i in mine:
             batch.add(prompts[i])
@@ -452,7 +453,8 @@ def run_b200_arm(args):
             "dp_decode": {
                 "metric": "batched greedy decode tok/s (64 sequences, ctx U[128,4096], "
                           "Qwen3-0.6B bf16)",
-                "value": round(DP_SEQS * DP_STEPS / max(dp_ms / 1e3, 1e-12), 1), "unit": "tok/s",
+                "value": round(args.dp_seqs * DP_STEPS / max(dp_ms / 1e3, 1e-12), 1), "unit": "tok/s",
+                "sequences": args.dp_seqs,
                 "steps": DP_STEPS, "ms_per_step": round(dp_ms / DP_STEPS, 4),
                 "seqs_per_gpu": len(mine), "scaling": "strong",
                 "roofline": {"bound": "hbm", "achieved": round(dp_gbs, 1),
@@ -508,6 +510,9 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--path", choices=["auto", "fused", "layerwise"], default="auto",
                     help="decode path of the b200 arm (auto: fused when the shape allows)")
+    ap.add_argument("--dp-seqs", type=int, default=DP_SEQS,
+                    help="sequences of the batched-decode leg (the first n of the 64; a smaller "
+                         "case for a profiler run)")
     ap.add_argument("--legs", default="decode,prefill,dp,tp",
                     help="comma-separated legs of the b200 arm to run (decode: the headline "
                          "B=1 decode; prefill; dp: batched decode; tp: tensor-parallel decode); "
