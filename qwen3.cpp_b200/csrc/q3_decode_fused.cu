@@ -80,7 +80,8 @@ enum Mode : int { kTag = 0, kPair = 2, kLogits = 3 };
 
 struct __align__(128) Smem {
     uint8_t ring[NS][SLOT];
-    float xf[D];              // staged fp32 activation of a GEMV
+    float4 xa[D / 8];         // staged fp32 activation of a GEMV: elements 8u..8u+3 in xa[u],
+    float4 xb[D / 8];         // 8u+4..8u+7 in xb[u] (a warp's 32 consecutive units, no conflicts)
     float4 xs4[H / 4];        // attention staging and merge buffers
     float qk[4][HD];          // q head 2g, q head 2g+1, k and v at kv_pos (bf16-rounded)
     float hbuf[64];           // h of this CTA's MLP indices
@@ -568,9 +569,12 @@ __device__ __forceinline__ float consumer_sum(float v, Smem& sm) {
     return t;
 }
 
-// The staged activation x of a GEMV is kept in fp32 (sm.xf) and multiplied against the bf16
-// weights on the CUDA cores with fp32 accumulation, as the reference's MatMul does.
-__device__ __forceinline__ void xs_put(Smem& sm, int e, float val) { sm.xf[e] = val; }
+// The staged activation x of a GEMV is kept in fp32 (sm.xa / sm.xb) and multiplied against the
+// bf16 weights on the CUDA cores with fp32 accumulation, as the reference's MatMul does.
+__device__ __forceinline__ void xs_put(Smem& sm, int e, float val) {
+    float* half = reinterpret_cast<float*>((e & 4) ? sm.xb : sm.xa);
+    half[(e >> 3) * 4 + (e & 3)] = val;
+}
 
 // Stage xs = RmsNorm(x) (src/inference.cpp:887-923) for a K=1024 GEMV; thread t holds x[4t..4t+3]
 // and its norm weights wv.
@@ -578,7 +582,7 @@ __device__ __forceinline__ void stage_norm(Smem& sm, float4 xv, uint2 wv, float 
     const int t = threadIdx.x;
     const float ss = consumer_sum(xv.x * xv.x + xv.y * xv.y + xv.z * xv.z + xv.w * xv.w, sm);
     const float inv = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
-    reinterpret_cast<float4*>(sm.xf)[t] =
+    ((t & 1) ? sm.xb : sm.xa)[t >> 1] =
         make_float4((xv.x * inv) * bf16_lo(wv.x), (xv.y * inv) * bf16_hi(wv.x),
                     (xv.z * inv) * bf16_lo(wv.y), (xv.w * inv) * bf16_hi(wv.y));
     bar_consumers();
@@ -598,8 +602,8 @@ __device__ __forceinline__ void fma_rows8(const Smem& sm, const FusedArgs& a, co
     float xr[U][8];
 #pragma unroll
     for (int j = 0; j < U; ++j) {
-        const float4 p = reinterpret_cast<const float4*>(sm.xf)[2 * (lane + 32 * j)];
-        const float4 q = reinterpret_cast<const float4*>(sm.xf)[2 * (lane + 32 * j) + 1];
+        const float4 p = sm.xa[lane + 32 * j];
+        const float4 q = sm.xb[lane + 32 * j];
         xr[j][0] = p.x; xr[j][1] = p.y; xr[j][2] = p.z; xr[j][3] = p.w;
         xr[j][4] = q.x; xr[j][5] = q.y; xr[j][6] = q.z; xr[j][7] = q.w;
     }
