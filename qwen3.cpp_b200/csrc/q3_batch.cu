@@ -279,6 +279,7 @@ void Batch::enqueue_step(bool forced, int n_forced) {
         g.bn = 128;
         g.max_ksplit = 16;
         g.min_slice_kblocks = 2;
+        g.dependent = true;
         Q3_CUDA(launch_gemm(a, b, nullptr, out, g, epi, sms, s_, &a_lo));
     };
     uint16_t* Xn_lo = static_cast<uint16_t*>(xn_lo_.ptr);
