@@ -39,9 +39,10 @@ WEIGHT_BYTES = 1_191_968_768          # 28 layers + tied lm_head, bf16
 KV_BYTES_PER_POS = 2 * 28 * 1024 * 2  # K and V rows of every layer
 LM_HEAD_BYTES = VOCAB * 1024 * 2
 # DRAM traffic of one fused decode step (dram__bytes_read.sum + dram__bytes_write.sum), from an
-# `ncu --set full` capture of the timed one-step launch of `bench.py --steps 1 --warmup 3`
-# (kv_len 17): 1.1959 GB read + 5.22 MB written. Re-captured whenever the kernel changes.
-FUSED_TRAFFIC_PER_STEP = 1_201_132_000
+# `ncu --set full` capture of the timed one-step launch of
+# `bench.py --legs decode --steps 1 --warmup 3` (kv_len 17): 1.196968 GB read + 5.722624 MB
+# written. Re-captured whenever the kernel changes.
+FUSED_TRAFFIC_PER_STEP = 1_202_690_624
 # Long-prompt prefill: 2048 seeded prompt IDs (seed 2) at context 4096, batched on the tensor cores.
 PREFILL_LEN = 2048
 PREFILL_CTX = 4096
