@@ -152,218 +152,6 @@ __global__ void __launch_bounds__(256) prefill_qkv_kernel(PrefillQkvArgs a) {
     reinterpret_cast<uint2*>(dst)[lane] = make_uint2(pack2_bf16(v.x, v.y), pack2_bf16(v.z, v.w));
 }
 
-// ------------------------------------------------------------------ causal flash attention
-
-constexpr int PA_THREADS = 256;          // 8 warps: 2 query heads x 4 groups of 16 rows
-constexpr int PA_BQ = 64;                // query tokens per CTA
-constexpr int PA_BKV = 64;               // KV positions per tile (4 pages)
-constexpr int PA_TILE = PA_BKV * HD * 2; // bytes of one K (or V) tile
-constexpr int PA_SMEM = 2 * 2 * PA_TILE; // double-buffered K and V
-
-__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
-                                               uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-        "{%8,%9}, {%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(addr));
-}
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() {
-    asm volatile("cp.async.commit_group;" ::: "memory");
-}
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-// Byte offset of 16-byte chunk `ch` of tile row `row` (256-byte rows, XOR swizzle on the low 3
-// bits of the chunk so that 8 consecutive rows at one chunk hit 8 different bank groups).
-__device__ __forceinline__ uint32_t tile_off(int row, int ch) {
-    return static_cast<uint32_t>(row * 256 + ((ch ^ (row & 7)) << 4));
-}
-
-__global__ void __launch_bounds__(PA_THREADS, 1) prefill_attn_kernel(PrefillAttnArgs a) {
-    extern __shared__ __align__(128) uint8_t sm[];
-    const int qb = gridDim.x - 1 - blockIdx.x;  // longest query blocks first
-    const int g = blockIdx.y;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int h = g * 2 + (warp >> 2);
-    const int qd = a.n_heads * HD;
-    const int r0 = qb * PA_BQ + (warp & 3) * 16;
-    const int last_row = min(a.rows, (qb + 1) * PA_BQ) - 1;
-    const int kv_end = a.pos0 + last_row + 1;
-    const int ntiles = (kv_end + PA_BKV - 1) / PA_BKV;
-    const int valid_pages = (kv_end + kPageTokens - 1) / kPageTokens;
-    const int cq = (lane & 3) * 2;
-    const int ra = r0 + (lane >> 2), rb = ra + 8;
-    const int qpos_a = a.pos0 + min(ra, a.rows - 1);
-    const int qpos_b = a.pos0 + min(rb, a.rows - 1);
-    const int warp_qmax = a.pos0 + min(r0 + 15, a.rows - 1);
-
-    // Q fragments (m16 x k16 row-major A operand) of this warp's 16 rows, 8 k-steps of 16 dims.
-    uint32_t qf[8][4];
-    {
-        const uint16_t* qa = a.q + static_cast<size_t>(min(ra, a.rows - 1)) * qd + h * HD + cq;
-        const uint16_t* qbp = a.q + static_cast<size_t>(min(rb, a.rows - 1)) * qd + h * HD + cq;
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-            qf[kk][0] = *reinterpret_cast<const uint32_t*>(qa + kk * 16);
-            qf[kk][1] = *reinterpret_cast<const uint32_t*>(qbp + kk * 16);
-            qf[kk][2] = *reinterpret_cast<const uint32_t*>(qa + kk * 16 + 8);
-            qf[kk][3] = *reinterpret_cast<const uint32_t*>(qbp + kk * 16 + 8);
-        }
-    }
-
-    auto load_tile = [&](int j, int st) {
-        uint8_t* ks = sm + st * 2 * PA_TILE;
-        uint8_t* vs = ks + PA_TILE;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int c = tid + PA_THREADS * i;  // 1024 chunks of 16 B per tile
-            const int row = c >> 4, ch = c & 15;
-            const int t = j * PA_BKV + row;
-            const int page = t / kPageTokens;
-            const uint32_t off = tile_off(row, ch);
-            if (page < valid_pages) {
-                const size_t e =
-                    ((static_cast<size_t>(a.page_table[page]) * a.n_kv + g) * kPageTokens +
-                     t % kPageTokens) * HD + ch * 8;
-                cp_async16(smem_addr(ks + off), a.k_cache + e);
-                cp_async16(smem_addr(vs + off), a.v_cache + e);
-            } else {
-                *reinterpret_cast<uint4*>(ks + off) = make_uint4(0, 0, 0, 0);
-                *reinterpret_cast<uint4*>(vs + off) = make_uint4(0, 0, 0, 0);
-            }
-        }
-        cp_async_commit();
-    };
-
-    float o[16][4];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
-    float m_a = -FLT_MAX, m_b = -FLT_MAX, l_a = 0.0f, l_b = 0.0f;
-    // Scores in the log2 domain: s * log2(e) / sqrt(head_dim), then exp2.
-    const float scale = 1.4426950408889634f / sqrtf(static_cast<float>(HD));
-
-    load_tile(0, 0);
-    for (int j = 0; j < ntiles; ++j) {
-        if (j + 1 < ntiles) {
-            load_tile(j + 1, (j + 1) & 1);
-        } else {
-            cp_async_commit();
-        }
-        cp_async_wait<1>();
-        __syncthreads();
-        const uint8_t* ks = sm + (j & 1) * 2 * PA_TILE;
-        const uint8_t* vs = ks + PA_TILE;
-        if (j * PA_BKV <= warp_qmax) {
-            float s[8][4];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.0f;
-            const int mat = lane >> 3;
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
-#pragma unroll
-                for (int np = 0; np < 4; ++np) {
-                    uint32_t b[4];
-                    const int row = np * 16 + (lane & 7) + (mat >> 1) * 8;
-                    ldsm_x4(b, smem_addr(ks + tile_off(row, kk * 2 + (mat & 1))));
-                    mma_bf16_16816(s[2 * np], qf[kk], b[0], b[1]);
-                    mma_bf16_16816(s[2 * np + 1], qf[kk], b[2], b[3]);
-                }
-            }
-            float mx_a = -FLT_MAX, mx_b = -FLT_MAX;
-#pragma unroll
-            for (int nb = 0; nb < 8; ++nb) {
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    const int t = j * PA_BKV + nb * 8 + cq + e;
-                    s[nb][e] = t <= qpos_a ? s[nb][e] * scale : -INFINITY;
-                    s[nb][2 + e] = t <= qpos_b ? s[nb][2 + e] * scale : -INFINITY;
-                    mx_a = fmaxf(mx_a, s[nb][e]);
-                    mx_b = fmaxf(mx_b, s[nb][2 + e]);
-                }
-            }
-            mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
-            mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
-            mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
-            mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
-            const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
-            const float corr_a = exp2f(m_a - mn_a), corr_b = exp2f(m_b - mn_b);
-            m_a = mn_a;
-            m_b = mn_b;
-            float sum_a = 0.0f, sum_b = 0.0f;
-#pragma unroll
-            for (int nb = 0; nb < 8; ++nb) {
-                s[nb][0] = exp2f(s[nb][0] - mn_a);
-                s[nb][1] = exp2f(s[nb][1] - mn_a);
-                s[nb][2] = exp2f(s[nb][2] - mn_b);
-                s[nb][3] = exp2f(s[nb][3] - mn_b);
-                sum_a += s[nb][0] + s[nb][1];
-                sum_b += s[nb][2] + s[nb][3];
-            }
-            l_a = l_a * corr_a + sum_a;
-            l_b = l_b * corr_b + sum_b;
-#pragma unroll
-            for (int nb = 0; nb < 16; ++nb) {
-                o[nb][0] *= corr_a;
-                o[nb][1] *= corr_a;
-                o[nb][2] *= corr_b;
-                o[nb][3] *= corr_b;
-            }
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-                const uint32_t pa[4] = {pack2_bf16(s[2 * kk][0], s[2 * kk][1]),
-                                        pack2_bf16(s[2 * kk][2], s[2 * kk][3]),
-                                        pack2_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]),
-                                        pack2_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3])};
-#pragma unroll
-                for (int np = 0; np < 8; ++np) {
-                    uint32_t b[4];
-                    const int row = kk * 16 + (lane & 7) + (mat & 1) * 8;
-                    ldsm_x4_t(b, smem_addr(vs + tile_off(row, np * 2 + (mat >> 1))));
-                    mma_bf16_16816(o[2 * np], pa, b[0], b[1]);
-                    mma_bf16_16816(o[2 * np + 1], pa, b[2], b[3]);
-                }
-            }
-        }
-        __syncthreads();
-    }
-    cp_async_wait<0>();
-
-    l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
-    l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
-    l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
-    l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
-    const float inv_a = 1.0f / l_a, inv_b = 1.0f / l_b;
-    if (ra < a.rows) {
-        uint16_t* out = a.out + static_cast<size_t>(ra) * qd + h * HD + cq;
-#pragma unroll
-        for (int nb = 0; nb < 16; ++nb) {
-            *reinterpret_cast<uint32_t*>(out + nb * 8) = pack2_bf16(o[nb][0] * inv_a, o[nb][1] * inv_a);
-        }
-    }
-    if (rb < a.rows) {
-        uint16_t* out = a.out + static_cast<size_t>(rb) * qd + h * HD + cq;
-#pragma unroll
-        for (int nb = 0; nb < 16; ++nb) {
-            *reinterpret_cast<uint32_t*>(out + nb * 8) = pack2_bf16(o[nb][2] * inv_b, o[nb][3] * inv_b);
-        }
-    }
-}
-
 int device_sms(int device) {
     int n = 0;
     Q3_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device));
@@ -386,21 +174,6 @@ void launch_prefill_qkv(const PrefillQkvArgs& a, cudaStream_t s) {
     if (a.rows <= 0) return;
     const dim3 grid(a.rows, (a.n_heads + 2 * a.n_kv + 7) / 8);
     launch_dep(false, prefill_qkv_kernel, grid, dim3(256), 0, s, a);
-    Q3_CUDA(cudaGetLastError());
-}
-
-void launch_prefill_attention(const PrefillAttnArgs& a, cudaStream_t s) {
-    if (a.rows <= 0) return;
-    static bool configured[64] = {};
-    int dev = 0;
-    Q3_CUDA(cudaGetDevice(&dev));
-    if (!configured[dev & 63]) {
-        Q3_CUDA(cudaFuncSetAttribute(prefill_attn_kernel,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, PA_SMEM));
-        configured[dev & 63] = true;
-    }
-    const dim3 grid((a.rows + PA_BQ - 1) / PA_BQ, a.n_kv);
-    prefill_attn_kernel<<<grid, PA_THREADS, PA_SMEM, s>>>(a);
     Q3_CUDA(cudaGetLastError());
 }
 
@@ -558,31 +331,17 @@ void Prefill::run(const int32_t* ids_dev, int n, int pos0, const uint16_t* embed
             g.qkv.eps = c.norm_eps;
             Q3_CUDA(launch_gemm(m_xn, wm.wqkv, nullptr, m_xn, g, kEpiQkvRope, num_sms_, s));
             g.qkv = QkvEpilogue{};
-            if (use_tc_attention_) {
-                PrefillAttnTcArgs ta{};
-                ta.page_table = kv.page_table;
-                ta.out = static_cast<uint16_t*>(o_.ptr);
-                ta.err = err;
-                ta.rows = S;
-                ta.pos0 = p0;
-                ta.n_kv = c.n_kv_heads;
-                ta.n_pages = kv.n_pages;
-                ta.pages_per_seq = table_len;
-                ta.layer = l;
-                launch_prefill_attention_tc(m_q, kmap_, vmap_, kmap4_, vmap4_, ta, s);
-            } else {
-                PrefillAttnArgs aa{};
-                aa.q = static_cast<const uint16_t*>(q_.ptr);
-                aa.k_cache = kv.k_base + layer_elems(kv) * l;
-                aa.v_cache = kv.v_base + layer_elems(kv) * l;
-                aa.page_table = kv.page_table;
-                aa.out = static_cast<uint16_t*>(o_.ptr);
-                aa.rows = S;
-                aa.pos0 = p0;
-                aa.n_heads = c.n_heads;
-                aa.n_kv = c.n_kv_heads;
-                launch_prefill_attention(aa, s);
-            }
+            PrefillAttnTcArgs ta{};
+            ta.page_table = kv.page_table;
+            ta.out = static_cast<uint16_t*>(o_.ptr);
+            ta.err = err;
+            ta.rows = S;
+            ta.pos0 = p0;
+            ta.n_kv = c.n_kv_heads;
+            ta.n_pages = kv.n_pages;
+            ta.pages_per_seq = table_len;
+            ta.layer = l;
+            launch_prefill_attention_tc(m_q, kmap_, vmap_, kmap4_, vmap4_, ta, s);
             // x += wo . attn (:846-849).
             g.N = c.dim;
             g.K = qd;

@@ -50,18 +50,8 @@ void launch_prefill_qkv(const PrefillQkvArgs& a, cudaStream_t s);
 
 // Causal attention of `rows` query tokens (positions pos0..) over KV positions [0, pos] of the
 // paged cache (FastAttn + Softmax, src/inference.cpp:1017-1058, :925-946, for every prompt token
-// at once); head_dim 128, two query heads per KV head. out bf16 [rows, n_heads*128].
-struct PrefillAttnArgs {
-    const uint16_t* q;
-    const uint16_t* k_cache;
-    const uint16_t* v_cache;
-    const int32_t* page_table;
-    uint16_t* out;
-    int rows, pos0, n_heads, n_kv;
-};
-void launch_prefill_attention(const PrefillAttnArgs& a, cudaStream_t s);
-
-// The same attention on tcgen05 tensor cores (q3_prefill_attn.cu). q maps the bf16 q rows
+// at once) on the tcgen05 tensor cores (q3_prefill_attn.cu); head_dim 128, two query heads per KV
+// head, out bf16 [rows, n_heads*128]. q maps the bf16 q rows
 // [rows, n_heads*128] with 64 x 64 boxes; k and v map each whole paged cache (every layer) as
 // [n_layers * n_pages * n_kv * 16, 128] with 64 x 16 boxes, k4 and v4 as 4-D page maps
 // (make_tmap_kv_pages over n_layers * n_pages pages).
@@ -114,7 +104,6 @@ public:
     // Non-zero when a contraction's bounded wait gave up in the last run.
     unsigned read_error(cudaStream_t s);
     // Attention kernel: tcgen05 (default) or the mma.sync flash-attention kernel.
-    void set_tc_attention(bool on) { use_tc_attention_ = on; }
 
     // TMA maps of the paged caches (2-D rows and 4-D page boxes) for a view; cached.
     void ensure_kv_maps(const KvView& kv, int n_layers);
@@ -134,7 +123,6 @@ private:
     int device_ = 0;
     int num_sms_ = 148;
     int cap_rows_ = 0;
-    bool use_tc_attention_ = true;
     DeviceBuffer x_, xn_, q_, o_, h_, err_;
     struct LayerMaps {
         CUtensorMap wqkv, wo, w1, w3, w2;
