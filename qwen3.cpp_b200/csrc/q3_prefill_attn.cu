@@ -263,9 +263,25 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             issued |= 1u;
             uint32_t vissued = 0, vissued_parity = 0;
+            // Page rows of a tile's 8 pages (the last tile's pages past the table repeat its last
+            // valid page; such a tile takes the per-page path).
+            constexpr int PPT = KEYS / kPageTokens;
+            auto load_rows = [&](int j, int (&r)[PPT]) {
+                const int lp0 = j * PPT;
+                const bool all_in = lp0 + PPT <= table_len;
+#pragma unroll
+                for (int pg = 0; pg < PPT; ++pg) {
+                    r[pg] = __ldg(table + (all_in ? lp0 + pg : min(lp0 + pg, valid_pages - 1)));
+                }
+            };
+            // The page rows of tile step + 1 are loaded while the waits of step run (they were a
+            // dependent global round trip in front of every copy).
+            int rows_k[PPT] = {}, rows_v[PPT] = {}, rows_n[PPT] = {};
+            if (ntiles > 0) load_rows(0, rows_k);
             // Loads run K one tile ahead of V: K_{j+1} waits only for S_{j-1}, V_j for PV_{j-2},
             // so the score MMAs never wait behind the slower P.V chain.
             for (int step = 0; step <= ntiles && !*abort; ++step) {
+                if (step + 1 < ntiles) load_rows(step + 1, rows_n);
                 for (int kind = 0; kind < 2 && !*abort; ++kind) {
                     const int j = kind ? step - 1 : step;   // kind 0: K_step, kind 1: V_{step-1}
                     if (j < 0 || j >= ntiles) continue;
@@ -274,14 +290,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     uint8_t* dst = sm + KV_OFF + st * KV_STAGE + kind * 2 * PANEL;
                     uint64_t* emp = kind ? &v_empty[st] : &kv_empty[st];
                     uint64_t* ful = kind ? &v_full[st] : &kv_full[st];
-                    int rows8[KEYS / kPageTokens];
-                    const int lp0 = j * (KEYS / kPageTokens);
-                    const bool all_in = lp0 + KEYS / kPageTokens <= table_len;
+                    int rows8[PPT];
 #pragma unroll
-                    for (int pg = 0; pg < KEYS / kPageTokens; ++pg) {
-                        const int page = all_in ? lp0 + pg : min(lp0 + pg, valid_pages - 1);
-                        rows8[pg] = __ldg(table + page);
-                    }
+                    for (int pg = 0; pg < PPT; ++pg) rows8[pg] = kind ? rows_v[pg] : rows_k[pg];
+                    const bool all_in = j * PPT + PPT <= table_len;
                     bool contiguous = all_in;
 #pragma unroll
                     for (int pg = 1; pg < KEYS / kPageTokens; ++pg) {
@@ -317,6 +329,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         issued |= 2u << st;
                         issued_parity = (issued_parity & ~(2u << st)) | (ph << (st + 1));
                     }
+                }
+#pragma unroll
+                for (int pg = 0; pg < PPT; ++pg) {
+                    rows_v[pg] = rows_k[pg];
+                    rows_k[pg] = rows_n[pg];
                 }
             }
             for (int st = 0; st < 2; ++st) {
