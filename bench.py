@@ -285,7 +285,7 @@ def run_b200_arm(args):
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         for i in range(e2e_steps):
-            lg = model.forward_token(tok, PROMPT_LEN + i)
+            lg = model.forward_token_ref(tok, PROMPT_LEN + i)
             tok = int(np.argmax(lg))
         e2e_s = time.perf_counter() - t0
         e2e_tps = world * e2e_steps / e2e_s
@@ -448,7 +448,8 @@ def run_b200_arm(args):
                 "frac": round(step_bytes * per_gpu_tps / 1e9 / pk["hbm_gbs"], 4)},
             "e2e": {"value": round(e2e_tps, 2), "unit": UNIT, "h2d_bytes_per_step": 32,
                     "d2h_bytes_per_step": VOCAB * 4,
-                    "api": "q3_forward_token per step + host argmax"},
+                    "api": "q3_forward_token_ref per step (logits in the model's pinned "
+                           "buffer, the reference's const-reference return) + host argmax"},
             "cpu_baseline": cpu,
             "clocks": clk,
             "dp_decode": {

@@ -103,6 +103,11 @@ q3_status q3_reset(q3_model* model);
  * (attention-sink ring buffer once pos >= context), logits[vocab_size] to logits_host. */
 q3_status q3_forward_token(q3_model* model, int32_t token, int pos, float* logits_host);
 
+/* Qwen3::ForwardToken with the reference's return convention (`const std::vector<float>&`,
+ * include/inference.h:227-229, src/inference.cpp:592-637): *logits points at vocab_size floats in
+ * a model-owned pinned host buffer, valid until the next call on this model. */
+q3_status q3_forward_token_ref(q3_model* model, int32_t token, int pos, const float** logits);
+
 /* ForwardToken with debug taps: hidden_host[(n_layers+1)*dim] receives the embedding row and
  * the hidden state after each layer (the per-layer view of src/inference.cpp:615-617). Either
  * output may be NULL. */

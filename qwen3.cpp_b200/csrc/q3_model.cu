@@ -924,8 +924,14 @@ void Model::forward_token(int32_t token, int pos, float* hidden_host, float* log
     e.write_step(start_params(token, pos, 0));
     clear_fused_error();
     run_steps(1, false, hidden_host != nullptr, nullptr);
-    check_fused_error();
     cudaStream_t s = e.stream();
+    // The error word comes back with the outputs: one synchronisation per call.
+    pinned_err_.ensure(sizeof(unsigned));
+    *static_cast<unsigned*>(pinned_err_.ptr) = 0u;
+    if (fused_enabled()) {
+        Q3_CUDA(cudaMemcpyAsync(pinned_err_.ptr, static_cast<unsigned*>(fused_sync_.ptr) + 32,
+                                sizeof(unsigned), cudaMemcpyDeviceToHost, s));
+    }
     if (hidden_host) {
         Q3_CUDA(cudaMemcpyAsync(hidden_host, e.taps(),
                                 static_cast<size_t>(cfg_.n_layers + 1) * cfg_.dim * 4,
@@ -936,6 +942,13 @@ void Model::forward_token(int32_t token, int pos, float* hidden_host, float* log
                                 cudaMemcpyDeviceToHost, s));
     }
     Q3_CUDA(cudaStreamSynchronize(s));
+    if (*static_cast<const unsigned*>(pinned_err_.ptr) != 0u) check_fused_error();  // throws
+}
+
+const float* Model::forward_token_ref(int32_t token, int pos) {
+    pinned_logits_.ensure(static_cast<size_t>(cfg_.vocab_size) * 4);
+    forward_token(token, pos, nullptr, static_cast<float*>(pinned_logits_.ptr));
+    return static_cast<const float*>(pinned_logits_.ptr);
 }
 
 void Model::decode_loop(const int32_t* forced_host, int n, int32_t first_token, int pos0,
@@ -1322,6 +1335,13 @@ q3_status q3_forward_token(q3_model* model, int32_t token, int pos, float* logit
     return guard([&] {
         if (!model) throw std::invalid_argument("null argument");
         model->m->forward_token(token, pos, nullptr, logits_host);
+    });
+}
+
+q3_status q3_forward_token_ref(q3_model* model, int32_t token, int pos, const float** logits) {
+    return guard([&] {
+        if (!model || !logits) throw std::invalid_argument("null argument");
+        *logits = model->m->forward_token_ref(token, pos);
     });
 }
 

@@ -163,6 +163,9 @@ public:
 
     void reset();
     void forward_token(int32_t token, int pos, float* hidden_host, float* logits_host);
+    // ForwardToken returning the logits in a model-owned pinned host buffer, valid until the
+    // next call (the reference returns a reference to its logits vector).
+    const float* forward_token_ref(int32_t token, int pos);
     void decode_loop(const int32_t* forced_host, int n, int32_t first_token, int pos0,
                      int32_t* out_tokens_host, float* last_logits_host, float* all_logits_host);
     // Prompt prefill. Batched (tensor-core contractions over all tokens) when the shape allows
@@ -217,6 +220,7 @@ private:
     DeviceBuffer logits_, argmax_part_, argmax_out_, token_log_, forced_;
     int log_cap_ = 0;
     PinnedBuffer pinned_io_;
+    PinnedBuffer pinned_logits_, pinned_err_;
     // Fused decode state.
     int fused_grid_ = 0;
     int fused_s_max_ = 0;

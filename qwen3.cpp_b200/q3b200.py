@@ -96,6 +96,7 @@ def lib() -> C.CDLL:
         "q3_model_tensor_count": [vp, C.POINTER(C.c_int)],
         "q3_reset": [vp],
         "q3_forward_token": [vp, i32, C.c_int, vp],
+        "q3_forward_token_ref": [vp, i32, C.c_int, C.POINTER(C.POINTER(C.c_float))],
         "q3_forward_token_layers": [vp, i32, C.c_int, vp, vp],
         "q3_kv_row": [vp, C.c_int, C.c_int, U16P, U16P],
         "q3_prefill": [vp, I32P, C.c_int, C.c_int, vp, vp],
@@ -241,6 +242,15 @@ class Qwen3:
         out = np.empty(self.config["vocab_size"], np.float32)
         check(lib().q3_forward_token(self._h, int(token), int(pos), out.ctypes.data))
         return out
+
+    def forward_token_ref(self, token: int, pos: int) -> np.ndarray:
+        """ForwardToken returning a read-only view of the model's pinned logits buffer, valid
+        until the next call (the reference returns a reference to its logits vector)."""
+        ptr = C.POINTER(C.c_float)()
+        check(lib().q3_forward_token_ref(self._h, int(token), int(pos), C.byref(ptr)))
+        view = np.ctypeslib.as_array(ptr, shape=(self.config["vocab_size"],))
+        view.flags.writeable = False
+        return view
 
     def forward_token_layers(self, token: int, pos: int):
         c = self.config

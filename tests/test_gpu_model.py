@@ -137,6 +137,26 @@ def test_generate_semantics(models, oracle_run):
     assert st["prefill_seconds"] > 0 and st["decode_seconds"] > 0
 
 
+def test_forward_token_ref_matches_copy(models, oracle_run):
+    """The zero-copy ForwardToken returns the same logits as the copying one, in a read-only
+    view of the model's buffer that the next call overwrites (the reference's const reference)."""
+    gpu, _ = models
+    seq, _, _ = oracle_run
+    gpu.reset()
+    for pos in range(4):
+        gpu.forward_token(int(seq[pos]), pos)
+    a = gpu.forward_token(int(seq[4]), 4)
+    gpu.reset()
+    for pos in range(4):
+        gpu.forward_token(int(seq[pos]), pos)
+    view = gpu.forward_token_ref(int(seq[4]), 4)
+    assert not view.flags.writeable
+    np.testing.assert_allclose(view, a, rtol=0, atol=LOGITS_MAX_ABS)
+    first = view.copy()
+    gpu.forward_token_ref(int(seq[5]), 5)
+    assert not np.array_equal(view, first)  # the buffer now holds the next position's logits
+
+
 def test_range_errors(models, q3lib):
     gpu, _ = models
     with pytest.raises(q3lib.OutOfRange):
