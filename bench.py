@@ -117,6 +117,14 @@ class Clocks:
                  "-i", str(gpu_index), "-lms", "20"], stdout=self.f, stderr=subprocess.DEVNULL)
         except (FileNotFoundError, OSError):
             self.p = None
+        # nvidia-smi takes a moment to start: wait (up to 3 s) for its first sample, so that the
+        # timed region that follows is sampled.
+        t0 = time.perf_counter()
+        while self.p is not None and time.perf_counter() - t0 < 3.0:
+            self.f.flush()
+            if Path(self.f.name).stat().st_size > 0:
+                break
+            time.sleep(0.01)
 
     def stop(self):
         if self.p is None:
