@@ -656,6 +656,54 @@ __device__ __forceinline__ void fma_rows8(const Smem& sm, const FusedArgs& a, co
     y1 = __shfl_sync(0xffffffffu, v, 8 * t + 4);
 }
 
+// As fma_rows8 for 4 rows; returns the row sums with row q in lanes 8q..8q+7.
+template <int K>
+__device__ __forceinline__ float fma_rows4(const Smem& sm, const uint8_t* rows, int row0) {
+    constexpr int U = K / 256;
+    const int lane = threadIdx.x & 31;
+    float xr[U][8];
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+        const float4 p = sm.xa[lane + 32 * j];
+        const float4 q = sm.xb[lane + 32 * j];
+        xr[j][0] = p.x; xr[j][1] = p.y; xr[j][2] = p.z; xr[j][3] = p.w;
+        xr[j][4] = q.x; xr[j][5] = q.y; xr[j][6] = q.z; xr[j][7] = q.w;
+    }
+    float s[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        const uint8_t* rp = rows + r * K * 2;
+        const int sw = ((row0 + r) & 1) << 2;
+        float acc0 = 0.0f, acc1 = 0.0f;
+#pragma unroll
+        for (int j = 0; j < U; ++j) {
+            const uint4 w = *reinterpret_cast<const uint4*>(rp + (((lane + 32 * j) ^ sw) << 4));
+            acc0 = fmaf(bf16_lo(w.x), xr[j][0], acc0);
+            acc1 = fmaf(bf16_hi(w.x), xr[j][1], acc1);
+            acc0 = fmaf(bf16_lo(w.y), xr[j][2], acc0);
+            acc1 = fmaf(bf16_hi(w.y), xr[j][3], acc1);
+            acc0 = fmaf(bf16_lo(w.z), xr[j][4], acc0);
+            acc1 = fmaf(bf16_hi(w.z), xr[j][5], acc1);
+            acc0 = fmaf(bf16_lo(w.w), xr[j][6], acc0);
+            acc1 = fmaf(bf16_hi(w.w), xr[j][7], acc1);
+        }
+        s[r] = acc0 + acc1;
+    }
+    const bool b4 = lane & 16, b3 = lane & 8;
+    float t2[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const float send = b4 ? s[i] : s[i + 2];
+        const float keep = b4 ? s[i + 2] : s[i];
+        t2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+    float v = (b3 ? t2[1] : t2[0]) + __shfl_xor_sync(0xffffffffu, b3 ? t2[0] : t2[1], 8);
+    v += __shfl_xor_sync(0xffffffffu, v, 4);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    return v;
+}
+
 __device__ __forceinline__ uint2 load_norm(const uint16_t* nw) {
     return __ldg(reinterpret_cast<const uint2*>(nw) + threadIdx.x);
 }
@@ -767,6 +815,26 @@ __device__ __forceinline__ void unpack_bf16x4(uint2 v, float y[4]) {
     y[1] = bf16_hi(v.x);
     y[2] = bf16_lo(v.y);
     y[3] = bf16_hi(v.y);
+}
+
+// Phase A with at most NCW / 2 chunks of 8 rows: two warps per chunk, four rows each, so that
+// every consumer warp takes part; rows go out as tagged words to outt[row].
+__device__ __forceinline__ void consume_rows_halves(Smem& sm, const FusedArgs& a, uint32_t q0,
+                                                    int r0, int n, unsigned long long* outt,
+                                                    unsigned tag) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nch = (n + RPC_ROW - 1) / RPC_ROW;
+    const int ci = warp >> 1, half = warp & 1;
+    if (ci >= nch) return;
+    const uint32_t qq = q0 + ci;
+    const int slot = qq % NS;
+    if (!warp_wait_full(sm, slot, (qq / NS) & 1, a)) return;
+    const int rb = r0 + ci * RPC_ROW + 4 * half;  // first row of this warp's half
+    const float v = fma_rows4<D>(sm, sm.ring[slot] + half * 4 * D * 2, rb);
+    __syncwarp();
+    if (lane == 0) mbar_arrive_n(&sm.empty[slot], NCW / 2);  // two warps release the chunk
+    const float y = __shfl_sync(0xffffffffu, v, 8 * (lane & 3));
+    if (lane < 4 && rb + lane < r0 + n) st_tagged(outt + rb + lane, y, tag);
 }
 
 // Static inputs of the attention prologue, loaded before the phase's grid wait.
@@ -1300,7 +1368,11 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) 
                 stage_norm(sm, xv, nw, a.eps);
                 stamp(a, k, G, c, 3);
                 const Span s = part(QKV_ROWS, G, c);
-                consume_rows<D, RPC_ROW, kTag>(sm, a, q, s.r0, s.n, nullptr, QKV_ROWS, a.qkvt, tag);
+                if (chunks_of(s.n, RPC_ROW) * 2 <= NCW) {
+                    consume_rows_halves(sm, a, q, s.r0, s.n, a.qkvt, tag);
+                } else {
+                    consume_rows<D, RPC_ROW, kTag>(sm, a, q, s.r0, s.n, nullptr, QKV_ROWS, a.qkvt, tag);
+                }
                 q += chunks_of(s.n, RPC_ROW);
                 stamp(a, k, G, c, 4);
                 phase_end(sm, a, k++, false, G, c);
