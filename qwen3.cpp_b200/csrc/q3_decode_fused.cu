@@ -329,6 +329,9 @@ __device__ __forceinline__ bool warp_wait_full(Smem& sm, int slot, uint32_t pari
     const int lane = threadIdx.x & 31;
     int ok = 0;
     if (!Q3_CHECK(slot >= 0 && slot < NS, 20, slot, parity, 0)) return false;
+    // Fast path: the chunk has landed (the usual case, the ring runs ahead): every lane's own
+    // non-blocking probe observes the completed phase.
+    if (__all_sync(0xffffffffu, mbar_test_wait(&sm.full[slot], parity))) return true;
     if (lane == 0) {
         if (a.prof && !mbar_test_wait(&sm.full[slot], parity)) {
             // Instrumentation: time this warp spends waiting for ring data.
