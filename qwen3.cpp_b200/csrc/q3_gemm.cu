@@ -279,7 +279,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         for (int t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
             const int tmn = t % (num_m * num_n);
             const int tm = tmn % num_m, tn = tmn / num_m;
-            if (!mbar_wait(&tfull[acc], acc_phase, args.budget, abort)) {
+            if (!mbar_wait_warp(&tfull[acc], acc_phase, args.budget, abort)) {
                 fail(abort, args.err, 6);
                 break;
             }

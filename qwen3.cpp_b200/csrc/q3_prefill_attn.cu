@@ -144,7 +144,7 @@ __device__ __forceinline__ bool fold_o(float (&acc)[HD / 2], float& m_acc, int i
                                        uint32_t tmem_lane_half, uint64_t* o_full,
                                        uint64_t* o_empty, int lane, long long budget,
                                        volatile int* abort) {
-    if (!mbar_wait(&o_full[i & 1], (i >> 1) & 1, budget, abort)) return false;
+    if (!mbar_wait_warp(&o_full[i & 1], (i >> 1) & 1, budget, abort)) return false;
     tc_fence_after();
     const float f = ex2(m_acc - m_i);
     const uint32_t ob = tmem_lane_half + static_cast<uint32_t>(256 + (i & 1) * 128);
@@ -171,7 +171,7 @@ __device__ __forceinline__ float exchange_row(float* red, uint64_t* mx_bar, int 
     uint64_t* b = &mx_bar[(t & 1) * 4 + (r >> 5)];
     red[((t & 1) * 2 + half) * ROWS + r] = v;
     mbar_arrive(b);
-    if (!mbar_wait(b, (t >> 1) & 1, budget, abort)) return __int_as_float(0x7fc00000);
+    if (!mbar_wait_warp(b, (t >> 1) & 1, budget, abort)) return __int_as_float(0x7fc00000);
     return red[((t & 1) * 2 + (half ^ 1)) * ROWS + r];
 }
 
@@ -437,7 +437,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         bool ok = true;
 
         for (int t = 0; t < ntiles && !*abort; ++t) {
-            if (!mbar_wait(&s_full[t & 1], (t >> 1) & 1, a.budget, abort)) {
+            if (!mbar_wait_warp(&s_full[t & 1], (t >> 1) & 1, a.budget, abort)) {
                 fail(abort, a.err, 17);
                 ok = false;
                 break;

@@ -39,6 +39,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// Non-blocking probe of the phase of parity `parity` (try_wait may suspend the thread first).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
 // Waits for the phase of parity `parity` to complete. Gives up (returns false) once `budget`
 // cycles have passed or *abort is set by another thread of the CTA.
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, long long budget,
@@ -50,6 +62,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, long lon
         if (clock64() - t0 > budget) return false;
     }
     return true;
+}
+// mbar_wait for every lane of a converged warp: a non-blocking probe by every lane first, so a
+// phase that has already completed costs one probe (a blocking try_wait by 32 lanes costs
+// hundreds of cycles even then).
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* b, uint32_t parity, long long budget,
+                                               volatile int* abort) {
+    if (__all_sync(0xffffffffu, mbar_test_wait(b, parity))) return true;
+    return mbar_wait(b, parity, budget, abort);
 }
 
 // 2-D tiled TMA load global -> shared (this CTA), completing on an mbarrier. x is the innermost
