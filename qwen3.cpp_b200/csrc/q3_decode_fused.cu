@@ -400,6 +400,34 @@ __device__ __forceinline__ int barriers_of(const FusedArgs& a, bool shrt) {
 
 // ------------------------------------------------------------------ producer
 
+// L2 prefetch of unit u of a CTA's copy sequence (u < n_layers: this CTA's weight rows of layer
+// u; u == n_layers: the first rows of its lm_head slice), so that the ring copies of that unit hit
+// L2 while the HBM stream keeps running through the grid-wide waits in between. Out of line (run
+// once per unit): it stays out of the producer loop's instruction working set.
+__device__ __noinline__ void prefetch_unit(const FusedLayer* layers, int n_layers,
+                                           const uint16_t* lm_head, int vocab, int u, int G, int c) {
+    const int P = G / NKV;
+    const int g = c % NKV, p = c / NKV;
+    if (u < n_layers) {
+        const FusedLayer w = layers[u];
+        Span sp = part(QKV_ROWS, G, c);
+        prefetch_l2(w.wqkv + static_cast<size_t>(sp.r0) * D, sp.n * D * 2);
+        if (c < NKV * P) {
+            sp = part(D, P, p);
+            prefetch_l2(w.wop + static_cast<size_t>(g) * D * GRP + static_cast<size_t>(sp.r0) * GRP,
+                        sp.n * GRP * 2);
+        }
+        sp = part(H, G, c);
+        prefetch_l2(w.w1 + static_cast<size_t>(sp.r0) * D, sp.n * D * 2);
+        prefetch_l2(w.w3 + static_cast<size_t>(sp.r0) * D, sp.n * D * 2);
+        prefetch_l2(w.w2t + static_cast<size_t>(sp.r0) * D, sp.n * D * 2);
+    } else {
+        const Span sp = part(vocab, G, c);
+        prefetch_l2(lm_head + static_cast<size_t>(sp.r0) * D, min(sp.n, 96) * D * 2);
+    }
+}
+
+
 struct Producer {
     Smem& sm;
     const FusedArgs& a;
@@ -474,34 +502,12 @@ struct Producer {
         return true;
     }
 
-    // L2 prefetch of unit u of the copy sequence (u < n_layers: this CTA's weight rows of layer
-    // u; u == n_layers: the first rows of its lm_head slice), so that the ring copies of that
-    // unit hit L2 while the HBM stream keeps running through the grid-wide waits in between.
-    __device__ void prefetch_unit(int u, int G, int c) {
-        const int P = G / NKV;
-        const int g = c % NKV, p = c / NKV;
-        if (u < a.n_layers) {
-            const FusedLayer w = a.layers[u];
-            Span sp = part(QKV_ROWS, G, c);
-            prefetch_l2(w.wqkv + static_cast<size_t>(sp.r0) * D, sp.n * D * 2);
-            if (c < NKV * P) {
-                sp = part(D, P, p);
-                prefetch_l2(w.wop + static_cast<size_t>(g) * D * GRP + static_cast<size_t>(sp.r0) * GRP,
-                            sp.n * GRP * 2);
-            }
-            sp = part(H, G, c);
-            prefetch_l2(w.w1 + static_cast<size_t>(sp.r0) * D, sp.n * D * 2);
-            prefetch_l2(w.w3 + static_cast<size_t>(sp.r0) * D, sp.n * D * 2);
-            prefetch_l2(w.w2t + static_cast<size_t>(sp.r0) * D, sp.n * D * 2);
-        } else {
-            const Span sp = part(a.vocab, G, c);
-            prefetch_l2(a.lm_head + static_cast<size_t>(sp.r0) * D, min(sp.n, 96) * D * 2);
-        }
-    }
     // Prefetches unit k of the whole call (units n_layers + 1 per step) if it exists.
     __device__ void prefetch_ahead(int k, int G, int c) {
         const int per = a.n_layers + 1;
-        if (a.l2_ahead > 0 && k < a.n_steps * per) prefetch_unit(k % per, G, c);
+        if (a.l2_ahead > 0 && k < a.n_steps * per) {
+            prefetch_unit(a.layers, a.n_layers, a.lm_head, a.vocab, k % per, G, c);
+        }
     }
 
     __device__ void run(int G, int c) {
@@ -558,6 +564,12 @@ struct Producer {
 };
 
 // ------------------------------------------------------------------ consumer helpers
+
+__device__ __forceinline__ uint8_t* smem_raw_ptr() {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    return smem_raw;
+}
+
 //
 
 __device__ __forceinline__ float consumer_sum(float v, Smem& sm) {
@@ -596,11 +608,14 @@ __device__ __forceinline__ void stage_norm(Smem& sm, float4 xv, uint2 wv, float 
 // fp32 activation. Lane l takes the 16-byte units u = l + 32 j (j < K / 256) of every row and
 // holds the matching activation elements 8u..8u+7 in registers; a transposing butterfly over the
 // eight row sums leaves row q in lanes 4q..4q+3. Result: lanes 0-3 hold rows 2t and 2t+1
-// (t = lane) in y0, y1.
+// (t = lane) in .x, .y. Out of line: every phase that dots K-element rows runs the same copy of
+// this code, which keeps the kernel's instruction working set small.
 template <int K>
-__device__ __forceinline__ void fma_rows8(const Smem& sm, const FusedArgs& a, const uint8_t* rows,
-                                          int row0, float& y0, float& y1) {
+__device__ __noinline__ float2 fma_rows8(int slot, int row0) {
+    static_assert(8 * K * 2 <= SLOT, "eight rows per ring chunk");
     constexpr int U = K / 256;
+    const Smem& sm = *reinterpret_cast<const Smem*>(smem_raw_ptr());
+    const uint8_t* rows = sm.ring[slot];
     const int lane = threadIdx.x & 31;
     float xr[U][8];
 #pragma unroll
@@ -619,10 +634,6 @@ __device__ __forceinline__ void fma_rows8(const Smem& sm, const FusedArgs& a, co
 #pragma unroll
         for (int j = 0; j < U; ++j) {
             const int u = (lane + 32 * j) ^ sw;
-#ifdef Q3_FUSED_CHECKS
-            const long long woff = (rp - &sm.ring[0][0]) + (u << 4);
-            Q3_CHECK(woff >= 0 && woff + 16 <= static_cast<long long>(NS) * SLOT, 40, woff, row0, j);
-#endif
             const uint4 w = *reinterpret_cast<const uint4*>(rp + (u << 4));
             acc0 = fmaf(bf16_lo(w.x), xr[j][0], acc0);
             acc1 = fmaf(bf16_hi(w.x), xr[j][1], acc1);
@@ -655,8 +666,7 @@ __device__ __forceinline__ void fma_rows8(const Smem& sm, const FusedArgs& a, co
     v += __shfl_xor_sync(0xffffffffu, v, 2);
     v += __shfl_xor_sync(0xffffffffu, v, 1);
     const int t = lane & 3;
-    y0 = __shfl_sync(0xffffffffu, v, 8 * t);
-    y1 = __shfl_sync(0xffffffffu, v, 8 * t + 4);
+    return make_float2(__shfl_sync(0xffffffffu, v, 8 * t), __shfl_sync(0xffffffffu, v, 8 * t + 4));
 }
 
 // As fma_rows8 for 4 rows; returns the row sums with row q in lanes 8q..8q+7.
@@ -736,8 +746,8 @@ __device__ __forceinline__ void consume_rows(Smem& sm, const FusedArgs& a, uint3
         if (!warp_wait_full(sm, slot, (qq / NS) & 1, a)) continue;
         const int rb = r0 + ci * rpc;
         const int rn = min(rpc, r0 + n - rb);
-        float y0, y1;
-        fma_rows8<K>(sm, a, sm.ring[slot], rb, y0, y1);
+        const float2 yv = fma_rows8<K>(slot, rb);
+        const float y0 = yv.x, y1 = yv.y;
         __syncwarp();
         if (lane == 0) mbar_arrive_n(&sm.empty[slot], NCW);  // a warp-owned chunk
         if (mode == kPair) {
@@ -1208,20 +1218,16 @@ __device__ __forceinline__ int reduce_argmax(const FusedArgs& a, int G) {
     return bi == INT_MAX ? 0 : bi;
 }
 
-__device__ __forceinline__ uint8_t* smem_raw_ptr() {
-    extern __shared__ __align__(128) uint8_t smem_raw[];
-    return smem_raw;
+__device__ __noinline__ void stamp_write(unsigned long long* slot) {
+    // Nanoseconds on the globaltimer scale, interpolated with the SM cycle counter (at the
+    // 1965 MHz maximum clock) for a resolution finer than the globaltimer's update interval.
+    Smem& sm = *reinterpret_cast<Smem*>(smem_raw_ptr());
+    const long long dc = clock64() - sm.clk0;
+    *slot = sm.gt0 + static_cast<unsigned long long>(dc * 1000 / 1965);
 }
 
 __device__ __forceinline__ void stamp(const FusedArgs& a, unsigned kk, int G, int c, int which) {
-    if (a.prof && threadIdx.x == 0) {
-        // Nanoseconds on the globaltimer scale, interpolated with the SM cycle counter (at the
-        // 1965 MHz maximum clock) for a resolution finer than the globaltimer's update interval.
-        Smem& sm = *reinterpret_cast<Smem*>(smem_raw_ptr());
-        const long long dc = clock64() - sm.clk0;
-        a.prof[(static_cast<size_t>(kk) * G + c) * 8 + which] =
-            sm.gt0 + static_cast<unsigned long long>(dc * 1000 / 1965);
-    }
+    if (a.prof && threadIdx.x == 0) stamp_write(a.prof + (static_cast<size_t>(kk) * G + c) * 8 + which);
 }
 
 // Phase entry: with nb > 0 thread 0 waits until every CTA has made nb arrivals; in any case one
@@ -1334,6 +1340,21 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) 
         sm.wait_cycles = 0;
         sm.gt0 = globaltimer();
         sm.clk0 = clock64();
+        if (a.prof) {
+            // Instrumentation: pair the cycle counter with the moment the globaltimer ticks, so
+            // that the stamps of different SMs share one time base to within a loop iteration
+            // rather than to within the timer's update interval. Bounded: gives up after 2^16
+            // reads and keeps the first pairing.
+            for (int it = 0; it < (1 << 16); ++it) {
+                const unsigned long long t = globaltimer();
+                const long long cnow = clock64();
+                if (t != sm.gt0) {
+                    sm.gt0 = t;
+                    sm.clk0 = cnow;
+                    break;
+                }
+            }
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
