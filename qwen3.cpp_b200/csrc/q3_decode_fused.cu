@@ -1313,13 +1313,31 @@ __device__ __forceinline__ float4 phase_a_input(Smem& sm, const FusedArgs& a, co
 
 // Xcur = x + sum_g partial_g over the eight KV-head groups (in group order), this thread's four
 // elements, from the tagged o_proj partials of phase BC / C.
+// The first probes of all eight groups are issued together (one L2 round trip when the partials
+// have landed); only groups not yet written are then polled, one after another.
 __device__ __forceinline__ float4 gather_oproj(Smem& sm, const FusedArgs& a, float4 xv,
                                                unsigned tag) {
+    unsigned long long w[NKV][4];
+#pragma unroll
+    for (int gg = 0; gg < NKV; ++gg) {
+        const unsigned long long* p = a.opart + static_cast<size_t>(gg) * D + 4 * threadIdx.x;
+        ld_tagged2(p, w[gg][0], w[gg][1]);
+        ld_tagged2(p + 2, w[gg][2], w[gg][3]);
+    }
     float4 proj = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
     for (int gg = 0; gg < NKV; ++gg) {
-        const float4 p = poll4(a, a.opart + static_cast<size_t>(gg) * D + 4 * threadIdx.x, tag,
-                               &sm.abort_flag, 3);
+        const bool ready = static_cast<unsigned>(w[gg][0] >> 32) == tag &&
+                           static_cast<unsigned>(w[gg][1] >> 32) == tag &&
+                           static_cast<unsigned>(w[gg][2] >> 32) == tag &&
+                           static_cast<unsigned>(w[gg][3] >> 32) == tag;
+        const float4 p =
+            ready ? make_float4(__uint_as_float(static_cast<unsigned>(w[gg][0])),
+                                __uint_as_float(static_cast<unsigned>(w[gg][1])),
+                                __uint_as_float(static_cast<unsigned>(w[gg][2])),
+                                __uint_as_float(static_cast<unsigned>(w[gg][3])))
+                  : poll4(a, a.opart + static_cast<size_t>(gg) * D + 4 * threadIdx.x, tag,
+                          &sm.abort_flag, 3);
         proj = add4(proj, p);
     }
     return add4(xv, proj);
