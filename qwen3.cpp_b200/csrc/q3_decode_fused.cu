@@ -513,7 +513,7 @@ struct Producer {
     __device__ void run(int G, int c) {
         pol_w = evict_first_policy();
         pol_kv = evict_last_policy();
-        const StepParams sp0 = *a.sp;
+        const StepParams sp0 = a.sp_from_args ? a.sp_init : *a.sp;
         const int P = G / NKV;
         const bool in_grp = c < NKV * P;
         const int g = c % NKV, p = c / NKV;
@@ -1301,7 +1301,7 @@ __device__ __forceinline__ float4 phase_a_input(Smem& sm, const FusedArgs& a, co
         // Zero this CTA's share of the other step parity's down-projection accumulators: their
         // last readers arrived at the previous step's lm_head barrier, their next writers (next
         // step) come after this step's.
-        float* yz = a.ybuf + static_cast<size_t>((st + 1) & 1) * a.n_layers * kYRep * D;
+        float* yz = a.ybuf + static_cast<size_t>((a.parity0 + st + 1) & 1) * a.n_layers * kYRep * D;
         const Span ys = part(a.n_layers * kYRep * D, G, c);
         for (int i = tid; i < ys.n; i += NCT) yz[ys.r0 + i] = 0.0f;
     } else {
@@ -1386,7 +1386,7 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) 
     }
 
     // ---------------- consumers
-    const StepParams sp0 = *a.sp;
+    const StepParams sp0 = a.sp_from_args ? a.sp_init : *a.sp;
     const int P = G / NKV;
     const bool in_grp = c < NKV * P;
     const int g = c % NKV, gp = c / NKV;
@@ -1397,7 +1397,7 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) 
 
     for (int st = 0; st < a.n_steps; ++st) {
         const StepPos p = step_pos(a, sp0, st);
-        float* yb = a.ybuf + static_cast<size_t>(st & 1) * a.n_layers * kYRep * D;
+        float* yb = a.ybuf + static_cast<size_t>((a.parity0 + st) & 1) * a.n_layers * kYRep * D;
         for (int l = 0; l < a.n_layers; ++l) {
             const FusedLayer w = a.layers[l];
             const unsigned tag = step_tag(a, st, l);
@@ -1525,6 +1525,10 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) 
                 *a.sp = np;
             }
         }
+        // Every CTA has made its last arrival and waits on the counter no more (each producer
+        // passed its last grid wait before its consumers could finish): the counter starts the
+        // next launch at zero.
+        if (tid == 0) *a.bar = 0u;
     }
 }
 

@@ -40,7 +40,10 @@ struct FusedArgs {
     const float2* rope;          // [rope_len][64] (cos, sin)
     int rope_len;
     float* ybuf;                 // [2][n_layers][copies][1024] down-projection accumulators (by
-                                 // step parity; parity 0 zero at launch), fused_ybuf_floats()
+                                 // step parity), fused_ybuf_floats(); the first step's parity
+                                 // zero at launch (each step zeroes the other parity, which
+                                 // the next step - of this launch or the next - uses)
+    int parity0;                 // accumulator parity of the first step
     unsigned long long* qkvt;    // [4096] q|k|v, tagged (value bits | tag << 32)
     unsigned long long* opart;   // [8][1024] o_proj partial of each KV-head group, tagged
     unsigned epoch;              // tag base of this launch (differs from the previous launch)
@@ -49,10 +52,13 @@ struct FusedArgs {
     float2* am_part;             // [grid] per-CTA (value, index) of the lm_head rows
     float* logits;               // [vocab]
     float* taps;                 // nullable: [(n_layers+1), 1024]
-    StepParams* sp;
-    int32_t* token_log;
+    StepParams* sp;              // device step parameters: read at launch unless sp_from_args,
+                                 // advanced past the last step at the end
+    StepParams sp_init;          // the first step's parameters when sp_from_args
+    int sp_from_args;    int32_t* token_log;
     const int32_t* forced;       // nullable: teacher-forced tokens
-    unsigned* bar;               // grid arrival counter, zero at launch
+    unsigned* bar;               // grid arrival counter: zero at launch; CTA 0 sets it back to
+                                 // zero once every arrival of the launch has been made
     unsigned* err;               // error word: 1 = a bounded wait gave up
     int n_layers, vocab, ctx, n_steps, s_max;
     float eps;

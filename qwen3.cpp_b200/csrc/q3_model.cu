@@ -683,6 +683,7 @@ Model::Model(const std::string& path, int ctx, int device) : file_(path) {
             Q3_CUDA(cudaMemcpy(fused_layers_.ptr, fl.data(), fl.size() * sizeof(FusedLayer),
                                cudaMemcpyHostToDevice));
             fused_y_.alloc(fused_ybuf_floats(c.n_layers) * 4);
+            Q3_CUDA(cudaMemset(fused_y_.ptr, 0, fused_y_.bytes));
             // Tagged q|k|v [4096] and o_proj partials [8][1024]; zero tags never match a launch's.
             fused_tagged_.alloc((static_cast<size_t>(c.n_heads + 2 * c.n_kv_heads) * c.head_dim +
                                  static_cast<size_t>(c.n_kv_heads) * D) * 8);
@@ -728,7 +729,7 @@ void Model::fused_profile(int32_t token, int pos, uint64_t* stamps, size_t cap, 
 }
 
 void Model::launch_fused(int n_steps, bool forced, bool taps, long long spin_cycles, int offset,
-                         unsigned long long* prof) {
+                         unsigned long long* prof, const StepParams* sp_init) {
     Engine& e = *engine_;
     FusedArgs a{};
     a.prof = prof;
@@ -744,6 +745,10 @@ void Model::launch_fused(int n_steps, bool forced, bool taps, long long spin_cyc
     a.rope = e.rope();
     a.rope_len = e.rope_len();
     a.ybuf = static_cast<float*>(fused_y_.ptr);
+    // The first step's accumulators were zeroed by the previous launch's last step (or at
+    // allocation / after a launch that gave up).
+    a.parity0 = fused_parity_;
+    fused_parity_ = (fused_parity_ + n_steps) & 1;
     a.qkvt = static_cast<unsigned long long*>(fused_tagged_.ptr);
     a.opart = a.qkvt + static_cast<size_t>(cfg_.n_heads + 2 * cfg_.n_kv_heads) * cfg_.head_dim;
     fused_epoch_ = (fused_epoch_ + 1) & 0xFFFu;
@@ -755,6 +760,10 @@ void Model::launch_fused(int n_steps, bool forced, bool taps, long long spin_cyc
     a.logits = static_cast<float*>(logits_.ptr);
     a.taps = taps ? e.taps() : nullptr;
     a.sp = e.step_params();
+    if (sp_init) {
+        a.sp_init = *sp_init;
+        a.sp_from_args = 1;
+    }
     a.token_log = static_cast<int32_t*>(token_log_.ptr);
     a.forced = forced ? static_cast<const int32_t*>(forced_.ptr) : nullptr;
     a.bar = static_cast<unsigned*>(fused_sync_.ptr);
@@ -768,15 +777,24 @@ void Model::launch_fused(int n_steps, bool forced, bool taps, long long spin_cyc
     a.spin_cycles = spin_cycles;
     a.barrier_offset = offset;
     a.l2_ahead = fused_l2_ahead();
-    Q3_CUDA(cudaMemsetAsync(a.bar, 0, sizeof(unsigned), e.stream()));
-    Q3_CUDA(cudaMemsetAsync(fused_y_.ptr, 0, fused_y_.bytes, e.stream()));
+    // The arrival counter is zero here: set at allocation, back to zero at the end of every
+    // launch that completed (CTA 0), and by reset_fused_state after one that gave up.
     launch_decode_fused(a, fused_grid_, e.stream());
 }
 
+void Model::reset_fused_state() {
+    cudaStream_t s = engine_->stream();
+    Q3_CUDA(cudaStreamSynchronize(s));
+    Q3_CUDA(cudaMemsetAsync(fused_sync_.ptr, 0, fused_sync_.bytes, s));
+    Q3_CUDA(cudaMemsetAsync(fused_y_.ptr, 0, fused_y_.bytes, s));
+    Q3_CUDA(cudaStreamSynchronize(s));
+    fused_parity_ = 0;
+}
+
+// The error word is zero unless a launch gave up, and check_fused_error zeroes the state again
+// when it reports one; only the self-check record (checking builds) is cleared per call.
 void Model::clear_fused_error() {
     if (!fused_enabled()) return;
-    Q3_CUDA(cudaMemsetAsync(static_cast<unsigned*>(fused_sync_.ptr) + 32, 0, sizeof(unsigned),
-                            engine_->stream()));
     if (fused_dbg_.ptr) {
         Q3_CUDA(cudaMemsetAsync(fused_dbg_.ptr, 0, fused_dbg_.bytes, engine_->stream()));
     }
@@ -793,6 +811,7 @@ void Model::check_fused_error() {
                                 engine_->stream()));
     }
     Q3_CUDA(cudaStreamSynchronize(engine_->stream()));
+    if (dbg[0] || err) reset_fused_state();
     if (dbg[0]) {
         throw std::runtime_error(
             "fused decode kernel self-check " + std::to_string(dbg[0]) + " failed in CTA " +
@@ -811,17 +830,13 @@ bool Model::fused_timeout_selftest() {
     Engine& e = *engine_;
     e.ensure_rope(2);
     e.write_step(start_params(0, 0, 0));
-    Q3_CUDA(cudaMemsetAsync(static_cast<unsigned*>(fused_sync_.ptr) + 32, 0, sizeof(unsigned),
-                            e.stream()));
     // ~10 ms bound; barrier target one above what the grid can reach.
     launch_fused(1, false, false, 20000000LL, 1);
     unsigned err = 0;
     Q3_CUDA(cudaMemcpyAsync(&err, static_cast<unsigned*>(fused_sync_.ptr) + 32, sizeof(unsigned),
                             cudaMemcpyDeviceToHost, e.stream()));
     Q3_CUDA(cudaStreamSynchronize(e.stream()));
-    Q3_CUDA(cudaMemsetAsync(static_cast<unsigned*>(fused_sync_.ptr) + 32, 0, sizeof(unsigned),
-                            e.stream()));
-    Q3_CUDA(cudaStreamSynchronize(e.stream()));
+    reset_fused_state();  // the launch gave up: counter, error word and accumulators undefined
     return err != 0;
 }
 
@@ -866,11 +881,14 @@ void Model::enqueue_step(bool forced, bool taps) {
                         forced ? static_cast<const int32_t*>(forced_.ptr) : nullptr, s);
 }
 
-void Model::run_steps(int n, bool forced, bool taps, float* logits_log_dev) {
+void Model::run_steps(int n, bool forced, bool taps, float* logits_log_dev,
+                      const StepParams* sp_init) {
     Engine& e = *engine_;
     if (fused_enabled()) {
         constexpr long long kSpinCycles = 4000000000LL;  // ~2 s at the B200 boost clock
-        if (logits_log_dev || taps) {
+        if (sp_init) {
+            launch_fused(1, forced, taps, kSpinCycles, 0, nullptr, sp_init);
+        } else if (logits_log_dev || taps) {
             for (int i = 0; i < n; ++i) {
                 launch_fused(1, forced, taps, kSpinCycles, 0);
                 if (logits_log_dev) {
@@ -921,9 +939,15 @@ void Model::forward_token(int32_t token, int pos, float* hidden_host, float* log
     check_token_pos(token, pos);
     Engine& e = *engine_;
     e.ensure_rope(pos + 2);
-    e.write_step(start_params(token, pos, 0));
+    const StepParams sp = start_params(token, pos, 0);
     clear_fused_error();
-    run_steps(1, false, hidden_host != nullptr, nullptr);
+    if (fused_enabled()) {
+        // The step's parameters travel with the launch (no staging copy, no synchronisation).
+        run_steps(1, false, hidden_host != nullptr, nullptr, &sp);
+    } else {
+        e.write_step(sp);
+        run_steps(1, false, hidden_host != nullptr, nullptr);
+    }
     cudaStream_t s = e.stream();
     // The error word comes back with the outputs: one synchronisation per call.
     pinned_err_.ensure(sizeof(unsigned));

@@ -199,13 +199,19 @@ private:
     StepParams start_params(int32_t token, int pos, int n_forced) const;
     void ensure_logs(int n);
     void enqueue_step(bool forced, bool taps);
-    void run_steps(int n, bool forced, bool taps, float* logits_log_dev);
+    // sp_init (fused path, n == 1): the step's parameters go to the kernel as an argument and
+    // the device copy is not written first.
+    void run_steps(int n, bool forced, bool taps, float* logits_log_dev,
+                   const StepParams* sp_init = nullptr);
     void prefill_batched(const int32_t* ids, int n, int pos0, float* last_logits, int32_t* next,
                          float* hidden_host);
     void launch_fused(int n_steps, bool forced, bool taps, long long spin_cycles, int offset,
-                      unsigned long long* prof = nullptr);
+                      unsigned long long* prof = nullptr, const StepParams* sp_init = nullptr);
     void clear_fused_error();
     void check_fused_error();
+    // Zeroes the arrival counter, the error word and both accumulator parities (after a launch
+    // that gave up, whose state is then undefined).
+    void reset_fused_state();
 
     ModelFile file_;
     q3_config cfg_{};
@@ -232,6 +238,7 @@ private:
     DeviceBuffer fused_layers_, fused_part_o_, fused_part_ml_, fused_am_, fused_sync_, fused_wperm_,
         fused_y_, fused_tagged_, fused_dbg_;
     unsigned fused_epoch_ = 0;  // tag base of the last fused launch (1..4095)
+    int fused_parity_ = 0;      // accumulator parity of the next launch's first step
 };
 
 // class Block of the reference (include/inference.h:178-202) on one GPU.

@@ -157,6 +157,26 @@ def test_forward_token_ref_matches_copy(models, oracle_run):
     assert not np.array_equal(view, first)  # the buffer now holds the next position's logits
 
 
+def test_interleaved_launches(models, oracle_run):
+    """Single-step calls (the fused path passes the step's parameters with the launch) and
+    teacher-forced device loops of odd and even lengths, interleaved: each launch starts from the
+    state the previous one left (accumulator parity, arrival counter, step parameters)."""
+    gpu, _ = models
+    seq, argmax, logits = oracle_run
+    gpu.reset()
+    pos = 0
+    for kind, n in (("one", 1), ("loop", 3), ("one", 1), ("one", 1), ("loop", 4), ("loop", 1),
+                    ("one", 1), ("loop", 5)):
+        if kind == "one":
+            lg = gpu.forward_token(int(seq[pos]), pos)[None]
+            am = lg.argmax(axis=1)
+        else:
+            am, lg = gpu.decode_forced(seq[pos:pos + n], pos, want_logits=True)
+        assert np.abs(lg - logits[pos:pos + n]).max() <= LOGITS_MAX_ABS, (kind, pos)
+        assert (np.asarray(am) == argmax[pos:pos + n]).mean() >= 0.5, (kind, pos)
+        pos += n
+
+
 def test_range_errors(models, q3lib):
     gpu, _ = models
     with pytest.raises(q3lib.OutOfRange):
