@@ -57,8 +57,9 @@ constexpr int NT = NCT + 32;           // + one producer warp
 constexpr int NS = 8;                  // ring slots
 constexpr int kProducerSleepNs = 256;  // back-off of the producer while the ring is full
 // Copies of each layer's down-projection accumulator: CTA c adds into copy c % kYRep, which cuts
-// the number of fp32 atomics per address kYRep-fold; phase A sums the copies.
-constexpr int kYRep = 8;
+// the number of fp32 atomics per address kYRep-fold; phase A sums the copies (measured: 4 copies
+// 0.6% faster than 8, 16 copies 1.5% slower).
+constexpr int kYRep = 4;
 constexpr int SLOT = 16384;            // bytes per slot
 // Chunk q lives in slot q % NS and, in warp-owned tasks, is consumed by warp q % NCW; shared
 // chunks (KV pages, w2t rows) are read by every consumer warp. A slot is free again after NCW

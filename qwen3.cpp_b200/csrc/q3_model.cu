@@ -636,7 +636,10 @@ Model::Model(const std::string& path, int ctx, int device) : file_(path) {
     tensor_count_ = static_cast<int>(file_.tensor_count());
 
     engine_ = std::make_unique<Engine>(cfg_, c.n_layers, device_, ctx);
-    logits_.alloc(V * 4);
+    // The fused kernel's error word sits right after the logits, so that one copy brings back
+    // both (q3_forward_token_ref).
+    logits_.alloc(V * 4 + 64);
+    Q3_CUDA(cudaMemset(logits_.ptr, 0, logits_.bytes));
     argmax_part_.alloc(static_cast<size_t>(gemv_grid(c.vocab_size)) * sizeof(float2));
     argmax_out_.alloc(16);
     ensure_logs(1024);
@@ -691,7 +694,7 @@ Model::Model(const std::string& path, int ctx, int device) : file_(path) {
             fused_part_o_.alloc(static_cast<size_t>(c.n_heads) * fused_s_max_ * c.head_dim * 4);
             fused_part_ml_.alloc(static_cast<size_t>(c.n_heads) * fused_s_max_ * sizeof(float2));
             fused_am_.alloc(static_cast<size_t>(fused_grid_) * sizeof(float2));
-            fused_sync_.alloc(256);  // [0] arrival counter, [32] error word
+            fused_sync_.alloc(256);  // [0] arrival counter
             Q3_CUDA(cudaMemset(fused_sync_.ptr, 0, 256));
             if (getenv("Q3_FUSED_CHECKS")) {
                 // Record buffer of the self-checking build (compiled with -DQ3_FUSED_CHECKS).
@@ -767,7 +770,7 @@ void Model::launch_fused(int n_steps, bool forced, bool taps, long long spin_cyc
     a.token_log = static_cast<int32_t*>(token_log_.ptr);
     a.forced = forced ? static_cast<const int32_t*>(forced_.ptr) : nullptr;
     a.bar = static_cast<unsigned*>(fused_sync_.ptr);
-    a.err = static_cast<unsigned*>(fused_sync_.ptr) + 32;
+    a.err = fused_err_word();
     a.n_layers = cfg_.n_layers;
     a.vocab = cfg_.vocab_size;
     a.ctx = cfg_.max_seq_len;
@@ -786,6 +789,7 @@ void Model::reset_fused_state() {
     cudaStream_t s = engine_->stream();
     Q3_CUDA(cudaStreamSynchronize(s));
     Q3_CUDA(cudaMemsetAsync(fused_sync_.ptr, 0, fused_sync_.bytes, s));
+    Q3_CUDA(cudaMemsetAsync(fused_err_word(), 0, sizeof(unsigned), s));
     Q3_CUDA(cudaMemsetAsync(fused_y_.ptr, 0, fused_y_.bytes, s));
     Q3_CUDA(cudaStreamSynchronize(s));
     fused_parity_ = 0;
@@ -804,7 +808,7 @@ void Model::check_fused_error() {
     if (!fused_enabled()) return;
     unsigned err = 0;
     unsigned long long dbg[8] = {};
-    Q3_CUDA(cudaMemcpyAsync(&err, static_cast<unsigned*>(fused_sync_.ptr) + 32, sizeof(unsigned),
+    Q3_CUDA(cudaMemcpyAsync(&err, fused_err_word(), sizeof(unsigned),
                             cudaMemcpyDeviceToHost, engine_->stream()));
     if (fused_dbg_.ptr) {
         Q3_CUDA(cudaMemcpyAsync(dbg, fused_dbg_.ptr, sizeof(dbg), cudaMemcpyDeviceToHost,
@@ -833,7 +837,7 @@ bool Model::fused_timeout_selftest() {
     // ~10 ms bound; barrier target one above what the grid can reach.
     launch_fused(1, false, false, 20000000LL, 1);
     unsigned err = 0;
-    Q3_CUDA(cudaMemcpyAsync(&err, static_cast<unsigned*>(fused_sync_.ptr) + 32, sizeof(unsigned),
+    Q3_CUDA(cudaMemcpyAsync(&err, fused_err_word(), sizeof(unsigned),
                             cudaMemcpyDeviceToHost, e.stream()));
     Q3_CUDA(cudaStreamSynchronize(e.stream()));
     reset_fused_state();  // the launch gave up: counter, error word and accumulators undefined
@@ -935,7 +939,13 @@ void Model::check_token_pos(int32_t token, int pos) const {
     if (pos < 0) throw std::out_of_range("Token position must not be negative");
 }
 
-void Model::forward_token(int32_t token, int pos, float* hidden_host, float* logits_host) {
+unsigned* Model::fused_err_word() const {
+    return reinterpret_cast<unsigned*>(static_cast<char*>(logits_.ptr) +
+                                       static_cast<size_t>(cfg_.vocab_size) * 4);
+}
+
+void Model::forward_token(int32_t token, int pos, float* hidden_host, float* logits_host,
+                          bool err_after_logits) {
     check_token_pos(token, pos);
     Engine& e = *engine_;
     e.ensure_rope(pos + 2);
@@ -949,12 +959,16 @@ void Model::forward_token(int32_t token, int pos, float* hidden_host, float* log
         run_steps(1, false, hidden_host != nullptr, nullptr);
     }
     cudaStream_t s = e.stream();
-    // The error word comes back with the outputs: one synchronisation per call.
+    // The error word comes back with the outputs: one synchronisation per call; with
+    // err_after_logits it is the word after the logits in logits_host (one copy for both).
     pinned_err_.ensure(sizeof(unsigned));
-    *static_cast<unsigned*>(pinned_err_.ptr) = 0u;
-    if (fused_enabled()) {
-        Q3_CUDA(cudaMemcpyAsync(pinned_err_.ptr, static_cast<unsigned*>(fused_sync_.ptr) + 32,
-                                sizeof(unsigned), cudaMemcpyDeviceToHost, s));
+    unsigned* err_host = static_cast<unsigned*>(pinned_err_.ptr);
+    *err_host = 0u;
+    if (err_after_logits) {
+        err_host = reinterpret_cast<unsigned*>(logits_host + cfg_.vocab_size);
+    } else if (fused_enabled()) {
+        Q3_CUDA(cudaMemcpyAsync(err_host, fused_err_word(), sizeof(unsigned),
+                                cudaMemcpyDeviceToHost, s));
     }
     if (hidden_host) {
         Q3_CUDA(cudaMemcpyAsync(hidden_host, e.taps(),
@@ -962,16 +976,18 @@ void Model::forward_token(int32_t token, int pos, float* hidden_host, float* log
                                 cudaMemcpyDeviceToHost, s));
     }
     if (logits_host) {
-        Q3_CUDA(cudaMemcpyAsync(logits_host, logits_.ptr, static_cast<size_t>(cfg_.vocab_size) * 4,
+        Q3_CUDA(cudaMemcpyAsync(logits_host, logits_.ptr,
+                                static_cast<size_t>(cfg_.vocab_size) * 4 +
+                                    (err_after_logits ? sizeof(unsigned) : 0),
                                 cudaMemcpyDeviceToHost, s));
     }
     Q3_CUDA(cudaStreamSynchronize(s));
-    if (*static_cast<const unsigned*>(pinned_err_.ptr) != 0u) check_fused_error();  // throws
+    if (*err_host != 0u) check_fused_error();  // throws
 }
 
 const float* Model::forward_token_ref(int32_t token, int pos) {
-    pinned_logits_.ensure(static_cast<size_t>(cfg_.vocab_size) * 4);
-    forward_token(token, pos, nullptr, static_cast<float*>(pinned_logits_.ptr));
+    pinned_logits_.ensure(static_cast<size_t>(cfg_.vocab_size) * 4 + sizeof(unsigned));
+    forward_token(token, pos, nullptr, static_cast<float*>(pinned_logits_.ptr), true);
     return static_cast<const float*>(pinned_logits_.ptr);
 }
 

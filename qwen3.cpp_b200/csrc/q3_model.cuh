@@ -162,7 +162,10 @@ public:
     float* logits() const { return static_cast<float*>(logits_.ptr); }
 
     void reset();
-    void forward_token(int32_t token, int pos, float* hidden_host, float* logits_host);
+    // err_after_logits: logits_host has room for one more word, which receives the fused
+    // kernel's error word in the same copy.
+    void forward_token(int32_t token, int pos, float* hidden_host, float* logits_host,
+                       bool err_after_logits = false);
     // ForwardToken returning the logits in a model-owned pinned host buffer, valid until the
     // next call (the reference returns a reference to its logits vector).
     const float* forward_token_ref(int32_t token, int pos);
@@ -212,6 +215,7 @@ private:
     // Zeroes the arrival counter, the error word and both accumulator parities (after a launch
     // that gave up, whose state is then undefined).
     void reset_fused_state();
+    unsigned* fused_err_word() const;  // the word after the logits in logits_
 
     ModelFile file_;
     q3_config cfg_{};
