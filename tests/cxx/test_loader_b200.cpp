@@ -6,6 +6,7 @@
 #include "inference_b200.h"
 
 #include <algorithm>
+#include <cmath>
 #include <iostream>
 #include <stdexcept>
 #include <string>
@@ -99,7 +100,22 @@ int main(int argc, char** argv) {
                                                       Expect(toks.size() == calls,
                                                              "callback span size");
                                                   });
-        Expect(a.tokens.size() == 12 && b.tokens == a.tokens, "Generate paths disagree");
+        Expect(a.tokens.size() == 12 && b.tokens.size() == 12, "Generate token counts");
+        // The two paths agree token for token, or first part at a near tie: the down-projection
+        // sums use fp32 atomics whose order varies from run to run, so where two logits are
+        // closer than twice the logit tolerance either token is a correct greedy choice.
+        size_t first = 0;
+        while (first < a.tokens.size() && a.tokens[first] == b.tokens[first]) ++first;
+        if (first < a.tokens.size()) {
+            model.ResetInference();
+            int pos = 0;
+            const std::vector<float>* lg = nullptr;
+            for (const std::int32_t t : prompt) lg = &model.ForwardToken(t, pos++, state);
+            for (size_t i = 0; i < first; ++i) lg = &model.ForwardToken(a.tokens[i], pos++, state);
+            const float gap = std::fabs((*lg)[a.tokens[first]] - (*lg)[b.tokens[first]]);
+            Expect(gap <= 0.1f, "Generate paths disagree at token " + std::to_string(first) +
+                                    " by a logit gap of " + std::to_string(gap));
+        }
         Expect(calls == 12, "callback count");
         Expect(a.stats.prompt_tokens == prompt.size() && a.stats.generated_tokens == 12,
                "generation stats");
