@@ -40,9 +40,9 @@ KV_BYTES_PER_POS = 2 * 28 * 1024 * 2  # K and V rows of every layer
 LM_HEAD_BYTES = VOCAB * 1024 * 2
 # DRAM traffic of one fused decode step (dram__bytes_read.sum + dram__bytes_write.sum), from an
 # `ncu --set full` capture of the timed one-step launch of
-# `bench.py --legs decode --steps 1 --warmup 3` (kv_len 17): 1.196952 GB read + 5.642496 MB
+# `bench.py --legs decode --steps 1 --warmup 3` (kv_len 17): 1.196486 GB read + 4.693760 MB
 # written. Re-captured whenever the kernel changes.
-FUSED_TRAFFIC_PER_STEP = 1_202_594_496
+FUSED_TRAFFIC_PER_STEP = 1_201_179_760
 # Long-prompt prefill: 2048 seeded prompt IDs (seed 2) at context 4096, batched on the tensor cores.
 PREFILL_LEN = 2048
 PREFILL_CTX = 4096
