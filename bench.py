@@ -101,6 +101,34 @@ def dist_info():
     return world, rank, local
 
 
+def max_over_ranks(v: float, world: int, device: str = "cuda") -> float:
+    """The largest of every rank's v (a time: the slowest rank's); v itself on one rank. A
+    collective: every rank calls it at the same point."""
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def dp_share(n_seqs: int, rank: int, world: int) -> list[int]:
+    """This rank's sequences of the data-parallel workload: every world-th one from its rank
+    (the ranks' shares are disjoint and cover all sequences; no collective on the data path)."""
+    return list(range(rank, n_seqs, world))
+
+
+def gather_handles(handle: bytes, world: int) -> list:
+    """Every rank's exchange-buffer handle, in rank order (the tensor-parallel set-up)."""
+    if world == 1:
+        return [handle]
+    import torch.distributed as dist
+    handles = [None] * world
+    dist.all_gather_object(handles, handle)
+    return handles
+
+
 class Clocks:
     """nvidia-smi sampling during the timed region."""
 
@@ -277,10 +305,7 @@ def run_b200_arm(args):
             total_ms += e0.elapsed_time(e1)
             kv_pos_sum += sum(PROMPT_LEN + i + 1 for i in range(n))
             done += n
-        if world > 1:
-            t = torch.tensor([total_ms], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            total_ms = float(t.item())
+        total_ms = max_over_ranks(total_ms, world)
         clk = clocks.stop()
 
         # End to end through the public API with host buffers: ForwardToken per step (token and
@@ -323,10 +348,7 @@ def run_b200_arm(args):
             torch.cuda.synchronize()
             p_ms += e0.elapsed_time(e1)
         p_ms /= PREFILL_RUNS
-        if world > 1:
-            t = torch.tensor([p_ms], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            p_ms = float(t.item())
+        p_ms = max_over_ranks(p_ms, world)
         batched = pm.prefill_path == pm.PREFILL_BATCHED
 
     # Data-parallel batched decode: this rank's share of the 64 sequences in one batch.
@@ -334,7 +356,7 @@ def run_b200_arm(args):
     mine = []
     if "dp" in legs:
         lens, prompts = dp_workload(args.dp_seqs)
-        mine = list(range(rank, args.dp_seqs, world))
+        mine = dp_share(args.dp_seqs, rank, world)
         batch = q3b200.Batch(pm, len(mine), int(max(lens[i] for i in mine)) + DP_WARMUP + DP_STEPS)
         for i in mine:
             batch.add(prompts[i])
@@ -349,10 +371,7 @@ def run_b200_arm(args):
         e1.record(bext)
         torch.cuda.synchronize()
         dp_ms = e0.elapsed_time(e1)
-        if world > 1:
-            t = torch.tensor([dp_ms], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            dp_ms = float(t.item())
+        dp_ms = max_over_ranks(dp_ms, world)
         # Bytes per step on this rank: the weights once + every sequence's KV rows at its length.
         kv_tokens = sum(int(lens[i]) + DP_WARMUP + DP_STEPS / 2 for i in mine)
         dp_bytes_step = WEIGHT_BYTES + KV_BYTES_PER_POS * kv_tokens
@@ -368,12 +387,7 @@ def run_b200_arm(args):
         tprompt = np.random.default_rng(4).integers(0, VOCAB, TP_PROMPT).astype(np.int32)
         _, tnext = tm.prefill(tprompt, 0, want_logits=False)
         tp = q3b200.TpDecoder(tm, rank, world)
-        if world > 1:
-            handles = [None] * world
-            dist.all_gather_object(handles, tp.ipc_handle())
-        else:
-            handles = [tp.ipc_handle()]
-        tp.connect(handles)
+        tp.connect(gather_handles(tp.ipc_handle(), world))
         tpx = torch.cuda.ExternalStream(tp.stream)
         warm = tp.decode(tnext, TP_PROMPT, TP_WARMUP)
         torch.cuda.synchronize()
@@ -385,10 +399,7 @@ def run_b200_arm(args):
         e1.record(tpx)
         torch.cuda.synchronize()
         tp_ms = e0.elapsed_time(e1)
-        if world > 1:
-            t = torch.tensor([tp_ms], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            tp_ms = float(t.item())
+        tp_ms = max_over_ranks(tp_ms, world)
         tp_kv = TP_PROMPT + TP_WARMUP + TP_STEPS / 2
         tp_bytes_gpu = (WEIGHT_BYTES + KV_BYTES_PER_POS * tp_kv) / world
         tp_gbs = tp_bytes_gpu * TP_STEPS / (tp_ms / 1e3) / 1e9
