@@ -160,8 +160,15 @@ class Clocks:
         self.p.terminate()
         self.p.wait(timeout=10)
         self.f.flush()
-        rows = [r.split(",") for r in Path(self.f.name).read_text().splitlines() if r.strip()]
+        text = Path(self.f.name).read_text()
         os.unlink(self.f.name)
+        return self.summarize(text)
+
+    @staticmethod
+    def summarize(text: str) -> dict:
+        """Median SM clock, maximum SM clock, the throttle reasons seen Active and the sample
+        count of nvidia-smi CSV rows in FIELDS order (no header, no units)."""
+        rows = [r.split(",") for r in text.splitlines() if r.strip()]
         sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit()]
         mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].strip().replace(".", "").isdigit()]
         reasons = set()

@@ -1,6 +1,7 @@
-"""The multi-rank host logic of bench.py on CPU: two gloo ranks (spawned processes) take the
-slowest rank's time, split the data-parallel sequences without overlap, and exchange the
-tensor-parallel handles in rank order - the steps `bench.py --gpus N` takes under torchrun."""
+"""Host logic of bench.py on CPU. Two gloo ranks (spawned processes) take the slowest rank's time,
+split the data-parallel sequences without overlap, and exchange the tensor-parallel handles in rank
+order - the steps `bench.py --gpus N` takes under torchrun; and the summary of the nvidia-smi clock
+samples that goes into the bench line."""
 import multiprocessing as mp
 import os
 import socket
@@ -71,3 +72,22 @@ def test_single_rank_needs_no_process_group():
     assert bench.max_over_ranks(3.5, 1) == 3.5
     assert bench.dp_share(5, 0, 1) == [0, 1, 2, 3, 4]
     assert bench.gather_handles(b"h", 1) == [b"h"]
+
+
+def test_clock_samples_summary():
+    """bench.py's reading of nvidia-smi samples: median SM clock, maximum, reasons seen Active."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    text = "\n".join([
+        "0, 1965, 1965, 700.1, 0x0000000000000000, Not Active, Not Active, Not Active, Not Active",
+        "0, 1950, 1965, 990.5, 0x0000000000000004, Not Active, Not Active, Not Active, Active",
+        "0, 1800, 1965, 1000.0, 0x0000000000000004, Not Active, Not Active, Not Active, Active",
+        "0, [N/A], [N/A], [N/A], [N/A], [N/A], [N/A], [N/A], [N/A]",
+        "",
+    ])
+    got = bench.Clocks.summarize(text)
+    assert got == {"sm_mhz": 1950.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"],
+                   "samples": 4}
+    assert bench.Clocks.summarize("") == {"sm_mhz": None, "sm_max_mhz": None, "reasons": [],
+                                          "samples": 0}
