@@ -218,6 +218,8 @@ def port_lib():
         lib.q3o_model_reset.argtypes = [C.c_void_p]
         lib.q3o_model_forward.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
         lib.q3o_model_kv_row.argtypes = [C.c_void_p, C.c_int, C.c_int, U16P, U16P]
+        lib.q3o_model_prefill.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p,
+                                          C.c_void_p, C.c_void_p, C.c_void_p]
         lib.q3o_rmsnorm.argtypes = [F32P, F32P, U16P, C.c_float, C.c_int]
         lib.q3o_softmax.argtypes = [F32P, F32P, C.c_int]
         lib.q3o_silu.restype = C.c_float
@@ -352,6 +354,32 @@ class PortModel:
         v = np.empty(kvd, np.uint16)
         _check_port(port_lib().q3o_model_kv_row(self._h, layer, kv_pos, k, v))
         return k, v
+
+    def forward_many(self, tokens, pos0: int = 0, want=None, logits: bool = False,
+                     layers: bool = False):
+        """ForwardToken over tokens at positions pos0.. (no ring wrap), computed layer by layer
+        over all tokens; bit-identical to calling forward() per token. want: boolean mask of the
+        tokens whose logits are computed (default all). Returns a dict with 'argmax' ([n], -1
+        where not wanted), 'logits' ([wanted, vocab], when logits) and 'hidden_last'
+        ([(n_layers + 1), dim] of the last token, when layers)."""
+        c = self.config
+        toks = np.ascontiguousarray(tokens, np.int32)
+        n = toks.size
+        mask = (np.ones(n, np.uint8) if want is None
+                else np.ascontiguousarray(np.asarray(want, bool), np.uint8))
+        am = np.empty(n, np.int32)
+        lg = np.empty((int(mask.sum()), c["vocab_size"]), np.float32) if logits else None
+        hid = np.empty((c["n_layers"] + 1, c["dim"]), np.float32) if layers else None
+        _check_port(port_lib().q3o_model_prefill(
+            self._h, toks.ctypes.data, n, int(pos0), mask.ctypes.data,
+            lg.ctypes.data if logits else None, am.ctypes.data,
+            hid.ctypes.data if layers else None))
+        out = {"argmax": am}
+        if logits:
+            out["logits"] = lg
+        if layers:
+            out["hidden_last"] = hid
+        return out
 
 
 class RefModel:

@@ -13,6 +13,7 @@
  * Status codes: 0 ok, 2 invalid_argument, 3 out_of_range (the exception types the reference
  * throws at src/inference.cpp:594-599, :774-790).
  */
+#include <immintrin.h>
 #include <math.h>
 #include <stdint.h>
 #include <stdlib.h>
@@ -319,6 +320,199 @@ int q3o_model_forward(q3o_model* m, int token, int pos, float* hidden_layers, fl
     q3o_matmul(m->logits, m->normed, m->embed, m->vocab_size, c->dim);
     if (logits) memcpy(logits, m->logits, (size_t)m->vocab_size * 4);
     return Q3O_OK;
+}
+
+/* ------------------------------------------------------------------ many tokens at once
+ *
+ * The oracle for long prompts: ForwardToken over tokens[0..n) at positions pos0.. run layer by
+ * layer over all the tokens instead of token by token. Every value is computed by the same
+ * functions in the same order as q3o_model_forward computes it for that token (each dot product
+ * is dot_bf16 over the same operands; token t attends to cache rows 0..pos0+t, which hold the same
+ * bf16 values either way), so the results are bit-identical to n calls of q3o_model_forward;
+ * only the loop order differs, which lets the weights be reused from cache across tokens. The
+ * ring buffer must not wrap (pos0 + n <= context). */
+
+/* dot_bf16 of one weight row with four activation vectors at once, written with AVX2 lanes:
+ * lane l of the low / high accumulator is the scalar code's lo[l] / hi[l] (the same fmaf chain
+ * in the same order), followed by the same reduction, so each result equals dot_bf16's bit for
+ * bit. m % 16 == 0. */
+static inline __m256 bf16x8_to_f32(const uint16_t* p) {
+    const __m128i h = _mm_loadu_si128((const __m128i*)p);
+    return _mm256_castsi256_ps(_mm256_slli_epi32(_mm256_cvtepu16_epi32(h), 16));
+}
+static inline float reduce_lanes(__m256 lo, __m256 hi) {
+    float s[8];
+    _mm256_storeu_ps(s, _mm256_add_ps(lo, hi));
+    return reduce8(s);
+}
+static void dot4_bf16(const uint16_t* w, const float* x0, const float* x1, const float* x2,
+                      const float* x3, int m, float* o) {
+    __m256 l0 = _mm256_setzero_ps(), h0 = l0, l1 = l0, h1 = l0, l2 = l0, h2 = l0, l3 = l0, h3 = l0;
+    for (int j = 0; j < m; j += 16) {
+        const __m256 wl = bf16x8_to_f32(w + j), wh = bf16x8_to_f32(w + j + 8);
+        l0 = _mm256_fmadd_ps(wl, _mm256_loadu_ps(x0 + j), l0);
+        h0 = _mm256_fmadd_ps(wh, _mm256_loadu_ps(x0 + j + 8), h0);
+        l1 = _mm256_fmadd_ps(wl, _mm256_loadu_ps(x1 + j), l1);
+        h1 = _mm256_fmadd_ps(wh, _mm256_loadu_ps(x1 + j + 8), h1);
+        l2 = _mm256_fmadd_ps(wl, _mm256_loadu_ps(x2 + j), l2);
+        h2 = _mm256_fmadd_ps(wh, _mm256_loadu_ps(x2 + j + 8), h2);
+        l3 = _mm256_fmadd_ps(wl, _mm256_loadu_ps(x3 + j), l3);
+        h3 = _mm256_fmadd_ps(wh, _mm256_loadu_ps(x3 + j + 8), h3);
+    }
+    o[0] = reduce_lanes(l0, h0);
+    o[1] = reduce_lanes(l1, h1);
+    o[2] = reduce_lanes(l2, h2);
+    o[3] = reduce_lanes(l3, h3);
+}
+
+/* out[t * ldo + i] = dot_bf16(W row i, x + t * ldx) for t < n, i < rows. */
+static void matmul_many(float* out, int ldo, const float* x, int ldx, const uint16_t* w, int rows,
+                        int m, int n) {
+    const int RB = 32, TB = 64;
+    const int nrb = (rows + RB - 1) / RB, ntb = (n + TB - 1) / TB;
+#pragma omp parallel for schedule(dynamic) collapse(2)
+    for (int tb = 0; tb < ntb; ++tb) {
+        for (int rb = 0; rb < nrb; ++rb) {
+            const int t1 = (tb + 1) * TB < n ? (tb + 1) * TB : n;
+            const int r1 = (rb + 1) * RB < rows ? (rb + 1) * RB : rows;
+            int t = tb * TB;
+            if (m % 16 == 0) {
+                for (; t + 4 <= t1; t += 4) {
+                    const float* xt = x + (size_t)t * ldx;
+                    for (int i = rb * RB; i < r1; ++i) {
+                        float o[4];
+                        dot4_bf16(w + (size_t)i * m, xt, xt + ldx, xt + 2 * (size_t)ldx,
+                                  xt + 3 * (size_t)ldx, m, o);
+                        for (int k = 0; k < 4; ++k) out[(size_t)(t + k) * ldo + i] = o[k];
+                    }
+                }
+            }
+            for (; t < t1; ++t)
+                for (int i = rb * RB; i < r1; ++i)
+                    out[(size_t)t * ldo + i] = dot_bf16(w + (size_t)i * m, x + (size_t)t * ldx, m);
+        }
+    }
+}
+
+/* hidden_last (nullable): [(n_layers + 1), dim] of the last token (as q3o_model_forward's
+ * hidden_layers). want (nullable, n flags): tokens whose logits are computed; logits_out
+ * receives them in token order ([count of flagged tokens, vocab]) and argmax_out[t] their greedy
+ * token (-1 for tokens not flagged). */
+int q3o_model_prefill(q3o_model* m, const int* tokens, int n, int pos0, const unsigned char* want,
+                      float* logits_out, int* argmax_out, float* hidden_last) {
+    const q3o_cfg* c = &m->c;
+    if (n <= 0 || pos0 < 0 || pos0 + n > c->max_seq_len) return Q3O_OUT_OF_RANGE;
+    for (int t = 0; t < n; ++t)
+        if (tokens[t] < 0 || tokens[t] >= m->vocab_size) return Q3O_OUT_OF_RANGE;
+    const int D = c->dim, hd = c->head_dim, qd = c->n_heads * hd, kvd = c->n_kv_heads * hd;
+    const int Hd = c->hidden_dim, per_kv = c->n_heads / c->n_kv_heads;
+    float* X = (float*)malloc((size_t)n * D * 4);
+    float* N = (float*)malloc((size_t)n * D * 4);
+    float* Q = (float*)malloc((size_t)n * qd * 4);
+    float* K = (float*)malloc((size_t)n * kvd * 4);
+    float* V = (float*)malloc((size_t)n * kvd * 4);
+    float* A = (float*)malloc((size_t)n * qd * 4);
+    float* P = (float*)malloc((size_t)n * D * 4);
+    float* L1 = (float*)malloc((size_t)n * Hd * 4);
+    float* L2 = (float*)malloc((size_t)n * Hd * 4);
+    if (!X || !N || !Q || !K || !V || !A || !P || !L1 || !L2) {
+        free(X); free(N); free(Q); free(K); free(V); free(A); free(P); free(L1); free(L2);
+        return Q3O_INVALID_ARGUMENT;
+    }
+    for (int t = 0; t < n; ++t) {
+        const uint16_t* row = m->embed + (size_t)tokens[t] * D;
+        for (int i = 0; i < D; ++i) X[(size_t)t * D + i] = bf2f(row[i]);
+    }
+    if (hidden_last) memcpy(hidden_last, X + (size_t)(n - 1) * D, (size_t)D * 4);
+    for (int l = 0; l < m->n_layers; ++l) {
+        q3o_block* b = m->blocks[l];
+        const uint16_t *attn_norm = b->w[0], *q_norm = b->w[1], *k_norm = b->w[2], *wq = b->w[3],
+                       *wk = b->w[4], *wv = b->w[5], *wo = b->w[6], *mlp_norm = b->w[7],
+                       *w1 = b->w[8], *w2 = b->w[9], *w3 = b->w[10];
+#pragma omp parallel for schedule(static)
+        for (int t = 0; t < n; ++t)
+            q3o_rmsnorm(N + (size_t)t * D, X + (size_t)t * D, attn_norm, c->norm_eps, D);
+        matmul_many(Q, qd, N, D, wq, qd, D, n);
+        matmul_many(K, kvd, N, D, wk, kvd, D, n);
+        matmul_many(V, kvd, N, D, wv, kvd, D, n);
+#pragma omp parallel for schedule(static)
+        for (int t = 0; t < n; ++t) {
+            float* q = Q + (size_t)t * qd;
+            float* k = K + (size_t)t * kvd;
+            const float* v = V + (size_t)t * kvd;
+            for (int h = 0; h < c->n_heads; ++h) q3o_rmsnorm(q + h * hd, q + h * hd, q_norm, c->norm_eps, hd);
+            for (int h = 0; h < c->n_kv_heads; ++h) q3o_rmsnorm(k + h * hd, k + h * hd, k_norm, c->norm_eps, hd);
+            q3o_rope(q, qd, hd, pos0 + t, c->rope_theta, c->rotary_dim);
+            q3o_rope(k, kvd, hd, pos0 + t, c->rope_theta, c->rotary_dim);
+            const size_t kv_pos = (size_t)(pos0 + t);
+            for (int i = 0; i < kvd; ++i) {
+                b->k_cache[kv_pos * kvd + i] = f2bf(k[i]);
+                b->v_cache[kv_pos * kvd + i] = f2bf(v[i]);
+            }
+        }
+#pragma omp parallel
+        {
+            float* sc = (float*)malloc((size_t)(pos0 + n) * 4);
+#pragma omp for schedule(dynamic) collapse(2)
+            for (int t = 0; t < n; ++t) {
+                for (int h = 0; h < c->n_heads; ++h) {
+                    const int g = h / per_kv;
+                    q3o_attn(A + (size_t)t * qd + h * hd, sc, Q + (size_t)t * qd + h * hd,
+                             b->k_cache + g * hd, b->v_cache + g * hd, hd, c->n_kv_heads, pos0 + t + 1);
+                }
+            }
+            free(sc);
+        }
+        matmul_many(P, D, A, qd, wo, D, qd, n);
+#pragma omp parallel for schedule(static)
+        for (int t = 0; t < n; ++t) {
+            float* x = X + (size_t)t * D;
+            const float* p = P + (size_t)t * D;
+            for (int i = 0; i < D; ++i) x[i] += p[i];
+            q3o_rmsnorm(N + (size_t)t * D, x, mlp_norm, c->norm_eps, D);
+        }
+        matmul_many(L1, Hd, N, D, w1, Hd, D, n);
+        matmul_many(L2, Hd, N, D, w3, Hd, D, n);
+#pragma omp parallel for schedule(static)
+        for (int t = 0; t < n; ++t)
+            for (int i = 0; i < Hd; ++i)
+                L1[(size_t)t * Hd + i] = q3o_silu(L1[(size_t)t * Hd + i]) * L2[(size_t)t * Hd + i];
+        matmul_many(P, D, L1, Hd, w2, D, Hd, n);
+#pragma omp parallel for schedule(static)
+        for (int t = 0; t < n; ++t) {
+            float* x = X + (size_t)t * D;
+            const float* p = P + (size_t)t * D;
+            for (int i = 0; i < D; ++i) x[i] += p[i];
+        }
+        if (hidden_last) memcpy(hidden_last + (size_t)(l + 1) * D, X + (size_t)(n - 1) * D, (size_t)D * 4);
+    }
+    /* Final RmsNorm and the tied lm_head of the flagged tokens, in chunks of 64 tokens. */
+    const int CH = 64;
+    float* lg = (float*)malloc((size_t)CH * m->vocab_size * 4);
+    int* idx = (int*)malloc((size_t)CH * sizeof(int));
+    size_t emitted = 0;
+    for (int t0 = 0; t0 < n && lg && idx; t0 += CH) {
+        int cnt = 0;
+        for (int t = t0; t < n && t < t0 + CH; ++t) {
+            if (argmax_out) argmax_out[t] = -1;
+            if (!want || want[t]) {
+                q3o_rmsnorm(N + (size_t)cnt * D, X + (size_t)t * D, m->final_norm, c->norm_eps, D);
+                idx[cnt++] = t;
+            }
+        }
+        if (!cnt) continue;
+        matmul_many(lg, m->vocab_size, N, D, m->embed, m->vocab_size, D, cnt);
+        for (int j = 0; j < cnt; ++j) {
+            const float* row = lg + (size_t)j * m->vocab_size;
+            if (argmax_out) argmax_out[idx[j]] = q3o_greedy(row, m->vocab_size);
+            if (logits_out) memcpy(logits_out + emitted * m->vocab_size, row, (size_t)m->vocab_size * 4);
+            ++emitted;
+        }
+    }
+    const int ok = lg && idx;
+    free(lg); free(idx);
+    free(X); free(N); free(Q); free(K); free(V); free(A); free(P); free(L1); free(L2);
+    return ok ? Q3O_OK : Q3O_INVALID_ARGUMENT;
 }
 
 int q3o_model_kv_row(q3o_model* m, int layer, int kv_pos, uint16_t* k, uint16_t* v) {

@@ -1,9 +1,10 @@
 """Batched decode of independent sequences (q3_batch_*) against the oracle.
 
 Each sequence of a batch must behave like the reference run on that sequence alone: its prompt's
-next token and logits, teacher-forced argmax agreement >= 99% (or every disagreement a near tie of
-the oracle's logits) with logits max-abs <= 5e-2, and
-KV rows (rel-L2 <= 1e-2) in its own pages. The device-driven greedy loop (CUDA graph) must agree
+next token and logits, teacher-forced argmax agreement >= 99% over every decode position of the
+batch (219 of them) with logits max-abs <= 5e-2, and KV rows (rel-L2 <= 1e-2) in its own pages; at
+short prompts and at prompts spanning the batched-decode configuration's context range (129 to
+3000 tokens). The device-driven greedy loop (CUDA graph) must agree
 with teacher-forced steps fed its own tokens, and capacity and range errors must be reported.
 """
 import numpy as np
@@ -19,7 +20,8 @@ TOP1_AGREEMENT = 0.99
 REL_L2 = 1e-2
 
 PROMPT_LENS = (40, 130, 75)
-STEPS = 24
+LONG_PROMPT_LENS = (129, 1100, 3000)
+STEPS = 72
 
 
 def rel_l2(a, b):
@@ -28,29 +30,35 @@ def rel_l2(a, b):
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
 
+def make_seqs(lens, seed):
+    rng = np.random.default_rng(seed)
+    return [(rng.integers(0, 151936, n).astype(np.int32),
+             rng.integers(0, 151936, STEPS).astype(np.int32)) for n in lens]
+
+
+def run_oracle(weights, seqs, ctx):
+    """Per sequence, from the oracle run on that sequence alone: argmax and logits after the last
+    prompt token and every continuation token, and a few KV rows."""
+    out = []
+    for prompt, cont in seqs:
+        cpu = oracle.PortModel(weights, ctx)
+        full = np.concatenate([prompt, cont])
+        want = np.zeros(full.size, bool)
+        want[len(prompt) - 1:] = True
+        r = cpu.forward_many(full, 0, want=want, logits=True)
+        kv = {(l, p): cpu.kv_row(l, p) for l in (0, 27) for p in (0, len(prompt) - 1, len(full) - 1)}
+        out.append((r["argmax"][len(prompt) - 1:], r["logits"], kv))
+    return out
+
+
 @pytest.fixture(scope="module")
 def seqs():
-    rng = np.random.default_rng(31)
-    return [(rng.integers(0, 151936, n).astype(np.int32),
-             rng.integers(0, 151936, STEPS).astype(np.int32)) for n in PROMPT_LENS]
+    return make_seqs(PROMPT_LENS, 31)
 
 
 @pytest.fixture(scope="module")
 def oracle_runs(full_weights, seqs):
-    """Per sequence: argmax and logits after every position of prompt + continuation, and a few
-    KV rows, from the oracle run on that sequence alone."""
-    out = []
-    for prompt, cont in seqs:
-        cpu = oracle.PortModel(full_weights, 512)
-        full = np.concatenate([prompt, cont])
-        am, lgs = [], []
-        for pos, t in enumerate(full):
-            lg = cpu.forward(int(t), pos)
-            am.append(int(np.argmax(lg)))
-            lgs.append(lg)
-        kv = {(l, p): cpu.kv_row(l, p) for l in (0, 27) for p in (0, len(prompt) - 1, len(full) - 1)}
-        out.append((np.array(am), np.stack(lgs), kv))
-    return out
+    return run_oracle(full_weights, seqs, 512)
 
 
 @pytest.fixture(scope="module")
@@ -60,36 +68,52 @@ def model(q3lib, full_weights):
     m.close()
 
 
-def test_batch_matches_oracle(q3lib, model, seqs, oracle_runs):
-    batch = q3lib.Batch(model, 4, 512)
+def check_batch(q3lib, model, seqs, runs, max_tokens, what):
+    batch = q3lib.Batch(model, 4, max_tokens)
     try:
+        firsts = []
         for i, (prompt, _) in enumerate(seqs):
             slot, nxt, lg = batch.add(prompt, want_logits=True)
-            am, lgs, _ = oracle_runs[i]
+            am, lgs, _ = runs[i]
             assert slot == i
-            assert nxt == am[len(prompt) - 1]
-            assert np.abs(lg - lgs[len(prompt) - 1]).max() <= LOGITS_MAX_ABS
+            firsts.append(nxt)
+            assert np.abs(lg - lgs[0]).max() <= LOGITS_MAX_ABS
         forced = np.stack([cont for _, cont in seqs], axis=1)  # [steps, seqs]
         am, lg = batch.decode_forced(forced, want_logits=True)
-        for i, (prompt, cont) in enumerate(seqs):
-            ref_am, ref_lg, kv = oracle_runs[i]
-            n = len(prompt)
-            ours, ref = am[:, i], ref_am[n:n + STEPS]
-            agree = float((ours == ref).mean())
-            # A disagreement is a near tie of the oracle's logits when the gap between its top-1
-            # and ours is within twice the logits tolerance (each may be off by up to it); the
-            # split-K sums of the contractions make such flips vary from run to run.
-            steps = np.nonzero(ours != ref)[0]
-            gaps = [float(ref_lg[n + s, ref[s]] - ref_lg[n + s, ours[s]]) for s in steps]
-            assert agree >= TOP1_AGREEMENT or max(gaps) <= 2 * LOGITS_MAX_ABS, (i, agree, gaps)
-            assert np.abs(lg[:, i] - ref_lg[n:n + STEPS]).max() <= LOGITS_MAX_ABS
-            f = gen_weights.bf16_bits_to_f32
-            for (l, p), (ko, vo) in kv.items():
+        ours = np.concatenate([np.array(firsts)[None, :], am], axis=0)
+        ref = np.stack([r[0] for r in runs], axis=1)
+        agree = float((ours == ref).mean())
+        err = max(float(np.abs(lg[:, i] - runs[i][1][1:STEPS + 1]).max()) for i in range(len(seqs)))
+        f = gen_weights.bf16_bits_to_f32
+        worst = 0.0
+        for i in range(len(seqs)):
+            for (l, p), (ko, vo) in runs[i][2].items():
                 k, v = batch.kv_row(i, l, p)
-                assert rel_l2(f(k), f(ko)) <= REL_L2, ("k", i, l, p)
-                assert rel_l2(f(v), f(vo)) <= REL_L2, ("v", i, l, p)
+                e = max(rel_l2(f(k), f(ko)), rel_l2(f(v), f(vo)))
+                worst = max(worst, e)
+                assert e <= REL_L2, (what, i, l, p, e)
+        print(f"\n[parity] batch ({what}): positions={ours.size}, agree={agree}, "
+              f"flips={int((ours != ref).sum())}, logits_max_abs={err}, kv_rel_l2={worst}")
+        assert agree >= TOP1_AGREEMENT, (what, agree)
+        assert err <= LOGITS_MAX_ABS, (what, err)
     finally:
         batch.close()
+
+
+def test_batch_matches_oracle(q3lib, model, seqs, oracle_runs):
+    check_batch(q3lib, model, seqs, oracle_runs, 512, "short prompts")
+
+
+def test_batch_long_contexts_match_oracle(q3lib, full_weights):
+    """Prompts across the batched-decode configuration's context range, 16-token pages."""
+    seqs = make_seqs(LONG_PROMPT_LENS, 33)
+    ctx = max(LONG_PROMPT_LENS) + STEPS + 1
+    runs = run_oracle(full_weights, seqs, ctx)
+    m = q3lib.Qwen3(full_weights, ctx)
+    try:
+        check_batch(q3lib, m, seqs, runs, ctx, "prompts 129-3000")
+    finally:
+        m.close()
 
 
 def test_graph_loop_matches_forced_steps(q3lib, model, seqs):

@@ -1,0 +1,184 @@
+"""Long-context and ring-wrap parity of the decode paths against the oracle.
+
+* The long-prompt configuration (2048 seeded prompt IDs, seed 2, context 4096, 256 decode steps):
+  the fused whole-step kernel teacher-forced through all 2304 positions (its short-context ring
+  attention up to 128 cached positions, its split-K attention past them), and the batched
+  tensor-core prefill of the prompt followed by 256 teacher-forced decode steps on both decode
+  paths. Top-1 agreement >= 99% at every teacher-forced position, logits max-abs <= 5e-2, the
+  per-layer hidden states of the last position rel-L2 <= 1e-2, KV rows at the page and
+  attention-mode boundaries.
+* The ring buffer at the Qwen3-0.6B shape: context 64 driven to position 223 (sink rows
+  re-rotated, slots reused) on both decode paths, logits and top-1 at every position, hidden
+  states of the last one, and every cache slot of three layers.
+
+The oracle (the C restatement, bit-exact with the reference) runs the long prompt layer by layer
+over all tokens (PortModel.forward_many, bit-identical to token-by-token ForwardToken calls).
+"""
+import numpy as np
+import pytest
+
+import gen_weights
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+HIDDEN_REL_L2 = 1e-2   # per-layer hidden states
+LOGITS_MAX_ABS = 5e-2  # final logits
+TOP1_AGREEMENT = 0.99  # teacher-forced greedy tokens
+KV_REL_L2 = 1e-2
+
+LONG_CTX, LONG_PROMPT, LONG_STEPS = 4096, 2048, 256
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def report(name, **kv):
+    print(f"\n[parity] {name}: " + ", ".join(f"{k}={v}" for k, v in kv.items()))
+
+
+@pytest.fixture(scope="module")
+def long_case(full_weights):
+    """Prompt (seed 2, the long-prompt configuration), a seeded teacher-forced continuation, and
+    the oracle's argmax at every position, logits at the continuation's positions, the hidden
+    states of one further position and KV rows."""
+    prompt = np.random.default_rng(2).integers(0, 151936, LONG_PROMPT).astype(np.int32)
+    cont = np.random.default_rng(102).integers(0, 151936, LONG_STEPS + 1).astype(np.int32)
+    cpu = oracle.PortModel(full_weights, LONG_CTX)
+    head = cpu.forward_many(prompt, 0)
+    tail = cpu.forward_many(cont[:LONG_STEPS], LONG_PROMPT, logits=True)
+    last = LONG_PROMPT + LONG_STEPS
+    hid, last_lg = cpu.forward(int(cont[LONG_STEPS]), last, layers=True)
+    kv = {(l, p): cpu.kv_row(l, p) for l in (0, 27)
+          for p in (0, 15, 16, 127, 128, 1000, LONG_PROMPT - 1, LONG_PROMPT, last)}
+    return dict(prompt=prompt, cont=cont, am=np.concatenate([head["argmax"], tail["argmax"]]),
+                lg=tail["logits"], hid=hid, last_lg=last_lg, kv=kv)
+
+
+def _check_kv(m, kv, what):
+    f = gen_weights.bf16_bits_to_f32
+    worst = 0.0
+    for (l, p), (ko, vo) in kv.items():
+        k, v = m.kv_row(l, p)
+        e = max(rel_l2(f(k), f(ko)), rel_l2(f(v), f(vo)))
+        worst = max(worst, e)
+        assert e <= KV_REL_L2, (what, l, p, e)
+    return worst
+
+
+def _check_last(m, case, what):
+    """One more ForwardToken with per-layer taps at the position after the continuation."""
+    last = LONG_PROMPT + LONG_STEPS
+    h, lg = m.forward_token_layers(int(case["cont"][LONG_STEPS]), last)
+    worst = max(rel_l2(h[l], case["hid"][l]) for l in range(h.shape[0]))
+    assert worst <= HIDDEN_REL_L2, (what, worst)
+    assert np.abs(lg - case["last_lg"]).max() <= LOGITS_MAX_ABS, what
+    return worst
+
+
+def test_fused_long_prompt_teacher_forced(q3lib, full_weights, long_case):
+    """The fused kernel on every position of the long prompt and its continuation."""
+    c = long_case
+    m = q3lib.Qwen3(full_weights, LONG_CTX)
+    try:
+        assert m.decode_path == m.PATH_FUSED
+        am_p, _ = m.decode_forced(c["prompt"], 0)
+        am_c, lg = m.decode_forced(c["cont"][:LONG_STEPS], LONG_PROMPT, want_logits=True)
+        am = np.concatenate([am_p, am_c])
+        agree = float((am == c["am"]).mean())
+        err = float(np.abs(lg - c["lg"]).max())
+        hid = _check_last(m, c, "fused")
+        kv = _check_kv(m, c["kv"], "fused")
+        report("fused long prompt", positions=am.size, agree=agree,
+               flips=int((am != c["am"]).sum()), logits_max_abs=err, hidden_rel_l2=hid,
+               kv_rel_l2=kv)
+        assert agree >= TOP1_AGREEMENT, agree
+        assert err <= LOGITS_MAX_ABS, err
+    finally:
+        m.close()
+
+
+@pytest.mark.parametrize("path", ["fused", "layerwise"])
+def test_batched_prefill_then_decode_long(q3lib, full_weights, long_case, path):
+    """The tensor-core prefill of the 2048-token prompt, then 256 teacher-forced decode steps
+    reading the cache it wrote."""
+    c = long_case
+    m = q3lib.Qwen3(full_weights, LONG_CTX)
+    try:
+        assert m.prefill_path == m.PREFILL_BATCHED
+        m.decode_path = m.PATH_FUSED if path == "fused" else m.PATH_LAYERWISE
+        _, nxt = m.prefill(c["prompt"], 0, want_logits=False)
+        am, lg = m.decode_forced(c["cont"][:LONG_STEPS], LONG_PROMPT, want_logits=True)
+        ours = np.concatenate([[nxt], am])
+        ref = c["am"][LONG_PROMPT - 1:]
+        agree = float((ours == ref).mean())
+        err = float(np.abs(lg - c["lg"]).max())
+        hid = _check_last(m, c, path)
+        kv = _check_kv(m, c["kv"], path)
+        report(f"batched prefill + {path} decode", positions=ours.size, agree=agree,
+               flips=int((ours != ref).sum()), logits_max_abs=err, hidden_rel_l2=hid,
+               kv_rel_l2=kv)
+        assert agree >= TOP1_AGREEMENT, agree
+        assert err <= LOGITS_MAX_ABS, err
+    finally:
+        m.close()
+
+
+WRAP_CTX, WRAP_POSITIONS = 64, 224
+
+
+@pytest.fixture(scope="module")
+def wrap_case(full_weights):
+    """The oracle driven through a context-64 ring buffer at the Qwen3-0.6B shape: logits at
+    every position, hidden states of the last, every cache slot of three layers."""
+    toks = np.random.default_rng(77).integers(0, 151936, WRAP_POSITIONS).astype(np.int32)
+    cpu = oracle.PortModel(full_weights, WRAP_CTX)
+    lgs = [cpu.forward(int(t), pos) for pos, t in enumerate(toks[:-1])]
+    hid, lg = cpu.forward(int(toks[-1]), WRAP_POSITIONS - 1, layers=True)
+    lgs.append(lg)
+    slots = {(l, s): cpu.kv_row(l, s) for l in (0, 13, 27) for s in range(WRAP_CTX)}
+    return toks, np.stack(lgs), hid, slots
+
+
+@pytest.mark.parametrize("path", ["fused", "layerwise"])
+def test_ring_wrap_qwen3_shape(q3lib, full_weights, wrap_case, path):
+    """Position math past the context (num_sink, kv_pos, kv_len), sink re-rotation and slot
+    reuse of the decode paths at the Qwen3-0.6B shape against the oracle."""
+    toks, lgs, hid, slots = wrap_case
+    m = q3lib.Qwen3(full_weights, WRAP_CTX)
+    try:
+        m.decode_path = m.PATH_FUSED if path == "fused" else m.PATH_LAYERWISE
+        am, lg = m.decode_forced(toks[:-1], 0, want_logits=True)
+        h, lg_last = m.forward_token_layers(int(toks[-1]), WRAP_POSITIONS - 1)
+        lg = np.concatenate([lg, lg_last[None]])
+        am = np.concatenate([am, [int(np.argmax(lg_last))]])
+        ref = lgs.argmax(axis=1)
+        agree = float((am == ref).mean())
+        err = float(np.abs(lg - lgs).max())
+        worst_h = max(rel_l2(h[l], hid[l]) for l in range(h.shape[0]))
+        f = gen_weights.bf16_bits_to_f32
+        worst_kv = 0.0
+        for (l, s), (ko, vo) in slots.items():
+            k, v = m.kv_row(l, s)
+            if l == 0:
+                # First layer: one bf16 rounding step apart at most (a different fp32 summation
+                # order can move a value across a rounding boundary).
+                for a, b in ((k, ko), (v, vo)):
+                    fa, fb = f(a), f(b)
+                    rms = float(np.sqrt(np.mean(fb.astype(np.float64) ** 2)))
+                    tol = 2.0 ** -7 * np.abs(fb) + 1e-3 * rms
+                    assert np.all(np.abs(fa - fb) <= tol), (path, l, s)
+            e = max(rel_l2(f(k), f(ko)), rel_l2(f(v), f(vo)))
+            worst_kv = max(worst_kv, e)
+            assert e <= KV_REL_L2, (path, l, s, e)
+        report(f"ring wrap ({path})", positions=am.size, agree=agree,
+               flips=int((am != ref).sum()), logits_max_abs=err, hidden_rel_l2=worst_h,
+               kv_rel_l2=worst_kv)
+        assert agree >= TOP1_AGREEMENT, agree
+        assert err <= LOGITS_MAX_ABS, err
+        assert worst_h <= HIDDEN_REL_L2, worst_h
+    finally:
+        m.close()

@@ -4,7 +4,8 @@
   operands, for every epilogue, at the prefill shapes and ragged row counts.
 * The whole batched prefill against the oracle: per-layer hidden state of the last prompt token
   rel-L2 <= 1e-2, its logits max-abs <= 5e-2, KV rows rel-L2 <= 1e-2, and teacher-forced top-1
-  agreement >= 99% for decode steps that read the batched cache.
+  agreement >= 99% for decode steps that read the batched cache (224 positions per decode path)
+  and for Generate (200 generated tokens).
 """
 import numpy as np
 import pytest
@@ -138,15 +139,15 @@ def test_batched_prefill_matches_oracle(q3lib, full_weights, prompt100, oracle_p
 
 
 def test_decode_after_batched_prefill(q3lib, full_weights):
-    """Teacher-forced decode over the cache a batched prefill wrote."""
+    """Teacher-forced decode (224 positions per decode path) over the cache a batched prefill
+    wrote."""
     rng = np.random.default_rng(0)
-    seq = rng.integers(0, 151936, 80).astype(np.int32)
+    seq = rng.integers(0, 151936, 256).astype(np.int32)
     cpu = oracle.PortModel(full_weights, 512)
-    ref_am, ref_lg = [], []
-    for pos, t in enumerate(seq):
-        lg = cpu.forward(int(t), pos)
-        ref_am.append(int(np.argmax(lg)))
-        ref_lg.append(lg)
+    want = np.zeros(seq.size, bool)
+    want[31:] = True
+    r = cpu.forward_many(seq, 0, want=want, logits=True)
+    ref_am, ref_lg = r["argmax"][31:], r["logits"]
     m = q3lib.Qwen3(full_weights, 512)
     try:
         for path in (m.PATH_FUSED, m.PATH_LAYERWISE):
@@ -154,9 +155,13 @@ def test_decode_after_batched_prefill(q3lib, full_weights):
             m.reset()
             _, nxt = m.prefill(seq[:32], 0)
             am, lg = m.decode_forced(seq[32:], 32, want_logits=True)
-            agree = float((am == np.array(ref_am[32:])).mean())
+            ours = np.concatenate([[nxt], am])
+            agree = float((ours == ref_am).mean())
+            err = float(np.abs(lg - ref_lg[1:]).max())
+            print(f"\n[parity] decode after batched prefill (path {path}): positions={ours.size}, "
+                  f"agree={agree}, flips={int((ours != ref_am).sum())}, logits_max_abs={err}")
             assert agree >= TOP1_AGREEMENT, (path, agree)
-            assert np.abs(lg - np.stack(ref_lg[32:])).max() <= LOGITS_MAX_ABS
+            assert err <= LOGITS_MAX_ABS, (path, err)
     finally:
         m.close()
 
@@ -202,25 +207,21 @@ def test_prompt_past_context_falls_back(q3lib, full_weights):
 
 
 def test_generate_with_batched_prefill(q3lib, full_weights):
-    """Generate's tokens, each checked against the oracle's argmax given the same history."""
+    """Generate's 200 tokens, each checked against the oracle's argmax given the same history."""
     rng = np.random.default_rng(21)
     prompt = rng.integers(0, 151936, 48).astype(np.int32)
     m = q3lib.Qwen3(full_weights, 512)
     try:
-        toks, st = m.generate(prompt, 24, stop_on_eos=False)
+        toks, st = m.generate(prompt, 200, stop_on_eos=False)
     finally:
         m.close()
-    assert st["prompt_tokens"] == 48 and st["generated_tokens"] == 24
-    cpu = oracle.PortModel(full_weights, 512)
-    seq = list(prompt) + list(toks)
-    agree, gaps = 0, [0.0]
-    for pos in range(len(seq) - 1):
-        lg = cpu.forward(int(seq[pos]), pos)
-        if pos >= len(prompt) - 1:
-            nxt = int(seq[pos + 1])
-            agree += int(np.argmax(lg)) == nxt
-            # A disagreement is a near tie when the oracle's top-1 logit beats the generated
-            # token's by no more than two logit tolerances (the split-K sums vary in their last
-            # bits from run to run, so either side of such a tie is within tolerance).
-            gaps.append(float(lg.max() - lg[nxt]))
-    assert agree / len(toks) >= TOP1_AGREEMENT or max(gaps) <= 2 * LOGITS_MAX_ABS, (agree, gaps)
+    assert st["prompt_tokens"] == 48 and st["generated_tokens"] == 200
+    seq = np.concatenate([prompt, toks]).astype(np.int32)
+    want = np.zeros(seq.size, bool)
+    want[len(prompt) - 1:-1] = True
+    ref = oracle.PortModel(full_weights, 512).forward_many(seq[:-1], 0, want=want[:-1])["argmax"]
+    ref = ref[len(prompt) - 1:]
+    agree = float((ref == toks).mean())
+    print(f"\n[parity] generate after batched prefill: positions={toks.size}, agree={agree}, "
+          f"flips={int((ref != toks).sum())}")
+    assert agree >= TOP1_AGREEMENT, agree

@@ -157,3 +157,34 @@ def test_port_rejects_bad_ranges():
         with pytest.raises(oracle.OracleError) as e:
             b.forward(x, *args)
         assert e.value.code == 3
+
+
+def test_port_forward_many_is_tokenwise_bit_exact(tmp_path):
+    """The layer-by-layer many-token oracle (used for long prompts) equals token-by-token
+    ForwardToken calls bit for bit: logits, argmax, per-layer hidden states of the last token,
+    KV rows, and a token-wise step afterwards; and rejects a range that would wrap the ring."""
+    cfg = dict(gen_weights.QWEN3_0_6B, n_layers=2, vocab_size=4096)
+    path = gen_weights.write_model(tmp_path / "m.bin", cfg, seed=3)
+    toks = np.random.default_rng(1).integers(0, 4096, 71).astype(np.int32)
+    a, b = oracle.PortModel(path, 128), oracle.PortModel(path, 128)
+    for pos in range(10):
+        a.forward(int(toks[pos]), pos)
+        b.forward(int(toks[pos]), pos)
+    lgs = []
+    for pos in range(10, 71):
+        h, lg = a.forward(int(toks[pos]), pos, layers=True)
+        lgs.append(lg)
+    want = np.ones(61, bool)
+    want[5:20] = False
+    r = b.forward_many(toks[10:], 10, want=want, logits=True, layers=True)
+    np.testing.assert_array_equal(r["logits"], np.stack(lgs)[want])
+    assert np.array_equal(r["argmax"][want], np.stack(lgs)[want].argmax(axis=1))
+    assert np.all(r["argmax"][~want] == -1)
+    np.testing.assert_array_equal(r["hidden_last"], h)
+    for l in range(2):
+        for s in (0, 9, 10, 42, 70):
+            for x, y in zip(a.kv_row(l, s), b.kv_row(l, s)):
+                np.testing.assert_array_equal(x, y)
+    np.testing.assert_array_equal(a.forward(5, 71), b.forward(5, 71))
+    with pytest.raises(oracle.OracleError):
+        b.forward_many(toks[:60], 100)
