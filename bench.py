@@ -186,14 +186,23 @@ class Clocks:
 
 # ------------------------------------------------------------------ reference arm / CPU baseline
 
+def ref_build() -> tuple[bool, str]:
+    """Which build of the reference engine this host times: its -march=native build for the GPU
+    hosts' CPU when this CPU has those instructions, else the portable AVX2 build."""
+    import oracle
+    native = oracle.REF_NATIVE_LIB.exists() and oracle.host_runs_native_build()
+    return native, ("-O3 -march=sapphirerapids (the reference's -march=native on this host's "
+                    "CPU)" if native else "-O3 -mavx2 -mfma (portable)")
+
+
 def reference_decode(model_path: str, steps: int, warmup: int, threads: int,
-                     with_prefill: bool = False):
+                     with_prefill: bool = False, native: bool = False):
     """The reference engine (oracle/_ref, built from the reference sources) on the host cores:
     prefill of the 16-token prompt, then greedy steps (Qwen3::Generate's loops with
     `--benchmark` semantics), timed with its steady_clock marks. Returns (tok/s, decode s), plus
     its prefill tok/s when with_prefill."""
     import oracle
-    m = oracle.RefModel(model_path, CTX)
+    m = oracle.RefModel(model_path, CTX, native=native)
     p = prompt_ids()
     if warmup:
         m.generate_ids(p, min(warmup, RUN_STEPS))
@@ -210,6 +219,54 @@ def reference_decode(model_path: str, steps: int, warmup: int, threads: int,
     return steps / secs, secs
 
 
+def reference_positions(m, positions) -> float:
+    """Mean seconds of one Qwen3::ForwardToken call of the reference engine at each of the given
+    positions (one call each after a warm-up call). The reference prefills and decodes one
+    ForwardToken per token; a call's cost depends on its position (attention over kv_len =
+    pos + 1 cached rows, src/inference.cpp:1017-1058) and not on what the cache holds, so calls
+    at positions spread over a workload sample its per-token cost without replaying the tokens
+    before them."""
+    m.forward(1, int(positions[0]))
+    t0 = time.perf_counter()
+    for i, pos in enumerate(positions):
+        m.forward((7919 * i) % VOCAB, int(pos))
+    return (time.perf_counter() - t0) / len(positions)
+
+
+def cpu_baselines(model_path: str, threads: int) -> dict:
+    """The reference engine on the host cores for the long-prompt, batched and tensor-parallel
+    configurations, each on a bounded sample (about a second of CPU work or less each)."""
+    import oracle
+    native, build = ref_build()
+    # One engine at the largest context serves every sample (below the context the positions'
+    # costs do not depend on it).
+    m = oracle.RefModel(model_path, TP_CTX, native=native)
+    out = {}
+    pre_pos = [int((i + 0.5) * PREFILL_LEN / 16) for i in range(16)]
+    s = reference_positions(m, pre_pos)
+    out["prefill"] = {"value": round(1.0 / s, 3), "unit": "tok/s", "cores": threads,
+                      "kind": "reference", "build": build,
+                      "sample": "16 ForwardToken calls at positions spread uniformly over the "
+                                f"{PREFILL_LEN}-token prompt (positions {pre_pos[0]}..{pre_pos[-1]}); "
+                                "the reference prefills one token per call"}
+    lens, _ = dp_workload(DP_SEQS)
+    pick = list(range(0, DP_SEQS, 8))
+    dp_pos = [int(lens[i]) + DP_WARMUP + DP_STEPS // 2 for i in pick]
+    s = reference_positions(m, dp_pos)
+    out["dp_decode"] = {"value": round(1.0 / s, 3), "unit": "tok/s", "cores": threads,
+                        "kind": "reference", "build": build,
+                        "sample": f"ForwardToken of sequences {pick[0]}, {pick[1]}, ..., "
+                                  f"{pick[-1]} of the 64 at the middle of their 128 decode steps "
+                                  "(the reference serves one sequence at a time)"}
+    tp_pos = [TP_PROMPT + TP_WARMUP + TP_STEPS // 2 + k for k in range(3)]
+    s = reference_positions(m, tp_pos)
+    out["tp_decode"] = {"value": round(1.0 / s, 3), "unit": "tok/s", "cores": threads,
+                        "kind": "reference", "build": build,
+                        "sample": f"3 ForwardToken calls at positions {tp_pos[0]}..{tp_pos[-1]}, "
+                                  "the middle of the 128 decode steps"}
+    return out
+
+
 def run_reference_arm(args):
     world, rank, _ = dist_info()
     if rank != 0:
@@ -217,7 +274,8 @@ def run_reference_arm(args):
     import gen_weights
     threads = os.cpu_count() or 1
     path = gen_weights.cached_model(0)
-    tps, secs = reference_decode(str(path), args.steps, args.warmup, threads)
+    native, build = ref_build()
+    tps, secs = reference_decode(str(path), args.steps, args.warmup, threads, native=native)
     line = {
         "impl": "reference", "metric": METRIC, "value": round(tps, 3), "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -225,9 +283,9 @@ def run_reference_arm(args):
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": "Qwen3-0.6B B=1 greedy decode, ctx 512, 16-token prompt, "
                                "64-step runs (reference CPU engine)",
-                   "threads": threads},
+                   "threads": threads, "build": build},
         "cpu_baseline": {"value": round(tps, 3), "unit": UNIT, "cores": threads,
-                         "kind": "reference",
+                         "kind": "reference", "build": build,
                          "sample": f"{args.steps} greedy decode steps in runs of {RUN_STEPS} after "
                                    f"a {PROMPT_LEN}-token prefill, OMP_NUM_THREADS={threads}"},
         "e2e": {"value": round(tps, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
@@ -436,15 +494,19 @@ def run_b200_arm(args):
 
     cpu = None
     cpu_prefill = None
-    if rank == 0 and world == 1 and dec and q3_ref_available():
+    cpu_legs = {}
+    if rank == 0 and world == 1 and q3_ref_available():
         threads = os.cpu_count() or 1
-        tps, _, pre_tps = reference_decode(str(path), RUN_STEPS, 0, threads, with_prefill=True)
-        cpu = {"value": round(tps, 3), "unit": UNIT, "cores": threads, "kind": "reference",
-               "sample": f"{RUN_STEPS} greedy decode steps after a {PROMPT_LEN}-token prefill, "
-                         f"ctx {CTX}, OMP_NUM_THREADS={threads}"}
-        cpu_prefill = {"value": round(pre_tps, 3), "unit": "tok/s", "cores": threads,
-                       "kind": "reference",
-                       "sample": f"its token-by-token prefill of the {PROMPT_LEN}-token prompt"}
+        native, build = ref_build()
+        if dec:
+            tps, _ = reference_decode(str(path), RUN_STEPS, 0, threads, native=native)
+            cpu = {"value": round(tps, 3), "unit": UNIT, "cores": threads, "kind": "reference",
+                   "build": build,
+                   "sample": f"{RUN_STEPS} greedy decode steps after a {PROMPT_LEN}-token "
+                             f"prefill, ctx {CTX}, OMP_NUM_THREADS={threads}"}
+        if legs & {"prefill", "dp", "tp"}:
+            cpu_legs = cpu_baselines(str(path), threads)
+        cpu_prefill = cpu_legs.get("prefill")
     p_tps = world * PREFILL_LEN / (p_ms / 1e3) if p_ms else 0.0
     p_tflops = prefill_flops(PREFILL_LEN) / (p_ms / 1e3) / 1e12 if p_ms else 0.0
 
@@ -485,6 +547,7 @@ def run_b200_arm(args):
                 "sequences": args.dp_seqs,
                 "steps": DP_STEPS, "ms_per_step": round(dp_ms / DP_STEPS, 4),
                 "seqs_per_gpu": len(mine), "scaling": "strong",
+                "cpu_baseline": cpu_legs.get("dp_decode"),
                 "roofline": {"bound": "hbm", "achieved": round(dp_gbs, 1),
                              "peak": pk["hbm_gbs"], "unit": "GB/s",
                              "frac": round(dp_gbs / pk["hbm_gbs"], 4),
@@ -496,7 +559,9 @@ def run_b200_arm(args):
                 "value": round(TP_STEPS / max(tp_ms / 1e3, 1e-12), 1), "unit": "tok/s",
                 "steps": TP_STEPS, "ms_per_step": round(tp_ms / TP_STEPS, 4),
                 "parallelism": f"tp{world}", "scaling": "strong",
-                "collective": "one-shot all-reduce over NVLink peer memory (library kernel)",
+                "cpu_baseline": cpu_legs.get("tp_decode"),
+                "collective": "this library's own one-shot all-reduce kernel over NVLink peer "
+                              "memory (CUDA IPC handles), not NCCL",
                 "roofline": {"bound": "hbm", "achieved": round(tp_gbs, 1),
                              "peak": pk["hbm_gbs"], "unit": "GB/s per GPU",
                              "frac": round(tp_gbs / pk["hbm_gbs"], 4),

@@ -236,6 +236,14 @@ q3_status q3_tp_decode(q3_tp* tp, int32_t first_token, int pos0, int n_steps,
 /* Teacher-forced: feeds tokens_host[i] at pos0 + i; argmax_host[n] receives each step's argmax. */
 q3_status q3_tp_decode_forced(q3_tp* tp, const int32_t* tokens_host, int n, int pos0,
                               int32_t* argmax_host);
+/* solo_allreduce != 0: at world 1, the o_proj / down_proj partials go through the all-reduce
+ * kernel with this rank as its only member (default: added into the residual directly).
+ * wait_cycles: budget in SM clock cycles of every bounded flag wait (default 4e9, ~2 s). Every
+ * rank of a group configures alike. A wait that runs out makes decode return
+ * Q3_ERR_DEVICE_TIMEOUT; the decoder then refuses to decode (Q3_ERR_RUNTIME) until
+ * q3_tp_reset, which every rank calls (and the ranks meet on the host) before decoding again. */
+q3_status q3_tp_configure(q3_tp* tp, int solo_allreduce, long long wait_cycles);
+q3_status q3_tp_reset(q3_tp* tp);
 
 /* ------------------------------------------------------------------ one block (class Block) */
 

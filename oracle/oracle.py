@@ -28,7 +28,29 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 PORT_LIB = HERE / "_build" / "libq3oracle.so"
 REF_LIB = HERE / "_ref" / "libq3ref.so"
-REFERENCE_TREE = Path("/root/reference")
+# The same sources built with the reference's -march=native resolved for the GPU hosts' CPU
+# (-march=sapphirerapids); used for CPU timing where this host's CPU has those instructions.
+REF_NATIVE_LIB = HERE / "_ref" / "libq3ref_spr.so"
+NATIVE_FLAGS = ("avx512f", "avx512bw", "avx512vl", "avx512dq", "avx512cd", "avx512ifma",
+                "avx512vbmi", "avx512_vbmi2", "avx512_vnni", "avx512_bitalg", "avx512_vpopcntdq",
+                "avx512_bf16", "avx512_fp16", "avx_vnni", "amx_tile", "amx_bf16", "amx_int8")
+
+
+def host_runs_native_build() -> bool:
+    """True when this host's CPU has the instruction sets -march=sapphirerapids may use."""
+    try:
+        text = Path("/proc/cpuinfo").read_text()
+    except OSError:
+        return False
+    flags = set()
+    for line in text.splitlines():
+        if line.startswith("flags"):
+            flags = set(line.split(":", 1)[1].split())
+            break
+    return all(f in flags for f in NATIVE_FLAGS)
+# The reference source tree (asriva32/Qwen3.cpp), when this machine has one: Q3_REFERENCE_TREE.
+REFERENCE_TREE = (Path(os.environ["Q3_REFERENCE_TREE"]) if os.environ.get("Q3_REFERENCE_TREE")
+                  else None)
 
 _lock = threading.Lock()
 
@@ -176,18 +198,18 @@ def build_port() -> Path:
 def build_ref() -> Path | None:
     """Build oracle/_ref from the reference tree when it exists; else use a prebuilt copy."""
     with _lock:
-        if REFERENCE_TREE.exists():
+        if REFERENCE_TREE is not None and REFERENCE_TREE.exists():
             subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF={REFERENCE_TREE}"],
                            check=True)
     return REF_LIB if REF_LIB.exists() else None
 
 
 def ref_available() -> bool:
-    return REF_LIB.exists() or REFERENCE_TREE.exists()
+    return REF_LIB.exists() or (REFERENCE_TREE is not None and REFERENCE_TREE.exists())
 
 
 _port = None
-_ref = None
+_ref = {}
 F32P = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 U16P = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
 
@@ -236,10 +258,13 @@ def port_lib():
     return _port
 
 
-def ref_lib():
-    global _ref
-    if _ref is None:
+def ref_lib(native: bool = False):
+    """The reference engine library; native=True: its -march=native build for the GPU hosts'
+    CPU (callers check host_runs_native_build() first)."""
+    if native not in _ref:
         path = build_ref()
+        if native:
+            path = REF_NATIVE_LIB if REF_NATIVE_LIB.exists() else None
         if path is None:
             raise FileNotFoundError("oracle/_ref/libq3ref.so is not built")
         lib = C.CDLL(str(path))
@@ -273,8 +298,8 @@ def ref_lib():
         lib.q3ref_fastattn.argtypes = [F32P, F32P, F32P, C.c_void_p, C.c_void_p, C.c_int,
                                        C.c_int, C.c_int]
         lib.q3ref_greedy.argtypes = [F32P, C.c_int, C.POINTER(C.c_int)]
-        _ref = lib
-    return _ref
+        _ref[native] = lib
+    return _ref[native]
 
 
 class OracleError(Exception):
@@ -388,8 +413,8 @@ class RefModel:
 
     kind = "reference"
 
-    def __init__(self, path, ctx: int = 512):
-        lib = ref_lib()
+    def __init__(self, path, ctx: int = 512, native: bool = False):
+        lib = self._lib = ref_lib(native)
         h = C.c_void_p()
         _check_ref(lib.q3ref_load(str(path).encode(), ctx, C.byref(h)))
         self._h = h
@@ -405,24 +430,24 @@ class RefModel:
 
     def __del__(self):
         if getattr(self, "_h", None):
-            ref_lib().q3ref_free(self._h)
+            self._lib.q3ref_free(self._h)
             self._h = None
 
     def tensor_count(self) -> int:
-        return ref_lib().q3ref_tensor_count(self._h)
+        return self._lib.q3ref_tensor_count(self._h)
 
     def reset(self):
-        _check_ref(ref_lib().q3ref_reset(self._h))
+        _check_ref(self._lib.q3ref_reset(self._h))
 
     def forward(self, token: int, pos: int, layers: bool = False):
         c = self.config
         logits = np.empty(c["vocab_size"], np.float32)
         if layers:
             hid = np.empty((c["n_layers"] + 1, c["dim"]), np.float32)
-            _check_ref(ref_lib().q3ref_forward_layers(self._h, token, pos, hid.ctypes.data,
+            _check_ref(self._lib.q3ref_forward_layers(self._h, token, pos, hid.ctypes.data,
                                                       logits.ctypes.data))
             return hid, logits
-        _check_ref(ref_lib().q3ref_forward_token(self._h, token, pos, logits.ctypes.data))
+        _check_ref(self._lib.q3ref_forward_token(self._h, token, pos, logits.ctypes.data))
         return logits
 
     def forward_layers(self, token: int, pos: int):
@@ -432,14 +457,14 @@ class RefModel:
         kvd = self.config["n_kv_heads"] * self.config["head_dim"]
         k = np.empty(kvd, np.uint16)
         v = np.empty(kvd, np.uint16)
-        _check_ref(ref_lib().q3ref_kv_row(self._h, layer, kv_pos, k, v))
+        _check_ref(self._lib.q3ref_kv_row(self._h, layer, kv_pos, k, v))
         return k, v
 
     def generate_ids(self, prompt, steps: int):
         p = (C.c_int * len(prompt))(*[int(t) for t in prompt])
         out = (C.c_int * max(steps, 1))()
         ps, ds = C.c_double(), C.c_double()
-        _check_ref(ref_lib().q3ref_generate_ids(self._h, p, len(prompt), steps, out,
+        _check_ref(self._lib.q3ref_generate_ids(self._h, p, len(prompt), steps, out,
                                                 C.byref(ps), C.byref(ds)))
         return list(out)[:steps], ps.value, ds.value
 

@@ -1613,6 +1613,20 @@ q3_status q3_tp_decode_forced(q3_tp* tp, const int32_t* tokens_host, int n, int 
     });
 }
 
+q3_status q3_tp_configure(q3_tp* tp, int solo_allreduce, long long wait_cycles) {
+    return guard([&] {
+        if (!tp) throw std::invalid_argument("null argument");
+        tp->t->configure(solo_allreduce != 0, wait_cycles);
+    });
+}
+
+q3_status q3_tp_reset(q3_tp* tp) {
+    return guard([&] {
+        if (!tp) throw std::invalid_argument("null argument");
+        tp->t->reset();
+    });
+}
+
 q3_status q3_block_create(const q3_config* cfg, const uint16_t* const* weights_host,
                           const size_t* counts, int device, q3_block** out) {
     return guard([&] {

@@ -57,20 +57,30 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
 }
 
 // Waits (bounded) until every source's flag in this rank's buffer reached seq. Threads
-// [0, world) poll one source each. Returns false on timeout.
-__device__ bool wait_flags(const uint8_t* own, int world, unsigned seq, long long budget) {
+// [0, world) poll one source each; a poller also gives up as soon as another kernel of this
+// rank has reported an error (so that one timeout does not make every later all-reduce of the
+// step wait out its own budget). Returns false on timeout or error.
+__device__ bool wait_flags(const uint8_t* own, int world, unsigned seq, long long budget,
+                           const unsigned* err) {
     bool ok = true;
     if (static_cast<int>(threadIdx.x) < world) {
         const unsigned* f = reinterpret_cast<const unsigned*>(own + kFlagOff) + threadIdx.x;
         const long long t0 = clock64();
-        while (ld_acquire_sys(f) < seq) {
-            if (clock64() - t0 > budget) {
+        for (unsigned it = 0; ld_acquire_sys(f) < seq; ++it) {
+            if ((it & 63) == 63 && (*reinterpret_cast<const volatile unsigned*>(err) != 0u ||
+                                    clock64() - t0 > budget)) {
                 ok = false;
                 break;
             }
         }
     }
     return __syncthreads_and(ok) != 0;
+}
+
+// True when an earlier kernel of this rank reported an error: the kernel then returns without
+// touching the exchange buffers (its peers see no flag from it and give up in their turn).
+__device__ __forceinline__ bool failed_before(const unsigned* err) {
+    return *reinterpret_cast<const volatile unsigned*>(err) != 0u;
 }
 
 __device__ void raise_flags(const TpPeers& P, int world, int rank, unsigned seq) {
@@ -87,6 +97,7 @@ __global__ void __launch_bounds__(256) tp_allreduce_kernel(TpPeers P, const floa
     __shared__ unsigned s_seq;
     pdl_wait();
     pdl_trigger();
+    if (failed_before(err)) return;
     const int tid = threadIdx.x;
     if (tid == 0) s_seq = *counter + 1;
     __syncthreads();
@@ -102,7 +113,7 @@ __global__ void __launch_bounds__(256) tp_allreduce_kernel(TpPeers P, const floa
     // the barrier (release is cumulative).
     __syncthreads();
     raise_flags(P, world, rank, seq);
-    if (!wait_flags(P.buf[rank], world, seq, budget)) {
+    if (!wait_flags(P.buf[rank], world, seq, budget, err)) {
         if (tid == 0) atomicCAS(err, 0u, 21u);
         return;
     }
@@ -134,6 +145,7 @@ __global__ void __launch_bounds__(1024) tp_argmax_kernel(
     const int32_t* forced) {
     pdl_wait();
     pdl_trigger();
+    if (failed_before(err)) return;
     __shared__ float bv[32];
     __shared__ int bi[32];
     __shared__ unsigned s_seq;
@@ -177,7 +189,7 @@ __global__ void __launch_bounds__(1024) tp_argmax_kernel(
     }
     __syncthreads();  // the flag releases below are ordered after thread 0's stores
     raise_flags(P, world, rank, seq);
-    if (!wait_flags(P.buf[rank], world, seq, budget)) {
+    if (!wait_flags(P.buf[rank], world, seq, budget, err)) {
         if (tid == 0) atomicCAS(err, 0u, 22u);
         return;
     }
@@ -302,6 +314,25 @@ TpDecoder::~TpDecoder() {
     if (s_) cudaStreamDestroy(s_);
 }
 
+void TpDecoder::configure(bool solo_allreduce, long long wait_cycles) {
+    if (wait_cycles <= 0) throw std::invalid_argument("tensor parallelism: wait budget must be > 0");
+    solo_allreduce_ = solo_allreduce;
+    wait_cycles_ = wait_cycles;
+    if (graph_) cudaGraphExecDestroy(graph_);  // the captured step holds both
+    graph_ = nullptr;
+}
+
+void TpDecoder::reset() {
+    // Invocation counter, error word, exchange data and flags back to zero: every rank resets
+    // (and the ranks meet on the host) before any of them decodes again.
+    Q3_CUDA(cudaStreamSynchronize(s_));
+    for (DeviceBuffer* b : {&err_, &counter_, &xbuf_}) {
+        Q3_CUDA(cudaMemsetAsync(b->ptr, 0, b->bytes, s_));
+    }
+    Q3_CUDA(cudaStreamSynchronize(s_));
+    failed_ = false;
+}
+
 void TpDecoder::ipc_handle(void* out) const {
     cudaIpcMemHandle_t h;
     Q3_CUDA(cudaIpcGetMemHandle(&h, xbuf_.ptr));
@@ -312,9 +343,19 @@ void TpDecoder::ipc_handle(void* out) const {
 void TpDecoder::connect(const void* handles) {
     if (connected_) throw std::runtime_error("tensor parallelism: already connected");
     peer_mapped_.assign(world_, nullptr);
+    self_peer_.assign(world_, 0);
+    uint8_t own[64];
+    ipc_handle(own);
     const auto* hs = static_cast<const uint8_t*>(handles);
     for (int p = 0; p < world_; ++p) {
         if (p == rank_) continue;
+        if (std::memcmp(hs + 64 * p, own, 64) == 0) {
+            // This rank's own buffer given as a peer's (a process cannot open its own IPC
+            // handle): used as is. Nothing raises that peer's flag, so every all-reduce of such
+            // a decoder ends in the bounded wait's timeout - the form the timeout test uses.
+            self_peer_[p] = 1;
+            continue;
+        }
         cudaIpcMemHandle_t h;
         std::memcpy(&h, hs + 64 * p, 64);
         void* ptr = nullptr;
@@ -331,16 +372,18 @@ void TpDecoder::enqueue_step(bool forced) {
     unsigned* counter = static_cast<unsigned*>(counter_.ptr);
     TpPeers P{};
     for (int p = 0; p < world_; ++p) {
-        P.buf[p] = static_cast<uint8_t*>(p == rank_ ? xbuf_.ptr : peer_mapped_[p]);
+        const bool own = p == rank_ || (p < static_cast<int>(self_peer_.size()) && self_peer_[p]);
+        P.buf[p] = static_cast<uint8_t*>(own ? xbuf_.ptr : peer_mapped_[p]);
     }
-    constexpr long long kBudget = 4000000000LL;
+    const long long kBudget = wait_cycles_;
     float* X = static_cast<float*>(x_.ptr);
     float* qkv = static_cast<float*>(qkv_.ptr);
     float* part = static_cast<float*>(part_.ptr);
     Engine& e = m_.engine();
-    // One rank: the projections add straight into x. Several: each writes its partial, and the
-    // all-reduce adds the ranks' partials in rank order.
-    const bool solo = world_ == 1;
+    // One rank: the projections add straight into x, unless configured to route them through
+    // the all-reduce kernel with this rank as its only member. Several: each writes its partial,
+    // and the all-reduce adds the ranks' partials in rank order.
+    const bool solo = world_ == 1 && !solo_allreduce_;
     const int proj_epi = solo ? kEpiResidual : kEpiStore;
     float* proj_out = solo ? X : part;
     auto allreduce = [&]() {
@@ -424,6 +467,10 @@ void TpDecoder::enqueue_step(bool forced) {
 void TpDecoder::decode(int32_t first, int pos0, int n_steps, const int32_t* forced_host,
                        int32_t* tokens_host) {
     const q3_config& c = cfg_;
+    if (failed_) {
+        throw std::runtime_error("tensor-parallel decode: an earlier step timed out; every rank "
+                                 "must reset the decoder before decoding again");
+    }
     if (!connected_ && world_ > 1) throw std::runtime_error("tensor parallelism: not connected");
     if (world_ == 1 && !connected_) {
         peer_mapped_.assign(1, nullptr);
@@ -494,7 +541,8 @@ void TpDecoder::decode(int32_t first, int pos0, int n_steps, const int32_t* forc
     unsigned e = 0;
     Q3_CUDA(cudaMemcpy(&e, err_.ptr, 4, cudaMemcpyDeviceToHost));
     if (e) {
-        Q3_CUDA(cudaMemset(err_.ptr, 0, 4));
+        // The ranks' invocation counters may now disagree: refuse further steps until reset.
+        failed_ = true;
         throw DeviceTimeout("tensor-parallel decode: a bounded wait gave up (code " +
                             std::to_string(e) + ")");
     }

@@ -46,6 +46,13 @@ public:
     void decode(int32_t first, int pos0, int n_steps, const int32_t* forced_host,
                 int32_t* tokens_host);
     cudaStream_t stream() const { return s_; }
+    // solo_allreduce: at world 1, send the o_proj / down_proj partials through the all-reduce
+    // kernel (this rank as its only member) instead of adding them into x directly.
+    // wait_cycles: budget (SM clock cycles) of each bounded flag wait.
+    void configure(bool solo_allreduce, long long wait_cycles);
+    // After a timeout (decode threw DeviceTimeout and refuses further steps): zero the
+    // invocation counter, error word and exchange buffer. Every rank resets before any decodes.
+    void reset();
 
 private:
     void enqueue_step(bool forced);
@@ -69,7 +76,11 @@ private:
     DeviceBuffer pos_, tok_, step_, forced_, log_, err_, counter_, part_o_, part_ml_, attn_counter_;
     DeviceBuffer xbuf_;     // exchange buffer (IPC-exported): data, argmax slots, flags
     std::vector<void*> peer_mapped_;
+    std::vector<uint8_t> self_peer_;  // peers given this rank's own handle
     bool connected_ = false;
+    bool failed_ = false;
+    bool solo_allreduce_ = false;
+    long long wait_cycles_ = 4000000000LL;  // ~2 s at the B200 boost clock
     int log_cap_ = 0;
     int attn_pps_ = 8, attn_splits_ = 1;  // decode attention: pages per split, splits
     int sms_ = 0;

@@ -117,6 +117,8 @@ def lib() -> C.CDLL:
         "q3_tp_stream": [vp, C.POINTER(vp)],
         "q3_tp_decode": [vp, i32, C.c_int, C.c_int, vp],
         "q3_tp_decode_forced": [vp, I32P, C.c_int, C.c_int, vp],
+        "q3_tp_configure": [vp, C.c_int, C.c_longlong],
+        "q3_tp_reset": [vp],
         "q3_decode_greedy": [vp, i32, C.c_int, C.c_int, vp, vp],
         "q3_decode_forced": [vp, I32P, C.c_int, C.c_int, vp, vp],
         "q3_generate": [vp, vp, C.c_int, sz, C.c_int, vp, C.POINTER(sz), C.POINTER(GenStats)],
@@ -435,6 +437,15 @@ class TpDecoder:
         out = np.empty(max(tokens.size, 1), np.int32)
         check(self._lib.q3_tp_decode_forced(self._h, tokens, tokens.size, pos0, out.ctypes.data))
         return out[:tokens.size]
+
+    def configure(self, solo_allreduce: bool = False, wait_cycles: int = 4_000_000_000) -> None:
+        """solo_allreduce: at world 1, route the partials through the all-reduce kernel;
+        wait_cycles: budget of each bounded flag wait (SM clock cycles)."""
+        check(self._lib.q3_tp_configure(self._h, int(bool(solo_allreduce)), int(wait_cycles)))
+
+    def reset(self) -> None:
+        """Clears the state a timed-out step left (every rank resets before decoding again)."""
+        check(self._lib.q3_tp_reset(self._h))
 
 
 class Block:

@@ -2,7 +2,12 @@
 torch.distributed.run). Prefills the prompt on this rank's own model, connects the ranks' exchange
 buffers, runs teacher-forced and free-running decode, and writes its results to <out>.rank<r>.npz.
 
-    python -m torch.distributed.run --nproc-per-node N tests/tp_worker.py <weights> <inputs.npz> <out>
+    python -m torch.distributed.run --nproc-per-node N tests/tp_worker.py <weights> <inputs.npz> <out> [mode]
+
+mode "decode" (default): the parity run. Mode "leave": after one decode call together, every rank
+but 0 stops taking part (leaves between steps, nothing of its own in flight); rank 0 decodes once
+more with a short wait budget and records whether it timed out, how long that took, and whether
+the decoder then refused another step.
 """
 import os
 import sys
@@ -22,6 +27,7 @@ def main():
     import q3b200
 
     weights, inputs, out = sys.argv[1], sys.argv[2], sys.argv[3]
+    mode = sys.argv[4] if len(sys.argv) > 4 else "decode"
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
@@ -35,6 +41,29 @@ def main():
     dist.all_gather_object(handles, tp.ipc_handle())
     tp.connect(handles)
     dist.barrier()
+    if mode == "leave":
+        import time
+        tp.configure(wait_cycles=20_000_000)  # ~10 ms at the boost clock
+        tp.decode_forced(cont[:2], len(prompt))
+        dist.barrier()  # every rank's first call has finished; rank 1 now leaves
+        res = {"timed_out": 0, "refused": 0, "seconds": 0.0}
+        if rank == 0:
+            t0 = time.perf_counter()
+            try:
+                tp.decode_forced(cont[2:4], len(prompt) + 2)
+            except q3b200.DeviceTimeout:
+                res["timed_out"] = 1
+            res["seconds"] = time.perf_counter() - t0
+            try:
+                tp.decode_forced(cont[4:5], len(prompt) + 4)
+            except q3b200.Q3RuntimeError as e:
+                res["refused"] = int(not isinstance(e, q3b200.DeviceTimeout))
+        np.savez(f"{out}.rank{rank}.npz", **res)
+        dist.barrier()
+        tp.close()
+        m.close()
+        dist.destroy_process_group()
+        return
     am = tp.decode_forced(cont, len(prompt))
     free = tp.decode(int(am[-1]), len(prompt) + len(cont), 8)
     dist.barrier()
