@@ -373,18 +373,19 @@ def run_b200_arm(args):
         total_ms = max_over_ranks(total_ms, world)
         clk = clocks.stop()
 
-        # End to end through the public API with host buffers: ForwardToken per step (token and
-        # position in, 151936 fp32 logits out to host), greedy argmax on the host - the way a user
-        # of the reference drives ForwardToken + Sampler::Greedy.
+        # End to end through the public API with host buffers: ForwardToken + Sampler::Greedy
+        # per step (q3_forward_token_greedy: token and position in; the 151936 fp32 logits and
+        # their greedy token out to host) - the two calls of each step of Qwen3::Generate.
         model.reset()
         _, nxt = model.prefill(p, 0, want_logits=False)
         e2e_steps = min(args.steps, RUN_STEPS)
         tok = nxt
+        for i in range(3):  # warm-up calls (positions rewritten below)
+            model.forward_token_greedy(tok, PROMPT_LEN + i)
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         for i in range(e2e_steps):
-            lg = model.forward_token_ref(tok, PROMPT_LEN + i)
-            tok = int(np.argmax(lg))
+            lg, tok = model.forward_token_greedy(tok, PROMPT_LEN + i)
         e2e_s = time.perf_counter() - t0
         e2e_tps = world * e2e_steps / e2e_s
 
@@ -535,9 +536,10 @@ def run_b200_arm(args):
                 "achieved_gbs": round(step_bytes * per_gpu_tps / 1e9, 1),
                 "frac": round(step_bytes * per_gpu_tps / 1e9 / pk["hbm_gbs"], 4)},
             "e2e": {"value": round(e2e_tps, 2), "unit": UNIT, "h2d_bytes_per_step": 32,
-                    "d2h_bytes_per_step": VOCAB * 4,
-                    "api": "q3_forward_token_ref per step (logits in the model's pinned "
-                           "buffer, the reference's const-reference return) + host argmax"},
+                    "d2h_bytes_per_step": VOCAB * 4 + 8,
+                    "api": "q3_forward_token_greedy per step: ForwardToken + Sampler::Greedy "
+                           "(logits into the model's pinned buffer, the reference's "
+                           "const-reference return, and their greedy token)"},
             "cpu_baseline": cpu,
             "clocks": clk,
             "dp_decode": {

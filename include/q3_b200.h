@@ -108,6 +108,12 @@ q3_status q3_forward_token(q3_model* model, int32_t token, int pos, float* logit
  * a model-owned pinned host buffer, valid until the next call on this model. */
 q3_status q3_forward_token_ref(q3_model* model, int32_t token, int pos, const float** logits);
 
+/* Qwen3::ForwardToken followed by Sampler::Greedy on its logits (the two calls of each step of
+ * Qwen3::Generate, src/inference.cpp:680-683, :703-709): *logits as q3_forward_token_ref, and
+ * *next_token = the index of their first maximum, computed on the device. */
+q3_status q3_forward_token_greedy(q3_model* model, int32_t token, int pos, const float** logits,
+                                  int32_t* next_token);
+
 /* ForwardToken with debug taps: hidden_host[(n_layers+1)*dim] receives the embedding row and
  * the hidden state after each layer (the per-layer view of src/inference.cpp:615-617). Either
  * output may be NULL. */
@@ -131,14 +137,23 @@ q3_status q3_prefill_layers(q3_model* model, const int32_t* ids_host, int n, int
                             float* hidden_host, float* last_logits_host, int32_t* next_token_host);
 
 /* Prefill paths (no reference counterpart: the reference prefills token by token). BATCHED runs
- * every projection as a tensor-core contraction over all prompt tokens (tcgen05, bf16 operands,
- * fp32 accumulation) and causal attention over the paged cache; it is used when the model shape
+ * every projection as a tensor-core contraction over all prompt tokens (tcgen05, fp32
+ * accumulation) and causal attention over the paged cache; it is used when the model shape
  * allows it (head_dim 128, two query heads per KV head) and pos0 + n <= context, and is the
  * default. TOKENWISE feeds the prompt through the decode path one token at a time. */
 enum { Q3_PREFILL_TOKENWISE = 0, Q3_PREFILL_BATCHED = 1 };
 q3_status q3_model_set_prefill_path(q3_model* model, int path);
 /* The path q3_prefill takes for prompts that fit below the context. */
 q3_status q3_model_prefill_path(const q3_model* model, int* path);
+/* Operand precision of the batched prefill (also used by q3_batch_add). F16 (the default): fp16
+ * copies of the weights (the bf16 values, exact in their range; made on first use, +0.88 GB for
+ * Qwen3-0.6B) and fp16 activations, the [wq;wk;wv] input as an fp16 hi + lo pair, attention on
+ * fp16 copies of the cache rows (+ the cache's size); decode after a long prompt then agrees with
+ * the reference as decode after a short one does. BF16: one bf16 rounding per activation operand
+ * (8 significant bits against 11), no extra memory. The tensor-core rate is the same. */
+enum { Q3_PREFILL_BF16 = 0, Q3_PREFILL_F16 = 1 };
+q3_status q3_model_set_prefill_precision(q3_model* model, int precision);
+q3_status q3_model_prefill_precision(const q3_model* model, int* precision);
 
 /* n_steps greedy decode steps driven on the device (the loop of src/inference.cpp:679-690 with
  * stop_on_eos = false, i.e. `--benchmark N`): step i feeds token t_i at position pos0+i and
@@ -318,6 +333,10 @@ q3_status q3_attn_noalloc(float* out, const float* q, const uint16_t* k, const u
 enum { Q3_GEMM_STORE_F32 = 0, Q3_GEMM_ADD_F32 = 1, Q3_GEMM_SWIGLU = 2, Q3_GEMM_STORE_BF16 = 3 };
 q3_status q3_gemm_bf16(void* out, const uint16_t* a, const uint16_t* w, const uint16_t* w3, int M,
                        int N, int K, int epilogue, void* stream);
+/* As q3_gemm_bf16 with fp16 A and W (and W3); Q3_GEMM_SWIGLU and Q3_GEMM_STORE_BF16 then write
+ * fp16 (saturated to +-65504). The operand precision of the default batched prefill. */
+q3_status q3_gemm_f16(void* out, const uint16_t* a, const uint16_t* w, const uint16_t* w3, int M,
+                      int N, int K, int epilogue, void* stream);
 
 /* Sampler::Greedy (src/inference.cpp:703-709): index of the first maximum of logits[n], written
  * to *out_index (device int32). n == 0 is rejected like the reference's empty span. */

@@ -191,8 +191,11 @@ int Batch::add(const int32_t* ids, int n, int32_t* next_token, float* last_logit
     std::vector<LayerWeights> layers(c.n_layers);
     for (int l = 0; l < c.n_layers; ++l) layers[l] = m_.layer(l);
     // The prompt's slot range is checked against the slot's pages, not the model's context.
+    prefill_->set_precision(m_.prefill_precision());
+    const std::vector<LayerWeights>* l16 =
+        m_.prefill_precision() == Prefill::kPrecisionF16 ? &m_.layers_f16() : nullptr;
     prefill_->run(static_cast<const int32_t*>(ids_.ptr), n, 0, m_.embed(), layers, kv, xl,
-                  nullptr, s_);
+                  nullptr, s_, l16);
     DeviceBuffer lg, am;
     lg.alloc(static_cast<size_t>(c.vocab_size) * 4);
     am.alloc(4);

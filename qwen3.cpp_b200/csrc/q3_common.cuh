@@ -101,6 +101,33 @@ __device__ __forceinline__ uint16_t f32_to_bf16(float f) {
     return static_cast<uint16_t>(u >> 16);
 }
 
+// fp16 operands of the prefill's tensor-core contractions and attention (an 11-bit significand
+// against bf16's 8, at the same MMA rate). Two fp32 -> one packed f16x2 (a in the low half),
+// rounded to nearest even and saturated to +-65504 rather than overflowing to infinity.
+__device__ __forceinline__ uint32_t pack2_f16(float a, float b) {
+    uint32_t r;
+    asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+    return r;
+}
+__device__ __forceinline__ float f16_lo(uint32_t packed) {
+    float f;
+    asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %1;\n\tcvt.f32.f16 %0, l;\n\t}"
+        : "=f"(f) : "r"(packed));
+    return f;
+}
+__device__ __forceinline__ float f16_hi(uint32_t packed) {
+    float f;
+    asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %1;\n\tcvt.f32.f16 %0, h;\n\t}"
+        : "=f"(f) : "r"(packed));
+    return f;
+}
+// Packed bf16 pair -> packed fp16 pair holding the same values (exact for magnitudes in
+// [2^-17, 65504]: every bf16 value there is an fp16 value; smaller ones round to the fp16
+// subnormal grid, larger ones saturate).
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t packed) {
+    return pack2_f16(bf16_lo(packed), bf16_hi(packed));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

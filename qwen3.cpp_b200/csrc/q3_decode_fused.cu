@@ -551,6 +551,9 @@ struct Producer {
             prev_short = sp.shrt;
             base += barriers_of(a, sp.shrt);
         }
+        // This CTA's rows of the first layer into L2 for the next launch (a decode loop of
+        // one-step calls would otherwise start every step on a cold stream).
+        if (ok && a.l2_ahead > 0) prefetch_unit(a.layers, a.n_layers, a.lm_head, a.vocab, 0, G, c);
         if (a.prof) a.prof[static_cast<size_t>(c) * 8 + 4] = blocked;
         // Wait for every copy still in flight before the CTA may exit.
         const uint32_t first = q > NS ? q - NS : 0;

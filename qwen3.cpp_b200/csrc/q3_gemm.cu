@@ -194,7 +194,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     } else if (warp == 1) {
         if (lane == 0) {
             // ---------------------------------------------------------------- MMA issuer
-            const uint32_t idesc = idesc_bf16_f32(BM, BN);
+            const uint32_t idesc = args.f16 ? idesc_f16_f32(BM, BN) : idesc_bf16_f32(BM, BN);
             int stage = 0;
             uint32_t phase = 0;
             int acc = 0;
@@ -305,9 +305,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         }
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
-                            row[hlf * 4 + i] = make_uint4(
-                                pack_bf16(g[8 * i], g[8 * i + 1]), pack_bf16(g[8 * i + 2], g[8 * i + 3]),
-                                pack_bf16(g[8 * i + 4], g[8 * i + 5]), pack_bf16(g[8 * i + 6], g[8 * i + 7]));
+                            row[hlf * 4 + i] = args.f16
+                                ? make_uint4(pack2_f16(g[8 * i], g[8 * i + 1]), pack2_f16(g[8 * i + 2], g[8 * i + 3]),
+                                             pack2_f16(g[8 * i + 4], g[8 * i + 5]), pack2_f16(g[8 * i + 6], g[8 * i + 7]))
+                                : make_uint4(pack_bf16(g[8 * i], g[8 * i + 1]), pack_bf16(g[8 * i + 2], g[8 * i + 3]),
+                                             pack_bf16(g[8 * i + 4], g[8 * i + 5]), pack_bf16(g[8 * i + 6], g[8 * i + 7]));
                         }
                     }
                     stage_store(row, tn * (BN / 2) + c, y);
@@ -338,13 +340,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         inv = 1.0f / sqrtf(ss / 128.0f + e.eps);
                     }
                     uint16_t* dst = nullptr;
+                    uint16_t* dst16 = nullptr;  // fp16 copy of a K/V row
+                    const bool isq = head < nq;
                     if (live) {
-                        if (head < nq) {
+                        if (isq) {
                             dst = e.q_out + static_cast<size_t>(token) * nq * 128 + head * 128;
                         } else {
                             const int g = qk ? head - nq : head - nq - nk;
                             const size_t page = static_cast<size_t>(__ldg(e.page_table + pos / 16));
-                            dst = (qk ? e.k_cache : e.v_cache) + ((page * nk + g) * 16 + pos % 16) * 128;
+                            const size_t off = ((page * nk + g) * 16 + pos % 16) * 128;
+                            dst = (qk ? e.k_cache : e.v_cache) + off;
+                            uint16_t* st = qk ? e.k_stage : e.v_stage;
+                            if (st) dst16 = st + off;
                         }
                     }
                     const uint16_t* w = head < nq ? e.q_norm : e.k_norm;
@@ -383,14 +390,32 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                             }
                         }
                         if (live) {
+                            const bool f16q = isq && e.q_f16;
 #pragma unroll
                             for (int i = 0; i < 4; ++i) {
-                                reinterpret_cast<uint4*>(dst + c)[i] = make_uint4(
-                                    pack_bf16(a[8 * i], a[8 * i + 1]), pack_bf16(a[8 * i + 2], a[8 * i + 3]),
-                                    pack_bf16(a[8 * i + 4], a[8 * i + 5]), pack_bf16(a[8 * i + 6], a[8 * i + 7]));
-                                reinterpret_cast<uint4*>(dst + 64 + c)[i] = make_uint4(
-                                    pack_bf16(b[8 * i], b[8 * i + 1]), pack_bf16(b[8 * i + 2], b[8 * i + 3]),
-                                    pack_bf16(b[8 * i + 4], b[8 * i + 5]), pack_bf16(b[8 * i + 6], b[8 * i + 7]));
+                                uint4 va, vb;
+                                if (f16q) {
+                                    va = make_uint4(pack2_f16(a[8 * i], a[8 * i + 1]), pack2_f16(a[8 * i + 2], a[8 * i + 3]),
+                                                    pack2_f16(a[8 * i + 4], a[8 * i + 5]), pack2_f16(a[8 * i + 6], a[8 * i + 7]));
+                                    vb = make_uint4(pack2_f16(b[8 * i], b[8 * i + 1]), pack2_f16(b[8 * i + 2], b[8 * i + 3]),
+                                                    pack2_f16(b[8 * i + 4], b[8 * i + 5]), pack2_f16(b[8 * i + 6], b[8 * i + 7]));
+                                } else {
+                                    va = make_uint4(pack_bf16(a[8 * i], a[8 * i + 1]), pack_bf16(a[8 * i + 2], a[8 * i + 3]),
+                                                    pack_bf16(a[8 * i + 4], a[8 * i + 5]), pack_bf16(a[8 * i + 6], a[8 * i + 7]));
+                                    vb = make_uint4(pack_bf16(b[8 * i], b[8 * i + 1]), pack_bf16(b[8 * i + 2], b[8 * i + 3]),
+                                                    pack_bf16(b[8 * i + 4], b[8 * i + 5]), pack_bf16(b[8 * i + 6], b[8 * i + 7]));
+                                }
+                                reinterpret_cast<uint4*>(dst + c)[i] = va;
+                                reinterpret_cast<uint4*>(dst + 64 + c)[i] = vb;
+                                if (dst16) {
+                                    // The cache's bf16 values, as fp16 (exact in range).
+                                    reinterpret_cast<uint4*>(dst16 + c)[i] = make_uint4(
+                                        bf16x2_to_f16x2(va.x), bf16x2_to_f16x2(va.y),
+                                        bf16x2_to_f16x2(va.z), bf16x2_to_f16x2(va.w));
+                                    reinterpret_cast<uint4*>(dst16 + 64 + c)[i] = make_uint4(
+                                        bf16x2_to_f16x2(vb.x), bf16x2_to_f16x2(vb.y),
+                                        bf16x2_to_f16x2(vb.z), bf16x2_to_f16x2(vb.w));
+                                }
                             }
                         }
                     }
@@ -405,9 +430,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         tmem_ld32(tb_addr + c + hlf * 32, v);
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
-                            row[hlf * 4 + i] = make_uint4(
-                                pack_bf16(v[8 * i], v[8 * i + 1]), pack_bf16(v[8 * i + 2], v[8 * i + 3]),
-                                pack_bf16(v[8 * i + 4], v[8 * i + 5]), pack_bf16(v[8 * i + 6], v[8 * i + 7]));
+                            row[hlf * 4 + i] = args.f16
+                                ? make_uint4(pack2_f16(v[8 * i], v[8 * i + 1]), pack2_f16(v[8 * i + 2], v[8 * i + 3]),
+                                             pack2_f16(v[8 * i + 4], v[8 * i + 5]), pack2_f16(v[8 * i + 6], v[8 * i + 7]))
+                                : make_uint4(pack_bf16(v[8 * i], v[8 * i + 1]), pack_bf16(v[8 * i + 2], v[8 * i + 3]),
+                                             pack_bf16(v[8 * i + 4], v[8 * i + 5]), pack_bf16(v[8 * i + 6], v[8 * i + 7]));
                         }
                     }
                     stage_store(row, tn * BN + c, y);
@@ -584,6 +611,7 @@ void prepare_gemm_kernels() {
     Q3_CUDA((configure_t<128, kEpiAddF32, true>()));
     Q3_CUDA((configure_t<256, kEpiStoreF32, true>()));
     Q3_CUDA((configure_t<256, kEpiAddF32, true>()));
+    Q3_CUDA((configure_t<256, kEpiQkvRope, true>()));
 }
 
 cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap* b2,
@@ -606,6 +634,9 @@ cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtens
         if (epi == kEpiAddF32) {
             return bn == 256 ? launch_t<256, kEpiAddF32, true>(a, b, bb, out, args, num_sms, stream, *a_lo)
                              : launch_t<128, kEpiAddF32, true>(a, b, bb, out, args, num_sms, stream, *a_lo);
+        }
+        if (epi == kEpiQkvRope) {
+            return launch_t<256, kEpiQkvRope, true>(a, b, bb, out, args, num_sms, stream, *a_lo);
         }
         return cudaErrorInvalidValue;
     }
@@ -631,9 +662,26 @@ cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtens
 
 // ------------------------------------------------------------------ C ABI
 
+namespace {
+q3_status gemm_entry(void* out, const uint16_t* a, const uint16_t* w, const uint16_t* w3, int M,
+                     int N, int K, int epilogue, void* stream, bool f16);
+}
+
 extern "C" q3_status q3_gemm_bf16(void* out, const uint16_t* a, const uint16_t* w,
                                   const uint16_t* w3, int M, int N, int K, int epilogue,
                                   void* stream) {
+    return gemm_entry(out, a, w, w3, M, N, K, epilogue, stream, false);
+}
+
+extern "C" q3_status q3_gemm_f16(void* out, const uint16_t* a, const uint16_t* w,
+                                 const uint16_t* w3, int M, int N, int K, int epilogue,
+                                 void* stream) {
+    return gemm_entry(out, a, w, w3, M, N, K, epilogue, stream, true);
+}
+
+namespace {
+q3_status gemm_entry(void* out, const uint16_t* a, const uint16_t* w, const uint16_t* w3, int M,
+                     int N, int K, int epilogue, void* stream, bool f16) {
     using namespace q3;
     return guard([&] {
         if (!out || !a || !w) throw std::invalid_argument("null argument");
@@ -666,6 +714,7 @@ extern "C" q3_status q3_gemm_bf16(void* out, const uint16_t* a, const uint16_t* 
         g.N = tile_space;
         g.K = K;
         g.err = err;
+        g.f16 = f16 ? 1 : 0;
         const cudaError_t le = launch_gemm(ma, mb, swiglu ? &mb3 : nullptr, mo, g, epilogue, sms, s);
         unsigned herr = 0;
         const cudaError_t ce = cudaMemcpyAsync(&herr, err, sizeof(unsigned),
@@ -678,3 +727,4 @@ extern "C" q3_status q3_gemm_bf16(void* out, const uint16_t* a, const uint16_t* 
         if (herr) throw DeviceTimeout("gemm: a pipeline wait gave up (code " + std::to_string(herr) + ")");
     });
 }
+}  // namespace

@@ -32,6 +32,11 @@ struct QkvEpilogue {
     const uint16_t* k_norm = nullptr;    // [128]
     int pos0 = 0, n_heads = 0, n_kv = 0;
     float eps = 0.0f;
+    int q_f16 = 0;                       // q rows as fp16 instead of bf16
+    // Nullable: fp16 copies of the K/V rows written to the cache (the same bf16-rounded values,
+    // same paged layout), the operands of the fp16 prefill attention.
+    uint16_t* k_stage = nullptr;
+    uint16_t* v_stage = nullptr;
 };
 
 // A 2-D K-major bf16 matrix [rows, cols] (cols contiguous) as a TMA tensor map with 128-byte
@@ -65,6 +70,8 @@ struct GemmArgs {
     int min_slice_kblocks = 8;  // ... of at least this many 64-wide k-blocks
     QkvEpilogue qkv;            // kEpiQkvRope only
     bool dependent = false;     // programmatic dependent launch (see launch_dep)
+    // A and B are fp16 (else bf16); the SwiGLU epilogue then writes fp16 as well.
+    int f16 = 0;
 };
 
 // Opts every contraction kernel into its shared memory on the current device (launch_gemm does it
@@ -78,8 +85,9 @@ int gemm_tile_n(int epi, int N);
 // `out` (make_tmap_out) maps the output: fp32 [M, N] (store or residual add) or bf16 ([M, N/2]
 // for SwiGLU, [M, N] for kEpiStoreBF16). K must be a multiple of 64, N a multiple of the tile
 // width. Grid: one persistent CTA per SM at most. Returns cudaSuccess or the launch error.
-// a_lo (optional; store and residual-add epilogues): the A operand is a + a_lo, two bf16 parts of
-// fp32 activations (same shape and boxes as a), multiplied into the same accumulator.
+// a_lo (optional; store, residual-add and QKV epilogues): the A operand is a + a_lo, two parts
+// (bf16, or fp16 with GemmArgs::f16) of fp32 activations (same shape and boxes as a), multiplied
+// into the same accumulator.
 cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap* b2,
                         const CUtensorMap& out, const GemmArgs& args, int epi, int num_sms,
                         cudaStream_t stream, const CUtensorMap* a_lo = nullptr);

@@ -945,7 +945,7 @@ unsigned* Model::fused_err_word() const {
 }
 
 void Model::forward_token(int32_t token, int pos, float* hidden_host, float* logits_host,
-                          bool err_after_logits) {
+                          bool err_after_logits, int32_t* next_host) {
     check_token_pos(token, pos);
     Engine& e = *engine_;
     e.ensure_rope(pos + 2);
@@ -981,14 +981,22 @@ void Model::forward_token(int32_t token, int pos, float* hidden_host, float* log
                                     (err_after_logits ? sizeof(unsigned) : 0),
                                 cudaMemcpyDeviceToHost, s));
     }
+    if (next_host) {
+        // The step's greedy token (both decode paths log it at index 0 of a one-step call).
+        Q3_CUDA(cudaMemcpyAsync(next_host, token_log_.ptr, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    }
     Q3_CUDA(cudaStreamSynchronize(s));
     if (*err_host != 0u) check_fused_error();  // throws
 }
 
-const float* Model::forward_token_ref(int32_t token, int pos) {
-    pinned_logits_.ensure(static_cast<size_t>(cfg_.vocab_size) * 4 + sizeof(unsigned));
-    forward_token(token, pos, nullptr, static_cast<float*>(pinned_logits_.ptr), true);
-    return static_cast<const float*>(pinned_logits_.ptr);
+const float* Model::forward_token_ref(int32_t token, int pos, int32_t* next) {
+    // [logits][error word][greedy token]
+    pinned_logits_.ensure(static_cast<size_t>(cfg_.vocab_size) * 4 + 2 * sizeof(unsigned));
+    float* buf = static_cast<float*>(pinned_logits_.ptr);
+    int32_t* tok = reinterpret_cast<int32_t*>(buf + cfg_.vocab_size + 1);
+    forward_token(token, pos, nullptr, buf, true, next ? tok : nullptr);
+    if (next) *next = *tok;
+    return buf;
 }
 
 void Model::decode_loop(const int32_t* forced_host, int n, int32_t first_token, int pos0,
@@ -1035,6 +1043,22 @@ void Model::decode_loop(const int32_t* forced_host, int n, int32_t first_token, 
     Q3_CUDA(cudaStreamSynchronize(s));
 }
 
+void Model::set_prefill_precision(int p) {
+    if (p != Prefill::kPrecisionBF16 && p != Prefill::kPrecisionF16) {
+        throw std::invalid_argument("unknown prefill precision");
+    }
+    prefill_precision_ = p;
+}
+
+const std::vector<LayerWeights>& Model::layers_f16() {
+    if (layers16_.empty()) {
+        cudaStream_t s = engine_->stream();
+        make_f16_layers(cfg_, layers_, f16_arena_, layers16_, s);
+        Q3_CUDA(cudaStreamSynchronize(s));
+    }
+    return layers16_;
+}
+
 bool Model::batched_prefill_ok(int n, int pos0) const {
     return use_batched_prefill_ && Prefill::supported(cfg_) && n > 0 && pos0 >= 0 &&
            pos0 <= cfg_.max_seq_len - n;
@@ -1070,6 +1094,9 @@ void Model::prefill_batched(const int32_t* ids, int n, int pos0, float* last_log
     cudaStream_t s = e.stream();
     e.ensure_rope(pos0 + n + 1);
     if (!prefill_) prefill_ = std::make_unique<Prefill>(cfg_, device_);
+    prefill_->set_precision(prefill_precision_);
+    const std::vector<LayerWeights>* l16 =
+        prefill_precision_ == Prefill::kPrecisionF16 ? &layers_f16() : nullptr;
     if (prefill_ids_.bytes < static_cast<size_t>(n) * 4) {
         Q3_CUDA(cudaStreamSynchronize(s));
         prefill_ids_.alloc(static_cast<size_t>(n) * 4);
@@ -1080,7 +1107,7 @@ void Model::prefill_batched(const int32_t* ids, int n, int pos0, float* last_log
     Q3_CUDA(cudaMemcpyAsync(prefill_ids_.ptr, pinned_io_.ptr, static_cast<size_t>(n) * 4,
                             cudaMemcpyHostToDevice, s));
     prefill_->run(static_cast<const int32_t*>(prefill_ids_.ptr), n, pos0, embed_, layers_,
-                  engine_view(e), e.x(), hidden_host ? e.taps() : nullptr, s);
+                  engine_view(e), e.x(), hidden_host ? e.taps() : nullptr, s, l16);
     // Final RmsNorm + tied lm_head of the last token (src/inference.cpp:619-635) and Greedy.
     const q3_config& c = cfg_;
     launch_gemv(kEpiStore, output_, nullptr, e.x(), final_norm_, c.norm_eps,
@@ -1385,6 +1412,14 @@ q3_status q3_forward_token_ref(q3_model* model, int32_t token, int pos, const fl
     });
 }
 
+q3_status q3_forward_token_greedy(q3_model* model, int32_t token, int pos, const float** logits,
+                                  int32_t* next_token) {
+    return guard([&] {
+        if (!model || !logits || !next_token) throw std::invalid_argument("null argument");
+        *logits = model->m->forward_token_ref(token, pos, next_token);
+    });
+}
+
 q3_status q3_forward_token_layers(q3_model* model, int32_t token, int pos, float* hidden_host,
                                   float* logits_host) {
     return guard([&] {
@@ -1432,6 +1467,25 @@ q3_status q3_model_prefill_path(const q3_model* model, int* path) {
         *path = model->m->batched_prefill_enabled() && q3::Prefill::supported(model->m->config())
                     ? Q3_PREFILL_BATCHED
                     : Q3_PREFILL_TOKENWISE;
+    });
+}
+
+q3_status q3_model_set_prefill_precision(q3_model* model, int precision) {
+    return guard([&] {
+        if (!model) throw std::invalid_argument("null argument");
+        if (precision != Q3_PREFILL_BF16 && precision != Q3_PREFILL_F16) {
+            throw std::invalid_argument("unknown prefill precision");
+        }
+        model->m->set_prefill_precision(precision == Q3_PREFILL_F16 ? q3::Prefill::kPrecisionF16
+                                                                    : q3::Prefill::kPrecisionBF16);
+    });
+}
+
+q3_status q3_model_prefill_precision(const q3_model* model, int* precision) {
+    return guard([&] {
+        if (!model || !precision) throw std::invalid_argument("null argument");
+        *precision = model->m->prefill_precision() == q3::Prefill::kPrecisionF16 ? Q3_PREFILL_F16
+                                                                                 : Q3_PREFILL_BF16;
     });
 }
 

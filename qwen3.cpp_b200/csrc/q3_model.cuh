@@ -164,11 +164,13 @@ public:
     void reset();
     // err_after_logits: logits_host has room for one more word, which receives the fused
     // kernel's error word in the same copy.
+    // next_host (nullable): the step's greedy token (Sampler::Greedy of the logits).
     void forward_token(int32_t token, int pos, float* hidden_host, float* logits_host,
-                       bool err_after_logits = false);
+                       bool err_after_logits = false, int32_t* next_host = nullptr);
     // ForwardToken returning the logits in a model-owned pinned host buffer, valid until the
-    // next call (the reference returns a reference to its logits vector).
-    const float* forward_token_ref(int32_t token, int pos);
+    // next call (the reference returns a reference to its logits vector); next (nullable)
+    // receives their greedy token, computed on the device.
+    const float* forward_token_ref(int32_t token, int pos, int32_t* next = nullptr);
     void decode_loop(const int32_t* forced_host, int n, int32_t first_token, int pos0,
                      int32_t* out_tokens_host, float* last_logits_host, float* all_logits_host);
     // Prompt prefill. Batched (tensor-core contractions over all tokens) when the shape allows
@@ -179,6 +181,12 @@ public:
                  float* hidden_host = nullptr);
     bool batched_prefill_enabled() const { return use_batched_prefill_; }
     void set_batched_prefill(bool on) { use_batched_prefill_ = on; }
+    // Operand precision of the batched prefill (Prefill::Precision; fp16 by default).
+    int prefill_precision() const { return prefill_precision_; }
+    void set_prefill_precision(int p);
+    // The layers with fp16 copies of their five matrices (made on first use), the operands of
+    // the fp16 batched prefill of this model and of its batches.
+    const std::vector<LayerWeights>& layers_f16();
     bool batched_prefill_ok(int n, int pos0) const;
     void generate(const int32_t* prompt, int n_prompt, size_t max_new, bool stop_on_eos,
                   int32_t* out, size_t* n_out, q3_generation_stats* stats);
@@ -239,6 +247,9 @@ private:
     bool use_batched_prefill_ = true;
     std::unique_ptr<Prefill> prefill_;
     DeviceBuffer prefill_ids_;
+    int prefill_precision_ = 1;  // Prefill::kPrecisionF16
+    DeviceBuffer f16_arena_;
+    std::vector<LayerWeights> layers16_;
     DeviceBuffer fused_layers_, fused_part_o_, fused_part_ml_, fused_am_, fused_sync_, fused_wperm_,
         fused_y_, fused_tagged_, fused_dbg_;
     unsigned fused_epoch_ = 0;  // tag base of the last fused launch (1..4095)

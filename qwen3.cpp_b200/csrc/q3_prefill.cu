@@ -33,7 +33,7 @@ __global__ void __launch_bounds__(kNormWarps * 32)
     rmsnorm_rows_kernel(const int32_t* __restrict__ ids, const uint16_t* __restrict__ embed,
                         float* __restrict__ x, const uint16_t* __restrict__ w, float eps,
                         uint16_t* __restrict__ out, uint16_t* __restrict__ out_lo, int rows,
-                        int dim) {
+                        int dim, int f16) {
     pdl_wait();
     pdl_trigger();
     const int lane = threadIdx.x & 31;
@@ -66,6 +66,16 @@ __global__ void __launch_bounds__(kNormWarps * 32)
         const uint2 wb = *reinterpret_cast<const uint2*>(w + i);
         const float y0 = (v.x * inv) * bf16_lo(wb.x), y1 = (v.y * inv) * bf16_hi(wb.x);
         const float y2 = (v.z * inv) * bf16_lo(wb.y), y3 = (v.w * inv) * bf16_hi(wb.y);
+        if (f16) {
+            const uint2 hi = make_uint2(pack2_f16(y0, y1), pack2_f16(y2, y3));
+            *reinterpret_cast<uint2*>(orow + i) = hi;
+            if (out_lo) {  // y - f16(y): the hi + lo pair carries 22 significant bits
+                *reinterpret_cast<uint2*>(out_lo + static_cast<size_t>(row) * dim + i) =
+                    make_uint2(pack2_f16(y0 - f16_lo(hi.x), y1 - f16_hi(hi.x)),
+                               pack2_f16(y2 - f16_lo(hi.y), y3 - f16_hi(hi.y)));
+            }
+            continue;
+        }
         const uint2 hi = make_uint2(pack2_bf16(y0, y1), pack2_bf16(y2, y3));
         *reinterpret_cast<uint2*>(orow + i) = hi;
         if (out_lo) {  // y - bf16(y): the hi + lo pair carries 16 significant bits
@@ -152,6 +162,37 @@ __global__ void __launch_bounds__(256) prefill_qkv_kernel(PrefillQkvArgs a) {
     reinterpret_cast<uint2*>(dst)[lane] = make_uint2(pack2_bf16(v.x, v.y), pack2_bf16(v.z, v.w));
 }
 
+// bf16 -> fp16 (same values in range), 8 elements per thread.
+__global__ void bf16_to_f16_kernel(const uint16_t* __restrict__ src, uint16_t* __restrict__ dst,
+                                   size_t n8) {
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n8;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const uint4 v = reinterpret_cast<const uint4*>(src)[i];
+        reinterpret_cast<uint4*>(dst)[i] =
+            make_uint4(bf16x2_to_f16x2(v.x), bf16x2_to_f16x2(v.y), bf16x2_to_f16x2(v.z),
+                       bf16x2_to_f16x2(v.w));
+    }
+}
+
+// fp16 copies of the cache rows of logical pages [0, pages) of one sequence, every layer (the
+// rows a prefill at a later position attends to but did not write itself). Block (page, layer).
+__global__ void kv_to_f16_kernel(const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
+                                 uint16_t* __restrict__ k16, uint16_t* __restrict__ v16,
+                                 const int32_t* __restrict__ table, size_t layer_elems,
+                                 int page_elems) {
+    const size_t base = static_cast<size_t>(blockIdx.y) * layer_elems +
+                        static_cast<size_t>(__ldg(table + blockIdx.x)) * page_elems;
+    for (int i = threadIdx.x; i < page_elems / 8; i += blockDim.x) {
+        const size_t e = base / 8 + i;
+        const uint4 kv = reinterpret_cast<const uint4*>(k)[e];
+        const uint4 vv = reinterpret_cast<const uint4*>(v)[e];
+        reinterpret_cast<uint4*>(k16)[e] = make_uint4(bf16x2_to_f16x2(kv.x), bf16x2_to_f16x2(kv.y),
+                                                      bf16x2_to_f16x2(kv.z), bf16x2_to_f16x2(kv.w));
+        reinterpret_cast<uint4*>(v16)[e] = make_uint4(bf16x2_to_f16x2(vv.x), bf16x2_to_f16x2(vv.y),
+                                                      bf16x2_to_f16x2(vv.z), bf16x2_to_f16x2(vv.w));
+    }
+}
+
 int device_sms(int device) {
     int n = 0;
     Q3_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device));
@@ -162,11 +203,12 @@ int device_sms(int device) {
 
 void launch_rmsnorm_rows_bf16(const int32_t* ids, const uint16_t* embed, float* x,
                               const uint16_t* w, float eps, uint16_t* out, int rows, int dim,
-                              cudaStream_t s, uint16_t* out_lo, bool dependent) {
+                              cudaStream_t s, uint16_t* out_lo, bool dependent, bool f16) {
     if (rows <= 0) return;
     if (dim % 256 != 0) throw std::invalid_argument("row RmsNorm needs a width that is a multiple of 256");
     launch_dep(dependent, rmsnorm_rows_kernel, dim3((rows + kNormWarps - 1) / kNormWarps),
-               dim3(kNormWarps * 32), 0, s, ids, embed, x, w, eps, out, out_lo, rows, dim);
+               dim3(kNormWarps * 32), 0, s, ids, embed, x, w, eps, out, out_lo, rows, dim,
+               static_cast<int>(f16));
     Q3_CUDA(cudaGetLastError());
 }
 
@@ -192,6 +234,40 @@ Prefill::Prefill(const q3_config& c, int device) : cfg_(c), device_(device) {
     Q3_CUDA(cudaMemset(err_.ptr, 0, sizeof(unsigned)));
 }
 
+void make_f16_layers(const q3_config& c, const std::vector<LayerWeights>& layers,
+                     DeviceBuffer& arena, std::vector<LayerWeights>& out, cudaStream_t s) {
+    const size_t D = c.dim, H = c.hidden_dim;
+    const size_t qkv = static_cast<size_t>(c.n_heads + 2 * c.n_kv_heads) * HD;
+    const size_t qd = static_cast<size_t>(c.n_heads) * HD;
+    const size_t per = qkv * D + D * qd + 2 * H * D + D * H;  // elements of one layer
+    arena.alloc(per * layers.size() * 2);
+    out = layers;
+    auto conv = [&](const uint16_t* src, uint16_t* dst, size_t n) {
+        if (n % 8 != 0) throw std::invalid_argument("fp16 copy: size not a multiple of 8");
+        bf16_to_f16_kernel<<<1024, 256, 0, s>>>(src, dst, n / 8);
+        Q3_CUDA(cudaGetLastError());
+    };
+    for (size_t l = 0; l < layers.size(); ++l) {
+        const LayerWeights& w = layers[l];
+        uint16_t* p = static_cast<uint16_t*>(arena.ptr) + per * l;
+        uint16_t* wqkv = p;
+        uint16_t* wo = wqkv + qkv * D;
+        uint16_t* w1 = wo + D * qd;
+        uint16_t* w3 = w1 + H * D;
+        uint16_t* w2 = w3 + H * D;
+        conv(w.wqkv, wqkv, qkv * D);
+        conv(w.wo, wo, D * qd);
+        conv(w.w1, w1, H * D);
+        conv(w.w3, w3, H * D);
+        conv(w.w2, w2, D * H);
+        out[l].wqkv = wqkv;
+        out[l].wo = wo;
+        out[l].w1 = w1;
+        out[l].w3 = w3;
+        out[l].w2 = w2;
+    }
+}
+
 void Prefill::ensure_rows(int rows) {
     if (rows <= cap_rows_) return;
     const int cap = (rows + 127) / 128 * 128;
@@ -199,6 +275,7 @@ void Prefill::ensure_rows(int rows) {
     const size_t qd = static_cast<size_t>(c.n_heads) * HD;
     x_.alloc(static_cast<size_t>(cap) * c.dim * 4);
     xn_.alloc(static_cast<size_t>(cap) * c.dim * 2);
+    xn_lo_.alloc(static_cast<size_t>(cap) * c.dim * 2);
     q_.alloc(static_cast<size_t>(cap) * qd * 2);
     o_.alloc(static_cast<size_t>(cap) * qd * 2);
     h_.alloc(static_cast<size_t>(cap) * c.hidden_dim * 2);
@@ -227,23 +304,36 @@ size_t Prefill::layer_elems(const KvView& kv) const {
 }
 
 void Prefill::ensure_kv_maps(const KvView& kv, int L) {
-    if (kv_key_ == kv.k_base && kv_pages_ == kv.n_pages) return;
+    const bool f16 = precision_ == kPrecisionF16;
+    if (kv_key_ == kv.k_base && kv_pages_ == kv.n_pages && kv_maps_f16_ == f16) return;
     const q3_config& c = cfg_;
     const uint64_t kv_rows = static_cast<uint64_t>(L) * kv.n_pages * c.n_kv_heads * kPageTokens;
-    make_tmap_bf16(&kmap_, kv.k_base, kv_rows, HD, kPageTokens);
-    make_tmap_bf16(&vmap_, kv.v_base, kv_rows, HD, kPageTokens);
+    const void* kb = kv.k_base;
+    const void* vb = kv.v_base;
+    if (f16) {
+        const size_t bytes = kv_rows * HD * 2;
+        if (k16_.bytes != bytes || kv_key_ != kv.k_base) {
+            k16_.alloc(bytes);
+            v16_.alloc(bytes);
+        }
+        kb = k16_.ptr;
+        vb = v16_.ptr;
+    }
+    make_tmap_bf16(&kmap_, kb, kv_rows, HD, kPageTokens);
+    make_tmap_bf16(&vmap_, vb, kv_rows, HD, kPageTokens);
     // The 4-D page maps serve tiles of 8 pages inside one layer; with fewer pages per layer the
     // kernel never takes that path and the 2-D maps stand in.
     if (kv.n_pages >= 8) {
         const uint64_t pages = static_cast<uint64_t>(L) * kv.n_pages;
-        make_tmap_kv_pages(&kmap4_, kv.k_base, c.n_kv_heads, pages);
-        make_tmap_kv_pages(&vmap4_, kv.v_base, c.n_kv_heads, pages);
+        make_tmap_kv_pages(&kmap4_, kb, c.n_kv_heads, pages);
+        make_tmap_kv_pages(&vmap4_, vb, c.n_kv_heads, pages);
     } else {
         kmap4_ = kmap_;
         vmap4_ = vmap_;
     }
     kv_key_ = kv.k_base;
     kv_pages_ = kv.n_pages;
+    kv_maps_f16_ = f16;
 }
 
 unsigned Prefill::read_error(cudaStream_t s) {
@@ -267,7 +357,7 @@ KvView engine_view(Engine& e) {
 
 void Prefill::run(const int32_t* ids_dev, int n, int pos0, const uint16_t* embed,
                   const std::vector<LayerWeights>& layers, const KvView& kv, float* x_last,
-                  float* taps, cudaStream_t s) {
+                  float* taps, cudaStream_t s, const std::vector<LayerWeights>* layers16) {
     const q3_config& c = cfg_;
     if (n <= 0) return;
     const int table_len = kv.table_len ? kv.table_len : kv.n_pages;
@@ -278,20 +368,36 @@ void Prefill::run(const int32_t* ids_dev, int n, int pos0, const uint16_t* embed
     const int qd = c.n_heads * HD;
     const int qkv = (c.n_heads + 2 * c.n_kv_heads) * HD;
     const int L = static_cast<int>(layers.size());
+    const bool f16 = precision_ == kPrecisionF16;
+    if (f16 && (!layers16 || layers16->size() != layers.size())) {
+        throw std::invalid_argument("fp16 prefill needs the fp16 weight copies");
+    }
     ensure_rows(std::min(n, kMaxChunk));
-    ensure_weight_maps(layers);
+    ensure_weight_maps(f16 ? *layers16 : layers);
     ensure_kv_maps(kv, L);
     float* X = static_cast<float*>(x_.ptr);
     uint16_t* Xn = static_cast<uint16_t*>(xn_.ptr);
+    uint16_t* XnLo = f16 ? static_cast<uint16_t*>(xn_lo_.ptr) : nullptr;
     unsigned* err = static_cast<unsigned*>(err_.ptr);
+    uint16_t* k16 = f16 ? static_cast<uint16_t*>(k16_.ptr) : nullptr;
+    uint16_t* v16 = f16 ? static_cast<uint16_t*>(v16_.ptr) : nullptr;
+    if (f16 && pos0 > 0) {
+        // Cache rows before this prompt (earlier prompts, decoded tokens): their fp16 copies.
+        const int pages = (pos0 + kPageTokens - 1) / kPageTokens;
+        const int page_elems = c.n_kv_heads * kPageTokens * HD;
+        kv_to_f16_kernel<<<dim3(pages, L), 256, 0, s>>>(kv.k_base, kv.v_base, k16, v16,
+                                                        kv.page_table, layer_elems(kv), page_elems);
+        Q3_CUDA(cudaGetLastError());
+    }
 
     for (int c0 = 0; c0 < n; c0 += kMaxChunk) {
         const int S = std::min(kMaxChunk, n - c0);
         const int p0 = pos0 + c0;
         const bool last = c0 + S == n;
-        CUtensorMap m_xn, m_o, m_h, m_q;
+        CUtensorMap m_xn, m_xn_lo, m_o, m_h, m_q;
         make_tmap_bf16(&m_q, q_.ptr, S, qd, 64);
         make_tmap_bf16(&m_xn, xn_.ptr, S, c.dim, 128);
+        make_tmap_bf16(&m_xn_lo, xn_lo_.ptr, S, c.dim, 128);
         make_tmap_bf16(&m_o, o_.ptr, S, qd, 128);
         make_tmap_bf16(&m_h, h_.ptr, S, c.hidden_dim, 128);
         CUtensorMap o_x, o_h;  // contraction outputs
@@ -305,7 +411,7 @@ void Prefill::run(const int32_t* ids_dev, int n, int pos0, const uint16_t* embed
             }
         };
         launch_rmsnorm_rows_bf16(ids_dev + c0, embed, X, layers[0].attn_norm, c.norm_eps, Xn, S,
-                                 c.dim, s, nullptr, true);
+                                 c.dim, s, XnLo, true, f16);
         tap(0);
         for (int l = 0; l < L; ++l) {
             const LayerWeights& w = layers[l];
@@ -313,6 +419,7 @@ void Prefill::run(const int32_t* ids_dev, int n, int pos0, const uint16_t* embed
             GemmArgs g;
             g.err = err;
             g.dependent = true;  // the prefill's kernels launch as programmatic dependents
+            g.f16 = f16 ? 1 : 0;
             g.M = S;
             // [wq; wk; wv] . xn (src/inference.cpp:795-798) with the QK-RMSNorm, RoPE and the
             // paged K/V write (:800-815) in the epilogue: q rows to q_ (bf16).
@@ -329,7 +436,18 @@ void Prefill::run(const int32_t* ids_dev, int n, int pos0, const uint16_t* embed
             g.qkv.n_heads = c.n_heads;
             g.qkv.n_kv = c.n_kv_heads;
             g.qkv.eps = c.norm_eps;
-            Q3_CUDA(launch_gemm(m_xn, wm.wqkv, nullptr, m_xn, g, kEpiQkvRope, num_sms_, s));
+            if (f16) {
+                // fp16 q for the attention, fp16 copies of the K/V rows it reads; the
+                // RmsNorm'd input as an fp16 hi + lo pair (the one input where the error of a
+                // single fp16 rounding still shows in the hidden states).
+                g.qkv.q_f16 = 1;
+                g.qkv.k_stage = k16 + layer_elems(kv) * l;
+                g.qkv.v_stage = v16 + layer_elems(kv) * l;
+                Q3_CUDA(launch_gemm(m_xn, wm.wqkv, nullptr, m_xn, g, kEpiQkvRope, num_sms_, s,
+                                    &m_xn_lo));
+            } else {
+                Q3_CUDA(launch_gemm(m_xn, wm.wqkv, nullptr, m_xn, g, kEpiQkvRope, num_sms_, s));
+            }
             g.qkv = QkvEpilogue{};
             PrefillAttnTcArgs ta{};
             ta.page_table = kv.page_table;
@@ -341,13 +459,14 @@ void Prefill::run(const int32_t* ids_dev, int n, int pos0, const uint16_t* embed
             ta.n_pages = kv.n_pages;
             ta.pages_per_seq = table_len;
             ta.layer = l;
+            ta.f16 = f16 ? 1 : 0;
             launch_prefill_attention_tc(m_q, kmap_, vmap_, kmap4_, vmap4_, ta, s);
             // x += wo . attn (:846-849).
             g.N = c.dim;
             g.K = qd;
             Q3_CUDA(launch_gemm(m_o, wm.wo, nullptr, o_x, g, kEpiAddF32, num_sms_, s));
             launch_rmsnorm_rows_bf16(nullptr, nullptr, X, w.mlp_norm, c.norm_eps, Xn, S, c.dim, s,
-                                     nullptr, true);
+                                     nullptr, true, f16);
             // h = silu(w1 . xn) * (w3 . xn) (:851, :1005-1011).
             g.N = 2 * c.hidden_dim;
             g.K = c.dim;
@@ -358,7 +477,7 @@ void Prefill::run(const int32_t* ids_dev, int n, int pos0, const uint16_t* embed
             Q3_CUDA(launch_gemm(m_h, wm.w2, nullptr, o_x, g, kEpiAddF32, num_sms_, s));
             if (l + 1 < L) {
                 launch_rmsnorm_rows_bf16(nullptr, nullptr, X, layers[l + 1].attn_norm, c.norm_eps,
-                                         Xn, S, c.dim, s, nullptr, true);
+                                         Xn, S, c.dim, s, XnLo, true, f16);
             }
             tap(l + 1);
         }

@@ -14,13 +14,14 @@
 
 namespace q3 {
 
-// Row-wise RmsNorm (src/inference.cpp:887-923) of fp32 rows into bf16 MMA operands; with ids
-// non-null, the fp32 rows are first gathered from the embedding (:601-603) into x.
-// out_lo (nullable) receives y - bf16(y), so that out + out_lo carries 16 significant bits.
-// dependent: programmatic dependent launch (launch_dep).
+// Row-wise RmsNorm (src/inference.cpp:887-923) of fp32 rows into bf16 MMA operands (fp16 with
+// f16); with ids non-null, the fp32 rows are first gathered from the embedding (:601-603) into x.
+// out_lo (nullable) receives y - out(y), so that out + out_lo carries 16 (fp16: 22) significant
+// bits. dependent: programmatic dependent launch (launch_dep).
 void launch_rmsnorm_rows_bf16(const int32_t* ids, const uint16_t* embed, float* x,
                               const uint16_t* w, float eps, uint16_t* out, int rows, int dim,
-                              cudaStream_t s, uint16_t* out_lo = nullptr, bool dependent = false);
+                              cudaStream_t s, uint16_t* out_lo = nullptr, bool dependent = false,
+                              bool f16 = false);
 
 // Per-token, per-head QK-RMSNorm + RoPE (src/inference.cpp:800-810) and bf16 K/V write into the
 // paged cache at kv_pos = pos (:812-815) for tokens at positions pos0 .. pos0+rows-1, all below
@@ -63,6 +64,9 @@ struct PrefillAttnTcArgs {
     int rows, pos0, n_kv, n_pages, layer;
     int pages_per_seq = 0;       // length of page_table (0: n_pages)
     uint16_t* out_lo = nullptr;  // optional: attention output - bf16(output)
+    // q, K, V and the probabilities are fp16 (k and v then map fp16 copies of the cache), the
+    // output is fp16 (out_lo unused).
+    int f16 = 0;
 };
 void launch_prefill_attention_tc(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
                                  const CUtensorMap& k4, const CUtensorMap& v4,
@@ -82,6 +86,12 @@ struct KvView {
 };
 KvView engine_view(Engine& e);
 
+// fp16 copies of the five matrices of every layer ([wq;wk;wv], wo, w1, w3, w2: each bf16 value
+// is an fp16 value in the range the weights take, and smaller ones round to the fp16 subnormal
+// grid), in one arena; the norm pointers are those of `layers`.
+void make_f16_layers(const q3_config& c, const std::vector<LayerWeights>& layers,
+                     DeviceBuffer& arena, std::vector<LayerWeights>& out, cudaStream_t s);
+
 // Driver of a batched prefill over the layers of a Model.
 class Prefill {
 public:
@@ -98,14 +108,26 @@ public:
     // writing each layer's K/V rows into the engine's cache, and leaves the hidden state of the
     // last token in x_last (fp32 [dim]). taps (nullable) receive the last token's hidden state
     // before the first layer and after every layer ([(n_layers+1) * dim]).
+    // layers16: the same layers with the five matrices ([wq;wk;wv], wo, w1, w3, w2) as fp16
+    // copies (the norms as in `layers`); required in the fp16 precision.
     void run(const int32_t* ids_dev, int n, int pos0, const uint16_t* embed,
              const std::vector<LayerWeights>& layers, const KvView& kv, float* x_last,
-             float* taps, cudaStream_t s);
+             float* taps, cudaStream_t s, const std::vector<LayerWeights>* layers16 = nullptr);
+
+    // Operand precision of the contractions and the attention. kPrecisionF16 (the default):
+    // fp16 weights (exact copies of the bf16 values) and fp16 activations, the [wq;wk;wv] input
+    // as an fp16 hi + lo pair (two MMAs), the attention on fp16 copies of the cache rows (the
+    // same bf16 values); fp32 accumulation throughout. kPrecisionBF16: bf16 activations (one bf16
+    // rounding per operand: 8 significant bits against fp16's 11).
+    enum Precision : int { kPrecisionBF16 = 0, kPrecisionF16 = 1 };
+    void set_precision(int p) { precision_ = p; }
+    int precision() const { return precision_; }
     // Non-zero when a contraction's bounded wait gave up in the last run.
     unsigned read_error(cudaStream_t s);
     // Attention kernel: tcgen05 (default) or the mma.sync flash-attention kernel.
 
-    // TMA maps of the paged caches (2-D rows and 4-D page boxes) for a view; cached.
+    // TMA maps of the paged caches (2-D rows and 4-D page boxes) for a view, over the cache
+    // itself (bf16 precision) or over its fp16 copy (allocated here on first use); cached.
     void ensure_kv_maps(const KvView& kv, int n_layers);
     const CUtensorMap& kmap() const { return kmap_; }
     const CUtensorMap& vmap() const { return vmap_; }
@@ -123,7 +145,12 @@ private:
     int device_ = 0;
     int num_sms_ = 148;
     int cap_rows_ = 0;
-    DeviceBuffer x_, xn_, q_, o_, h_, err_;
+    int precision_ = kPrecisionF16;
+    DeviceBuffer x_, xn_, xn_lo_, q_, o_, h_, err_;
+    // fp16 copies of the K/V rows of the cache this driver serves ([n_layers] x the view's
+    // layout), the operands of the fp16 attention.
+    DeviceBuffer k16_, v16_;
+    bool kv_maps_f16_ = false;
     struct LayerMaps {
         CUtensorMap wqkv, wo, w1, w3, w2;
     };

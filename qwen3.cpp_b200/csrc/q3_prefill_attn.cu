@@ -365,8 +365,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     } else if (warp == 1) {
         if (lane == 0) {
             // ------------------------------------------------------------ MMA issuer
-            const uint32_t idesc_s = idesc_bf16_f32(ROWS, KEYS);
-            const uint32_t idesc_pv = idesc_bf16_f32(ROWS, HD) | (1u << 16);  // B MN-major
+            const uint32_t idesc_s = a.f16 ? idesc_f16_f32(ROWS, KEYS) : idesc_bf16_f32(ROWS, KEYS);
+            const uint32_t idesc_pv =
+                (a.f16 ? idesc_f16_f32(ROWS, HD) : idesc_bf16_f32(ROWS, HD)) | (1u << 16);  // B MN-major
             const uint32_t q_addr = smem_u32(sm + Q_OFF);
             bool ok = mbar_wait(q_full, 0, a.budget, abort);
             if (!ok) fail(abort, a.err, 13);
@@ -495,14 +496,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             for (int k = 0; k < 64; k += 2) s4[(k >> 1) & 3] = fadd2(s4[(k >> 1) & 3], make_float2(sv[k], sv[k + 1]));
             const float2 s2 = fadd2(fadd2(s4[0], s4[1]), fadd2(s4[2], s4[3]));
             sum = s2.x + s2.y;
+            if (a.f16) {
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                const int chunk = q ^ (r & 7);
-                *reinterpret_cast<uint4*>(prow + chunk * 16) =
-                    make_uint4(pack_bf16x2(sv[8 * q], sv[8 * q + 1]),
-                               pack_bf16x2(sv[8 * q + 2], sv[8 * q + 3]),
-                               pack_bf16x2(sv[8 * q + 4], sv[8 * q + 5]),
-                               pack_bf16x2(sv[8 * q + 6], sv[8 * q + 7]));
+                for (int q = 0; q < 8; ++q) {
+                    const int chunk = q ^ (r & 7);
+                    *reinterpret_cast<uint4*>(prow + chunk * 16) =
+                        make_uint4(pack2_f16(sv[8 * q], sv[8 * q + 1]),
+                                   pack2_f16(sv[8 * q + 2], sv[8 * q + 3]),
+                                   pack2_f16(sv[8 * q + 4], sv[8 * q + 5]),
+                                   pack2_f16(sv[8 * q + 6], sv[8 * q + 7]));
+                }
+            } else {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const int chunk = q ^ (r & 7);
+                    *reinterpret_cast<uint4*>(prow + chunk * 16) =
+                        make_uint4(pack_bf16x2(sv[8 * q], sv[8 * q + 1]),
+                                   pack_bf16x2(sv[8 * q + 2], sv[8 * q + 3]),
+                                   pack_bf16x2(sv[8 * q + 4], sv[8 * q + 5]),
+                                   pack_bf16x2(sv[8 * q + 6], sv[8 * q + 7]));
+                }
             }
             tc_fence_before();
             fence_proxy_async_smem();
@@ -545,6 +558,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         float y[8];
 #pragma unroll
                         for (int k = 0; k < 8; ++k) y[k] = acc[8 * i + k] * inv;
+                        if (a.f16) {
+                            dst[i] = make_uint4(pack2_f16(y[0], y[1]), pack2_f16(y[2], y[3]),
+                                                pack2_f16(y[4], y[5]), pack2_f16(y[6], y[7]));
+                            continue;
+                        }
                         const uint4 hi = make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]),
                                                     pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7]));
                         dst[i] = hi;

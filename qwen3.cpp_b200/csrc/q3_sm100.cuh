@@ -131,6 +131,13 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
            | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16
 }
 
+// As idesc_bf16_f32 with fp16 A and B operands (kind::f16 takes both of one type).
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n) {
+    return (1u << 4)                                  // D format f32
+           | (static_cast<uint32_t>(n >> 3) << 17)    // N / 8
+           | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16 (A, B format 0: f16)
+}
+
 // D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread.
 __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                          uint32_t idesc, uint32_t accumulate) {

@@ -98,12 +98,17 @@ def lib() -> C.CDLL:
         "q3_forward_token": [vp, i32, C.c_int, vp],
         "q3_forward_token_ref": [vp, i32, C.c_int, C.POINTER(C.POINTER(C.c_float))],
         "q3_forward_token_layers": [vp, i32, C.c_int, vp, vp],
+        "q3_forward_token_greedy": [vp, i32, C.c_int, C.POINTER(C.POINTER(C.c_float)),
+                                    C.POINTER(C.c_int32)],
         "q3_kv_row": [vp, C.c_int, C.c_int, U16P, U16P],
         "q3_prefill": [vp, I32P, C.c_int, C.c_int, vp, vp],
         "q3_prefill_layers": [vp, I32P, C.c_int, C.c_int, vp, vp, vp],
         "q3_model_set_prefill_path": [vp, C.c_int],
         "q3_model_prefill_path": [vp, C.POINTER(C.c_int)],
+        "q3_model_set_prefill_precision": [vp, C.c_int],
+        "q3_model_prefill_precision": [vp, C.POINTER(C.c_int)],
         "q3_gemm_bf16": [vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, vp],
+        "q3_gemm_f16": [vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, vp],
         "q3_batch_create": [vp, C.c_int, C.c_int, C.POINTER(vp)],
         "q3_batch_add": [vp, I32P, C.c_int, C.POINTER(C.c_int), vp, vp],
         "q3_batch_size": [vp, C.POINTER(C.c_int)],
@@ -254,6 +259,17 @@ class Qwen3:
         view.flags.writeable = False
         return view
 
+    def forward_token_greedy(self, token: int, pos: int):
+        """ForwardToken + Sampler::Greedy: (read-only view of the model's pinned logits buffer,
+        valid until the next call; the greedy token computed on the device)."""
+        ptr = C.POINTER(C.c_float)()
+        nxt = C.c_int32()
+        check(lib().q3_forward_token_greedy(self._h, int(token), int(pos), C.byref(ptr),
+                                            C.byref(nxt)))
+        view = np.ctypeslib.as_array(ptr, shape=(self.config["vocab_size"],))
+        view.flags.writeable = False
+        return view, int(nxt.value)
+
     def forward_token_layers(self, token: int, pos: int):
         c = self.config
         hid = np.empty((c["n_layers"] + 1, c["dim"]), np.float32)
@@ -299,6 +315,18 @@ class Qwen3:
     @prefill_path.setter
     def prefill_path(self, path: int) -> None:
         check(lib().q3_model_set_prefill_path(self._h, int(path)))
+
+    PREFILL_BF16, PREFILL_F16 = 0, 1
+
+    @property
+    def prefill_precision(self) -> int:
+        p = C.c_int()
+        check(lib().q3_model_prefill_precision(self._h, C.byref(p)))
+        return p.value
+
+    @prefill_precision.setter
+    def prefill_precision(self, precision: int) -> None:
+        check(lib().q3_model_set_prefill_precision(self._h, int(precision)))
 
     def decode_greedy(self, first_token: int, pos0: int, n_steps: int, want_logits=False):
         toks = np.empty(max(n_steps, 1), np.int32)
@@ -540,3 +568,8 @@ GEMM_STORE_F32, GEMM_ADD_F32, GEMM_SWIGLU, GEMM_STORE_BF16 = 0, 1, 2, 3
 def gemm_bf16(out: int, a: int, w: int, w3, M: int, N: int, K: int, epilogue: int, stream=None):
     """q3_gemm_bf16 on device pointers: out[M, N] = epilogue(A[M, K] . W[N, K]^T)."""
     check(lib().q3_gemm_bf16(out, a, w, w3, M, N, K, epilogue, stream))
+
+
+def gemm_f16(out: int, a: int, w: int, w3, M: int, N: int, K: int, epilogue: int, stream=None):
+    """q3_gemm_f16: as gemm_bf16 with fp16 operands (and fp16 SwiGLU / 16-bit stores)."""
+    check(lib().q3_gemm_f16(out, a, w, w3, M, N, K, epilogue, stream))

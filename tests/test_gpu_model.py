@@ -31,7 +31,7 @@ def models(request, q3lib, full_weights, cpu_model):
     gpu = q3lib.Qwen3(full_weights, 512)
     gpu.decode_path = gpu.PATH_FUSED if request.param == "fused" else gpu.PATH_LAYERWISE
     # These tests check the decode paths token for token against the oracle's free-running
-    # greedy run; the batched (bf16-operand) prefill has its own tests in test_gpu_prefill.py.
+    # greedy run; the batched tensor-core prefill has its own tests in test_gpu_prefill.py.
     gpu.prefill_path = gpu.PREFILL_TOKENWISE
     assert gpu.decode_path == (gpu.PATH_FUSED if request.param == "fused" else gpu.PATH_LAYERWISE)
     yield gpu, cpu_model
@@ -141,7 +141,7 @@ def test_forward_token_ref_matches_copy(models, oracle_run):
     """The zero-copy ForwardToken returns the same logits as the copying one, in a read-only
     view of the model's buffer that the next call overwrites (the reference's const reference)."""
     gpu, _ = models
-    seq, _, _ = oracle_run
+    seq, _, logits = oracle_run
     gpu.reset()
     for pos in range(4):
         gpu.forward_token(int(seq[pos]), pos)
@@ -155,6 +155,12 @@ def test_forward_token_ref_matches_copy(models, oracle_run):
     first = view.copy()
     gpu.forward_token_ref(int(seq[5]), 5)
     assert not np.array_equal(view, first)  # the buffer now holds the next position's logits
+    # ForwardToken + Greedy: the same logits and their first maximum, computed on the device.
+    gpu.reset()
+    for pos in range(6):
+        lg, nxt = gpu.forward_token_greedy(int(seq[pos]), pos)
+        assert nxt == int(np.argmax(lg))
+    assert np.abs(lg - logits[5]).max() <= LOGITS_MAX_ABS
 
 
 def test_interleaved_launches(models, oracle_run):

@@ -90,6 +90,49 @@ def test_gemm_swiglu(q3lib):
     assert float(((got - ref).abs() / (ref.abs() + 1e-3 * scale)).max()) < 2 ** -7
 
 
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 1024), (300, 4096, 1024), (2048, 1024, 2048)])
+def test_gemm_f16_store_f32(q3lib, M, N, K):
+    """fp16 operands (the default prefill's) against a float64 product of the same values."""
+    import torch
+    g = torch.Generator().manual_seed(M * 5 + N + K)
+    a = torch.randn(M, K, generator=g).half()
+    w = (torch.randn(N, K, generator=g) * 0.02).half()
+    ref = a.double() @ w.double().T
+    da, dw = a.cuda(), w.cuda()
+    out = torch.full((M, N), float("nan"), device="cuda")
+    q3lib.gemm_f16(out.data_ptr(), da.data_ptr(), dw.data_ptr(), None, M, N, K,
+                   q3lib.GEMM_STORE_F32, torch.cuda.current_stream().cuda_stream)
+    got = out.cpu().double()
+    assert torch.isfinite(got).all()
+    assert float((got - ref).abs().max() / ref.abs().max()) < GEMM_REL
+
+
+def test_gemm_f16_swiglu_and_store(q3lib):
+    """fp16 SwiGLU output (one fp16 rounding) and the 16-bit store epilogue in fp16."""
+    import torch
+    M, N, K = 200, 3072, 1024
+    g = torch.Generator().manual_seed(8)
+    a = torch.randn(M, K, generator=g).half()
+    w1 = (torch.randn(N, K, generator=g) * 0.05).half()
+    w3 = (torch.randn(N, K, generator=g) * 0.05).half()
+    g1 = a.double() @ w1.double().T
+    g3 = a.double() @ w3.double().T
+    ref = g1 / (1.0 + torch.exp(-g1)) * g3
+    out = torch.empty(M, N, dtype=torch.float16, device="cuda")
+    da, d1, d3 = a.cuda(), w1.cuda(), w3.cuda()
+    s = torch.cuda.current_stream().cuda_stream
+    q3lib.gemm_f16(out.data_ptr(), da.data_ptr(), d1.data_ptr(), d3.data_ptr(), M, N, K,
+                   q3lib.GEMM_SWIGLU, s)
+    got = out.cpu().double()
+    scale = ref.abs().max()
+    assert float(((got - ref).abs() / (ref.abs() + 1e-3 * scale)).max()) < 2 ** -10
+    o16 = torch.empty(M, N, dtype=torch.float16, device="cuda")
+    q3lib.gemm_f16(o16.data_ptr(), da.data_ptr(), d1.data_ptr(), None, M, N, K,
+                   q3lib.GEMM_STORE_BF16, s)
+    got = o16.cpu().double()
+    assert float(((got - g1).abs() / (g1.abs() + 1e-3 * g1.abs().max())).max()) < 2 ** -10
+
+
 def test_gemm_rejects_bad_shapes(q3lib):
     with pytest.raises(q3lib.InvalidArgument):
         q3lib.gemm_bf16(16, 16, 16, None, 4, 1024, 100, q3lib.GEMM_STORE_F32)
@@ -114,11 +157,18 @@ def oracle_prompt100(full_weights, prompt100):
     return h, lg, kv
 
 
-def test_batched_prefill_matches_oracle(q3lib, full_weights, prompt100, oracle_prompt100):
+@pytest.mark.parametrize("precision", ["f16", "bf16"])
+def test_batched_prefill_matches_oracle(q3lib, full_weights, prompt100, oracle_prompt100,
+                                        precision):
+    """Both operand precisions keep the last token's hidden states, logits and the KV rows within
+    the tolerances (fp16, the default, also keeps decode after long prompts at >= 99% top-1:
+    test_gpu_long.py)."""
     ho, lo, kvo = oracle_prompt100
     m = q3lib.Qwen3(full_weights, 512)
     try:
         assert m.prefill_path == m.PREFILL_BATCHED
+        assert m.prefill_precision == m.PREFILL_F16
+        m.prefill_precision = m.PREFILL_F16 if precision == "f16" else m.PREFILL_BF16
         h, lg, nxt = m.prefill_layers(prompt100, 0)
         for l in range(h.shape[0]):
             assert rel_l2(h[l], ho[l]) <= HIDDEN_REL_L2, (l, rel_l2(h[l], ho[l]))
@@ -164,6 +214,38 @@ def test_decode_after_batched_prefill(q3lib, full_weights):
             assert err <= LOGITS_MAX_ABS, (path, err)
     finally:
         m.close()
+
+
+def test_prefill_continuation_after_decode(q3lib, full_weights):
+    """A batched prefill at pos0 > 0 attends to rows that earlier prefills and decode steps wrote
+    (the fp16 precision reads fp16 copies of them, made at the call): prompt, decoded tokens, a
+    second prompt, more decode steps, all against the oracle on the same tokens."""
+    rng = np.random.default_rng(13)
+    p1 = rng.integers(0, 151936, 300).astype(np.int32)
+    d1 = rng.integers(0, 151936, 40).astype(np.int32)
+    p2 = rng.integers(0, 151936, 200).astype(np.int32)
+    d2 = rng.integers(0, 151936, 224).astype(np.int32)
+    seq = np.concatenate([p1, d1, p2, d2])
+    want = np.zeros(seq.size, bool)
+    a = len(p1) + len(d1) + len(p2)
+    want[a - 1:] = True
+    r = oracle.PortModel(full_weights, 1024).forward_many(seq, 0, want=want, logits=True)
+    ref_am, ref_lg = r["argmax"][a - 1:], r["logits"]
+    m = q3lib.Qwen3(full_weights, 1024)
+    try:
+        m.prefill(p1, 0, want_logits=False)
+        m.decode_forced(d1, len(p1))
+        lg_p, nxt = m.prefill(p2, len(p1) + len(d1))
+        am, lg = m.decode_forced(d2, a, want_logits=True)
+    finally:
+        m.close()
+    ours = np.concatenate([[nxt], am])
+    agree = float((ours == ref_am).mean())
+    err = max(float(np.abs(lg_p - ref_lg[0]).max()), float(np.abs(lg - ref_lg[1:]).max()))
+    print(f"\n[parity] prefill continuation after decode: positions={ours.size}, agree={agree}, "
+          f"flips={int((ours != ref_am).sum())}, logits_max_abs={err}")
+    assert agree >= TOP1_AGREEMENT, agree
+    assert err <= LOGITS_MAX_ABS, err
 
 
 def test_batched_and_tokenwise_prefill_agree_chunked(q3lib, full_weights):
