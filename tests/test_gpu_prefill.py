@@ -4,8 +4,9 @@
   operands, for every epilogue, at the prefill shapes and ragged row counts.
 * The whole batched prefill against the oracle: per-layer hidden state of the last prompt token
   rel-L2 <= 1e-2, its logits max-abs <= 5e-2, KV rows rel-L2 <= 1e-2, and teacher-forced top-1
-  agreement >= 99% for decode steps that read the batched cache (224 positions per decode path)
-  and for Generate (200 generated tokens).
+  agreement >= 99% for decode steps that read the batched cache (992 positions per decode path,
+  about a thousand per check so that the 1% bound is not decided by one or two near ties of the
+  random-init model's logits) and for Generate (960 generated tokens).
 """
 import numpy as np
 import pytest
@@ -189,23 +190,24 @@ def test_batched_prefill_matches_oracle(q3lib, full_weights, prompt100, oracle_p
 
 
 def test_decode_after_batched_prefill(q3lib, full_weights):
-    """Teacher-forced decode (224 positions per decode path) over the cache a batched prefill
-    wrote."""
+    """Teacher-forced decode (992 positions per decode path, logits checked on the first 224)
+    over the cache a batched prefill of 32 tokens wrote."""
     rng = np.random.default_rng(0)
-    seq = rng.integers(0, 151936, 256).astype(np.int32)
-    cpu = oracle.PortModel(full_weights, 512)
-    want = np.zeros(seq.size, bool)
-    want[31:] = True
-    r = cpu.forward_many(seq, 0, want=want, logits=True)
-    ref_am, ref_lg = r["argmax"][31:], r["logits"]
-    m = q3lib.Qwen3(full_weights, 512)
+    seq = rng.integers(0, 151936, 1024).astype(np.int32)
+    cpu = oracle.PortModel(full_weights, 1024)
+    head = cpu.forward_many(seq[:256], 0, want=np.arange(256) >= 31, logits=True)
+    rest = cpu.forward_many(seq[256:], 256)
+    ref_am = np.concatenate([head["argmax"][31:], rest["argmax"]])
+    ref_lg = head["logits"]
+    m = q3lib.Qwen3(full_weights, 1024)
     try:
         for path in (m.PATH_FUSED, m.PATH_LAYERWISE):
             m.decode_path = path
             m.reset()
             _, nxt = m.prefill(seq[:32], 0)
-            am, lg = m.decode_forced(seq[32:], 32, want_logits=True)
-            ours = np.concatenate([[nxt], am])
+            am_a, lg = m.decode_forced(seq[32:256], 32, want_logits=True)
+            am_b, _ = m.decode_forced(seq[256:], 256)
+            ours = np.concatenate([[nxt], am_a, am_b])
             agree = float((ours == ref_am).mean())
             err = float(np.abs(lg - ref_lg[1:]).max())
             print(f"\n[parity] decode after batched prefill (path {path}): positions={ours.size}, "
@@ -224,22 +226,24 @@ def test_prefill_continuation_after_decode(q3lib, full_weights):
     p1 = rng.integers(0, 151936, 300).astype(np.int32)
     d1 = rng.integers(0, 151936, 40).astype(np.int32)
     p2 = rng.integers(0, 151936, 200).astype(np.int32)
-    d2 = rng.integers(0, 151936, 224).astype(np.int32)
+    d2 = rng.integers(0, 151936, 960).astype(np.int32)
     seq = np.concatenate([p1, d1, p2, d2])
-    want = np.zeros(seq.size, bool)
     a = len(p1) + len(d1) + len(p2)
-    want[a - 1:] = True
-    r = oracle.PortModel(full_weights, 1024).forward_many(seq, 0, want=want, logits=True)
-    ref_am, ref_lg = r["argmax"][a - 1:], r["logits"]
-    m = q3lib.Qwen3(full_weights, 1024)
+    cpu = oracle.PortModel(full_weights, 2048)
+    head = cpu.forward_many(seq[:a + 128], 0, want=np.arange(a + 128) >= a - 1, logits=True)
+    rest = cpu.forward_many(seq[a + 128:], a + 128)
+    ref_am = np.concatenate([head["argmax"][a - 1:], rest["argmax"]])
+    ref_lg = head["logits"]
+    m = q3lib.Qwen3(full_weights, 2048)
     try:
         m.prefill(p1, 0, want_logits=False)
         m.decode_forced(d1, len(p1))
         lg_p, nxt = m.prefill(p2, len(p1) + len(d1))
-        am, lg = m.decode_forced(d2, a, want_logits=True)
+        am_a, lg = m.decode_forced(d2[:128], a, want_logits=True)
+        am_b, _ = m.decode_forced(d2[128:], a + 128)
     finally:
         m.close()
-    ours = np.concatenate([[nxt], am])
+    ours = np.concatenate([[nxt], am_a, am_b])
     agree = float((ours == ref_am).mean())
     err = max(float(np.abs(lg_p - ref_lg[0]).max()), float(np.abs(lg - ref_lg[1:]).max()))
     print(f"\n[parity] prefill continuation after decode: positions={ours.size}, agree={agree}, "
@@ -289,19 +293,19 @@ def test_prompt_past_context_falls_back(q3lib, full_weights):
 
 
 def test_generate_with_batched_prefill(q3lib, full_weights):
-    """Generate's 200 tokens, each checked against the oracle's argmax given the same history."""
+    """Generate's 960 tokens, each checked against the oracle's argmax given the same history."""
     rng = np.random.default_rng(21)
     prompt = rng.integers(0, 151936, 48).astype(np.int32)
-    m = q3lib.Qwen3(full_weights, 512)
+    m = q3lib.Qwen3(full_weights, 1024)
     try:
-        toks, st = m.generate(prompt, 200, stop_on_eos=False)
+        toks, st = m.generate(prompt, 960, stop_on_eos=False)
     finally:
         m.close()
-    assert st["prompt_tokens"] == 48 and st["generated_tokens"] == 200
+    assert st["prompt_tokens"] == 48 and st["generated_tokens"] == 960
     seq = np.concatenate([prompt, toks]).astype(np.int32)
-    want = np.zeros(seq.size, bool)
-    want[len(prompt) - 1:-1] = True
-    ref = oracle.PortModel(full_weights, 512).forward_many(seq[:-1], 0, want=want[:-1])["argmax"]
+    want = np.zeros(seq.size - 1, bool)
+    want[len(prompt) - 1:] = True
+    ref = oracle.PortModel(full_weights, 1024).forward_many(seq[:-1], 0, want=want)["argmax"]
     ref = ref[len(prompt) - 1:]
     agree = float((ref == toks).mean())
     print(f"\n[parity] generate after batched prefill: positions={toks.size}, agree={agree}, "
