@@ -213,6 +213,17 @@ void q3_batch_free(q3_batch* batch);
  * last_logits_host (nullable, vocab_size floats) the prompt's last logits. */
 q3_status q3_batch_add(q3_batch* batch, const int32_t* ids_host, int n, int* slot,
                        int32_t* next_token_host, float* last_logits_host);
+/* Adds n_seqs sequences at once: prompt i is the next lens_host[i] tokens of ids_host (the
+ * prompts back to back). Prompts of up to 4096 tokens are prefilled together, one tensor-core
+ * pass over the tokens of all of them per 4096-token chunk, each token's K/V written into its own
+ * sequence's pages (the data-parallel configuration's many prompts); longer prompts are
+ * prefilled one by one. *first_slot receives the slot of the first (the others follow);
+ * next_tokens_host[n_seqs] and last_logits_host[n_seqs][vocab] (both nullable) as
+ * q3_batch_add's. (The reference prefills one sequence, token by token:
+ * src/inference.cpp:669-671.) */
+q3_status q3_batch_add_many(q3_batch* batch, const int32_t* ids_host, const int* lens_host,
+                            int n_seqs, int* first_slot, int32_t* next_tokens_host,
+                            float* last_logits_host);
 q3_status q3_batch_size(const q3_batch* batch, int* n_seqs);
 /* The batch's CUDA stream (cudaStream_t) for callers that order or time work against it. */
 q3_status q3_batch_stream(q3_batch* batch, void** stream);

@@ -133,6 +133,7 @@ Batch::Batch(Model& model, int max_seqs, int max_tokens)
     for (int i = 0; i < pool_pages_; ++i) table[i] = i;  // slot s owns pages [s*pps, (s+1)*pps)
     table_.alloc(table.size() * 4);
     Q3_CUDA(cudaMemcpy(table_.ptr, table.data(), table.size() * 4, cudaMemcpyHostToDevice));
+    table_host_ = table;
     rope_len_ = max_tokens + 1;
     const auto rt = rope_table_host(c.rope_theta, c.rotary_dim, rope_len_);
     rope_.alloc(rt.size() * sizeof(float2));
@@ -218,6 +219,117 @@ int Batch::add(const int32_t* ids, int n, int32_t* next_token, float* last_logit
     next_.push_back(nt);
     if (next_token) *next_token = nt;
     return slot;
+}
+
+int Batch::add_many(const int32_t* ids, const int* lens, int n_seqs, int32_t* next_tokens,
+                    float* last_logits) {
+    const q3_config& c = cfg_;
+    if (!ids || !lens || n_seqs <= 0) throw std::invalid_argument("add_many needs sequences");
+    if (size() + n_seqs > max_seqs_) throw std::out_of_range("the batch is full");
+    std::vector<int> off(n_seqs), len(n_seqs), toff(n_seqs);
+    size_t total = 0;
+    for (int i = 0; i < n_seqs; ++i) {
+        if (lens[i] <= 0) throw std::invalid_argument("a sequence needs at least one prompt token");
+        if (lens[i] > max_tokens_) {
+            throw std::out_of_range("prompt longer than the batch's sequence capacity");
+        }
+        off[i] = static_cast<int>(total);
+        len[i] = lens[i];
+        toff[i] = (size() + i) * pps_;
+        total += lens[i];
+    }
+    for (size_t i = 0; i < total; ++i) {
+        if (ids[i] < 0 || ids[i] >= c.vocab_size) {
+            throw std::out_of_range("Token id is outside the vocabulary");
+        }
+    }
+    const int slot0 = size();
+    if (ids_.bytes < total * 4) {
+        Q3_CUDA(cudaStreamSynchronize(s_));
+        ids_.alloc(total * 4);
+    }
+    Q3_CUDA(cudaMemcpyAsync(ids_.ptr, ids, total * 4, cudaMemcpyHostToDevice, s_));
+    KvView kv;
+    kv.k_base = static_cast<uint16_t*>(k_.ptr);
+    kv.v_base = static_cast<uint16_t*>(v_.ptr);
+    kv.n_pages = pool_pages_;
+    kv.page_table = static_cast<const int32_t*>(table_.ptr);
+    kv.rope = static_cast<const float2*>(rope_.ptr);
+    kv.rope_len = rope_len_;
+    kv.table_len = pps_;
+    std::vector<LayerWeights> layers(c.n_layers);
+    for (int l = 0; l < c.n_layers; ++l) layers[l] = m_.layer(l);
+    prefill_->set_precision(m_.prefill_precision());
+    const std::vector<LayerWeights>* l16 =
+        m_.prefill_precision() == Prefill::kPrecisionF16 ? &m_.layers_f16() : nullptr;
+    DeviceBuffer xl;
+    xl.alloc(static_cast<size_t>(n_seqs) * c.dim * 4);
+    float* XL = static_cast<float*>(xl.ptr);
+    // Prompts that fit one chunk go through the varlen pass, in runs of consecutive ones; their
+    // last hidden states land in XL at their own index.
+    std::vector<int> vo, vl, vt, vi;
+    auto flush = [&] {
+        if (vo.empty()) return;
+        DeviceBuffer xs;
+        xs.alloc(vo.size() * c.dim * 4);
+        prefill_->run_varlen(static_cast<const int32_t*>(ids_.ptr), vo, vl, vt, table_host_.data(),
+                             m_.embed(), layers, kv, static_cast<float*>(xs.ptr), s_, l16);
+        for (size_t j = 0; j < vi.size(); ++j) {
+            Q3_CUDA(cudaMemcpyAsync(XL + static_cast<size_t>(vi[j]) * c.dim,
+                                    static_cast<float*>(xs.ptr) + j * c.dim, c.dim * 4,
+                                    cudaMemcpyDeviceToDevice, s_));
+        }
+        Q3_CUDA(cudaStreamSynchronize(s_));
+        vo.clear();
+        vl.clear();
+        vt.clear();
+        vi.clear();
+    };
+    for (int i = 0; i < n_seqs; ++i) {
+        if (len[i] <= Prefill::kMaxChunk) {
+            vo.push_back(off[i]);
+            vl.push_back(len[i]);
+            vt.push_back(toff[i]);
+            vi.push_back(i);
+            continue;
+        }
+        flush();
+        KvView one = kv;
+        one.page_table = static_cast<const int32_t*>(table_.ptr) + toff[i];
+        prefill_->run(static_cast<const int32_t*>(ids_.ptr) + off[i], len[i], 0, m_.embed(),
+                      layers, one, XL + static_cast<size_t>(i) * c.dim, nullptr, s_, l16);
+    }
+    flush();
+    // Final RmsNorm + tied lm_head and Greedy of each prompt's last token (src/inference.cpp:
+    // 619-635, :703-709).
+    DeviceBuffer lg, am;
+    lg.alloc(static_cast<size_t>(c.vocab_size) * 4);
+    am.alloc(static_cast<size_t>(n_seqs) * 4);
+    for (int i = 0; i < n_seqs; ++i) {
+        launch_gemv(kEpiStore, m_.output(), nullptr, XL + static_cast<size_t>(i) * c.dim,
+                    m_.final_norm(), c.norm_eps, static_cast<float*>(lg.ptr), nullptr,
+                    c.vocab_size, c.dim, nullptr, gemv_grid(c.vocab_size), s_);
+        launch_argmax_full(static_cast<const float*>(lg.ptr), c.vocab_size,
+                           static_cast<int32_t*>(am.ptr) + i, s_);
+        if (last_logits) {
+            Q3_CUDA(cudaMemcpyAsync(last_logits + static_cast<size_t>(i) * c.vocab_size, lg.ptr,
+                                    lg.bytes, cudaMemcpyDeviceToHost, s_));
+        }
+    }
+    std::vector<int32_t> nt(n_seqs);
+    Q3_CUDA(cudaMemcpyAsync(nt.data(), am.ptr, static_cast<size_t>(n_seqs) * 4,
+                            cudaMemcpyDeviceToHost, s_));
+    Q3_CUDA(cudaStreamSynchronize(s_));
+    if (const unsigned e = prefill_->read_error(s_)) {
+        throw DeviceTimeout("batched prefill: a tensor-core pipeline wait gave up (code " +
+                            std::to_string(e) + ")");
+    }
+    for (int i = 0; i < n_seqs; ++i) {
+        len_.push_back(len[i]);
+        next_.push_back(nt[i]);
+        if (next_tokens) next_tokens[i] = nt[i];
+    }
+    return slot0;
 }
 
 void Batch::ensure_step_buffers() {

@@ -29,6 +29,13 @@ public:
     // Returns the slot; *next_token (nullable) receives the greedy token after the prompt,
     // last_logits (nullable, host) its logits.
     int add(const int32_t* ids_host, int n, int32_t* next_token, float* last_logits);
+    // Adds n_seqs sequences at once: prompt i is lens[i] tokens of ids_host (the prompts back to
+    // back). Prompts of up to 4096 tokens are prefilled together (one tensor-core pass over all
+    // their tokens per 4096-token chunk, Prefill::run_varlen), longer ones one by one. Returns the
+    // slot of the first; next_tokens[n_seqs] (nullable) and last_logits[n_seqs][vocab] (nullable,
+    // host) as add's.
+    int add_many(const int32_t* ids_host, const int* lens, int n_seqs, int32_t* next_tokens,
+                 float* last_logits);
     int size() const { return static_cast<int>(len_.size()); }
     cudaStream_t stream() const { return s_; }
     int length(int slot) const { return len_.at(slot); }
@@ -61,6 +68,7 @@ private:
     int rope_len_ = 0;
     int cap_rows_ = 0;  // rows the step buffers and maps were built for
     int log_cap_ = 0;
+    std::vector<int32_t> table_host_;  // the page table (slot s owns pages [s*pps, (s+1)*pps))
     std::vector<int> len_;             // positions filled per sequence
     std::vector<int32_t> next_;        // token each sequence feeds next
     PinnedBuffer pinned_;

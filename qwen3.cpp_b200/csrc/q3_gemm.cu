@@ -319,7 +319,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const QkvEpilogue& e = args.qkv;
                 const int token = y + lane;
                 const bool live = token < args.M;
-                const int pos = e.pos0 + token;
+                const int pos = e.tok_pos ? (live ? __ldg(e.tok_pos + token) : 0) : e.pos0 + token;
                 const int nq = e.n_heads, nk = e.n_kv;
 #pragma unroll 1
                 for (int hh = 0; hh < 2; ++hh) {
@@ -347,8 +347,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                             dst = e.q_out + static_cast<size_t>(token) * nq * 128 + head * 128;
                         } else {
                             const int g = qk ? head - nq : head - nq - nk;
-                            const size_t page = static_cast<size_t>(__ldg(e.page_table + pos / 16));
-                            const size_t off = ((page * nk + g) * 16 + pos % 16) * 128;
+                            const int crow = e.tok_row ? __ldg(e.tok_row + token)
+                                                       : __ldg(e.page_table + pos / 16) * 16 + pos % 16;
+                            const size_t page = static_cast<size_t>(crow / 16);
+                            const size_t off = ((page * nk + g) * 16 + crow % 16) * 128;
                             dst = (qk ? e.k_cache : e.v_cache) + off;
                             uint16_t* st = qk ? e.k_stage : e.v_stage;
                             if (st) dst16 = st + off;
@@ -622,7 +624,9 @@ cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtens
     if ((bn != 128 && bn != 256) || args.N % bn != 0) return cudaErrorInvalidValue;
     if (epi == kEpiSwiGLU && (!b2 || bn != 256)) return cudaErrorInvalidValue;
     if (epi == kEpiQkvRope && (bn != 256 || !args.qkv.q_out || !args.qkv.k_cache ||
-                               !args.qkv.v_cache || !args.qkv.page_table || !args.qkv.rope)) {
+                               !args.qkv.v_cache || !args.qkv.rope ||
+                               (!args.qkv.page_table && !args.qkv.tok_row) ||
+                               (!args.qkv.tok_pos != !args.qkv.tok_row))) {
         return cudaErrorInvalidValue;
     }
     const CUtensorMap& bb = b2 ? *b2 : b;

@@ -37,6 +37,11 @@ struct QkvEpilogue {
     // same paged layout), the operands of the fp16 prefill attention.
     uint16_t* k_stage = nullptr;
     uint16_t* v_stage = nullptr;
+    // Rows of several sequences (nullable): row m is the token at position tok_pos[m], whose K/V
+    // go to cache row tok_row[m] = physical page * 16 + position % 16 (page_table and pos0 are
+    // then unused).
+    const int32_t* tok_pos = nullptr;
+    const int32_t* tok_row = nullptr;
 };
 
 // A 2-D K-major bf16 matrix [rows, cols] (cols contiguous) as a TMA tensor map with 128-byte

@@ -1582,6 +1582,17 @@ q3_status q3_batch_add(q3_batch* batch, const int32_t* ids_host, int n, int* slo
     });
 }
 
+q3_status q3_batch_add_many(q3_batch* batch, const int32_t* ids_host, const int* lens_host,
+                            int n_seqs, int* first_slot, int32_t* next_tokens_host,
+                            float* last_logits_host) {
+    return guard([&] {
+        if (!batch || !ids_host || !lens_host) throw std::invalid_argument("null argument");
+        const int s = batch->b->add_many(ids_host, lens_host, n_seqs, next_tokens_host,
+                                         last_logits_host);
+        if (first_slot) *first_slot = s;
+    });
+}
+
 q3_status q3_batch_size(const q3_batch* batch, int* n_seqs) {
     return guard([&] {
         if (!batch || !n_seqs) throw std::invalid_argument("null argument");

@@ -355,6 +355,125 @@ KvView engine_view(Engine& e) {
     return v;
 }
 
+void Prefill::layer_pass(const int32_t* ids, int S, const PassRows& pr, const uint16_t* embed,
+                         const std::vector<LayerWeights>& layers, const KvView& kv, float* taps,
+                         cudaStream_t s) {
+    const q3_config& c = cfg_;
+    const int qd = c.n_heads * HD;
+    const int qkv = (c.n_heads + 2 * c.n_kv_heads) * HD;
+    const int L = static_cast<int>(layers.size());
+    const int table_len = kv.table_len ? kv.table_len : kv.n_pages;
+    const bool f16 = precision_ == kPrecisionF16;
+    float* X = static_cast<float*>(x_.ptr);
+    uint16_t* Xn = static_cast<uint16_t*>(xn_.ptr);
+    uint16_t* XnLo = f16 ? static_cast<uint16_t*>(xn_lo_.ptr) : nullptr;
+    unsigned* err = static_cast<unsigned*>(err_.ptr);
+    uint16_t* k16 = f16 ? static_cast<uint16_t*>(k16_.ptr) : nullptr;
+    uint16_t* v16 = f16 ? static_cast<uint16_t*>(v16_.ptr) : nullptr;
+    CUtensorMap m_xn, m_xn_lo, m_o, m_h, m_q;
+    make_tmap_bf16(&m_q, q_.ptr, S, qd, 64);
+    make_tmap_bf16(&m_xn, xn_.ptr, S, c.dim, 128);
+    make_tmap_bf16(&m_xn_lo, xn_lo_.ptr, S, c.dim, 128);
+    make_tmap_bf16(&m_o, o_.ptr, S, qd, 128);
+    make_tmap_bf16(&m_h, h_.ptr, S, c.hidden_dim, 128);
+    CUtensorMap o_x, o_h;  // contraction outputs
+    make_tmap_out(&o_x, X, S, c.dim, false);
+    make_tmap_out(&o_h, h_.ptr, S, c.hidden_dim, true);
+    auto tap = [&](int slot) {
+        if (taps) {
+            Q3_CUDA(cudaMemcpyAsync(taps + static_cast<size_t>(slot) * c.dim,
+                                    X + static_cast<size_t>(S - 1) * c.dim, c.dim * 4,
+                                    cudaMemcpyDeviceToDevice, s));
+        }
+    };
+    launch_rmsnorm_rows_bf16(ids, embed, X, layers[0].attn_norm, c.norm_eps, Xn, S, c.dim, s, XnLo,
+                             true, f16);
+    tap(0);
+    for (int l = 0; l < L; ++l) {
+        const LayerWeights& w = layers[l];
+        const LayerMaps& wm = wmaps_[l];
+        GemmArgs g;
+        g.err = err;
+        g.dependent = true;  // the prefill's kernels launch as programmatic dependents
+        g.f16 = f16 ? 1 : 0;
+        g.M = S;
+        // [wq; wk; wv] . xn (src/inference.cpp:795-798) with the QK-RMSNorm, RoPE and the paged
+        // K/V write (:800-815) in the epilogue: q rows to q_.
+        g.N = qkv;
+        g.K = c.dim;
+        g.qkv.q_out = static_cast<uint16_t*>(q_.ptr);
+        g.qkv.k_cache = kv.k_base + layer_elems(kv) * l;
+        g.qkv.v_cache = kv.v_base + layer_elems(kv) * l;
+        g.qkv.page_table = kv.page_table;
+        g.qkv.rope = kv.rope;
+        g.qkv.q_norm = w.q_norm;
+        g.qkv.k_norm = w.k_norm;
+        g.qkv.pos0 = pr.p0;
+        g.qkv.tok_pos = pr.tok_pos;
+        g.qkv.tok_row = pr.tok_row;
+        g.qkv.n_heads = c.n_heads;
+        g.qkv.n_kv = c.n_kv_heads;
+        g.qkv.eps = c.norm_eps;
+        if (f16) {
+            // fp16 q for the attention, fp16 copies of the K/V rows it reads; the RmsNorm'd
+            // input as an fp16 hi + lo pair (the one input where the error of a single fp16
+            // rounding still shows in the hidden states).
+            g.qkv.q_f16 = 1;
+            g.qkv.k_stage = k16 + layer_elems(kv) * l;
+            g.qkv.v_stage = v16 + layer_elems(kv) * l;
+            Q3_CUDA(launch_gemm(m_xn, wm.wqkv, nullptr, m_xn, g, kEpiQkvRope, num_sms_, s,
+                                &m_xn_lo));
+        } else {
+            Q3_CUDA(launch_gemm(m_xn, wm.wqkv, nullptr, m_xn, g, kEpiQkvRope, num_sms_, s));
+        }
+        g.qkv = QkvEpilogue{};
+        PrefillAttnTcArgs ta{};
+        ta.page_table = kv.page_table;
+        ta.out = static_cast<uint16_t*>(o_.ptr);
+        ta.err = err;
+        ta.rows = S;
+        ta.pos0 = pr.p0;
+        ta.n_kv = c.n_kv_heads;
+        ta.n_pages = kv.n_pages;
+        ta.pages_per_seq = table_len;
+        ta.layer = l;
+        ta.f16 = f16 ? 1 : 0;
+        ta.work = pr.work;
+        ta.n_work = pr.n_work;
+        launch_prefill_attention_tc(m_q, kmap_, vmap_, kmap4_, vmap4_, ta, s);
+        // x += wo . attn (:846-849).
+        g.N = c.dim;
+        g.K = qd;
+        Q3_CUDA(launch_gemm(m_o, wm.wo, nullptr, o_x, g, kEpiAddF32, num_sms_, s));
+        launch_rmsnorm_rows_bf16(nullptr, nullptr, X, w.mlp_norm, c.norm_eps, Xn, S, c.dim, s,
+                                 nullptr, true, f16);
+        // h = silu(w1 . xn) * (w3 . xn) (:851, :1005-1011).
+        g.N = 2 * c.hidden_dim;
+        g.K = c.dim;
+        Q3_CUDA(launch_gemm(m_xn, wm.w1, &wm.w3, o_h, g, kEpiSwiGLU, num_sms_, s));
+        // x += w2 . h (:1013, :863-865).
+        g.N = c.dim;
+        g.K = c.hidden_dim;
+        Q3_CUDA(launch_gemm(m_h, wm.w2, nullptr, o_x, g, kEpiAddF32, num_sms_, s));
+        if (l + 1 < L) {
+            launch_rmsnorm_rows_bf16(nullptr, nullptr, X, layers[l + 1].attn_norm, c.norm_eps, Xn,
+                                     S, c.dim, s, XnLo, true, f16);
+        }
+        tap(l + 1);
+    }
+}
+
+void Prefill::prepare(const std::vector<LayerWeights>& layers, const KvView& kv,
+                      const std::vector<LayerWeights>* layers16, int rows) {
+    const bool f16 = precision_ == kPrecisionF16;
+    if (f16 && (!layers16 || layers16->size() != layers.size())) {
+        throw std::invalid_argument("fp16 prefill needs the fp16 weight copies");
+    }
+    ensure_rows(rows);
+    ensure_weight_maps(f16 ? *layers16 : layers);
+    ensure_kv_maps(kv, static_cast<int>(layers.size()));
+}
+
 void Prefill::run(const int32_t* ids_dev, int n, int pos0, const uint16_t* embed,
                   const std::vector<LayerWeights>& layers, const KvView& kv, float* x_last,
                   float* taps, cudaStream_t s, const std::vector<LayerWeights>* layers16) {
@@ -365,126 +484,120 @@ void Prefill::run(const int32_t* ids_dev, int n, int pos0, const uint16_t* embed
         throw std::out_of_range("batched prefill past the context length");
     }
     if (kv.rope_len < pos0 + n) throw std::runtime_error("RoPE table shorter than the prompt");
-    const int qd = c.n_heads * HD;
-    const int qkv = (c.n_heads + 2 * c.n_kv_heads) * HD;
     const int L = static_cast<int>(layers.size());
-    const bool f16 = precision_ == kPrecisionF16;
-    if (f16 && (!layers16 || layers16->size() != layers.size())) {
-        throw std::invalid_argument("fp16 prefill needs the fp16 weight copies");
-    }
-    ensure_rows(std::min(n, kMaxChunk));
-    ensure_weight_maps(f16 ? *layers16 : layers);
-    ensure_kv_maps(kv, L);
-    float* X = static_cast<float*>(x_.ptr);
-    uint16_t* Xn = static_cast<uint16_t*>(xn_.ptr);
-    uint16_t* XnLo = f16 ? static_cast<uint16_t*>(xn_lo_.ptr) : nullptr;
-    unsigned* err = static_cast<unsigned*>(err_.ptr);
-    uint16_t* k16 = f16 ? static_cast<uint16_t*>(k16_.ptr) : nullptr;
-    uint16_t* v16 = f16 ? static_cast<uint16_t*>(v16_.ptr) : nullptr;
-    if (f16 && pos0 > 0) {
+    prepare(layers, kv, layers16, std::min(n, kMaxChunk));
+    if (precision_ == kPrecisionF16 && pos0 > 0) {
         // Cache rows before this prompt (earlier prompts, decoded tokens): their fp16 copies.
         const int pages = (pos0 + kPageTokens - 1) / kPageTokens;
         const int page_elems = c.n_kv_heads * kPageTokens * HD;
-        kv_to_f16_kernel<<<dim3(pages, L), 256, 0, s>>>(kv.k_base, kv.v_base, k16, v16,
-                                                        kv.page_table, layer_elems(kv), page_elems);
+        kv_to_f16_kernel<<<dim3(pages, L), 256, 0, s>>>(
+            kv.k_base, kv.v_base, static_cast<uint16_t*>(k16_.ptr),
+            static_cast<uint16_t*>(v16_.ptr), kv.page_table, layer_elems(kv), page_elems);
         Q3_CUDA(cudaGetLastError());
     }
-
+    const float* X = static_cast<const float*>(x_.ptr);
     for (int c0 = 0; c0 < n; c0 += kMaxChunk) {
         const int S = std::min(kMaxChunk, n - c0);
-        const int p0 = pos0 + c0;
         const bool last = c0 + S == n;
-        CUtensorMap m_xn, m_xn_lo, m_o, m_h, m_q;
-        make_tmap_bf16(&m_q, q_.ptr, S, qd, 64);
-        make_tmap_bf16(&m_xn, xn_.ptr, S, c.dim, 128);
-        make_tmap_bf16(&m_xn_lo, xn_lo_.ptr, S, c.dim, 128);
-        make_tmap_bf16(&m_o, o_.ptr, S, qd, 128);
-        make_tmap_bf16(&m_h, h_.ptr, S, c.hidden_dim, 128);
-        CUtensorMap o_x, o_h;  // contraction outputs
-        make_tmap_out(&o_x, X, S, c.dim, false);
-        make_tmap_out(&o_h, h_.ptr, S, c.hidden_dim, true);
-        auto tap = [&](int slot) {
-            if (taps && last) {
-                Q3_CUDA(cudaMemcpyAsync(taps + static_cast<size_t>(slot) * c.dim,
-                                        X + static_cast<size_t>(S - 1) * c.dim, c.dim * 4,
-                                        cudaMemcpyDeviceToDevice, s));
-            }
-        };
-        launch_rmsnorm_rows_bf16(ids_dev + c0, embed, X, layers[0].attn_norm, c.norm_eps, Xn, S,
-                                 c.dim, s, XnLo, true, f16);
-        tap(0);
-        for (int l = 0; l < L; ++l) {
-            const LayerWeights& w = layers[l];
-            const LayerMaps& wm = wmaps_[l];
-            GemmArgs g;
-            g.err = err;
-            g.dependent = true;  // the prefill's kernels launch as programmatic dependents
-            g.f16 = f16 ? 1 : 0;
-            g.M = S;
-            // [wq; wk; wv] . xn (src/inference.cpp:795-798) with the QK-RMSNorm, RoPE and the
-            // paged K/V write (:800-815) in the epilogue: q rows to q_ (bf16).
-            g.N = qkv;
-            g.K = c.dim;
-            g.qkv.q_out = static_cast<uint16_t*>(q_.ptr);
-            g.qkv.k_cache = kv.k_base + layer_elems(kv) * l;
-            g.qkv.v_cache = kv.v_base + layer_elems(kv) * l;
-            g.qkv.page_table = kv.page_table;
-            g.qkv.rope = kv.rope;
-            g.qkv.q_norm = w.q_norm;
-            g.qkv.k_norm = w.k_norm;
-            g.qkv.pos0 = p0;
-            g.qkv.n_heads = c.n_heads;
-            g.qkv.n_kv = c.n_kv_heads;
-            g.qkv.eps = c.norm_eps;
-            if (f16) {
-                // fp16 q for the attention, fp16 copies of the K/V rows it reads; the
-                // RmsNorm'd input as an fp16 hi + lo pair (the one input where the error of a
-                // single fp16 rounding still shows in the hidden states).
-                g.qkv.q_f16 = 1;
-                g.qkv.k_stage = k16 + layer_elems(kv) * l;
-                g.qkv.v_stage = v16 + layer_elems(kv) * l;
-                Q3_CUDA(launch_gemm(m_xn, wm.wqkv, nullptr, m_xn, g, kEpiQkvRope, num_sms_, s,
-                                    &m_xn_lo));
-            } else {
-                Q3_CUDA(launch_gemm(m_xn, wm.wqkv, nullptr, m_xn, g, kEpiQkvRope, num_sms_, s));
-            }
-            g.qkv = QkvEpilogue{};
-            PrefillAttnTcArgs ta{};
-            ta.page_table = kv.page_table;
-            ta.out = static_cast<uint16_t*>(o_.ptr);
-            ta.err = err;
-            ta.rows = S;
-            ta.pos0 = p0;
-            ta.n_kv = c.n_kv_heads;
-            ta.n_pages = kv.n_pages;
-            ta.pages_per_seq = table_len;
-            ta.layer = l;
-            ta.f16 = f16 ? 1 : 0;
-            launch_prefill_attention_tc(m_q, kmap_, vmap_, kmap4_, vmap4_, ta, s);
-            // x += wo . attn (:846-849).
-            g.N = c.dim;
-            g.K = qd;
-            Q3_CUDA(launch_gemm(m_o, wm.wo, nullptr, o_x, g, kEpiAddF32, num_sms_, s));
-            launch_rmsnorm_rows_bf16(nullptr, nullptr, X, w.mlp_norm, c.norm_eps, Xn, S, c.dim, s,
-                                     nullptr, true, f16);
-            // h = silu(w1 . xn) * (w3 . xn) (:851, :1005-1011).
-            g.N = 2 * c.hidden_dim;
-            g.K = c.dim;
-            Q3_CUDA(launch_gemm(m_xn, wm.w1, &wm.w3, o_h, g, kEpiSwiGLU, num_sms_, s));
-            // x += w2 . h (:1013, :863-865).
-            g.N = c.dim;
-            g.K = c.hidden_dim;
-            Q3_CUDA(launch_gemm(m_h, wm.w2, nullptr, o_x, g, kEpiAddF32, num_sms_, s));
-            if (l + 1 < L) {
-                launch_rmsnorm_rows_bf16(nullptr, nullptr, X, layers[l + 1].attn_norm, c.norm_eps,
-                                         Xn, S, c.dim, s, XnLo, true, f16);
-            }
-            tap(l + 1);
-        }
+        PassRows pr;
+        pr.p0 = pos0 + c0;
+        layer_pass(ids_dev + c0, S, pr, embed, layers, kv, last ? taps : nullptr, s);
         if (last) {
             Q3_CUDA(cudaMemcpyAsync(x_last, X + static_cast<size_t>(S - 1) * c.dim, c.dim * 4,
                                     cudaMemcpyDeviceToDevice, s));
         }
+    }
+}
+
+void Prefill::run_varlen(const int32_t* ids_dev, const std::vector<int>& offset,
+                         const std::vector<int>& len, const std::vector<int>& table_off,
+                         const int32_t* table_host, const uint16_t* embed,
+                         const std::vector<LayerWeights>& layers, const KvView& kv,
+                         float* x_last, cudaStream_t s,
+                         const std::vector<LayerWeights>* layers16) {
+    const q3_config& c = cfg_;
+    const int n_seqs = static_cast<int>(len.size());
+    if (n_seqs == 0) return;
+    if (offset.size() != len.size() || table_off.size() != len.size() || !table_host) {
+        throw std::invalid_argument("varlen prefill: one offset, length and table per sequence");
+    }
+    const int table_len = kv.table_len ? kv.table_len : kv.n_pages;
+    int max_len = 0;
+    for (int i = 0; i < n_seqs; ++i) {
+        if (len[i] <= 0 || len[i] > kMaxChunk) {
+            throw std::out_of_range("varlen prefill: every prompt 1 .. 4096 tokens");
+        }
+        if (len[i] > table_len * kPageTokens) {
+            throw std::out_of_range("batched prefill past the context length");
+        }
+        max_len = std::max(max_len, len[i]);
+    }
+    if (kv.rope_len < max_len) throw std::runtime_error("RoPE table shorter than the prompt");
+    prepare(layers, kv, layers16, kMaxChunk);
+    // Query blocks of one chunk: at most one partial block per sequence beyond the full ones.
+    constexpr int kMaxWork = kMaxChunk / 64 + kMaxChunk;
+    if (tok_pos_.bytes == 0) {
+        tok_pos_.alloc(static_cast<size_t>(kMaxChunk) * 4);
+        tok_row_.alloc(static_cast<size_t>(kMaxChunk) * 4);
+        work_.alloc(static_cast<size_t>(kMaxWork) * sizeof(int4));
+    }
+    pinned_varlen_.ensure(static_cast<size_t>(kMaxChunk) * 8 + kMaxWork * sizeof(int4));
+    int32_t* h_pos = static_cast<int32_t*>(pinned_varlen_.ptr);
+    int32_t* h_row = h_pos + kMaxChunk;
+    int4* h_work = reinterpret_cast<int4*>(h_row + kMaxChunk);
+    const float* X = static_cast<const float*>(x_.ptr);
+
+    for (int first = 0; first < n_seqs;) {
+        // Sequences [first, last): contiguous in ids, together at most one chunk of tokens.
+        int last = first, S = 0;
+        while (last < n_seqs && S + len[last] <= kMaxChunk &&
+               (last == first || offset[last] == offset[last - 1] + len[last - 1])) {
+            S += len[last];
+            ++last;
+        }
+        // The pinned staging is reused chunk after chunk: the previous chunk's copies are done.
+        Q3_CUDA(cudaStreamSynchronize(s));
+        std::vector<int4> items;
+        int row = 0;
+        for (int i = first; i < last; ++i) {
+            const int32_t* tab = table_host + table_off[i];
+            for (int p = 0; p < len[i]; ++p) {
+                h_pos[row + p] = p;
+                h_row[row + p] = tab[p / kPageTokens] * kPageTokens + p % kPageTokens;
+            }
+            for (int b = 0; b < len[i]; b += 64) {
+                items.push_back(make_int4(row + b, std::min(64, len[i] - b), b, table_off[i]));
+            }
+            row += len[i];
+        }
+        // Blocks with the most KV positions first (the longest work starts first).
+        std::stable_sort(items.begin(), items.end(), [](const int4& a, const int4& b) {
+            return a.z + a.y > b.z + b.y;
+        });
+        if (static_cast<int>(items.size()) > kMaxWork) {
+            throw std::runtime_error("varlen prefill: too many query blocks");
+        }
+        std::copy(items.begin(), items.end(), h_work);
+        Q3_CUDA(cudaMemcpyAsync(tok_pos_.ptr, h_pos, static_cast<size_t>(S) * 4,
+                                cudaMemcpyHostToDevice, s));
+        Q3_CUDA(cudaMemcpyAsync(tok_row_.ptr, h_row, static_cast<size_t>(S) * 4,
+                                cudaMemcpyHostToDevice, s));
+        Q3_CUDA(cudaMemcpyAsync(work_.ptr, h_work, items.size() * sizeof(int4),
+                                cudaMemcpyHostToDevice, s));
+        PassRows pr;
+        pr.tok_pos = static_cast<const int32_t*>(tok_pos_.ptr);
+        pr.tok_row = static_cast<const int32_t*>(tok_row_.ptr);
+        pr.work = static_cast<const int4*>(work_.ptr);
+        pr.n_work = static_cast<int>(items.size());
+        layer_pass(ids_dev + offset[first], S, pr, embed, layers, kv, nullptr, s);
+        int r0 = 0;
+        for (int i = first; i < last; ++i) {
+            r0 += len[i];
+            Q3_CUDA(cudaMemcpyAsync(x_last + static_cast<size_t>(i) * c.dim,
+                                    X + static_cast<size_t>(r0 - 1) * c.dim, c.dim * 4,
+                                    cudaMemcpyDeviceToDevice, s));
+        }
+        first = last;
     }
 }
 

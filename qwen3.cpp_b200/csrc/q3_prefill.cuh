@@ -67,6 +67,11 @@ struct PrefillAttnTcArgs {
     // q, K, V and the probabilities are fp16 (k and v then map fp16 copies of the cache), the
     // output is fp16 (out_lo unused).
     int f16 = 0;
+    // Several sequences at once (nullable): n_work query blocks {first q/out row, rows (<= 64),
+    // position of the first row, offset of the sequence's page table in page_table}, longest
+    // first; rows and pos0 are then unused.
+    const int4* work = nullptr;
+    int n_work = 0;
 };
 void launch_prefill_attention_tc(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
                                  const CUtensorMap& k4, const CUtensorMap& v4,
@@ -122,6 +127,19 @@ public:
     enum Precision : int { kPrecisionBF16 = 0, kPrecisionF16 = 1 };
     void set_precision(int p) { precision_ = p; }
     int precision() const { return precision_; }
+    // The prompts of several new sequences in one pass per chunk of at most kMaxChunk tokens
+    // (each sequence whole inside one chunk, so each prompt is at most kMaxChunk tokens): the
+    // contractions run over the tokens of every sequence of the chunk together (M = their sum),
+    // the QKV epilogue writes each token's K/V into its own sequence's pages, and the attention
+    // takes a list of (sequence, 64-token query block) items. Sequence i has the tokens
+    // ids_dev[offset[i] .. offset[i] + len[i]) at positions 0 .. len[i] - 1 and the page table
+    // kv.page_table + table_off[i] (table_host: the same table on the host, for the cache rows).
+    // x_last (device, [n_seqs, dim]) receives each sequence's last hidden state.
+    void run_varlen(const int32_t* ids_dev, const std::vector<int>& offset,
+                    const std::vector<int>& len, const std::vector<int>& table_off,
+                    const int32_t* table_host, const uint16_t* embed,
+                    const std::vector<LayerWeights>& layers, const KvView& kv, float* x_last,
+                    cudaStream_t s, const std::vector<LayerWeights>* layers16 = nullptr);
     // Non-zero when a contraction's bounded wait gave up in the last run.
     unsigned read_error(cudaStream_t s);
     // Attention kernel: tcgen05 (default) or the mma.sync flash-attention kernel.
@@ -137,6 +155,21 @@ public:
     int num_sms() const { return num_sms_; }
 
 private:
+    // Rows of one pass: one sequence at positions p0.. (tok_pos null), or the tokens of several
+    // (per-token positions and cache rows, the attention's work items).
+    struct PassRows {
+        int p0 = 0;
+        const int32_t* tok_pos = nullptr;
+        const int32_t* tok_row = nullptr;
+        const int4* work = nullptr;
+        int n_work = 0;
+    };
+    // Every layer over S rows (the chunk's token ids at `ids`); taps (nullable) as run's.
+    void layer_pass(const int32_t* ids, int S, const PassRows& pr, const uint16_t* embed,
+                    const std::vector<LayerWeights>& layers, const KvView& kv, float* taps,
+                    cudaStream_t s);
+    void prepare(const std::vector<LayerWeights>& layers, const KvView& kv,
+                 const std::vector<LayerWeights>* layers16, int rows);
     void ensure_rows(int rows);
     void ensure_weight_maps(const std::vector<LayerWeights>& layers);
     size_t layer_elems(const KvView& kv) const;
@@ -151,6 +184,9 @@ private:
     // layout), the operands of the fp16 attention.
     DeviceBuffer k16_, v16_;
     bool kv_maps_f16_ = false;
+    // Varlen pass: per-token positions and cache rows, attention work items (device), staging.
+    DeviceBuffer tok_pos_, tok_row_, work_;
+    PinnedBuffer pinned_varlen_;
     struct LayerMaps {
         CUtensorMap wqkv, wo, w1, w3, w2;
     };

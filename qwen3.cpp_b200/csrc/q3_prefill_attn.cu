@@ -210,12 +210,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // 1-D grid, longest query blocks first across every KV head, so that the block scheduler
     // starts the longest work first and the short blocks fill the tail.
     const int g = static_cast<int>(blockIdx.x) % a.n_kv;
-    const int n_qb = gridDim.x / a.n_kv;
-    const int qb = n_qb - 1 - static_cast<int>(blockIdx.x) / a.n_kv;
-    const int tok0 = qb * TOK;
-    const int last_tok = min(a.rows, tok0 + TOK) - 1;
-    const int kv_end = a.pos0 + last_tok + 1;
-    const int32_t* table = a.page_table;
+    // This CTA's query block: rows tok0 .. tok0 + nrows - 1 of the q / out buffers, the tokens at
+    // positions pos_first .. pos_first + nrows - 1 of the sequence whose page table is `table`.
+    int tok0, nrows, pos_first;
+    const int32_t* table;
+    if (a.work) {
+        // Several sequences (work items ordered longest first by the host).
+        const int4 it = a.work[blockIdx.x / a.n_kv];
+        tok0 = it.x;
+        nrows = it.y;
+        pos_first = it.z;
+        table = a.page_table + it.w;
+    } else {
+        const int n_qb = gridDim.x / a.n_kv;
+        const int qb = n_qb - 1 - static_cast<int>(blockIdx.x) / a.n_kv;
+        tok0 = qb * TOK;
+        nrows = min(a.rows - tok0, TOK);
+        pos_first = a.pos0 + tok0;
+        table = a.page_table;
+    }
+    const int kv_end = pos_first + nrows;
     const int table_len = a.pages_per_seq ? a.pages_per_seq : a.n_pages;
     const int ntiles = (kv_end + KEYS - 1) / KEYS;
     const int valid_pages = (kv_end + kPageTokens - 1) / kPageTokens;
@@ -427,7 +441,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int lg = warp & 3;
         const int half = (warp - 2) >> 2;                // key half of S, column half of O
         const int r = lg * 32 + lane;                    // row of the 128-row tile
-        const int qpos = a.pos0 + min(tok0 + (r & (TOK - 1)), last_tok);
+        const int qpos = pos_first + min(r & (TOK - 1), nrows - 1);
         const uint32_t lane_half = tmem + (static_cast<uint32_t>(lg * 32) << 16) +
                                    static_cast<uint32_t>(half * 64);
         const float scale = 1.4426950408889634f / sqrtf(static_cast<float>(HD));
@@ -548,7 +562,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 fail(abort, a.err, 19);
             } else {
                 const int token = tok0 + (r & (TOK - 1));
-                if (token < a.rows) {
+                if ((r & (TOK - 1)) < nrows) {
                     const float inv = 1.0f / (l + l_other);
                     const size_t off = static_cast<size_t>(token) * (2 * a.n_kv) * HD +
                                        (2 * g + (r >> 6)) * HD + half * 64;
@@ -602,7 +616,7 @@ void launch_prefill_attention_tc(const CUtensorMap& q, const CUtensorMap& k, con
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
         configured[dev & 63] = true;
     }
-    const dim3 grid(((a.rows + TOK - 1) / TOK) * a.n_kv);
+    const dim3 grid((a.work ? a.n_work : (a.rows + TOK - 1) / TOK) * a.n_kv);
     launch_dep(true, prefill_attn_tc_kernel, grid, dim3(NTHREADS), SMEM, s, q, k, v, k4, v4, a);
     Q3_CUDA(cudaGetLastError());
 }

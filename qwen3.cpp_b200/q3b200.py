@@ -111,6 +111,7 @@ def lib() -> C.CDLL:
         "q3_gemm_f16": [vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, vp],
         "q3_batch_create": [vp, C.c_int, C.c_int, C.POINTER(vp)],
         "q3_batch_add": [vp, I32P, C.c_int, C.POINTER(C.c_int), vp, vp],
+        "q3_batch_add_many": [vp, I32P, I32P, C.c_int, C.POINTER(C.c_int), vp, vp],
         "q3_batch_size": [vp, C.POINTER(C.c_int)],
         "q3_batch_stream": [vp, C.POINTER(vp)],
         "q3_batch_decode": [vp, C.c_int, vp],
@@ -397,6 +398,19 @@ class Batch:
         check(self._lib.q3_batch_add(self._h, ids, ids.size, C.byref(slot), nxt.ctypes.data,
                                      _ptr(lg)))
         return slot.value, int(nxt[0]), lg
+
+    def add_many(self, prompts, want_logits: bool = False):
+        """Adds several sequences, prefilling their prompts together; returns (first slot, next
+        tokens [n], logits [n, vocab] | None)."""
+        lens = np.ascontiguousarray([len(p) for p in prompts], np.int32)
+        ids = np.ascontiguousarray(np.concatenate([np.asarray(p, np.int32) for p in prompts]),
+                                   np.int32)
+        first = C.c_int()
+        nxt = np.zeros(len(prompts), np.int32)
+        lg = np.empty((len(prompts), self.vocab), np.float32) if want_logits else None
+        check(self._lib.q3_batch_add_many(self._h, ids, lens, len(prompts), C.byref(first),
+                                          nxt.ctypes.data, _ptr(lg)))
+        return first.value, nxt, lg
 
     def decode(self, n_steps: int) -> np.ndarray:
         """n_steps greedy steps for every sequence: tokens [n_steps, n_seqs]."""

@@ -71,16 +71,23 @@ def model(q3lib, full_weights):
     m.close()
 
 
-def check_batch(q3lib, model, seqs, runs, max_tokens, what):
+def check_batch(q3lib, model, seqs, runs, max_tokens, what, together=False):
+    """together: the prompts go in with one add_many (prefilled in one varlen pass)."""
     batch = q3lib.Batch(model, 4, max_tokens)
     try:
         firsts = []
-        for i, (prompt, _) in enumerate(seqs):
-            slot, nxt, lg = batch.add(prompt, want_logits=True)
-            am, lgs, _ = runs[i]
-            assert slot == i
-            firsts.append(nxt)
-            assert np.abs(lg - lgs[0]).max() <= LOGITS_MAX_ABS
+        if together:
+            slot0, nxt, lg = batch.add_many([p for p, _ in seqs], want_logits=True)
+            assert slot0 == 0
+            for i in range(len(seqs)):
+                firsts.append(int(nxt[i]))
+                assert np.abs(lg[i] - runs[i][1][0]).max() <= LOGITS_MAX_ABS
+        else:
+            for i, (prompt, _) in enumerate(seqs):
+                slot, nxt, lg = batch.add(prompt, want_logits=True)
+                assert slot == i
+                firsts.append(nxt)
+                assert np.abs(lg - runs[i][1][0]).max() <= LOGITS_MAX_ABS
         forced = np.stack([cont for _, cont in seqs], axis=1)  # [steps, seqs]
         am_a, lg = batch.decode_forced(forced[:LOGIT_STEPS], want_logits=True)
         am_b, _ = batch.decode_forced(forced[LOGIT_STEPS:])
@@ -109,14 +116,60 @@ def test_batch_matches_oracle(q3lib, model, seqs, oracle_runs):
     check_batch(q3lib, model, seqs, oracle_runs, 512, "short prompts")
 
 
-def test_batch_long_contexts_match_oracle(q3lib, full_weights):
-    """Prompts across the batched-decode configuration's context range, 16-token pages."""
+@pytest.fixture(scope="module")
+def long_runs(full_weights):
     seqs = make_seqs(LONG_PROMPT_LENS, 33)
     ctx = max(LONG_PROMPT_LENS) + STEPS + 1
-    runs = run_oracle(full_weights, seqs, ctx)
+    return seqs, run_oracle(full_weights, seqs, ctx), ctx
+
+
+@pytest.mark.parametrize("together", [False, True])
+def test_batch_long_contexts_match_oracle(q3lib, full_weights, long_runs, together):
+    """Prompts across the batched-decode configuration's context range, 16-token pages; added one
+    by one, or together (prefilled in one varlen pass: the three prompts' 4229 tokens in two
+    4096-token chunks)."""
+    seqs, runs, ctx = long_runs
     m = q3lib.Qwen3(full_weights, ctx)
     try:
-        check_batch(q3lib, m, seqs, runs, ctx, "prompts 129-3000")
+        check_batch(q3lib, m, seqs, runs, ctx,
+                    "prompts 129-3000" + (", prefilled together" if together else ""), together)
+    finally:
+        m.close()
+
+
+def test_batch_add_many_ragged_and_long(q3lib, full_weights):
+    """add_many over ragged prompts (1 token, one page exactly, a page + 1, a 64-token query
+    block boundary, and one longer than a chunk, which takes the one-by-one path): each
+    sequence's logits and KV rows as add() gives them."""
+    rng = np.random.default_rng(44)
+    lens = (1, 16, 17, 64, 65, 200, 4200, 33)
+    prompts = [rng.integers(0, 151936, n).astype(np.int32) for n in lens]
+    m = q3lib.Qwen3(full_weights, 4300)
+    try:
+        a = q3lib.Batch(m, len(lens), 4300)
+        b = q3lib.Batch(m, len(lens), 4300)
+        slot0, nxt, lg = a.add_many(prompts, want_logits=True)
+        assert slot0 == 0 and a.size == len(lens)
+        f = gen_weights.bf16_bits_to_f32
+        for i, p in enumerate(prompts):
+            s, n1, l1 = b.add(p, want_logits=True)
+            assert s == i
+            # The same kernels over a different row tiling: the split-K residual sums may round
+            # differently, so the next tokens agree unless the logits nearly tie.
+            assert np.abs(lg[i] - l1).max() <= LOGITS_MAX_ABS, i
+            if nxt[i] != n1:
+                assert abs(float(l1[nxt[i]]) - float(l1[n1])) <= 2 * LOGITS_MAX_ABS, i
+            for l in (0, 27):
+                for pos in {0, len(p) // 2, len(p) - 1}:
+                    ka, va = a.kv_row(i, l, pos)
+                    kb, vb = b.kv_row(i, l, pos)
+                    assert rel_l2(f(ka), f(kb)) <= REL_L2 and rel_l2(f(va), f(vb)) <= REL_L2, (i, l, pos)
+        toks = a.decode(4)
+        assert toks.shape == (4, len(lens))
+        with pytest.raises(q3lib.OutOfRange):
+            a.add_many([prompts[0]])  # full
+        a.close()
+        b.close()
     finally:
         m.close()
 

@@ -28,9 +28,11 @@ def test_attn_noalloc_matches_workspace_entry_point(q3lib):
     assert torch.cuda.is_available(), "GPU tests need a CUDA device"
     rng = np.random.default_rng(21)
     assert q3lib.lib().q3_attn_noalloc_max_scratch() == 64 * 256 * 4 + 256 + 64 * 8
-    # Two calls in a row on different shapes: the second reuses (and must not be confused by)
-    # what the first left in the shared static scratch.
-    for kv_len, head_dim, n_kv, head in ((300, 128, 8, 0), (5000, 128, 8, 7)):
+    # Calls in a row on different shapes: each reuses (and must not be confused by) what the one
+    # before left in the shared static scratch. The last two reach the static maximum: 64
+    # splits (kv_len > 16128), at head_dim 128 and at 256, which fills the whole array.
+    for kv_len, head_dim, n_kv, head in ((300, 128, 8, 0), (5000, 128, 8, 7), (16384, 128, 8, 3),
+                                         (16500, 256, 2, 1)):
         q = _dev(torch, rng.standard_normal(head_dim).astype(np.float32))
         k = _dev(torch, gen_weights.f32_to_bf16_bits(
             rng.standard_normal((kv_len, n_kv * head_dim)).astype(np.float32)))
