@@ -634,21 +634,18 @@ __device__ __noinline__ float2 fma_rows8(int slot, int row0) {
     for (int r = 0; r < 8; ++r) {
         const uint8_t* rp = rows + r * K * 2;
         const int sw = ((row0 + r) & 1) << 2;
-        float acc0 = 0.0f, acc1 = 0.0f;
+        // Even elements accumulate in .x, odd ones in .y: one packed fp32x2 FMA per weight pair.
+        float2 acc = make_float2(0.0f, 0.0f);
 #pragma unroll
         for (int j = 0; j < U; ++j) {
             const int u = (lane + 32 * j) ^ sw;
             const uint4 w = *reinterpret_cast<const uint4*>(rp + (u << 4));
-            acc0 = fmaf(bf16_lo(w.x), xr[j][0], acc0);
-            acc1 = fmaf(bf16_hi(w.x), xr[j][1], acc1);
-            acc0 = fmaf(bf16_lo(w.y), xr[j][2], acc0);
-            acc1 = fmaf(bf16_hi(w.y), xr[j][3], acc1);
-            acc0 = fmaf(bf16_lo(w.z), xr[j][4], acc0);
-            acc1 = fmaf(bf16_hi(w.z), xr[j][5], acc1);
-            acc0 = fmaf(bf16_lo(w.w), xr[j][6], acc0);
-            acc1 = fmaf(bf16_hi(w.w), xr[j][7], acc1);
+            acc = ffma2(make_float2(bf16_lo(w.x), bf16_hi(w.x)), make_float2(xr[j][0], xr[j][1]), acc);
+            acc = ffma2(make_float2(bf16_lo(w.y), bf16_hi(w.y)), make_float2(xr[j][2], xr[j][3]), acc);
+            acc = ffma2(make_float2(bf16_lo(w.z), bf16_hi(w.z)), make_float2(xr[j][4], xr[j][5]), acc);
+            acc = ffma2(make_float2(bf16_lo(w.w), bf16_hi(w.w)), make_float2(xr[j][6], xr[j][7]), acc);
         }
-        s[r] = acc0 + acc1;
+        s[r] = acc.x + acc.y;
     }
     // Butterfly: after xor 16 / 8 / 4 each lane keeps one row, q = lane >> 2, then xor 2 / 1.
     const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
@@ -691,20 +688,16 @@ __device__ __forceinline__ float fma_rows4(const Smem& sm, const uint8_t* rows, 
     for (int r = 0; r < 4; ++r) {
         const uint8_t* rp = rows + r * K * 2;
         const int sw = ((row0 + r) & 1) << 2;
-        float acc0 = 0.0f, acc1 = 0.0f;
+        float2 acc = make_float2(0.0f, 0.0f);
 #pragma unroll
         for (int j = 0; j < U; ++j) {
             const uint4 w = *reinterpret_cast<const uint4*>(rp + (((lane + 32 * j) ^ sw) << 4));
-            acc0 = fmaf(bf16_lo(w.x), xr[j][0], acc0);
-            acc1 = fmaf(bf16_hi(w.x), xr[j][1], acc1);
-            acc0 = fmaf(bf16_lo(w.y), xr[j][2], acc0);
-            acc1 = fmaf(bf16_hi(w.y), xr[j][3], acc1);
-            acc0 = fmaf(bf16_lo(w.z), xr[j][4], acc0);
-            acc1 = fmaf(bf16_hi(w.z), xr[j][5], acc1);
-            acc0 = fmaf(bf16_lo(w.w), xr[j][6], acc0);
-            acc1 = fmaf(bf16_hi(w.w), xr[j][7], acc1);
+            acc = ffma2(make_float2(bf16_lo(w.x), bf16_hi(w.x)), make_float2(xr[j][0], xr[j][1]), acc);
+            acc = ffma2(make_float2(bf16_lo(w.y), bf16_hi(w.y)), make_float2(xr[j][2], xr[j][3]), acc);
+            acc = ffma2(make_float2(bf16_lo(w.z), bf16_hi(w.z)), make_float2(xr[j][4], xr[j][5]), acc);
+            acc = ffma2(make_float2(bf16_lo(w.w), bf16_hi(w.w)), make_float2(xr[j][6], xr[j][7]), acc);
         }
-        s[r] = acc0 + acc1;
+        s[r] = acc.x + acc.y;
     }
     const bool b4 = lane & 16, b3 = lane & 8;
     float t2[2];
