@@ -197,14 +197,15 @@ int Batch::add(const int32_t* ids, int n, int32_t* next_token, float* last_logit
         m_.prefill_precision() == Prefill::kPrecisionF16 ? &m_.layers_f16() : nullptr;
     prefill_->run(static_cast<const int32_t*>(ids_.ptr), n, 0, m_.embed(), layers, kv, xl,
                   nullptr, s_, l16);
-    DeviceBuffer lg, am;
+    DeviceBuffer lg, am, part;
     lg.alloc(static_cast<size_t>(c.vocab_size) * 4);
     am.alloc(4);
+    part.alloc(static_cast<size_t>(gemv_grid(c.vocab_size)) * sizeof(float2));
     launch_gemv(kEpiStore, m_.output(), nullptr, xl, m_.final_norm(), c.norm_eps,
-                static_cast<float*>(lg.ptr), nullptr, c.vocab_size, c.dim, nullptr,
-                gemv_grid(c.vocab_size), s_);
-    launch_argmax_full(static_cast<const float*>(lg.ptr), c.vocab_size,
-                       static_cast<int32_t*>(am.ptr), s_);
+                static_cast<float*>(lg.ptr), nullptr, c.vocab_size, c.dim,
+                static_cast<float2*>(part.ptr), gemv_grid(c.vocab_size), s_);
+    launch_argmax_final(static_cast<const float2*>(part.ptr), gemv_grid(c.vocab_size),
+                        static_cast<int32_t*>(am.ptr), nullptr, nullptr, 0, nullptr, s_);
     int32_t nt = 0;
     Q3_CUDA(cudaMemcpyAsync(&nt, am.ptr, 4, cudaMemcpyDeviceToHost, s_));
     if (last_logits) {
@@ -302,15 +303,17 @@ int Batch::add_many(const int32_t* ids, const int* lens, int n_seqs, int32_t* ne
     flush();
     // Final RmsNorm + tied lm_head and Greedy of each prompt's last token (src/inference.cpp:
     // 619-635, :703-709).
-    DeviceBuffer lg, am;
+    DeviceBuffer lg, am, part;
     lg.alloc(static_cast<size_t>(c.vocab_size) * 4);
     am.alloc(static_cast<size_t>(n_seqs) * 4);
+    part.alloc(static_cast<size_t>(gemv_grid(c.vocab_size)) * sizeof(float2));
     for (int i = 0; i < n_seqs; ++i) {
         launch_gemv(kEpiStore, m_.output(), nullptr, XL + static_cast<size_t>(i) * c.dim,
                     m_.final_norm(), c.norm_eps, static_cast<float*>(lg.ptr), nullptr,
-                    c.vocab_size, c.dim, nullptr, gemv_grid(c.vocab_size), s_);
-        launch_argmax_full(static_cast<const float*>(lg.ptr), c.vocab_size,
-                           static_cast<int32_t*>(am.ptr) + i, s_);
+                    c.vocab_size, c.dim, static_cast<float2*>(part.ptr),
+                    gemv_grid(c.vocab_size), s_);
+        launch_argmax_final(static_cast<const float2*>(part.ptr), gemv_grid(c.vocab_size),
+                            static_cast<int32_t*>(am.ptr) + i, nullptr, nullptr, 0, nullptr, s_);
         if (last_logits) {
             Q3_CUDA(cudaMemcpyAsync(last_logits + static_cast<size_t>(i) * c.vocab_size, lg.ptr,
                                     lg.bytes, cudaMemcpyDeviceToHost, s_));

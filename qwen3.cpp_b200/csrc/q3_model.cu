@@ -1110,11 +1110,12 @@ void Model::prefill_batched(const int32_t* ids, int n, int pos0, float* last_log
                   engine_view(e), e.x(), hidden_host ? e.taps() : nullptr, s, l16);
     // Final RmsNorm + tied lm_head of the last token (src/inference.cpp:619-635) and Greedy.
     const q3_config& c = cfg_;
+    // Greedy over the GEMV's per-block (max, index) partials (two-level, lowest index on ties).
     launch_gemv(kEpiStore, output_, nullptr, e.x(), final_norm_, c.norm_eps,
-                static_cast<float*>(logits_.ptr), nullptr, c.vocab_size, c.dim, nullptr,
-                gemv_grid(c.vocab_size), s);
-    launch_argmax_full(static_cast<const float*>(logits_.ptr), c.vocab_size,
-                       static_cast<int32_t*>(argmax_out_.ptr), s);
+                static_cast<float*>(logits_.ptr), nullptr, c.vocab_size, c.dim,
+                static_cast<float2*>(argmax_part_.ptr), gemv_grid(c.vocab_size), s);
+    launch_argmax_final(static_cast<const float2*>(argmax_part_.ptr), gemv_grid(c.vocab_size),
+                        static_cast<int32_t*>(argmax_out_.ptr), nullptr, nullptr, 0, nullptr, s);
     int32_t am = 0;
     Q3_CUDA(cudaMemcpyAsync(&am, argmax_out_.ptr, 4, cudaMemcpyDeviceToHost, s));
     if (last_logits) {
