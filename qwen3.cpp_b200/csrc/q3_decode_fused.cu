@@ -74,7 +74,7 @@ constexpr int RPC_ROW = 8;             // 1024-element rows ([wq;wk;wv], lm_head
 constexpr int RPC_GRP = 8;             // 256-element rows (wo split by KV-head group)
 constexpr int RPC_PAIR = 4;            // w1 | w3 row pairs (4 + 4 rows)
 constexpr int T_SHORT = 128;           // KV positions up to which attention runs from the ring
-constexpr int ATT_TOK = 24;            // positions staged per sub-chunk (long contexts)
+constexpr int ATT_TOK = 24;            // at least this many positions per attention split
 constexpr int PAGE_BYTES = kPageTokens * HD * 2;
 
 enum Mode : int { kTag = 0, kPair = 2, kLogits = 3 };
@@ -394,6 +394,27 @@ __device__ __forceinline__ StepPos step_pos(const FusedArgs& a, const StepParams
     return p;
 }
 
+// Past T_SHORT positions: the positions [t0, t1) of KV head g that CTA c attends to (split
+// c / NKV of head c % NKV; t0 >= t1 for a split past kv_len), `on` for the CTAs that take part.
+// Its KV pages are [j0, j1) (none for an empty split).
+struct SplitRange {
+    bool on;
+    int g, s, t0, t1, j0, j1;
+};
+__device__ __forceinline__ SplitRange split_range(const StepPos& p, int c) {
+    SplitRange r;
+    r.on = !p.shrt && c < NKV * p.splits;
+    r.g = c % NKV;
+    r.s = c / NKV;
+    const int chunk = (p.kv_len + p.splits - 1) / p.splits;
+    r.t0 = min(r.s * chunk, p.kv_len);
+    r.t1 = min(p.kv_len, r.t0 + chunk);
+    r.j0 = r.t0 / kPageTokens;
+    r.j1 = r.t1 > r.t0 ? (r.t1 + kPageTokens - 1) / kPageTokens : r.j0;
+    return r;
+}
+__device__ __forceinline__ int chunks_of_i(int n, int per) { return (n + per - 1) / per; }
+
 // Grid arrivals of one step: after every DE (and every B past 128 positions) and the lm_head.
 __device__ __forceinline__ int barriers_of(const FusedArgs& a, bool shrt) {
     return a.n_layers * (shrt ? 1 : 2) + 1;
@@ -492,11 +513,11 @@ struct Producer {
         return true;
     }
 
-    __device__ bool kv_pages(int l, int g, int kv_len) {
+    // K and V pages [j0, j1) of KV head g, layer l: one chunk per page.
+    __device__ bool kv_pages(int l, int g, int j0, int j1) {
         const uint16_t* kc = a.k_cache + static_cast<size_t>(l) * a.layer_elems;
         const uint16_t* vc = a.v_cache + static_cast<size_t>(l) * a.layer_elems;
-        const int np = (kv_len + kPageTokens - 1) / kPageTokens;
-        for (int j = 0; j < np; ++j) {
+        for (int j = j0; j < j1; ++j) {
             const size_t e = page_elem(a.page_table, j, g);
             if (!issue(kc + e, PAGE_BYTES, vc + e, PAGE_BYTES, PAGE_BYTES, pol_kv)) return false;
         }
@@ -529,14 +550,18 @@ struct Producer {
                 const FusedLayer w = a.layers[l];
                 prefetch_ahead(st * per + l + a.l2_ahead, G, c);
                 ok = ok && rows<D * 2, RPC_ROW>(w.wqkv, part(QKV_ROWS, G, c));
-                if (ok && sp.shrt && in_grp) {
+                // KV pages this CTA's attention reads: all of head g's (short contexts) or those
+                // of its split (long ones).
+                const SplitRange sr = split_range(sp, c);
+                if (ok && (sp.shrt ? in_grp : sr.on)) {
                     // KV pages of this layer were last written (row kv_pos, sink rows) by the
                     // previous step's phases up to DE(l): wait until every CTA is past them.
                     if (st > 0) {
                         const unsigned de = prev_base + (prev_short ? l : 2 * l + 1);
                         ok = grid_wait(a, G * (de + 1) + a.barrier_offset, &sm.abort_flag, 3);
                     }
-                    ok = ok && kv_pages(l, g, sp.kv_len);
+                    ok = ok && (sp.shrt ? kv_pages(l, g, 0, chunks_of_i(sp.kv_len, kPageTokens))
+                                        : kv_pages(l, sr.g, sr.j0, sr.j1));
                 }
                 if (in_grp) {
                     ok = ok && rows<GRP * 2, RPC_GRP>(w.wop + static_cast<size_t>(g) * D * GRP,
@@ -912,33 +937,6 @@ __device__ __forceinline__ void acc_init(AttnAcc& s) {
     for (int j = 0; j < 4; ++j) s.o0[j] = s.o1[j] = 0.0f;
 }
 
-// One cached position: k4/v4 are this lane's 4 elements (FastAttn, src/inference.cpp:1029-1057).
-__device__ __forceinline__ void acc_add(AttnAcc& s, const float k4[4], const float v4[4],
-                                        float4 q0, float4 q1) {
-    const float sq = 11.313708498984761f;  // sqrtf(128), the reference's sqrtf(head_dim)
-    float d0 = k4[0] * q0.x;
-    d0 = fmaf(k4[1], q0.y, d0);
-    d0 = fmaf(k4[2], q0.z, d0);
-    d0 = fmaf(k4[3], q0.w, d0);
-    float d1 = k4[0] * q1.x;
-    d1 = fmaf(k4[1], q1.y, d1);
-    d1 = fmaf(k4[2], q1.z, d1);
-    d1 = fmaf(k4[3], q1.w, d1);
-    const float s0 = warp_sum(d0) / sq, s1 = warp_sum(d1) / sq;
-    const float n0 = fmaxf(s.m0, s0), n1 = fmaxf(s.m1, s1);
-    const float a0 = expf(s.m0 - n0), a1 = expf(s.m1 - n1);
-    const float p0 = expf(s0 - n0), p1 = expf(s1 - n1);
-    s.l0 = s.l0 * a0 + p0;
-    s.l1 = s.l1 * a1 + p1;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        s.o0[j] = s.o0[j] * a0 + p0 * v4[j];
-        s.o1[j] = s.o1[j] * a1 + p1 * v4[j];
-    }
-    s.m0 = n0;
-    s.m1 = n1;
-}
-
 // Two cached positions a, b (b only when has_b) in one online-softmax update: the four dot
 // products and their warp reductions are independent, and the running state is rescaled once.
 __device__ __forceinline__ void acc_add2(AttnAcc& s, const float ka[4], const float va[4],
@@ -1046,10 +1044,10 @@ __device__ __forceinline__ void merge_warps(Smem& sm, const FusedArgs& a, const 
 }
 
 // Phase BC attention (<= 128 cached positions): all positions of KV head g from the KV pages the
-// producer streamed into the ring (shared chunks, released by thread 0 after each page).
+// producer streamed into the ring (shared chunks, released by every warp after each page).
 __device__ __forceinline__ void attention_short(Smem& sm, const FusedArgs& a, const HeadPre& hp,
-                                             int kv_len, int kv_pos, int num_sink, int g,
-                                             uint32_t q0) {
+                                                int kv_len, int kv_pos, int num_sink, int g,
+                                                uint32_t q0) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const float4 q0v = reinterpret_cast<const float4*>(sm.qk[0])[lane];
     const float4 q1v = reinterpret_cast<const float4*>(sm.qk[1])[lane];
@@ -1081,37 +1079,189 @@ __device__ __forceinline__ void attention_short(Smem& sm, const FusedArgs& a, co
     merge_warps(sm, a, acc, g, 0, false);
 }
 
-// Phase B attention item (> 128 cached positions): split `split` of KV head g, positions staged
-// from global memory (L2) in sub-chunks; writes (max, sum, unnormalised output) partials.
-__device__ __forceinline__ void attention_long(Smem& sm, const FusedArgs& a, const HeadPre& hp,
-                                            int kv_len, int kv_pos, int num_sink, int splits,
-                                            int l, int g, int split) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int chunk = (kv_len + splits - 1) / splits;
-    const int t0 = split * chunk, t1 = min(kv_len, t0 + chunk);
-    const uint16_t* kc = a.k_cache + static_cast<size_t>(l) * a.layer_elems;
-    const uint16_t* vc = a.v_cache + static_cast<size_t>(l) * a.layer_elems;
-    const float4 q0v = reinterpret_cast<const float4*>(sm.qk[0])[lane];
-    const float4 q1v = reinterpret_cast<const float4*>(sm.qk[1])[lane];
+__device__ __forceinline__ void unpack8(const uint4 w, float f[8]) {
+    f[0] = bf16_lo(w.x);
+    f[1] = bf16_hi(w.x);
+    f[2] = bf16_lo(w.y);
+    f[3] = bf16_hi(w.y);
+    f[4] = bf16_lo(w.z);
+    f[5] = bf16_hi(w.z);
+    f[6] = bf16_lo(w.w);
+    f[7] = bf16_hi(w.w);
+}
+
+// One ring page of split attention (one warp): rows 2i + hb (hb = lane / 16) of page j, the lane's
+// 8 dimensions 8 dl .. 8 dl + 7 (dl = lane % 16), for both query heads; positions outside
+// [t0, t1) are masked. The row at kv_pos comes from sm.qk (this step's row, which the page copy
+// may predate); attention-sink rows are rotated by RoPE(position 1) and re-rounded on the fly
+// (src/inference.cpp:817-827). Updates the warp's online-softmax state (m, l warp-uniform; o per
+// lane over its rows of parity hb).
+__device__ __noinline__ void split_page(const Smem& sm, const FusedArgs& a, const uint8_t* page,
+                                        int j, int t0, int t1, int kv_pos, int num_sink,
+                                        const float (&q0)[8], const float (&q1)[8], float (&m)[2],
+                                        float (&l)[2], float (&o)[2][8]) {
+    const int lane = threadIdx.x & 31;
+    const int hb = lane >> 4, dl = lane & 15;
+    const int tp = j * kPageTokens;
+    float sv[16];
+    float vrow[8][8];
+    for (int i = 0; i < 8; ++i) {
+        const int r = 2 * i + hb, t = tp + r;
+        float kf[8];
+        unpack8(*reinterpret_cast<const uint4*>(page + (r * HD + 8 * dl) * 2), kf);
+        unpack8(*reinterpret_cast<const uint4*>(page + PAGE_BYTES + (r * HD + 8 * dl) * 2), vrow[i]);
+        if (t == kv_pos) {
+            const float4* kc = reinterpret_cast<const float4*>(sm.qk[2] + 8 * dl);
+            const float4* vc = reinterpret_cast<const float4*>(sm.qk[3] + 8 * dl);
+            const float4 k0 = kc[0], k1 = kc[1], v0 = vc[0], v1 = vc[1];
+            kf[0] = k0.x; kf[1] = k0.y; kf[2] = k0.z; kf[3] = k0.w;
+            kf[4] = k1.x; kf[5] = k1.y; kf[6] = k1.z; kf[7] = k1.w;
+            vrow[i][0] = v0.x; vrow[i][1] = v0.y; vrow[i][2] = v0.z; vrow[i][3] = v0.w;
+            vrow[i][4] = v1.x; vrow[i][5] = v1.y; vrow[i][6] = v1.z; vrow[i][7] = v1.w;
+        }
+        // Sink rows (page 0 of a wrapped cache): pairs (d, d + 64) sit in lanes dl, dl ^ 8.
+        if (tp < num_sink) {
+            const bool sink = t < num_sink && t != kv_pos;
+            const float2* cs = a.rope + HD / 2 + 8 * (dl & 7);  // RoPE at position 1
+            const bool first = dl < 8;
+#pragma unroll
+            for (int d = 0; d < 8; ++d) {
+                const float pr = __shfl_xor_sync(0xffffffffu, kf[d], 8);
+                const float2 c = __ldg(cs + d);
+                const float y = first ? (kf[d] * c.x - pr * c.y) : (kf[d] * c.x + pr * c.y);
+                if (sink) kf[d] = bf16_to_f32(f32_to_bf16(y));
+            }
+        }
+        float d0 = kf[0] * q0[0], d1 = kf[0] * q1[0];
+#pragma unroll
+        for (int d = 1; d < 8; ++d) {
+            d0 = fmaf(kf[d], q0[d], d0);
+            d1 = fmaf(kf[d], q1[d], d1);
+        }
+        sv[i] = d0;
+        sv[8 + i] = d1;
+    }
+    // Transposing butterfly over the 16 lanes of each half: lane dl ends with the full score of
+    // entry dl (head dl >> 3, row 2 (dl & 7) + hb).
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const bool up = dl & 8;
+        const float send = up ? sv[i] : sv[8 + i];
+        const float keep = up ? sv[8 + i] : sv[i];
+        sv[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const bool up = dl & 4;
+        const float send = up ? sv[i] : sv[4 + i];
+        const float keep = up ? sv[4 + i] : sv[i];
+        sv[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const bool up = dl & 2;
+        const float send = up ? sv[i] : sv[2 + i];
+        const float keep = up ? sv[2 + i] : sv[i];
+        sv[i] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+    }
+    float dot;
+    {
+        const bool up = dl & 1;
+        const float send = up ? sv[0] : sv[1];
+        const float keep = up ? sv[1] : sv[0];
+        dot = keep + __shfl_xor_sync(0xffffffffu, send, 1);
+    }
+    const float sq = 11.313708498984761f;  // sqrtf(128), the reference's sqrtf(head_dim)
+    const int my_h = dl >> 3, my_t = tp + 2 * (dl & 7) + hb;
+    const bool my_valid = my_t >= t0 && my_t < t1;
+    const float sc = my_valid ? dot / sq : -FLT_MAX;
+    float mx = sc;
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+    const float mx_other = __shfl_xor_sync(0xffffffffu, mx, 8);
+    const float mx0 = my_h ? mx_other : mx, mx1 = my_h ? mx : mx_other;
+    const float mn0 = fmaxf(m[0], mx0), mn1 = fmaxf(m[1], mx1);
+    const float p = my_valid ? expf(sc - (my_h ? mn1 : mn0)) : 0.0f;
+    float ps = p;
+    ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+    const float ps_other = __shfl_xor_sync(0xffffffffu, ps, 8);
+    const float ps0 = my_h ? ps_other : ps, ps1 = my_h ? ps : ps_other;
+    const float al0 = expf(m[0] - mn0), al1 = expf(m[1] - mn1);
+    l[0] = l[0] * al0 + ps0;
+    l[1] = l[1] * al1 + ps1;
+    m[0] = mn0;
+    m[1] = mn1;
+#pragma unroll
+    for (int d = 0; d < 8; ++d) {
+        o[0][d] *= al0;
+        o[1][d] *= al1;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float p0 = __shfl_sync(0xffffffffu, p, hb * 16 + i);
+        const float p1 = __shfl_sync(0xffffffffu, p, hb * 16 + 8 + i);
+#pragma unroll
+        for (int d = 0; d < 8; ++d) {
+            o[0][d] = fmaf(p0, vrow[i][d], o[0][d]);
+            o[1][d] = fmaf(p1, vrow[i][d], o[1][d]);
+        }
+    }
+}
+
+// Phase B attention (> 128 cached positions): split `split` of KV head g, positions [t0, t1),
+// from its KV pages [t0 / 16, ceil(t1 / 16)) in the ring (shared chunks: every warp waits for and
+// releases each); warp w attends over every NCW-th page; the warps' states are merged into the
+// split's (max, sum, unnormalised output) partials.
+__device__ __forceinline__ void attention_split(Smem& sm, const FusedArgs& a, int t0, int t1,
+                                                int kv_pos, int num_sink, int g, int split,
+                                                uint32_t q0) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int dl = lane & 15;
+    float q0r[8], q1r[8];
+#pragma unroll
+    for (int d = 0; d < 8; ++d) {
+        q0r[d] = sm.qk[0][8 * dl + d];
+        q1r[d] = sm.qk[1][8 * dl + d];
+    }
+    float m[2] = {-FLT_MAX, -FLT_MAX}, l[2] = {0.0f, 0.0f};
+    float o[2][8];
+#pragma unroll
+    for (int d = 0; d < 8; ++d) o[0][d] = o[1][d] = 0.0f;
+    const int j0 = t0 / kPageTokens, j1 = t1 > t0 ? (t1 + kPageTokens - 1) / kPageTokens : j0;
+    for (int j = j0; j < j1; ++j) {
+        const uint32_t qq = q0 + (j - j0);
+        const int slot = qq % NS;
+        if (warp_wait_full(sm, slot, (qq / NS) & 1, a) && (j - j0) % NCW == warp) {
+            split_page(sm, a, sm.ring[slot], j, t0, t1, kv_pos, num_sink, q0r, q1r, m, l, o);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.empty[slot]);  // one of NCW releases of a shared chunk
+    }
+    // The two row-parity halves hold partial sums over different rows: add them, then hand lane
+    // k the dimensions 4k .. 4k + 3 (merge_warps' layout).
     AttnAcc acc;
-    acc_init(acc);
-    uint4* stage = reinterpret_cast<uint4*>(sm.xs4);  // [ATT_TOK][K 16 | V 16] uint4
-    for (int tb = t0; tb < t1; tb += ATT_TOK) {
-        const int n = min(ATT_TOK, t1 - tb);
-        for (int idx = tid; idx < n * 32; idx += NCT) {
-            const int tok = idx >> 5, kind = (idx >> 4) & 1, vec = idx & 15;
-            const uint16_t* src = (kind ? vc : kc) + paged(a.page_table, tb + tok, g);
-            stage[idx] = __ldcg(reinterpret_cast<const uint4*>(src) + vec);
-        }
-        bar_consumers();
-        for (int tok = warp; tok < n; tok += NCW) {
-            const uint2 kk = reinterpret_cast<const uint2*>(stage + tok * 32)[lane];
-            const uint2 vv = reinterpret_cast<const uint2*>(stage + tok * 32 + 16)[lane];
-            float k4[4], v4[4];
-            kv_lane(sm, hp, tb + tok, kv_pos, num_sink, kk, vv, k4, v4);
-            acc_add(acc, k4, v4, q0v, q1v);
-        }
-        bar_consumers();
+    acc.m0 = m[0];
+    acc.m1 = m[1];
+    acc.l0 = l[0];
+    acc.l1 = l[1];
+#pragma unroll
+    for (int d = 0; d < 8; ++d) {
+        o[0][d] += __shfl_xor_sync(0xffffffffu, o[0][d], 16);
+        o[1][d] += __shfl_xor_sync(0xffffffffu, o[1][d], 16);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float a0 = __shfl_sync(0xffffffffu, o[0][k], lane >> 1);
+        const float b0 = __shfl_sync(0xffffffffu, o[0][4 + k], lane >> 1);
+        const float a1 = __shfl_sync(0xffffffffu, o[1][k], lane >> 1);
+        const float b1 = __shfl_sync(0xffffffffu, o[1][4 + k], lane >> 1);
+        acc.o0[k] = (lane & 1) ? b0 : a0;
+        acc.o1[k] = (lane & 1) ? b1 : a1;
     }
     merge_warps(sm, a, acc, g, split, true);
 }
@@ -1437,13 +1587,12 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) 
             } else {
                 // ---- B: split-K attention partials
                 if (!phase_begin(sm, a, k, 0, G, c)) return;
-                if (c < NKV * p.splits) {
-                    const int gg = c % NKV, s = c / NKV;
-                    const int chunk = (p.kv_len + p.splits - 1) / p.splits;
-                    const bool own =
-                        p.kv_pos >= s * chunk && p.kv_pos < min(p.kv_len, (s + 1) * chunk);
-                    prep_heads(sm, a, hp, l, gg, p.kv_pos, own, tag);
-                    attention_long(sm, a, hp, p.kv_len, p.kv_pos, p.num_sink, p.splits, l, gg, s);
+                const SplitRange sr = split_range(p, c);
+                if (sr.on) {
+                    const bool own = p.kv_pos >= sr.t0 && p.kv_pos < sr.t1;
+                    prep_heads(sm, a, hp, l, sr.g, p.kv_pos, own, tag);
+                    attention_split(sm, a, sr.t0, sr.t1, p.kv_pos, p.num_sink, sr.g, sr.s, q);
+                    q += static_cast<uint32_t>(sr.j1 - sr.j0);
                 }
                 phase_end(sm, a, k++, true, G, c);
                 ++nb;

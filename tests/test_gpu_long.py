@@ -8,9 +8,10 @@
   those and 768 more (1025 decoded positions, so that the 1% bound is not decided by one or two
   near ties of the random-init model's logits), the per-layer hidden states of the last position
   rel-L2 <= 1e-2, KV rows at the page and attention-mode boundaries.
-* The ring buffer at the Qwen3-0.6B shape: context 64 driven to position 223 (sink rows
-  re-rotated, slots reused) on both decode paths, logits and top-1 at every position, hidden
-  states of the last one, and every cache slot of three layers.
+* The ring buffer at the Qwen3-0.6B shape: contexts 64 and 160 driven to position 223 (sink rows
+  re-rotated, slots reused; at 160 the fused kernel's attention runs split over CTAs, past 128
+  cached positions) on both decode paths, logits and top-1 at every position, hidden states of
+  the last one, and every cache slot of three layers.
 
 The oracle (the C restatement, bit-exact with the reference) runs the long prompt layer by layer
 over all tokens (PortModel.forward_many, bit-identical to token-by-token ForwardToken calls).
@@ -147,25 +148,26 @@ WRAP_SINKS = 4  # attention-sink slots (min(4, ctx - 1), src/inference.cpp:605-6
 SINK_K_REL_L2 = 3e-2
 
 
-@pytest.fixture(scope="module")
-def wrap_case(full_weights):
-    """The oracle driven through a context-64 ring buffer at the Qwen3-0.6B shape: logits at
-    every position, hidden states of the last, every cache slot of three layers."""
+@pytest.fixture(scope="module", params=[WRAP_CTX, 160])
+def wrap_case(request, full_weights):
+    """The oracle driven through a ring buffer at the Qwen3-0.6B shape: logits at every
+    position, hidden states of the last, every cache slot of three layers."""
+    ctx = request.param
     toks = np.random.default_rng(77).integers(0, 151936, WRAP_POSITIONS).astype(np.int32)
-    cpu = oracle.PortModel(full_weights, WRAP_CTX)
+    cpu = oracle.PortModel(full_weights, ctx)
     lgs = [cpu.forward(int(t), pos) for pos, t in enumerate(toks[:-1])]
     hid, lg = cpu.forward(int(toks[-1]), WRAP_POSITIONS - 1, layers=True)
     lgs.append(lg)
-    slots = {(l, s): cpu.kv_row(l, s) for l in (0, 13, 27) for s in range(WRAP_CTX)}
-    return toks, np.stack(lgs), hid, slots
+    slots = {(l, s): cpu.kv_row(l, s) for l in (0, 13, 27) for s in range(ctx)}
+    return ctx, toks, np.stack(lgs), hid, slots
 
 
 @pytest.mark.parametrize("path", ["fused", "layerwise"])
 def test_ring_wrap_qwen3_shape(q3lib, full_weights, wrap_case, path):
     """Position math past the context (num_sink, kv_pos, kv_len), sink re-rotation and slot
     reuse of the decode paths at the Qwen3-0.6B shape against the oracle."""
-    toks, lgs, hid, slots = wrap_case
-    m = q3lib.Qwen3(full_weights, WRAP_CTX)
+    ctx, toks, lgs, hid, slots = wrap_case
+    m = q3lib.Qwen3(full_weights, ctx)
     try:
         m.decode_path = m.PATH_FUSED if path == "fused" else m.PATH_LAYERWISE
         am, lg = m.decode_forced(toks[:-1], 0, want_logits=True)
@@ -197,7 +199,7 @@ def test_ring_wrap_qwen3_shape(q3lib, full_weights, wrap_case, path):
             e = max(ek, ev)
             worst_kv = max(worst_kv, e)
             assert e <= KV_REL_L2, (path, l, s, e)
-        report(f"ring wrap ({path})", positions=am.size, agree=agree,
+        report(f"ring wrap ctx {ctx} ({path})", positions=am.size, agree=agree,
                flips=int((am != ref).sum()), logits_max_abs=err, hidden_rel_l2=worst_h,
                kv_rel_l2=worst_kv, sink_k_rel_l2=worst_sink)
         assert agree >= TOP1_AGREEMENT, agree
