@@ -1096,7 +1096,7 @@ __device__ __forceinline__ void unpack8(const uint4 w, float f[8]) {
 // may predate); attention-sink rows are rotated by RoPE(position 1) and re-rounded on the fly
 // (src/inference.cpp:817-827). Updates the warp's online-softmax state (m, l warp-uniform; o per
 // lane over its rows of parity hb).
-__device__ __noinline__ void split_page(const Smem& sm, const FusedArgs& a, const uint8_t* page,
+__device__ __forceinline__ void split_page(const Smem& sm, const FusedArgs& a, const uint8_t* page,
                                         int j, int t0, int t1, int kv_pos, int num_sink,
                                         const float (&q0)[8], const float (&q1)[8], float (&m)[2],
                                         float (&l)[2], float (&o)[2][8]) {
@@ -1104,20 +1104,16 @@ __device__ __noinline__ void split_page(const Smem& sm, const FusedArgs& a, cons
     const int hb = lane >> 4, dl = lane & 15;
     const int tp = j * kPageTokens;
     float sv[16];
-    float vrow[8][8];
+#pragma unroll
     for (int i = 0; i < 8; ++i) {
         const int r = 2 * i + hb, t = tp + r;
         float kf[8];
         unpack8(*reinterpret_cast<const uint4*>(page + (r * HD + 8 * dl) * 2), kf);
-        unpack8(*reinterpret_cast<const uint4*>(page + PAGE_BYTES + (r * HD + 8 * dl) * 2), vrow[i]);
         if (t == kv_pos) {
             const float4* kc = reinterpret_cast<const float4*>(sm.qk[2] + 8 * dl);
-            const float4* vc = reinterpret_cast<const float4*>(sm.qk[3] + 8 * dl);
-            const float4 k0 = kc[0], k1 = kc[1], v0 = vc[0], v1 = vc[1];
+            const float4 k0 = kc[0], k1 = kc[1];
             kf[0] = k0.x; kf[1] = k0.y; kf[2] = k0.z; kf[3] = k0.w;
             kf[4] = k1.x; kf[5] = k1.y; kf[6] = k1.z; kf[7] = k1.w;
-            vrow[i][0] = v0.x; vrow[i][1] = v0.y; vrow[i][2] = v0.z; vrow[i][3] = v0.w;
-            vrow[i][4] = v1.x; vrow[i][5] = v1.y; vrow[i][6] = v1.z; vrow[i][7] = v1.w;
         }
         // Sink rows (page 0 of a wrapped cache): pairs (d, d + 64) sit in lanes dl, dl ^ 8.
         if (tp < num_sink) {
@@ -1201,14 +1197,25 @@ __device__ __noinline__ void split_page(const Smem& sm, const FusedArgs& a, cons
         o[0][d] *= al0;
         o[1][d] *= al1;
     }
+    // o[h] += p(h, row 2i + hb) * V[row] over this lane's rows (V re-read from the page).
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
+        const int r = 2 * i + hb;
         const float p0 = __shfl_sync(0xffffffffu, p, hb * 16 + i);
         const float p1 = __shfl_sync(0xffffffffu, p, hb * 16 + 8 + i);
+        float vf[8];
+        if (tp + r == kv_pos) {
+            const float4* vc = reinterpret_cast<const float4*>(sm.qk[3] + 8 * dl);
+            const float4 v0 = vc[0], v1 = vc[1];
+            vf[0] = v0.x; vf[1] = v0.y; vf[2] = v0.z; vf[3] = v0.w;
+            vf[4] = v1.x; vf[5] = v1.y; vf[6] = v1.z; vf[7] = v1.w;
+        } else {
+            unpack8(*reinterpret_cast<const uint4*>(page + PAGE_BYTES + (r * HD + 8 * dl) * 2), vf);
+        }
 #pragma unroll
         for (int d = 0; d < 8; ++d) {
-            o[0][d] = fmaf(p0, vrow[i][d], o[0][d]);
-            o[1][d] = fmaf(p1, vrow[i][d], o[1][d]);
+            o[0][d] = fmaf(p0, vf[d], o[0][d]);
+            o[1][d] = fmaf(p1, vf[d], o[1][d]);
         }
     }
 }
