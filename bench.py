@@ -68,6 +68,13 @@ def dp_workload(n=DP_SEQS):
 
 # Tensor-parallel single-stream decode: context 32768, a 32000-token prompt of seeded random IDs
 # (seed 4) prefilled on every rank, then 128 greedy steps with heads / MLP split over the ranks.
+TP_ARM_COLLECTIVE = {
+    "fused": "tagged words pushed to every rank from inside the persistent kernel's phases",
+    "graph": "this library's one-shot all-reduce kernel after o_proj and down_proj, one CUDA "
+             "graph per step",
+    "graph_nccl": "ncclAllReduce after o_proj and down_proj and ncclAllGather of the greedy "
+                  "candidates, captured in the same per-step CUDA graph",
+}
 TP_CTX = 32768
 TP_PROMPT = 32000
 TP_STEPS = 128
@@ -455,8 +462,12 @@ def run_b200_arm(args):
 
     pm.close()
 
-    # Tensor-parallel decode of one long-context stream over all ranks.
+    # Tensor-parallel decode of one long-context stream over all ranks: the default path (the
+    # fused persistent kernel with its in-kernel exchange) timed first, then two comparison arms
+    # continuing the same stream: the per-step graph with this library's all-reduce kernels, and
+    # the same graph with NCCL's all-reduce / all-gather captured in their place.
     tp_ms = tp_gbs = tp_bytes_gpu = 0.0
+    tp_arms = {}
     if "tp" in legs:
         tm = q3b200.Qwen3(path, TP_CTX, device=local)
         tprompt = np.random.default_rng(4).integers(0, VOCAB, TP_PROMPT).astype(np.int32)
@@ -464,17 +475,33 @@ def run_b200_arm(args):
         tp = q3b200.TpDecoder(tm, rank, world)
         tp.connect(gather_handles(tp.ipc_handle(), world))
         tpx = torch.cuda.ExternalStream(tp.stream)
-        warm = tp.decode(tnext, TP_PROMPT, TP_WARMUP)
-        torch.cuda.synchronize()
+        uid = [q3b200.TpDecoder.nccl_unique_id() if rank == 0 else None]
         if world > 1:
-            dist.barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(tpx)
-        tp.decode(int(warm[-1]), TP_PROMPT + TP_WARMUP, TP_STEPS)
-        e1.record(tpx)
-        torch.cuda.synchronize()
-        tp_ms = e0.elapsed_time(e1)
-        tp_ms = max_over_ranks(tp_ms, world)
+            dist.broadcast_object_list(uid, src=0)
+        tp.nccl_connect(uid[0])
+        pos, tok = TP_PROMPT, tnext
+        names = {q3b200.TpDecoder.FUSED: "fused", q3b200.TpDecoder.GRAPH: "graph",
+                 q3b200.TpDecoder.GRAPH_NCCL: "graph_nccl"}
+        arms = [tp.path] + [a for a in (q3b200.TpDecoder.GRAPH, q3b200.TpDecoder.GRAPH_NCCL)
+                            if a != tp.path]
+        for arm in arms:
+            tp.path = arm
+            warm = tp.decode(tok, pos, TP_WARMUP)
+            pos += TP_WARMUP
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(tpx)
+            out = tp.decode(int(warm[-1]), pos, TP_STEPS)
+            e1.record(tpx)
+            torch.cuda.synchronize()
+            pos += TP_STEPS
+            tok = int(out[-1])
+            ms = max_over_ranks(e0.elapsed_time(e1), world)
+            tp_arms[names[arm]] = ms
+        tp_default = names[arms[0]]
+        tp_ms = tp_arms[tp_default]
         tp_kv = TP_PROMPT + TP_WARMUP + TP_STEPS / 2
         tp_bytes_gpu = (WEIGHT_BYTES + KV_BYTES_PER_POS * tp_kv) / world
         tp_gbs = tp_bytes_gpu * TP_STEPS / (tp_ms / 1e3) / 1e9
@@ -575,8 +602,16 @@ def run_b200_arm(args):
                 "steps": TP_STEPS, "ms_per_step": round(tp_ms / TP_STEPS, 4),
                 "parallelism": f"tp{world}", "scaling": "strong",
                 "cpu_baseline": cpu_legs.get("tp_decode"),
-                "collective": "this library's own one-shot all-reduce kernel over NVLink peer "
-                              "memory (CUDA IPC handles), not NCCL",
+                "path": tp_default,
+                "collective": ("in-kernel exchange of tagged words over NVLink peer memory (CUDA "
+                               "IPC handles) from the fused decode kernel's phases, not NCCL"
+                               if tp_default == "fused" else
+                               "this library's own one-shot all-reduce kernel over NVLink peer "
+                               "memory (CUDA IPC handles), not NCCL"),
+                "arms": {name: {"ms_per_step": round(ms / TP_STEPS, 4),
+                                "value": round(TP_STEPS / (ms / 1e3), 1),
+                                "collective": TP_ARM_COLLECTIVE[name]}
+                         for name, ms in tp_arms.items()},
                 "roofline": {"bound": "hbm", "achieved": round(tp_gbs, 1),
                              "peak": pk["hbm_gbs"], "unit": "GB/s per GPU",
                              "frac": round(tp_gbs / pk["hbm_gbs"], 4),

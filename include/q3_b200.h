@@ -270,6 +270,20 @@ q3_status q3_tp_decode_forced(q3_tp* tp, const int32_t* tokens_host, int n, int 
  * q3_tp_reset, which every rank calls (and the ranks meet on the host) before decoding again. */
 q3_status q3_tp_configure(q3_tp* tp, int solo_allreduce, long long wait_cycles);
 q3_status q3_tp_reset(q3_tp* tp);
+/* How the steps run (every rank of a group alike): Q3_TP_FUSED, the default where the model has
+ * the fused decode kernel, is one persistent kernel per GPU for up to 256 steps that sends its
+ * o_proj partials, down-projection sums and greedy candidates to every rank from inside its
+ * phases (with solo_allreduce at world 1 they go through this rank's own exchange words);
+ * Q3_TP_GRAPH is one CUDA graph per step with this library's all-reduce kernels;
+ * Q3_TP_GRAPH_NCCL, a comparison arm, is the same graph with ncclAllReduce / ncclAllGather
+ * captured in their place (needs q3_tp_nccl_connect; NCCL is loaded at run time). */
+enum { Q3_TP_FUSED = 0, Q3_TP_GRAPH = 1, Q3_TP_GRAPH_NCCL = 2 };
+q3_status q3_tp_set_path(q3_tp* tp, int path);
+q3_status q3_tp_path(q3_tp* tp, int* path);
+/* NCCL communicator of Q3_TP_GRAPH_NCCL: one process makes a 128-byte unique id, every rank
+ * connects with the same id. */
+q3_status q3_tp_nccl_unique_id(void* id_host);
+q3_status q3_tp_nccl_connect(q3_tp* tp, const void* id_host);
 
 /* ------------------------------------------------------------------ one block (class Block) */
 

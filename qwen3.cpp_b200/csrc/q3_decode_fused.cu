@@ -42,6 +42,8 @@
 #include <limits.h>
 #include <stdlib.h>
 
+#include <algorithm>
+
 #include "q3_decode_fused.cuh"
 
 namespace q3 {
@@ -49,7 +51,7 @@ namespace q3 {
 namespace {
 
 constexpr int D = 1024, H = 3072, NQ = 16, NKV = 8, HD = 128;
-constexpr int QD = NQ * HD, KVD = NKV * HD, QKV_ROWS = QD + 2 * KVD;
+constexpr int QD = NQ * HD, KVD = NKV * HD;
 constexpr int GRP = 2 * HD;            // attention output of one KV-head group (2 query heads)
 constexpr int NCW = 8;                 // consumer warps
 constexpr int NCT = NCW * 32;          // consumer threads
@@ -77,7 +79,18 @@ constexpr int T_SHORT = 128;           // KV positions up to which attention run
 constexpr int ATT_TOK = 24;            // at least this many positions per attention split
 constexpr int PAGE_BYTES = kPageTokens * HD * 2;
 
-enum Mode : int { kTag = 0, kPair = 2, kLogits = 3 };
+enum Mode : int { kTag = 0, kPair = 2, kLogits = 3, kTagX = 4 };
+
+// The kernel is instantiated twice: TP = false for one rank without the exchange (every shard
+// size a compile-time constant: all 8 KV groups, all 3072 MLP indices), TP = true for the
+// tensor-parallel shards of FusedArgs (nkv, kv0, hl, the exchange words).
+template <bool TP>
+struct Shard {
+    __device__ static int nkv(const FusedArgs& a) { return TP ? a.nkv : NKV; }
+    __device__ static int kv0(const FusedArgs& a) { return TP ? a.kv0 : 0; }
+    __device__ static int hl(const FusedArgs& a) { return TP ? a.hl : H; }
+    __device__ static bool xchg(const FusedArgs& a) { return TP && a.xchg != 0; }
+};
 
 struct __align__(128) Smem {
     uint8_t ring[NS][SLOT];
@@ -192,6 +205,40 @@ __device__ __forceinline__ void ld_tagged2(const unsigned long long* p, unsigned
                  : "l"(p)
                  : "memory");
 }
+// Tensor-parallel exchange: words written by other GPUs (or read by them) are accessed at system
+// scope; `sys` is uniform over the launch.
+__device__ __forceinline__ void ld_tagged2x(const unsigned long long* p, unsigned long long& w0,
+                                            unsigned long long& w1, bool sys) {
+    if (sys) {
+        asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];"
+                     : "=l"(w0), "=l"(w1)
+                     : "l"(p)
+                     : "memory");
+    } else {
+        ld_tagged2(p, w0, w1);
+    }
+}
+__device__ __forceinline__ void st_tagged_x(unsigned long long* p, float v, unsigned tag, bool sys) {
+    const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
+    if (sys) {
+        asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+    } else {
+        asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+    }
+}
+// Four tagged words (32-byte aligned) as two 16-byte stores.
+__device__ __forceinline__ void st_tagged4_x(unsigned long long* p, float4 v, unsigned tag, bool sys) {
+    const unsigned long long t = static_cast<unsigned long long>(tag) << 32;
+    const unsigned long long w0 = t | __float_as_uint(v.x), w1 = t | __float_as_uint(v.y);
+    const unsigned long long w2 = t | __float_as_uint(v.z), w3 = t | __float_as_uint(v.w);
+    if (sys) {
+        asm volatile("st.relaxed.sys.global.v2.b64 [%0], {%1, %2};" ::"l"(p), "l"(w0), "l"(w1) : "memory");
+        asm volatile("st.relaxed.sys.global.v2.b64 [%0], {%1, %2};" ::"l"(p + 2), "l"(w2), "l"(w3) : "memory");
+    } else {
+        asm volatile("st.relaxed.gpu.global.v2.b64 [%0], {%1, %2};" ::"l"(p), "l"(w0), "l"(w1) : "memory");
+        asm volatile("st.relaxed.gpu.global.v2.b64 [%0], {%1, %2};" ::"l"(p + 2), "l"(w2), "l"(w3) : "memory");
+    }
+}
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     unsigned v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -271,12 +318,12 @@ __device__ __forceinline__ unsigned step_tag(const FusedArgs& a, int st, int l) 
 
 // Bounded wait until the four tagged words at p (32-byte aligned) carry `tag`; their values.
 __device__ float4 poll4(const FusedArgs& a, const unsigned long long* p, unsigned tag,
-                        volatile int* abort, int site) {
+                        volatile int* abort, int site, bool sys = false) {
     unsigned long long w0, w1, w2, w3;
     const long long t0 = clock64();
     for (uint32_t it = 0;; ++it) {
-        ld_tagged2(p, w0, w1);
-        ld_tagged2(p + 2, w2, w3);
+        ld_tagged2x(p, w0, w1, sys);
+        ld_tagged2x(p + 2, w2, w3, sys);
         if (static_cast<unsigned>(w0 >> 32) == tag && static_cast<unsigned>(w1 >> 32) == tag &&
             static_cast<unsigned>(w2 >> 32) == tag && static_cast<unsigned>(w3 >> 32) == tag) {
             break;
@@ -370,7 +417,7 @@ __device__ __forceinline__ Span part(int rows, int G, int c) {
 }
 
 static_assert(RPC_ROW * D * 2 <= SLOT && RPC_GRP * GRP * 2 <= SLOT &&
-                  2 * RPC_PAIR * D * 2 <= SLOT && 2 * kPageTokens * HD * 2 <= SLOT,
+                  2 * RPC_PAIR * D * 2 <= SLOT && 4 * kPageTokens * HD * 2 <= SLOT,
               "ring slot too small");
 
 __device__ __forceinline__ size_t page_elem(const int32_t* table, int page, int g) {
@@ -394,18 +441,18 @@ __device__ __forceinline__ StepPos step_pos(const FusedArgs& a, const StepParams
     return p;
 }
 
-// Past T_SHORT positions: the positions [t0, t1) of KV head g that CTA c attends to (split
-// c / NKV of head c % NKV; t0 >= t1 for a split past kv_len), `on` for the CTAs that take part.
-// Its KV pages are [j0, j1) (none for an empty split).
+// Past T_SHORT positions: the positions [t0, t1) of this rank's KV group g (local index) that
+// CTA c attends to (split c / nkv of group c % nkv; t0 >= t1 for a split past kv_len), `on` for
+// the CTAs that take part. Its KV pages are [j0, j1) (none for an empty split).
 struct SplitRange {
     bool on;
     int g, s, t0, t1, j0, j1;
 };
-__device__ __forceinline__ SplitRange split_range(const StepPos& p, int c) {
+__device__ __forceinline__ SplitRange split_range(const StepPos& p, int c, int nkv) {
     SplitRange r;
-    r.on = !p.shrt && c < NKV * p.splits;
-    r.g = c % NKV;
-    r.s = c / NKV;
+    r.on = !p.shrt && c < nkv * p.splits;
+    r.g = c % nkv;
+    r.s = c / nkv;
     const int chunk = (p.kv_len + p.splits - 1) / p.splits;
     r.t0 = min(r.s * chunk, p.kv_len);
     r.t1 = min(p.kv_len, r.t0 + chunk);
@@ -426,30 +473,32 @@ __device__ __forceinline__ int barriers_of(const FusedArgs& a, bool shrt) {
 // u; u == n_layers: the first rows of its lm_head slice), so that the ring copies of that unit hit
 // L2 while the HBM stream keeps running through the grid-wide waits in between. Out of line (run
 // once per unit): it stays out of the producer loop's instruction working set.
-__device__ __noinline__ void prefetch_unit(const FusedLayer* layers, int n_layers,
-                                           const uint16_t* lm_head, int vocab, int u, int G, int c) {
-    const int P = G / NKV;
-    const int g = c % NKV, p = c / NKV;
-    if (u < n_layers) {
-        const FusedLayer w = layers[u];
-        Span sp = part(QKV_ROWS, G, c);
+template <bool TP>
+__device__ __noinline__ void prefetch_unit(const FusedArgs& a, int u, int G, int c) {
+    const int nkv = Shard<TP>::nkv(a);
+    const int P = G / nkv;
+    const int g = Shard<TP>::kv0(a) + c % nkv, p = c / nkv;
+    if (u < a.n_layers) {
+        const FusedLayer w = a.layers[u];
+        Span sp = part(nkv * 4 * HD, G, c);
         prefetch_l2(w.wqkv + static_cast<size_t>(sp.r0) * D, sp.n * D * 2);
-        if (c < NKV * P) {
+        if (c < nkv * P) {
             sp = part(D, P, p);
             prefetch_l2(w.wop + static_cast<size_t>(g) * D * GRP + static_cast<size_t>(sp.r0) * GRP,
                         sp.n * GRP * 2);
         }
-        sp = part(H, G, c);
+        sp = part(Shard<TP>::hl(a), G, c);
         prefetch_l2(w.w1 + static_cast<size_t>(sp.r0) * D, sp.n * D * 2);
         prefetch_l2(w.w3 + static_cast<size_t>(sp.r0) * D, sp.n * D * 2);
         prefetch_l2(w.w2t + static_cast<size_t>(sp.r0) * D, sp.n * D * 2);
     } else {
-        const Span sp = part(vocab, G, c);
-        prefetch_l2(lm_head + static_cast<size_t>(sp.r0) * D, min(sp.n, 96) * D * 2);
+        const Span sp = part(a.vocab, G, c);
+        prefetch_l2(a.lm_head + static_cast<size_t>(sp.r0) * D, min(sp.n, 96) * D * 2);
     }
 }
 
 
+template <bool TP>
 struct Producer {
     Smem& sm;
     const FusedArgs& a;
@@ -470,20 +519,43 @@ struct Producer {
                       31, reinterpret_cast<uintptr_t>(s1), reinterpret_cast<uintptr_t>(s2), q)) {
             return false;
         }
-        if (q >= NS) {
-            const uint32_t par = ((q / NS) - 1) & 1;
-            if (a.prof && !mbar_test_wait(&sm.empty[slot], par)) {
-                const long long t0 = clock64();
-                const bool ok = mbar_wait(&sm.empty[slot], par, a, &sm.abort_flag, 2, q, kProducerSleepNs);
-                blocked += clock64() - t0;
-                if (!ok) return false;
-            } else if (!mbar_wait(&sm.empty[slot], par, a, &sm.abort_flag, 2, q, kProducerSleepNs)) {
-                return false;
-            }
-        }
+        if (!take_slot(slot)) return false;
         mbar_arrive_expect_tx(&sm.full[slot], b1 + b2);
         bulk_g2s(sm.ring[slot], s1, b1, &sm.full[slot], pol);
         if (b2) bulk_g2s(sm.ring[slot] + off2, s2, b2, &sm.full[slot], pol);
+        ++q;
+        return true;
+    }
+
+    // Bounded wait until ring slot `slot` (chunk q) is free: its previous use (chunk q - NS) was
+    // released by every consumer warp.
+    __device__ bool take_slot(int slot) {
+        if (q < NS) return true;
+        const uint32_t par = ((q / NS) - 1) & 1;
+        if (a.prof && !mbar_test_wait(&sm.empty[slot], par)) {
+            const long long t0 = clock64();
+            const bool ok = mbar_wait(&sm.empty[slot], par, a, &sm.abort_flag, 2, q, kProducerSleepNs);
+            blocked += clock64() - t0;
+            return ok;
+        }
+        return mbar_wait(&sm.empty[slot], par, a, &sm.abort_flag, 2, q, kProducerSleepNs);
+    }
+
+    // One chunk of two KV pages: K and V of page e0 at [0, 2 PAGE_BYTES), of page e1 after them.
+    __device__ bool issue_page_pair(const uint16_t* kc, const uint16_t* vc, size_t e0, size_t e1) {
+        const int slot = q % NS;
+        if (!Q3_CHECK(((reinterpret_cast<uintptr_t>(kc + e0) | reinterpret_cast<uintptr_t>(vc + e0) |
+                        reinterpret_cast<uintptr_t>(kc + e1) | reinterpret_cast<uintptr_t>(vc + e1)) &
+                       15) == 0,
+                      32, e0, e1, q)) {
+            return false;
+        }
+        if (!take_slot(slot)) return false;
+        mbar_arrive_expect_tx(&sm.full[slot], 4 * PAGE_BYTES);
+        bulk_g2s(sm.ring[slot], kc + e0, PAGE_BYTES, &sm.full[slot], pol_kv);
+        bulk_g2s(sm.ring[slot] + PAGE_BYTES, vc + e0, PAGE_BYTES, &sm.full[slot], pol_kv);
+        bulk_g2s(sm.ring[slot] + 2 * PAGE_BYTES, kc + e1, PAGE_BYTES, &sm.full[slot], pol_kv);
+        bulk_g2s(sm.ring[slot] + 3 * PAGE_BYTES, vc + e1, PAGE_BYTES, &sm.full[slot], pol_kv);
         ++q;
         return true;
     }
@@ -524,11 +596,26 @@ struct Producer {
         return true;
     }
 
+    // K and V pages [j0, j1) of KV head g, layer l, two pages per chunk (a last odd page alone),
+    // for the split attention past T_SHORT positions.
+    __device__ bool kv_page_pairs(int l, int g, int j0, int j1) {
+        const uint16_t* kc = a.k_cache + static_cast<size_t>(l) * a.layer_elems;
+        const uint16_t* vc = a.v_cache + static_cast<size_t>(l) * a.layer_elems;
+        for (int j = j0; j < j1; j += 2) {
+            const size_t e0 = page_elem(a.page_table, j, g);
+            const bool ok = j + 1 < j1
+                                ? issue_page_pair(kc, vc, e0, page_elem(a.page_table, j + 1, g))
+                                : issue(kc + e0, PAGE_BYTES, vc + e0, PAGE_BYTES, PAGE_BYTES, pol_kv);
+            if (!ok) return false;
+        }
+        return true;
+    }
+
     // Prefetches unit k of the whole call (units n_layers + 1 per step) if it exists.
     __device__ void prefetch_ahead(int k, int G, int c) {
         const int per = a.n_layers + 1;
         if (a.l2_ahead > 0 && k < a.n_steps * per) {
-            prefetch_unit(a.layers, a.n_layers, a.lm_head, a.vocab, k % per, G, c);
+            prefetch_unit<TP>(a, k % per, G, c);
         }
     }
 
@@ -536,9 +623,10 @@ struct Producer {
         pol_w = evict_first_policy();
         pol_kv = evict_last_policy();
         const StepParams sp0 = a.sp_from_args ? a.sp_init : *a.sp;
-        const int P = G / NKV;
-        const bool in_grp = c < NKV * P;
-        const int g = c % NKV, p = c / NKV;
+        const int nkv = Shard<TP>::nkv(a), kv0 = Shard<TP>::kv0(a), hl = Shard<TP>::hl(a);
+        const int P = G / nkv;
+        const bool in_grp = c < nkv * P;
+        const int g = kv0 + c % nkv, p = c / nkv;  // KV group (global index) of BC
         const int per = a.n_layers + 1;
         bool ok = true;
         unsigned base = 0, prev_base = 0;
@@ -549,10 +637,10 @@ struct Producer {
             for (int l = 0; ok && l < a.n_layers; ++l) {
                 const FusedLayer w = a.layers[l];
                 prefetch_ahead(st * per + l + a.l2_ahead, G, c);
-                ok = ok && rows<D * 2, RPC_ROW>(w.wqkv, part(QKV_ROWS, G, c));
+                ok = ok && rows<D * 2, RPC_ROW>(w.wqkv, part(nkv * 4 * HD, G, c));
                 // KV pages this CTA's attention reads: all of head g's (short contexts) or those
                 // of its split (long ones).
-                const SplitRange sr = split_range(sp, c);
+                const SplitRange sr = split_range(sp, c, nkv);
                 if (ok && (sp.shrt ? in_grp : sr.on)) {
                     // KV pages of this layer were last written (row kv_pos, sink rows) by the
                     // previous step's phases up to DE(l): wait until every CTA is past them.
@@ -561,14 +649,14 @@ struct Producer {
                         ok = grid_wait(a, G * (de + 1) + a.barrier_offset, &sm.abort_flag, 3);
                     }
                     ok = ok && (sp.shrt ? kv_pages(l, g, 0, chunks_of_i(sp.kv_len, kPageTokens))
-                                        : kv_pages(l, sr.g, sr.j0, sr.j1));
+                                        : kv_page_pairs(l, kv0 + sr.g, sr.j0, sr.j1));
                 }
                 if (in_grp) {
                     ok = ok && rows<GRP * 2, RPC_GRP>(w.wop + static_cast<size_t>(g) * D * GRP,
                                                       part(D, P, p));
                 }
-                ok = ok && pairs(w.w1, w.w3, part(H, G, c));
-                ok = ok && rows<D * 2, RPC_ROW>(w.w2t, part(H, G, c));
+                ok = ok && pairs(w.w1, w.w3, part(hl, G, c));
+                ok = ok && rows<D * 2, RPC_ROW>(w.w2t, part(hl, G, c));
             }
             prefetch_ahead(st * per + a.n_layers + a.l2_ahead, G, c);
             ok = ok && rows<D * 2, RPC_ROW>(a.lm_head, part(a.vocab, G, c));
@@ -578,7 +666,7 @@ struct Producer {
         }
         // This CTA's rows of the first layer into L2 for the next launch (a decode loop of
         // one-step calls would otherwise start every step on a cold stream).
-        if (ok && a.l2_ahead > 0) prefetch_unit(a.layers, a.n_layers, a.lm_head, a.vocab, 0, G, c);
+        if (ok && a.l2_ahead > 0) prefetch_unit<TP>(a, 0, G, c);
         if (a.prof) a.prof[static_cast<size_t>(c) * 8 + 4] = blocked;
         // Wait for every copy still in flight before the CTA may exit.
         const uint32_t first = q > NS ? q - NS : 0;
@@ -749,14 +837,14 @@ __device__ __forceinline__ float4 add4(float4 a, float4 b) {
 
 // Dot the rows of this CTA's warp-owned chunks of one task (chunks q0.. of `rpc` rows of K
 // elements) with the staged activation, epilogue by `mode`: kTag writes row r as a tagged word to
-// outt[r], kPair h to out[], kLogits the logits to out[] and leaves each warp's best (value, index)
-// in sm.best. After an abort the remaining chunks are skipped (each wait then fails at once) but
+// outt[r], kTagX to a.opart_dst[d][xoff + r] of every rank d, kPair h to out[], kLogits the logits
+// to out[] and leaves each warp's best (value, index) in sm.best. After an abort the remaining chunks are skipped (each wait then fails at once) but
 // the warp still returns, so every consumer thread reaches the same barriers.
 template <int K, int rpc, int mode>
 __device__ __forceinline__ void consume_rows(Smem& sm, const FusedArgs& a, uint32_t q0, int r0,
                                              int n, float* out, int out_n,
                                              unsigned long long* outt = nullptr,
-                                             unsigned tag = 0) {
+                                             unsigned tag = 0, size_t xoff = 0) {
     static_assert(mode == kPair ? rpc == 4 : rpc == 8, "one 8-row dot group per chunk");
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, t = lane & 3;
     const int nch = (n + rpc - 1) / rpc;
@@ -796,6 +884,9 @@ __device__ __forceinline__ void consume_rows(Smem& sm, const FusedArgs& a, uint3
                 if (!Q3_CHECK(r >= 0 && r < out_n, 52, r, out_n, mode)) break;
                 if (mode == kLogits) out[r] = yy[j];
                 if (mode == kTag) st_tagged(outt + r, yy[j], tag);
+                if (mode == kTagX) {
+                    for (int d = 0; d < a.world; ++d) st_tagged_x(a.opart_dst[d] + xoff + r, yy[j], tag, a.sys);
+                }
                 if (mode == kLogits && better(yy[j], r, bv, bi)) {
                     bv = yy[j];
                     bi = r;
@@ -889,12 +980,16 @@ __device__ __forceinline__ void head_preload(HeadPre& hp, const FusedArgs& a, co
 
 // QK-RMSNorm (src/inference.cpp:800-807) + RoPE (:809-810) of q heads 2g, 2g+1 and k head g into
 // sm.qk[0..2]; v head g into sm.qk[3]; k and v rounded to bf16 as the cache stores them (:812-815)
-// and, when `writer`, written to the cache at kv_pos. Ends with a consumer barrier.
+// and, when `writer`, written to the cache at kv_pos. g: global KV head; gl: its index among this
+// rank's groups (the rows of a.qkvt: q of the 2 nkv local query heads, then k, then v). Ends with
+// a consumer barrier.
 __device__ __forceinline__ void prep_heads(Smem& sm, const FusedArgs& a, const HeadPre& hp, int l,
-                                        int g, int kv_pos, bool writer, unsigned tag) {
+                                        int nkv, int gl, int g, int kv_pos, bool writer,
+                                        unsigned tag) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int qd = nkv * 2 * HD, kvd = nkv * HD;
     if (warp < 3) {
-        const unsigned long long* src = warp < 2 ? a.qkvt + (2 * g + warp) * HD : a.qkvt + QD + g * HD;
+        const unsigned long long* src = warp < 2 ? a.qkvt + (2 * gl + warp) * HD : a.qkvt + qd + gl * HD;
         const float4 e = poll4(a, src + 4 * lane, tag, &sm.abort_flag, 1);
         const float ss = warp_sum(e.x * e.x + e.y * e.y + e.z * e.z + e.w * e.w);
         const float inv = 1.0f / sqrtf(ss / static_cast<float>(HD) + a.eps);
@@ -911,7 +1006,7 @@ __device__ __forceinline__ void prep_heads(Smem& sm, const FusedArgs& a, const H
         }
         reinterpret_cast<float4*>(sm.qk[warp])[lane] = make_float4(y[0], y[1], y[2], y[3]);
     } else if (warp == 3) {
-        const float4 e = poll4(a, a.qkvt + QD + KVD + g * HD + 4 * lane, tag, &sm.abort_flag, 2);
+        const float4 e = poll4(a, a.qkvt + qd + kvd + gl * HD + 4 * lane, tag, &sm.abort_flag, 2);
         float y[4] = {e.x, e.y, e.z, e.w};
         const uint2 vb = pack_bf16x4(y);
         unpack_bf16x4(vb, y);
@@ -1224,9 +1319,11 @@ __device__ __forceinline__ void split_page(const Smem& sm, const FusedArgs& a, c
 // from its KV pages [t0 / 16, ceil(t1 / 16)) in the ring (shared chunks: every warp waits for and
 // releases each); warp w attends over every NCW-th page; the warps' states are merged into the
 // split's (max, sum, unnormalised output) partials.
-__device__ __forceinline__ void attention_split(Smem& sm, const FusedArgs& a, int t0, int t1,
-                                                int kv_pos, int num_sink, int g, int split,
-                                                uint32_t q0) {
+// Out of line (its register allocation stays apart from the rest of the kernel's); the shared
+// memory is re-derived from the kernel's extern array so that its accesses stay shared-space ones.
+__device__ __noinline__ void attention_split(const FusedArgs& a, int t0, int t1, int kv_pos,
+                                             int num_sink, int g, int split, uint32_t q0) {
+    Smem& sm = *reinterpret_cast<Smem*>(smem_raw_ptr());
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int dl = lane & 15;
     float q0r[8], q1r[8];
@@ -1239,12 +1336,18 @@ __device__ __forceinline__ void attention_split(Smem& sm, const FusedArgs& a, in
     float o[2][8];
 #pragma unroll
     for (int d = 0; d < 8; ++d) o[0][d] = o[1][d] = 0.0f;
+    // Pages [j0, j1) arrive two per chunk; page j0 + i belongs to warp i % NCW, so a warp's pages
+    // sit in every fourth chunk and alternate between two ring slots: the next one lands while
+    // the warp works on the current one.
     const int j0 = t0 / kPageTokens, j1 = t1 > t0 ? (t1 + kPageTokens - 1) / kPageTokens : j0;
-    for (int j = j0; j < j1; ++j) {
-        const uint32_t qq = q0 + (j - j0);
+    const int np = j1 - j0;
+    for (int ci = 0; 2 * ci < np; ++ci) {
+        const uint32_t qq = q0 + ci;
         const int slot = qq % NS;
-        if (warp_wait_full(sm, slot, (qq / NS) & 1, a) && (j - j0) % NCW == warp) {
-            split_page(sm, a, sm.ring[slot], j, t0, t1, kv_pos, num_sink, q0r, q1r, m, l, o);
+        const int h = (warp - 2 * ci) & (NCW - 1);  // this warp's page in the chunk when h < 2
+        if (warp_wait_full(sm, slot, (qq / NS) & 1, a) && h < 2 && 2 * ci + h < np) {
+            split_page(sm, a, sm.ring[slot] + h * 2 * PAGE_BYTES, j0 + 2 * ci + h, t0, t1, kv_pos,
+                       num_sink, q0r, q1r, m, l, o);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.empty[slot]);  // one of NCW releases of a shared chunk
@@ -1347,8 +1450,9 @@ __device__ __forceinline__ void sink_writeback(const FusedArgs& a, const HeadPre
     row[lane] = pack_bf16x4(y);
 }
 
-// Greedy argmax over the per-CTA partials (one warp), lowest index on ties.
-__device__ __forceinline__ int reduce_argmax(const FusedArgs& a, int G) {
+// Greedy argmax over the per-CTA partials (one warp), lowest index on ties: (value, index bits),
+// the index local to this rank's lm_head rows (INT_MAX when there are none).
+__device__ __forceinline__ float2 reduce_argmax(const FusedArgs& a, int G) {
     const int lane = threadIdx.x & 31;
     float bv = -FLT_MAX;
     int bi = INT_MAX;
@@ -1358,6 +1462,69 @@ __device__ __forceinline__ int reduce_argmax(const FusedArgs& a, int G) {
         if (better(p.x, j, bv, bi)) {
             bv = p.x;
             bi = j;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float v = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int j = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (better(v, j, bv, bi)) {
+            bv = v;
+            bi = j;
+        }
+    }
+    return make_float2(bv, __int_as_float(bi));
+}
+
+// Bounded wait until the two tagged words at p (16-byte aligned) carry `tag`.
+__device__ bool poll2(const FusedArgs& a, const unsigned long long* p, unsigned tag,
+                      volatile int* abort, unsigned long long& w0, unsigned long long& w1) {
+    const long long t0 = clock64();
+    for (uint32_t it = 0;; ++it) {
+        ld_tagged2x(p, w0, w1, a.sys != 0);
+        if (static_cast<unsigned>(w0 >> 32) == tag && static_cast<unsigned>(w1 >> 32) == tag) {
+            return true;
+        }
+        if ((it & 15) == 15) {
+            if (*abort || *reinterpret_cast<volatile unsigned*>(a.err) != 0u) {
+                *abort = 1;
+                return false;
+            }
+            if (clock64() - t0 > a.spin_cycles) {
+                *abort = 1;
+                atomicOr(a.err, 1u);
+                Q3_CHECK(false, 3006, tag, static_cast<long long>(w0 >> 32), 0);
+                return false;
+            }
+        }
+    }
+}
+
+// The greedy token of step st over every rank's lm_head rows (one warp per CTA): CTA 0 sends
+// this rank's best (value, global index) to every rank as two tagged words; lane r waits for
+// rank r's pair and the warp keeps the best (lowest index on ties, src/inference.cpp:703-709).
+// One rank without the exchange: the local best.
+__device__ __noinline__ int greedy_token(Smem& sm, const FusedArgs& a, int G, int st, int c) {
+    const int lane = threadIdx.x & 31;
+    const float2 lb = reduce_argmax(a, G);
+    int bi = __float_as_int(lb.y);
+    if (!a.xchg) return bi == INT_MAX ? 0 : bi;  // one rank of the TP instance, no exchange
+    const unsigned tag = step_tag(a, st, 0);
+    if (c == 0 && lane == 0) {
+        const unsigned gi = bi == INT_MAX ? 0x7fffffffu : static_cast<unsigned>(bi + a.v0);
+        for (int d = 0; d < a.world; ++d) {
+            unsigned long long* p = a.amx_dst[d] + 2 * a.rank;
+            st_tagged_x(p, lb.x, tag, a.sys != 0);
+            st_tagged_x(p + 1, __uint_as_float(gi), tag, a.sys != 0);
+        }
+    }
+    float bv = -FLT_MAX;
+    bi = INT_MAX;
+    if (lane < a.world) {
+        unsigned long long w0, w1;
+        if (poll2(a, a.amx + 2 * lane, tag, &sm.abort_flag, w0, w1)) {
+            bv = __uint_as_float(static_cast<unsigned>(w0));
+            bi = static_cast<int>(static_cast<unsigned>(w1));
         }
     }
 #pragma unroll
@@ -1427,11 +1594,52 @@ __device__ __forceinline__ float4 sum_y(const float* y) {
     return t;
 }
 
+// Tensor parallelism: x's down-projection update of layer lp (step st) summed over the ranks in
+// rank order (the same sum on every rank): CTA 0 sends this rank's sum (the kYRep copies at y) to
+// every rank as tagged words; every thread then waits for its four elements from each rank. The
+// words alternate between two buffers from one exchange to the next: a rank writes a buffer again
+// two exchanges later, after every rank's CTAs have read it (each rank's next exchange follows
+// its DE grid barrier, which every CTA reaches after phase A).
+__device__ __noinline__ float4 y_exchange(Smem& sm, const FusedArgs& a, const float* y, int st, int lp, int c) {
+    const int x = st * a.n_layers + lp;
+    const unsigned tag = step_tag(a, st, lp);
+    const size_t base = static_cast<size_t>(x & 1) * kFusedMaxRanks * D + 4 * threadIdx.x;
+    if (c == 0) {
+        const float4 v = sum_y(y);
+        for (int d = 0; d < a.world; ++d) {
+            st_tagged4_x(a.yx_dst[d] + base + static_cast<size_t>(a.rank) * D, v, tag, a.sys != 0);
+        }
+    }
+    float4 t = poll4(a, a.yx + base, tag, &sm.abort_flag, 5, a.sys != 0);
+    for (int r = 1; r < a.world; ++r) {
+        t = add4(t, poll4(a, a.yx + base + static_cast<size_t>(r) * D, tag, &sm.abort_flag, 5,
+                          a.sys != 0));
+    }
+    return t;
+}
+
+// x = Xcur + Y[lp]: this rank's accumulators, or the ranks' sums through the exchange.
+template <bool TP>
+__device__ __forceinline__ float4 x_after(Smem& sm, const FusedArgs& a, float4 xcur, const float* yb,
+                                          int st, int lp, int c) {
+    const float* y = yb + static_cast<size_t>(lp) * kYRep * D;
+    return add4(xcur, Shard<TP>::xchg(a) ? y_exchange(sm, a, y, st, lp, c) : sum_y(y));
+}
+
+// Greedy token of step st: this rank's best (TP = false), else over every rank.
+template <bool TP>
+__device__ __forceinline__ int step_token(Smem& sm, const FusedArgs& a, int G, int st, int c) {
+    if (TP) return greedy_token(sm, a, G, st, c);
+    const int bi = __float_as_int(reduce_argmax(a, G).y);
+    return bi == INT_MAX ? 0 : bi;
+}
+
 // Phase A input: the embedding row of the step's token (layer 0; the token is the greedy argmax of
 // the previous step, or the teacher-forced one) or x = Xcur + Y[l-1], with Xcur this thread's four
 // elements of the residual stream after the previous layer's o_proj (kept in registers) and yb the
 // step's down-projection accumulators; writes (CTA 0) the debug tap. Returns this thread's
 // four elements of x.
+template <bool TP>
 __device__ __forceinline__ float4 phase_a_input(Smem& sm, const FusedArgs& a, const StepParams& sp0,
                                              int st, int l, float4 xcur, const float* yb, int G,
                                              int c) {
@@ -1441,7 +1649,7 @@ __device__ __forceinline__ float4 phase_a_input(Smem& sm, const FusedArgs& a, co
         if (warp == 0) {
             int tok = sp0.token;
             if (st > 0) {
-                const int best = reduce_argmax(a, G);
+                const int best = step_token<TP>(sm, a, G, st - 1, c);
                 const int idx = sp0.step + st;
                 tok = (a.forced && idx < sp0.n_forced) ? __ldg(a.forced + idx) : best;
                 if (c == 0 && lane == 0) a.token_log[idx - 1] = best;
@@ -1459,7 +1667,7 @@ __device__ __forceinline__ float4 phase_a_input(Smem& sm, const FusedArgs& a, co
         const Span ys = part(a.n_layers * kYRep * D, G, c);
         for (int i = tid; i < ys.n; i += NCT) yz[ys.r0 + i] = 0.0f;
     } else {
-        xv = add4(xcur, sum_y(yb + static_cast<size_t>(l - 1) * kYRep * D));
+        xv = x_after<TP>(sm, a, xcur, yb, st, l - 1, c);
     }
     if (a.taps && c == 0) reinterpret_cast<float4*>(a.taps + static_cast<size_t>(l) * D)[tid] = xv;
     return xv;
@@ -1469,14 +1677,15 @@ __device__ __forceinline__ float4 phase_a_input(Smem& sm, const FusedArgs& a, co
 // elements, from the tagged o_proj partials of phase BC / C.
 // The first probes of all eight groups are issued together (one L2 round trip when the partials
 // have landed); only groups not yet written are then polled, one after another.
+template <bool SYS>
 __device__ __forceinline__ float4 gather_oproj(Smem& sm, const FusedArgs& a, float4 xv,
                                                unsigned tag) {
     unsigned long long w[NKV][4];
 #pragma unroll
     for (int gg = 0; gg < NKV; ++gg) {
         const unsigned long long* p = a.opart + static_cast<size_t>(gg) * D + 4 * threadIdx.x;
-        ld_tagged2(p, w[gg][0], w[gg][1]);
-        ld_tagged2(p + 2, w[gg][2], w[gg][3]);
+        ld_tagged2x(p, w[gg][0], w[gg][1], SYS);
+        ld_tagged2x(p + 2, w[gg][2], w[gg][3], SYS);
     }
     float4 proj = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
@@ -1491,13 +1700,14 @@ __device__ __forceinline__ float4 gather_oproj(Smem& sm, const FusedArgs& a, flo
                                 __uint_as_float(static_cast<unsigned>(w[gg][2])),
                                 __uint_as_float(static_cast<unsigned>(w[gg][3])))
                   : poll4(a, a.opart + static_cast<size_t>(gg) * D + 4 * threadIdx.x, tag,
-                          &sm.abort_flag, 3);
+                          &sm.abort_flag, 3, SYS);
         proj = add4(proj, p);
     }
     return add4(xv, proj);
 }
 
-__global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) {
+template <bool TP>
+__global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const __grid_constant__ FusedArgs a) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1533,7 +1743,7 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) 
 
     if (warp == NCW) {
         if (lane == 0) {
-            Producer pr{sm, a};
+            Producer<TP> pr{sm, a};
             pr.run(G, c);
         }
         return;
@@ -1541,9 +1751,10 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) 
 
     // ---------------- consumers
     const StepParams sp0 = a.sp_from_args ? a.sp_init : *a.sp;
-    const int P = G / NKV;
-    const bool in_grp = c < NKV * P;
-    const int g = c % NKV, gp = c / NKV;
+    const int nkv = Shard<TP>::nkv(a), kv0 = Shard<TP>::kv0(a), hl = Shard<TP>::hl(a);
+    const int P = G / nkv;
+    const bool in_grp = c < nkv * P;
+    const int gl = c % nkv, g = kv0 + gl, gp = c / nkv;  // BC: KV group (local, global)
     unsigned k = 0;   // global phase index (profiling stamps)
     unsigned nb = 0;  // grid arrivals every CTA has made so far
     uint32_t q = 0;   // ring chunk index
@@ -1560,14 +1771,15 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) 
             {
                 const uint2 nw = load_norm(w.attn_norm);
                 if (!phase_begin(sm, a, k, nb, G, c)) return;
-                xv = phase_a_input(sm, a, sp0, st, l, xcur, yb, G, c);
+                xv = phase_a_input<TP>(sm, a, sp0, st, l, xcur, yb, G, c);
                 stage_norm(sm, xv, nw, a.eps);
                 stamp(a, k, G, c, 3);
-                const Span s = part(QKV_ROWS, G, c);
+                const int qkv_rows = nkv * 4 * HD;
+                const Span s = part(qkv_rows, G, c);
                 if (chunks_of(s.n, RPC_ROW) * 2 <= NCW) {
                     consume_rows_halves(sm, a, q, s.r0, s.n, a.qkvt, tag);
                 } else {
-                    consume_rows<D, RPC_ROW, kTag>(sm, a, q, s.r0, s.n, nullptr, QKV_ROWS, a.qkvt, tag);
+                    consume_rows<D, RPC_ROW, kTag>(sm, a, q, s.r0, s.n, nullptr, qkv_rows, a.qkvt, tag);
                 }
                 q += chunks_of(s.n, RPC_ROW);
                 stamp(a, k, G, c, 4);
@@ -1576,17 +1788,18 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) 
             HeadPre hp;
             head_preload(hp, a, w, p.pos);
             const Span os = part(D, P, gp);
-            unsigned long long* opart_g = a.opart + static_cast<size_t>(g) * D;
+            const size_t opart_g = static_cast<size_t>(g) * D;  // group g's partial in every opart
             if (p.shrt) {
                 // ---- BC: attention of KV head g from the ring, o_proj partial of group g
                 if (!phase_begin(sm, a, k, 0, G, c)) return;
                 if (in_grp) {
-                    prep_heads(sm, a, hp, l, g, p.kv_pos, gp == 0, tag);
+                    prep_heads(sm, a, hp, l, nkv, gl, g, p.kv_pos, gp == 0, tag);
                     stamp(a, k, G, c, 2);
-                    attention_short(sm, a, hp, p.kv_len, p.kv_pos, p.num_sink, g, q);
+                    attention_short(sm, a, hp, p.kv_len, p.kv_pos, p.num_sink, gl, q);
                     q += chunks_of(p.kv_len, kPageTokens);
                     stamp(a, k, G, c, 3);
-                    consume_rows<GRP, RPC_GRP, kTag>(sm, a, q, os.r0, os.n, nullptr, D, opart_g, tag);
+                    consume_rows<GRP, RPC_GRP, TP ? kTagX : kTag>(sm, a, q, os.r0, os.n, nullptr, D,
+                                                                  a.opart + opart_g, tag, opart_g);
                     q += chunks_of(os.n, RPC_GRP);
                     stamp(a, k, G, c, 4);
                 }
@@ -1594,20 +1807,21 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) 
             } else {
                 // ---- B: split-K attention partials
                 if (!phase_begin(sm, a, k, 0, G, c)) return;
-                const SplitRange sr = split_range(p, c);
+                const SplitRange sr = split_range(p, c, nkv);
                 if (sr.on) {
                     const bool own = p.kv_pos >= sr.t0 && p.kv_pos < sr.t1;
-                    prep_heads(sm, a, hp, l, sr.g, p.kv_pos, own, tag);
-                    attention_split(sm, a, sr.t0, sr.t1, p.kv_pos, p.num_sink, sr.g, sr.s, q);
-                    q += static_cast<uint32_t>(sr.j1 - sr.j0);
+                    prep_heads(sm, a, hp, l, nkv, sr.g, kv0 + sr.g, p.kv_pos, own, tag);
+                    attention_split(a, sr.t0, sr.t1, p.kv_pos, p.num_sink, sr.g, sr.s, q);
+                    q += static_cast<uint32_t>(chunks_of_i(sr.j1 - sr.j0, 2));
                 }
                 phase_end(sm, a, k++, true, G, c);
                 ++nb;
                 // ---- C: combine + o_proj partial of group g
                 if (!phase_begin(sm, a, k, nb, G, c)) return;
                 if (in_grp) {
-                    combine_group(sm, a, p.splits, g);
-                    consume_rows<GRP, RPC_GRP, kTag>(sm, a, q, os.r0, os.n, nullptr, D, opart_g, tag);
+                    combine_group(sm, a, p.splits, gl);
+                    consume_rows<GRP, RPC_GRP, TP ? kTagX : kTag>(sm, a, q, os.r0, os.n, nullptr, D,
+                                                                  a.opart + opart_g, tag, opart_g);
                     q += chunks_of(os.n, RPC_GRP);
                 }
                 phase_end(sm, a, k++, false, G, c);
@@ -1616,10 +1830,11 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) 
             {
                 const uint2 mw = load_norm(w.mlp_norm);
                 if (!phase_begin(sm, a, k, 0, G, c)) return;
-                xcur = gather_oproj(sm, a, xv, tag);
+                xcur = (TP && a.sys) ? gather_oproj<true>(sm, a, xv, tag)
+                                     : gather_oproj<false>(sm, a, xv, tag);
                 stage_norm(sm, xcur, mw, a.eps);
                 stamp(a, k, G, c, 2);
-                const Span hs = part(H, G, c);
+                const Span hs = part(hl, G, c);
                 consume_rows<D, RPC_PAIR, kPair>(sm, a, q, hs.r0, hs.n, sm.hbuf, 64);
                 q += chunks_of(hs.n, RPC_PAIR);
                 bar_consumers();
@@ -1628,7 +1843,7 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) 
                 q += chunks_of(hs.n, RPC_ROW);
                 stamp(a, k, G, c, 4);
                 red_add4(yb + (static_cast<size_t>(l) * kYRep + c % kYRep) * D + 4 * tid, yd);
-                if (c < NKV && p.num_sink > 0) sink_writeback(a, hp, l, c, p.num_sink);
+                if (c < nkv && p.num_sink > 0) sink_writeback(a, hp, l, kv0 + c, p.num_sink);
                 phase_end(sm, a, k++, true, G, c);
                 ++nb;
             }
@@ -1636,7 +1851,7 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) 
         // ---- final RmsNorm + lm_head + per-CTA argmax
         const uint2 fw = load_norm(a.final_norm);
         if (!phase_begin(sm, a, k, nb, G, c)) return;
-        const float4 xv = add4(xcur, sum_y(yb + static_cast<size_t>(a.n_layers - 1) * kYRep * D));
+        const float4 xv = x_after<TP>(sm, a, xcur, yb, st, a.n_layers - 1, c);
         if (a.taps && c == 0) {
             reinterpret_cast<float4*>(a.taps + static_cast<size_t>(a.n_layers) * D)[tid] = xv;
         }
@@ -1666,7 +1881,7 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const FusedArgs a) 
     if (c == 0) {
         if (!phase_begin(sm, a, k, nb, G, c)) return;
         if (warp == 0) {
-            const int best = reduce_argmax(a, G);
+            const int best = step_token<TP>(sm, a, G, a.n_steps - 1, c);
             if (lane == 0) {
                 const int idx = sp0.step + a.n_steps;
                 a.token_log[idx - 1] = best;
@@ -1752,11 +1967,14 @@ int fused_phases_per_step(int n_layers, int kv_len) {
 int fused_grid(int device) {
     int sms = 0;
     Q3_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
-    Q3_CUDA(cudaFuncSetAttribute(decode_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(sizeof(Smem))));
-    int per_sm = 0;
-    Q3_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_fused_kernel, NT,
-                                                          sizeof(Smem)));
+    int per_sm = 1;
+    for (auto kern : {decode_fused_kernel<false>, decode_fused_kernel<true>}) {
+        Q3_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(sizeof(Smem))));
+        int n = 0;
+        Q3_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, NT, sizeof(Smem)));
+        per_sm = std::min(per_sm, n);
+    }
     if (per_sm < 1) return 0;
     // Every CTA must own at most 64 MLP indices (the h buffer) and the grid must cover 8 groups.
     if (sms < 48) return 0;
@@ -1774,7 +1992,12 @@ void launch_decode_fused(const FusedArgs& a, int grid, cudaStream_t s) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    Q3_CUDA(cudaLaunchKernelEx(&cfg, decode_fused_kernel, a));
+    // The tensor-parallel instance for several ranks or a routed exchange; else the one-rank one.
+    if (a.world > 1 || a.xchg) {
+        Q3_CUDA(cudaLaunchKernelEx(&cfg, decode_fused_kernel<true>, a));
+    } else {
+        Q3_CUDA(cudaLaunchKernelEx(&cfg, decode_fused_kernel<false>, a));
+    }
 }
 
 void launch_permute_wo(const uint16_t* wo, uint16_t* wop, cudaStream_t s) {

@@ -11,22 +11,9 @@
 
 namespace q3 {
 
-// Per-layer weights as the fused kernel streams them: copies made at load time so that every
-// CTA's share of a phase is one contiguous byte range, with the row-parity swizzle on the matrices
-// multiplied by MMAs (wqkv, wop, w1, w3 and the lm_head copy):
-//   wop[g][r][j] = wo[r][256*g + j]   (o_proj split by KV-head group: [8][1024][256])
-//   w2t[i][r]    = w2[r][i]           (down_proj split by MLP index: [3072][1024])
-struct FusedLayer {
-    const uint16_t* wqkv;       // [4096][1024]: wq; wk; wv rows (swizzled)
-    const uint16_t* wop;        // [8][1024][256] (swizzled)
-    const uint16_t* w1;         // [3072][1024] (swizzled)
-    const uint16_t* w3;         // [3072][1024] (swizzled)
-    const uint16_t* w2t;        // [3072][1024]
-    const uint16_t* attn_norm;  // [1024]
-    const uint16_t* q_norm;     // [128]
-    const uint16_t* k_norm;     // [128]
-    const uint16_t* mlp_norm;   // [1024]
-};
+constexpr int kFusedMaxRanks = 8;
+
+// FusedLayer (the per-layer weight copies the kernel streams) is declared in q3_model.cuh.
 
 struct FusedArgs {
     const FusedLayer* layers;    // device array [n_layers]
@@ -68,7 +55,26 @@ struct FusedArgs {
                                  // ring copies (0: none)
     unsigned long long* prof;    // nullable: per (phase, CTA) globaltimer stamps [k][G][8]
     unsigned long long* dbg;     // nullable: first failed self-check (builds with Q3_FUSED_CHECKS)
+
+    // Tensor parallelism (one kernel per GPU, `world` ranks). This rank runs KV-head groups
+    // [kv0, kv0 + nkv) (layers[].wqkv then holds only their [wq;wk;wv] rows: q rows of the 2 nkv
+    // query heads, k rows, v rows), MLP indices [rank hl, rank hl + hl) (layers[].w1 / w3 / w2t
+    // point at them) and lm_head rows [v0, v0 + vocab). One rank: nkv 8, kv0 0, hl 3072, v0 0.
+    int nkv, kv0, hl, v0;
+    int world, rank;
+    // xchg: exchange the down-projection sums and the greedy argmax between ranks through the
+    // tagged words below (set for world > 1; at world 1 it routes them through this rank's own
+    // buffers). sys: the exchanged words cross GPUs (system-scope accesses).
+    int xchg, sys;
+    unsigned long long* opart_dst[kFusedMaxRanks];  // every rank's opart (this rank's = opart)
+    unsigned long long* yx;                          // [2][kFusedMaxRanks][1024] per-rank sums
+    unsigned long long* yx_dst[kFusedMaxRanks];
+    unsigned long long* amx;                         // [kFusedMaxRanks][2] (value, index) words
+    unsigned long long* amx_dst[kFusedMaxRanks];
 };
+
+// Tagged words of the tensor-parallel exchange region (opart [8][1024], yx, amx), in u64 words.
+constexpr size_t kFusedXchgWords = 8 * 1024 + 2 * kFusedMaxRanks * 1024 + 2 * kFusedMaxRanks;
 
 // Whether the fused kernel serves this config, and its launch geometry on `device`.
 bool fused_supported(const q3_config& c);

@@ -682,6 +682,7 @@ Model::Model(const std::string& path, int ctx, int device) : file_(path) {
             fused_lm_ = wp + per_layer * c.n_layers;
             launch_swizzle_rows(output_, const_cast<uint16_t*>(fused_lm_), V, static_cast<int>(D), ls);
             Q3_CUDA(cudaStreamSynchronize(ls));
+            fused_host_layers_ = fl;
             fused_layers_.alloc(fl.size() * sizeof(FusedLayer));
             Q3_CUDA(cudaMemcpy(fused_layers_.ptr, fl.data(), fl.size() * sizeof(FusedLayer),
                                cudaMemcpyHostToDevice));
@@ -780,6 +781,14 @@ void Model::launch_fused(int n_steps, bool forced, bool taps, long long spin_cyc
     a.spin_cycles = spin_cycles;
     a.barrier_offset = offset;
     a.l2_ahead = fused_l2_ahead();
+    // One rank: every KV group, MLP index and lm_head row; o_proj partials into its own buffer.
+    a.nkv = cfg_.n_kv_heads;
+    a.kv0 = 0;
+    a.hl = cfg_.hidden_dim;
+    a.v0 = 0;
+    a.world = 1;
+    a.rank = 0;
+    a.opart_dst[0] = a.opart;
     // The arrival counter is zero here: set at allocation, back to zero at the end of every
     // launch that completed (CTA 0), and by reset_fused_state after one that gave up.
     launch_decode_fused(a, fused_grid_, e.stream());
@@ -1690,6 +1699,34 @@ q3_status q3_tp_reset(q3_tp* tp) {
     return guard([&] {
         if (!tp) throw std::invalid_argument("null argument");
         tp->t->reset();
+    });
+}
+
+q3_status q3_tp_set_path(q3_tp* tp, int path) {
+    return guard([&] {
+        if (!tp) throw std::invalid_argument("null argument");
+        tp->t->set_path(path);
+    });
+}
+
+q3_status q3_tp_path(q3_tp* tp, int* path) {
+    return guard([&] {
+        if (!tp || !path) throw std::invalid_argument("null argument");
+        *path = tp->t->path();
+    });
+}
+
+q3_status q3_tp_nccl_unique_id(void* id_host) {
+    return guard([&] {
+        if (!id_host) throw std::invalid_argument("null argument");
+        q3::TpDecoder::nccl_unique_id(id_host);
+    });
+}
+
+q3_status q3_tp_nccl_connect(q3_tp* tp, const void* id_host) {
+    return guard([&] {
+        if (!tp || !id_host) throw std::invalid_argument("null argument");
+        tp->t->nccl_connect(id_host);
     });
 }
 

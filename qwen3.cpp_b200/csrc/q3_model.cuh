@@ -20,6 +20,23 @@ namespace q3 {
 void validate_config(const q3_config& c);
 void validate_kernel_limits(const q3_config& c);
 
+// Per-layer weights as the fused kernel streams them: copies made at load time so that every
+// CTA's share of a phase is one contiguous byte range, with the row-parity swizzle on the matrices
+// multiplied by MMAs (wqkv, wop, w1, w3 and the lm_head copy):
+//   wop[g][r][j] = wo[r][256*g + j]   (o_proj split by KV-head group: [8][1024][256])
+//   w2t[i][r]    = w2[r][i]           (down_proj split by MLP index: [3072][1024])
+struct FusedLayer {
+    const uint16_t* wqkv;       // [4096][1024]: wq; wk; wv rows (swizzled)
+    const uint16_t* wop;        // [8][1024][256] (swizzled)
+    const uint16_t* w1;         // [3072][1024] (swizzled)
+    const uint16_t* w3;         // [3072][1024] (swizzled)
+    const uint16_t* w2t;        // [3072][1024]
+    const uint16_t* attn_norm;  // [1024]
+    const uint16_t* q_norm;     // [128]
+    const uint16_t* k_norm;     // [128]
+    const uint16_t* mlp_norm;   // [1024]
+};
+
 // A parsed, memory-mapped Qwen3.bin (the layout of the reference's convert.py:2-20).
 class ModelFile {
 public:
@@ -198,6 +215,9 @@ public:
     bool fused_enabled() const { return use_fused_ && fused_grid_ > 0; }
     void set_fused(bool on) { use_fused_ = on; }
     int fused_grid() const { return fused_grid_; }
+    // The fused kernel's weight copies (host copy of its per-layer pointers) and lm_head copy.
+    const std::vector<FusedLayer>& fused_layers_host() const { return fused_host_layers_; }
+    const uint16_t* fused_lm() const { return fused_lm_; }
     // Runs one fused launch whose grid-wide waits can never complete, with a short bound, and
     // reports whether the kernel returned with its timeout status set (failure-path test).
     bool fused_timeout_selftest();
@@ -252,6 +272,7 @@ private:
     std::vector<LayerWeights> layers16_;
     DeviceBuffer fused_layers_, fused_part_o_, fused_part_ml_, fused_am_, fused_sync_, fused_wperm_,
         fused_y_, fused_tagged_, fused_dbg_;
+    std::vector<FusedLayer> fused_host_layers_;
     unsigned fused_epoch_ = 0;  // tag base of the last fused launch (1..4095)
     int fused_parity_ = 0;      // accumulator parity of the next launch's first step
 };

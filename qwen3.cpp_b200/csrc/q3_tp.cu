@@ -20,7 +20,9 @@
 // can only write parity c&1 again at invocation c+2, after it has seen this rank's flag c+1,
 // which this rank raises after it consumed invocation c.
 #include <cuda_bf16.h>
+#include <dlfcn.h>
 #include <float.h>
+#include <nccl.h>
 
 #include <algorithm>
 #include <cstring>
@@ -41,7 +43,12 @@ constexpr int kDim = 1024;          // residual width the exchange buffer is siz
 constexpr size_t kDataBytes = 2ull * kTpMaxRanks * kDim * 4;
 constexpr size_t kAmOff = kDataBytes;
 constexpr size_t kFlagOff = kAmOff + 2ull * kTpMaxRanks * sizeof(float2);
-constexpr size_t kXbufBytes = kFlagOff + 256;
+// Fused path: tagged words of the fused kernel's exchange (o_proj partials [8][1024], per-rank
+// down-projection sums [2][8][1024], greedy candidates [8][2]).
+constexpr size_t kFxOff = (kFlagOff + 256 + 255) / 256 * 256;
+constexpr size_t kFxOpart = 0, kFxYx = 8 * 1024, kFxAmx = kFxYx + 2ull * kFusedMaxRanks * 1024;
+constexpr size_t kXbufBytes = kFxOff + kFusedXchgWords * 8;
+static_assert(kTpMaxRanks == kFusedMaxRanks, "one rank limit");
 
 struct TpPeers {
     uint8_t* buf[kTpMaxRanks];  // exchange buffers of every rank (this rank's own included)
@@ -134,6 +141,132 @@ __global__ void __launch_bounds__(256) tp_allreduce_kernel(TpPeers P, const floa
     xv.w += sum.w;
     *reinterpret_cast<float4*>(x + i) = xv;
     if (tid == 0) *counter = seq;
+}
+
+// NCCL comparison path: x += the all-reduced partial (one block of 256 threads).
+__global__ void __launch_bounds__(256) tp_add_kernel(float* x, const float* sum) {
+    pdl_wait();
+    pdl_trigger();
+    const int i = threadIdx.x * 4;
+    float4 xv = *reinterpret_cast<float4*>(x + i);
+    const float4 v = *reinterpret_cast<const float4*>(sum + i);
+    xv.x += v.x;
+    xv.y += v.y;
+    xv.z += v.z;
+    xv.w += v.w;
+    *reinterpret_cast<float4*>(x + i) = xv;
+}
+
+// Block argmax of logits[0, vn) (lowest index on ties); valid in thread 0.
+__device__ void block_argmax(const float* logits, int vn, float& best_out, int& idx_out) {
+    __shared__ float bv[32];
+    __shared__ int bi[32];
+    const int tid = threadIdx.x;
+    float best = -INFINITY;
+    int idx = INT_MAX;
+    for (int i = tid; i < vn; i += blockDim.x) {
+        const float v = logits[i];
+        if (v > best || (v == best && i < idx)) {
+            best = v;
+            idx = i;
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (ov > best || (ov == best && oi < idx)) {
+            best = ov;
+            idx = oi;
+        }
+    }
+    if ((tid & 31) == 0) {
+        bv[tid >> 5] = best;
+        bi[tid >> 5] = idx;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) {
+            if (bv[w] > best || (bv[w] == best && bi[w] < idx)) {
+                best = bv[w];
+                idx = bi[w];
+            }
+        }
+    }
+    best_out = best;
+    idx_out = idx;
+}
+
+// NCCL comparison path, first half of the greedy step: this rank's (value, global index).
+__global__ void __launch_bounds__(1024) tp_argmax_local_kernel(const float* logits, int vn, int v0,
+                                                                float2* out) {
+    pdl_wait();
+    pdl_trigger();
+    float b;
+    int i;
+    block_argmax(logits, vn, b, i);
+    if (threadIdx.x == 0) *out = make_float2(b, __int_as_float(i + v0));
+}
+
+// Second half, after the all-gather of every rank's pair: the greedy token (lowest index on
+// ties), then log[step] = token, the next token (argmax or forced), position + 1, step + 1.
+__global__ void tp_argmax_final_kernel(const float2* am, int world, int32_t* tok, int32_t* pos,
+                                       int32_t* log, int32_t* state, const int32_t* forced) {
+    pdl_wait();
+    pdl_trigger();
+    float b = am[0].x;
+    int bi0 = __float_as_int(am[0].y);
+    for (int s = 1; s < world; ++s) {
+        const int si = __float_as_int(am[s].y);
+        if (am[s].x > b || (am[s].x == b && si < bi0)) {
+            b = am[s].x;
+            bi0 = si;
+        }
+    }
+    const int step = state[0];
+    log[step] = bi0;
+    tok[0] = (forced && step + 1 < state[1]) ? forced[step + 1] : bi0;
+    pos[0] += 1;
+    state[0] = step + 1;
+}
+
+// NCCL entry points, resolved at run time from the process's libnccl.so.2 (the copy PyTorch
+// loaded, else the system one), so that the library needs NCCL only when this path is used.
+struct NcclApi {
+    decltype(&ncclGetUniqueId) get_id = nullptr;
+    decltype(&ncclCommInitRank) init_rank = nullptr;
+    decltype(&ncclAllReduce) all_reduce = nullptr;
+    decltype(&ncclAllGather) all_gather = nullptr;
+    decltype(&ncclCommDestroy) destroy = nullptr;
+    decltype(&ncclGetErrorString) error_string = nullptr;
+};
+
+const NcclApi& nccl() {
+    static const NcclApi api = [] {
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW);
+        if (!h) throw std::runtime_error("tensor parallelism: NCCL (libnccl.so.2) is not available");
+        NcclApi a;
+        auto sym = [&](const char* name) {
+            void* f = dlsym(h, name);
+            if (!f) throw std::runtime_error(std::string("tensor parallelism: NCCL lacks ") + name);
+            return f;
+        };
+        a.get_id = reinterpret_cast<decltype(a.get_id)>(sym("ncclGetUniqueId"));
+        a.init_rank = reinterpret_cast<decltype(a.init_rank)>(sym("ncclCommInitRank"));
+        a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(sym("ncclAllReduce"));
+        a.all_gather = reinterpret_cast<decltype(a.all_gather)>(sym("ncclAllGather"));
+        a.destroy = reinterpret_cast<decltype(a.destroy)>(sym("ncclCommDestroy"));
+        a.error_string = reinterpret_cast<decltype(a.error_string)>(sym("ncclGetErrorString"));
+        return a;
+    }();
+    return api;
+}
+
+void nccl_check(ncclResult_t r, const char* what) {
+    if (r != ncclSuccess) {
+        throw std::runtime_error(std::string("tensor parallelism: ") + what + ": " +
+                                 nccl().error_string(r));
+    }
 }
 
 // Greedy argmax over this rank's vocabulary rows, all-reduced (lowest index wins ties,
@@ -303,11 +436,166 @@ TpDecoder::TpDecoder(Model& model, int rank, int world)
     part_ml_.alloc(static_cast<size_t>(hkv_) * attn_splits_ * 2 * sizeof(float2));
     attn_counter_.alloc(static_cast<size_t>(hkv_) * sizeof(unsigned));
     Q3_CUDA(cudaMemsetAsync(attn_counter_.ptr, 0, attn_counter_.bytes, s_));
+    if (model.fused_available() && model.fused_grid() / hkv_ >= 1 &&
+        hl_ <= 64 * model.fused_grid()) {
+        setup_fused();
+        fused_ = true;
+    }
     Q3_CUDA(cudaStreamSynchronize(s_));
 }
 
+void TpDecoder::setup_fused() {
+    const q3_config& c = cfg_;
+    const size_t D = c.dim, qd = static_cast<size_t>(c.n_heads) * HD;
+    const size_t kvd = static_cast<size_t>(c.n_kv_heads) * HD;
+    const size_t qkv_l = static_cast<size_t>(hq_ + 2 * hkv_) * HD;
+    f_grid_ = m_.fused_grid();
+    f_smax_ = f_grid_ / hkv_;
+    // Per layer: the local q, k and v rows of the fused kernel's swizzled [wq;wk;wv] copy (row
+    // offsets are even, so every row keeps its parity swizzle), and pointers into its wop (by
+    // global KV group), w1 / w3 / w2t (this rank's MLP indices) copies.
+    const std::vector<FusedLayer>& fl = m_.fused_layers_host();
+    f_wqkv_.alloc(qkv_l * D * 2 * c.n_layers);
+    std::vector<FusedLayer> ll(c.n_layers);
+    const size_t mlp0 = static_cast<size_t>(rank_) * hl_ * D;
+    for (int l = 0; l < c.n_layers; ++l) {
+        uint16_t* dst = static_cast<uint16_t*>(f_wqkv_.ptr) + qkv_l * D * l;
+        const uint16_t* src = fl[l].wqkv;
+        const size_t q0 = static_cast<size_t>(rank_) * hq_ * HD, k0 = static_cast<size_t>(rank_) * hkv_ * HD;
+        Q3_CUDA(cudaMemcpyAsync(dst, src + q0 * D, static_cast<size_t>(hq_) * HD * D * 2,
+                                cudaMemcpyDeviceToDevice, s_));
+        Q3_CUDA(cudaMemcpyAsync(dst + static_cast<size_t>(hq_) * HD * D, src + (qd + k0) * D,
+                                static_cast<size_t>(hkv_) * HD * D * 2, cudaMemcpyDeviceToDevice, s_));
+        Q3_CUDA(cudaMemcpyAsync(dst + static_cast<size_t>(hq_ + hkv_) * HD * D,
+                                src + (qd + kvd + k0) * D, static_cast<size_t>(hkv_) * HD * D * 2,
+                                cudaMemcpyDeviceToDevice, s_));
+        ll[l] = fl[l];
+        ll[l].wqkv = dst;
+        ll[l].w1 = fl[l].w1 + mlp0;
+        ll[l].w3 = fl[l].w3 + mlp0;
+        ll[l].w2t = fl[l].w2t + mlp0;
+    }
+    f_layers_.alloc(ll.size() * sizeof(FusedLayer));
+    Q3_CUDA(cudaMemcpyAsync(f_layers_.ptr, ll.data(), f_layers_.bytes, cudaMemcpyHostToDevice, s_));
+    f_y_.alloc(fused_ybuf_floats(c.n_layers) * 4);
+    f_qkvt_.alloc(qkv_l * 8);
+    f_part_o_.alloc(static_cast<size_t>(hq_) * f_smax_ * HD * 4);
+    f_part_ml_.alloc(static_cast<size_t>(hq_) * f_smax_ * sizeof(float2));
+    f_am_.alloc(static_cast<size_t>(f_grid_) * sizeof(float2));
+    f_sync_.alloc(256);
+    f_sp_.alloc(sizeof(StepParams));
+    for (DeviceBuffer* b : {&f_y_, &f_qkvt_, &f_sync_}) {
+        Q3_CUDA(cudaMemsetAsync(b->ptr, 0, b->bytes, s_));
+    }
+    Q3_CUDA(cudaStreamSynchronize(s_));  // the host copy of the layer pointers goes out of scope
+}
+
+void TpDecoder::set_path(int path) {
+    if (path == Q3_TP_FUSED && !fused_available()) {
+        throw std::invalid_argument("tensor parallelism: the fused decode kernel is not available");
+    }
+    if (path == Q3_TP_GRAPH_NCCL && !nccl_comm_) {
+        throw std::invalid_argument("tensor parallelism: connect NCCL first (q3_tp_nccl_connect)");
+    }
+    if (path != Q3_TP_FUSED && path != Q3_TP_GRAPH && path != Q3_TP_GRAPH_NCCL) {
+        throw std::invalid_argument("unknown tensor-parallel path");
+    }
+    const bool nccl_on = path == Q3_TP_GRAPH_NCCL;
+    if (nccl_on != use_nccl_ && graph_) {  // the captured step holds the collective calls
+        cudaGraphExecDestroy(graph_);
+        graph_ = nullptr;
+    }
+    fused_ = path == Q3_TP_FUSED;
+    use_nccl_ = nccl_on;
+}
+
+int TpDecoder::path() const {
+    return fused_ ? Q3_TP_FUSED : (use_nccl_ ? Q3_TP_GRAPH_NCCL : Q3_TP_GRAPH);
+}
+
+void TpDecoder::nccl_unique_id(void* out) {
+    ncclUniqueId id;
+    nccl_check(nccl().get_id(&id), "ncclGetUniqueId");
+    std::memcpy(out, &id, sizeof(id));
+}
+
+void TpDecoder::nccl_connect(const void* id) {
+    if (nccl_comm_) throw std::runtime_error("tensor parallelism: NCCL already connected");
+    ncclUniqueId uid;
+    std::memcpy(&uid, id, sizeof(uid));
+    Q3_CUDA(cudaSetDevice(m_.device()));
+    ncclComm_t comm = nullptr;
+    nccl_check(nccl().init_rank(&comm, world_, uid, rank_), "ncclCommInitRank");
+    nccl_comm_ = comm;
+    am_nccl_.alloc(static_cast<size_t>(1 + world_) * sizeof(float2));
+}
+
+void TpDecoder::launch_fused(int n_steps, bool forced) {
+    const q3_config& c = cfg_;
+    Engine& e = m_.engine();
+    FusedArgs a{};
+    a.layers = static_cast<const FusedLayer*>(f_layers_.ptr);
+    a.embed = m_.embed();
+    a.lm_head = m_.fused_lm() + static_cast<size_t>(v0_) * c.dim;
+    a.final_norm = m_.final_norm();
+    a.k_cache = e.k_layer(0);
+    a.v_cache = e.v_layer(0);
+    a.layer_elems = e.layer_elems();
+    a.page_table = e.page_table();
+    a.rope = e.rope();
+    a.rope_len = e.rope_len();
+    a.ybuf = static_cast<float*>(f_y_.ptr);
+    a.parity0 = f_parity_;
+    f_parity_ = (f_parity_ + n_steps) & 1;
+    a.qkvt = static_cast<unsigned long long*>(f_qkvt_.ptr);
+    f_epoch_ = (f_epoch_ + 1) & 0xFFFu;
+    if (f_epoch_ == 0) f_epoch_ = 1;
+    a.epoch = f_epoch_;
+    a.part_o = static_cast<float*>(f_part_o_.ptr);
+    a.part_ml = static_cast<float2*>(f_part_ml_.ptr);
+    a.am_part = static_cast<float2*>(f_am_.ptr);
+    a.logits = static_cast<float*>(logits_.ptr);
+    a.taps = nullptr;
+    a.sp = static_cast<StepParams*>(f_sp_.ptr);
+    a.token_log = static_cast<int32_t*>(log_.ptr);
+    a.forced = forced ? static_cast<const int32_t*>(forced_.ptr) : nullptr;
+    a.bar = static_cast<unsigned*>(f_sync_.ptr);
+    a.err = static_cast<unsigned*>(err_.ptr);
+    a.n_layers = c.n_layers;
+    a.vocab = vn_;
+    a.ctx = c.max_seq_len;
+    a.n_steps = n_steps;
+    a.s_max = f_smax_;
+    a.eps = c.norm_eps;
+    a.spin_cycles = wait_cycles_;
+    a.l2_ahead = fused_l2_ahead();
+    a.nkv = hkv_;
+    a.kv0 = rank_ * hkv_;
+    a.hl = hl_;
+    a.v0 = v0_;
+    a.world = world_;
+    a.rank = rank_;
+    a.xchg = (world_ > 1 || solo_allreduce_) ? 1 : 0;
+    a.sys = world_ > 1 ? 1 : 0;
+    auto* own = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(xbuf_.ptr) + kFxOff);
+    a.opart = own + kFxOpart;
+    a.yx = own + kFxYx;
+    a.amx = own + kFxAmx;
+    for (int p = 0; p < world_; ++p) {
+        const bool mine = p == rank_ || (p < static_cast<int>(self_peer_.size()) && self_peer_[p]);
+        auto* base = mine ? own
+                          : reinterpret_cast<unsigned long long*>(
+                                static_cast<uint8_t*>(peer_mapped_[p]) + kFxOff);
+        a.opart_dst[p] = base + kFxOpart;
+        a.yx_dst[p] = base + kFxYx;
+        a.amx_dst[p] = base + kFxAmx;
+    }
+    launch_decode_fused(a, f_grid_, s_);
+}
+
 TpDecoder::~TpDecoder() {
-    if (graph_) cudaGraphExecDestroy(graph_);
+    if (graph_) cudaGraphExecDestroy(graph_);  // before the communicator its NCCL calls use
+    if (nccl_comm_) nccl().destroy(static_cast<ncclComm_t>(nccl_comm_));
     for (void* p : peer_mapped_) {
         if (p) cudaIpcCloseMemHandle(p);
     }
@@ -326,10 +614,12 @@ void TpDecoder::reset() {
     // Invocation counter, error word, exchange data and flags back to zero: every rank resets
     // (and the ranks meet on the host) before any of them decodes again.
     Q3_CUDA(cudaStreamSynchronize(s_));
-    for (DeviceBuffer* b : {&err_, &counter_, &xbuf_}) {
-        Q3_CUDA(cudaMemsetAsync(b->ptr, 0, b->bytes, s_));
+    for (DeviceBuffer* b : {&err_, &counter_, &xbuf_, &f_y_, &f_qkvt_, &f_sync_}) {
+        if (b->ptr) Q3_CUDA(cudaMemsetAsync(b->ptr, 0, b->bytes, s_));
     }
     Q3_CUDA(cudaStreamSynchronize(s_));
+    f_epoch_ = 0;
+    f_parity_ = 0;
     failed_ = false;
 }
 
@@ -383,13 +673,22 @@ void TpDecoder::enqueue_step(bool forced) {
     // One rank: the projections add straight into x, unless configured to route them through
     // the all-reduce kernel with this rank as its only member. Several: each writes its partial,
     // and the all-reduce adds the ranks' partials in rank order.
-    const bool solo = world_ == 1 && !solo_allreduce_;
+    const bool solo = world_ == 1 && !solo_allreduce_ && !use_nccl_;
     const int proj_epi = solo ? kEpiResidual : kEpiStore;
     float* proj_out = solo ? X : part;
     auto allreduce = [&]() {
         if (solo) return;
-        launch_dep(false, tp_allreduce_kernel, dim3(1), dim3(256), 0, s_, P, static_cast<const float*>(part), X,
-                   rank_, world_, counter, err, kBudget);
+        if (use_nccl_) {
+            // Comparison arm: NCCL sums the partials in place, then x += sum.
+            nccl_check(nccl().all_reduce(part, part, c.dim, ncclFloat32, ncclSum,
+                                         static_cast<ncclComm_t>(nccl_comm_), s_),
+                       "ncclAllReduce");
+            launch_dep(false, tp_add_kernel, dim3(1), dim3(256), 0, s_, X,
+                       static_cast<const float*>(part));
+        } else {
+            launch_dep(false, tp_allreduce_kernel, dim3(1), dim3(256), 0, s_, P,
+                       static_cast<const float*>(part), X, rank_, world_, counter, err, kBudget);
+        }
         Q3_CUDA(cudaGetLastError());
     };
     // x = embedding row of the step's token (the bf16 normalised copy is not used).
@@ -456,11 +755,25 @@ void TpDecoder::enqueue_step(bool forced) {
     launch_gemv(kEpiStore, m_.output() + static_cast<size_t>(v0_) * c.dim, nullptr, X,
                 m_.final_norm(), c.norm_eps, static_cast<float*>(logits_.ptr), nullptr, vn_, c.dim,
                 nullptr, 0, s_);
-    launch_dep(false, tp_argmax_kernel, dim3(1), dim3(1024), 0, s_, P,
-               static_cast<const float*>(logits_.ptr), vn_, v0_, rank_, world_, counter, err,
-               kBudget, static_cast<int32_t*>(tok_.ptr), static_cast<int32_t*>(pos_.ptr),
-               static_cast<int32_t*>(log_.ptr), static_cast<int32_t*>(step_.ptr),
-               forced ? static_cast<const int32_t*>(forced_.ptr) : nullptr);
+    if (use_nccl_) {
+        float2* am = static_cast<float2*>(am_nccl_.ptr);
+        launch_dep(false, tp_argmax_local_kernel, dim3(1), dim3(1024), 0, s_,
+                   static_cast<const float*>(logits_.ptr), vn_, v0_, am);
+        nccl_check(nccl().all_gather(am, am + 1, 2, ncclFloat32,
+                                     static_cast<ncclComm_t>(nccl_comm_), s_),
+                   "ncclAllGather");
+        launch_dep(false, tp_argmax_final_kernel, dim3(1), dim3(1), 0, s_,
+                   static_cast<const float2*>(am + 1), world_, static_cast<int32_t*>(tok_.ptr),
+                   static_cast<int32_t*>(pos_.ptr), static_cast<int32_t*>(log_.ptr),
+                   static_cast<int32_t*>(step_.ptr),
+                   forced ? static_cast<const int32_t*>(forced_.ptr) : nullptr);
+    } else {
+        launch_dep(false, tp_argmax_kernel, dim3(1), dim3(1024), 0, s_, P,
+                   static_cast<const float*>(logits_.ptr), vn_, v0_, rank_, world_, counter, err,
+                   kBudget, static_cast<int32_t*>(tok_.ptr), static_cast<int32_t*>(pos_.ptr),
+                   static_cast<int32_t*>(log_.ptr), static_cast<int32_t*>(step_.ptr),
+                   forced ? static_cast<const int32_t*>(forced_.ptr) : nullptr);
+    }
     Q3_CUDA(cudaGetLastError());
 }
 
@@ -509,6 +822,38 @@ void TpDecoder::decode(int32_t first, int pos0, int n_steps, const int32_t* forc
                                 cudaMemcpyHostToDevice, s_));
     }
     const bool forced = forced_host != nullptr;
+    if (fused_) {
+        StepParams sp{};
+        sp.token = t0;
+        sp.pos = pos0;
+        step_positions(pos0, c.max_seq_len, &sp.num_sink, &sp.kv_pos, &sp.kv_len);
+        sp.step = 0;
+        sp.n_forced = forced ? n_steps : 0;
+        Q3_CUDA(cudaMemcpyAsync(f_sp_.ptr, &sp, sizeof(sp), cudaMemcpyHostToDevice, s_));
+        constexpr int kMaxStepsPerLaunch = 256;
+        for (int done = 0; done < n_steps; done += kMaxStepsPerLaunch) {
+            launch_fused(std::min(kMaxStepsPerLaunch, n_steps - done), forced);
+        }
+    } else {
+        run_graph(forced, n_steps);
+    }
+    if (tokens_host) {
+        Q3_CUDA(cudaMemcpyAsync(tokens_host, log_.ptr, static_cast<size_t>(n_steps) * 4,
+                                cudaMemcpyDeviceToHost, s_));
+    }
+    Q3_CUDA(cudaStreamSynchronize(s_));
+    unsigned e = 0;
+    Q3_CUDA(cudaMemcpy(&e, err_.ptr, 4, cudaMemcpyDeviceToHost));
+    if (e) {
+        // The ranks' invocation counters (graph) or the kernel's arrival counter and exchange
+        // words (fused) may now disagree: refuse further steps until reset.
+        failed_ = true;
+        throw DeviceTimeout("tensor-parallel decode: a bounded wait gave up (code " +
+                            std::to_string(e) + ")");
+    }
+}
+
+void TpDecoder::run_graph(bool forced, int n_steps) {
     if (graph_rope_ != m_.engine().rope()) {  // the graph holds the RoPE table's address
         if (graph_) cudaGraphExecDestroy(graph_);
         graph_ = nullptr;
@@ -533,19 +878,6 @@ void TpDecoder::decode(int32_t first, int pos0, int n_steps, const int32_t* forc
         graph_rope_ = m_.engine().rope();
     }
     for (int i = 0; i < n_steps; ++i) Q3_CUDA(cudaGraphLaunch(graph_, s_));
-    if (tokens_host) {
-        Q3_CUDA(cudaMemcpyAsync(tokens_host, log_.ptr, static_cast<size_t>(n_steps) * 4,
-                                cudaMemcpyDeviceToHost, s_));
-    }
-    Q3_CUDA(cudaStreamSynchronize(s_));
-    unsigned e = 0;
-    Q3_CUDA(cudaMemcpy(&e, err_.ptr, 4, cudaMemcpyDeviceToHost));
-    if (e) {
-        // The ranks' invocation counters may now disagree: refuse further steps until reset.
-        failed_ = true;
-        throw DeviceTimeout("tensor-parallel decode: a bounded wait gave up (code " +
-                            std::to_string(e) + ")");
-    }
 }
 
 }  // namespace q3

@@ -7,10 +7,18 @@
 // a partial sum of x's update: an all-reduce over NVLink peer memory (each rank pushes its 4 KB
 // partial into every peer's buffer, then raises a flag there) adds them in rank order, so x stays
 // bit-identical on every rank. The greedy argmax is all-reduced the same way over the vocabulary
-// slices (lowest index on ties). A step is one captured CUDA graph: CUDA-core GEMVs on the local
-// weight slices (fp32 activations, RmsNorm fused as their prologue), the paged decode attention
-// of the local KV heads, and the two all-reduces. The reference has no counterpart (it runs on
-// one CPU).
+// slices (lowest index on ties). Two ways to run the steps:
+//   fused (default where the model has the fused decode kernel): one persistent kernel per GPU
+//     runs up to 256 steps; the o_proj partials of each rank's KV-head groups go straight into
+//     every rank's buffer as tagged words from the kernel's o_proj epilogue, and the ranks'
+//     down-projection sums and greedy candidates travel the same way, polled in rank order by
+//     the next phase (no separate all-reduce launch, no flag round trip).
+//   graph: one captured CUDA graph per step: CUDA-core GEMVs on the local weight slices (fp32
+//     activations, RmsNorm fused as their prologue), the paged decode attention of the local KV
+//     heads, and the two all-reduce kernels.
+//   graph + NCCL (a comparison arm): the same graph with ncclAllReduce (and an all-gather of the
+//     greedy candidates) captured in place of this library's all-reduce kernels.
+// The reference has no counterpart (it runs on one CPU).
 #pragma once
 
 #include <cuda.h>
@@ -20,6 +28,7 @@
 #include <memory>
 #include <vector>
 
+#include "q3_decode_fused.cuh"
 #include "q3_model.cuh"
 
 namespace q3 {
@@ -53,9 +62,21 @@ public:
     // After a timeout (decode threw DeviceTimeout and refuses further steps): zero the
     // invocation counter, error word and exchange buffer. Every rank resets before any decodes.
     void reset();
+    // Step path (Q3_TP_FUSED, Q3_TP_GRAPH, Q3_TP_GRAPH_NCCL); every rank of a group picks alike.
+    void set_path(int path);
+    int path() const;
+    bool fused() const { return fused_; }
+    // NCCL communicator of the graph + NCCL path: one rank makes the unique id (128 bytes), every
+    // rank connects with it.
+    static void nccl_unique_id(void* out);
+    void nccl_connect(const void* id);
+    bool fused_available() const { return f_grid_ > 0; }
 
 private:
     void enqueue_step(bool forced);
+    void setup_fused();
+    void launch_fused(int n_steps, bool forced);
+    void run_graph(bool forced, int n_steps);
 
     Model& m_;
     q3_config cfg_;
@@ -87,6 +108,16 @@ private:
     cudaGraphExec_t graph_ = nullptr;
     bool graph_forced_ = false;
     const float2* graph_rope_ = nullptr;
+    // Fused path: local [wq;wk;wv] rows of the fused kernel's weight copies, per-layer pointers,
+    // and the kernel's own state (down-projection accumulators, tagged q|k|v, attention split
+    // partials, per-CTA argmax, arrival counter, step parameters).
+    bool fused_ = false;
+    bool use_nccl_ = false;
+    void* nccl_comm_ = nullptr;  // ncclComm_t
+    DeviceBuffer am_nccl_;       // [1 + world] (value, index): this rank's, then the gathered
+    int f_grid_ = 0, f_smax_ = 0, f_parity_ = 0;
+    unsigned f_epoch_ = 0;
+    DeviceBuffer f_wqkv_, f_layers_, f_y_, f_qkvt_, f_part_o_, f_part_ml_, f_am_, f_sync_, f_sp_;
 };
 
 }  // namespace q3

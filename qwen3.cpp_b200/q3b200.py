@@ -125,6 +125,10 @@ def lib() -> C.CDLL:
         "q3_tp_decode_forced": [vp, I32P, C.c_int, C.c_int, vp],
         "q3_tp_configure": [vp, C.c_int, C.c_longlong],
         "q3_tp_reset": [vp],
+        "q3_tp_set_path": [vp, C.c_int],
+        "q3_tp_path": [vp, C.POINTER(C.c_int)],
+        "q3_tp_nccl_unique_id": [vp],
+        "q3_tp_nccl_connect": [vp, vp],
         "q3_decode_greedy": [vp, i32, C.c_int, C.c_int, vp, vp],
         "q3_decode_forced": [vp, I32P, C.c_int, C.c_int, vp, vp],
         "q3_generate": [vp, vp, C.c_int, sz, C.c_int, vp, C.POINTER(sz), C.POINTER(GenStats)],
@@ -488,6 +492,30 @@ class TpDecoder:
     def reset(self) -> None:
         """Clears the state a timed-out step left (every rank resets before decoding again)."""
         check(self._lib.q3_tp_reset(self._h))
+
+    FUSED, GRAPH, GRAPH_NCCL = 0, 1, 2  # Q3_TP_FUSED, Q3_TP_GRAPH, Q3_TP_GRAPH_NCCL
+
+    @staticmethod
+    def nccl_unique_id() -> bytes:
+        """A new 128-byte NCCL unique id (one rank makes it; every rank connects with it)."""
+        buf = (C.c_uint8 * 128)()
+        check(lib().q3_tp_nccl_unique_id(buf))
+        return bytes(buf)
+
+    def nccl_connect(self, uid: bytes) -> None:
+        """NCCL communicator for the GRAPH_NCCL comparison path."""
+        buf = (C.c_uint8 * 128).from_buffer_copy(uid)
+        check(self._lib.q3_tp_nccl_connect(self._h, buf))
+
+    @property
+    def path(self) -> int:
+        v = C.c_int()
+        check(self._lib.q3_tp_path(self._h, C.byref(v)))
+        return v.value
+
+    @path.setter
+    def path(self, p: int) -> None:
+        check(self._lib.q3_tp_set_path(self._h, int(p)))
 
 
 class Block:

@@ -2,12 +2,12 @@
 torch.distributed.run). Prefills the prompt on this rank's own model, connects the ranks' exchange
 buffers, runs teacher-forced and free-running decode, and writes its results to <out>.rank<r>.npz.
 
-    python -m torch.distributed.run --nproc-per-node N tests/tp_worker.py <weights> <inputs.npz> <out> [mode]
+    python -m torch.distributed.run --nproc-per-node N tests/tp_worker.py <weights> <inputs.npz> <out> [mode] [path]
 
 mode "decode" (default): the parity run. Mode "leave": after one decode call together, every rank
 but 0 stops taking part (leaves between steps, nothing of its own in flight); rank 0 decodes once
 more with a short wait budget and records whether it timed out, how long that took, and whether
-the decoder then refused another step.
+the decoder then refused another step. path: "fused" (default), "graph" or "graph_nccl".
 """
 import os
 import sys
@@ -28,6 +28,7 @@ def main():
 
     weights, inputs, out = sys.argv[1], sys.argv[2], sys.argv[3]
     mode = sys.argv[4] if len(sys.argv) > 4 else "decode"
+    path = sys.argv[5] if len(sys.argv) > 5 else "fused"
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
@@ -37,6 +38,12 @@ def main():
     m = q3b200.Qwen3(weights, int(d["ctx"]), device=local)
     _, nxt = m.prefill(prompt, 0)
     tp = q3b200.TpDecoder(m, rank, world)
+    if path == "graph_nccl":
+        uid = [q3b200.TpDecoder.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        tp.nccl_connect(uid[0])
+    tp.path = {"fused": q3b200.TpDecoder.FUSED, "graph": q3b200.TpDecoder.GRAPH,
+               "graph_nccl": q3b200.TpDecoder.GRAPH_NCCL}[path]
     handles = [None] * world
     dist.all_gather_object(handles, tp.ipc_handle())
     tp.connect(handles)
