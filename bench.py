@@ -326,6 +326,7 @@ def run_b200_arm(args):
     import numpy as np
     import torch
     import torch.distributed as dist
+    from torch.cuda import nvtx
 
     import gen_weights
     import q3b200
@@ -371,7 +372,9 @@ def run_b200_arm(args):
                 dist.barrier()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(ext)
+            nvtx.range_push("q3.decode")  # NVTX ranges name each leg's timed work for ncu filters
             model.decode_greedy(nxt, PROMPT_LEN, n)
+            nvtx.range_pop()
             e1.record(ext)
             torch.cuda.synchronize()
             total_ms += e0.elapsed_time(e1)
@@ -416,7 +419,9 @@ def run_b200_arm(args):
         for _ in range(PREFILL_RUNS):
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(pext)
+            nvtx.range_push("q3.prefill")
             pm.prefill(pp, 0, want_logits=False)
+            nvtx.range_pop()
             e1.record(pext)
             torch.cuda.synchronize()
             p_ms += e0.elapsed_time(e1)
@@ -438,7 +443,9 @@ def run_b200_arm(args):
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(bext)
+        nvtx.range_push("q3.dp_prefill")
         batch.add_many([prompts[i] for i in mine])
+        nvtx.range_pop()
         e1.record(bext)
         torch.cuda.synchronize()
         dp_prefill_ms = max_over_ranks(e0.elapsed_time(e1), world)
@@ -449,7 +456,9 @@ def run_b200_arm(args):
             dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(bext)
+        nvtx.range_push("q3.dp_decode")
         batch.decode(DP_STEPS)
+        nvtx.range_pop()
         e1.record(bext)
         torch.cuda.synchronize()
         dp_ms = e0.elapsed_time(e1)
@@ -468,6 +477,7 @@ def run_b200_arm(args):
     # the same graph with NCCL's all-reduce / all-gather captured in their place.
     tp_ms = tp_gbs = tp_bytes_gpu = 0.0
     tp_arms = {}
+    tp_default = None
     if "tp" in legs:
         tm = q3b200.Qwen3(path, TP_CTX, device=local)
         tprompt = np.random.default_rng(4).integers(0, VOCAB, TP_PROMPT).astype(np.int32)
@@ -493,7 +503,9 @@ def run_b200_arm(args):
                 dist.barrier()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(tpx)
+            nvtx.range_push("q3.tp_" + names[arm])
             out = tp.decode(int(warm[-1]), pos, TP_STEPS)
+            nvtx.range_pop()
             e1.record(tpx)
             torch.cuda.synchronize()
             pos += TP_STEPS
