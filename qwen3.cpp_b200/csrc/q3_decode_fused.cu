@@ -415,6 +415,13 @@ __device__ __forceinline__ Span part(int rows, int G, int c) {
     const int r1 = static_cast<int>((static_cast<long long>(rows) * (c + 1)) / G);
     return {r0, r1 - r0};
 }
+// As part, in whole row pairs (rows even): every share starts on an even row, so the lm_head
+// epilogue writes its logits as aligned 8-byte pairs (fewer, fuller transactions, which matters
+// when the logits go straight to pinned host memory).
+__device__ __forceinline__ Span part2(int rows, int G, int c) {
+    const Span s = part(rows / 2, G, c);
+    return {2 * s.r0, 2 * s.n};
+}
 
 static_assert(RPC_ROW * D * 2 <= SLOT && RPC_GRP * GRP * 2 <= SLOT &&
                   2 * RPC_PAIR * D * 2 <= SLOT && 4 * kPageTokens * HD * 2 <= SLOT,
@@ -494,7 +501,7 @@ __device__ __noinline__ void prefetch_unit(const FusedLayer* layers, int n_layer
         prefetch_l2(w.w3 + static_cast<size_t>(sp.r0) * D, sp.n * D * 2);
         prefetch_l2(w.w2t + static_cast<size_t>(sp.r0) * D, sp.n * D * 2);
     } else {
-        const Span sp = part(vocab, G, c);
+        const Span sp = part2(vocab, G, c);
         prefetch_l2(lm_head + static_cast<size_t>(sp.r0) * D, min(sp.n, 96) * D * 2);
     }
 }
@@ -662,7 +669,7 @@ struct Producer {
                 ok = ok && rows<D * 2, RPC_ROW>(w.w2t, part(hl, G, c));
             }
             prefetch_ahead(st * per + a.n_layers + a.l2_ahead, G, c);
-            ok = ok && rows<D * 2, RPC_ROW>(a.lm_head, part(a.vocab, G, c));
+            ok = ok && rows<D * 2, RPC_ROW>(a.lm_head, part2(a.vocab, G, c));
             prev_base = base;
             prev_short = sp.shrt;
             base += barriers_of(a, sp.shrt);
@@ -882,6 +889,19 @@ __device__ __forceinline__ void consume_rows(Smem& sm, const FusedArgs& a, uint3
         } else if (lane < 4) {
             const int i = 2 * t;
             const float yy[2] = {y0, y1};
+            if (mode == kLogits && i + 1 < rn && ((rb + i) & 1) == 0 &&
+                Q3_CHECK(rb + i >= 0 && rb + i + 1 < out_n, 53, rb, i, out_n)) {
+                // Rows rb + i, rb + i + 1 as one aligned pair (every lm_head share starts even).
+                *reinterpret_cast<float2*>(out + rb + i) = make_float2(y0, y1);
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    if (better(yy[j], rb + i + j, bv, bi)) {
+                        bv = yy[j];
+                        bi = rb + i + j;
+                    }
+                }
+                continue;
+            }
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
                 if (i + j >= rn) break;
@@ -1861,7 +1881,7 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const __grid_consta
             reinterpret_cast<float4*>(a.taps + static_cast<size_t>(a.n_layers) * D)[tid] = xv;
         }
         stage_norm(sm, xv, fw, a.eps);
-        const Span vs = part(a.vocab, G, c);
+        const Span vs = part2(a.vocab, G, c);
         consume_rows<D, RPC_ROW, kLogits>(sm, a, q, vs.r0, vs.n, a.logits, a.vocab);
         q += chunks_of(vs.n, RPC_ROW);
         bar_consumers();
@@ -1890,6 +1910,8 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const __grid_consta
             if (lane == 0) {
                 const int idx = sp0.step + a.n_steps;
                 a.token_log[idx - 1] = best;
+                if (a.token_out) *a.token_out = best;
+                if (a.err_out) *a.err_out = *reinterpret_cast<volatile unsigned*>(a.err);
                 StepParams np = sp0;
                 np.token = (a.forced && idx < sp0.n_forced) ? a.forced[idx] : best;
                 np.step = idx;

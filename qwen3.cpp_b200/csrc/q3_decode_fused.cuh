@@ -71,6 +71,12 @@ struct FusedArgs {
     unsigned long long* yx_dst[kFusedMaxRanks];
     unsigned long long* amx;                         // [kFusedMaxRanks][2] (value, index) words
     unsigned long long* amx_dst[kFusedMaxRanks];
+    // nullable: the last step's greedy token also goes here (pinned host memory of a one-step
+    // ForwardToken + Greedy call, whose logits pointer is pinned host memory too).
+    int32_t* token_out;
+    // nullable: CTA 0 copies the error word here at the end of a launch that ran to completion
+    // (the caller presets it to a non-zero value, so an aborted launch leaves it non-zero).
+    unsigned* err_out;
 };
 
 // Tagged words of the tensor-parallel exchange region (opart [8][1024], yx, amx), in u64 words.

@@ -761,7 +761,9 @@ void Model::launch_fused(int n_steps, bool forced, bool taps, long long spin_cyc
     a.part_o = static_cast<float*>(fused_part_o_.ptr);
     a.part_ml = static_cast<float2*>(fused_part_ml_.ptr);
     a.am_part = static_cast<float2*>(fused_am_.ptr);
-    a.logits = static_cast<float*>(logits_.ptr);
+    a.logits = fused_logits_out_ ? fused_logits_out_ : static_cast<float*>(logits_.ptr);
+    a.token_out = fused_token_out_;
+    a.err_out = fused_err_out_;
     a.taps = taps ? e.taps() : nullptr;
     a.sp = e.step_params();
     if (sp_init) {
@@ -1002,8 +1004,44 @@ const float* Model::forward_token_ref(int32_t token, int pos, int32_t* next) {
     // [logits][error word][greedy token]
     pinned_logits_.ensure(static_cast<size_t>(cfg_.vocab_size) * 4 + 2 * sizeof(unsigned));
     float* buf = static_cast<float*>(pinned_logits_.ptr);
+    unsigned* err_host = reinterpret_cast<unsigned*>(buf + cfg_.vocab_size);
     int32_t* tok = reinterpret_cast<int32_t*>(buf + cfg_.vocab_size + 1);
-    forward_token(token, pos, nullptr, buf, true, next ? tok : nullptr);
+    if (!fused_enabled()) {
+        forward_token(token, pos, nullptr, buf, true, next ? tok : nullptr);
+        if (next) *next = *tok;
+        return buf;
+    }
+    // Fused path: the kernel's lm_head phase writes the logits into this pinned buffer (over the
+    // host link while the phase runs) and CTA 0 the greedy token; only the error word is copied.
+    check_token_pos(token, pos);
+    Engine& e = *engine_;
+    e.ensure_rope(pos + 2);
+    const StepParams sp = start_params(token, pos, 0);
+    clear_fused_error();
+    void* dev_buf = nullptr;
+    Q3_CUDA(cudaHostGetDevicePointer(&dev_buf, buf, 0));
+    float* dev_logits = static_cast<float*>(dev_buf);
+    // The kernel's CTA 0 overwrites the preset error slot when the launch runs to completion.
+    *err_host = ~0u;
+    fused_logits_out_ = dev_logits;
+    fused_token_out_ = reinterpret_cast<int32_t*>(dev_logits + cfg_.vocab_size + 1);
+    fused_err_out_ = reinterpret_cast<unsigned*>(dev_logits + cfg_.vocab_size);
+    try {
+        run_steps(1, false, false, nullptr, &sp);
+    } catch (...) {
+        fused_logits_out_ = nullptr;
+        fused_token_out_ = nullptr;
+        fused_err_out_ = nullptr;
+        throw;
+    }
+    fused_logits_out_ = nullptr;
+    fused_token_out_ = nullptr;
+    fused_err_out_ = nullptr;
+    Q3_CUDA(cudaStreamSynchronize(e.stream()));
+    if (*err_host != 0u) {
+        check_fused_error();  // throws when the device error word is set
+        throw std::runtime_error("fused decode: the launch did not run to completion");
+    }
     if (next) *next = *tok;
     return buf;
 }

@@ -273,6 +273,11 @@ private:
     DeviceBuffer fused_layers_, fused_part_o_, fused_part_ml_, fused_am_, fused_sync_, fused_wperm_,
         fused_y_, fused_tagged_, fused_dbg_;
     std::vector<FusedLayer> fused_host_layers_;
+    // One-step ForwardToken + Greedy on the fused path: the launch writes its logits and token
+    // straight into pinned host memory (device addresses of it), no copy afterwards.
+    float* fused_logits_out_ = nullptr;
+    int32_t* fused_token_out_ = nullptr;
+    unsigned* fused_err_out_ = nullptr;
     unsigned fused_epoch_ = 0;  // tag base of the last fused launch (1..4095)
     int fused_parity_ = 0;      // accumulator parity of the next launch's first step
 };
