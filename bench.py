@@ -39,10 +39,11 @@ WEIGHT_BYTES = 1_191_968_768          # 28 layers + tied lm_head, bf16
 KV_BYTES_PER_POS = 2 * 28 * 1024 * 2  # K and V rows of every layer
 LM_HEAD_BYTES = VOCAB * 1024 * 2
 # DRAM traffic of one fused decode step (dram__bytes_read.sum + dram__bytes_write.sum), from an
-# `ncu --set full` capture of the timed one-step launch of
-# `bench.py --legs decode --steps 1 --warmup 3` (kv_len 17): 1.196486 GB read + 4.693760 MB
-# written. Re-captured whenever the kernel changes.
-FUSED_TRAFFIC_PER_STEP = 1_201_179_760
+# `ncu --set full` capture of a one-step launch of `bench.py --legs decode --steps 8 --warmup 3`
+# (kv_len ~17): 1.227272 GB read + 6.184704 MB written (the read includes the ~30 MB of the first
+# layer's rows that a launch prefetches into L2 for the next one at its end). Re-captured whenever
+# the kernel changes.
+FUSED_TRAFFIC_PER_STEP = 1_233_456_704
 # Long-prompt prefill: 2048 seeded prompt IDs (seed 2) at context 4096, batched on the tensor cores.
 PREFILL_LEN = 2048
 PREFILL_CTX = 4096
@@ -478,6 +479,7 @@ def run_b200_arm(args):
     tp_ms = tp_gbs = tp_bytes_gpu = 0.0
     tp_arms = {}
     tp_default = None
+    tp_failed = {}
     if "tp" in legs:
         tm = q3b200.Qwen3(path, TP_CTX, device=local)
         tprompt = np.random.default_rng(4).integers(0, VOCAB, TP_PROMPT).astype(np.int32)
@@ -495,8 +497,14 @@ def run_b200_arm(args):
         arms = [tp.path] + [a for a in (q3b200.TpDecoder.GRAPH, q3b200.TpDecoder.GRAPH_NCCL)
                             if a != tp.path]
         for arm in arms:
+            # A decode that raises (a bounded wait gave up) leaves the arm out of the line; every
+            # rank still takes the same collective steps, agrees on the outcome and resets.
+            ok, why, out = True, "", None
             tp.path = arm
-            warm = tp.decode(tok, pos, TP_WARMUP)
+            try:
+                warm = tp.decode(tok, pos, TP_WARMUP)
+            except q3b200.Q3Error as e:
+                ok, why = False, str(e)
             pos += TP_WARMUP
             torch.cuda.synchronize()
             if world > 1:
@@ -504,16 +512,26 @@ def run_b200_arm(args):
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(tpx)
             nvtx.range_push("q3.tp_" + names[arm])
-            out = tp.decode(int(warm[-1]), pos, TP_STEPS)
+            if ok:
+                try:
+                    out = tp.decode(int(warm[-1]), pos, TP_STEPS)
+                except q3b200.Q3Error as e:
+                    ok, why = False, str(e)
             nvtx.range_pop()
             e1.record(tpx)
             torch.cuda.synchronize()
             pos += TP_STEPS
-            tok = int(out[-1])
             ms = max_over_ranks(e0.elapsed_time(e1), world)
+            if max_over_ranks(0.0 if ok else 1.0, world) > 0:
+                tp_failed[names[arm]] = why or "failed on another rank"
+                tp.reset()
+                if world > 1:
+                    dist.barrier()
+                continue
+            tok = int(out[-1])
             tp_arms[names[arm]] = ms
-        tp_default = names[arms[0]]
-        tp_ms = tp_arms[tp_default]
+        tp_default = next((names[a] for a in arms if names[a] in tp_arms), None)
+        tp_ms = tp_arms.get(tp_default, float("inf"))
         tp_kv = TP_PROMPT + TP_WARMUP + TP_STEPS / 2
         tp_bytes_gpu = (WEIGHT_BYTES + KV_BYTES_PER_POS * tp_kv) / world
         tp_gbs = tp_bytes_gpu * TP_STEPS / (tp_ms / 1e3) / 1e9
@@ -620,6 +638,7 @@ def run_b200_arm(args):
                                if tp_default == "fused" else
                                "this library's own one-shot all-reduce kernel over NVLink peer "
                                "memory (CUDA IPC handles), not NCCL"),
+                "failed_arms": tp_failed or None,
                 "arms": {name: {"ms_per_step": round(ms / TP_STEPS, 4),
                                 "value": round(TP_STEPS / (ms / 1e3), 1),
                                 "collective": TP_ARM_COLLECTIVE[name]}
