@@ -53,6 +53,10 @@ public:
 private:
     void ensure_step_buffers();
     void enqueue_step(bool forced, int n_forced);
+    void enqueue_small_layers();
+    // Decode steps of at most 16 sequences (of 1024-multiple widths) run their weight products as
+    // CUDA-core GEMVs over fp32 rows instead of tensor-core contractions.
+    bool small_path() const;
     void run(int n_steps, const int32_t* forced_host, int32_t* log_host, float* logits_host);
 
     Model& m_;
@@ -63,7 +67,7 @@ private:
     std::unique_ptr<Prefill> prefill_;
     DeviceBuffer k_, v_, table_, rope_, pos_, tok_, step_, forced_, log_, err_;
     DeviceBuffer x_, xn_, qkv_, o_, gu_, h_, logits_, x_last_, ids_, xn_lo_, o_lo_, h_lo_;
-    DeviceBuffer q32_, attn_part_o_, attn_part_ml_, attn_counter_;
+    DeviceBuffer q32_, attn_part_o_, attn_part_ml_, attn_counter_, o32_, h32_, am_part_, am_counter_;
     int attn_pps_ = 8, attn_splits_ = 1;
     int rope_len_ = 0;
     int cap_rows_ = 0;  // rows the step buffers and maps were built for

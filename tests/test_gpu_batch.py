@@ -222,3 +222,38 @@ def test_batch_capacity_and_range_errors(q3lib, model):
         assert toks.shape == (4, 2)
     finally:
         batch.close()
+
+
+def test_batch_past_16_sequences_matches_oracle(q3lib, full_weights):
+    """Batches of up to 16 sequences run their weight products as CUDA-core GEMVs (the tests
+    above); more sequences take the tensor-core contractions with bf16 hi + lo activations. 20
+    sequences: every prompt's next token and 12 teacher-forced steps each (260 positions) against
+    the oracle, top-1 >= 99%, logits max-abs <= 5e-2 on the first two steps."""
+    rng = np.random.default_rng(46)
+    n_seqs, steps = 20, 12
+    prompts = [rng.integers(0, 151936, int(n)).astype(np.int32) for n in rng.integers(8, 40, n_seqs)]
+    cont = rng.integers(0, 151936, (steps, n_seqs)).astype(np.int32)
+    ref_am, ref_lg = [], []
+    for i, p in enumerate(prompts):
+        cpu = oracle.PortModel(full_weights, 128)
+        head = np.concatenate([p, cont[:, i]])
+        r = cpu.forward_many(head, 0, want=np.arange(head.size) >= len(p) - 1, logits=True)
+        ref_am.append(r["argmax"][len(p) - 1:])
+        ref_lg.append(r["logits"])
+    m = q3lib.Qwen3(full_weights, 128)
+    try:
+        b = q3lib.Batch(m, n_seqs, 128)
+        slot0, nxt, _ = b.add_many(prompts)
+        am, lg = b.decode_forced(cont[:2], want_logits=True)
+        am2, _ = b.decode_forced(cont[2:])
+        ours = np.concatenate([np.asarray(nxt)[None, :], am, am2], axis=0)
+        ref = np.stack(ref_am, axis=1)
+        agree = float((ours == ref).mean())
+        err = max(float(np.abs(lg[:, i] - ref_lg[i][1:3]).max()) for i in range(n_seqs))
+        print(f"\n[parity] batch of 20 (tensor-core contractions): positions={ours.size}, "
+              f"agree={agree}, flips={int((ours != ref).sum())}, logits_max_abs={err}")
+        assert agree >= TOP1_AGREEMENT
+        assert err <= LOGITS_MAX_ABS
+        b.close()
+    finally:
+        m.close()
