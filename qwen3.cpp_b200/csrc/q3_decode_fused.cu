@@ -1424,6 +1424,69 @@ __device__ __forceinline__ void combine_group(Smem& sm, const FusedArgs& a, int 
     bar_consumers();
 }
 
+// Phase C prologue of the tensor-parallel instance, whose ranks hold one to four KV groups and so
+// 37 to 148 splits per group (up to 18 in the one-rank instance, which keeps the loop above).
+__device__ __noinline__ void combine_group_wide(Smem& sm, const FusedArgs& a, int S, int g) {
+    // Phase C: the flash-decoding merge of the S splits of KV group g (both query heads): each
+    // split's (max, sum) pair staged in shared memory with one load per thread, the heads' maxima
+    // and every split's scale computed once, then warp w sums the scaled o-partials of splits
+    // w, w + NCW, ... (lane l: dimensions 4l .. 4l + 3 of both heads, the loads independent) and
+    // the warps' sums meet in shared memory. Empty splits (sum 0) take no part.
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    float2* mls = reinterpret_cast<float2*>(sm.xs4);             // [2][S]: (max, sum) -> (scale, -)
+    float* ows = reinterpret_cast<float*>(sm.xs4) + 4 * a.s_max;  // [NCW][2][HD] warp sums
+    for (int i = t; i < 2 * S; i += NCT) {
+        const int hq = i / S, sp = i - hq * S;
+        mls[i] = __ldcg(a.part_ml + static_cast<size_t>(2 * g + hq) * a.s_max + sp);
+    }
+    bar_consumers();
+    if (warp < 2) {
+        float2* m2 = mls + warp * S;
+        float M = -FLT_MAX;
+        for (int sp = lane; sp < S; sp += 32) {
+            const float2 ml = m2[sp];
+            if (ml.y > 0.0f) M = fmaxf(M, ml.x);
+        }
+        M = warp_max(M);
+        float L = 0.0f;
+        for (int sp = lane; sp < S; sp += 32) {
+            const float2 ml = m2[sp];
+            const float sc = ml.y > 0.0f ? expf(ml.x - M) : 0.0f;
+            L += ml.y * sc;
+            m2[sp].x = ml.y > 0.0f ? sc : -1.0f;  // -1: an empty split
+        }
+        L = warp_sum(L);
+        if (lane == 0) sm.red[warp] = L;
+    }
+    bar_consumers();
+    float4 o0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f), o1 = o0;
+    const float4* p0 = reinterpret_cast<const float4*>(a.part_o + static_cast<size_t>(2 * g) * a.s_max * HD) + lane;
+    const float4* p1 = reinterpret_cast<const float4*>(a.part_o + static_cast<size_t>(2 * g + 1) * a.s_max * HD) + lane;
+#pragma unroll 4
+    for (int sp = warp; sp < S; sp += NCW) {
+        const float sc0 = mls[sp].x, sc1 = mls[S + sp].x;
+        const float4 u = __ldcg(p0 + static_cast<size_t>(sp) * (HD / 4));
+        const float4 v = __ldcg(p1 + static_cast<size_t>(sp) * (HD / 4));
+        if (sc0 >= 0.0f) {
+            o0.x = fmaf(u.x, sc0, o0.x); o0.y = fmaf(u.y, sc0, o0.y);
+            o0.z = fmaf(u.z, sc0, o0.z); o0.w = fmaf(u.w, sc0, o0.w);
+        }
+        if (sc1 >= 0.0f) {
+            o1.x = fmaf(v.x, sc1, o1.x); o1.y = fmaf(v.y, sc1, o1.y);
+            o1.z = fmaf(v.z, sc1, o1.z); o1.w = fmaf(v.w, sc1, o1.w);
+        }
+    }
+    reinterpret_cast<float4*>(ows + (warp * 2 + 0) * HD)[lane] = o0;
+    reinterpret_cast<float4*>(ows + (warp * 2 + 1) * HD)[lane] = o1;
+    bar_consumers();
+    const int hq = t >> 7, d = t & (HD - 1);
+    float o = 0.0f;
+#pragma unroll
+    for (int w = 0; w < NCW; ++w) o += ows[(w * 2 + hq) * HD + d];
+    xs_put(sm, t, o / sm.red[hq]);
+    bar_consumers();
+}
+
 // Phase DE tail: sum_i h_i * w2t[i] over this CTA's MLP indices (shared chunks: warp w owns
 // output columns [128w, 128w+128), 4 per lane); returns this lane's 4 sums (columns
 // 128 warp + 4 lane ..), which the caller adds into Y[l] with one float4 atomic.
@@ -1844,7 +1907,11 @@ __global__ void __launch_bounds__(NT, 1) decode_fused_kernel(const __grid_consta
                 // ---- C: combine + o_proj partial of group g
                 if (!phase_begin(sm, a, k, nb, G, c)) return;
                 if (in_grp) {
-                    combine_group(sm, a, p.splits, gl);
+                    if (TP) {
+                        combine_group_wide(sm, a, p.splits, gl);
+                    } else {
+                        combine_group(sm, a, p.splits, gl);
+                    }
                     consume_rows<GRP, RPC_GRP, TP ? kTagX : kTag>(sm, a, q, os.r0, os.n, nullptr, D,
                                                                   a.opart + opart_g, tag, opart_g);
                     q += chunks_of(os.n, RPC_GRP);
@@ -2009,6 +2076,11 @@ int fused_grid(int device) {
 }
 
 void launch_decode_fused(const FusedArgs& a, int grid, cudaStream_t s) {
+    // combine_group stages 2 x s_max (max, sum) pairs and NCW x 2 x HD warp sums in sm.xs4.
+    static_assert(sizeof(Smem::xs4) >= 16 * 256 + NCW * 2 * HD * 4, "combine staging");
+    if (a.s_max < 1 || a.s_max > 256) {
+        throw std::invalid_argument("fused decode: 1..256 attention splits per KV group");
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(NT);
