@@ -224,13 +224,15 @@ def test_batch_capacity_and_range_errors(q3lib, model):
         batch.close()
 
 
-def test_batch_past_16_sequences_matches_oracle(q3lib, full_weights):
-    """Batches of up to 16 sequences run their weight products as CUDA-core GEMVs (the tests
-    above); more sequences take the tensor-core contractions with bf16 hi + lo activations. 20
-    sequences: every prompt's next token and 12 teacher-forced steps each (260 positions) against
-    the oracle, top-1 >= 99%, logits max-abs <= 5e-2 on the first two steps."""
-    rng = np.random.default_rng(46)
-    n_seqs, steps = 20, 12
+@pytest.mark.parametrize("n_seqs", [12, 20])
+def test_batch_step_kinds_match_oracle(q3lib, full_weights, n_seqs):
+    """The decode step's weight products by batch size: up to 16 sequences CUDA-core GEMVs over
+    fp32 rows (8-row tasks up to 8 sequences: the tests above; 16-row tasks from 9: 12 here), more
+    the tcgen05 contractions with bf16 hi + lo activations (20 here). Every prompt's next token and 16 teacher-forced steps each
+    (204 / 340 positions) against the oracle, top-1 >= 99%, logits max-abs <= 5e-2 on the first two
+    steps."""
+    rng = np.random.default_rng(46 + n_seqs)
+    steps = 16
     prompts = [rng.integers(0, 151936, int(n)).astype(np.int32) for n in rng.integers(8, 40, n_seqs)]
     cont = rng.integers(0, 151936, (steps, n_seqs)).astype(np.int32)
     ref_am, ref_lg = [], []
@@ -250,7 +252,7 @@ def test_batch_past_16_sequences_matches_oracle(q3lib, full_weights):
         ref = np.stack(ref_am, axis=1)
         agree = float((ours == ref).mean())
         err = max(float(np.abs(lg[:, i] - ref_lg[i][1:3]).max()) for i in range(n_seqs))
-        print(f"\n[parity] batch of 20 (tensor-core contractions): positions={ours.size}, "
+        print(f"\n[parity] batch of {n_seqs}: positions={ours.size}, "
               f"agree={agree}, flips={int((ours != ref).sum())}, logits_max_abs={err}")
         assert agree >= TOP1_AGREEMENT
         assert err <= LOGITS_MAX_ABS
