@@ -29,6 +29,37 @@ __device__ __forceinline__ uint32_t pack2_bf16(float a, float b) {
 
 constexpr int kNormWarps = 8;  // rows per block, one warp per row
 
+// Elements i..i+3 of the normalised row as bf16 (or fp16) at out, their low parts at out_lo.
+__device__ __forceinline__ void norm_emit4(uint16_t* orow, uint16_t* lorow, int i, float4 v,
+                                           float inv, const uint16_t* w, int f16) {
+    const uint2 wb = *reinterpret_cast<const uint2*>(w + i);
+    const float y0 = (v.x * inv) * bf16_lo(wb.x), y1 = (v.y * inv) * bf16_hi(wb.x);
+    const float y2 = (v.z * inv) * bf16_lo(wb.y), y3 = (v.w * inv) * bf16_hi(wb.y);
+    if (f16) {
+        const uint2 hi = make_uint2(pack2_f16(y0, y1), pack2_f16(y2, y3));
+        *reinterpret_cast<uint2*>(orow + i) = hi;
+        if (lorow) {  // y - f16(y): the hi + lo pair carries 22 significant bits
+            *reinterpret_cast<uint2*>(lorow + i) =
+                make_uint2(pack2_f16(y0 - f16_lo(hi.x), y1 - f16_hi(hi.x)),
+                           pack2_f16(y2 - f16_lo(hi.y), y3 - f16_hi(hi.y)));
+        }
+        return;
+    }
+    const uint2 hi = make_uint2(pack2_bf16(y0, y1), pack2_bf16(y2, y3));
+    *reinterpret_cast<uint2*>(orow + i) = hi;
+    if (lorow) {  // y - bf16(y): the hi + lo pair carries 16 significant bits
+        *reinterpret_cast<uint2*>(lorow + i) =
+            make_uint2(pack2_bf16(y0 - bf16_lo(hi.x), y1 - bf16_hi(hi.x)),
+                       pack2_bf16(y2 - bf16_lo(hi.y), y3 - bf16_hi(hi.y)));
+    }
+}
+
+// One warp per row: x (from the embedding rows of ids when given) -> RmsNorm (src/inference.cpp:
+// 905-921: (x * (1 / rms)) * w, rms = sqrtf(ss / n + eps)) -> bf16 / fp16 (+ low parts). DIM > 0:
+// the row width as a constant, the row held in registers between the sum of squares and the
+// output (one read of x); DIM = 0: any width (a multiple of 256), x read twice. Both sum the
+// squares in the same order, so they give the same bits.
+template <int DIM>
 __global__ void __launch_bounds__(kNormWarps * 32)
     rmsnorm_rows_kernel(const int32_t* __restrict__ ids, const uint16_t* __restrict__ embed,
                         float* __restrict__ x, const uint16_t* __restrict__ w, float eps,
@@ -39,7 +70,40 @@ __global__ void __launch_bounds__(kNormWarps * 32)
     const int lane = threadIdx.x & 31;
     const int row = blockIdx.x * kNormWarps + (threadIdx.x >> 5);
     if (row >= rows) return;
+    if (DIM > 0) dim = DIM;
     float* xr = x + static_cast<size_t>(row) * dim;
+    uint16_t* orow = out + static_cast<size_t>(row) * dim;
+    uint16_t* lorow = out_lo ? out_lo + static_cast<size_t>(row) * dim : nullptr;
+    if (DIM > 0) {
+        constexpr int NV = DIM > 0 ? DIM / 128 : 1;  // float4 per lane
+        float4 v[NV];
+        if (ids) {
+            const uint16_t* er = embed + static_cast<size_t>(ids[row]) * dim;
+#pragma unroll
+            for (int j = 0; j < NV; ++j) {
+                const int i = lane * 4 + 128 * j;
+                const uint2 e = *reinterpret_cast<const uint2*>(er + i);
+                v[j] = make_float4(bf16_lo(e.x), bf16_hi(e.x), bf16_lo(e.y), bf16_hi(e.y));
+                *reinterpret_cast<float4*>(xr + i) = v[j];
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < NV; ++j) v[j] = *reinterpret_cast<const float4*>(xr + lane * 4 + 128 * j);
+        }
+        float ss = 0.0f;
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            ss = fmaf(v[j].x, v[j].x, ss);
+            ss = fmaf(v[j].y, v[j].y, ss);
+            ss = fmaf(v[j].z, v[j].z, ss);
+            ss = fmaf(v[j].w, v[j].w, ss);
+        }
+        ss = warp_sum(ss);
+        const float inv = 1.0f / sqrtf(ss / static_cast<float>(dim) + eps);
+#pragma unroll
+        for (int j = 0; j < NV; ++j) norm_emit4(orow, lorow, lane * 4 + 128 * j, v[j], inv, w, f16);
+        return;
+    }
     if (ids) {
         const uint16_t* er = embed + static_cast<size_t>(ids[row]) * dim;
         for (int i = lane * 8; i < dim; i += 256) {
@@ -58,31 +122,9 @@ __global__ void __launch_bounds__(kNormWarps * 32)
         ss = fmaf(v.w, v.w, ss);
     }
     ss = warp_sum(ss);
-    // RmsNorm (src/inference.cpp:905-921): (x * (1 / rms)) * w, rms = sqrtf(ss / n + eps).
     const float inv = 1.0f / sqrtf(ss / static_cast<float>(dim) + eps);
-    uint16_t* orow = out + static_cast<size_t>(row) * dim;
     for (int i = lane * 4; i < dim; i += 128) {
-        const float4 v = *reinterpret_cast<const float4*>(xr + i);
-        const uint2 wb = *reinterpret_cast<const uint2*>(w + i);
-        const float y0 = (v.x * inv) * bf16_lo(wb.x), y1 = (v.y * inv) * bf16_hi(wb.x);
-        const float y2 = (v.z * inv) * bf16_lo(wb.y), y3 = (v.w * inv) * bf16_hi(wb.y);
-        if (f16) {
-            const uint2 hi = make_uint2(pack2_f16(y0, y1), pack2_f16(y2, y3));
-            *reinterpret_cast<uint2*>(orow + i) = hi;
-            if (out_lo) {  // y - f16(y): the hi + lo pair carries 22 significant bits
-                *reinterpret_cast<uint2*>(out_lo + static_cast<size_t>(row) * dim + i) =
-                    make_uint2(pack2_f16(y0 - f16_lo(hi.x), y1 - f16_hi(hi.x)),
-                               pack2_f16(y2 - f16_lo(hi.y), y3 - f16_hi(hi.y)));
-            }
-            continue;
-        }
-        const uint2 hi = make_uint2(pack2_bf16(y0, y1), pack2_bf16(y2, y3));
-        *reinterpret_cast<uint2*>(orow + i) = hi;
-        if (out_lo) {  // y - bf16(y): the hi + lo pair carries 16 significant bits
-            *reinterpret_cast<uint2*>(out_lo + static_cast<size_t>(row) * dim + i) =
-                make_uint2(pack2_bf16(y0 - bf16_lo(hi.x), y1 - bf16_hi(hi.x)),
-                           pack2_bf16(y2 - bf16_lo(hi.y), y3 - bf16_hi(hi.y)));
-        }
+        norm_emit4(orow, lorow, i, *reinterpret_cast<const float4*>(xr + i), inv, w, f16);
     }
 }
 
@@ -206,9 +248,9 @@ void launch_rmsnorm_rows_bf16(const int32_t* ids, const uint16_t* embed, float* 
                               cudaStream_t s, uint16_t* out_lo, bool dependent, bool f16) {
     if (rows <= 0) return;
     if (dim % 256 != 0) throw std::invalid_argument("row RmsNorm needs a width that is a multiple of 256");
-    launch_dep(dependent, rmsnorm_rows_kernel, dim3((rows + kNormWarps - 1) / kNormWarps),
-               dim3(kNormWarps * 32), 0, s, ids, embed, x, w, eps, out, out_lo, rows, dim,
-               static_cast<int>(f16));
+    launch_dep(dependent, dim == 1024 ? rmsnorm_rows_kernel<1024> : rmsnorm_rows_kernel<0>,
+               dim3((rows + kNormWarps - 1) / kNormWarps), dim3(kNormWarps * 32), 0, s, ids, embed,
+               x, w, eps, out, out_lo, rows, dim, static_cast<int>(f16));
     Q3_CUDA(cudaGetLastError());
 }
 
